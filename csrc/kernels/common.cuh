@@ -1,0 +1,75 @@
+// Shared device helpers for the barq sm_100a kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define BARQ_DEV __device__ __forceinline__
+
+namespace barq {
+
+// Activation in the "q8" layout consumed by the dp4a GEMV kernels: per token row of K values,
+// int8 qs[K] and one float2 (scale d, d * sum(qs)) per 32 values.
+struct ActQ8 {
+  const int8_t* q;   // [B, K]
+  const float2* s;   // [B, K/32]
+};
+
+BARQ_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+BARQ_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+BARQ_DEV int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+BARQ_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+BARQ_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+BARQ_DEV float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+BARQ_DEV float to_f(float v) { return v; }
+BARQ_DEV float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+BARQ_DEV float to_f(__half v) { return __half2float(v); }
+
+template <typename T> BARQ_DEV T from_f(float v);
+template <> BARQ_DEV float from_f<float>(float v) { return v; }
+template <> BARQ_DEV __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+template <> BARQ_DEV __half from_f<__half>(float v) { return __float2half(v); }
+
+BARQ_DEV int4 ldg16(const void* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
+// Streaming (evict-first) 16-byte load for weights that are read exactly once per step.
+BARQ_DEV int4 ldg16_stream(const void* p) {
+  int4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+// Quantize 32 consecutive values held one per lane into int8 with a shared scale.
+// Returns the lane's int8 value; lane 0's (d, d*sum) is written by the caller.
+BARQ_DEV int8_t quant_lane32(float v, float& d_out, float& s_out) {
+  float amax = warp_max(fabsf(v));
+  float d = amax / 127.0f;
+  float id = d > 0.f ? 1.0f / d : 0.f;
+  int q = __float2int_rn(v * id);
+  q = max(-127, min(127, q));
+  int qs = warp_sum_int(q);
+  d_out = d;
+  s_out = d * (float)qs;
+  return (int8_t)q;
+}
+
+}  // namespace barq
