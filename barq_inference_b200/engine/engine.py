@@ -1,0 +1,424 @@
+"""The inference engine: model runner + paged KV + scheduler + device sampler + CUDA graphs.
+
+Public API (what the CLI, the HTTP/UDS servers and ``bench.py`` call):
+
+* ``Engine.from_gguf(path, ...)`` / ``Engine(cfg, tensors, ...)``
+* ``Engine.generate(prompts, params) -> list[GenerationResult]`` (batched, blocking)
+* ``Engine.add_request(prompt, params, on_token=...)`` + ``Engine.step()`` (streaming / serving)
+
+Parity: ``ModelContext::{encode, decode, sample, generate}`` (``models/src/context.rs:391-556``),
+``BatchEngine::run`` (``advanced/src/batch_engine.rs:106-191``, whose forward samples random
+logits) and the CUDA-graph flag (``cli/src/performance.rs:16-22``, env var only).  Here decode steps
+are captured once per batch-size bucket as CUDA graphs (embedding through sampling), prompts are
+prefilled in chunks, and tokens stream out one step at a time.
+"""
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.runner import LlamaRunner, StepInput
+from .kv_cache import BlockManager
+from .scheduler import ScheduledStep, Scheduler, SchedulerConfig
+from .sampling_params import SamplingParams
+from .sequence import Sequence, SeqStatus
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 64
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 4096
+    block_size: int = 16
+    num_blocks: int | None = None   # None -> sized from kv_cache_gb
+    kv_cache_gb: float = 8.0
+    kv_dtype: str = "fp16"          # fp16 | bf16
+    cuda_graphs: bool = True
+    graph_buckets: tuple[int, ...] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
+    prefix_caching: bool = False
+    chunked_prefill: bool = True
+    device: str = "cuda"
+    ser_threshold: float = 0.0      # MoE smart expert reduction (--ser)
+    fused_moe: bool = True          # --fmoe
+
+    @staticmethod
+    def preset(name: str, **kw) -> "EngineConfig":
+        """CLI presets (``cli/src/main.rs`` --preset) mapped to concrete switches."""
+        base = {
+            "max-speed": dict(cuda_graphs=True, kv_dtype="fp16", max_num_seqs=128),
+            "balanced": dict(cuda_graphs=True, kv_dtype="fp16"),
+            "max-quality": dict(cuda_graphs=True, kv_dtype="bf16"),
+            "gpu": dict(cuda_graphs=True),
+            "cpu": dict(cuda_graphs=False),
+        }[name]
+        base.update(kw)
+        return EngineConfig(**base)
+
+
+@dataclass
+class GenerationResult:
+    prompt: list[int]
+    tokens: list[int]
+    finish_reason: str
+    ttft_s: float | None
+    latency_s: float
+    logprobs: list[float] = field(default_factory=list)
+
+
+class _GraphBucket:
+    __slots__ = ("B", "graph", "out_ids")
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, tensors, engine_cfg: EngineConfig | None = None, runner=None):
+        self.cfg = cfg
+        self.ecfg = ec = engine_cfg or EngineConfig()
+        self.device = torch.device(ec.device)
+        kv_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16}[ec.kv_dtype]
+        self.runner = runner or make_runner(cfg, tensors, self.device, kv_dtype, ec)
+        self.max_blocks_per_seq = (ec.max_model_len + ec.block_size - 1) // ec.block_size
+        nb = ec.num_blocks
+        if nb is None:
+            nb = max(64, int(ec.kv_cache_gb * (1 << 30) // self.runner.kv_bytes_per_block(ec.block_size)))
+        self.runner.allocate_kv(nb, ec.block_size)
+        self.blocks = BlockManager(nb, ec.block_size)
+        self.dummy_block = self.blocks.allocate(1)[0]  # padding rows of graph batches write here
+        self.prefix_cache = None
+        if ec.prefix_caching:
+            from .prefix_cache import RadixPrefixCache
+
+            self.prefix_cache = RadixPrefixCache(self.blocks)
+        self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
+                                               ec.chunked_prefill), self.blocks, self.prefix_cache)
+        self.graphs: dict[int, _GraphBucket] = {}
+        self._static = None
+        self.metrics = None
+        self.step_count = 0
+        self.timings = {"prefill_s": 0.0, "decode_s": 0.0, "prefill_tokens": 0, "decode_tokens": 0}
+
+    # ------------------------------------------------------------------ construction helpers
+    @staticmethod
+    def from_gguf(path: str, engine_cfg: EngineConfig | None = None, device: str | None = None) -> "Engine":
+        from ..gguf import read_gguf
+        from ..models.config import config_from_gguf
+        from ..models.weights import tensors_from_gguf
+
+        g = read_gguf(path)
+        cfg = config_from_gguf(g.metadata, set(g.tensors))
+        ec = engine_cfg or EngineConfig()
+        if device:
+            ec.device = device
+        ec.max_model_len = min(ec.max_model_len, cfg.max_ctx)
+        tensors = tensors_from_gguf(g, device="cpu")
+        eng = Engine(cfg, tensors, ec)
+        eng.gguf = g
+        return eng
+
+    # ------------------------------------------------------------------ request API
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None, request_id: str = "",
+                    on_token=None) -> Sequence:
+        params = params or SamplingParams()
+        seq = Sequence(list(prompt), params, request_id=request_id, on_token=on_token)
+        if any(t < 0 or t >= self.cfg.vocab for t in seq.prompt):
+            raise ValueError("prompt token id out of range")
+        if params.grammar or params.json_mode or params.json_schema:
+            from ..sampling.grammar_engine import make_grammar_state
+
+            seq.grammar_state = make_grammar_state(self, params)
+        if params.needs_host_sampler:
+            from ..sampling.host_samplers import HostSampler
+
+            seq.host_sampler = HostSampler(params, self.cfg.vocab)
+        self.sched.add(seq)
+        return seq
+
+    def has_work(self) -> bool:
+        return self.sched.has_work
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
+                 ) -> list[GenerationResult]:
+        if params is None or isinstance(params, SamplingParams):
+            params = [params or SamplingParams()] * len(prompts)
+        seqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        while self.sched.has_work:
+            self.step()
+        return [self._result(s) for s in seqs]
+
+    def _result(self, s: Sequence) -> GenerationResult:
+        return GenerationResult(s.prompt, s.output, s.finish_reason or "", s.ttft,
+                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs)
+
+    # ------------------------------------------------------------------ one engine step
+    def step(self) -> list[Sequence]:
+        plan = self.sched.schedule()
+        if plan is None:
+            if self.sched.waiting:
+                raise RuntimeError("KV cache too small for the waiting request")
+            return []
+        t0 = time.perf_counter()
+        if plan.kind == "decode":
+            ids = self._run_decode(plan)
+        else:
+            ids = self._run_prefill(plan)
+        dt = time.perf_counter() - t0
+        key = "decode" if plan.kind == "decode" else "prefill"
+        self.timings[key + "_s"] += dt
+        self.timings[key + "_tokens"] += sum(plan.n_new)
+        self.step_count += 1
+        return self._commit(plan, ids)
+
+    def _commit(self, plan: ScheduledStep, ids: list[int | None]) -> list[Sequence]:
+        now = time.perf_counter()
+        done = []
+        for s, n, tok in zip(plan.seqs, plan.n_new, ids):
+            s.n_cached += n
+            if tok is None:  # prefill chunk that did not reach the end of the prompt
+                continue
+            if s.first_token_time is None:
+                s.first_token_time = now
+            s.output.append(tok)
+            if s.grammar_state is not None:
+                s.grammar_state.accept(tok)
+            if s.on_token is not None:
+                s.on_token(s, tok)
+            reason = self._stop_reason(s, tok)
+            if reason:
+                s.finish_time = now
+                self.sched.finish(s, reason)
+                done.append(s)
+                if s.on_token is not None:
+                    s.on_token(s, -1)
+        return done
+
+    def _stop_reason(self, s: Sequence, tok: int) -> str | None:
+        p = s.params
+        if not p.ignore_eos and tok in self.cfg.eos_ids:
+            return "stop"
+        if tok in p.stop_token_ids:
+            return "stop"
+        if s.grammar_state is not None and s.grammar_state.done():
+            return "stop"
+        if len(s.output) >= p.max_tokens:
+            return "length"
+        if s.n_tokens >= self.ecfg.max_model_len:
+            return "length"
+        return None
+
+    # ------------------------------------------------------------------ input building
+    def _pinned(self, arr: np.ndarray) -> torch.Tensor:
+        return torch.from_numpy(arr).pin_memory() if self.device.type == "cuda" else torch.from_numpy(arr)
+
+    def _stage(self, key: str, arr: np.ndarray) -> torch.Tensor:
+        """Copy ``arr`` into a reusable pinned host buffer (grown on demand) and return its view."""
+        bufs = self.__dict__.setdefault("_pin_bufs", {})
+        n = arr.size
+        buf = bufs.get(key)
+        if buf is None or buf.numel() < n or buf.dtype != torch.from_numpy(arr[:0].reshape(-1)).dtype:
+            buf = torch.empty(max(n, 256), dtype=torch.from_numpy(arr[:0].reshape(-1)).dtype,
+                              pin_memory=self.device.type == "cuda")
+            bufs[key] = buf
+        view = buf[:n].view(arr.shape)
+        view.numpy()[...] = arr
+        return view
+
+    def _to_dev(self, arr: np.ndarray) -> torch.Tensor:
+        return self._pinned(arr).to(self.device, non_blocking=True)
+
+    def _slot_of(self, s: Sequence, pos: int) -> int:
+        bs = self.ecfg.block_size
+        return s.block_table[pos // bs] * bs + pos % bs
+
+    def _run_prefill(self, plan: ScheduledStep) -> list[int | None]:
+        ids, pos, slots, last = [], [], [], []
+        q_start = [0]
+        for s, n in zip(plan.seqs, plan.n_new):
+            toks = s.tokens
+            for p in range(s.n_cached, s.n_cached + n):
+                ids.append(toks[p])
+                pos.append(p)
+                slots.append(self._slot_of(s, p))
+            q_start.append(len(ids))
+            last.append(len(ids) - 1)
+        S = len(plan.seqs)
+        mb = max(len(s.block_table) for s in plan.seqs)
+        bt = np.zeros((S, mb), np.int32)
+        for i, s in enumerate(plan.seqs):
+            bt[i, : len(s.block_table)] = s.block_table
+        seq_lens = np.array([s.n_cached + n for s, n in zip(plan.seqs, plan.n_new)], np.int32)
+        inp = StepInput(self._to_dev(np.array(ids, np.int32)), self._to_dev(np.array(pos, np.int32)),
+                        self._to_dev(np.array(slots, np.int64)), self._to_dev(bt), self._to_dev(seq_lens),
+                        self._to_dev(np.array(last, np.int64)), False,
+                        q_start=self._to_dev(np.array(q_start, np.int32)), max_q=max(plan.n_new))
+        logits = self.runner.forward(inp)
+        complete = [s.n_cached + n >= s.n_tokens for s, n in zip(plan.seqs, plan.n_new)]
+        out = self._sample(logits, plan.seqs)
+        return [t if c else None for t, c in zip(out, complete)]
+
+    def _decode_arrays(self, seqs: list[Sequence], B: int):
+        bs = self.ecfg.block_size
+        n = len(seqs)
+        ids = np.zeros(B, np.int32)
+        pos = np.zeros(B, np.int32)
+        slots = np.full(B, self.dummy_block * bs, np.int64)
+        lens = np.ones(B, np.int32)
+        bt = np.full((B, self.max_blocks_per_seq), self.dummy_block, np.int32)
+        for i, s in enumerate(seqs):
+            p = s.n_tokens - 1
+            ids[i] = s.tokens[-1]
+            pos[i] = p
+            slots[i] = self._slot_of(s, p)
+            lens[i] = s.n_tokens
+            bt[i, : len(s.block_table)] = s.block_table
+        return ids, pos, slots, lens, bt, n
+
+    def _run_decode(self, plan: ScheduledStep) -> list[int | None]:
+        seqs = plan.seqs
+        simple = all(s.grammar_state is None and s.host_sampler is None and not s.params.needs_penalties
+                     for s in seqs)
+        if self.ecfg.cuda_graphs and simple and self.device.type == "cuda":
+            B = next((b for b in self.ecfg.graph_buckets if b >= len(seqs)), None)
+            if B is not None:
+                return self._decode_graph(seqs, B)
+        ids, pos, slots, lens, bt, n = self._decode_arrays(seqs, len(seqs))
+        inp = StepInput(self._to_dev(ids), self._to_dev(pos), self._to_dev(slots), self._to_dev(bt),
+                        self._to_dev(lens), self._to_dev(np.arange(n, dtype=np.int64)), True)
+        logits = self.runner.forward(inp)
+        return self._sample(logits, seqs)
+
+    # ------------------------------------------------------------------ sampling
+    def _sampling_tensors(self, seqs: list[Sequence], B: int):
+        temp = np.zeros(B, np.float32)
+        topk = np.zeros(B, np.int32)
+        topp = np.ones(B, np.float32)
+        minp = np.zeros(B, np.float32)
+        seeds = np.zeros(B, np.int64)
+        steps = np.zeros(B, np.int32)
+        for i, s in enumerate(seqs):
+            p = s.params
+            temp[i] = p.temperature
+            topk[i] = p.top_k
+            topp[i] = p.top_p
+            minp[i] = p.min_p
+            seeds[i] = p.seed * 1000003 + s.seq_id if p.seed == 0 else p.seed
+            steps[i] = len(s.output)
+        return temp, topk, topp, minp, seeds, steps
+
+    def _sample(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
+        B = len(seqs)
+        temp, topk, topp, minp, seeds, steps = (self._to_dev(a) for a in self._sampling_tensors(seqs, B))
+        mask = None
+        if any(s.grammar_state is not None for s in seqs):
+            words = (self.cfg.vocab + 31) // 32
+            m = np.full((B, words), 0xFFFFFFFF, np.uint32)
+            for i, s in enumerate(seqs):
+                if s.grammar_state is not None:
+                    m[i] = s.grammar_state.allowed_mask(words)
+            mask = self._to_dev(m.view(np.int32))
+        pen = hist = None
+        if any(s.params.needs_penalties for s in seqs):
+            nh = max(s.params.penalty_last_n for s in seqs)
+            pa = np.zeros((B, 3), np.float32)
+            pa[:, 0] = 1.0
+            h = np.full((B, nh), -1, np.int32)
+            for i, s in enumerate(seqs):
+                pa[i] = (s.params.repetition_penalty, s.params.frequency_penalty, s.params.presence_penalty)
+                last = s.tokens[-s.params.penalty_last_n:] if s.params.penalty_last_n > 0 else []
+                h[i, : len(last)] = last
+            pen, hist = self._to_dev(pa), self._to_dev(h)
+        host = [i for i, s in enumerate(seqs) if s.host_sampler is not None]
+        if host:
+            lg = logits.float().cpu()
+        ids, lp = ops.sample(logits, temp, topk, topp, minp, seeds, steps, allow_mask=mask, penalties=pen,
+                             history=hist, want_logprob=any(s.params.logprobs for s in seqs))
+        out = ids.cpu().tolist()
+        lps = lp.cpu().tolist() if lp is not None else None
+        for i in host:
+            out[i] = seqs[i].host_sampler.sample(lg[i], seqs[i])
+        if lps is not None:
+            for s, v in zip(seqs, lps):
+                if s.params.logprobs:
+                    s.logprobs.append(v)
+        return out
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def _static_buffers(self):
+        if self._static is None:
+            Bm = max(self.ecfg.graph_buckets)
+            d = self.device
+            self._static = {
+                "ids": torch.zeros(Bm, dtype=torch.int32, device=d),
+                "pos": torch.zeros(Bm, dtype=torch.int32, device=d),
+                "slots": torch.zeros(Bm, dtype=torch.int64, device=d),
+                "lens": torch.ones(Bm, dtype=torch.int32, device=d),
+                "bt": torch.zeros(Bm, self.max_blocks_per_seq, dtype=torch.int32, device=d),
+                "last": torch.arange(Bm, dtype=torch.int64, device=d),
+                "temp": torch.zeros(Bm, dtype=torch.float32, device=d),
+                "topk": torch.zeros(Bm, dtype=torch.int32, device=d),
+                "topp": torch.ones(Bm, dtype=torch.float32, device=d),
+                "minp": torch.zeros(Bm, dtype=torch.float32, device=d),
+                "seeds": torch.zeros(Bm, dtype=torch.int64, device=d),
+                "steps": torch.zeros(Bm, dtype=torch.int32, device=d),
+                # one pinned host staging row holding every per-step input, copied with one H2D
+                "host": torch.zeros(0),
+            }
+        return self._static
+
+    def _graph_forward(self, B: int):
+        st = self._static
+        inp = StepInput(st["ids"][:B], st["pos"][:B], st["slots"][:B], st["bt"][:B], st["lens"][:B],
+                        st["last"][:B], True)
+        logits = self.runner.forward(inp)
+        ids, _ = ops.sample(logits, st["temp"][:B], st["topk"][:B], st["topp"][:B], st["minp"][:B],
+                            st["seeds"][:B], st["steps"][:B])
+        return ids
+
+    def _capture(self, B: int) -> _GraphBucket:
+        self._static_buffers()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm up allocations and lazily-set kernel attributes
+                self._graph_forward(B)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=getattr(self, "_graph_pool", None)):
+            out = self._graph_forward(B)
+        self._graph_pool = g.pool()
+        gb = _GraphBucket()
+        gb.B, gb.graph, gb.out_ids = B, g, out
+        return gb
+
+    def _decode_graph(self, seqs: list[Sequence], B: int) -> list[int]:
+        gb = self.graphs.get(B)
+        if gb is None:
+            gb = self.graphs[B] = self._capture(B)
+        st = self._static
+        ids, pos, slots, lens, bt, n = self._decode_arrays(seqs, B)
+        temp, topk, topp, minp, seeds, steps = self._sampling_tensors(seqs, B)
+        for k, a in (("ids", ids), ("pos", pos), ("slots", slots), ("lens", lens), ("bt", bt), ("temp", temp),
+                     ("topk", topk), ("topp", topp), ("minp", minp), ("seeds", seeds), ("steps", steps)):
+            st[k][:B].copy_(self._stage(k, a), non_blocking=True)
+        gb.graph.replay()
+        return gb.out_ids[:n].cpu().tolist()
+
+
+def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
+    if cfg.is_mla:
+        from ..models.deepseek2 import DeepseekV2Runner
+
+        return DeepseekV2Runner(cfg, tensors, device, kv_dtype, ser_threshold=ec.ser_threshold)
+    r = LlamaRunner(cfg, tensors, device, kv_dtype)
+    r.ser_threshold = ec.ser_threshold
+    r.fused_moe = ec.fused_moe
+    return r
+
+
+def env_flag(name: str, default: bool) -> bool:
+    v = os.environ.get(name)
+    return default if v is None else v not in ("0", "false", "False", "")

@@ -1,0 +1,160 @@
+"""Continuous-batching scheduler with chunked prefill, KV admission control and preemption.
+
+Parity: ``BatchScheduler`` (``advanced/src/continuous_batching.rs:27-180``: pending queue, admit up
+to ``max_sequences``, ``fill_batch`` emitting prompts for new sequences and last tokens for running
+ones, ``update_sequences`` retiring on EOS / ``max_tokens``) and its ``low_latency`` /
+``high_throughput`` presets (``:213-250``).  Added: a per-step token budget with chunked prefill,
+admission against free KV blocks, and preemption (recompute) of the youngest sequence when the
+block pool runs dry — the reference has no memory model for its batch at all.
+
+Each step is either a prefill step (new prompt tokens of one or more sequences) or a decode step
+(one token for every running sequence); prefill has priority so TTFT stays low.
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass
+
+from .kv_cache import BlockManager
+from .sequence import Sequence, SeqStatus
+
+
+@dataclass
+class SchedulerConfig:
+    max_num_seqs: int = 64
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 8192
+    chunked_prefill: bool = True
+
+    @staticmethod
+    def low_latency() -> "SchedulerConfig":
+        return SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=2048)
+
+    @staticmethod
+    def high_throughput() -> "SchedulerConfig":
+        return SchedulerConfig(max_num_seqs=128, max_num_batched_tokens=16384)
+
+
+@dataclass
+class ScheduledStep:
+    kind: str  # "prefill" | "decode"
+    seqs: list[Sequence]
+    n_new: list[int]  # new tokens per sequence this step
+
+
+class Scheduler:
+    def __init__(self, cfg: SchedulerConfig, blocks: BlockManager, prefix_cache=None):
+        self.cfg = cfg
+        self.blocks = blocks
+        self.waiting: deque[Sequence] = deque()
+        self.running: list[Sequence] = []
+        self.prefix_cache = prefix_cache
+        self.n_preemptions = 0
+
+    def add(self, seq: Sequence) -> None:
+        if len(seq.prompt) == 0:
+            raise ValueError("empty prompt")
+        if len(seq.prompt) >= self.cfg.max_model_len:
+            raise ValueError(f"prompt of {len(seq.prompt)} tokens exceeds max_model_len {self.cfg.max_model_len}")
+        self.waiting.append(seq)
+
+    @property
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def _free(self, seq: Sequence) -> None:
+        if seq.block_table:
+            self.blocks.release(seq.block_table)
+        seq.block_table = []
+        seq.n_cached = 0
+
+    def finish(self, seq: Sequence, reason: str) -> None:
+        seq.status = SeqStatus.FINISHED
+        seq.finish_reason = reason
+        if self.prefix_cache is not None:
+            self.prefix_cache.insert(seq.tokens[: seq.n_cached], seq.block_table)
+        self._free(seq)
+        if seq in self.running:
+            self.running.remove(seq)
+
+    def _preempt_youngest(self, protect: Sequence | None = None) -> bool:
+        cands = [s for s in self.running if s is not protect]
+        if not cands:
+            return False
+        victim = max(cands, key=lambda s: s.arrival)
+        self.running.remove(victim)
+        self._free(victim)
+        victim.status = SeqStatus.WAITING
+        victim.n_preempted += 1
+        self.n_preemptions += 1
+        self.waiting.appendleft(victim)
+        return True
+
+    def schedule(self) -> ScheduledStep | None:
+        cfg = self.cfg
+        # 1) continue chunked prefills of running sequences first
+        pre = [s for s in self.running if s.n_uncached > 1]
+        budget = cfg.max_num_batched_tokens
+        seqs, n_new = [], []
+        for s in pre:
+            n = min(s.n_uncached, budget)
+            if n <= 0:
+                break
+            if not self._reserve(s, s.n_cached + n):
+                break
+            seqs.append(s)
+            n_new.append(n)
+            budget -= n
+        # 2) admit waiting sequences
+        while self.waiting and budget > 0 and len(self.running) < cfg.max_num_seqs:
+            s = self.waiting[0]
+            if self.prefix_cache is not None and not s.block_table:
+                hit_blocks, hit_tokens = self.prefix_cache.match(s.tokens[:-1])
+                if hit_blocks:
+                    self.blocks.retain(hit_blocks)
+                    s.block_table = list(hit_blocks)
+                    s.n_cached = hit_tokens
+                    s.prefix_hit = hit_tokens
+            total = s.n_uncached
+            n = total if total <= budget else (budget if cfg.chunked_prefill else 0)
+            if n <= 0:
+                break
+            need = self.blocks.blocks_for(s.n_cached + n) - len(s.block_table)
+            if not self.blocks.can_allocate(need):
+                if self.prefix_cache is not None and self.prefix_cache.evict(need - self.blocks.n_free):
+                    continue
+                if s.block_table and s.prefix_hit:
+                    self._free(s)
+                break
+            self.waiting.popleft()
+            self.blocks.grow(s.block_table, s.n_cached + n)
+            s.status = SeqStatus.RUNNING
+            self.running.append(s)
+            seqs.append(s)
+            n_new.append(n)
+            budget -= n
+        if seqs:
+            return ScheduledStep("prefill", seqs, n_new)
+        # 3) decode every running sequence
+        if not self.running:
+            return None
+        dec = []
+        for s in sorted(self.running, key=lambda s: s.arrival):
+            if s not in self.running:
+                continue  # preempted below
+            if self._reserve(s, s.n_tokens):
+                dec.append(s)
+        dec = [s for s in dec if s in self.running]
+        if not dec:
+            return None
+        return ScheduledStep("decode", dec, [1] * len(dec))
+
+    def _reserve(self, s: Sequence, n_tokens: int) -> bool:
+        need = self.blocks.blocks_for(n_tokens) - len(s.block_table)
+        while need > self.blocks.n_free:
+            if self.prefix_cache is not None and self.prefix_cache.evict(need - self.blocks.n_free):
+                continue
+            if not self._preempt_youngest(protect=s):
+                return False
+        self.blocks.grow(s.block_table, n_tokens)
+        return True

@@ -1,0 +1,188 @@
+"""Device model runner: the llama-family decoder (Llama 2/3, Mistral, Mixtral, Qwen2/3) on the
+sm_100a kernels, over a paged KV cache.
+
+Parity: ``LlamaTransformer::forward`` (``models/src/transformer.rs:81-498``) — embedding gather,
+per layer {RMSNorm, Q/K/V (+bias), RoPE, KV append, causal GQA attention, O proj, residual,
+RMSNorm, SwiGLU FFN, residual}, final norm, last-token logits.  Here every step is a fused kernel:
+
+* decode (<= 8 tokens per GEMV launch): RMSNorm -> int8 q8 activations -> dp4a GEMV (K1) with the
+  fused QKV projection; RoPE + paged-KV write (K11); paged flash-decode (K8) whose epilogue emits the
+  q8 input of the O projection; O/down projections add straight into the f32 residual stream; the
+  gate/up GEMV's epilogue computes SiLU(g)*u and its q8 quantization (interleaved gate/up rows).
+* prefill: the same graph with the tcgen05 GEMM (K2) for projections and the paged prefill
+  attention (K9).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..gguf import GGMLType
+from ..ops import EPI_ADD_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU_Q8, Q8Act, QWeight
+from .config import ModelConfig
+from .rope import attn_scale, rope_cos_sin
+from .weights import PackedTensor
+
+GEMV_MAX_T = 8
+
+
+@dataclass
+class StepInput:
+    """Device tensors describing one forward step over a batch of sequences."""
+
+    ids: torch.Tensor          # int32 [T]
+    pos: torch.Tensor          # int32 [T]
+    slots: torch.Tensor        # int64 [T]
+    block_tables: torch.Tensor  # int32 [S, max_blocks]
+    seq_lens: torch.Tensor     # int32 [S] context length after this step
+    last_idx: torch.Tensor     # int64 [S] row of each sequence's last new token
+    decode: bool               # every sequence has exactly one new token (T == S)
+    q_start: torch.Tensor | None = None  # int32 [S+1] (prefill)
+    max_q: int = 1
+
+
+def _qw(pt: PackedTensor, device) -> QWeight:
+    N = pt.rows
+    return QWeight.from_packed(pt.data, pt.ggml_type, N, pt.cols, device)
+
+
+def _f32(pt: PackedTensor, device) -> torch.Tensor:
+    from .reference import dequant_tensor
+
+    return dequant_tensor(pt).reshape(-1).to(device, torch.float32).contiguous()
+
+
+class Layer:
+    pass
+
+
+class LlamaRunner:
+    def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], device="cuda",
+                 kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.kv_dtype = kv_dtype
+        self.scale = attn_scale(cfg)
+        self.use_gemm = use_gemm
+        dev = self.device
+        self.embed_w = _qw(tensors["token_embd.weight"], dev)
+        self.out_norm = _f32(tensors["output_norm.weight"], dev)
+        self.out_w = _qw(tensors["output.weight"], dev) if "output.weight" in tensors else self.embed_w
+        self.layers: list[Layer] = []
+        F = cfg.ffn
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            L = Layer()
+            L.attn_norm = _f32(tensors[p + "attn_norm.weight"], dev)
+            L.ffn_norm = _f32(tensors[p + "ffn_norm.weight"], dev)
+            q, k, v = (_qw(tensors[p + n], dev) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight"))
+            L.qkv_fused = q.wtype == k.wtype == v.wtype
+            L.qkv = ops.cat_rows([q, k, v]) if L.qkv_fused else (q, k, v)
+            if cfg.qkv_bias:
+                L.qkv_bias = torch.cat([_f32(tensors[p + f"attn_{n}.bias"], dev) for n in "qkv"])
+            else:
+                L.qkv_bias = None
+            L.q_norm = _f32(tensors[p + "attn_q_norm.weight"], dev) if cfg.qk_norm else None
+            L.k_norm = _f32(tensors[p + "attn_k_norm.weight"], dev) if cfg.qk_norm else None
+            L.wo = _qw(tensors[p + "attn_output.weight"], dev)
+            if cfg.layer_is_moe(i):
+                from .moe import MoEBlock
+
+                L.moe = MoEBlock(cfg, tensors, p, dev)
+            else:
+                L.moe = None
+                g, u = _qw(tensors[p + "ffn_gate.weight"], dev), _qw(tensors[p + "ffn_up.weight"], dev)
+                L.gu_interleaved = g.wtype == u.wtype and g.wtype != ops.W_BF16 and F % 32 == 0
+                L.gate_up = ops.interleave_gate_up(g, u) if L.gu_interleaved else (
+                    ops.cat_rows([g, u]) if g.wtype == u.wtype else (g, u))
+                L.down = _qw(tensors[p + "ffn_down.weight"], dev)
+            self.layers.append(L)
+        self.cos, self.sin = rope_cos_sin(cfg, cfg.max_ctx, dev)
+
+    # ------------------------------------------------------------------ KV cache
+    def allocate_kv(self, num_blocks: int, block_size: int = 16) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        cfg = self.cfg
+        shape = (cfg.n_layers, 2, num_blocks, cfg.n_kv_heads, block_size, cfg.head_dim)
+        kv = torch.zeros(shape, dtype=self.kv_dtype, device=self.device)
+        self.kv_storage = kv
+        self.kv = [(kv[i, 0], kv[i, 1]) for i in range(cfg.n_layers)]
+        return self.kv
+
+    def kv_bytes_per_block(self, block_size: int = 16) -> int:
+        cfg = self.cfg
+        return cfg.n_layers * 2 * cfg.n_kv_heads * block_size * cfg.head_dim * torch.finfo(self.kv_dtype).bits // 8
+
+    # ------------------------------------------------------------------ linear layers
+    def _lin_q8(self, w, x: Q8Act, T: int, mode: int, out=None, bias=None, xb=None):
+        """GEMV in launches of <= 8 tokens."""
+        if isinstance(w, tuple):
+            outs = [self._lin_q8(wi, x, T, EPI_STORE_F32, xb=xb) for wi in w]
+            r = torch.cat(outs, 1)
+            if bias is not None:
+                r += bias
+            if mode == EPI_ADD_F32:
+                out += r
+                return out
+            return r
+        if mode == EPI_SWIGLU_Q8:
+            oq = Q8Act.empty(T, w.N // 2, self.device)
+            for t0 in range(0, T, GEMV_MAX_T):
+                t1 = min(T, t0 + GEMV_MAX_T)
+                ops.gemv(w, x.rows(t0, t1) if x is not None else None, t1 - t0, mode, out_q=oq.rows(t0, t1),
+                         xb=None if xb is None else xb[t0:t1])
+            return oq
+        if out is None:
+            out = torch.empty(T, w.N, dtype=torch.bfloat16 if mode == EPI_STORE_BF16 else torch.float32,
+                              device=self.device)
+        for t0 in range(0, T, GEMV_MAX_T):
+            t1 = min(T, t0 + GEMV_MAX_T)
+            ops.gemv(w, x.rows(t0, t1) if x is not None else None, t1 - t0, mode, out=out[t0:t1], bias=bias,
+                     xb=None if xb is None else xb[t0:t1].contiguous())
+        return out
+
+    def _needs_bf16(self, w) -> bool:
+        if isinstance(w, tuple):
+            return any(self._needs_bf16(x) for x in w)
+        return w.wtype == ops.W_BF16
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, inp: StepInput) -> torch.Tensor:
+        """Logits (f32) of the last new token of each sequence: [S, vocab]."""
+        cfg = self.cfg
+        T = inp.ids.numel()
+        H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        x = ops.embed(self.embed_w, inp.ids)
+        for li, L in enumerate(self.layers):
+            kc, vc = self.kv[li]
+            hb, hq = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.qkv))
+            qkv = self._lin_q8(L.qkv, hq, T, EPI_STORE_F32, bias=L.qkv_bias, xb=hb)
+            q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
+                                  cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
+            if inp.decode:
+                ab, aq = ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
+                                              cfg.sliding_window)
+            else:
+                ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
+                                           H, Hkv, D, self.scale, cfg.sliding_window)
+                aq = ops.quantize_q8(ab)
+            self._lin_q8(L.wo, aq, T, EPI_ADD_F32, out=x, xb=ab)
+            if L.moe is not None:
+                hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=True)
+                L.moe.forward(self, hq, hb, T, x)
+                continue
+            down_bf16 = self._needs_bf16(L.down)
+            hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.gate_up))
+            if L.gu_interleaved and not down_bf16:
+                h2 = self._lin_q8(L.gate_up, hq, T, EPI_SWIGLU_Q8)
+                self._lin_q8(L.down, h2, T, EPI_ADD_F32, out=x)
+            else:
+                gu = self._lin_q8(L.gate_up, hq, T, EPI_STORE_F32, xb=hb)
+                if L.gu_interleaved:  # undo the 32-row interleave for the elementwise kernel
+                    gu = gu.view(T, -1, 2, 32).transpose(1, 2).reshape(T, -1).contiguous()
+                hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16)
+                self._lin_q8(L.down, hq2, T, EPI_ADD_F32, out=x, xb=hb2)
+        xl = x.index_select(0, inp.last_idx) if not inp.decode else x
+        _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True)
+        return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32)

@@ -1,0 +1,171 @@
+"""Python wrappers of the sm_100a kernels (``barq_inference_b200._C``).
+
+The extension is built in-tree by ``setup.py build_ext --inplace``.  On a machine with a GPU a
+missing or stale extension is an error (``require_ext``): there is no silent PyTorch fallback.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .qweight import NATIVE, W_BF16, QWeight, cat_rows, interleave_gate_up  # noqa: F401
+
+try:
+    from .. import _C  # type: ignore
+except ImportError as e:  # pragma: no cover - depends on build state
+    _C = None
+    _IMPORT_ERROR = e
+else:
+    _IMPORT_ERROR = None
+
+EPI_STORE_F32, EPI_ADD_F32, EPI_STORE_BF16, EPI_SWIGLU_Q8 = 0, 1, 2, 3
+
+# Number of kernel launches issued through these wrappers (bench.py reports launches per step).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def require_ext():
+    if _C is None:
+        raise RuntimeError(
+            "barq_inference_b200._C is not built; run `python setup.py build_ext --inplace` "
+            f"({_IMPORT_ERROR})")
+    return _C
+
+
+class Q8Act:
+    """int8 activation rows + (scale, scale*sum) per 32 values — the GEMV input format."""
+
+    __slots__ = ("q", "s", "T", "K")
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor, T: int, K: int):
+        self.q, self.s, self.T, self.K = q, s, T, K
+
+    @staticmethod
+    def empty(T: int, K: int, device) -> "Q8Act":
+        return Q8Act(torch.empty(T, K, dtype=torch.int8, device=device),
+                     torch.empty(T, K // 32, 2, dtype=torch.float32, device=device), T, K)
+
+    def rows(self, a: int, b: int) -> "Q8Act":
+        return Q8Act(self.q[a:b], self.s[a:b], b - a, self.K)
+
+
+def quantize_q8(x: torch.Tensor) -> Q8Act:
+    T, K = x.shape
+    out = Q8Act.empty(T, K, x.device)
+    require_ext().quantize_q8(x, T, K, x.stride(0), out.q, out.s)
+    _count()
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, add: torch.Tensor | None = None,
+            want_bf16: bool = False, want_q8: bool = False):
+    """x (f32 [T,H], updated in place by ``add``) -> (bf16 | None, Q8Act | None)."""
+    T, H = x.shape
+    ob = torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None
+    oq = Q8Act.empty(T, H, x.device) if want_q8 else None
+    require_ext().rmsnorm(x, add, w, eps, ob, oq.q if oq else None, oq.s if oq else None)
+    _count()
+    return ob, oq
+
+
+def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
+         xb: torch.Tensor | None = None, bias: torch.Tensor | None = None, out_q: Q8Act | None = None):
+    """Decode GEMV for T <= 8 tokens.  Returns ``out`` (allocated if None for store modes)."""
+    C = require_ext()
+    dev = w.device
+    if mode == EPI_SWIGLU_Q8:
+        F = w.N // 2
+        if out_q is None:
+            out_q = Q8Act.empty(T, F, dev)
+        C.qgemv(*w.args(), x.q if x else None, x.s if x else None, xb, T, mode, None, out, out_q.q, out_q.s, bias, F)
+        _count()
+        return out_q
+    if out is None:
+        dt = torch.bfloat16 if mode == EPI_STORE_BF16 else torch.float32
+        out = torch.empty(T, w.N, dtype=dt, device=dev)
+    ld = out.stride(0)
+    f32 = out if out.dtype == torch.float32 else None
+    bf = out if out.dtype == torch.bfloat16 else None
+    C.qgemv(*w.args(), x.q if x else None, x.s if x else None, xb, T, mode, f32, bf, None, None, bias, ld)
+    _count()
+    return out
+
+
+def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False):
+    T = gu.shape[0]
+    ob = torch.empty(T, F, dtype=torch.bfloat16, device=gu.device) if want_bf16 else None
+    oq = Q8Act.empty(T, F, gu.device) if want_q8 else None
+    require_ext().swiglu(gu, T, F, gu.stride(0), ob, oq.q if oq else None, oq.s if oq else None)
+    _count()
+    return ob, oq
+
+
+def rope_kv_write(qkv, pos, slots, cos_t, sin_t, H, Hkv, D, rot, neox, kcache, vcache,
+                  q_norm=None, k_norm=None, norm_eps=1e-6):
+    T = qkv.shape[0]
+    q_out = torch.empty(T, H, D, dtype=torch.bfloat16, device=qkv.device)
+    require_ext().rope_kv_write(qkv, qkv.stride(0), pos, slots, cos_t, sin_t, q_norm, k_norm, norm_eps,
+                                T, H, Hkv, D, rot, neox, q_out, kcache, vcache)
+    _count()
+    return q_out
+
+
+def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
+    return max(1, min(32, math.ceil(2 * n_sm / max(1, B * Hkv))))
+
+
+def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,
+                     want_q8=True, scratch=None):
+    B = q.shape[0]
+    C = require_ext()
+    if splits is None:
+        splits = decode_splits(B, Hkv)
+    if scratch is None:
+        scratch = torch.empty(C.decode_attention_scratch_floats(B, H, Hkv, D, splits), dtype=torch.float32,
+                              device=q.device)
+    out = torch.empty(B, H * D, dtype=torch.bfloat16, device=q.device)
+    oq = Q8Act.empty(B, H * D, q.device) if want_q8 else None
+    C.decode_attention(q, kcache, vcache, block_tables, seq_lens, B, H, Hkv, D, scale, window, splits, scratch,
+                       out, oq.q if oq else None, oq.s if oq else None)
+    _count(2)
+    return out, oq
+
+
+def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0):
+    T = q.shape[0]
+    S = block_tables.shape[0]
+    out = torch.empty(T, H * D, dtype=torch.bfloat16, device=q.device)
+    require_ext().prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, S, max_q, H, Hkv, D,
+                                    scale, window, out)
+    _count()
+    return out
+
+
+def embed(w: QWeight, ids: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(ids.numel(), w.K, dtype=torch.float32, device=ids.device)
+    require_ext().embed_gather(*w.args(), ids, out)
+    _count()
+    return out
+
+
+def dequant_rows(w: QWeight, r0: int = 0, n: int | None = None) -> torch.Tensor:
+    n = w.N - r0 if n is None else n
+    out = torch.empty(n, w.K, dtype=torch.bfloat16, device=w.device)
+    require_ext().dequant_rows(*w.args(), r0, n, out)
+    return out
+
+
+def sample(logits, temperature, top_k, top_p, min_p, seeds, steps, allow_mask=None, penalties=None,
+           history=None, want_logprob=False):
+    B, V = logits.shape
+    ids = torch.empty(B, dtype=torch.int32, device=logits.device)
+    lp = torch.empty(B, dtype=torch.float32, device=logits.device) if want_logprob else None
+    require_ext().sample(logits, B, V, temperature, top_k, top_p, min_p, seeds, steps, ids, lp, allow_mask,
+                         penalties, history)
+    _count()
+    return ids, lp

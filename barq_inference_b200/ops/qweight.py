@@ -1,0 +1,143 @@
+"""Quantized weights in the kernels' planar layout (see ``csrc/kernels/qweight.cuh``).
+
+``QWeight.from_packed`` splits GGUF blocks into aligned planes on the device without changing a
+bit; ``to_gguf_rows`` re-emits the original blocks (tests check the round trip).  Types without a
+native kernel (Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, IQ4_XS, F16, F32, ...) are dequantized once at load to
+bf16 and use the dense GEMV/GEMM; the reference instead dequantizes *everything* to f32 at load
+(``barq_core/src/gguf.rs:306-311``).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..gguf import TYPE_TRAITS, GGMLType, dequantize
+
+NATIVE = {GGMLType.Q4_0, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q5_K, GGMLType.Q6_K, GGMLType.IQ4_NL}
+W_BF16 = 0
+
+
+def _blocks(raw: torch.Tensor, N: int, t: GGMLType) -> torch.Tensor:
+    ts = TYPE_TRAITS[t].type_size
+    return raw.reshape(N, -1, ts)
+
+
+def _u16(x: torch.Tensor) -> torch.Tensor:
+    """[..., 2] uint8 -> [...] int16 bit pattern (fp16 scales)."""
+    return x.contiguous().view(torch.int16).squeeze(-1)
+
+
+@dataclass
+class QWeight:
+    wtype: int  # GGMLType value for native types, 0 for bf16
+    N: int
+    K: int
+    p0: torch.Tensor
+    p1: torch.Tensor | None = None
+    p2: torch.Tensor | None = None
+    d: torch.Tensor | None = None
+    src_type: GGMLType | None = None
+
+    @property
+    def device(self) -> torch.device:
+        return self.p0.device
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.p0, self.p1, self.p2, self.d) if t is not None)
+
+    def args(self):
+        return (self.wtype, self.N, self.K, self.p0, self.p1, self.p2, self.d)
+
+    @staticmethod
+    def from_packed(raw: torch.Tensor, t: GGMLType, N: int, K: int, device=None) -> "QWeight":
+        """raw: uint8 ``[N, row_bytes]`` GGUF rows (any device)."""
+        t = GGMLType(t)
+        dev = torch.device(device) if device is not None else raw.device
+        raw = raw.to(dev)
+        if t not in NATIVE or K % TYPE_TRAITS[t].block_size:
+            if t == GGMLType.BF16:
+                w = raw.contiguous().view(torch.bfloat16).reshape(N, K)
+            elif t == GGMLType.F16:
+                w = raw.contiguous().view(torch.float16).reshape(N, K).to(torch.bfloat16)
+            elif t == GGMLType.F32:
+                w = raw.contiguous().view(torch.float32).reshape(N, K).to(torch.bfloat16)
+            else:
+                arr = dequantize(raw.cpu().numpy(), t, (N, K))
+                w = torch.from_numpy(arr).to(dev, torch.bfloat16)
+            return QWeight(W_BF16, N, K, w.contiguous().view(torch.uint8), src_type=t)
+        b = _blocks(raw, N, t)
+        c = lambda x: x.contiguous().reshape(N, -1)  # noqa: E731
+        if t in (GGMLType.Q4_0, GGMLType.IQ4_NL):
+            return QWeight(int(t), N, K, c(b[..., 2:18]), d=_u16(b[..., 0:2]).reshape(N, -1).contiguous(), src_type=t)
+        if t == GGMLType.Q8_0:
+            return QWeight(int(t), N, K, c(b[..., 2:34]), d=_u16(b[..., 0:2]).reshape(N, -1).contiguous(), src_type=t)
+        if t == GGMLType.Q4_K:
+            return QWeight(int(t), N, K, c(b[..., 16:144]), p2=c(b[..., 0:16]), src_type=t)
+        if t == GGMLType.Q5_K:
+            return QWeight(int(t), N, K, c(b[..., 48:176]), p1=c(b[..., 16:48]), p2=c(b[..., 0:16]), src_type=t)
+        if t == GGMLType.Q6_K:
+            return QWeight(int(t), N, K, c(b[..., 0:128]), p1=c(b[..., 128:192]), p2=c(b[..., 192:208]),
+                           d=_u16(b[..., 208:210]).reshape(N, -1).contiguous(), src_type=t)
+        raise AssertionError(t)
+
+    def to_gguf_rows(self) -> torch.Tensor:
+        """Inverse of ``from_packed`` for native types: uint8 ``[N, row_bytes]``."""
+        t = GGMLType(self.wtype)
+        N = self.N
+        nbk = lambda x, per: x.reshape(N, -1, per)  # noqa: E731
+        dd = lambda: self.d.contiguous().view(torch.uint8).reshape(N, -1, 2)  # noqa: E731
+        if t in (GGMLType.Q4_0, GGMLType.IQ4_NL):
+            parts = [dd(), nbk(self.p0, 16)]
+        elif t == GGMLType.Q8_0:
+            parts = [dd(), nbk(self.p0, 32)]
+        elif t == GGMLType.Q4_K:
+            parts = [nbk(self.p2, 16), nbk(self.p0, 128)]
+        elif t == GGMLType.Q5_K:
+            parts = [nbk(self.p2, 16), nbk(self.p1, 32), nbk(self.p0, 128)]
+        elif t == GGMLType.Q6_K:
+            parts = [nbk(self.p0, 128), nbk(self.p1, 64), nbk(self.p2, 16), dd()]
+        else:
+            raise ValueError("bf16 weights have no GGUF block form")
+        return torch.cat(parts, -1).reshape(N, -1)
+
+    def select_rows(self, idx: torch.Tensor) -> "QWeight":
+        """Row gather (used to fuse/interleave projections and to shard for tensor parallelism)."""
+        idx = idx.to(self.p0.device)
+        g = lambda x: None if x is None else x.index_select(0, idx).contiguous()  # noqa: E731
+        return QWeight(self.wtype, int(idx.numel()), self.K, g(self.p0), g(self.p1), g(self.p2), g(self.d), self.src_type)
+
+    def col_shard(self, k0: int, k1: int) -> "QWeight":
+        """Columns [k0, k1) (block-aligned) — row-parallel sharding for tensor parallelism."""
+        K = self.K
+        bs = 256 if self.wtype in (12, 13, 14) else (32 if self.wtype else 1)
+        if k0 % bs or k1 % bs:
+            raise ValueError(f"column shard [{k0},{k1}) not aligned to block {bs}")
+        def cs(x):
+            if x is None:
+                return None
+            per = x.shape[1] * (1 if x.dim() == 2 else 1)
+            a, b = k0 * per // K, k1 * per // K
+            return x[:, a:b].contiguous()
+        return QWeight(self.wtype, self.N, k1 - k0, cs(self.p0), cs(self.p1), cs(self.p2), cs(self.d), self.src_type)
+
+
+def cat_rows(ws: list[QWeight]) -> QWeight:
+    t = ws[0].wtype
+    if any(w.wtype != t or w.K != ws[0].K for w in ws):
+        raise ValueError("cat_rows: types or K differ")
+    c = lambda xs: None if xs[0] is None else torch.cat(xs, 0)  # noqa: E731
+    return QWeight(t, sum(w.N for w in ws), ws[0].K, c([w.p0 for w in ws]), c([w.p1 for w in ws]),
+                   c([w.p2 for w in ws]), c([w.d for w in ws]), ws[0].src_type)
+
+
+def interleave_gate_up(gate: QWeight, up: QWeight, group: int = 32) -> QWeight:
+    """Rows ordered [gate 32g..32g+31, up 32g..32g+31] per group (the SwiGLU epilogues' layout)."""
+    if gate.N != up.N or gate.N % group:
+        raise ValueError("interleave_gate_up: N must match and be a multiple of the group")
+    both = cat_rows([gate, up])
+    F = gate.N
+    g = torch.arange(F).view(F // group, 1, group)
+    idx = torch.cat([g, g + F], 1).reshape(-1)
+    return both.select_rows(idx)

@@ -1,0 +1,282 @@
+"""Headline benchmark: Llama-3-8B (Q4_K, Q6_K head), decode tok/s at batch 64 with 1024-token prompts,
+plus prefill tok/s, batch-1 decode tok/s and p50 TTFT of a 512-token prompt — on random-init weights
+and uniform-random prompt ids (no checkpoint or dataset is available offline).
+
+    python bench.py --gpus N --steps K --warmup W           (N > 1: one process per GPU via torchrun)
+    python bench.py --impl reference ...                     (reference arm)
+
+Multi-GPU: every rank is an independent data-parallel engine replica (weak scaling: per-GPU work is
+fixed); the reported value is the whole-job aggregate, timed on the device with CUDA events as the
+max over ranks.  A "step" is one continuous-batching decode step of the engine's public ``step()``
+API: it includes the host->device copy of the step's inputs from pinned memory, the CUDA-graph
+replay (embedding .. sampling) and the device->host read of the sampled ids.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (bs1, bs64) + prefill tok/s + p50 TTFT at 1/2/4/8 B200, max over ranks"
+MODEL = "Llama-3-8B (Q4_K, Q6_K output), random-init"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="barq", choices=["barq", "reference"])
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=1024)
+    ap.add_argument("--ttft-prompt", type=int, default=512)
+    ap.add_argument("--ttft-reps", type=int, default=5)
+    ap.add_argument("--bs1-steps", type=int, default=64)
+    ap.add_argument("--e2e-tokens", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    why = ("the reference (YASSERRMD/barq-inference) is a pure-Rust Cargo workspace with no Python package "
+           "and no Rust toolchain on this image (pip install: 'Neither setup.py nor pyproject.toml found'); "
+           "its CUDA backend launches no kernels (host fallbacks) and has no multi-GPU path")
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from barq_inference_b200 import ops
+    from barq_inference_b200.engine.engine import Engine, EngineConfig
+    from barq_inference_b200.engine.sampling_params import SamplingParams
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+
+    cfg = preset(args.model)
+    if args.layers:
+        cfg.n_layers = args.layers
+    t_init = time.time()
+    tensors = random_tensors(cfg, POLICIES[args.model], seed=0, device=dev)
+    B, P = args.batch, args.prompt_len
+    max_len = P + args.warmup + args.steps + args.e2e_tokens + 64
+    max_len = max(max_len, args.ttft_prompt + args.bs1_steps + 16)
+    max_len = (max_len + 15) // 16 * 16
+    blocks_needed = B * (max_len // 16 + 2) + 64
+    ec = EngineConfig(max_num_seqs=max(B, 1), max_num_batched_tokens=8192, max_model_len=max_len,
+                      num_blocks=blocks_needed, cuda_graphs=True)
+    eng = Engine(cfg, tensors, ec)
+    del tensors
+    torch.cuda.empty_cache()
+    init_s = time.time() - t_init
+    rng = np.random.default_rng(1 + rank)
+    greedy = lambda n: SamplingParams.greedy_params(max_tokens=n, ignore_eos=True)  # noqa: E731
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- (1) TTFT of a 512-token prompt at batch 1, then batch-1 decode
+    ttfts = []
+    for r in range(args.ttft_reps + 1):
+        seq = eng.add_request(rng.integers(0, cfg.vocab, args.ttft_prompt).tolist(), greedy(args.bs1_steps + 2))
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record()
+        while not seq.output:
+            eng.step()
+        e1.record()
+        torch.cuda.synchronize()
+        if r > 0:
+            ttfts.append(e0.elapsed_time(e1))
+        if r < args.ttft_reps:
+            while not seq.finished:
+                eng.step()
+    # seq (last) continues: batch-1 decode
+    for _ in range(4):
+        eng.step()
+    barrier()
+    e0, e1 = ev(), ev()
+    e0.record()
+    n1 = 0
+    while not seq.finished and n1 < args.bs1_steps - 6:
+        eng.step()
+        n1 += 1
+    e1.record()
+    torch.cuda.synchronize()
+    bs1_ms = max_over_ranks(e0.elapsed_time(e1) / max(1, n1))
+    while eng.has_work():
+        eng.step()
+
+    # ---- (2) batch-B prefill of P-token prompts
+    seqs = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), greedy(args.warmup + args.steps + 4))
+            for _ in range(B)]
+    barrier()
+    e0, e1 = ev(), ev()
+    e0.record()
+    while any(not s.output for s in seqs):
+        eng.step()
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # ---- (3) timed decode steps at batch B
+    for _ in range(args.warmup):
+        eng.step()
+    launches0 = ops.LAUNCHES[0]
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    e0, e1 = ev(), ev()
+    e0.record()
+    for _ in range(args.steps):
+        eng.step()
+    e1.record()
+    barrier()
+    ck = clocks.stop()
+    dec_ms = max_over_ranks(e0.elapsed_time(e1))
+    while eng.has_work():
+        eng.step()
+    # kernel launches per decode step: one eager (non-graph) forward of the same batch, counted
+    eng.ecfg.cuda_graphs = False
+    probe = [eng.add_request(rng.integers(0, cfg.vocab, 16).tolist(), greedy(3)) for _ in range(B)]
+    while any(not s.output for s in probe):
+        eng.step()
+    c0 = ops.LAUNCHES[0]
+    eng.step()
+    launches_per_step = ops.LAUNCHES[0] - c0
+    while eng.has_work():
+        eng.step()
+    eng.ecfg.cuda_graphs = True
+
+    # ---- (4) end to end through the public generate() API (host clock, includes H2D + D2H every step)
+    prompts = [rng.integers(0, cfg.vocab, P).tolist() for _ in range(B)]
+    eng.timings = {k: 0 for k in eng.timings}
+    barrier()
+    t0 = time.perf_counter()
+    res = eng.generate(prompts, greedy(args.e2e_tokens))
+    torch.cuda.synchronize()
+    t_e2e = time.perf_counter() - t0
+    e2e_dec = eng.timings["decode_tokens"] / max(1e-9, eng.timings["decode_s"])
+    e2e_dec = max_over_ranks(-e2e_dec) * -1 if world > 1 else e2e_dec  # slowest rank
+    mb = eng.max_blocks_per_seq
+    h2d = B * (4 + 4 + 8 + 4 + 4 * mb + 4 + 4 + 4 + 4 + 8 + 4)
+    d2h = B * 4
+
+    if rank == 0:
+        value = world * B * args.steps / (dec_ms / 1e3)
+        out = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tokens/s (decode, batch %d per GPU, aggregate)" % B,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dec_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16/fp32 compute on Q4_K/Q6_K weights, int8 decode activations, fp16 KV",
+            "data": "synthetic: random-init N(0,0.02) weights quantized to Q4_K/Q6_K, uniform-random prompt ids",
+            "config": {"model": MODEL + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * world,
+                       "seq_len": P, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)"},
+            "extra": {
+                "decode_tok_s_bs1": round(world * 1e3 / bs1_ms, 2),
+                "prefill_tok_s": round(world * B * P / (prefill_ms / 1e3), 1),
+                "ttft_p50_ms_512": round(statistics.median(ttfts), 3) if ttfts else None,
+                "init_s": round(init_s, 1),
+            },
+            "e2e": {"value": round(world * e2e_dec, 2), "unit": "tokens/s decode via Engine.generate()",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "wall_s": round(t_e2e, 3), "tokens": sum(len(r.tokens) for r in res)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": ck,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

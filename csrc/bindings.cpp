@@ -1,0 +1,200 @@
+// Torch bindings for the barq sm_100a kernels.  Every op checks device, dtype and contiguity and
+// raises on a bad launch status; there is no CPU or library fallback behind these entry points.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels/launch.h"
+
+using torch::Tensor;
+using OptT = c10::optional<Tensor>;
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda() && (t).is_contiguous(), #t " must be a contiguous CUDA tensor")
+
+template <typename T> T* ptr(const Tensor& t) { return reinterpret_cast<T*>(t.data_ptr()); }
+template <typename T> T* optptr(const OptT& t) { return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr; }
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, ": launch rejected with status ", rc);
+  cudaError_t e = cudaPeekAtLastError();
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+barq::QW make_qw(int64_t type, int64_t N, int64_t K, const Tensor& p0, const OptT& p1, const OptT& p2, const OptT& d) {
+  CHECK_CUDA(p0);
+  barq::QW w;
+  w.p0 = ptr<const uint8_t>(p0);
+  w.p1 = optptr<const uint8_t>(p1);
+  w.p2 = optptr<const uint8_t>(p2);
+  w.d = optptr<const uint16_t>(d);
+  w.N = (int)N;
+  w.K = (int)K;
+  w.type = (int)type;
+  return w;
+}
+
+void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, OptT xq, OptT xs, OptT xb,
+           int64_t B, int64_t mode, OptT out_f32, OptT out_bf16, OptT out_q, OptT out_s, OptT bias, int64_t ld_out) {
+  c10::cuda::CUDAGuard g(p0.device());
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  barq::ActQ8 x{optptr<const int8_t>(xq), optptr<const float2>(xs)};
+  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q),
+                   optptr<float2>(out_s), optptr<const float>(bias), (int)ld_out};
+  int ldxb = (int)K;
+  check(barq::qgemv(w, x, optptr<const __nv_bfloat16>(xb), ldxb, (int)B, ep, cur_stream()), "qgemv");
+}
+
+void rmsnorm(Tensor x, OptT add, Tensor w, double eps, OptT out_bf16, OptT out_q, OptT out_s) {
+  CHECK_CUDA(x);
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32, "rmsnorm: residual stream must be f32");
+  int H = (int)x.size(-1), T = (int)(x.numel() / H);
+  check(barq::rmsnorm(ptr<float>(x), optptr<const float>(add), ptr<const float>(w), (float)eps, T, H,
+                      optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q), optptr<float2>(out_s), cur_stream()),
+        "rmsnorm");
+}
+
+void quantize_q8(Tensor x, int64_t T, int64_t H, int64_t ldx, Tensor out_q, Tensor out_s) {
+  c10::cuda::CUDAGuard g(x.device());
+  check(barq::quantize_q8(x.data_ptr(), x.scalar_type() == torch::kBFloat16, (int)T, (int)H, (int)ldx,
+                          ptr<int8_t>(out_q), ptr<float2>(out_s), cur_stream()),
+        "quantize_q8");
+}
+
+void swiglu(Tensor in, int64_t T, int64_t F, int64_t ld_in, OptT out_bf16, OptT out_q, OptT out_s) {
+  c10::cuda::CUDAGuard g(in.device());
+  check(barq::swiglu(in.data_ptr(), in.scalar_type() == torch::kBFloat16, (int)T, (int)F, (int)ld_in,
+                     optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q), optptr<float2>(out_s), cur_stream()),
+        "swiglu");
+}
+
+void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor cos_t, Tensor sin_t, OptT q_norm,
+                   OptT k_norm, double norm_eps, int64_t T, int64_t H, int64_t Hkv, int64_t D, int64_t rot,
+                   bool neox, Tensor q_out, Tensor kcache, Tensor vcache) {
+  c10::cuda::CUDAGuard g(qkv.device());
+  barq::RopeKVArgs a;
+  a.qkv = qkv.data_ptr();
+  a.qkv_is_bf16 = qkv.scalar_type() == torch::kBFloat16;
+  a.ld_qkv = (int)ld_qkv;
+  a.pos = ptr<const int>(pos);
+  a.slots = optptr<const int64_t>(slots);
+  a.cos_t = ptr<const float>(cos_t);
+  a.sin_t = ptr<const float>(sin_t);
+  a.q_norm = optptr<const float>(q_norm);
+  a.k_norm = optptr<const float>(k_norm);
+  a.norm_eps = (float)norm_eps;
+  a.T = (int)T; a.H = (int)H; a.Hkv = (int)Hkv; a.D = (int)D; a.rot = (int)rot; a.neox = neox;
+  a.q_out = ptr<__nv_bfloat16>(q_out);
+  a.kcache = kcache.data_ptr();
+  a.vcache = vcache.data_ptr();
+  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.block_size = (int)kcache.size(-2);
+  check(barq::rope_kv_write(a, cur_stream()), "rope_kv_write");
+}
+
+void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor seq_lens, int64_t B,
+                      int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window, int64_t splits, Tensor scratch,
+                      Tensor out, OptT out_q, OptT out_s) {
+  c10::cuda::CUDAGuard g(q.device());
+  TORCH_CHECK(scratch.scalar_type() == torch::kFloat32, "scratch must be f32");
+  size_t need = barq::decode_attention_scratch_floats((int)B, (int)H, (int)Hkv, (int)D, (int)splits);
+  TORCH_CHECK((size_t)scratch.numel() >= need, "decode_attention: scratch too small (", scratch.numel(), " < ", need, ")");
+  barq::DecodeAttnArgs a;
+  a.q = ptr<const __nv_bfloat16>(q);
+  a.kcache = kcache.data_ptr();
+  a.vcache = vcache.data_ptr();
+  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.block_tables = ptr<const int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.seq_lens = ptr<const int>(seq_lens);
+  a.B = (int)B; a.H = (int)H; a.Hkv = (int)Hkv; a.D = (int)D;
+  a.block_size = (int)kcache.size(-2);
+  a.scale = (float)scale;
+  a.window = (int)window;
+  a.splits = (int)splits;
+  a.part_acc = ptr<float>(scratch);
+  a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)B * H * splits * D);
+  a.out = ptr<__nv_bfloat16>(out);
+  a.out_q = optptr<int8_t>(out_q);
+  a.out_s = optptr<float2>(out_s);
+  check(barq::decode_attention(a, cur_stream()), "decode_attention");
+}
+
+void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor q_start, Tensor ctx_lens,
+                       int64_t S, int64_t max_q, int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window,
+                       Tensor out) {
+  c10::cuda::CUDAGuard g(q.device());
+  barq::PrefillAttnArgs a;
+  a.q = ptr<const __nv_bfloat16>(q);
+  a.kcache = kcache.data_ptr();
+  a.vcache = vcache.data_ptr();
+  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.block_tables = ptr<const int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.q_start = ptr<const int>(q_start);
+  a.ctx_lens = ptr<const int>(ctx_lens);
+  a.S = (int)S; a.max_q = (int)max_q; a.H = (int)H; a.Hkv = (int)Hkv; a.D = (int)D;
+  a.block_size = (int)kcache.size(-2);
+  a.scale = (float)scale;
+  a.window = (int)window;
+  a.out = ptr<__nv_bfloat16>(out);
+  check(barq::prefill_attention(a, cur_stream()), "prefill_attention");
+}
+
+void embed_gather(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor ids, Tensor out) {
+  c10::cuda::CUDAGuard g(p0.device());
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  check(barq::embed_gather(w, ptr<const int>(ids), (int)ids.numel(), ptr<float>(out), cur_stream()), "embed_gather");
+}
+
+void dequant_rows(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, int64_t r0, int64_t n,
+                  Tensor out) {
+  c10::cuda::CUDAGuard g(p0.device());
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  check(barq::dequant_rows(w, (int)r0, (int)n, ptr<__nv_bfloat16>(out), cur_stream()), "dequant_rows");
+}
+
+void sample(Tensor logits, int64_t B, int64_t V, Tensor temperature, Tensor top_k, Tensor top_p, Tensor min_p,
+            Tensor seeds, Tensor steps, Tensor out_ids, OptT out_logprob, OptT allow_mask, OptT penalties,
+            OptT history) {
+  c10::cuda::CUDAGuard g(logits.device());
+  barq::SampleArgs a;
+  a.logits = ptr<const float>(logits);
+  a.B = (int)B; a.V = (int)V; a.ld = (int)logits.size(-1);
+  a.temperature = ptr<const float>(temperature);
+  a.top_k = ptr<const int>(top_k);
+  a.top_p = ptr<const float>(top_p);
+  a.min_p = ptr<const float>(min_p);
+  a.seeds = reinterpret_cast<const uint64_t*>(seeds.data_ptr());
+  a.steps = ptr<const int>(steps);
+  a.out_ids = ptr<int>(out_ids);
+  a.out_logprob = optptr<float>(out_logprob);
+  a.allow_mask = optptr<const uint32_t>(allow_mask);
+  a.penalties = optptr<const float>(penalties);
+  a.pen_counts_idx = optptr<const int>(history);
+  a.max_hist = history.has_value() ? (int)history->size(-1) : 0;
+  check(barq::sample_tokens(a, cur_stream()), "sample");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "barq sm_100a kernels";
+  m.def("qgemv", &qgemv);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("quantize_q8", &quantize_q8);
+  m.def("swiglu", &swiglu);
+  m.def("rope_kv_write", &rope_kv_write);
+  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention_scratch_floats", [](int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t s) {
+    return (int64_t)barq::decode_attention_scratch_floats((int)B, (int)H, (int)Hkv, (int)D, (int)s);
+  });
+  m.def("prefill_attention", &prefill_attention);
+  m.def("embed_gather", &embed_gather);
+  m.def("dequant_rows", &dequant_rows);
+  m.def("sample", &sample);
+}

@@ -4,17 +4,12 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include "qweight.cuh"
 
 #define BARQ_DEV __device__ __forceinline__
 
 namespace barq {
 
-// Activation in the "q8" layout consumed by the dp4a GEMV kernels: per token row of K values,
-// int8 qs[K] and one float2 (scale d, d * sum(qs)) per 32 values.
-struct ActQ8 {
-  const int8_t* q;   // [B, K]
-  const float2* s;   // [B, K/32]
-};
 
 BARQ_DEV float warp_sum(float v) {
 #pragma unroll
@@ -50,10 +45,10 @@ template <> BARQ_DEV __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __flo
 template <> BARQ_DEV __half from_f<__half>(float v) { return __float2half(v); }
 
 BARQ_DEV int4 ldg16(const void* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
-// Streaming (evict-first) 16-byte load for weights that are read exactly once per step.
+// Streaming 16-byte load (no L1 allocation) for weights that are read exactly once per step.
 BARQ_DEV int4 ldg16_stream(const void* p) {
   int4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v4.s32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }

@@ -1,0 +1,228 @@
+// K11 pieces and small fused ops: residual-add + RMSNorm (-> bf16 / int8 q8), activation
+// quantization, SwiGLU, RoPE + paged KV write, embedding gather, row dequantization.
+//
+// Parity: the reference's rms_norm / rope / SwiGLU run as separate f32 CPU loops
+// (models/src/transformer.rs:148-172, 378-408, 514-568); here they are fused into the producers
+// and consumers of each GEMV/GEMM so the residual stream is touched once per sub-layer.
+#include "common.cuh"
+#include "launch.h"
+#include "qweight.cuh"
+
+namespace barq {
+
+// One CTA per token row.  blockDim = 256.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
+                                                      const float* __restrict__ w, float eps, int H,
+                                                      __nv_bfloat16* __restrict__ ob, int8_t* __restrict__ oq,
+                                                      float2* __restrict__ os) {
+  const int t = blockIdx.x;
+  float* xr = x + (size_t)t * H;
+  const float* ar = add ? add + (size_t)t * H : nullptr;
+  __shared__ float red[8];
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += 256) {
+    float v = xr[i];
+    if (ar) {
+      v += ar[i];
+      xr[i] = v;
+    }
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0] / (float)H + eps);
+  // Each warp walks 32-value groups so the q8 quantization of a group happens inside one warp.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ngroups = (H + 31) / 32;
+  for (int g = warp; g < ngroups; g += 8) {
+    int i = g * 32 + lane;
+    float v = i < H ? xr[i] * r * w[i] : 0.f;
+    if (ob && i < H) ob[(size_t)t * H + i] = __float2bfloat16(v);
+    if (oq) {
+      float d, s;
+      int8_t q = quant_lane32(v, d, s);
+      if (i < H) oq[(size_t)t * H + i] = q;
+      if (lane == 0) os[(size_t)t * (H / 32) + g] = make_float2(d, s);
+    }
+  }
+}
+
+int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
+            int8_t* out_q, float2* out_s, cudaStream_t st) {
+  if (out_q && (H % 32)) return -1;
+  if (T <= 0) return 0;
+  rmsnorm_kernel<<<T, 256, 0, st>>>(x, add, w, eps, H, out_bf16, out_q, out_s);
+  return 0;
+}
+
+template <typename T>
+__global__ void quant_q8_kernel(const T* __restrict__ x, int H, int ldx, int8_t* __restrict__ oq,
+                                float2* __restrict__ os) {
+  const int t = blockIdx.y;
+  const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (g * 32 >= H) return;
+  float v = to_f(x[(size_t)t * ldx + g * 32 + lane]);
+  float d, s;
+  int8_t q = quant_lane32(v, d, s);
+  oq[(size_t)t * H + g * 32 + lane] = q;
+  if (lane == 0) os[(size_t)t * (H / 32) + g] = make_float2(d, s);
+}
+
+int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, int8_t* out_q, float2* out_s,
+                cudaStream_t st) {
+  if (H % 32) return -1;
+  if (T <= 0) return 0;
+  dim3 g((H / 32 + 7) / 8, T);
+  if (x_is_bf16)
+    quant_q8_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)x, H, ldx, out_q, out_s);
+  else
+    quant_q8_kernel<float><<<g, 256, 0, st>>>((const float*)x, H, ldx, out_q, out_s);
+  return 0;
+}
+
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, __nv_bfloat16* __restrict__ ob,
+                              int8_t* __restrict__ oq, float2* __restrict__ os) {
+  const int t = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int i = g * 32 + lane;
+  if (g * 32 >= F) return;
+  float h = 0.f;
+  if (i < F) h = silu(to_f(in[(size_t)t * ld + i])) * to_f(in[(size_t)t * ld + F + i]);
+  if (ob && i < F) ob[(size_t)t * F + i] = __float2bfloat16(h);
+  if (oq) {
+    float d, s;
+    int8_t q = quant_lane32(h, d, s);
+    oq[(size_t)t * F + i] = q;
+    if (lane == 0) os[(size_t)t * (F / 32) + g] = make_float2(d, s);
+  }
+}
+
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, int8_t* out_q,
+           float2* out_s, cudaStream_t st) {
+  if (out_q && (F % 32)) return -1;
+  if (T <= 0) return 0;
+  dim3 g(((F + 31) / 32 + 7) / 8, T);
+  if (in_is_bf16)
+    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_bf16, out_q, out_s);
+  else
+    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_bf16, out_q, out_s);
+  return 0;
+}
+
+// ------------------------------------------------------------------------------ RoPE + KV write
+// One CTA per token, one warp per head (q heads first, then k heads, then v heads).
+template <typename TIN, typename TC>
+__global__ void __launch_bounds__(256) rope_kv_kernel(RopeKVArgs a) {
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nh = a.H + 2 * a.Hkv;
+  const TIN* row = reinterpret_cast<const TIN*>(a.qkv) + (size_t)t * a.ld_qkv;
+  const int pos = a.pos[t];
+  const int64_t slot = a.slots ? a.slots[t] : -1;
+  const int D = a.D, half = a.rot / 2;
+  const float* cs = a.cos_t + (size_t)pos * half;
+  const float* sn = a.sin_t + (size_t)pos * half;
+  for (int h = warp + blockIdx.y * 8; h < nh; h += 8 * gridDim.y) {
+    const TIN* src = row + (size_t)h * D;
+    const bool is_q = h < a.H, is_k = !is_q && h < a.H + a.Hkv;
+    // Load the head (D <= 256) into registers: lane owns elements lane + 32*j.
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int i = lane + 32 * j;
+      v[j] = i < D ? to_f(src[i]) : 0.f;
+    }
+    const float* nw = is_q ? a.q_norm : (is_k ? a.k_norm : nullptr);
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+      ss = warp_sum(ss);
+      float r = rsqrtf(ss / D + a.norm_eps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int i = lane + 32 * j;
+        if (i < D) v[j] = v[j] * r * nw[i];
+      }
+    }
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = v[j];
+    if (is_q || is_k) {
+      // Rotate pairs: neox (i, i+half) or normal (2i, 2i+1); partner values fetched by shuffle
+      // through a shared staging row.
+      __shared__ float stage[8][256];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int i = lane + 32 * j;
+        if (i < D) stage[warp][i] = v[j];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int i = lane + 32 * j;
+        if (i < a.rot) {
+          int pi, fi;
+          float sign;
+          if (a.neox) {
+            fi = i < half ? i : i - half;
+            pi = i < half ? i + half : i - half;
+            sign = i < half ? -1.f : 1.f;
+          } else {
+            fi = i >> 1;
+            pi = i ^ 1;
+            sign = (i & 1) ? 1.f : -1.f;
+          }
+          float c = cs[fi], s = sn[fi];
+          o[j] = v[j] * c + sign * stage[warp][pi] * s;
+        }
+      }
+      __syncwarp();
+    }
+    if (is_q) {
+      __nv_bfloat16* dst = a.q_out + ((size_t)t * a.H + h) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int i = lane + 32 * j;
+        if (i < D) dst[i] = __float2bfloat16(o[j]);
+      }
+    } else if (slot >= 0) {
+      const int kvh = is_k ? h - a.H : h - a.H - a.Hkv;
+      const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+      TC* cache = reinterpret_cast<TC*>(is_k ? a.kcache : a.vcache);
+      TC* dst = cache + (((size_t)blk * a.Hkv + kvh) * a.block_size + off) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int i = lane + 32 * j;
+        if (i < D) dst[i] = from_f<TC>(o[j]);
+      }
+    }
+  }
+}
+
+int rope_kv_write(const RopeKVArgs& a, cudaStream_t st) {
+  if (a.D > 256 || a.rot > a.D || (a.rot & 1)) return -1;
+  if (a.T <= 0) return 0;
+  const int nh = a.H + 2 * a.Hkv;
+  dim3 g(a.T, (nh + 7) / 8 > 4 ? 4 : (nh + 7) / 8);
+  if (a.qkv_is_bf16) {
+    if (a.cache_is_bf16) rope_kv_kernel<__nv_bfloat16, __nv_bfloat16><<<g, 256, 0, st>>>(a);
+    else rope_kv_kernel<__nv_bfloat16, __half><<<g, 256, 0, st>>>(a);
+  } else {
+    if (a.cache_is_bf16) rope_kv_kernel<float, __nv_bfloat16><<<g, 256, 0, st>>>(a);
+    else rope_kv_kernel<float, __half><<<g, 256, 0, st>>>(a);
+  }
+  return 0;
+}
+
+}  // namespace barq

@@ -1,0 +1,220 @@
+// Per-type "part" traits for the dp4a quantized GEMV (decode, 1..8 tokens).
+//
+// A part is 32 weights of one row.  Lane l of a warp owns parts l, l+32, l+64, ... of the row, so
+// a warp's 32 loads of a part-plane are one contiguous 512-byte span (fully coalesced) and, because
+// 32 is a multiple of 8, a lane's position inside a 256-weight super-block is the same for every
+// part it visits.  Activations are int8 with one (scale, scale*sum) pair per 32 values (ActQ8).
+#pragma once
+#include "common.cuh"
+#include "qweight.cuh"
+
+namespace barq {
+
+BARQ_DEV int4 ld_x16(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }
+
+BARQ_DEV int dot16(int4 w, int4 x) {
+  int s = dp4a(w.x, x.x, 0);
+  s = dp4a(w.y, x.y, s);
+  s = dp4a(w.z, x.z, s);
+  return dp4a(w.w, x.w, s);
+}
+
+BARQ_DEV int4 nib_lo(int4 q) {
+  return make_int4(q.x & 0x0F0F0F0F, q.y & 0x0F0F0F0F, q.z & 0x0F0F0F0F, q.w & 0x0F0F0F0F);
+}
+BARQ_DEV int4 nib_hi(int4 q) {
+  return make_int4((q.x >> 4) & 0x0F0F0F0F, (q.y >> 4) & 0x0F0F0F0F, (q.z >> 4) & 0x0F0F0F0F,
+                   (q.w >> 4) & 0x0F0F0F0F);
+}
+BARQ_DEV int4 vsub4(int4 q, int c) {
+  return make_int4(__vsub4(q.x, c), __vsub4(q.y, c), __vsub4(q.z, c), __vsub4(q.w, c));
+}
+
+// 4-bit code -> signed int8 through a 16-entry byte table (IQ4_NL codebook), four codes per word.
+// The 16 table bytes live in t0..t3; PRMT selects bytes 0-7 of a register pair, so the low and
+// high halves of the table are looked up separately and merged by each code's bit 3.
+BARQ_DEV int lut16(int codes /* 4 bytes, each 0..15 */, int t0, int t1, int t2, int t3) {
+  uint32_t c = (uint32_t)codes;
+  uint32_t n = (c | (c >> 4));
+  uint32_t sel = (n & 0xFFu) | ((n >> 8) & 0xFF00u);  // code_i in nibble i
+  uint32_t lo = __byte_perm(t0, t1, sel & 0x7777u);
+  uint32_t hi = __byte_perm(t2, t3, sel & 0x7777u);
+  uint32_t pick = 0x3210u | ((sel & 0x8888u) >> 1);
+  return (int)__byte_perm(lo, hi, pick);
+}
+
+// Unpack 6-bit (scale, min) number `is` (0..7) of the 12-byte K-quant scale field.
+BARQ_DEV void kscale(uint32_t s0, uint32_t s1, uint32_t s2, int is, int& sc, int& m) {
+  uint32_t b[12];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    b[i] = (s0 >> (8 * i)) & 0xFF;
+    b[4 + i] = (s1 >> (8 * i)) & 0xFF;
+    b[8 + i] = (s2 >> (8 * i)) & 0xFF;
+  }
+  if (is < 4) {
+    sc = b[is] & 63;
+    m = b[is + 4] & 63;
+  } else {
+    sc = (b[is + 4] & 0xF) | ((b[is - 4] >> 6) << 4);
+    m = (b[is + 4] >> 4) | ((b[is] >> 6) << 4);
+  }
+}
+
+// ---------------------------------------------------------------- Q4_0 / IQ4_NL (32-weight blocks)
+template <bool NL>
+struct T4Block {
+  struct W { int4 q; float d; };
+  struct X { int4 a, b; float d; };
+  static BARQ_DEV W load_w(const QW& w, int row, int p) {
+    W r;
+    r.q = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
+    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 32) + p));
+    return r;
+  }
+  static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
+    X x;
+    x.a = ld_x16(xq + 32 * p);
+    x.b = ld_x16(xq + 32 * p + 16);
+    x.d = xs[p].x;
+    return x;
+  }
+  static BARQ_DEV float dot(const W& w, const X& x, int /*lane*/) {
+    int4 lo = nib_lo(w.q), hi = nib_hi(w.q);
+    if (NL) {
+      const int t0 = 0xBFAD9881, t1 = 0xF6EADDCF, t2 = 0x26190D01, t3 = 0x71594535;
+      lo = make_int4(lut16(lo.x, t0, t1, t2, t3), lut16(lo.y, t0, t1, t2, t3), lut16(lo.z, t0, t1, t2, t3),
+                     lut16(lo.w, t0, t1, t2, t3));
+      hi = make_int4(lut16(hi.x, t0, t1, t2, t3), lut16(hi.y, t0, t1, t2, t3), lut16(hi.z, t0, t1, t2, t3),
+                     lut16(hi.w, t0, t1, t2, t3));
+    } else {
+      lo = vsub4(lo, 0x08080808);
+      hi = vsub4(hi, 0x08080808);
+    }
+    int s = dot16(lo, x.a) + dot16(hi, x.b);
+    return w.d * x.d * (float)s;
+  }
+};
+
+// ---------------------------------------------------------------- Q8_0
+struct TQ8_0 {
+  struct W { int4 a, b; float d; };
+  struct X { int4 a, b; float d; };
+  static BARQ_DEV W load_w(const QW& w, int row, int p) {
+    W r;
+    const uint8_t* base = w.p0 + (size_t)row * w.K + (size_t)p * 32;
+    r.a = ldg16_stream(base);
+    r.b = ldg16_stream(base + 16);
+    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 32) + p));
+    return r;
+  }
+  static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
+    X x;
+    x.a = ld_x16(xq + 32 * p);
+    x.b = ld_x16(xq + 32 * p + 16);
+    x.d = xs[p].x;
+    return x;
+  }
+  static BARQ_DEV float dot(const W& w, const X& x, int) {
+    return w.d * x.d * (float)(dot16(w.a, x.a) + dot16(w.b, x.b));
+  }
+};
+
+// ---------------------------------------------------------------- Q4_K / Q5_K
+// Part p of a super-block b: j = (p%8)/2 selects the 32-byte qs chunk (sub-blocks 2j and 2j+1),
+// h = p%2 its 16-byte half: low nibbles are weights 64j+16h+[0,16), high nibbles 64j+32+16h+[0,16).
+template <bool FIVE>
+struct TK45 {
+  struct W { int4 q; int4 hdr; int4 qh; };
+  struct X { int4 a, b; float2 sa, sb; };
+  static BARQ_DEV W load_w(const QW& w, int row, int p) {
+    W r;
+    int b = p >> 3;
+    r.q = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
+    r.hdr = ldg16(w.p2 + ((size_t)row * (w.K / 256) + b) * 16);
+    if (FIVE) r.qh = ldg16(w.p1 + (size_t)row * (w.K / 8) + (size_t)b * 32 + (p & 1) * 16);
+    return r;
+  }
+  static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
+    int b = p >> 3, j = (p & 7) >> 1, h = p & 1;
+    X x;
+    x.a = ld_x16(xq + 256 * b + 64 * j + 16 * h);
+    x.b = ld_x16(xq + 256 * b + 64 * j + 32 + 16 * h);
+    x.sa = xs[8 * b + 2 * j];
+    x.sb = xs[8 * b + 2 * j + 1];
+    return x;
+  }
+  static BARQ_DEV float dot(const W& w, const X& x, int lane) {
+    int j = (lane & 7) >> 1, h = lane & 1;
+    int4 lo = nib_lo(w.q), hi = nib_hi(w.q);
+    if (FIVE) {
+      int sl = 2 * j, sh = 2 * j + 1;
+      lo.x |= ((w.qh.x >> sl) & 0x01010101) << 4;
+      lo.y |= ((w.qh.y >> sl) & 0x01010101) << 4;
+      lo.z |= ((w.qh.z >> sl) & 0x01010101) << 4;
+      lo.w |= ((w.qh.w >> sl) & 0x01010101) << 4;
+      hi.x |= ((w.qh.x >> sh) & 0x01010101) << 4;
+      hi.y |= ((w.qh.y >> sh) & 0x01010101) << 4;
+      hi.z |= ((w.qh.z >> sh) & 0x01010101) << 4;
+      hi.w |= ((w.qh.w >> sh) & 0x01010101) << 4;
+    }
+    int s0 = dot16(lo, x.a), s1 = dot16(hi, x.b);
+    uint32_t dm = (uint32_t)w.hdr.x;
+    float d = h2f(dm & 0xFFFF), dmin = h2f(dm >> 16);
+    int sc0, m0, sc1, m1;
+    kscale(w.hdr.y, w.hdr.z, w.hdr.w, 2 * j, sc0, m0);
+    kscale(w.hdr.y, w.hdr.z, w.hdr.w, 2 * j + 1, sc1, m1);
+    float r = d * ((float)sc0 * x.sa.x * (float)s0 + (float)sc1 * x.sb.x * (float)s1);
+    if (h == 0) r -= dmin * ((float)m0 * x.sa.y + (float)m1 * x.sb.y);
+    return r;
+  }
+};
+
+// ---------------------------------------------------------------- Q6_K
+// Part (n, c, h) = p%8 as n*4 + c*2 + h: ql chunk [64n + 32c + 16h, +16): low nibbles are weights
+// 128n + 32c + 16h + [0,16), high nibbles the same +64; qh bytes [32n + 16h, +16) bits 2c / 4+2c.
+struct TQ6_K {
+  struct W { int4 ql, qh; uint32_t sc; float d; };
+  struct X { int4 a, b; float da, db; };
+  static BARQ_DEV W load_w(const QW& w, int row, int p) {
+    W r;
+    int b = p >> 3, q = p & 7, n = q >> 2, c = (q >> 1) & 1, h = q & 1;
+    r.ql = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
+    r.qh = ldg16(w.p1 + (size_t)row * (w.K / 4) + (size_t)b * 64 + 32 * n + 16 * h);
+    const int8_t* sc = reinterpret_cast<const int8_t*>(w.p2) + (size_t)row * (w.K / 16) + (size_t)b * 16;
+    int lo = __ldg(sc + 8 * n + 2 * c + h), hi = __ldg(sc + 8 * n + 4 + 2 * c + h);
+    r.sc = (uint32_t)(lo & 0xFFFF) | ((uint32_t)hi << 16);
+    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 256) + b));
+    return r;
+  }
+  static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
+    int b = p >> 3, q = p & 7, n = q >> 2, c = (q >> 1) & 1, h = q & 1;
+    int e = 256 * b + 128 * n + 32 * c + 16 * h;
+    X x;
+    x.a = ld_x16(xq + e);
+    x.b = ld_x16(xq + e + 64);
+    x.da = xs[8 * b + 4 * n + c].x;
+    x.db = xs[8 * b + 4 * n + 2 + c].x;
+    return x;
+  }
+  static BARQ_DEV float dot(const W& w, const X& x, int lane) {
+    int c = (lane >> 1) & 1;
+    int s_lo = 2 * c, s_hi = 4 + 2 * c;
+    int4 lo = nib_lo(w.ql), hi = nib_hi(w.ql);
+    lo.x |= ((w.qh.x >> s_lo) & 0x03030303) << 4;
+    lo.y |= ((w.qh.y >> s_lo) & 0x03030303) << 4;
+    lo.z |= ((w.qh.z >> s_lo) & 0x03030303) << 4;
+    lo.w |= ((w.qh.w >> s_lo) & 0x03030303) << 4;
+    hi.x |= ((w.qh.x >> s_hi) & 0x03030303) << 4;
+    hi.y |= ((w.qh.y >> s_hi) & 0x03030303) << 4;
+    hi.z |= ((w.qh.z >> s_hi) & 0x03030303) << 4;
+    hi.w |= ((w.qh.w >> s_hi) & 0x03030303) << 4;
+    lo = vsub4(lo, 0x20202020);
+    hi = vsub4(hi, 0x20202020);
+    int sa = dot16(lo, x.a), sb = dot16(hi, x.b);
+    float sc_lo = (float)(int16_t)(w.sc & 0xFFFF), sc_hi = (float)(int16_t)(w.sc >> 16);
+    return w.d * (sc_lo * x.da * (float)sa + sc_hi * x.db * (float)sb);
+  }
+};
+
+}  // namespace barq

@@ -1,0 +1,122 @@
+// Host-side launch API of the barq sm_100a kernels (plain C++ types, no torch headers), so each
+// .cu file compiles quickly and the torch binding layer stays in one translation unit.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include "qweight.cuh"
+
+namespace barq {
+
+enum EpiMode : int { EPI_STORE_F32 = 0, EPI_ADD_F32 = 1, EPI_STORE_BF16 = 2, EPI_SWIGLU_Q8 = 3 };
+
+struct GemvEpi {
+  int mode;
+  float* out_f32;
+  __nv_bfloat16* out_bf16;
+  int8_t* out_q;
+  float2* out_s;
+  const float* bias;
+  int ld_out;
+};
+
+// K1 quantized GEMV, B <= 8 tokens.  xb/ldxb are only read for bf16 weights.
+int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B, const GemvEpi& ep,
+          cudaStream_t st);
+
+// Fused (residual add +) RMSNorm.  x: f32 [T, H] residual stream (updated in place when `add`
+// is given: x += add).  Outputs any of bf16 [T, H] and int8 q8 [T, H] + scales [T, H/32].
+int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
+            int8_t* out_q, float2* out_s, cudaStream_t st);
+
+// Quantize bf16 or f32 rows to the q8 activation layout (H % 32 == 0).
+int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, int8_t* out_q, float2* out_s,
+                cudaStream_t st);
+
+// h = silu(g) * u with g = in[t, i], u = in[t, F + i] (f32 or bf16 input) -> bf16 and/or q8.
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, int8_t* out_q,
+           float2* out_s, cudaStream_t st);
+
+struct RopeKVArgs {
+  const void* qkv;       // [T, (H + 2*Hkv) * D]  f32 or bf16
+  int qkv_is_bf16;
+  int ld_qkv;            // elements per token row
+  const int* pos;        // [T]
+  const int64_t* slots;  // [T] physical slot = block * block_size + offset (-1 = skip)
+  const float* cos_t;    // [max_pos, rot/2]
+  const float* sin_t;
+  const float* q_norm;   // optional [D] (Qwen3 QK-norm)
+  const float* k_norm;
+  float norm_eps;
+  int T, H, Hkv, D, rot, neox;
+  __nv_bfloat16* q_out;  // [T, H, D]
+  void* kcache;          // [num_blocks, Hkv, block_size, D] (fp16 or bf16)
+  void* vcache;
+  int cache_is_bf16;
+  int block_size;
+};
+int rope_kv_write(const RopeKVArgs& a, cudaStream_t st);
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;   // [B, H, D]
+  const void* kcache;       // [num_blocks, Hkv, bs, D]
+  const void* vcache;
+  int cache_is_bf16;
+  const int* block_tables;  // [B, max_blocks]
+  int max_blocks;
+  const int* seq_lens;      // [B] tokens in cache including the current one
+  int B, H, Hkv, D, block_size;
+  float scale;
+  int window;               // sliding window (0 = none)
+  int splits;               // KV splits per (b, kv head)
+  float* part_acc;          // scratch [B, Hkv, splits, G, D]
+  float2* part_ml;          // scratch [B, Hkv, splits, G] (max, sum)
+  __nv_bfloat16* out;       // [B, H*D]
+  int8_t* out_q;            // optional q8 of out
+  float2* out_s;
+};
+int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
+size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits);
+
+struct PrefillAttnArgs {
+  const __nv_bfloat16* q;   // [T, H, D]  (rows of all sequences, concatenated)
+  const void* kcache;
+  const void* vcache;
+  int cache_is_bf16;
+  const int* block_tables;  // [S, max_blocks]
+  int max_blocks;
+  const int* q_start;       // [S+1] prefix sums of new tokens per sequence
+  const int* ctx_lens;      // [S] total tokens in cache after this step (prefix + new)
+  int S, max_q, H, Hkv, D, block_size;
+  float scale;
+  int window;
+  __nv_bfloat16* out;       // [T, H*D]
+};
+int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st);
+
+// Token embedding rows gathered from a quantized [V, H] table (planar layout) into f32 [T, H].
+int embed_gather(const QW& table, const int* ids, int T, float* out, cudaStream_t st);
+
+// Dequantize rows [r0, r0+n) of a quantized weight to bf16 [n, K] (used by the GEMM path tests
+// and for types without a native kernel).
+int dequant_rows(const QW& w, int r0, int n, __nv_bfloat16* out, cudaStream_t st);
+
+struct SampleArgs {
+  const float* logits;  // [B, V]
+  int B, V, ld;
+  const float* temperature;  // [B]  (<= 0 -> greedy)
+  const int* top_k;          // [B]  (<= 0 -> off)
+  const float* top_p;        // [B]  (>= 1 -> off)
+  const float* min_p;        // [B]  (<= 0 -> off)
+  const uint64_t* seeds;     // [B]
+  const int* steps;          // [B] per-sequence offset into the Philox stream
+  int* out_ids;              // [B]
+  float* out_logprob;        // optional [B]
+  const uint32_t* allow_mask;  // optional [B, ceil(V/32)] grammar bitmask (1 = allowed)
+  const float* penalties;    // optional [B, 3] (repetition, frequency, presence)
+  const int* pen_counts_idx; // optional [B, max_hist] token history (-1 padded)
+  int max_hist;
+};
+int sample_tokens(const SampleArgs& a, cudaStream_t st);
+
+}  // namespace barq

@@ -18,6 +18,7 @@
 // which is what both the vector loads of the GEMV kernels and the TMA boxes of the tcgen05 GEMM need.
 #pragma once
 #include <stdint.h>
+#include <vector_types.h>
 
 namespace barq {
 
@@ -29,6 +30,13 @@ enum WType : int {
   W_Q5_K = 13,
   W_Q6_K = 14,
   W_IQ4_NL = 20,
+};
+
+// Activation in the "q8" layout consumed by the dp4a GEMV kernels: per token row of K values,
+// int8 qs[K] and one float2 (scale d, d * sum(qs)) per 32 values.
+struct ActQ8 {
+  const int8_t* q;   // [B, K]
+  const float2* s;   // [B, K/32]
 };
 
 struct QW {
