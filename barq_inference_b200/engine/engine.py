@@ -46,6 +46,7 @@ class EngineConfig:
     device: str = "cuda"
     ser_threshold: float = 0.0      # MoE smart expert reduction (--ser)
     fused_moe: bool = True          # --fmoe
+    act_x2: bool = True             # two-term int8 decode activations (False: single int8 term)
 
     @staticmethod
     def preset(name: str, **kw) -> "EngineConfig":
@@ -413,7 +414,7 @@ def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
         from ..models.deepseek2 import DeepseekV2Runner
 
         return DeepseekV2Runner(cfg, tensors, device, kv_dtype, ser_threshold=ec.ser_threshold)
-    r = LlamaRunner(cfg, tensors, device, kv_dtype)
+    r = LlamaRunner(cfg, tensors, device, kv_dtype, act_x2=ec.act_x2)
     r.ser_threshold = ec.ser_threshold
     r.fused_moe = ec.fused_moe
     return r

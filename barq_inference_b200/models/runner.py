@@ -60,12 +60,14 @@ class Layer:
 
 class LlamaRunner:
     def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], device="cuda",
-                 kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None):
+                 kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None, act_x2: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.kv_dtype = kv_dtype
         self.scale = attn_scale(cfg)
         self.use_gemm = use_gemm
+        # two-term int8 decode activations (accurate mode); False = single int8 term (fastest)
+        self.x2 = act_x2
         dev = self.device
         self.embed_w = _qw(tensors["token_embd.weight"], dev)
         self.out_norm = _f32(tensors["output_norm.weight"], dev)
@@ -127,7 +129,7 @@ class LlamaRunner:
                 return out
             return r
         if mode == EPI_SWIGLU_Q8:
-            oq = Q8Act.empty(T, w.N // 2, self.device)
+            oq = Q8Act.empty(T, w.N // 2, self.device, self.x2)
             for t0 in range(0, T, GEMV_MAX_T):
                 t1 = min(T, t0 + GEMV_MAX_T)
                 ops.gemv(w, x.rows(t0, t1) if x is not None else None, t1 - t0, mode, out_q=oq.rows(t0, t1),
@@ -156,24 +158,26 @@ class LlamaRunner:
         x = ops.embed(self.embed_w, inp.ids)
         for li, L in enumerate(self.layers):
             kc, vc = self.kv[li]
-            hb, hq = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.qkv))
+            hb, hq = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.qkv),
+                                 x2=self.x2)
             qkv = self._lin_q8(L.qkv, hq, T, EPI_STORE_F32, bias=L.qkv_bias, xb=hb)
             q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
                                   cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
             if inp.decode:
                 ab, aq = ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
-                                              cfg.sliding_window)
+                                              cfg.sliding_window, x2=self.x2)
             else:
                 ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
                                            H, Hkv, D, self.scale, cfg.sliding_window)
-                aq = ops.quantize_q8(ab)
+                aq = ops.quantize_q8(ab, self.x2)
             self._lin_q8(L.wo, aq, T, EPI_ADD_F32, out=x, xb=ab)
             if L.moe is not None:
-                hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=True)
+                hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=True, x2=self.x2)
                 L.moe.forward(self, hq, hb, T, x)
                 continue
             down_bf16 = self._needs_bf16(L.down)
-            hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.gate_up))
+            hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.gate_up),
+                                 x2=self.x2)
             if L.gu_interleaved and not down_bf16:
                 h2 = self._lin_q8(L.gate_up, hq, T, EPI_SWIGLU_Q8)
                 self._lin_q8(L.down, h2, T, EPI_ADD_F32, out=x)
@@ -181,8 +185,9 @@ class LlamaRunner:
                 gu = self._lin_q8(L.gate_up, hq, T, EPI_STORE_F32, xb=hb)
                 if L.gu_interleaved:  # undo the 32-row interleave for the elementwise kernel
                     gu = gu.view(T, -1, 2, 32).transpose(1, 2).reshape(T, -1).contiguous()
-                hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16)
+                hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16,
+                                      x2=self.x2)
                 self._lin_q8(L.down, hq2, T, EPI_ADD_F32, out=x, xb=hb2)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
-        _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True)
+        _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
         return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32)

@@ -38,51 +38,75 @@ def require_ext():
 
 
 class Q8Act:
-    """int8 activation rows + (scale, scale*sum) per 32 values — the GEMV input format."""
+    """int8 activation rows + (scale, scale*sum) per 32 values — the GEMV input format.
 
-    __slots__ = ("q", "s", "T", "K")
+    With ``x2`` a second int8 term holds the quantized residual (x ~= d*q + dl*ql), which brings the
+    activation error from ~2^-8 to ~2^-15 of the group max at twice the dp4a work."""
 
-    def __init__(self, q: torch.Tensor, s: torch.Tensor, T: int, K: int):
-        self.q, self.s, self.T, self.K = q, s, T, K
+    __slots__ = ("q", "s", "ql", "dl", "T", "K")
+
+    def __init__(self, q, s, T: int, K: int, ql=None, dl=None):
+        self.q, self.s, self.ql, self.dl, self.T, self.K = q, s, ql, dl, T, K
 
     @staticmethod
-    def empty(T: int, K: int, device) -> "Q8Act":
-        return Q8Act(torch.empty(T, K, dtype=torch.int8, device=device),
-                     torch.empty(T, K // 32, 2, dtype=torch.float32, device=device), T, K)
+    def empty(T: int, K: int, device, x2: bool = False) -> "Q8Act":
+        q = torch.empty(T, K, dtype=torch.int8, device=device)
+        s = torch.empty(T, K // 32, 2, dtype=torch.float32, device=device)
+        if not x2:
+            return Q8Act(q, s, T, K)
+        return Q8Act(q, s, T, K, torch.empty(T, K, dtype=torch.int8, device=device),
+                     torch.empty(T, K // 32, 2, dtype=torch.float32, device=device))
+
+    @property
+    def x2(self) -> bool:
+        return self.ql is not None
 
     def rows(self, a: int, b: int) -> "Q8Act":
-        return Q8Act(self.q[a:b], self.s[a:b], b - a, self.K)
+        lo = (self.ql[a:b], self.dl[a:b]) if self.x2 else (None, None)
+        return Q8Act(self.q[a:b], self.s[a:b], b - a, self.K, *lo)
+
+    def outs(self):
+        return (self.q, self.s, self.ql, self.dl)
 
 
-def quantize_q8(x: torch.Tensor) -> Q8Act:
+def _ins(x):
+    return (None, None, None, None) if x is None else (x.q, x.s, x.ql, x.dl)
+
+
+def _outs(x):
+    return (None, None, None, None) if x is None else x.outs()
+
+
+def quantize_q8(x: torch.Tensor, x2: bool = False) -> Q8Act:
     T, K = x.shape
-    out = Q8Act.empty(T, K, x.device)
-    require_ext().quantize_q8(x, T, K, x.stride(0), out.q, out.s)
+    out = Q8Act.empty(T, K, x.device, x2)
+    require_ext().quantize_q8(x, T, K, x.stride(0), *out.outs())
     _count()
     return out
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, add: torch.Tensor | None = None,
-            want_bf16: bool = False, want_q8: bool = False):
+            want_bf16: bool = False, want_q8: bool = False, x2: bool = False):
     """x (f32 [T,H], updated in place by ``add``) -> (bf16 | None, Q8Act | None)."""
     T, H = x.shape
     ob = torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None
-    oq = Q8Act.empty(T, H, x.device) if want_q8 else None
-    require_ext().rmsnorm(x, add, w, eps, ob, oq.q if oq else None, oq.s if oq else None)
+    oq = Q8Act.empty(T, H, x.device, x2) if want_q8 else None
+    require_ext().rmsnorm(x, add, w, eps, ob, *_outs(oq))
     _count()
     return ob, oq
 
 
 def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
-         xb: torch.Tensor | None = None, bias: torch.Tensor | None = None, out_q: Q8Act | None = None):
+         xb: torch.Tensor | None = None, bias: torch.Tensor | None = None, out_q: Q8Act | None = None,
+         x2: bool = False):
     """Decode GEMV for T <= 8 tokens.  Returns ``out`` (allocated if None for store modes)."""
     C = require_ext()
     dev = w.device
     if mode == EPI_SWIGLU_Q8:
         F = w.N // 2
         if out_q is None:
-            out_q = Q8Act.empty(T, F, dev)
-        C.qgemv(*w.args(), x.q if x else None, x.s if x else None, xb, T, mode, None, out, out_q.q, out_q.s, bias, F)
+            out_q = Q8Act.empty(T, F, dev, x2)
+        C.qgemv(*w.args(), *_ins(x), xb, T, mode, None, out, *out_q.outs(), bias, F)
         _count()
         return out_q
     if out is None:
@@ -91,16 +115,16 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
     ld = out.stride(0)
     f32 = out if out.dtype == torch.float32 else None
     bf = out if out.dtype == torch.bfloat16 else None
-    C.qgemv(*w.args(), x.q if x else None, x.s if x else None, xb, T, mode, f32, bf, None, None, bias, ld)
+    C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld)
     _count()
     return out
 
 
-def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False):
+def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False, x2: bool = False):
     T = gu.shape[0]
     ob = torch.empty(T, F, dtype=torch.bfloat16, device=gu.device) if want_bf16 else None
-    oq = Q8Act.empty(T, F, gu.device) if want_q8 else None
-    require_ext().swiglu(gu, T, F, gu.stride(0), ob, oq.q if oq else None, oq.s if oq else None)
+    oq = Q8Act.empty(T, F, gu.device, x2) if want_q8 else None
+    require_ext().swiglu(gu, T, F, gu.stride(0), ob, *_outs(oq))
     _count()
     return ob, oq
 
@@ -120,7 +144,7 @@ def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
 
 
 def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,
-                     want_q8=True, scratch=None):
+                     want_q8=True, scratch=None, x2=False):
     B = q.shape[0]
     C = require_ext()
     if splits is None:
@@ -129,9 +153,9 @@ def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale
         scratch = torch.empty(C.decode_attention_scratch_floats(B, H, Hkv, D, splits), dtype=torch.float32,
                               device=q.device)
     out = torch.empty(B, H * D, dtype=torch.bfloat16, device=q.device)
-    oq = Q8Act.empty(B, H * D, q.device) if want_q8 else None
+    oq = Q8Act.empty(B, H * D, q.device, x2) if want_q8 else None
     C.decode_attention(q, kcache, vcache, block_tables, seq_lens, B, H, Hkv, D, scale, window, splits, scratch,
-                       out, oq.q if oq else None, oq.s if oq else None)
+                       out, *_outs(oq))
     _count(2)
     return out, oq
 

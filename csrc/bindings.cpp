@@ -24,6 +24,10 @@ void check(int rc, const char* what) {
   TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
 }
 
+barq::ActOut act_out(const OptT& q, const OptT& s, const OptT& ql, const OptT& dl) {
+  return barq::ActOut{optptr<int8_t>(q), optptr<float2>(s), optptr<int8_t>(ql), optptr<float2>(dl)};
+}
+
 barq::QW make_qw(int64_t type, int64_t N, int64_t K, const Tensor& p0, const OptT& p1, const OptT& p2, const OptT& d) {
   CHECK_CUDA(p0);
   barq::QW w;
@@ -37,38 +41,42 @@ barq::QW make_qw(int64_t type, int64_t N, int64_t K, const Tensor& p0, const Opt
   return w;
 }
 
-void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, OptT xq, OptT xs, OptT xb,
-           int64_t B, int64_t mode, OptT out_f32, OptT out_bf16, OptT out_q, OptT out_s, OptT bias, int64_t ld_out) {
+void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, OptT xq, OptT xs, OptT xql,
+           OptT xdl, OptT xb, int64_t B, int64_t mode, OptT out_f32, OptT out_bf16, OptT out_q, OptT out_s,
+           OptT out_ql, OptT out_dl, OptT bias, int64_t ld_out) {
   c10::cuda::CUDAGuard g(p0.device());
   barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
-  barq::ActQ8 x{optptr<const int8_t>(xq), optptr<const float2>(xs)};
-  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q),
-                   optptr<float2>(out_s), optptr<const float>(bias), (int)ld_out};
+  barq::ActQ8 x{optptr<const int8_t>(xq), optptr<const float2>(xs), optptr<const int8_t>(xql),
+                optptr<const float2>(xdl)};
+  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16),
+                   act_out(out_q, out_s, out_ql, out_dl), optptr<const float>(bias), (int)ld_out};
   int ldxb = (int)K;
   check(barq::qgemv(w, x, optptr<const __nv_bfloat16>(xb), ldxb, (int)B, ep, cur_stream()), "qgemv");
 }
 
-void rmsnorm(Tensor x, OptT add, Tensor w, double eps, OptT out_bf16, OptT out_q, OptT out_s) {
+void rmsnorm(Tensor x, OptT add, Tensor w, double eps, OptT out_bf16, OptT out_q, OptT out_s, OptT out_ql,
+             OptT out_dl) {
   CHECK_CUDA(x);
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(x.scalar_type() == torch::kFloat32, "rmsnorm: residual stream must be f32");
   int H = (int)x.size(-1), T = (int)(x.numel() / H);
   check(barq::rmsnorm(ptr<float>(x), optptr<const float>(add), ptr<const float>(w), (float)eps, T, H,
-                      optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q), optptr<float2>(out_s), cur_stream()),
+                      optptr<__nv_bfloat16>(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
         "rmsnorm");
 }
 
-void quantize_q8(Tensor x, int64_t T, int64_t H, int64_t ldx, Tensor out_q, Tensor out_s) {
+void quantize_q8(Tensor x, int64_t T, int64_t H, int64_t ldx, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl) {
   c10::cuda::CUDAGuard g(x.device());
   check(barq::quantize_q8(x.data_ptr(), x.scalar_type() == torch::kBFloat16, (int)T, (int)H, (int)ldx,
-                          ptr<int8_t>(out_q), ptr<float2>(out_s), cur_stream()),
+                          act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
         "quantize_q8");
 }
 
-void swiglu(Tensor in, int64_t T, int64_t F, int64_t ld_in, OptT out_bf16, OptT out_q, OptT out_s) {
+void swiglu(Tensor in, int64_t T, int64_t F, int64_t ld_in, OptT out_bf16, OptT out_q, OptT out_s, OptT out_ql,
+            OptT out_dl) {
   c10::cuda::CUDAGuard g(in.device());
   check(barq::swiglu(in.data_ptr(), in.scalar_type() == torch::kBFloat16, (int)T, (int)F, (int)ld_in,
-                     optptr<__nv_bfloat16>(out_bf16), optptr<int8_t>(out_q), optptr<float2>(out_s), cur_stream()),
+                     optptr<__nv_bfloat16>(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
         "swiglu");
 }
 
@@ -98,7 +106,7 @@ void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor co
 
 void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor seq_lens, int64_t B,
                       int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window, int64_t splits, Tensor scratch,
-                      Tensor out, OptT out_q, OptT out_s) {
+                      Tensor out, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl) {
   c10::cuda::CUDAGuard g(q.device());
   TORCH_CHECK(scratch.scalar_type() == torch::kFloat32, "scratch must be f32");
   size_t need = barq::decode_attention_scratch_floats((int)B, (int)H, (int)Hkv, (int)D, (int)splits);
@@ -119,8 +127,7 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.part_acc = ptr<float>(scratch);
   a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)B * H * splits * D);
   a.out = ptr<__nv_bfloat16>(out);
-  a.out_q = optptr<int8_t>(out_q);
-  a.out_s = optptr<float2>(out_s);
+  a.out_q = act_out(out_q, out_s, out_ql, out_dl);
   check(barq::decode_attention(a, cur_stream()), "decode_attention");
 }
 

@@ -188,12 +188,7 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeAttnArgs a) {
   float o = L > 0.f ? A / L : 0.f;
   const size_t oi = (size_t)b * a.H * D + (size_t)h * D + d;
   a.out[oi] = __float2bfloat16(o);
-  if (a.out_q) {
-    float dd, ss;
-    int8_t q = quant_lane32(o, dd, ss);
-    a.out_q[oi] = q;
-    if ((d & 31) == 0) a.out_s[oi / 32] = make_float2(dd, ss);
-  }
+  if (a.out_q.q) act_store32(a.out_q, o, oi, oi / 32, d & 31);
 }
 
 size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits) {

@@ -67,4 +67,43 @@ BARQ_DEV int8_t quant_lane32(float v, float& d_out, float& s_out) {
   return (int8_t)q;
 }
 
+// Two-term version: v ~= d*q + dl*ql.  s_out is the sum of both terms over the 32 values.
+BARQ_DEV void quant_lane32x2(float v, int8_t& q, int8_t& ql, float& d_out, float& dl_out, float& s_out) {
+  float amax = warp_max(fabsf(v));
+  float d = amax / 127.0f;
+  float id = d > 0.f ? 1.0f / d : 0.f;
+  int qi = max(-127, min(127, __float2int_rn(v * id)));
+  float r = v - d * (float)qi;
+  float rmax = warp_max(fabsf(r));
+  float dl = rmax / 127.0f;
+  float idl = dl > 0.f ? 1.0f / dl : 0.f;
+  int qli = max(-127, min(127, __float2int_rn(r * idl)));
+  int sq = warp_sum_int(qi), sql = warp_sum_int(qli);
+  q = (int8_t)qi;
+  ql = (int8_t)qli;
+  d_out = d;
+  dl_out = dl;
+  s_out = d * (float)sq + dl * (float)sql;
+}
+
+// Writes lane's value of a 32-value group into an activation (single or two-term).
+BARQ_DEV void act_store32(const ActOut& o, float v, size_t elem, size_t group, int lane) {
+  if (o.ql) {
+    int8_t q, ql;
+    float d, dl, s;
+    quant_lane32x2(v, q, ql, d, dl, s);
+    o.q[elem] = q;
+    o.ql[elem] = ql;
+    if (lane == 0) {
+      o.s[group] = make_float2(d, s);
+      o.dl[group] = make_float2(dl, 0.f);
+    }
+  } else {
+    float d, s;
+    int8_t q = quant_lane32(v, d, s);
+    o.q[elem] = q;
+    if (lane == 0) o.s[group] = make_float2(d, s);
+  }
+}
+
 }  // namespace barq

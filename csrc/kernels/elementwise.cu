@@ -13,8 +13,7 @@ namespace barq {
 // One CTA per token row.  blockDim = 256.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
                                                       const float* __restrict__ w, float eps, int H,
-                                                      __nv_bfloat16* __restrict__ ob, int8_t* __restrict__ oq,
-                                                      float2* __restrict__ os) {
+                                                      __nv_bfloat16* __restrict__ ob, ActOut oq) {
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * H;
   const float* ar = add ? add + (size_t)t * H : nullptr;
@@ -45,52 +44,42 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
     int i = g * 32 + lane;
     float v = i < H ? xr[i] * r * w[i] : 0.f;
     if (ob && i < H) ob[(size_t)t * H + i] = __float2bfloat16(v);
-    if (oq) {
-      float d, s;
-      int8_t q = quant_lane32(v, d, s);
-      if (i < H) oq[(size_t)t * H + i] = q;
-      if (lane == 0) os[(size_t)t * (H / 32) + g] = make_float2(d, s);
-    }
+    if (oq.q) act_store32(oq, v, (size_t)t * H + i, (size_t)t * (H / 32) + g, lane);
   }
 }
 
 int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
-            int8_t* out_q, float2* out_s, cudaStream_t st) {
-  if (out_q && (H % 32)) return -1;
+            ActOut out_q, cudaStream_t st) {
+  if (out_q.q && (H % 32)) return -1;
   if (T <= 0) return 0;
-  rmsnorm_kernel<<<T, 256, 0, st>>>(x, add, w, eps, H, out_bf16, out_q, out_s);
+  rmsnorm_kernel<<<T, 256, 0, st>>>(x, add, w, eps, H, out_bf16, out_q);
   return 0;
 }
 
 template <typename T>
-__global__ void quant_q8_kernel(const T* __restrict__ x, int H, int ldx, int8_t* __restrict__ oq,
-                                float2* __restrict__ os) {
+__global__ void quant_q8_kernel(const T* __restrict__ x, int H, int ldx, ActOut oq) {
   const int t = blockIdx.y;
   const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (g * 32 >= H) return;
   float v = to_f(x[(size_t)t * ldx + g * 32 + lane]);
-  float d, s;
-  int8_t q = quant_lane32(v, d, s);
-  oq[(size_t)t * H + g * 32 + lane] = q;
-  if (lane == 0) os[(size_t)t * (H / 32) + g] = make_float2(d, s);
+  act_store32(oq, v, (size_t)t * H + g * 32 + lane, (size_t)t * (H / 32) + g, lane);
 }
 
-int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, int8_t* out_q, float2* out_s,
-                cudaStream_t st) {
+int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_q, cudaStream_t st) {
   if (H % 32) return -1;
   if (T <= 0) return 0;
   dim3 g((H / 32 + 7) / 8, T);
   if (x_is_bf16)
-    quant_q8_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)x, H, ldx, out_q, out_s);
+    quant_q8_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)x, H, ldx, out_q);
   else
-    quant_q8_kernel<float><<<g, 256, 0, st>>>((const float*)x, H, ldx, out_q, out_s);
+    quant_q8_kernel<float><<<g, 256, 0, st>>>((const float*)x, H, ldx, out_q);
   return 0;
 }
 
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, __nv_bfloat16* __restrict__ ob,
-                              int8_t* __restrict__ oq, float2* __restrict__ os) {
+                              ActOut oq) {
   const int t = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -99,23 +88,18 @@ __global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, __nv_bflo
   float h = 0.f;
   if (i < F) h = silu(to_f(in[(size_t)t * ld + i])) * to_f(in[(size_t)t * ld + F + i]);
   if (ob && i < F) ob[(size_t)t * F + i] = __float2bfloat16(h);
-  if (oq) {
-    float d, s;
-    int8_t q = quant_lane32(h, d, s);
-    oq[(size_t)t * F + i] = q;
-    if (lane == 0) os[(size_t)t * (F / 32) + g] = make_float2(d, s);
-  }
+  if (oq.q) act_store32(oq, h, (size_t)t * F + i, (size_t)t * (F / 32) + g, lane);
 }
 
-int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, int8_t* out_q,
-           float2* out_s, cudaStream_t st) {
-  if (out_q && (F % 32)) return -1;
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, ActOut out_q,
+           cudaStream_t st) {
+  if (out_q.q && (F % 32)) return -1;
   if (T <= 0) return 0;
   dim3 g(((F + 31) / 32 + 7) / 8, T);
   if (in_is_bf16)
-    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_bf16, out_q, out_s);
+    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_bf16, out_q);
   else
-    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_bf16, out_q, out_s);
+    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_bf16, out_q);
   return 0;
 }
 

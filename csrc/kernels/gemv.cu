@@ -17,7 +17,7 @@
 
 namespace barq {
 
-template <class T, int BS, int RW, int NW>
+template <class T, int BS, int RW, int NW, bool X2>
 __global__ void __launch_bounds__(NW * 32) qgemv_kernel(QW w, ActQ8 x, int B, GemvEpi ep) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * NW + warp) * RW;
@@ -45,6 +45,11 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(QW w, ActQ8 x, int B, Ge
         typename T::X xr = T::load_x(xq + (size_t)b * K, xs + (size_t)b * nparts, p);
 #pragma unroll
         for (int r = 0; r < RW; ++r) acc[r][b] += T::dot(wr[r], xr, lane);
+        if (X2) {  // second (residual) activation term
+          typename T::X xl = T::load_x(x.ql + (size_t)b * K, x.dl + (size_t)b * nparts, p);
+#pragma unroll
+          for (int r = 0; r < RW; ++r) acc[r][b] += T::dot(wr[r], xl, lane);
+        }
       }
     }
   }
@@ -69,10 +74,7 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(QW w, ActQ8 x, int B, Ge
       for (int b = 0; b < B; ++b) {
         float g = red[lane][b], u = red[32 + lane][b];
         float h = silu(g) * u;
-        float d, s;
-        int8_t q = quant_lane32(h, d, s);
-        ep.out_q[(size_t)b * n_out + o] = q;
-        if (lane == 0) ep.out_s[(size_t)b * (n_out / 32) + blockIdx.x] = make_float2(d, s);
+        act_store32(ep.out_q, h, (size_t)b * n_out + o, (size_t)b * (n_out / 32) + blockIdx.x, lane);
         if (ep.out_bf16) ep.out_bf16[(size_t)b * ep.ld_out + o] = __float2bfloat16(h);
       }
     }
@@ -134,16 +136,24 @@ __global__ void __launch_bounds__(128) bf16_gemv_kernel(const __nv_bfloat16* __r
   }
 }
 
-template <class T, int BS>
-static void launch_t(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, cudaStream_t st) {
+template <class T, int BS, bool X2>
+static void launch_t2(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, cudaStream_t st) {
   if (ep.mode == EPI_SWIGLU_Q8) {
     constexpr int RW = 4, NW = 16;  // 64 rows = 32 gate + 32 up
-    qgemv_kernel<T, BS, RW, NW><<<w.N / 64, NW * 32, 0, st>>>(w, x, B, ep);
+    qgemv_kernel<T, BS, RW, NW, X2><<<w.N / 64, NW * 32, 0, st>>>(w, x, B, ep);
   } else {
     constexpr int RW = 2, NW = 4;
     int rows_per_cta = RW * NW;
-    qgemv_kernel<T, BS, RW, NW><<<(w.N + rows_per_cta - 1) / rows_per_cta, NW * 32, 0, st>>>(w, x, B, ep);
+    qgemv_kernel<T, BS, RW, NW, X2><<<(w.N + rows_per_cta - 1) / rows_per_cta, NW * 32, 0, st>>>(w, x, B, ep);
   }
+}
+
+template <class T, int BS>
+static void launch_t(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, cudaStream_t st) {
+  if (x.ql)
+    launch_t2<T, BS, true>(w, x, B, ep, st);
+  else
+    launch_t2<T, BS, false>(w, x, B, ep, st);
 }
 
 template <class T>

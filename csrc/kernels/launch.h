@@ -14,8 +14,7 @@ struct GemvEpi {
   int mode;
   float* out_f32;
   __nv_bfloat16* out_bf16;
-  int8_t* out_q;
-  float2* out_s;
+  ActOut out_q;
   const float* bias;
   int ld_out;
 };
@@ -27,15 +26,14 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // Fused (residual add +) RMSNorm.  x: f32 [T, H] residual stream (updated in place when `add`
 // is given: x += add).  Outputs any of bf16 [T, H] and int8 q8 [T, H] + scales [T, H/32].
 int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
-            int8_t* out_q, float2* out_s, cudaStream_t st);
+            ActOut out_q, cudaStream_t st);
 
 // Quantize bf16 or f32 rows to the q8 activation layout (H % 32 == 0).
-int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, int8_t* out_q, float2* out_s,
-                cudaStream_t st);
+int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_q, cudaStream_t st);
 
 // h = silu(g) * u with g = in[t, i], u = in[t, F + i] (f32 or bf16 input) -> bf16 and/or q8.
-int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, int8_t* out_q,
-           float2* out_s, cudaStream_t st);
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, ActOut out_q,
+           cudaStream_t st);
 
 struct RopeKVArgs {
   const void* qkv;       // [T, (H + 2*Hkv) * D]  f32 or bf16
@@ -72,8 +70,7 @@ struct DecodeAttnArgs {
   float* part_acc;          // scratch [B, Hkv, splits, G, D]
   float2* part_ml;          // scratch [B, Hkv, splits, G] (max, sum)
   __nv_bfloat16* out;       // [B, H*D]
-  int8_t* out_q;            // optional q8 of out
-  float2* out_s;
+  ActOut out_q;             // optional q8 of out (q == null: none)
 };
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
 size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits);

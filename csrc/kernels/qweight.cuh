@@ -34,9 +34,21 @@ enum WType : int {
 
 // Activation in the "q8" layout consumed by the dp4a GEMV kernels: per token row of K values,
 // int8 qs[K] and one float2 (scale d, d * sum(qs)) per 32 values.
+// Optional second term (ql, dl): the int8 residual x - d*q quantized with its own scale, so that
+// x ~= d*q + dl*ql to ~16 bits; s.y then holds the sum of both terms.
 struct ActQ8 {
   const int8_t* q;   // [B, K]
   const float2* s;   // [B, K/32]
+  const int8_t* ql;  // [B, K] or null
+  const float2* dl;  // [B, K/32] (scale, 0) or null
+};
+
+// Output side of an activation producer (q / s required when used, ql / dl optional).
+struct ActOut {
+  int8_t* q;
+  float2* s;
+  int8_t* ql;
+  float2* dl;
 };
 
 struct QW {
