@@ -144,6 +144,25 @@ class LlamaRunner:
                      xb=None if xb is None else xb[t0:t1].contiguous())
         return out
 
+    def _lin_bf16(self, w, xb: torch.Tensor, T: int, mode: int, out=None, bias=None):
+        """Projection of bf16 activations [T, K] on the tcgen05 GEMM (K2)."""
+        if isinstance(w, tuple):
+            r = torch.cat([self._lin_bf16(wi, xb, T, EPI_STORE_F32) for wi in w], 1)
+            if bias is not None:
+                r += bias
+            if mode == EPI_ADD_F32:
+                out += r
+                return out
+            return r
+        if w.wtype == ops.W_BF16:  # dense weights (non-blocked GGUF tensors): GEMV in chunks
+            if out is None:
+                out = torch.empty(T, w.N, dtype=torch.float32, device=self.device)
+            for t0 in range(0, T, GEMV_MAX_T):
+                t1 = min(T, t0 + GEMV_MAX_T)
+                ops.gemv(w, None, t1 - t0, mode, out=out[t0:t1], bias=bias, xb=xb[t0:t1].contiguous())
+            return out
+        return ops.gemm(w, xb, mode, out=out, bias=bias)
+
     def _needs_bf16(self, w) -> bool:
         if isinstance(w, tuple):
             return any(self._needs_bf16(x) for x in w)
@@ -152,6 +171,53 @@ class LlamaRunner:
     # ------------------------------------------------------------------ forward
     def forward(self, inp: StepInput) -> torch.Tensor:
         """Logits (f32) of the last new token of each sequence: [S, vocab]."""
+        T = inp.ids.numel()
+        if T > GEMV_MAX_T and self.use_gemm is not False:
+            return self._forward_gemm(inp)
+        return self._forward_gemv(inp)
+
+    def _attention(self, L, li, qkv, inp, T, want_q8):
+        cfg = self.cfg
+        H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        kc, vc = self.kv[li]
+        q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
+                              cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
+        if inp.decode:
+            return ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
+                                        cfg.sliding_window, want_q8=want_q8, x2=self.x2)
+        ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
+                                   H, Hkv, D, self.scale, cfg.sliding_window)
+        return ab, (ops.quantize_q8(ab, self.x2) if want_q8 else None)
+
+    def _forward_gemm(self, inp: StepInput) -> torch.Tensor:
+        """Many tokens (prefill, batched decode): bf16 activations on the tcgen05 GEMM."""
+        cfg = self.cfg
+        T = inp.ids.numel()
+        x = ops.embed(self.embed_w, inp.ids)
+        for li, L in enumerate(self.layers):
+            hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True)
+            qkv = self._lin_bf16(L.qkv, hb, T, EPI_STORE_F32, bias=L.qkv_bias)
+            ab, _ = self._attention(L, li, qkv, inp, T, want_q8=False)
+            self._lin_bf16(L.wo, ab, T, EPI_ADD_F32, out=x)
+            hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_bf16=True,
+                                 want_q8=L.moe is not None, x2=self.x2)
+            if L.moe is not None:
+                L.moe.forward(self, hq, hb, T, x)
+                continue
+            if L.gu_interleaved:
+                h = ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
+            else:
+                gu = self._lin_bf16(L.gate_up, hb, T, EPI_STORE_F32)
+                h, _ = ops.swiglu(gu, cfg.ffn, want_bf16=True)
+            self._lin_bf16(L.down, h, T, EPI_ADD_F32, out=x)
+        xl = x.index_select(0, inp.last_idx) if not inp.decode else x
+        ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True)
+        if xl.shape[0] <= GEMV_MAX_T:
+            _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
+            return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32, xb=ob)
+        return self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32)
+
+    def _forward_gemv(self, inp: StepInput) -> torch.Tensor:
         cfg = self.cfg
         T = inp.ids.numel()
         H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim

@@ -120,6 +120,30 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
     return out
 
 
+def gemm(w: QWeight, x: torch.Tensor, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
+         bias: torch.Tensor | None = None, k_splits: int = 0) -> torch.Tensor:
+    """tcgen05 quantized GEMM: x bf16 [T, K] -> out (f32/bf16 [T, N]; SwiGLU mode: bf16 [T, N/2]).
+
+    ``k_splits`` 0 = automatic split-K for the f32 modes (accumulated with atomics)."""
+    T = x.shape[0]
+    if mode == EPI_SWIGLU_Q8:
+        if out is None:
+            out = torch.empty(T, w.N // 2, dtype=torch.bfloat16, device=x.device)
+    elif out is None:
+        out = torch.empty(T, w.N, dtype=torch.bfloat16 if mode == EPI_STORE_BF16 else torch.float32,
+                          device=x.device)
+    f32 = out if out.dtype == torch.float32 else None
+    bf = out if out.dtype == torch.bfloat16 else None
+    require_ext().qgemm(*w.args(), x, T, mode, f32, bf, bias, out.stride(0), k_splits)
+    _count(2 if (k_splits != 1 and mode == EPI_STORE_F32) else 1)
+    return out
+
+
+def gemm_error() -> int:
+    """Sticky device error word of the tcgen05 kernels (0 = ok; 0x100|site = bounded wait expired)."""
+    return int(require_ext().gemm_error())
+
+
 def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False, x2: bool = False):
     T = gu.shape[0]
     ob = torch.empty(T, F, dtype=torch.bfloat16, device=gu.device) if want_bf16 else None

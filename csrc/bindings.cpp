@@ -54,6 +54,24 @@ void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT
   check(barq::qgemv(w, x, optptr<const __nv_bfloat16>(xb), ldxb, (int)B, ep, cur_stream()), "qgemv");
 }
 
+void qgemm(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor x, int64_t T, int64_t mode,
+           OptT out_f32, OptT out_bf16, OptT bias, int64_t ld_out, int64_t k_splits) {
+  c10::cuda::CUDAGuard g(p0.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(-1) == K, "qgemm: x must be bf16 [T, K]");
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16), barq::ActOut{},
+                   optptr<const float>(bias), (int)ld_out};
+  check(barq::qgemm_tc(w, ptr<const __nv_bfloat16>(x), (int)T, ep, (int)k_splits, cur_stream()), "qgemm");
+}
+
+int64_t gemm_error() {
+  int v = 0;
+  TORCH_CHECK(barq::gemm_error_word(&v) == 0, "gemm_error: read failed");
+  return v;
+}
+
+void gemm_clear_error() { TORCH_CHECK(barq::gemm_clear_error_word() == 0, "gemm_clear_error failed"); }
+
 void rmsnorm(Tensor x, OptT add, Tensor w, double eps, OptT out_bf16, OptT out_q, OptT out_s, OptT out_ql,
              OptT out_dl) {
   CHECK_CUDA(x);
@@ -193,6 +211,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "barq sm_100a kernels";
   m.def("qgemv", &qgemv);
   m.def("rmsnorm", &rmsnorm);
+  m.def("qgemm", &qgemm);
+  m.def("gemm_error", &gemm_error);
+  m.def("gemm_clear_error", &gemm_clear_error);
   m.def("quantize_q8", &quantize_q8);
   m.def("swiglu", &swiglu);
   m.def("rope_kv_write", &rope_kv_write);

@@ -1,0 +1,500 @@
+// K2: quantized GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), GGUF dequant in the
+// mainloop.  out[t, n] = sum_k x[t, k] * W[n, k] for prefill and batched decode.
+//
+// The reference's quantized matmul is a host round trip (backend/src/cuda_quant.rs:104-126); its
+// dense path is a rayon triple loop (barq_core/src/blas.rs:193-207).
+//
+// Swap-AB tiling: the MMA "A" operand is a 128-row tile of *weights* (dequantized to bf16 on the
+// fly), the "B" operand a BN-row tile of *tokens* (bf16 activations), so D = W_tile * X_tile^T sits
+// in TMEM as 128 lanes (output features) x BN columns (tokens).  This keeps M = 128 for any token
+// count and lets small decode batches (BN = 64) use the same kernel.
+//
+// Warp roles (320 threads):
+//   warps 0-7  dequant: wait for the quantized planes of stage s in shared memory (TMA), expand
+//              them to bf16 directly in the UMMA 128B-swizzle K-major layout, fence the async proxy,
+//              signal "A full"; after the mainloop they run the epilogue (tcgen05.ld -> global).
+//   warp 8     TMA producer: quantized weight planes and the activation tile of every stage.
+//   warp 9     MMA issuer: one elected thread issues 4 x tcgen05.mma (K = 16) per 64-wide stage and
+//              commits each stage's completion to the stage's "consumed" mbarrier.
+// Every wait is bounded (tc_common.cuh); on expiry the CTA records an error word and unwinds.
+// No TMA load here uses .multicast::cluster.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "gemv_traits.cuh"
+#include "launch.h"
+#include "tc_common.cuh"
+
+namespace barq {
+
+using namespace tc;
+
+struct GemmDev {
+  int N, K, T;
+  const uint16_t* d;  // per-block f16 scale plane (Q4_0 / IQ4_NL / Q8_0 / Q6_K)
+  int mode;
+  float* out_f32;
+  __nv_bfloat16* out_bf16;
+  const float* bias;
+  int ld_out;
+  int k_splits;
+  int* err;
+};
+
+// Staging box widths (bytes per weight row per 64-wide K stage) and x-coordinate rule per plane.
+template <int WT> struct Planes;
+template <> struct Planes<W_Q4_K> {
+  static constexpr int w0 = 32, w1 = 0, w2 = 16;
+  static BARQ_DEV int x0(int s) { return 32 * s; }
+  static BARQ_DEV int x1(int) { return 0; }
+  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
+};
+template <> struct Planes<W_Q5_K> {
+  static constexpr int w0 = 32, w1 = 32, w2 = 16;
+  static BARQ_DEV int x0(int s) { return 32 * s; }
+  static BARQ_DEV int x1(int s) { return 32 * (s >> 2); }
+  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
+};
+template <> struct Planes<W_Q6_K> {
+  static constexpr int w0 = 64, w1 = 32, w2 = 16;
+  static BARQ_DEV int x0(int s) { return 64 * (s >> 1); }
+  static BARQ_DEV int x1(int s) { return 32 * (s >> 1); }
+  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
+};
+template <> struct Planes<W_Q8_0> {
+  static constexpr int w0 = 64, w1 = 0, w2 = 0;
+  static BARQ_DEV int x0(int s) { return 64 * s; }
+  static BARQ_DEV int x1(int) { return 0; }
+  static BARQ_DEV int x2(int) { return 0; }
+};
+template <> struct Planes<W_Q4_0> {
+  static constexpr int w0 = 32, w1 = 0, w2 = 0;
+  static BARQ_DEV int x0(int s) { return 32 * s; }
+  static BARQ_DEV int x1(int) { return 0; }
+  static BARQ_DEV int x2(int) { return 0; }
+};
+template <> struct Planes<W_IQ4_NL> : Planes<W_Q4_0> {};
+
+__device__ __constant__ float kNL[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f,
+                                         1.f,    13.f,   25.f,  38.f,  53.f,  69.f,  89.f,  113.f};
+
+// Dequantize this thread's 32 weights of stage s (row r, half h) into v[].
+template <int WT>
+BARQ_DEV void dequant32(const uint8_t* st0, const uint8_t* st1, const uint8_t* st2, int r, int h, int s,
+                        int grow, const GemmDev& g, float* v) {
+  using P = Planes<WT>;
+  if constexpr (WT == W_Q4_K || WT == W_Q5_K) {
+    const int j = s & 3;
+    uint4 qa = *reinterpret_cast<const uint4*>(st0 + r * 32);
+    uint4 qb = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16);
+    uint4 hd = *reinterpret_cast<const uint4*>(st2 + r * 16);
+    float d = h2f(hd.x & 0xFFFF), dmin = h2f(hd.x >> 16);
+    int sc, m;
+    kscale(hd.y, hd.z, hd.w, 2 * j + h, sc, m);
+    const float a = d * (float)sc, b = dmin * (float)m;
+    uint32_t wds[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t hw[8];
+    if constexpr (WT == W_Q5_K) {
+      uint4 ha = *reinterpret_cast<const uint4*>(st1 + r * 32);
+      uint4 hb = *reinterpret_cast<const uint4*>(st1 + r * 32 + 16);
+      hw[0] = ha.x; hw[1] = ha.y; hw[2] = ha.z; hw[3] = ha.w; hw[4] = hb.x; hw[5] = hb.y; hw[6] = hb.z; hw[7] = hb.w;
+    }
+    const int sh = h ? 4 : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int q = (wds[i] >> (8 * k + sh)) & 0xF;
+        if constexpr (WT == W_Q5_K) q |= ((hw[i] >> (8 * k + 2 * j + h)) & 1) << 4;
+        v[4 * i + k] = fmaf(a, (float)q, -b);
+      }
+    }
+  } else if constexpr (WT == W_Q6_K) {
+    const int c4 = s & 3, hh = c4 & 1, qd = 2 * hh + h;
+    const uint8_t* ql = st0 + r * 64 + ((qd & 1) ? 32 : 0);
+    uint4 qa = *reinterpret_cast<const uint4*>(ql), qb = *reinterpret_cast<const uint4*>(ql + 16);
+    uint4 ha = *reinterpret_cast<const uint4*>(st1 + r * 32), hb = *reinterpret_cast<const uint4*>(st1 + r * 32 + 16);
+    const int n = c4 >> 1;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(st2 + r * 16) + 8 * n + 2 * qd;
+    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 256) + (s >> 2)]) : 0.f;
+    const float s0 = dd * (float)sc[0], s1 = dd * (float)sc[1];
+    uint32_t wds[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    const int sh = qd >= 2 ? 4 : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int q = ((wds[i] >> (8 * k + sh)) & 0xF) | (((hw[i] >> (8 * k + 2 * qd)) & 3) << 4);
+        v[4 * i + k] = (i < 4 ? s0 : s1) * (float)(q - 32);
+      }
+    }
+  } else if constexpr (WT == W_Q8_0) {
+    const int8_t* q = reinterpret_cast<const int8_t*>(st0 + r * 64 + 32 * h);
+    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + h]) : 0.f;
+    int4 a = *reinterpret_cast<const int4*>(q), b = *reinterpret_cast<const int4*>(q + 16);
+    uint32_t wds[8] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w,
+                       (uint32_t)b.x, (uint32_t)b.y, (uint32_t)b.z, (uint32_t)b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[4 * i + k] = dd * (float)(int8_t)((wds[i] >> (8 * k)) & 0xFF);
+  } else {  // Q4_0 / IQ4_NL: block 2s+h, 16 bytes: low nibbles -> 0..15, high -> 16..31
+    uint4 qa = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16 * h);
+    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + h]) : 0.f;
+    uint32_t wds[4] = {qa.x, qa.y, qa.z, qa.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int lo = (wds[i] >> (8 * k)) & 0xF, hi = (wds[i] >> (8 * k + 4)) & 0xF;
+        if constexpr (WT == W_IQ4_NL) {
+          v[4 * i + k] = dd * kNL[lo];
+          v[16 + 4 * i + k] = dd * kNL[hi];
+        } else {
+          v[4 * i + k] = dd * (float)(lo - 8);
+          v[16 + 4 * i + k] = dd * (float)(hi - 8);
+        }
+      }
+  }
+}
+
+template <int WT, int BN, int S>
+struct GemmSmem {
+  static constexpr int A_BYTES = 128 * 128;       // 128 rows x 64 bf16
+  static constexpr int B_BYTES = BN * 128;        // BN rows x 64 bf16
+  static constexpr int QW0 = Planes<WT>::w0 * 128, QW1 = Planes<WT>::w1 * 128, QW2 = Planes<WT>::w2 * 128;
+  static constexpr int Q_BYTES = QW0 + QW1 + QW2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + S * A_BYTES;
+  static constexpr int OFF_Q = OFF_B + S * B_BYTES;
+  static constexpr int OFF_BAR = OFF_Q + S * Q_BYTES;
+  static constexpr int N_BAR = 5 * S + 1;
+  static constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
+  static constexpr int TOTAL = OFF_TMEM + 16 + 1024;  // + alignment slack
+};
+
+constexpr int kDequantWarps = 8;
+constexpr int kThreads = (kDequantWarps + 2) * 32;
+
+template <int WT, int BN, int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tp0,
+                    const __grid_constant__ CUtensorMap tp1, const __grid_constant__ CUtensorMap tp2, GemmDev g) {
+  using L = GemmSmem<WT, BN, S>;
+  using P = Planes<WT>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* fullQ = bars;
+  uint64_t* emptyQ = bars + S;
+  uint64_t* fullB = bars + 2 * S;
+  uint64_t* fullA = bars + 3 * S;
+  uint64_t* consumed = bars + 4 * S;
+  uint64_t* accFull = bars + 5 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
+  __shared__ int err_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BN;
+  const int nst_total = g.K / 64;
+  const int z = blockIdx.z;
+  const int kb = (int)((long)nst_total * z / g.k_splits), ke = (int)((long)nst_total * (z + 1) / g.k_splits);
+  const int nst = ke - kb;
+
+  if (threadIdx.x == 0) {
+    err_s = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&fullQ[i], 1);
+      mbar_init(&emptyQ[i], kDequantWarps);
+      mbar_init(&fullB[i], 1);
+      mbar_init(&fullA[i], kDequantWarps);
+      mbar_init(&consumed[i], 1);
+    }
+    mbar_init(accFull, 1);
+    fence_mbar_init();
+  }
+  if (warp == kDequantWarps + 1) tmem_alloc(tmem_slot, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  volatile int* err = &err_s;
+
+  if (warp == kDequantWarps) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tx);
+      prefetch_tmap(&tp0);
+      if (P::w1) prefetch_tmap(&tp1);
+      if (P::w2) prefetch_tmap(&tp2);
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S, ph = (i / S) & 1, ks = kb + i;
+        if (i >= S && !mbar_wait(&emptyQ[s], ph ^ 1, err, 1)) break;
+        uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
+        mbar_expect_tx(&fullQ[s], L::Q_BYTES);
+        tma_load_2d(q, &tp0, P::x0(ks), n0, &fullQ[s]);
+        if (P::w1) tma_load_2d(q + L::QW0, &tp1, P::x1(ks), n0, &fullQ[s]);
+        if (P::w2) tma_load_2d(q + L::QW0 + L::QW1, &tp2, P::x2(ks), n0, &fullQ[s]);
+        if (i >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) break;
+        mbar_expect_tx(&fullB[s], L::B_BYTES);
+        tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, t0, &fullB[s]);
+      }
+    }
+  } else if (warp == kDequantWarps + 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, BN);
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S, ph = (i / S) & 1;
+        if (!mbar_wait(&fullA[s], ph, err, 3)) break;
+        if (!mbar_wait(&fullB[s], ph, err, 4)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
+        const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
+        mma_commit(&consumed[s]);
+      }
+      mma_commit(accFull);
+    }
+  } else {
+    // ---------------------------------------------------------------- dequant producers
+    const int quad = warp & 3, h = warp >> 2;
+    const int r = quad * 32 + lane;
+    const int grow = n0 + r;
+    for (int i = 0; i < nst; ++i) {
+      const int s = i % S, ph = (i / S) & 1, ks = kb + i;
+      if (!mbar_wait(&fullQ[s], ph, err, 5)) break;
+      const uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
+      float v[32];
+      dequant32<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, h, ks, grow, g, v);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&emptyQ[s]);
+      if (i >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) break;
+      uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int chunk = 4 * h + c;
+        uint4 pk;
+        __nv_bfloat162 b0 = __floats2bfloat162_rn(v[8 * c + 0], v[8 * c + 1]);
+        __nv_bfloat162 b1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
+        __nv_bfloat162 b3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&b0);
+        pk.y = *reinterpret_cast<uint32_t*>(&b1);
+        pk.z = *reinterpret_cast<uint32_t*>(&b2);
+        pk.w = *reinterpret_cast<uint32_t*>(&b3);
+        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = pk;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&fullA[s]);
+    }
+    // ---------------------------------------------------------------- epilogue
+    mbar_wait(accFull, 0, err, 7);
+    tc_fence_after();
+    // All 256 epilogue threads agree on `run`: after this barrier nothing can set the error word.
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const bool run = !*err;
+    if (run) {
+      const int n = n0 + r;
+      const bool atomic = g.k_splits > 1;
+      float* xch = reinterpret_cast<float*>(smem + L::OFF_A);  // [4 quads][32 cols][32 lanes] for SwiGLU
+      for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+        if (g.mode == EPI_SWIGLU_Q8) {
+          // rows [32 gate | 32 up] x 2 groups: quads 0,2 gate; 1,3 up.  The two halves (h) take
+          // disjoint columns and disjoint exchange buffers.
+          float* buf = xch + (h * 4 + quad) * 32 * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = v[j];
+          asm volatile("bar.sync 1, 256;" ::: "memory");
+          if ((quad & 1) == 0) {
+            const float* up = xch + (h * 4 + quad + 1) * 32 * 32;
+            const int f = n0 / 2 + (quad >> 1) * 32 + lane;
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) {
+              const int t = t0 + c0 + j;
+              if (t < g.T && f < g.N / 2)
+                g.out_bf16[(size_t)t * g.ld_out + f] = __float2bfloat16(silu(v[j]) * up[j * 32 + lane]);
+            }
+          }
+          asm volatile("bar.sync 1, 256;" ::: "memory");
+          continue;
+        }
+        if (n < g.N) {
+          const float bias = (g.bias && z == 0) ? g.bias[n] : 0.f;
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            const int t = t0 + c0 + j;
+            if (t >= g.T) break;
+            const size_t idx = (size_t)t * g.ld_out + n;
+            const float val = v[j] + bias;
+            if (g.mode == EPI_STORE_BF16) {
+              g.out_bf16[idx] = __float2bfloat16(val);
+            } else if (atomic) {
+              atomicAdd(g.out_f32 + idx, val);
+            } else if (g.mode == EPI_ADD_F32) {
+              g.out_f32[idx] += val;
+            } else {
+              g.out_f32[idx] = val;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kDequantWarps + 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+  if (threadIdx.x == 0 && err_s && g.err) atomicExch(g.err, err_s);
+}
+
+// ------------------------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static int make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                       uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                       CUtensorMapSwizzle sw) {
+  auto enc = get_encode();
+  if (!enc) return -10;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -11;
+}
+
+static int* device_err_word() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::unordered_map<int, int*> words;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = words.find(dev);
+  if (it != words.end()) return it->second;
+  int* p = nullptr;
+  if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+  cudaMemset(p, 0, sizeof(int));
+  words[dev] = p;
+  return p;
+}
+
+int gemm_error_word(int* host_out) {
+  int* p = device_err_word();
+  if (!p) return -1;
+  return cudaMemcpy(host_out, p, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
+int gemm_clear_error_word() {
+  int* p = device_err_word();
+  return p && cudaMemset(p, 0, sizeof(int)) == cudaSuccess ? 0 : -1;
+}
+
+template <int WT, int BN, int S>
+static int launch_gemm(const QW& w, const CUtensorMap& tx, const CUtensorMap& m0, const CUtensorMap& m1,
+                       const CUtensorMap& m2, const GemmDev& g, int tiles_t, cudaStream_t st) {
+  using L = GemmSmem<WT, BN, S>;
+  static_assert(L::TOTAL <= 232448, "shared memory budget");
+  auto kern = qgemm_tc_kernel<WT, BN, S>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  dim3 grid((w.N + 127) / 128, tiles_t, g.k_splits);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(tx, m0, m1, m2, g);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
+}
+
+template <int WT>
+static int dispatch_bn(const QW& w, const __nv_bfloat16* x, int T, const GemmDev& g0, cudaStream_t st) {
+  using P = Planes<WT>;
+  GemmDev g = g0;
+  const int K = w.K, N = w.N;
+  CUtensorMap mx, m0, m1, m2;
+  memset(&m1, 0, sizeof(m1));
+  memset(&m2, 0, sizeof(m2));
+  int bn = T <= 64 ? 64 : (T <= 128 ? 128 : 256);
+  int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, T, (uint64_t)K * 2, 64, bn,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  uint64_t rb0 = WT == W_Q8_0 ? K : (WT == W_Q6_K ? K / 2 : K / 2);
+  rc = make_map_2d(&m0, w.p0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb0, N, rb0, P::w0, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (P::w1) {
+    uint64_t rb1 = WT == W_Q5_K ? K / 8 : K / 4;
+    rc = make_map_2d(&m1, w.p1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb1, N, rb1, P::w1, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  if (P::w2) {
+    uint64_t rb2 = WT == W_Q6_K ? K / 16 : (K / 256) * 16;
+    rc = make_map_2d(&m2, w.p2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb2, N, rb2, P::w2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  const int tiles_t = (T + bn - 1) / bn;
+  if (g.k_splits == 0) {  // auto split-K so that small token counts still fill the 148 SMs
+    const int tiles = ((N + 127) / 128) * tiles_t, nst = K / 64;
+    int ks = 1;
+    if (g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32)
+      while (tiles * ks * 2 <= 2 * 148 && nst / (ks * 2) >= 4) ks *= 2;
+    g.k_splits = ks;
+  }
+  if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
+    if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)N * 4, T, st) != cudaSuccess) return -6;
+  }
+  if (bn == 64) return launch_gemm<WT, 64, 5>(w, mx, m0, m1, m2, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, 4>(w, mx, m0, m1, m2, g, tiles_t, st);
+  return launch_gemm<WT, 256, 3>(w, mx, m0, m1, m2, g, tiles_t, st);
+}
+
+int qgemm_tc(const QW& w, const __nv_bfloat16* x, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (w.K % 256 && !(w.K % 64 == 0 && (w.type == W_Q8_0 || w.type == W_Q4_0 || w.type == W_IQ4_NL))) return -2;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (w.K * 2) % 16) return -3;
+  if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128 || k_splits > 1)) return -4;
+  if (ep.mode == EPI_SWIGLU_Q8 || ep.mode == EPI_STORE_BF16) k_splits = 1;
+  if (k_splits < 0) k_splits = 0;
+  GemmDev g;
+  g.N = w.N;
+  g.K = w.K;
+  g.T = T;
+  g.d = w.d;
+  g.mode = ep.mode;
+  g.out_f32 = ep.out_f32;
+  g.out_bf16 = ep.out_bf16;
+  g.bias = ep.bias;
+  g.ld_out = ep.ld_out;
+  g.k_splits = k_splits;
+  g.err = device_err_word();
+  switch (w.type) {
+    case W_Q4_K: return dispatch_bn<W_Q4_K>(w, x, T, g, st);
+    case W_Q5_K: return dispatch_bn<W_Q5_K>(w, x, T, g, st);
+    case W_Q6_K: return dispatch_bn<W_Q6_K>(w, x, T, g, st);
+    case W_Q8_0: return dispatch_bn<W_Q8_0>(w, x, T, g, st);
+    case W_Q4_0: return dispatch_bn<W_Q4_0>(w, x, T, g, st);
+    case W_IQ4_NL: return dispatch_bn<W_IQ4_NL>(w, x, T, g, st);
+  }
+  return -7;
+}
+
+}  // namespace barq

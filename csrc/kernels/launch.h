@@ -23,6 +23,13 @@ struct GemvEpi {
 int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B, const GemvEpi& ep,
           cudaStream_t st);
 
+// K2 tcgen05 quantized GEMM: out[t, n] (+)= x[t, :] . W[n, :], x bf16 [T, K] (row pitch K).
+// Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
+// 0 = automatic (f32 modes only; accumulated with atomics).
+int qgemm_tc(const QW& w, const __nv_bfloat16* x, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
+int gemm_error_word(int* host_out);
+int gemm_clear_error_word();
+
 // Fused (residual add +) RMSNorm.  x: f32 [T, H] residual stream (updated in place when `add`
 // is given: x += add).  Outputs any of bf16 [T, H] and int8 q8 [T, H] + scales [T, H/32].
 int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,

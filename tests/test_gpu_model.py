@@ -82,3 +82,40 @@ def test_engine_sampling_runs():
     r = eng.generate([prompt] * 3, SamplingParams(max_tokens=12, temperature=0.9, top_k=40, top_p=0.95, seed=3))
     assert all(len(x.tokens) == 12 for x in r)
     assert all(0 <= t < cfg.vocab for x in r for t in x.tokens)
+
+
+def test_small_q4k_gemm_and_gemv_paths_match_reference():
+    """Llama-3-style (Q4_K + Q6_K head) small model: prefill on the tcgen05 GEMM path and decode on the
+    GEMV path both track the fp32 reference."""
+    cfg = preset("llama3-8b", n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024, vocab=1000,
+                 max_ctx=512)
+    tensors = random_tensors(cfg, POLICIES["llama3-8b"], seed=4)
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, cfg.vocab, (100,), generator=g).tolist()
+    ref = ReferenceModel(cfg, tensors)
+    ref_tokens, ref_logits = ref.greedy(prompt, 4)
+    runner = LlamaRunner(cfg, tensors, DEV)
+    runner.allocate_kv(64)
+    table = list(range(1, 12))
+    lg = _run(runner, prompt, 0, table, decode=False)
+    scale = ref_logits[0].abs().max().item()
+    assert (lg - ref_logits[0]).abs().max().item() < 2e-2 * scale
+    pos = len(prompt)
+    for i, t in enumerate(ref_tokens[:-1]):
+        lg = _run(runner, [t], pos, table, decode=True)
+        pos += 1
+        assert (lg - ref_logits[i + 1]).abs().max().item() < 1e-2 * scale
+
+
+def test_batched_decode_gemm_path_matches_gemv_path():
+    cfg = preset("llama3-8b", n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024, vocab=1000,
+                 max_ctx=512)
+    tensors = random_tensors(cfg, POLICIES["llama3-8b"], seed=4)
+    prompts = [list(range(i, i + 20 + i)) for i in range(20)]
+    outs = []
+    for gemm in (True, False):
+        eng = Engine(cfg, tensors, EngineConfig(max_num_seqs=32, max_model_len=256, num_blocks=256, cuda_graphs=False))
+        eng.runner.use_gemm = gemm
+        outs.append([r.tokens for r in eng.generate(prompts, SamplingParams.greedy_params(max_tokens=6))])
+    same = sum(a == b for a, b in zip(outs[0], outs[1]))
+    assert same >= 18, same
