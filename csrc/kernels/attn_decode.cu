@@ -176,12 +176,25 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeAttnArgs a) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int G = a.H / a.Hkv, kvh = h / G, g = h % G;
   const size_t base = ((size_t)b * a.Hkv + kvh) * a.splits;
-  float M = -1e30f;
-  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.part_ml[(base + s) * G + g].x);
+  // (max, sum) of every split staged in shared memory with one parallel load, then a single pass
+  // over the partial accumulators with independent (unrolled) loads.
+  __shared__ float2 ml_s[64];
+  __shared__ float M_s;
+  for (int s = d; s < a.splits; s += D) ml_s[s] = a.part_ml[(base + s) * G + g];
+  __syncthreads();
+  if (d < 32) {
+    float mx = -1e30f;
+    for (int s = d; s < a.splits; s += 32) mx = fmaxf(mx, ml_s[s].x);
+    mx = warp_max(mx);
+    if (d == 0) M_s = mx;
+  }
+  __syncthreads();
+  const float M = M_s;
   float A = 0.f, L = 0.f;
+#pragma unroll 8
   for (int s = 0; s < a.splits; ++s) {
-    float2 ml = a.part_ml[(base + s) * G + g];
-    float f = exp2f(ml.x - M);
+    const float2 ml = ml_s[s];
+    const float f = exp2f(ml.x - M);
     L += ml.y * f;
     A += a.part_acc[((base + s) * G + g) * D + d] * f;
   }
@@ -212,6 +225,7 @@ static int launch_g(const DecodeAttnArgs& a, cudaStream_t st) {
 
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st) {
   if (a.block_size != kBS) return -1;
+  if (a.splits < 1 || a.splits > 64) return -5;
   if (a.H % a.Hkv) return -2;
   if (a.B <= 0) return 0;
   if (a.D == 128) return a.cache_is_bf16 ? launch_g<__nv_bfloat16, 128>(a, st) : launch_g<__half, 128>(a, st);

@@ -10,16 +10,18 @@
 
 namespace barq {
 
-// One CTA per token row.  blockDim = 256.
-__global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
+// One CTA per token row, 1024 threads (32 warps), so a decode row of 4096 values is 4 groups of
+// 32 per warp: the per-group quantization reductions run in parallel instead of in series.
+constexpr int kNormThreads = 1024;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
                                                       const float* __restrict__ w, float eps, int H,
                                                       __nv_bfloat16* __restrict__ ob, ActOut oq) {
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * H;
   const float* ar = add ? add + (size_t)t * H : nullptr;
-  __shared__ float red[8];
+  __shared__ float red[32];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += 256) {
+  for (int i = threadIdx.x; i < H; i += kNormThreads) {
     float v = xr[i];
     if (ar) {
       v += ar[i];
@@ -31,7 +33,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    float v = red[threadIdx.x];
     v = warp_sum(v);
     if (threadIdx.x == 0) red[0] = v;
   }
@@ -40,7 +42,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
   // Each warp walks 32-value groups so the q8 quantization of a group happens inside one warp.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ngroups = (H + 31) / 32;
-  for (int g = warp; g < ngroups; g += 8) {
+  for (int g = warp; g < ngroups; g += kNormThreads / 32) {
     int i = g * 32 + lane;
     float v = i < H ? xr[i] * r * w[i] : 0.f;
     if (ob && i < H) ob[(size_t)t * H + i] = __float2bfloat16(v);
@@ -52,7 +54,7 @@ int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H,
             ActOut out_q, cudaStream_t st) {
   if (out_q.q && (H % 32)) return -1;
   if (T <= 0) return 0;
-  rmsnorm_kernel<<<T, 256, 0, st>>>(x, add, w, eps, H, out_bf16, out_q);
+  rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, add, w, eps, H, out_bf16, out_q);
   return 0;
 }
 

@@ -77,8 +77,9 @@ template <> struct Planes<W_Q4_0> {
 };
 template <> struct Planes<W_IQ4_NL> : Planes<W_Q4_0> {};
 
-__device__ __constant__ float kNL[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f,
-                                         1.f,    13.f,   25.f,  38.f,  53.f,  69.f,  89.f,  113.f};
+// Small non-negative integer -> float at full ALU rate: OR it into the mantissa of 2^23 and subtract
+// (exact for 0 <= v < 2^23).  `bias` is subtracted too, so callers fold their zero point into it.
+BARQ_DEV float u2f(uint32_t v, float bias) { return __uint_as_float(0x4B000000u | v) - (8388608.0f + bias); }
 
 // Dequantize this thread's 32 weights of stage s (row r, half h) into v[].
 template <int WT>
@@ -106,9 +107,9 @@ BARQ_DEV void dequant32(const uint8_t* st0, const uint8_t* st1, const uint8_t* s
     for (int i = 0; i < 8; ++i) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        int q = (wds[i] >> (8 * k + sh)) & 0xF;
+        uint32_t q = (wds[i] >> (8 * k + sh)) & 0xF;
         if constexpr (WT == W_Q5_K) q |= ((hw[i] >> (8 * k + 2 * j + h)) & 1) << 4;
-        v[4 * i + k] = fmaf(a, (float)q, -b);
+        v[4 * i + k] = fmaf(a, u2f(q, 0.f), -b);
       }
     }
   } else if constexpr (WT == W_Q6_K) {
@@ -127,8 +128,8 @@ BARQ_DEV void dequant32(const uint8_t* st0, const uint8_t* st1, const uint8_t* s
     for (int i = 0; i < 8; ++i) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        int q = ((wds[i] >> (8 * k + sh)) & 0xF) | (((hw[i] >> (8 * k + 2 * qd)) & 3) << 4);
-        v[4 * i + k] = (i < 4 ? s0 : s1) * (float)(q - 32);
+        uint32_t q = ((wds[i] >> (8 * k + sh)) & 0xF) | (((hw[i] >> (8 * k + 2 * qd)) & 3) << 4);
+        v[4 * i + k] = (i < 4 ? s0 : s1) * u2f(q, 32.f);
       }
     }
   } else if constexpr (WT == W_Q8_0) {
@@ -140,24 +141,26 @@ BARQ_DEV void dequant32(const uint8_t* st0, const uint8_t* st1, const uint8_t* s
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[4 * i + k] = dd * (float)(int8_t)((wds[i] >> (8 * k)) & 0xFF);
+      for (int k = 0; k < 4; ++k) v[4 * i + k] = dd * u2f(((wds[i] >> (8 * k)) & 0xFF) ^ 0x80u, 128.f);
   } else {  // Q4_0 / IQ4_NL: block 2s+h, 16 bytes: low nibbles -> 0..15, high -> 16..31
     uint4 qa = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16 * h);
     const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + h]) : 0.f;
     uint32_t wds[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 4; ++i) {
+      uint32_t lo4 = wds[i] & 0x0F0F0F0Fu, hi4 = (wds[i] >> 4) & 0x0F0F0F0Fu;
+      if constexpr (WT == W_IQ4_NL) {  // codebook through byte permutes, then signed byte + 128
+        const int t0 = 0xBFAD9881, t1 = 0xF6EADDCF, t2 = 0x26190D01, t3 = 0x71594535;
+        lo4 = (uint32_t)lut16((int)lo4, t0, t1, t2, t3) ^ 0x80808080u;
+        hi4 = (uint32_t)lut16((int)hi4, t0, t1, t2, t3) ^ 0x80808080u;
+      }
+      const float zp = WT == W_IQ4_NL ? 128.f : 8.f;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        int lo = (wds[i] >> (8 * k)) & 0xF, hi = (wds[i] >> (8 * k + 4)) & 0xF;
-        if constexpr (WT == W_IQ4_NL) {
-          v[4 * i + k] = dd * kNL[lo];
-          v[16 + 4 * i + k] = dd * kNL[hi];
-        } else {
-          v[4 * i + k] = dd * (float)(lo - 8);
-          v[16 + 4 * i + k] = dd * (float)(hi - 8);
-        }
+        v[4 * i + k] = dd * u2f((lo4 >> (8 * k)) & 0xFF, zp);
+        v[16 + 4 * i + k] = dd * u2f((hi4 >> (8 * k)) & 0xFF, zp);
       }
+    }
   }
 }
 
@@ -317,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if ((quad & 1) == 0) {
             const float* up = xch + (h * 4 + quad + 1) * 32 * 32;
             const int f = n0 / 2 + (quad >> 1) * 32 + lane;
-#pragma unroll 4
+#pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int t = t0 + c0 + j;
               if (t < g.T && f < g.N / 2)
@@ -329,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (n < g.N) {
           const float bias = (g.bias && z == 0) ? g.bias[n] : 0.f;
-#pragma unroll 4
+#pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int t = t0 + c0 + j;
-            if (t >= g.T) break;
+            if (t >= g.T) continue;
             const size_t idx = (size_t)t * g.ld_out + n;
             const float val = v[j] + bias;
             if (g.mode == EPI_STORE_BF16) {

@@ -43,21 +43,18 @@ BARQ_DEV int lut16(int codes /* 4 bytes, each 0..15 */, int t0, int t1, int t2, 
   return (int)__byte_perm(lo, hi, pick);
 }
 
-// Unpack 6-bit (scale, min) number `is` (0..7) of the 12-byte K-quant scale field.
+// Unpack 6-bit (scale, min) number `is` (0..7) of the 12-byte K-quant scale field held in three
+// little-endian words (bytes 0-3, 4-7, 8-11).  Register-only: runtime shifts, no indexed arrays.
 BARQ_DEV void kscale(uint32_t s0, uint32_t s1, uint32_t s2, int is, int& sc, int& m) {
-  uint32_t b[12];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    b[i] = (s0 >> (8 * i)) & 0xFF;
-    b[4 + i] = (s1 >> (8 * i)) & 0xFF;
-    b[8 + i] = (s2 >> (8 * i)) & 0xFF;
-  }
   if (is < 4) {
-    sc = b[is] & 63;
-    m = b[is + 4] & 63;
+    const int sh = 8 * is;
+    sc = (s0 >> sh) & 63;
+    m = (s1 >> sh) & 63;
   } else {
-    sc = (b[is + 4] & 0xF) | ((b[is - 4] >> 6) << 4);
-    m = (b[is + 4] >> 4) | ((b[is] >> 6) << 4);
+    const int sh = 8 * (is - 4);
+    const uint32_t hi = (s2 >> sh) & 0xFF;
+    sc = (hi & 0xF) | (((s0 >> sh) >> 6 & 3) << 4);
+    m = (hi >> 4) | (((s1 >> sh) >> 6 & 3) << 4);
   }
 }
 
