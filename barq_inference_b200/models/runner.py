@@ -68,6 +68,9 @@ class LlamaRunner:
         self.use_gemm = use_gemm
         # two-term int8 decode activations (accurate mode); False = single int8 term (fastest)
         self.x2 = act_x2
+        # dtype of the tensor-core GEMM activations: fp16 (more mantissa, 1-instruction nibble
+        # expansion in the GEMM mainloop) unless the family is known to overflow fp16 (DeepSeek)
+        self.act_dtype = torch.bfloat16 if cfg.arch.startswith("deepseek") else torch.float16
         dev = self.device
         self.embed_w = _qw(tensors["token_embd.weight"], dev)
         self.out_norm = _f32(tensors["output_norm.weight"], dev)
@@ -155,6 +158,7 @@ class LlamaRunner:
                 return out
             return r
         if w.wtype == ops.W_BF16:  # dense weights (non-blocked GGUF tensors): GEMV in chunks
+            xb = xb.to(torch.bfloat16)
             if out is None:
                 out = torch.empty(T, w.N, dtype=torch.float32, device=self.device)
             for t0 in range(0, T, GEMV_MAX_T):
@@ -184,9 +188,9 @@ class LlamaRunner:
                               cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
         if inp.decode:
             return ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
-                                        cfg.sliding_window, want_q8=want_q8, x2=self.x2)
+                                        cfg.sliding_window, want_q8=want_q8, x2=self.x2, act_dtype=self.act_dtype)
         ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
-                                   H, Hkv, D, self.scale, cfg.sliding_window)
+                                   H, Hkv, D, self.scale, cfg.sliding_window, act_dtype=self.act_dtype)
         return ab, (ops.quantize_q8(ab, self.x2) if want_q8 else None)
 
     def _forward_gemm(self, inp: StepInput) -> torch.Tensor:
@@ -195,12 +199,12 @@ class LlamaRunner:
         T = inp.ids.numel()
         x = ops.embed(self.embed_w, inp.ids)
         for li, L in enumerate(self.layers):
-            hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True)
+            hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
             qkv = self._lin_bf16(L.qkv, hb, T, EPI_STORE_F32, bias=L.qkv_bias)
             ab, _ = self._attention(L, li, qkv, inp, T, want_q8=False)
             self._lin_bf16(L.wo, ab, T, EPI_ADD_F32, out=x)
             hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_bf16=True,
-                                 want_q8=L.moe is not None, x2=self.x2)
+                                 want_q8=L.moe is not None, x2=self.x2, act_dtype=self.act_dtype)
             if L.moe is not None:
                 L.moe.forward(self, hq, hb, T, x)
                 continue
@@ -208,13 +212,13 @@ class LlamaRunner:
                 h = ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
             else:
                 gu = self._lin_bf16(L.gate_up, hb, T, EPI_STORE_F32)
-                h, _ = ops.swiglu(gu, cfg.ffn, want_bf16=True)
+                h, _ = ops.swiglu(gu, cfg.ffn, want_bf16=True, act_dtype=self.act_dtype)
             self._lin_bf16(L.down, h, T, EPI_ADD_F32, out=x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
-        ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True)
+        ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
         if xl.shape[0] <= GEMV_MAX_T:
             _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
-            return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32, xb=ob)
+            return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32, xb=ob.to(torch.bfloat16))
         return self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32)
 
     def _forward_gemv(self, inp: StepInput) -> torch.Tensor:

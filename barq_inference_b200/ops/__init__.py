@@ -86,10 +86,10 @@ def quantize_q8(x: torch.Tensor, x2: bool = False) -> Q8Act:
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, add: torch.Tensor | None = None,
-            want_bf16: bool = False, want_q8: bool = False, x2: bool = False):
-    """x (f32 [T,H], updated in place by ``add``) -> (bf16 | None, Q8Act | None)."""
+            want_bf16: bool = False, want_q8: bool = False, x2: bool = False, act_dtype=torch.bfloat16):
+    """x (f32 [T,H], updated in place by ``add``) -> (activation [T,H] in ``act_dtype`` | None, Q8Act | None)."""
     T, H = x.shape
-    ob = torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None
+    ob = torch.empty(T, H, dtype=act_dtype, device=x.device) if want_bf16 else None
     oq = Q8Act.empty(T, H, x.device, x2) if want_q8 else None
     require_ext().rmsnorm(x, add, w, eps, ob, *_outs(oq))
     _count()
@@ -122,18 +122,17 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
 
 def gemm(w: QWeight, x: torch.Tensor, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
          bias: torch.Tensor | None = None, k_splits: int = 0) -> torch.Tensor:
-    """tcgen05 quantized GEMM: x bf16 [T, K] -> out (f32/bf16 [T, N]; SwiGLU mode: bf16 [T, N/2]).
+    """tcgen05 quantized GEMM: x fp16/bf16 [T, K] -> out (f32 or x.dtype [T, N]; SwiGLU: x.dtype [T, N/2]).
 
     ``k_splits`` 0 = automatic split-K for the f32 modes (accumulated with atomics)."""
     T = x.shape[0]
     if mode == EPI_SWIGLU_Q8:
         if out is None:
-            out = torch.empty(T, w.N // 2, dtype=torch.bfloat16, device=x.device)
+            out = torch.empty(T, w.N // 2, dtype=x.dtype, device=x.device)
     elif out is None:
-        out = torch.empty(T, w.N, dtype=torch.bfloat16 if mode == EPI_STORE_BF16 else torch.float32,
-                          device=x.device)
+        out = torch.empty(T, w.N, dtype=x.dtype if mode == EPI_STORE_BF16 else torch.float32, device=x.device)
     f32 = out if out.dtype == torch.float32 else None
-    bf = out if out.dtype == torch.bfloat16 else None
+    bf = out if out.dtype != torch.float32 else None
     require_ext().qgemm(*w.args(), x, T, mode, f32, bf, bias, out.stride(0), k_splits)
     _count(2 if (k_splits != 1 and mode == EPI_STORE_F32) else 1)
     return out
@@ -144,9 +143,10 @@ def gemm_error() -> int:
     return int(require_ext().gemm_error())
 
 
-def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False, x2: bool = False):
+def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = False, x2: bool = False,
+           act_dtype=torch.bfloat16):
     T = gu.shape[0]
-    ob = torch.empty(T, F, dtype=torch.bfloat16, device=gu.device) if want_bf16 else None
+    ob = torch.empty(T, F, dtype=act_dtype, device=gu.device) if want_bf16 else None
     oq = Q8Act.empty(T, F, gu.device, x2) if want_q8 else None
     require_ext().swiglu(gu, T, F, gu.stride(0), ob, *_outs(oq))
     _count()
@@ -170,7 +170,7 @@ def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
 
 
 def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,
-                     want_q8=True, scratch=None, x2=False):
+                     want_q8=True, scratch=None, x2=False, act_dtype=torch.bfloat16):
     B = q.shape[0]
     C = require_ext()
     if splits is None:
@@ -178,7 +178,7 @@ def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale
     if scratch is None:
         scratch = torch.empty(C.decode_attention_scratch_floats(B, H, Hkv, D, splits), dtype=torch.float32,
                               device=q.device)
-    out = torch.empty(B, H * D, dtype=torch.bfloat16, device=q.device)
+    out = torch.empty(B, H * D, dtype=act_dtype, device=q.device)
     oq = Q8Act.empty(B, H * D, q.device, x2) if want_q8 else None
     C.decode_attention(q, kcache, vcache, block_tables, seq_lens, B, H, Hkv, D, scale, window, splits, scratch,
                        out, *_outs(oq))
@@ -186,10 +186,11 @@ def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale
     return out, oq
 
 
-def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0):
+def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0,
+                      act_dtype=torch.bfloat16):
     T = q.shape[0]
     S = block_tables.shape[0]
-    out = torch.empty(T, H * D, dtype=torch.bfloat16, device=q.device)
+    out = torch.empty(T, H * D, dtype=act_dtype, device=q.device)
     require_ext().prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, S, max_q, H, Hkv, D,
                                     scale, window, out)
     _count()

@@ -24,6 +24,8 @@ void check(int rc, const char* what) {
   TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
 }
 
+int is_f16(const OptT& t) { return t.has_value() && t->defined() && t->scalar_type() == torch::kHalf; }
+
 barq::ActOut act_out(const OptT& q, const OptT& s, const OptT& ql, const OptT& dl) {
   return barq::ActOut{optptr<int8_t>(q), optptr<float2>(s), optptr<int8_t>(ql), optptr<float2>(dl)};
 }
@@ -57,11 +59,15 @@ void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT
 void qgemm(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor x, int64_t T, int64_t mode,
            OptT out_f32, OptT out_bf16, OptT bias, int64_t ld_out, int64_t k_splits) {
   c10::cuda::CUDAGuard g(p0.device());
-  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(-1) == K, "qgemm: x must be bf16 [T, K]");
+  const bool f16 = x.scalar_type() == torch::kHalf;
+  TORCH_CHECK((f16 || x.scalar_type() == torch::kBFloat16) && x.is_contiguous() && x.size(-1) == K,
+              "qgemm: x must be fp16 or bf16 [T, K]");
+  if (out_bf16.has_value() && out_bf16->defined())
+    TORCH_CHECK(out_bf16->scalar_type() == x.scalar_type(), "qgemm: activation output must have x's dtype");
   barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
   barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16), barq::ActOut{},
                    optptr<const float>(bias), (int)ld_out};
-  check(barq::qgemm_tc(w, ptr<const __nv_bfloat16>(x), (int)T, ep, (int)k_splits, cur_stream()), "qgemm");
+  check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, (int)k_splits, cur_stream()), "qgemm");
 }
 
 int64_t gemm_error() {
@@ -79,7 +85,7 @@ void rmsnorm(Tensor x, OptT add, Tensor w, double eps, OptT out_bf16, OptT out_q
   TORCH_CHECK(x.scalar_type() == torch::kFloat32, "rmsnorm: residual stream must be f32");
   int H = (int)x.size(-1), T = (int)(x.numel() / H);
   check(barq::rmsnorm(ptr<float>(x), optptr<const float>(add), ptr<const float>(w), (float)eps, T, H,
-                      optptr<__nv_bfloat16>(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
+                      optptr<void>(out_bf16), is_f16(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
         "rmsnorm");
 }
 
@@ -94,7 +100,7 @@ void swiglu(Tensor in, int64_t T, int64_t F, int64_t ld_in, OptT out_bf16, OptT 
             OptT out_dl) {
   c10::cuda::CUDAGuard g(in.device());
   check(barq::swiglu(in.data_ptr(), in.scalar_type() == torch::kBFloat16, (int)T, (int)F, (int)ld_in,
-                     optptr<__nv_bfloat16>(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
+                     optptr<void>(out_bf16), is_f16(out_bf16), act_out(out_q, out_s, out_ql, out_dl), cur_stream()),
         "swiglu");
 }
 
@@ -144,7 +150,8 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.splits = (int)splits;
   a.part_acc = ptr<float>(scratch);
   a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)B * H * splits * D);
-  a.out = ptr<__nv_bfloat16>(out);
+  a.out = out.data_ptr();
+  a.out_f16 = out.scalar_type() == torch::kHalf;
   a.out_q = act_out(out_q, out_s, out_ql, out_dl);
   check(barq::decode_attention(a, cur_stream()), "decode_attention");
 }
@@ -166,7 +173,8 @@ void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tabl
   a.block_size = (int)kcache.size(-2);
   a.scale = (float)scale;
   a.window = (int)window;
-  a.out = ptr<__nv_bfloat16>(out);
+  a.out = out.data_ptr();
+  a.out_f16 = out.scalar_type() == torch::kHalf;
   check(barq::prefill_attention(a, cur_stream()), "prefill_attention");
 }
 

@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeAttnArgs a) {
   }
   float o = L > 0.f ? A / L : 0.f;
   const size_t oi = (size_t)b * a.H * D + (size_t)h * D + d;
-  a.out[oi] = __float2bfloat16(o);
+  store_act(a.out, oi, o, a.out_f16);
   if (a.out_q.q) act_store32(a.out_q, o, oi, oi / 32, d & 31);
 }
 

@@ -234,11 +234,16 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
     int qi = q0 + warp * 16 + g + r * 8;
     if (qi >= n_new) continue;
     float inv = lrow[r] > 0.f ? 1.f / lrow[r] : 0.f;
-    __nv_bfloat16* dst = a.out + ((size_t)(q_begin + qi) * a.H + h) * D;
+    const size_t base = ((size_t)(q_begin + qi) * a.H + h) * D;
 #pragma unroll
     for (int j = 0; j < ND; ++j) {
-      __nv_bfloat162 v = __floats2bfloat162_rn(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
-      *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * tig) = v;
+      const float v0 = o[j][2 * r] * inv, v1 = o[j][2 * r + 1] * inv;
+      if (a.out_f16) {
+        *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(a.out) + base + j * 8 + 2 * tig) = __floats2half2_rn(v0, v1);
+      } else {
+        *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(a.out) + base + j * 8 + 2 * tig) =
+            __floats2bfloat162_rn(v0, v1);
+      }
     }
   }
 }

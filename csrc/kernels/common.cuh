@@ -53,6 +53,14 @@ BARQ_DEV int4 ldg16_stream(const void* p) {
   return r;
 }
 
+// Activation store in the run-time activation dtype (fp16 or bf16).
+BARQ_DEV void store_act(void* p, size_t i, float v, int f16) {
+  if (f16)
+    reinterpret_cast<__half*>(p)[i] = __float2half(v);
+  else
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
+}
+
 // Quantize 32 consecutive values held one per lane into int8 with a shared scale.
 // Returns the lane's int8 value; lane 0's (d, d*sum) is written by the caller.
 BARQ_DEV int8_t quant_lane32(float v, float& d_out, float& s_out) {

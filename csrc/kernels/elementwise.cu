@@ -15,7 +15,7 @@ namespace barq {
 constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
                                                       const float* __restrict__ w, float eps, int H,
-                                                      __nv_bfloat16* __restrict__ ob, ActOut oq) {
+                                                      void* __restrict__ ob, int ob_f16, ActOut oq) {
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * H;
   const float* ar = add ? add + (size_t)t * H : nullptr;
@@ -45,16 +45,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict
   for (int g = warp; g < ngroups; g += kNormThreads / 32) {
     int i = g * 32 + lane;
     float v = i < H ? xr[i] * r * w[i] : 0.f;
-    if (ob && i < H) ob[(size_t)t * H + i] = __float2bfloat16(v);
+    if (ob && i < H) store_act(ob, (size_t)t * H + i, v, ob_f16);
     if (oq.q) act_store32(oq, v, (size_t)t * H + i, (size_t)t * (H / 32) + g, lane);
   }
 }
 
-int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
+int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, void* out_act, int out_f16,
             ActOut out_q, cudaStream_t st) {
   if (out_q.q && (H % 32)) return -1;
   if (T <= 0) return 0;
-  rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, add, w, eps, H, out_bf16, out_q);
+  rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, add, w, eps, H, out_act, out_f16, out_q);
   return 0;
 }
 
@@ -80,7 +80,7 @@ int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_
 }
 
 template <typename T>
-__global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, __nv_bfloat16* __restrict__ ob,
+__global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, void* __restrict__ ob, int ob_f16,
                               ActOut oq) {
   const int t = blockIdx.y;
   const int lane = threadIdx.x & 31;
@@ -89,19 +89,19 @@ __global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, __nv_bflo
   if (g * 32 >= F) return;
   float h = 0.f;
   if (i < F) h = silu(to_f(in[(size_t)t * ld + i])) * to_f(in[(size_t)t * ld + F + i]);
-  if (ob && i < F) ob[(size_t)t * F + i] = __float2bfloat16(h);
+  if (ob && i < F) store_act(ob, (size_t)t * F + i, h, ob_f16);
   if (oq.q) act_store32(oq, h, (size_t)t * F + i, (size_t)t * (F / 32) + g, lane);
 }
 
-int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, ActOut out_q,
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, void* out_act, int out_f16, ActOut out_q,
            cudaStream_t st) {
   if (out_q.q && (F % 32)) return -1;
   if (T <= 0) return 0;
   dim3 g(((F + 31) / 32 + 7) / 8, T);
   if (in_is_bf16)
-    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_bf16, out_q);
+    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_act, out_f16, out_q);
   else
-    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_bf16, out_q);
+    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_act, out_f16, out_q);
   return 0;
 }
 

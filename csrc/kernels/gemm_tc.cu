@@ -21,6 +21,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "gemv_traits.cuh"
@@ -77,91 +78,116 @@ template <> struct Planes<W_Q4_0> {
 };
 template <> struct Planes<W_IQ4_NL> : Planes<W_Q4_0> {};
 
-// Small non-negative integer -> float at full ALU rate: OR it into the mantissa of 2^23 and subtract
-// (exact for 0 <= v < 2^23).  `bias` is subtracted too, so callers fold their zero point into it.
-BARQ_DEV float u2f(uint32_t v, float bias) { return __uint_as_float(0x4B000000u | v) - (8388608.0f + bias); }
+// ---- dequantization of one thread's 16 weights (row r, quarter qq of the 64-wide stage s)
+//
+// Every format is first reduced to four words of unsigned byte codes u (one code per weight, in
+// natural element order) plus (zero point zp, scale sc, bias bi) so that  w = (u - zp) * sc + bi.
+// fp16 operands: a byte permute places two codes in the mantissas of 1024.0h (exact), one packed
+// subtract removes 1024 + zp, one packed FMA applies scale and bias: ~2 instructions per weight.
+// bf16 operands: the same codes go through fp32 (mantissa of 2^23, subtract, FMA) and a packed
+// round to bf16x2.
+struct Codes {
+  uint32_t u[4];
+  float zp, sc, bi;
+};
 
-// Dequantize this thread's 32 weights of stage s (row r, half h) into v[].
 template <int WT>
-BARQ_DEV void dequant32(const uint8_t* st0, const uint8_t* st1, const uint8_t* st2, int r, int h, int s,
-                        int grow, const GemmDev& g, float* v) {
-  using P = Planes<WT>;
+BARQ_DEV Codes load_codes(const uint8_t* st0, const uint8_t* st1, const uint8_t* st2, int r, int qq, int s,
+                          int grow, const GemmDev& g) {
+  Codes c;
   if constexpr (WT == W_Q4_K || WT == W_Q5_K) {
-    const int j = s & 3;
-    uint4 qa = *reinterpret_cast<const uint4*>(st0 + r * 32);
-    uint4 qb = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16);
+    const int j = s & 3, h = qq >> 1, l0 = 16 * (qq & 1);
+    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 32 + l0);
     uint4 hd = *reinterpret_cast<const uint4*>(st2 + r * 16);
-    float d = h2f(hd.x & 0xFFFF), dmin = h2f(hd.x >> 16);
-    int sc, m;
-    kscale(hd.y, hd.z, hd.w, 2 * j + h, sc, m);
-    const float a = d * (float)sc, b = dmin * (float)m;
-    uint32_t wds[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint32_t hw[8];
+    int scl, mn;
+    kscale(hd.y, hd.z, hd.w, 2 * j + h, scl, mn);
+    c.sc = h2f(hd.x & 0xFFFF) * (float)scl;
+    c.bi = -h2f(hd.x >> 16) * (float)mn;
+    c.zp = 0.f;
+    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint32_t hb[4] = {0, 0, 0, 0};
     if constexpr (WT == W_Q5_K) {
-      uint4 ha = *reinterpret_cast<const uint4*>(st1 + r * 32);
-      uint4 hb = *reinterpret_cast<const uint4*>(st1 + r * 32 + 16);
-      hw[0] = ha.x; hw[1] = ha.y; hw[2] = ha.z; hw[3] = ha.w; hw[4] = hb.x; hw[5] = hb.y; hw[6] = hb.z; hw[7] = hb.w;
+      uint4 qh = *reinterpret_cast<const uint4*>(st1 + r * 32 + l0);
+      hb[0] = qh.x; hb[1] = qh.y; hb[2] = qh.z; hb[3] = qh.w;
     }
-    const int sh = h ? 4 : 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t q = (wds[i] >> (8 * k + sh)) & 0xF;
-        if constexpr (WT == W_Q5_K) q |= ((hw[i] >> (8 * k + 2 * j + h)) & 1) << 4;
-        v[4 * i + k] = fmaf(a, u2f(q, 0.f), -b);
-      }
-    }
-  } else if constexpr (WT == W_Q6_K) {
-    const int c4 = s & 3, hh = c4 & 1, qd = 2 * hh + h;
-    const uint8_t* ql = st0 + r * 64 + ((qd & 1) ? 32 : 0);
-    uint4 qa = *reinterpret_cast<const uint4*>(ql), qb = *reinterpret_cast<const uint4*>(ql + 16);
-    uint4 ha = *reinterpret_cast<const uint4*>(st1 + r * 32), hb = *reinterpret_cast<const uint4*>(st1 + r * 32 + 16);
-    const int n = c4 >> 1;
-    const int8_t* sc = reinterpret_cast<const int8_t*>(st2 + r * 16) + 8 * n + 2 * qd;
-    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 256) + (s >> 2)]) : 0.f;
-    const float s0 = dd * (float)sc[0], s1 = dd * (float)sc[1];
-    uint32_t wds[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    const int sh = qd >= 2 ? 4 : 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t q = ((wds[i] >> (8 * k + sh)) & 0xF) | (((hw[i] >> (8 * k + 2 * qd)) & 3) << 4);
-        v[4 * i + k] = (i < 4 ? s0 : s1) * u2f(q, 32.f);
-      }
-    }
-  } else if constexpr (WT == W_Q8_0) {
-    const int8_t* q = reinterpret_cast<const int8_t*>(st0 + r * 64 + 32 * h);
-    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + h]) : 0.f;
-    int4 a = *reinterpret_cast<const int4*>(q), b = *reinterpret_cast<const int4*>(q + 16);
-    uint32_t wds[8] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w,
-                       (uint32_t)b.x, (uint32_t)b.y, (uint32_t)b.z, (uint32_t)b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) v[4 * i + k] = dd * u2f(((wds[i] >> (8 * k)) & 0xFF) ^ 0x80u, 128.f);
-  } else {  // Q4_0 / IQ4_NL: block 2s+h, 16 bytes: low nibbles -> 0..15, high -> 16..31
-    uint4 qa = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16 * h);
-    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + h]) : 0.f;
-    uint32_t wds[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint32_t lo4 = wds[i] & 0x0F0F0F0Fu, hi4 = (wds[i] >> 4) & 0x0F0F0F0Fu;
-      if constexpr (WT == W_IQ4_NL) {  // codebook through byte permutes, then signed byte + 128
-        const int t0 = 0xBFAD9881, t1 = 0xF6EADDCF, t2 = 0x26190D01, t3 = 0x71594535;
-        lo4 = (uint32_t)lut16((int)lo4, t0, t1, t2, t3) ^ 0x80808080u;
-        hi4 = (uint32_t)lut16((int)hi4, t0, t1, t2, t3) ^ 0x80808080u;
-      }
-      const float zp = WT == W_IQ4_NL ? 128.f : 8.f;
+      uint32_t v = (h ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
+      if constexpr (WT == W_Q5_K) v |= ((hb[i] >> (2 * j + h)) & 0x01010101u) << 4;
+      c.u[i] = v;
+    }
+  } else if constexpr (WT == W_Q6_K) {
+    const int c4 = s & 3, n = c4 >> 1, hh = c4 & 1, qd = 2 * hh + (qq >> 1), l0 = 16 * (qq & 1);
+    uint4 ql = *reinterpret_cast<const uint4*>(st0 + r * 64 + ((qd & 1) ? 32 : 0) + l0);
+    uint4 qh = *reinterpret_cast<const uint4*>(st1 + r * 32 + l0);
+    const int8_t scl = reinterpret_cast<const int8_t*>(st2 + r * 16)[8 * n + 2 * qd + (l0 >> 4)];
+    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 256) + (s >> 2)]) : 0.f;
+    c.sc = dd * (float)scl;
+    c.bi = 0.f;
+    c.zp = 32.f;
+    uint32_t w[4] = {ql.x, ql.y, ql.z, ql.w}, hb[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[4 * i + k] = dd * u2f((lo4 >> (8 * k)) & 0xFF, zp);
-        v[16 + 4 * i + k] = dd * u2f((hi4 >> (8 * k)) & 0xFF, zp);
+    for (int i = 0; i < 4; ++i)
+      c.u[i] = ((qd >= 2 ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * qd)) & 0x03030303u) << 4);
+  } else if constexpr (WT == W_Q8_0) {
+    const int blk = qq >> 1;
+    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 64 + 32 * blk + 16 * (qq & 1));
+    c.sc = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + blk]) : 0.f;
+    c.bi = 0.f;
+    c.zp = 128.f;
+    c.u[0] = q.x ^ 0x80808080u; c.u[1] = q.y ^ 0x80808080u; c.u[2] = q.z ^ 0x80808080u; c.u[3] = q.w ^ 0x80808080u;
+  } else {  // Q4_0 / IQ4_NL: block 2s + qq/2; qq&1 selects low (elements 0-15) or high nibbles (16-31)
+    const int blk = qq >> 1, hi = qq & 1;
+    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16 * blk);
+    c.sc = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + blk]) : 0.f;
+    c.bi = 0.f;
+    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t v = (hi ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
+      if constexpr (WT == W_IQ4_NL) {
+        const int t0 = 0xBFAD9881, t1 = 0xF6EADDCF, t2 = 0x26190D01, t3 = 0x71594535;
+        v = (uint32_t)lut16((int)v, t0, t1, t2, t3) ^ 0x80808080u;
       }
+      c.u[i] = v;
+    }
+    c.zp = WT == W_IQ4_NL ? 128.f : 8.f;
+  }
+  return c;
+}
+
+// 16 codes -> two 16-byte chunks of fp16 (F16 = true) or bf16 operands.
+template <bool F16>
+BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
+  uint32_t r[8];
+  if constexpr (F16) {
+    const __half2 off = __float2half2_rn(1024.f + c.zp);
+    const __half2 sc = __float2half2_rn(c.sc);
+    const __half2 bi = __float2half2_rn(c.bi);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t p0 = __byte_perm(c.u[i], 0x64646464u, 0x4140);  // (1024 + u0, 1024 + u1)
+      uint32_t p1 = __byte_perm(c.u[i], 0x64646464u, 0x4342);  // (1024 + u2, 1024 + u3)
+      __half2 h0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p0), off), sc, bi);
+      __half2 h1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p1), off), sc, bi);
+      r[2 * i] = *reinterpret_cast<uint32_t*>(&h0);
+      r[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h1);
+    }
+  } else {
+    const float off = 8388608.0f + c.zp;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float f[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        f[k] = fmaf(__uint_as_float(__byte_perm(c.u[i], 0x4B000000u, 0x7650 + k)) - off, c.sc, c.bi);
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(f[0], f[1]), b1 = __floats2bfloat162_rn(f[2], f[3]);
+      r[2 * i] = *reinterpret_cast<uint32_t*>(&b0);
+      r[2 * i + 1] = *reinterpret_cast<uint32_t*>(&b1);
     }
   }
+  out[0] = make_uint4(r[0], r[1], r[2], r[3]);
+  out[1] = make_uint4(r[4], r[5], r[6], r[7]);
 }
 
 template <int WT, int BN, int S>
@@ -179,10 +205,11 @@ struct GemmSmem {
   static constexpr int TOTAL = OFF_TMEM + 16 + 1024;  // + alignment slack
 };
 
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;  // 4 per TMEM lane quadrant; each thread expands 16 weights per stage
+constexpr int kEpiWarps = 8;        // warps 0-7 drain the accumulator
 constexpr int kThreads = (kDequantWarps + 2) * 32;
 
-template <int WT, int BN, int S>
+template <int WT, int BN, int S, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tp0,
                     const __grid_constant__ CUtensorMap tp1, const __grid_constant__ CUtensorMap tp2, GemmDev g) {
@@ -249,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kDequantWarps + 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, BN);
+      constexpr uint32_t idesc = F16 ? idesc_f16(128, BN) : idesc_bf16(128, BN);
       for (int i = 0; i < nst; ++i) {
         const int s = i % S, ph = (i / S) & 1;
         if (!mbar_wait(&fullA[s], ph, err, 3)) break;
@@ -266,45 +293,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- dequant producers
-    const int quad = warp & 3, h = warp >> 2;
+    const int quad = warp & 3, qq = warp >> 2;
     const int r = quad * 32 + lane;
     const int grow = n0 + r;
     for (int i = 0; i < nst; ++i) {
       const int s = i % S, ph = (i / S) & 1, ks = kb + i;
       if (!mbar_wait(&fullQ[s], ph, err, 5)) break;
       const uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
-      float v[32];
-      dequant32<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, h, ks, grow, g, v);
+      const Codes cd = load_codes<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, qq, ks, grow, g);
       __syncwarp();
       if (lane == 0) mbar_arrive(&emptyQ[s]);
+      uint4 ops[2];
+      codes_to_operands<F16>(cd, ops);
       if (i >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) break;
       uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int chunk = 4 * h + c;
-        uint4 pk;
-        __nv_bfloat162 b0 = __floats2bfloat162_rn(v[8 * c + 0], v[8 * c + 1]);
-        __nv_bfloat162 b1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
-        __nv_bfloat162 b3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
-        pk.x = *reinterpret_cast<uint32_t*>(&b0);
-        pk.y = *reinterpret_cast<uint32_t*>(&b1);
-        pk.z = *reinterpret_cast<uint32_t*>(&b2);
-        pk.w = *reinterpret_cast<uint32_t*>(&b3);
-        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = pk;
-      }
+      *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
+      *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&fullA[s]);
     }
-    // ---------------------------------------------------------------- epilogue
+    // ---------------------------------------------------------------- epilogue (warps 0-7)
+    if (warp < kEpiWarps) {
     mbar_wait(accFull, 0, err, 7);
     tc_fence_after();
     // All 256 epilogue threads agree on `run`: after this barrier nothing can set the error word.
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const bool run = !*err;
     if (run) {
+      const int h = warp >> 2;
       const int n = n0 + r;
+      using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
+      AT* out_act = reinterpret_cast<AT*>(g.out_bf16);
       const bool atomic = g.k_splits > 1;
       float* xch = reinterpret_cast<float*>(smem + L::OFF_A);  // [4 quads][32 cols][32 lanes] for SwiGLU
       for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
@@ -324,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) {
               const int t = t0 + c0 + j;
               if (t < g.T && f < g.N / 2)
-                g.out_bf16[(size_t)t * g.ld_out + f] = __float2bfloat16(silu(v[j]) * up[j * 32 + lane]);
+                out_act[(size_t)t * g.ld_out + f] = from_f<AT>(silu(v[j]) * up[j * 32 + lane]);
             }
           }
           asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -339,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const size_t idx = (size_t)t * g.ld_out + n;
             const float val = v[j] + bias;
             if (g.mode == EPI_STORE_BF16) {
-              g.out_bf16[idx] = __float2bfloat16(val);
+              out_act[idx] = from_f<AT>(val);
             } else if (atomic) {
               atomicAdd(g.out_f32 + idx, val);
             } else if (g.mode == EPI_ADD_F32) {
@@ -351,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    }  // epilogue warps
   }
   tc_fence_before();
   __syncthreads();
@@ -417,20 +438,20 @@ int gemm_clear_error_word() {
   return p && cudaMemset(p, 0, sizeof(int)) == cudaSuccess ? 0 : -1;
 }
 
-template <int WT, int BN, int S>
+template <int WT, int BN, int S, bool F16>
 static int launch_gemm(const QW& w, const CUtensorMap& tx, const CUtensorMap& m0, const CUtensorMap& m1,
                        const CUtensorMap& m2, const GemmDev& g, int tiles_t, cudaStream_t st) {
   using L = GemmSmem<WT, BN, S>;
   static_assert(L::TOTAL <= 232448, "shared memory budget");
-  auto kern = qgemm_tc_kernel<WT, BN, S>;
+  auto kern = qgemm_tc_kernel<WT, BN, S, F16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   dim3 grid((w.N + 127) / 128, tiles_t, g.k_splits);
   kern<<<grid, kThreads, L::TOTAL, st>>>(tx, m0, m1, m2, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
 }
 
-template <int WT>
-static int dispatch_bn(const QW& w, const __nv_bfloat16* x, int T, const GemmDev& g0, cudaStream_t st) {
+template <int WT, bool F16>
+static int dispatch_bn(const QW& w, const void* x, int T, const GemmDev& g0, cudaStream_t st) {
   using P = Planes<WT>;
   GemmDev g = g0;
   const int K = w.K, N = w.N;
@@ -438,8 +459,8 @@ static int dispatch_bn(const QW& w, const __nv_bfloat16* x, int T, const GemmDev
   memset(&m1, 0, sizeof(m1));
   memset(&m2, 0, sizeof(m2));
   int bn = T <= 64 ? 64 : (T <= 128 ? 128 : 256);
-  int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, T, (uint64_t)K * 2, 64, bn,
-                       CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_map_2d(&mx, x, F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, T,
+                       (uint64_t)K * 2, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   uint64_t rb0 = WT == W_Q8_0 ? K : (WT == W_Q6_K ? K / 2 : K / 2);
   rc = make_map_2d(&m0, w.p0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb0, N, rb0, P::w0, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -465,12 +486,25 @@ static int dispatch_bn(const QW& w, const __nv_bfloat16* x, int T, const GemmDev
   if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
     if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)N * 4, T, st) != cudaSuccess) return -6;
   }
-  if (bn == 64) return launch_gemm<WT, 64, 5>(w, mx, m0, m1, m2, g, tiles_t, st);
-  if (bn == 128) return launch_gemm<WT, 128, 4>(w, mx, m0, m1, m2, g, tiles_t, st);
-  return launch_gemm<WT, 256, 3>(w, mx, m0, m1, m2, g, tiles_t, st);
+  if (bn == 64) return launch_gemm<WT, 64, 5, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, 4, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
+  return launch_gemm<WT, 256, 3, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
 }
 
-int qgemm_tc(const QW& w, const __nv_bfloat16* x, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
+template <bool F16>
+static int dispatch_type(const QW& w, const void* x, int T, const GemmDev& g, cudaStream_t st) {
+  switch (w.type) {
+    case W_Q4_K: return dispatch_bn<W_Q4_K, F16>(w, x, T, g, st);
+    case W_Q5_K: return dispatch_bn<W_Q5_K, F16>(w, x, T, g, st);
+    case W_Q6_K: return dispatch_bn<W_Q6_K, F16>(w, x, T, g, st);
+    case W_Q8_0: return dispatch_bn<W_Q8_0, F16>(w, x, T, g, st);
+    case W_Q4_0: return dispatch_bn<W_Q4_0, F16>(w, x, T, g, st);
+    case W_IQ4_NL: return dispatch_bn<W_IQ4_NL, F16>(w, x, T, g, st);
+  }
+  return -7;
+}
+
+int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
   if (T <= 0) return 0;
   if (w.K % 256 && !(w.K % 64 == 0 && (w.type == W_Q8_0 || w.type == W_Q4_0 || w.type == W_IQ4_NL))) return -2;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (w.K * 2) % 16) return -3;
@@ -489,15 +523,7 @@ int qgemm_tc(const QW& w, const __nv_bfloat16* x, int T, const GemvEpi& ep, int 
   g.ld_out = ep.ld_out;
   g.k_splits = k_splits;
   g.err = device_err_word();
-  switch (w.type) {
-    case W_Q4_K: return dispatch_bn<W_Q4_K>(w, x, T, g, st);
-    case W_Q5_K: return dispatch_bn<W_Q5_K>(w, x, T, g, st);
-    case W_Q6_K: return dispatch_bn<W_Q6_K>(w, x, T, g, st);
-    case W_Q8_0: return dispatch_bn<W_Q8_0>(w, x, T, g, st);
-    case W_Q4_0: return dispatch_bn<W_Q4_0>(w, x, T, g, st);
-    case W_IQ4_NL: return dispatch_bn<W_IQ4_NL>(w, x, T, g, st);
-  }
-  return -7;
+  return x_is_f16 ? dispatch_type<true>(w, x, T, g, st) : dispatch_type<false>(w, x, T, g, st);
 }
 
 }  // namespace barq

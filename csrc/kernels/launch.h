@@ -26,20 +26,21 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // K2 tcgen05 quantized GEMM: out[t, n] (+)= x[t, :] . W[n, :], x bf16 [T, K] (row pitch K).
 // Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
 // 0 = automatic (f32 modes only; accumulated with atomics).
-int qgemm_tc(const QW& w, const __nv_bfloat16* x, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
+// x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
+int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
 int gemm_error_word(int* host_out);
 int gemm_clear_error_word();
 
 // Fused (residual add +) RMSNorm.  x: f32 [T, H] residual stream (updated in place when `add`
 // is given: x += add).  Outputs any of bf16 [T, H] and int8 q8 [T, H] + scales [T, H/32].
-int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, __nv_bfloat16* out_bf16,
+int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H, void* out_act, int out_f16,
             ActOut out_q, cudaStream_t st);
 
 // Quantize bf16 or f32 rows to the q8 activation layout (H % 32 == 0).
 int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_q, cudaStream_t st);
 
 // h = silu(g) * u with g = in[t, i], u = in[t, F + i] (f32 or bf16 input) -> bf16 and/or q8.
-int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, __nv_bfloat16* out_bf16, ActOut out_q,
+int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, void* out_act, int out_f16, ActOut out_q,
            cudaStream_t st);
 
 struct RopeKVArgs {
@@ -76,7 +77,8 @@ struct DecodeAttnArgs {
   int splits;               // KV splits per (b, kv head)
   float* part_acc;          // scratch [B, Hkv, splits, G, D]
   float2* part_ml;          // scratch [B, Hkv, splits, G] (max, sum)
-  __nv_bfloat16* out;       // [B, H*D]
+  void* out;                // [B, H*D] activation dtype
+  int out_f16;
   ActOut out_q;             // optional q8 of out (q == null: none)
 };
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
@@ -94,7 +96,8 @@ struct PrefillAttnArgs {
   int S, max_q, H, Hkv, D, block_size;
   float scale;
   int window;
-  __nv_bfloat16* out;       // [T, H*D]
+  void* out;                // [T, H*D] activation dtype
+  int out_f16;
 };
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st);
 

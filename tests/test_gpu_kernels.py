@@ -280,11 +280,12 @@ GEMM_TYPES = [GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q5_K, GGMLType.Q8_0, GGMLTy
 
 @pytest.mark.parametrize("t", GEMM_TYPES)
 @pytest.mark.parametrize("T", [1, 37, 64, 200, 300])
-def test_gemm_tc(t, T):
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_tc(t, T, dt):
     N, K = 384, 1024
     qw, ref, _ = _qw(t, N, K, seed=5)
-    x = torch.randn(T, K, device=DEV).bfloat16()
-    y_ref = x.float().cpu() @ ref.bfloat16().float().T
+    x = torch.randn(T, K, device=DEV).to(dt)
+    y_ref = x.float().cpu() @ ref.to(dt).float().T
     tol = y_ref.abs().max().item() * 2e-3
     for ks in (1, 0):
         y = ops.gemm(qw, x, ops.EPI_STORE_F32, k_splits=ks).cpu()
@@ -294,23 +295,25 @@ def test_gemm_tc(t, T):
     out = base.clone()
     ops.gemm(qw, x, ops.EPI_ADD_F32, out=out)
     assert torch.allclose(out.cpu(), base.cpu() + y_ref, atol=tol, rtol=1e-2)
-    yb = ops.gemm(qw, x, ops.EPI_STORE_BF16).float().cpu()
-    assert torch.allclose(yb, y_ref, atol=tol + y_ref.abs().max().item() / 128, rtol=1e-2)
+    yb = ops.gemm(qw, x, ops.EPI_STORE_BF16)
+    assert yb.dtype == dt
+    assert torch.allclose(yb.float().cpu(), y_ref, atol=tol + y_ref.abs().max().item() / 128, rtol=1e-2)
 
 
 @pytest.mark.parametrize("T", [5, 130])
-def test_gemm_tc_swiglu_and_ragged_n(T):
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_tc_swiglu_and_ragged_n(T, dt):
     F, K = 192, 512
     g, gref, _ = _qw(GGMLType.Q4_K, F, K, seed=1)
     u, uref, _ = _qw(GGMLType.Q4_K, F, K, seed=2)
     w = ops.interleave_gate_up(g, u)
-    x = torch.randn(T, K, device=DEV).bfloat16()
+    x = torch.randn(T, K, device=DEV).to(dt)
     h = ops.gemm(w, x, ops.EPI_SWIGLU_Q8).float().cpu()
     xf = x.float().cpu()
-    h_ref = torch.nn.functional.silu(xf @ gref.bfloat16().float().T) * (xf @ uref.bfloat16().float().T)
+    h_ref = torch.nn.functional.silu(xf @ gref.to(dt).float().T) * (xf @ uref.to(dt).float().T)
     assert torch.allclose(h, h_ref, atol=h_ref.abs().max().item() / 60, rtol=2e-2)
     # N not a multiple of the 128-row tile
     qw, ref, _ = _qw(GGMLType.Q4_K, 200, K, seed=3)
     y = ops.gemm(qw, x).cpu()
-    y_ref = xf @ ref.bfloat16().float().T
+    y_ref = xf @ ref.to(dt).float().T
     assert torch.allclose(y, y_ref, atol=y_ref.abs().max().item() * 2e-3, rtol=1e-2)
