@@ -1,0 +1,137 @@
+"""Thread-safe streaming front for an engine: one background thread owns the engine and runs
+continuous-batching steps; callers submit requests and consume tokens as they are sampled.
+
+Parity: ``BatchEngine`` / ``BatchEngineHandle::submit`` (``advanced/src/batch_engine.rs:45-191``, an
+mpsc request queue drained by a tokio loop) — but the forward pass here is the real batched model,
+so every request in flight shares each decode step, and tokens are streamed per step (the
+reference's HTTP server generates the whole completion before it starts streaming,
+``cli/src/server.rs:738``).
+"""
+from __future__ import annotations
+
+import asyncio
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+
+from ..engine.sampling_params import SamplingParams
+
+
+@dataclass
+class StreamItem:
+    token: int | None  # None = finished
+    finish_reason: str | None = None
+    seq: object = None
+
+
+@dataclass
+class Submission:
+    prompt: list[int]
+    params: SamplingParams
+    request_id: str
+    sink: "queue.Queue[StreamItem] | None" = None
+    loop: asyncio.AbstractEventLoop | None = None
+    aqueue: asyncio.Queue | None = None
+    error: list = field(default_factory=list)
+    accepted: threading.Event = field(default_factory=threading.Event)
+
+
+class AsyncEngine:
+    def __init__(self, engine, metrics=None, idle_sleep: float = 0.002):
+        self.engine = engine
+        self.metrics = metrics
+        self.inbox: "queue.Queue[Submission]" = queue.Queue()
+        self.idle_sleep = idle_sleep
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, name="barq-engine", daemon=True)
+        self._thread.start()
+        self.healthy = True
+        self.last_error: str | None = None
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        self._thread.join(timeout=5)
+
+    # ------------------------------------------------------------------ engine thread
+    def _deliver(self, sub: Submission, item: StreamItem) -> None:
+        if sub.aqueue is not None and sub.loop is not None:
+            sub.loop.call_soon_threadsafe(sub.aqueue.put_nowait, item)
+        elif sub.sink is not None:
+            sub.sink.put(item)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                while True:
+                    sub = self.inbox.get_nowait()
+                    self._admit(sub)
+            except queue.Empty:
+                pass
+            if not self.engine.has_work():
+                time.sleep(self.idle_sleep)
+                continue
+            try:
+                self.engine.step()
+                self.healthy = True
+            except Exception as e:  # fail the in-flight requests, keep serving
+                self.healthy = False
+                self.last_error = f"{type(e).__name__}: {e}"
+                self._fail_all(self.last_error)
+
+    def _admit(self, sub: Submission) -> None:
+        def on_token(seq, tok, sub=sub):
+            if tok < 0:
+                self._deliver(sub, StreamItem(None, seq.finish_reason, seq))
+            else:
+                self._deliver(sub, StreamItem(tok, None, seq))
+
+        try:
+            seq = self.engine.add_request(sub.prompt, sub.params, sub.request_id, on_token=on_token)
+            sub.seq = seq
+        except Exception as e:
+            sub.error.append(str(e))
+            self._deliver(sub, StreamItem(None, "error"))
+        sub.accepted.set()
+
+    def _fail_all(self, msg: str) -> None:
+        eng = self.engine
+        seqs = list(getattr(getattr(eng, "sched", None), "running", [])) + list(getattr(getattr(eng, "sched", None), "waiting", []))
+        seqs += list(getattr(eng, "running", [])) + list(getattr(eng, "waiting", []))
+        for s in seqs:
+            s.finish_reason = "error"
+            if s.on_token is not None:
+                s.on_token(s, -1)
+        if hasattr(eng, "sched"):
+            for s in list(eng.sched.running):
+                eng.sched.finish(s, "error")
+            eng.sched.waiting.clear()
+        else:
+            eng.running.clear()
+            eng.waiting.clear()
+
+    # ------------------------------------------------------------------ caller side
+    async def stream(self, prompt: list[int], params: SamplingParams, request_id: str = ""):
+        """Async generator of StreamItem; the last item has token None."""
+        loop = asyncio.get_running_loop()
+        sub = Submission(prompt, params, request_id, loop=loop, aqueue=asyncio.Queue())
+        self.inbox.put(sub)
+        while True:
+            item = await sub.aqueue.get()
+            if item.token is None and item.finish_reason == "error" and sub.error:
+                raise ValueError(sub.error[0])
+            yield item
+            if item.token is None:
+                return
+
+    def generate_blocking(self, prompt: list[int], params: SamplingParams, request_id: str = "", timeout=None):
+        """Iterator of StreamItem for synchronous callers (UDS server, CLI)."""
+        sub = Submission(prompt, params, request_id, sink=queue.Queue())
+        self.inbox.put(sub)
+        while True:
+            item = sub.sink.get(timeout=timeout)
+            if item.token is None and item.finish_reason == "error" and sub.error:
+                raise ValueError(sub.error[0])
+            yield item
+            if item.token is None:
+                return

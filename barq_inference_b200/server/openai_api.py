@@ -1,0 +1,334 @@
+"""OpenAI-compatible HTTP API with true token-by-token SSE streaming.
+
+Parity: ``cli/src/server.rs`` — routes ``GET /``, ``GET /v1/models``, ``POST /v1/completions``,
+``POST /v1/chat/completions``, ``POST /v1/responses``, ``OPTIONS *`` (CORS), per-IP token-bucket rate
+limiting (429 ``rate_limit_error``), request defaults (max_tokens 128, temperature 0.8, top_k 40,
+top_p 0.95), ``/v1/responses`` accepting ``input`` / ``prompt`` / ``messages`` and
+``max_output_tokens``, ids ``cmpl-`` / ``chatcmpl-`` / ``resp-<unix ts>``, SSE chunk objects
+``text_completion.chunk``, ``chat.completion.chunk`` (role delta first) and ``response.chunk``,
+``data: [DONE]``.  Added: ``/health``, ``/metrics`` (Prometheus), ``response_format`` JSON mode,
+``stop``, ``seed``, and continuous batching across concurrent requests.
+"""
+from __future__ import annotations
+
+import json
+import threading
+import time
+from typing import Any
+
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
+
+from ..engine.sampling_params import SamplingParams
+from ..tokenizer import ChatTemplate, StreamDecoder
+from .async_engine import AsyncEngine
+from .metrics import InferenceMetrics, context_health
+
+DEFAULTS = dict(max_tokens=128, temperature=0.8, top_k=40, top_p=0.95)
+CORS = {"Access-Control-Allow-Origin": "*", "Access-Control-Allow-Methods": "GET, POST, OPTIONS",
+        "Access-Control-Allow-Headers": "*"}
+
+
+class RateLimiter:
+    """Token bucket per client key; capacity = requests per minute, refilled continuously."""
+
+    def __init__(self, rpm: int):
+        self.capacity = float(max(1, rpm))
+        self.refill = self.capacity / 60.0
+        self.state: dict[str, tuple[float, float]] = {}
+        self.lock = threading.Lock()
+
+    def allow(self, key: str, now: float | None = None) -> bool:
+        now = time.monotonic() if now is None else now
+        with self.lock:
+            tokens, last = self.state.get(key, (self.capacity, now))
+            tokens = min(self.capacity, tokens + (now - last) * self.refill)
+            ok = tokens >= 1.0
+            self.state[key] = (tokens - 1.0 if ok else tokens, now)
+            return ok
+
+
+def _err(status: int, msg: str, kind: str = "invalid_request_error") -> JSONResponse:
+    return JSONResponse({"error": {"message": msg, "type": kind}}, status_code=status, headers=CORS)
+
+
+def _params(body: dict, max_key: str = "max_tokens") -> SamplingParams:
+    mt = body.get(max_key)
+    if mt is None:
+        mt = body.get("max_output_tokens", body.get("max_tokens", DEFAULTS["max_tokens"]))
+    p = SamplingParams(
+        max_tokens=int(mt),
+        temperature=float(body.get("temperature", DEFAULTS["temperature"])),
+        top_k=int(body.get("top_k", DEFAULTS["top_k"])),
+        top_p=float(body.get("top_p", DEFAULTS["top_p"])),
+        min_p=float(body.get("min_p", 0.0)),
+        repetition_penalty=float(body.get("repetition_penalty", 1.0)),
+        frequency_penalty=float(body.get("frequency_penalty", 0.0)),
+        presence_penalty=float(body.get("presence_penalty", 0.0)),
+        seed=int(body.get("seed", 0) or 0),
+        logprobs=bool(body.get("logprobs", False)),
+    )
+    if p.max_tokens < 1:
+        raise ValueError("max_tokens must be >= 1")
+    rf = body.get("response_format") or {}
+    if isinstance(rf, dict):
+        if rf.get("type") == "json_object":
+            p.json_mode = True
+        elif rf.get("type") == "json_schema":
+            js = rf.get("json_schema") or {}
+            p.json_schema = js.get("schema", js) if isinstance(js, dict) else None
+            p.json_mode = True
+    if body.get("grammar"):
+        p.grammar = str(body["grammar"])
+    return p
+
+
+class OpenAIServer:
+    def __init__(self, engine, tokenizer, model_id: str = "barq", chat_template: ChatTemplate | None = None,
+                 rate_limit_rpm: int = 0, arch: str = "llama"):
+        self.metrics = InferenceMetrics()
+        self.aengine = AsyncEngine(engine, self.metrics)
+        self.engine = engine
+        self.tok = tokenizer
+        self.model_id = model_id
+        self.arch = arch
+        self.template = chat_template or ChatTemplate("generic")
+        self.limiter = RateLimiter(rate_limit_rpm) if rate_limit_rpm > 0 else None
+        self.app = self._build()
+
+    # ------------------------------------------------------------------ helpers
+    def _stops(self, body: dict) -> list[str]:
+        s = body.get("stop")
+        if s is None:
+            return []
+        return [s] if isinstance(s, str) else [str(x) for x in s]
+
+    async def _run(self, prompt_ids: list[int], params: SamplingParams, stops: list[str]):
+        """Yields (text_delta, finish_reason | None); finish at the end."""
+        dec = StreamDecoder(self.tok)
+        text = ""
+        async for item in self.aengine.stream(prompt_ids, params):
+            if item.token is None:
+                tail = dec.flush()
+                if tail:
+                    yield tail, None
+                yield "", item.finish_reason or "stop"
+                return
+            if item.token in self.engine.cfg.eos_ids and not params.ignore_eos:
+                continue
+            piece = dec.push(item.token)
+            if not piece:
+                continue
+            if stops:
+                text += piece
+                hit = min((text.find(s) for s in stops if s and text.find(s) >= 0), default=-1)
+                if hit >= 0:
+                    keep = text[:hit]
+                    already = len(text) - len(piece)
+                    if hit > already:
+                        yield keep[already:], None
+                    yield "", "stop"
+                    return
+            yield piece, None
+
+    def _limit(self, request: Request) -> JSONResponse | None:
+        if self.limiter is None:
+            return None
+        key = request.client.host if request.client else "unknown"
+        if not self.limiter.allow(key):
+            self.metrics.rate_limited += 1
+            return _err(429, "rate limit exceeded; retry later", "rate_limit_error")
+        return None
+
+    async def _body(self, request: Request) -> dict:
+        try:
+            body = await request.json()
+        except Exception:
+            raise ValueError("request body is not valid JSON")
+        if not isinstance(body, dict):
+            raise ValueError("request body must be a JSON object")
+        return body
+
+    def _sse(self, gen):
+        async def wrap():
+            async for obj in gen:
+                yield f"data: {json.dumps(obj)}\n\n"
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(wrap(), media_type="text/event-stream",
+                                 headers={**CORS, "Cache-Control": "no-cache"})
+
+    async def _complete(self, prompt_ids, params, stops, kind: str, model: str):
+        guard = self.metrics.begin()
+        created = int(time.time())
+        rid = {"text": "cmpl", "chat": "chatcmpl", "resp": "resp"}[kind] + f"-{created}{id(guard) % 100000}"
+        parts, reason, n = [], "stop", 0
+        try:
+            async for delta, fin in self._run(prompt_ids, params, stops):
+                if delta:
+                    guard.first_token()
+                    parts.append(delta)
+                    n += 1
+                if fin:
+                    reason = fin
+        except Exception:
+            guard.fail()
+            raise
+        guard.complete(len(prompt_ids), n)
+        text = "".join(parts)
+        usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": n, "total_tokens": len(prompt_ids) + n}
+        if kind == "text":
+            return {"id": rid, "object": "text_completion", "created": created, "model": model,
+                    "choices": [{"index": 0, "text": text, "finish_reason": reason}], "usage": usage}
+        if kind == "chat":
+            return {"id": rid, "object": "chat.completion", "created": created, "model": model,
+                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                 "finish_reason": reason}], "usage": usage}
+        return {"id": rid, "object": "response", "created": created, "model": model, "output": text, "usage": usage}
+
+    async def _stream(self, prompt_ids, params, stops, kind: str, model: str):
+        guard = self.metrics.begin()
+        created = int(time.time())
+        rid = {"text": "cmpl", "chat": "chatcmpl", "resp": "resp"}[kind] + f"-{created}{id(guard) % 100000}"
+        n = 0
+        try:
+            if kind == "chat":
+                yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model,
+                       "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]}
+            async for delta, fin in self._run(prompt_ids, params, stops):
+                if delta:
+                    guard.first_token()
+                    n += 1
+                if not delta and not fin:
+                    continue
+                if kind == "text":
+                    yield {"id": rid, "object": "text_completion.chunk", "created": created, "model": model,
+                           "choices": [{"index": 0, "text": delta, "finish_reason": fin}]}
+                elif kind == "chat":
+                    yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model,
+                           "choices": [{"index": 0, "delta": ({"content": delta} if delta else {}),
+                                        "finish_reason": fin}]}
+                else:
+                    yield {"id": rid, "object": "response.chunk", "created": created, "model": model, "output": delta}
+            guard.complete(len(prompt_ids), n)
+        finally:
+            if not guard.done:
+                guard.fail()
+
+    def _encode(self, text: str) -> list[int]:
+        ids = self.tok.encode(text, add_special=True)
+        if not ids:
+            raise ValueError("empty prompt")
+        return ids
+
+    def _chat_prompt(self, messages: Any) -> list[int]:
+        if not isinstance(messages, list) or not messages:
+            raise ValueError("messages must be a non-empty list")
+        for m in messages:
+            if not isinstance(m, dict) or "content" not in m:
+                raise ValueError("each message needs role and content")
+        text = self.template.render(messages, add_generation_prompt=True)
+        return self.tok.encode(text, add_special=not text.startswith(getattr(self.template, "bos_token", "") or "\0"))
+
+    # ------------------------------------------------------------------ app
+    def _build(self) -> FastAPI:
+        app = FastAPI(title="barq-inference", docs_url=None, redoc_url=None)
+        srv = self
+
+        @app.middleware("http")
+        async def cors(request: Request, call_next):
+            if request.method == "OPTIONS":
+                return Response(status_code=204, headers=CORS)
+            resp = await call_next(request)
+            for k, v in CORS.items():
+                resp.headers.setdefault(k, v)
+            return resp
+
+        @app.get("/")
+        async def root():
+            return {"object": "server.info", "model": srv.model_id, "architecture": srv.arch,
+                    "endpoints": ["/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions",
+                                  "/health", "/metrics"]}
+
+        @app.get("/v1/models")
+        async def models():
+            return {"object": "list", "data": [{"id": srv.model_id, "object": "model", "created": int(time.time()),
+                                                "owned_by": "barq"}]}
+
+        @app.get("/health")
+        async def health():
+            blocks = getattr(srv.engine, "blocks", None)
+            used = blocks.n_used / blocks.num_blocks if blocks is not None else 0.0
+            ok = srv.aengine.healthy
+            body = {"status": "ok" if ok else "degraded", "kv_usage": used,
+                    "context_health": context_health(used).value, "last_error": srv.aengine.last_error}
+            return JSONResponse(body, status_code=200 if ok else 503)
+
+        @app.get("/metrics")
+        async def metrics():
+            return PlainTextResponse(srv.metrics.prometheus(srv.engine), media_type="text/plain; version=0.0.4")
+
+        async def handle(request: Request, kind: str):
+            lim = srv._limit(request)
+            if lim is not None:
+                return lim
+            try:
+                body = await srv._body(request)
+                model = body.get("model") or srv.model_id
+                if kind == "text":
+                    prompt = body.get("prompt")
+                    if isinstance(prompt, list) and prompt and all(isinstance(t, int) for t in prompt):
+                        ids = list(prompt)
+                    elif isinstance(prompt, str):
+                        ids = srv._encode(prompt)
+                    else:
+                        raise ValueError("prompt must be a string or a list of token ids")
+                    params = _params(body)
+                elif kind == "chat":
+                    ids = srv._chat_prompt(body.get("messages"))
+                    params = _params(body)
+                else:
+                    if body.get("messages") is not None:
+                        ids = srv._chat_prompt(body["messages"])
+                    else:
+                        inp = body.get("input", body.get("prompt"))
+                        if isinstance(inp, list):
+                            ids = srv._chat_prompt(inp)
+                        elif isinstance(inp, str):
+                            ids = srv._encode(inp)
+                        else:
+                            raise ValueError("input (or prompt / messages) is required")
+                    params = _params(body, "max_output_tokens")
+                stops = srv._stops(body)
+                if body.get("stream"):
+                    return srv._sse(srv._stream(ids, params, stops, kind, model))
+                return JSONResponse(await srv._complete(ids, params, stops, kind, model))
+            except ValueError as e:
+                return _err(400, str(e))
+            except Exception as e:  # engine failure
+                return _err(500, f"{type(e).__name__}: {e}", "server_error")
+
+        @app.post("/v1/completions")
+        async def completions(request: Request):
+            return await handle(request, "text")
+
+        @app.post("/v1/chat/completions")
+        async def chat(request: Request):
+            return await handle(request, "chat")
+
+        @app.post("/v1/responses")
+        async def responses(request: Request):
+            return await handle(request, "resp")
+
+        @app.api_route("/{path:path}", methods=["GET", "POST", "PUT", "DELETE"])
+        async def not_found(path: str):
+            return _err(404, "route not found; try /v1/models, /v1/responses, /v1/completions or /v1/chat/completions",
+                        "not_found_error")
+
+        return app
+
+
+def serve(server: OpenAIServer, host: str = "0.0.0.0", port: int = 8000) -> None:
+    import uvicorn
+
+    uvicorn.run(server.app, host=host, port=port, log_level="info")

@@ -192,23 +192,41 @@ BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
 
 template <int WT, int BN, int S>
 struct GemmSmem {
-  static constexpr int A_BYTES = 128 * 128;       // 128 rows x 64 bf16
-  static constexpr int B_BYTES = BN * 128;        // BN rows x 64 bf16
+  static constexpr int A_BYTES = 128 * 128;       // 128 rows x 64 fp16/bf16
+  static constexpr int B_BYTES = BN * 128;        // BN rows x 64 fp16/bf16
   static constexpr int QW0 = Planes<WT>::w0 * 128, QW1 = Planes<WT>::w1 * 128, QW2 = Planes<WT>::w2 * 128;
   static constexpr int Q_BYTES = QW0 + QW1 + QW2;
+  static constexpr int XCH_BYTES = 4 * 32 * 32 * 4;  // SwiGLU gate/up exchange, one 32x32 f32 tile per quadrant
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + S * A_BYTES;
   static constexpr int OFF_Q = OFF_B + S * B_BYTES;
-  static constexpr int OFF_BAR = OFF_Q + S * Q_BYTES;
-  static constexpr int N_BAR = 5 * S + 1;
+  static constexpr int OFF_XCH = OFF_Q + S * Q_BYTES;
+  static constexpr int OFF_BAR = OFF_XCH + XCH_BYTES;
+  static constexpr int N_BAR = 5 * S + 4;
   static constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
   static constexpr int TOTAL = OFF_TMEM + 16 + 1024;  // + alignment slack
 };
 
+// Warp roles of the persistent kernel.
 constexpr int kDequantWarps = 16;  // 4 per TMEM lane quadrant; each thread expands 16 weights per stage
-constexpr int kEpiWarps = 8;        // warps 0-7 drain the accumulator
-constexpr int kThreads = (kDequantWarps + 2) * 32;
+constexpr int kEpiWarp0 = kDequantWarps;      // 4 epilogue warps, one per lane quadrant
+constexpr int kTmaWarp = kDequantWarps + 4;
+constexpr int kMmaWarp = kDequantWarps + 5;
+constexpr int kThreads = (kDequantWarps + 6) * 32;
 
+struct TileMap {
+  int n_tiles, t_tiles, ks, total;
+  BARQ_DEV void decode(int u, int& nt, int& tt, int& z) const {
+    nt = u % n_tiles;  // weight tiles fastest: concurrent CTAs share one activation tile in L2
+    const int rest = u / n_tiles;
+    z = rest % ks;
+    tt = rest / ks;
+  }
+};
+
+// Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...  The smem ring (S stages) and
+// the stage counter run continuously across tiles; the accumulator is double-buffered in TMEM
+// (2 x BN columns) so the epilogue of one tile overlaps the mainloop of the next.
 template <int WT, int BN, int S, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tp0,
@@ -223,16 +241,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* fullB = bars + 2 * S;
   uint64_t* fullA = bars + 3 * S;
   uint64_t* consumed = bars + 4 * S;
-  uint64_t* accFull = bars + 5 * S;
+  uint64_t* accFull = bars + 5 * S;      // [2]
+  uint64_t* accEmpty = bars + 5 * S + 2; // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
   __shared__ int err_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BN;
+  TileMap tm;
+  tm.n_tiles = (g.N + 127) / 128;
+  tm.t_tiles = (g.T + BN - 1) / BN;
+  tm.ks = g.k_splits;
+  tm.total = tm.n_tiles * tm.t_tiles * tm.ks;
   const int nst_total = g.K / 64;
-  const int z = blockIdx.z;
-  const int kb = (int)((long)nst_total * z / g.k_splits), ke = (int)((long)nst_total * (z + 1) / g.k_splits);
-  const int nst = ke - kb;
+  auto krange = [&](int z, int& kb, int& ke) {
+    kb = (int)((long)nst_total * z / g.k_splits);
+    ke = (int)((long)nst_total * (z + 1) / g.k_splits);
+  };
 
   if (threadIdx.x == 0) {
     err_s = 0;
@@ -243,102 +267,143 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&fullA[i], kDequantWarps);
       mbar_init(&consumed[i], 1);
     }
-    mbar_init(accFull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accFull[b], 1);
+      mbar_init(&accEmpty[b], 4);
+    }
     fence_mbar_init();
   }
-  if (warp == kDequantWarps + 1) tmem_alloc(tmem_slot, BN);
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   volatile int* err = &err_s;
 
-  if (warp == kDequantWarps) {
+  if (warp == kTmaWarp) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tx);
       prefetch_tmap(&tp0);
       if (P::w1) prefetch_tmap(&tp1);
       if (P::w2) prefetch_tmap(&tp2);
-      for (int i = 0; i < nst; ++i) {
-        const int s = i % S, ph = (i / S) & 1, ks = kb + i;
-        if (i >= S && !mbar_wait(&emptyQ[s], ph ^ 1, err, 1)) break;
-        uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
-        mbar_expect_tx(&fullQ[s], L::Q_BYTES);
-        tma_load_2d(q, &tp0, P::x0(ks), n0, &fullQ[s]);
-        if (P::w1) tma_load_2d(q + L::QW0, &tp1, P::x1(ks), n0, &fullQ[s]);
-        if (P::w2) tma_load_2d(q + L::QW0 + L::QW1, &tp2, P::x2(ks), n0, &fullQ[s]);
-        if (i >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) break;
-        mbar_expect_tx(&fullB[s], L::B_BYTES);
-        tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, t0, &fullB[s]);
+      int it = 0;
+      for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
+        int nt, tt, z, kb, ke;
+        tm.decode(u, nt, tt, z);
+        krange(z, kb, ke);
+        for (int ks = kb; ks < ke; ++ks, ++it) {
+          const int s = it % S, ph = (it / S) & 1;
+          if (it >= S && !mbar_wait(&emptyQ[s], ph ^ 1, err, 1)) break;
+          uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
+          mbar_expect_tx(&fullQ[s], L::Q_BYTES);
+          tma_load_2d(q, &tp0, P::x0(ks), nt * 128, &fullQ[s]);
+          if (P::w1) tma_load_2d(q + L::QW0, &tp1, P::x1(ks), nt * 128, &fullQ[s]);
+          if (P::w2) tma_load_2d(q + L::QW0 + L::QW1, &tp2, P::x2(ks), nt * 128, &fullQ[s]);
+          if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) break;
+          mbar_expect_tx(&fullB[s], L::B_BYTES);
+          tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, tt * BN, &fullB[s]);
+        }
       }
     }
-  } else if (warp == kDequantWarps + 1) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = F16 ? idesc_f16(128, BN) : idesc_bf16(128, BN);
-      for (int i = 0; i < nst; ++i) {
-        const int s = i % S, ph = (i / S) & 1;
-        if (!mbar_wait(&fullA[s], ph, err, 3)) break;
-        if (!mbar_wait(&fullB[s], ph, err, 4)) break;
+      int it = 0, tc = 0;
+      for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x, ++tc) {
+        int nt, tt, z, kb, ke;
+        tm.decode(u, nt, tt, z);
+        krange(z, kb, ke);
+        const int buf = tc & 1, use = tc >> 1;
+        if (tc >= 2 && !mbar_wait(&accEmpty[buf], (use - 1) & 1, err, 8)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
-        const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        bool ok = true;
+        for (int ks = kb; ks < ke; ++ks, ++it) {
+          const int s = it % S, ph = (it / S) & 1;
+          if (!mbar_wait(&fullA[s], ph, err, 3) || !mbar_wait(&fullB[s], ph, err, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
+          const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
-        mma_commit(&consumed[s]);
+          for (int k = 0; k < 4; ++k)
+            mma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (ks > kb) | (k > 0));
+          mma_commit(&consumed[s]);
+        }
+        if (!ok) break;
+        mma_commit(&accFull[buf]);
       }
-      mma_commit(accFull);
     }
-  } else {
+  } else if (warp < kDequantWarps) {
     // ---------------------------------------------------------------- dequant producers
     const int quad = warp & 3, qq = warp >> 2;
     const int r = quad * 32 + lane;
-    const int grow = n0 + r;
-    for (int i = 0; i < nst; ++i) {
-      const int s = i % S, ph = (i / S) & 1, ks = kb + i;
-      if (!mbar_wait(&fullQ[s], ph, err, 5)) break;
-      const uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
-      const Codes cd = load_codes<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, qq, ks, grow, g);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&emptyQ[s]);
-      uint4 ops[2];
-      codes_to_operands<F16>(cd, ops);
-      if (i >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) break;
-      uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
-      *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
-      *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&fullA[s]);
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < tm.total && ok && !*err; u += gridDim.x) {
+      int nt, tt, z, kb, ke;
+      tm.decode(u, nt, tt, z);
+      krange(z, kb, ke);
+      const int grow = nt * 128 + r;
+      for (int ks = kb; ks < ke; ++ks, ++it) {
+        const int s = it % S, ph = (it / S) & 1;
+        if (!mbar_wait(&fullQ[s], ph, err, 5)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
+        const Codes cd = load_codes<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, qq, ks, grow, g);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&emptyQ[s]);
+        uint4 ops[2];
+        codes_to_operands<F16>(cd, ops);
+        if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
+          ok = false;
+          break;
+        }
+        uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
+        *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
+        *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&fullA[s]);
+      }
     }
-    // ---------------------------------------------------------------- epilogue (warps 0-7)
-    if (warp < kEpiWarps) {
-    mbar_wait(accFull, 0, err, 7);
-    tc_fence_after();
-    // All 256 epilogue threads agree on `run`: after this barrier nothing can set the error word.
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    const bool run = !*err;
-    if (run) {
-      const int h = warp >> 2;
-      const int n = n0 + r;
-      using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-      AT* out_act = reinterpret_cast<AT*>(g.out_bf16);
-      const bool atomic = g.k_splits > 1;
-      float* xch = reinterpret_cast<float*>(smem + L::OFF_A);  // [4 quads][32 cols][32 lanes] for SwiGLU
-      for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
+  } else {
+    // ---------------------------------------------------------------- epilogue (4 warps)
+    const int quad = warp - kEpiWarp0;
+    const int r = quad * 32 + lane;
+    using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
+    AT* out_act = reinterpret_cast<AT*>(g.out_bf16);
+    float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);
+    const bool atomic = g.k_splits > 1;
+    int tc = 0;
+    for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
+      int nt, tt, z;
+      tm.decode(u, nt, tt, z);
+      const int buf = tc & 1, use = tc >> 1;
+      mbar_wait(&accFull[buf], use & 1, err, 7);
+      tc_fence_after();
+      // All 128 epilogue threads agree on `stop` (the error word only grows).
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (*err) break;
+      const int n0 = nt * 128, t0 = tt * BN, n = n0 + r;
+      const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(quad * 32) << 16);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(acc + (uint32_t)c0, v);
         if (g.mode == EPI_SWIGLU_Q8) {
-          // rows [32 gate | 32 up] x 2 groups: quads 0,2 gate; 1,3 up.  The two halves (h) take
-          // disjoint columns and disjoint exchange buffers.
-          float* buf = xch + (h * 4 + quad) * 32 * 32;
+          // rows [32 gate | 32 up] x 2 groups: quadrants 0,2 hold gate rows, 1,3 the matching up rows
+          float* mine = xch + quad * 32 * 32;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = v[j];
-          asm volatile("bar.sync 1, 256;" ::: "memory");
+          for (int j = 0; j < 32; ++j) mine[j * 32 + lane] = v[j];
+          asm volatile("bar.sync 2, 128;" ::: "memory");
           if ((quad & 1) == 0) {
-            const float* up = xch + (h * 4 + quad + 1) * 32 * 32;
+            const float* up = xch + (quad + 1) * 32 * 32;
             const int f = n0 / 2 + (quad >> 1) * 32 + lane;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -347,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 out_act[(size_t)t * g.ld_out + f] = from_f<AT>(silu(v[j]) * up[j * 32 + lane]);
             }
           }
-          asm volatile("bar.sync 1, 256;" ::: "memory");
+          asm volatile("bar.sync 2, 128;" ::: "memory");
           continue;
         }
         if (n < g.N) {
@@ -370,14 +435,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accEmpty[buf]);
     }
-    }  // epilogue warps
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kDequantWarps + 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
   if (threadIdx.x == 0 && err_s && g.err) atomicExch(g.err, err_s);
 }
@@ -445,7 +512,15 @@ static int launch_gemm(const QW& w, const CUtensorMap& tx, const CUtensorMap& m0
   static_assert(L::TOTAL <= 232448, "shared memory budget");
   auto kern = qgemm_tc_kernel<WT, BN, S, F16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-  dim3 grid((w.N + 127) / 128, tiles_t, g.k_splits);
+  const int total = ((w.N + 127) / 128) * tiles_t * g.k_splits;
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  dim3 grid(total < n_sm ? total : n_sm);
   kern<<<grid, kThreads, L::TOTAL, st>>>(tx, m0, m1, m2, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
 }
