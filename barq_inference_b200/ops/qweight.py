@@ -1,7 +1,9 @@
-"""Quantized weights in the kernels' planar layout (see ``csrc/kernels/qweight.cuh``).
+"""Quantized weights: GGUF blocks -> planar planes -> the kernels' tiled layout (``csrc/kernels/qtile.cuh``).
 
 ``QWeight.from_packed`` splits GGUF blocks into aligned planes on the device without changing a
-bit; ``to_gguf_rows`` re-emits the original blocks (tests check the round trip).  Types without a
+bit (the planar form is where rows are fused, interleaved or sharded); ``finalize`` then cuts the
+planes into 128-row x 256/64-column chunks with row-swizzled 16-byte pieces, the form every kernel
+reads.  ``to_gguf_rows`` re-emits the original blocks from either form (tests check the round trip).  Types without a
 native kernel (Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, IQ4_XS, F16, F32, ...) are dequantized once at load to
 bf16 and use the dense GEMV/GEMM; the reference instead dequantizes *everything* to f32 at load
 (``barq_core/src/gguf.rs:306-311``).
@@ -39,16 +41,35 @@ class QWeight:
     p2: torch.Tensor | None = None
     d: torch.Tensor | None = None
     src_type: GGMLType | None = None
+    tiled: torch.Tensor | None = None  # device layout (built on first use; planes then dropped)
 
     @property
     def device(self) -> torch.device:
-        return self.p0.device
+        return (self.tiled if self.tiled is not None else self.p0).device
 
     def nbytes(self) -> int:
+        if self.tiled is not None:
+            return self.tiled.numel()
         return sum(t.numel() * t.element_size() for t in (self.p0, self.p1, self.p2, self.d) if t is not None)
 
+    def finalize(self) -> "QWeight":
+        """Build the tiled device layout and release the planar planes."""
+        if self.wtype != W_BF16 and self.tiled is None:
+            self.tiled = tile_planes(self)
+            self.p0 = self.p1 = self.p2 = self.d = None
+        return self
+
+    def _planar(self) -> "QWeight":
+        if self.tiled is not None:  # rebuild planes (row operations after tiling)
+            pl = untile_planes(self)
+            return QWeight(self.wtype, self.N, self.K, pl["p0"], pl.get("p1"), pl.get("p2"), pl.get("d"), self.src_type)
+        return self
+
     def args(self):
-        return (self.wtype, self.N, self.K, self.p0, self.p1, self.p2, self.d)
+        if self.wtype == W_BF16:
+            return (self.wtype, self.N, self.K, self.p0, None, None, None)
+        self.finalize()
+        return (self.wtype, self.N, self.K, self.tiled, None, None, None)
 
     @staticmethod
     def from_packed(raw: torch.Tensor, t: GGMLType, N: int, K: int, device=None) -> "QWeight":
@@ -56,7 +77,7 @@ class QWeight:
         t = GGMLType(t)
         dev = torch.device(device) if device is not None else raw.device
         raw = raw.to(dev)
-        if t not in NATIVE or K % TYPE_TRAITS[t].block_size:
+        if t not in NATIVE or K % TILE_FMT[int(t)][0]:
             if t == GGMLType.BF16:
                 w = raw.contiguous().view(torch.bfloat16).reshape(N, K)
             elif t == GGMLType.F16:
@@ -83,7 +104,8 @@ class QWeight:
         raise AssertionError(t)
 
     def to_gguf_rows(self) -> torch.Tensor:
-        """Inverse of ``from_packed`` for native types: uint8 ``[N, row_bytes]``."""
+        """Inverse of ``from_packed`` (and of the tiling) for native types: uint8 ``[N, row_bytes]``."""
+        self = self._planar()
         t = GGMLType(self.wtype)
         N = self.N
         nbk = lambda x, per: x.reshape(N, -1, per)  # noqa: E731
@@ -104,12 +126,14 @@ class QWeight:
 
     def select_rows(self, idx: torch.Tensor) -> "QWeight":
         """Row gather (used to fuse/interleave projections and to shard for tensor parallelism)."""
+        self = self._planar()
         idx = idx.to(self.p0.device)
         g = lambda x: None if x is None else x.index_select(0, idx).contiguous()  # noqa: E731
         return QWeight(self.wtype, int(idx.numel()), self.K, g(self.p0), g(self.p1), g(self.p2), g(self.d), self.src_type)
 
     def col_shard(self, k0: int, k1: int) -> "QWeight":
         """Columns [k0, k1) (block-aligned) — row-parallel sharding for tensor parallelism."""
+        self = self._planar()
         K = self.K
         bs = 256 if self.wtype in (12, 13, 14) else (32 if self.wtype else 1)
         if k0 % bs or k1 % bs:
@@ -123,7 +147,71 @@ class QWeight:
         return QWeight(self.wtype, self.N, k1 - k0, cs(self.p0), cs(self.p1), cs(self.p2), cs(self.d), self.src_type)
 
 
+# ---------------------------------------------------------------- tiled device layout (qtile.cuh)
+# per type: group size G and planes in chunk order as (planar attribute, bytes per group per row)
+TILE_FMT = {
+    int(GGMLType.Q4_K): (256, [("p0", 128), ("p2", 16)]),
+    int(GGMLType.Q5_K): (256, [("p0", 128), ("p1", 32), ("p2", 16)]),
+    int(GGMLType.Q6_K): (256, [("p0", 128), ("p1", 64), ("p2", 16), ("d", 2)]),
+    int(GGMLType.Q8_0): (64, [("p0", 64), ("d", 4)]),
+    int(GGMLType.Q4_0): (64, [("p0", 32), ("d", 4)]),
+    int(GGMLType.IQ4_NL): (64, [("p0", 32), ("d", 4)]),
+}
+
+
+def _swz_index(rb: int, device) -> torch.Tensor | None:
+    """[128, rb/16] physical->logical chunk map (XOR swizzle is its own inverse)."""
+    if rb not in (32, 64, 128):
+        return None
+    r = torch.arange(128, device=device)[:, None]
+    c = torch.arange(rb // 16, device=device)[None, :]
+    f = {128: r & 7, 64: (r >> 1) & 3, 32: (r >> 2) & 1}[rb]
+    return c ^ f
+
+
+def tile_planes(w: "QWeight") -> torch.Tensor:
+    """Planar planes -> one uint8 buffer of chunks [NT, KG, CHUNK] (rows padded to 128)."""
+    G, planes = TILE_FMT[w.wtype]
+    N, K = w.N, w.K
+    NT, KG = (N + 127) // 128, K // G
+    parts = []
+    for attr, rb in planes:
+        x = getattr(w, attr)
+        x = x.contiguous().view(torch.uint8).reshape(N, KG, rb)
+        if NT * 128 != N:
+            x = torch.cat([x, torch.zeros(NT * 128 - N, KG, rb, dtype=torch.uint8, device=x.device)], 0)
+        x = x.reshape(NT, 128, KG, rb)
+        idx = _swz_index(rb, x.device)
+        if idx is not None:
+            x = x.reshape(NT, 128, KG, rb // 16, 16)
+            g = idx[None, :, None, :, None].expand(NT, 128, KG, rb // 16, 16)
+            x = torch.gather(x, 3, g).reshape(NT, 128, KG, rb)
+        parts.append(x.permute(0, 2, 1, 3).reshape(NT, KG, 128 * rb))
+    return torch.cat(parts, -1).contiguous().reshape(-1)
+
+
+def untile_planes(w: "QWeight") -> dict:
+    """Inverse of ``tile_planes``: tiled buffer -> planar planes (same attributes as before)."""
+    G, planes = TILE_FMT[w.wtype]
+    N, K = w.N, w.K
+    NT, KG = (N + 127) // 128, K // G
+    buf = w.tiled.reshape(NT, KG, -1)
+    out, off = {}, 0
+    for attr, rb in planes:
+        x = buf[:, :, off:off + 128 * rb].reshape(NT, KG, 128, rb).permute(0, 2, 1, 3)
+        off += 128 * rb
+        idx = _swz_index(rb, x.device)
+        if idx is not None:
+            x = x.reshape(NT, 128, KG, rb // 16, 16)
+            g = idx[None, :, None, :, None].expand(NT, 128, KG, rb // 16, 16)
+            x = torch.gather(x, 3, g)
+        x = x.reshape(NT * 128, KG * rb)[:N].contiguous()
+        out[attr] = x.view(torch.int16) if attr == "d" else x
+    return out
+
+
 def cat_rows(ws: list[QWeight]) -> QWeight:
+    ws = [w._planar() for w in ws]
     t = ws[0].wtype
     if any(w.wtype != t or w.K != ws[0].K for w in ws):
         raise ValueError("cat_rows: types or K differ")

@@ -1,0 +1,154 @@
+"""Unix-domain-socket streaming server and client.
+
+Parity: ``InferenceServer`` / ``InferenceClient`` (``advanced/src/uds_server.rs:18-395``).  Wire format
+(kept identical): each frame is a 4-byte big-endian length followed by a UTF-8 JSON object.  A
+request ``{"id", "prompt", "max_tokens", "temperature"}`` is answered by a stream of
+``{"id", "text", "tokens_generated", "ttft_ms", "total_time_ms", "done"}`` frames, one per generated
+token, the last with ``done: true``.  Requests from all connections share the continuous-batching
+engine (what the reference's unreachable ``cmd_server_batch`` intended, ``cli/src/main.rs:1045-1158``).
+Sampling uses top-k 40 / top-p 0.95 like the reference's handler.  Errors are reported as a final
+frame with ``done: true`` and an ``error`` field.
+"""
+from __future__ import annotations
+
+import json
+import os
+import socket
+import socketserver
+import struct
+import threading
+import time
+
+from ..engine.sampling_params import SamplingParams
+from ..tokenizer import StreamDecoder
+
+MAX_FRAME = 16 << 20
+
+
+def send_frame(sock: socket.socket, obj: dict) -> None:
+    data = json.dumps(obj).encode("utf-8")
+    sock.sendall(struct.pack(">I", len(data)) + data)
+
+
+def _recv_exact(sock: socket.socket, n: int) -> bytes | None:
+    buf = bytearray()
+    while len(buf) < n:
+        chunk = sock.recv(n - len(buf))
+        if not chunk:
+            return None
+        buf += chunk
+    return bytes(buf)
+
+
+def recv_frame(sock: socket.socket) -> dict | None:
+    head = _recv_exact(sock, 4)
+    if head is None:
+        return None
+    (n,) = struct.unpack(">I", head)
+    if n > MAX_FRAME:
+        raise ValueError(f"frame of {n} bytes exceeds {MAX_FRAME}")
+    body = _recv_exact(sock, n)
+    if body is None:
+        return None
+    return json.loads(body.decode("utf-8"))
+
+
+class UDSServer:
+    def __init__(self, aengine, tokenizer, socket_path: str = "/tmp/barq-inference.sock", queue_size: int = 100):
+        self.ae = aengine
+        self.tok = tokenizer
+        self.path = socket_path
+        self.sem = threading.BoundedSemaphore(queue_size)
+        self._server = None
+
+    def handle_request(self, conn: socket.socket, req: dict) -> None:
+        t0 = time.perf_counter()
+        rid = str(req.get("id", ""))
+        try:
+            prompt = req["prompt"]
+            ids = prompt if isinstance(prompt, list) else self.tok.encode(str(prompt))
+            params = SamplingParams(max_tokens=int(req.get("max_tokens", 128)),
+                                    temperature=float(req.get("temperature", 0.8)), top_k=40, top_p=0.95)
+        except (KeyError, TypeError, ValueError) as e:
+            send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
+                              "done": True, "error": f"bad request: {e}"})
+            return
+        dec = StreamDecoder(self.tok)
+        n, ttft = 0, None
+        try:
+            for item in self.ae.generate_blocking(ids, params, rid):
+                now = time.perf_counter()
+                if item.token is None:
+                    send_frame(conn, {"id": rid, "text": dec.flush(), "tokens_generated": n,
+                                      "ttft_ms": int(ttft or 0), "total_time_ms": int((now - t0) * 1e3), "done": True})
+                    return
+                n += 1
+                if ttft is None:
+                    ttft = (now - t0) * 1e3
+                send_frame(conn, {"id": rid, "text": dec.push(item.token), "tokens_generated": n,
+                                  "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
+        except ValueError as e:
+            send_frame(conn, {"id": rid, "text": "", "tokens_generated": n, "ttft_ms": 0,
+                              "total_time_ms": int((time.perf_counter() - t0) * 1e3), "done": True, "error": str(e)})
+
+    def start(self, background: bool = True):
+        if os.path.exists(self.path):
+            os.unlink(self.path)
+        srv = self
+
+        class Handler(socketserver.BaseRequestHandler):
+            def handle(self):
+                conn = self.request
+                while True:
+                    try:
+                        req = recv_frame(conn)
+                    except (ValueError, json.JSONDecodeError) as e:
+                        send_frame(conn, {"id": "", "text": "", "tokens_generated": 0, "ttft_ms": 0,
+                                          "total_time_ms": 0, "done": True, "error": str(e)})
+                        return
+                    if req is None:
+                        return
+                    if not srv.sem.acquire(blocking=False):
+                        send_frame(conn, {"id": str(req.get("id", "")), "text": "", "tokens_generated": 0,
+                                          "ttft_ms": 0, "total_time_ms": 0, "done": True, "error": "queue full"})
+                        continue
+                    try:
+                        srv.handle_request(conn, req)
+                    finally:
+                        srv.sem.release()
+
+        class Server(socketserver.ThreadingMixIn, socketserver.UnixStreamServer):
+            daemon_threads = True
+
+        self._server = Server(self.path, Handler)
+        if background:
+            threading.Thread(target=self._server.serve_forever, daemon=True).start()
+        else:
+            self._server.serve_forever()
+        return self
+
+    def stop(self):
+        if self._server is not None:
+            self._server.shutdown()
+            self._server.server_close()
+        if os.path.exists(self.path):
+            os.unlink(self.path)
+
+
+class UDSClient:
+    def __init__(self, socket_path: str = "/tmp/barq-inference.sock"):
+        self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.sock.connect(socket_path)
+
+    def stream(self, prompt, max_tokens: int = 128, temperature: float = 0.8, rid: str = "req"):
+        send_frame(self.sock, {"id": rid, "prompt": prompt, "max_tokens": max_tokens, "temperature": temperature})
+        while True:
+            fr = recv_frame(self.sock)
+            if fr is None:
+                return
+            yield fr
+            if fr.get("done"):
+                return
+
+    def close(self):
+        self.sock.close()

@@ -1,13 +1,25 @@
 // K13 embedding gather straight from quantized rows, and row dequantization to bf16.
-// Element-wise ggml-spec decoding of the planar layouts described in qweight.cuh.
+// Element-wise ggml-spec decoding of the tiled device layout described in qtile.cuh.
 #include "common.cuh"
 #include "launch.h"
 #include "qweight.cuh"
+#include "qtile.cuh"
 
 namespace barq {
 
 __device__ __constant__ int8_t kIQ4NL[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
                                              1,    13,   25,  38,  53,  69,  89,  113};
+
+// Byte `i` of plane P of (row, group kg), honouring the chunk swizzle.
+template <int WT, int P>
+BARQ_DEV uint8_t pbyte(const QW& w, int row, int kg, int i) {
+  return plane_chunk<WT, P>(w, row, kg, i >> 4)[i & 15];
+}
+template <int WT>
+BARQ_DEV float dplane(const QW& w, int row, int kg, int idx) {
+  const uint8_t* p = chunk_ptr<WT>(w, row >> 7, kg) + TileFmt<WT>::D_OFF;
+  return h2f(reinterpret_cast<const uint16_t*>(p)[(row & 127) * (TileFmt<WT>::G == 256 ? 1 : 2) + idx]);
+}
 
 BARQ_DEV float deq_elem(const QW& w, int row, int k) {
   const int K = w.K;
@@ -16,20 +28,23 @@ BARQ_DEV float deq_elem(const QW& w, int row, int k) {
       return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w.p0)[(size_t)row * K + k]);
     case W_Q4_0:
     case W_IQ4_NL: {
-      int blk = k >> 5, e = k & 31;
-      uint8_t byte = w.p0[(size_t)row * (K / 2) + blk * 16 + (e & 15)];
-      int q = e < 16 ? (byte & 15) : (byte >> 4);
-      float d = h2f(w.d[(size_t)row * (K / 32) + blk]);
+      const int kg = k >> 6, e = k & 63, bi = e >> 5, l = e & 31;
+      const uint8_t byte = w.type == W_Q4_0 ? pbyte<W_Q4_0, 0>(w, row, kg, 16 * bi + (l & 15))
+                                            : pbyte<W_IQ4_NL, 0>(w, row, kg, 16 * bi + (l & 15));
+      const int q = l < 16 ? (byte & 15) : (byte >> 4);
+      const float d = dplane<W_Q4_0>(w, row, kg, bi);
       return d * (float)(w.type == W_Q4_0 ? q - 8 : kIQ4NL[q]);
     }
     case W_Q8_0: {
-      int8_t q = reinterpret_cast<const int8_t*>(w.p0)[(size_t)row * K + k];
-      return h2f(w.d[(size_t)row * (K / 32) + (k >> 5)]) * (float)q;
+      const int kg = k >> 6, e = k & 63;
+      const int8_t q = (int8_t)pbyte<W_Q8_0, 0>(w, row, kg, e);
+      return dplane<W_Q8_0>(w, row, kg, e >> 5) * (float)q;
     }
     case W_Q4_K:
     case W_Q5_K: {
-      int b = k >> 8, e = k & 255, j = e >> 6, hiw = (e >> 5) & 1, l = e & 31;
-      const uint8_t* hdr = w.p2 + ((size_t)row * (K / 256) + b) * 16;
+      const int kg = k >> 8, e = k & 255, j = e >> 6, hiw = (e >> 5) & 1, l = e & 31;
+      const bool five = w.type == W_Q5_K;
+      const uint8_t* hdr = five ? plane_chunk<W_Q5_K, 2>(w, row, kg, 0) : plane_chunk<W_Q4_K, 1>(w, row, kg, 0);
       float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
       const uint8_t* s = hdr + 4;
       int is = 2 * j + hiw, sc, m;
@@ -40,25 +55,19 @@ BARQ_DEV float deq_elem(const QW& w, int row, int k) {
         sc = (s[is + 4] & 0xF) | ((s[is - 4] >> 6) << 4);
         m = (s[is + 4] >> 4) | ((s[is] >> 6) << 4);
       }
-      uint8_t byte = w.p0[(size_t)row * (K / 2) + b * 128 + 32 * j + l];
+      const uint8_t byte = five ? pbyte<W_Q5_K, 0>(w, row, kg, 32 * j + l) : pbyte<W_Q4_K, 0>(w, row, kg, 32 * j + l);
       int q = hiw ? (byte >> 4) : (byte & 15);
-      if (w.type == W_Q5_K) {
-        uint8_t h = w.p1[(size_t)row * (K / 8) + b * 32 + l];
-        q += ((h >> is) & 1) << 4;
-      }
+      if (five) q += ((pbyte<W_Q5_K, 1>(w, row, kg, l) >> is) & 1) << 4;
       return d * sc * q - dmin * m;
     }
     case W_Q6_K: {
-      int b = k >> 8, e = k & 255, n = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
-      const uint8_t* ql = w.p0 + (size_t)row * (K / 2) + b * 128 + 64 * n;
-      const uint8_t* qh = w.p1 + (size_t)row * (K / 4) + b * 64 + 32 * n;
-      const int8_t* sc = reinterpret_cast<const int8_t*>(w.p2) + (size_t)row * (K / 16) + b * 16 + 8 * n;
-      float d = h2f(w.d[(size_t)row * (K / 256) + b]);
-      int lo = (quarter & 1) ? ql[l + 32] : ql[l];
-      int nib = (quarter >= 2) ? (lo >> 4) : (lo & 15);
-      int hb = (qh[l] >> (2 * quarter)) & 3;
-      int q = (nib | (hb << 4)) - 32;
-      return d * sc[(l >> 4) + 2 * quarter] * q;
+      const int kg = k >> 8, e = k & 255, n = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
+      const int lo = pbyte<W_Q6_K, 0>(w, row, kg, 64 * n + ((quarter & 1) ? 32 : 0) + l);
+      const int nib = (quarter >= 2) ? (lo >> 4) : (lo & 15);
+      const int hb = (pbyte<W_Q6_K, 1>(w, row, kg, 32 * n + l) >> (2 * quarter)) & 3;
+      const int q = (nib | (hb << 4)) - 32;
+      const int8_t sc = (int8_t)pbyte<W_Q6_K, 2>(w, row, kg, 8 * n + 2 * quarter + (l >> 4));
+      return dplane<W_Q6_K>(w, row, kg, 0) * sc * q;
     }
   }
   return 0.f;

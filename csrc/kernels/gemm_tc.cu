@@ -4,20 +4,26 @@
 // The reference's quantized matmul is a host round trip (backend/src/cuda_quant.rs:104-126); its
 // dense path is a rayon triple loop (barq_core/src/blas.rs:193-207).
 //
-// Swap-AB tiling: the MMA "A" operand is a 128-row tile of *weights* (dequantized to bf16 on the
-// fly), the "B" operand a BN-row tile of *tokens* (bf16 activations), so D = W_tile * X_tile^T sits
-// in TMEM as 128 lanes (output features) x BN columns (tokens).  This keeps M = 128 for any token
-// count and lets small decode batches (BN = 64) use the same kernel.
+// Swap-AB tiling: the MMA "A" operand is a 128-row tile of *weights* (dequantized on the fly), the
+// "B" operand a BN-row tile of *tokens* (fp16/bf16 activations), so D = W_tile * X_tile^T sits in
+// TMEM as 128 lanes (output features) x BN columns (tokens).  M = 128 for any token count, so small
+// decode batches (BN = 64) and prefill (BN = 256) share the kernel.
 //
-// Warp roles (320 threads):
-//   warps 0-7  dequant: wait for the quantized planes of stage s in shared memory (TMA), expand
-//              them to bf16 directly in the UMMA 128B-swizzle K-major layout, fence the async proxy,
-//              signal "A full"; after the mainloop they run the epilogue (tcgen05.ld -> global).
-//   warp 8     TMA producer: quantized weight planes and the activation tile of every stage.
-//   warp 9     MMA issuer: one elected thread issues 4 x tcgen05.mma (K = 16) per 64-wide stage and
-//              commits each stage's completion to the stage's "consumed" mbarrier.
+// Data movement: weights are stored tiled (qtile.cuh), so the quantized planes of one 128-row x
+// G-column group are one contiguous chunk fetched with a single cp.async.bulk; activations arrive
+// as 128-byte-swizzled TMA tiles.  Persistent: one CTA per SM walks the tile list; the smem rings
+// and their stage counters run continuously across tiles, and the accumulator is double-buffered in
+// TMEM (2 x BN columns) so the epilogue of one tile overlaps the mainloop of the next.
+//
+// Warp roles (704 threads):
+//   warps 0-15  dequant: expand 16 weights each per 64-column stage straight into the UMMA
+//               128B-swizzle K-major layout, fence the async proxy, signal "A full";
+//   warps 16-19 epilogue: tcgen05.ld the finished accumulator -> global (store / residual add /
+//               split-K atomics / SwiGLU);
+//   warp 20     producer: bulk copy of weight chunks, TMA of activation tiles;
+//   warp 21     MMA: one thread issues 4 x tcgen05.mma (K = 16) per stage and commits completion.
 // Every wait is bounded (tc_common.cuh); on expiry the CTA records an error word and unwinds.
-// No TMA load here uses .multicast::cluster.
+// No load here uses .multicast::cluster.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -26,6 +32,7 @@
 
 #include "gemv_traits.cuh"
 #include "launch.h"
+#include "qtile.cuh"
 #include "tc_common.cuh"
 
 namespace barq {
@@ -34,82 +41,55 @@ using namespace tc;
 
 struct GemmDev {
   int N, K, T;
-  const uint16_t* d;  // per-block f16 scale plane (Q4_0 / IQ4_NL / Q8_0 / Q6_K)
+  const uint8_t* w;  // tiled weight chunks
   int mode;
   float* out_f32;
-  __nv_bfloat16* out_bf16;
+  void* out_act;
   const float* bias;
   int ld_out;
   int k_splits;
   int* err;
 };
 
-// Staging box widths (bytes per weight row per 64-wide K stage) and x-coordinate rule per plane.
-template <int WT> struct Planes;
-template <> struct Planes<W_Q4_K> {
-  static constexpr int w0 = 32, w1 = 0, w2 = 16;
-  static BARQ_DEV int x0(int s) { return 32 * s; }
-  static BARQ_DEV int x1(int) { return 0; }
-  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
-};
-template <> struct Planes<W_Q5_K> {
-  static constexpr int w0 = 32, w1 = 32, w2 = 16;
-  static BARQ_DEV int x0(int s) { return 32 * s; }
-  static BARQ_DEV int x1(int s) { return 32 * (s >> 2); }
-  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
-};
-template <> struct Planes<W_Q6_K> {
-  static constexpr int w0 = 64, w1 = 32, w2 = 16;
-  static BARQ_DEV int x0(int s) { return 64 * (s >> 1); }
-  static BARQ_DEV int x1(int s) { return 32 * (s >> 1); }
-  static BARQ_DEV int x2(int s) { return 16 * (s >> 2); }
-};
-template <> struct Planes<W_Q8_0> {
-  static constexpr int w0 = 64, w1 = 0, w2 = 0;
-  static BARQ_DEV int x0(int s) { return 64 * s; }
-  static BARQ_DEV int x1(int) { return 0; }
-  static BARQ_DEV int x2(int) { return 0; }
-};
-template <> struct Planes<W_Q4_0> {
-  static constexpr int w0 = 32, w1 = 0, w2 = 0;
-  static BARQ_DEV int x0(int s) { return 32 * s; }
-  static BARQ_DEV int x1(int) { return 0; }
-  static BARQ_DEV int x2(int) { return 0; }
-};
-template <> struct Planes<W_IQ4_NL> : Planes<W_Q4_0> {};
+// 1-D bulk copy global -> shared, completion on `bar` (transaction bytes).
+BARQ_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
 
-// ---- dequantization of one thread's 16 weights (row r, quarter qq of the 64-wide stage s)
-//
-// Every format is first reduced to four words of unsigned byte codes u (one code per weight, in
-// natural element order) plus (zero point zp, scale sc, bias bi) so that  w = (u - zp) * sc + bi.
-// fp16 operands: a byte permute places two codes in the mantissas of 1024.0h (exact), one packed
-// subtract removes 1024 + zp, one packed FMA applies scale and bias: ~2 instructions per weight.
-// bf16 operands: the same codes go through fp32 (mantissa of 2^23, subtract, FMA) and a packed
-// round to bf16x2.
+// ---- dequantization of one thread's 16 weights (row r, quarter qq of 64-column stage `sub` of
+// the staged chunk).  Every format is reduced to four words of unsigned byte codes u (one per
+// weight, natural order) plus (zero point zp, scale sc, bias bi) with  w = (u - zp) * sc + bi.
 struct Codes {
   uint32_t u[4];
   float zp, sc, bi;
 };
 
+BARQ_DEV void words(uint4 v, uint32_t* w) {
+  w[0] = v.x;
+  w[1] = v.y;
+  w[2] = v.z;
+  w[3] = v.w;
+}
+
 template <int WT>
-BARQ_DEV Codes load_codes(const uint8_t* st0, const uint8_t* st1, const uint8_t* st2, int r, int qq, int s,
-                          int grow, const GemmDev& g) {
+BARQ_DEV Codes load_codes(const uint8_t* ch, int r, int qq, int sub) {
+  using F = TileFmt<WT>;
   Codes c;
   if constexpr (WT == W_Q4_K || WT == W_Q5_K) {
-    const int j = s & 3, h = qq >> 1, l0 = 16 * (qq & 1);
-    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 32 + l0);
-    uint4 hd = *reinterpret_cast<const uint4*>(st2 + r * 16);
+    const int j = sub, h = qq >> 1;
+    uint32_t w[4];
+    words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, 2 * j + (qq & 1))), w);
+    constexpr int HP = WT == W_Q5_K ? 2 : 1;
+    const uint4 hd = *reinterpret_cast<const uint4*>(staged_chunk<WT, HP>(ch, r, 0));
     int scl, mn;
     kscale(hd.y, hd.z, hd.w, 2 * j + h, scl, mn);
     c.sc = h2f(hd.x & 0xFFFF) * (float)scl;
     c.bi = -h2f(hd.x >> 16) * (float)mn;
     c.zp = 0.f;
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
     uint32_t hb[4] = {0, 0, 0, 0};
-    if constexpr (WT == W_Q5_K) {
-      uint4 qh = *reinterpret_cast<const uint4*>(st1 + r * 32 + l0);
-      hb[0] = qh.x; hb[1] = qh.y; hb[2] = qh.z; hb[3] = qh.w;
-    }
+    if constexpr (WT == W_Q5_K) words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 1>(ch, r, qq & 1)), hb);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t v = (h ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
@@ -117,31 +97,33 @@ BARQ_DEV Codes load_codes(const uint8_t* st0, const uint8_t* st1, const uint8_t*
       c.u[i] = v;
     }
   } else if constexpr (WT == W_Q6_K) {
-    const int c4 = s & 3, n = c4 >> 1, hh = c4 & 1, qd = 2 * hh + (qq >> 1), l0 = 16 * (qq & 1);
-    uint4 ql = *reinterpret_cast<const uint4*>(st0 + r * 64 + ((qd & 1) ? 32 : 0) + l0);
-    uint4 qh = *reinterpret_cast<const uint4*>(st1 + r * 32 + l0);
-    const int8_t scl = reinterpret_cast<const int8_t*>(st2 + r * 16)[8 * n + 2 * qd + (l0 >> 4)];
-    const float dd = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 256) + (s >> 2)]) : 0.f;
+    const int n = sub >> 1, hh = sub & 1, qd = 2 * hh + (qq >> 1), l0c = qq & 1;
+    uint32_t w[4], hb[4];
+    words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, 4 * n + 2 * (qd & 1) + l0c)), w);
+    words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 1>(ch, r, 2 * n + l0c)), hb);
+    const int8_t scl = reinterpret_cast<const int8_t*>(staged_chunk<WT, 2>(ch, r, 0))[8 * n + 2 * qd + l0c];
+    const float dd = h2f(reinterpret_cast<const uint16_t*>(ch + F::D_OFF)[r]);
     c.sc = dd * (float)scl;
     c.bi = 0.f;
     c.zp = 32.f;
-    uint32_t w[4] = {ql.x, ql.y, ql.z, ql.w}, hb[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       c.u[i] = ((qd >= 2 ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * qd)) & 0x03030303u) << 4);
   } else if constexpr (WT == W_Q8_0) {
-    const int blk = qq >> 1;
-    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 64 + 32 * blk + 16 * (qq & 1));
-    c.sc = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + blk]) : 0.f;
+    const int bi = qq >> 1;
+    uint32_t w[4];
+    words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, 2 * bi + (qq & 1))), w);
+    c.sc = h2f(reinterpret_cast<const uint16_t*>(ch + F::D_OFF)[2 * r + bi]);
     c.bi = 0.f;
     c.zp = 128.f;
-    c.u[0] = q.x ^ 0x80808080u; c.u[1] = q.y ^ 0x80808080u; c.u[2] = q.z ^ 0x80808080u; c.u[3] = q.w ^ 0x80808080u;
-  } else {  // Q4_0 / IQ4_NL: block 2s + qq/2; qq&1 selects low (elements 0-15) or high nibbles (16-31)
-    const int blk = qq >> 1, hi = qq & 1;
-    uint4 q = *reinterpret_cast<const uint4*>(st0 + r * 32 + 16 * blk);
-    c.sc = grow < g.N ? h2f(g.d[(size_t)grow * (g.K / 32) + 2 * s + blk]) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c.u[i] = w[i] ^ 0x80808080u;
+  } else {  // Q4_0 / IQ4_NL: block qq/2 of the stage; qq&1 selects low (elements 0-15) or high nibbles
+    const int bi = qq >> 1, hi = qq & 1;
+    uint32_t w[4];
+    words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, bi)), w);
+    c.sc = h2f(reinterpret_cast<const uint16_t*>(ch + F::D_OFF)[2 * r + bi]);
     c.bi = 0.f;
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t v = (hi ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
@@ -157,6 +139,9 @@ BARQ_DEV Codes load_codes(const uint8_t* st0, const uint8_t* st1, const uint8_t*
 }
 
 // 16 codes -> two 16-byte chunks of fp16 (F16 = true) or bf16 operands.
+// fp16: a byte permute places two codes in the mantissas of 1024.0h (exact), one packed subtract
+// removes 1024 + zp, one packed FMA applies scale and bias (~2 instructions per weight).
+// bf16: codes go through fp32 (mantissa of 2^23, subtract, FMA) and a packed round to bf16x2.
 template <bool F16>
 BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
   uint32_t r[8];
@@ -190,26 +175,24 @@ BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
   out[1] = make_uint4(r[4], r[5], r[6], r[7]);
 }
 
-template <int WT, int BN, int S>
+template <int WT, int BN, int S, int SQ>
 struct GemmSmem {
   static constexpr int A_BYTES = 128 * 128;       // 128 rows x 64 fp16/bf16
   static constexpr int B_BYTES = BN * 128;        // BN rows x 64 fp16/bf16
-  static constexpr int QW0 = Planes<WT>::w0 * 128, QW1 = Planes<WT>::w1 * 128, QW2 = Planes<WT>::w2 * 128;
-  static constexpr int Q_BYTES = QW0 + QW1 + QW2;
-  static constexpr int XCH_BYTES = 4 * 32 * 32 * 4;  // SwiGLU gate/up exchange, one 32x32 f32 tile per quadrant
+  static constexpr int Q_BYTES = TileFmt<WT>::CHUNK;
+  static constexpr int XCH_BYTES = 4 * 32 * 32 * 4;  // SwiGLU exchange, one 32x32 f32 tile per quadrant
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + S * A_BYTES;
   static constexpr int OFF_Q = OFF_B + S * B_BYTES;
-  static constexpr int OFF_XCH = OFF_Q + S * Q_BYTES;
+  static constexpr int OFF_XCH = OFF_Q + ((SQ * Q_BYTES + 1023) / 1024) * 1024;
   static constexpr int OFF_BAR = OFF_XCH + XCH_BYTES;
-  static constexpr int N_BAR = 5 * S + 4;
+  static constexpr int N_BAR = 2 * SQ + 3 * S + 4;
   static constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
   static constexpr int TOTAL = OFF_TMEM + 16 + 1024;  // + alignment slack
 };
 
-// Warp roles of the persistent kernel.
 constexpr int kDequantWarps = 16;  // 4 per TMEM lane quadrant; each thread expands 16 weights per stage
-constexpr int kEpiWarp0 = kDequantWarps;      // 4 epilogue warps, one per lane quadrant
+constexpr int kEpiWarp0 = kDequantWarps;  // 4 epilogue warps, one per lane quadrant
 constexpr int kTmaWarp = kDequantWarps + 4;
 constexpr int kMmaWarp = kDequantWarps + 5;
 constexpr int kThreads = (kDequantWarps + 6) * 32;
@@ -224,25 +207,22 @@ struct TileMap {
   }
 };
 
-// Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...  The smem ring (S stages) and
-// the stage counter run continuously across tiles; the accumulator is double-buffered in TMEM
-// (2 x BN columns) so the epilogue of one tile overlaps the mainloop of the next.
-template <int WT, int BN, int S, bool F16>
+template <int WT, int BN, int S, int SQ, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
-    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tp0,
-                    const __grid_constant__ CUtensorMap tp1, const __grid_constant__ CUtensorMap tp2, GemmDev g) {
-  using L = GemmSmem<WT, BN, S>;
-  using P = Planes<WT>;
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, GemmDev g) {
+  using L = GemmSmem<WT, BN, S, SQ>;
+  using F = TileFmt<WT>;
+  constexpr int SPG = F::G / 64;  // 64-column stages per weight chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* fullQ = bars;
-  uint64_t* emptyQ = bars + S;
-  uint64_t* fullB = bars + 2 * S;
-  uint64_t* fullA = bars + 3 * S;
-  uint64_t* consumed = bars + 4 * S;
-  uint64_t* accFull = bars + 5 * S;      // [2]
-  uint64_t* accEmpty = bars + 5 * S + 2; // [2]
+  uint64_t* fullQ = bars;                // [SQ] chunk landed
+  uint64_t* emptyQ = bars + SQ;          // [SQ] chunk fully expanded
+  uint64_t* fullB = bars + 2 * SQ;       // [S]  activation tile landed
+  uint64_t* fullA = bars + 2 * SQ + S;   // [S]  weight operand written
+  uint64_t* consumed = bars + 2 * SQ + 2 * S;  // [S] MMAs of the stage done
+  uint64_t* accFull = bars + 2 * SQ + 3 * S;   // [2]
+  uint64_t* accEmpty = accFull + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
   __shared__ int err_s;
 
@@ -252,17 +232,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   tm.t_tiles = (g.T + BN - 1) / BN;
   tm.ks = g.k_splits;
   tm.total = tm.n_tiles * tm.t_tiles * tm.ks;
-  const int nst_total = g.K / 64;
-  auto krange = [&](int z, int& kb, int& ke) {
-    kb = (int)((long)nst_total * z / g.k_splits);
-    ke = (int)((long)nst_total * (z + 1) / g.k_splits);
+  const int KG = g.K / F::G;
+  auto grange = [&](int z, int& gb, int& ge) {
+    gb = (int)((long)KG * z / g.k_splits);
+    ge = (int)((long)KG * (z + 1) / g.k_splits);
   };
 
   if (threadIdx.x == 0) {
     err_s = 0;
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < SQ; ++i) {
       mbar_init(&fullQ[i], 1);
       mbar_init(&emptyQ[i], kDequantWarps);
+    }
+    for (int i = 0; i < S; ++i) {
       mbar_init(&fullB[i], 1);
       mbar_init(&fullA[i], kDequantWarps);
       mbar_init(&consumed[i], 1);
@@ -281,29 +263,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* err = &err_s;
 
   if (warp == kTmaWarp) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tmap(&tx);
-      prefetch_tmap(&tp0);
-      if (P::w1) prefetch_tmap(&tp1);
-      if (P::w2) prefetch_tmap(&tp2);
-      int it = 0;
+      int it = 0, qc = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
-        int nt, tt, z, kb, ke;
+        int nt, tt, z, gb, ge;
         tm.decode(u, nt, tt, z);
-        krange(z, kb, ke);
-        for (int ks = kb; ks < ke; ++ks, ++it) {
-          const int s = it % S, ph = (it / S) & 1;
-          if (it >= S && !mbar_wait(&emptyQ[s], ph ^ 1, err, 1)) break;
-          uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
-          mbar_expect_tx(&fullQ[s], L::Q_BYTES);
-          tma_load_2d(q, &tp0, P::x0(ks), nt * 128, &fullQ[s]);
-          if (P::w1) tma_load_2d(q + L::QW0, &tp1, P::x1(ks), nt * 128, &fullQ[s]);
-          if (P::w2) tma_load_2d(q + L::QW0 + L::QW1, &tp2, P::x2(ks), nt * 128, &fullQ[s]);
-          if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) break;
-          mbar_expect_tx(&fullB[s], L::B_BYTES);
-          tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, tt * BN, &fullB[s]);
+        grange(z, gb, ge);
+        bool ok = true;
+        for (int kg = gb; kg < ge && ok; ++kg, ++qc) {
+          const int qs = qc % SQ, qph = (qc / SQ) & 1;
+          if (qc >= SQ && !mbar_wait(&emptyQ[qs], qph ^ 1, err, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&fullQ[qs], L::Q_BYTES);
+          bulk_load(smem + L::OFF_Q + qs * L::Q_BYTES, g.w + ((size_t)nt * KG + kg) * F::CHUNK, L::Q_BYTES,
+                    &fullQ[qs]);
+          for (int sub = 0; sub < SPG; ++sub, ++it) {
+            const int s = it % S, ph = (it / S) & 1;
+            if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&fullB[s], L::B_BYTES);
+            tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * (kg * SPG + sub), tt * BN, &fullB[s]);
+          }
         }
+        if (!ok) break;
       }
     }
   } else if (warp == kMmaWarp) {
@@ -312,15 +300,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = F16 ? idesc_f16(128, BN) : idesc_bf16(128, BN);
       int it = 0, tc = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x, ++tc) {
-        int nt, tt, z, kb, ke;
+        int nt, tt, z, gb, ge;
         tm.decode(u, nt, tt, z);
-        krange(z, kb, ke);
+        grange(z, gb, ge);
         const int buf = tc & 1, use = tc >> 1;
         if (tc >= 2 && !mbar_wait(&accEmpty[buf], (use - 1) & 1, err, 8)) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         bool ok = true;
-        for (int ks = kb; ks < ke; ++ks, ++it) {
+        const int nst = (ge - gb) * SPG;
+        for (int i = 0; i < nst; ++i, ++it) {
           const int s = it % S, ph = (it / S) & 1;
           if (!mbar_wait(&fullA[s], ph, err, 3) || !mbar_wait(&fullB[s], ph, err, 4)) {
             ok = false;
@@ -331,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (ks > kb) | (k > 0));
+            mma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
           mma_commit(&consumed[s]);
         }
         if (!ok) break;
@@ -342,35 +331,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- dequant producers
     const int quad = warp & 3, qq = warp >> 2;
     const int r = quad * 32 + lane;
-    int it = 0;
+    int it = 0, qc = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < tm.total && ok && !*err; u += gridDim.x) {
-      int nt, tt, z, kb, ke;
+      int nt, tt, z, gb, ge;
       tm.decode(u, nt, tt, z);
-      krange(z, kb, ke);
-      const int grow = nt * 128 + r;
-      for (int ks = kb; ks < ke; ++ks, ++it) {
-        const int s = it % S, ph = (it / S) & 1;
-        if (!mbar_wait(&fullQ[s], ph, err, 5)) {
+      grange(z, gb, ge);
+      for (int kg = gb; kg < ge && ok; ++kg, ++qc) {
+        const int qs = qc % SQ, qph = (qc / SQ) & 1;
+        if (!mbar_wait(&fullQ[qs], qph, err, 5)) {
           ok = false;
           break;
         }
-        const uint8_t* q = smem + L::OFF_Q + s * L::Q_BYTES;
-        const Codes cd = load_codes<WT>(q, q + L::QW0, q + L::QW0 + L::QW1, r, qq, ks, grow, g);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&emptyQ[s]);
-        uint4 ops[2];
-        codes_to_operands<F16>(cd, ops);
-        if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
-          ok = false;
-          break;
+        const uint8_t* ch = smem + L::OFF_Q + qs * L::Q_BYTES;
+        for (int sub = 0; sub < SPG; ++sub, ++it) {
+          const int s = it % S, ph = (it / S) & 1;
+          const Codes cd = load_codes<WT>(ch, r, qq, sub);
+          uint4 ops[2];
+          codes_to_operands<F16>(cd, ops);
+          if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
+            ok = false;
+            break;
+          }
+          uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
+          *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
+          *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&fullA[s]);
         }
-        uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
-        *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
-        *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
-        fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&fullA[s]);
+        if (ok && lane == 0) mbar_arrive(&emptyQ[qs]);
       }
     }
   } else {
@@ -378,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp - kEpiWarp0;
     const int r = quad * 32 + lane;
     using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-    AT* out_act = reinterpret_cast<AT*>(g.out_bf16);
+    AT* out_act = reinterpret_cast<AT*>(g.out_act);
     float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);
     const bool atomic = g.k_splits > 1;
     int tc = 0;
@@ -388,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = tc & 1, use = tc >> 1;
       mbar_wait(&accFull[buf], use & 1, err, 7);
       tc_fence_after();
-      // All 128 epilogue threads agree on `stop` (the error word only grows).
+      // All 128 epilogue threads agree on stopping (the error word only ever grows).
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (*err) break;
       const int n0 = nt * 128, t0 = tt * BN, n = n0 + r;
@@ -464,18 +455,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-static int make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
-                       uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-                       CUtensorMapSwizzle sw) {
+static int make_act_map(CUtensorMap* m, const void* base, bool f16, int K, int T, int bn) {
   auto enc = get_encode();
   if (!enc) return -10;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)bn};
   cuuint32_t es[2] = {1, 1};
-  (void)elem_bytes;
-  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -11;
 }
 
@@ -505,84 +494,74 @@ int gemm_clear_error_word() {
   return p && cudaMemset(p, 0, sizeof(int)) == cudaSuccess ? 0 : -1;
 }
 
-template <int WT, int BN, int S, bool F16>
-static int launch_gemm(const QW& w, const CUtensorMap& tx, const CUtensorMap& m0, const CUtensorMap& m1,
-                       const CUtensorMap& m2, const GemmDev& g, int tiles_t, cudaStream_t st) {
-  using L = GemmSmem<WT, BN, S>;
-  static_assert(L::TOTAL <= 232448, "shared memory budget");
-  auto kern = qgemm_tc_kernel<WT, BN, S, F16>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-  const int total = ((w.N + 127) / 128) * tiles_t * g.k_splits;
-  static int n_sm = 0;
-  if (!n_sm) {
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    if (n_sm <= 0) n_sm = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
   }
-  dim3 grid(total < n_sm ? total : n_sm);
-  kern<<<grid, kThreads, L::TOTAL, st>>>(tx, m0, m1, m2, g);
+  return n;
+}
+
+template <int WT, int BN, int S, int SQ, bool F16>
+static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cudaStream_t st) {
+  using L = GemmSmem<WT, BN, S, SQ>;
+  static_assert(L::TOTAL <= 232448, "shared memory budget");
+  auto kern = qgemm_tc_kernel<WT, BN, S, SQ, F16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  const int total = ((g.N + 127) / 128) * tiles_t * g.k_splits;
+  const int n = sm_count();
+  kern<<<dim3(total < n ? total : n), kThreads, L::TOTAL, st>>>(tx, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
 }
 
 template <int WT, bool F16>
-static int dispatch_bn(const QW& w, const void* x, int T, const GemmDev& g0, cudaStream_t st) {
-  using P = Planes<WT>;
+static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
+  using F = TileFmt<WT>;
+  constexpr int SQ = F::CHUNK > 12000 ? 2 : 4;  // weight chunks in flight
   GemmDev g = g0;
-  const int K = w.K, N = w.N;
-  CUtensorMap mx, m0, m1, m2;
-  memset(&m1, 0, sizeof(m1));
-  memset(&m2, 0, sizeof(m2));
-  int bn = T <= 64 ? 64 : (T <= 128 ? 128 : 256);
-  int rc = make_map_2d(&mx, x, F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, T,
-                       (uint64_t)K * 2, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int bn = g.T <= 64 ? 64 : (g.T <= 128 ? 128 : 256);
+  CUtensorMap mx;
+  int rc = make_act_map(&mx, x, F16, g.K, g.T, bn);
   if (rc) return rc;
-  uint64_t rb0 = WT == W_Q8_0 ? K : (WT == W_Q6_K ? K / 2 : K / 2);
-  rc = make_map_2d(&m0, w.p0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb0, N, rb0, P::w0, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  if (P::w1) {
-    uint64_t rb1 = WT == W_Q5_K ? K / 8 : K / 4;
-    rc = make_map_2d(&m1, w.p1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb1, N, rb1, P::w1, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  }
-  if (P::w2) {
-    uint64_t rb2 = WT == W_Q6_K ? K / 16 : (K / 256) * 16;
-    rc = make_map_2d(&m2, w.p2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb2, N, rb2, P::w2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  }
-  const int tiles_t = (T + bn - 1) / bn;
-  if (g.k_splits == 0) {  // auto split-K so that small token counts still fill the 148 SMs
-    const int tiles = ((N + 127) / 128) * tiles_t, nst = K / 64;
+  const int tiles_t = (g.T + bn - 1) / bn;
+  const int KG = g.K / F::G;
+  if (g.k_splits == 0) {  // automatic split-K so that small token counts still fill the SMs
+    const int tiles = ((g.N + 127) / 128) * tiles_t, n = sm_count();
     int ks = 1;
     if (g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32)
-      while (tiles * ks * 2 <= 2 * 148 && nst / (ks * 2) >= 4) ks *= 2;
+      while (tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
     g.k_splits = ks;
   }
+  if (g.k_splits > KG) g.k_splits = KG;
   if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
-    if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)N * 4, T, st) != cudaSuccess) return -6;
+    if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)g.N * 4, g.T, st) != cudaSuccess) return -6;
   }
-  if (bn == 64) return launch_gemm<WT, 64, 5, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
-  if (bn == 128) return launch_gemm<WT, 128, 4, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
-  return launch_gemm<WT, 256, 3, F16>(w, mx, m0, m1, m2, g, tiles_t, st);
+  if (bn == 64) return launch_gemm<WT, 64, 6, SQ, F16>(mx, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, 4, SQ, F16>(mx, g, tiles_t, st);
+  return launch_gemm<WT, 256, 3, SQ, F16>(mx, g, tiles_t, st);
 }
 
 template <bool F16>
-static int dispatch_type(const QW& w, const void* x, int T, const GemmDev& g, cudaStream_t st) {
-  switch (w.type) {
-    case W_Q4_K: return dispatch_bn<W_Q4_K, F16>(w, x, T, g, st);
-    case W_Q5_K: return dispatch_bn<W_Q5_K, F16>(w, x, T, g, st);
-    case W_Q6_K: return dispatch_bn<W_Q6_K, F16>(w, x, T, g, st);
-    case W_Q8_0: return dispatch_bn<W_Q8_0, F16>(w, x, T, g, st);
-    case W_Q4_0: return dispatch_bn<W_Q4_0, F16>(w, x, T, g, st);
-    case W_IQ4_NL: return dispatch_bn<W_IQ4_NL, F16>(w, x, T, g, st);
+static int dispatch_type(int type, const void* x, const GemmDev& g, cudaStream_t st) {
+  switch (type) {
+    case W_Q4_K: return dispatch_bn<W_Q4_K, F16>(x, g, st);
+    case W_Q5_K: return dispatch_bn<W_Q5_K, F16>(x, g, st);
+    case W_Q6_K: return dispatch_bn<W_Q6_K, F16>(x, g, st);
+    case W_Q8_0: return dispatch_bn<W_Q8_0, F16>(x, g, st);
+    case W_Q4_0: return dispatch_bn<W_Q4_0, F16>(x, g, st);
+    case W_IQ4_NL: return dispatch_bn<W_IQ4_NL, F16>(x, g, st);
   }
   return -7;
 }
 
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
   if (T <= 0) return 0;
-  if (w.K % 256 && !(w.K % 64 == 0 && (w.type == W_Q8_0 || w.type == W_Q4_0 || w.type == W_IQ4_NL))) return -2;
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (w.K * 2) % 16) return -3;
+  const int G = (w.type == W_Q4_K || w.type == W_Q5_K || w.type == W_Q6_K) ? 256 : 64;
+  if (w.K % G) return -2;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w.p0) & 15)) return -3;
   if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128 || k_splits > 1)) return -4;
   if (ep.mode == EPI_SWIGLU_Q8 || ep.mode == EPI_STORE_BF16) k_splits = 1;
   if (k_splits < 0) k_splits = 0;
@@ -590,15 +569,15 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
   g.N = w.N;
   g.K = w.K;
   g.T = T;
-  g.d = w.d;
+  g.w = w.p0;
   g.mode = ep.mode;
   g.out_f32 = ep.out_f32;
-  g.out_bf16 = ep.out_bf16;
+  g.out_act = ep.out_bf16;
   g.bias = ep.bias;
   g.ld_out = ep.ld_out;
   g.k_splits = k_splits;
   g.err = device_err_word();
-  return x_is_f16 ? dispatch_type<true>(w, x, T, g, st) : dispatch_type<false>(w, x, T, g, st);
+  return x_is_f16 ? dispatch_type<true>(w.type, x, g, st) : dispatch_type<false>(w.type, x, g, st);
 }
 
 }  // namespace barq

@@ -7,6 +7,7 @@
 #pragma once
 #include "common.cuh"
 #include "qweight.cuh"
+#include "qtile.cuh"
 
 namespace barq {
 
@@ -63,10 +64,13 @@ template <bool NL>
 struct T4Block {
   struct W { int4 q; float d; };
   struct X { int4 a, b; float d; };
+  static constexpr int WT = NL ? W_IQ4_NL : W_Q4_0;
   static BARQ_DEV W load_w(const QW& w, int row, int p) {
     W r;
-    r.q = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
-    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 32) + p));
+    const int kg = p >> 1, bi = p & 1;
+    r.q = ldg16_stream(plane_chunk<WT, 0>(w, row, kg, bi));
+    r.d = h2f(__ldg(reinterpret_cast<const uint16_t*>(chunk_ptr<WT>(w, row >> 7, kg) + TileFmt<WT>::D_OFF +
+                                                      (row & 127) * 4) + bi));
     return r;
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
@@ -99,10 +103,11 @@ struct TQ8_0 {
   struct X { int4 a, b; float d; };
   static BARQ_DEV W load_w(const QW& w, int row, int p) {
     W r;
-    const uint8_t* base = w.p0 + (size_t)row * w.K + (size_t)p * 32;
-    r.a = ldg16_stream(base);
-    r.b = ldg16_stream(base + 16);
-    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 32) + p));
+    const int kg = p >> 1, bi = p & 1;
+    r.a = ldg16_stream(plane_chunk<W_Q8_0, 0>(w, row, kg, 2 * bi));
+    r.b = ldg16_stream(plane_chunk<W_Q8_0, 0>(w, row, kg, 2 * bi + 1));
+    r.d = h2f(__ldg(reinterpret_cast<const uint16_t*>(chunk_ptr<W_Q8_0>(w, row >> 7, kg) + TileFmt<W_Q8_0>::D_OFF +
+                                                      (row & 127) * 4) + bi));
     return r;
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
@@ -124,12 +129,17 @@ template <bool FIVE>
 struct TK45 {
   struct W { int4 q; int4 hdr; int4 qh; };
   struct X { int4 a, b; float2 sa, sb; };
+  static constexpr int WT = FIVE ? W_Q5_K : W_Q4_K;
   static BARQ_DEV W load_w(const QW& w, int row, int p) {
     W r;
-    int b = p >> 3;
-    r.q = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
-    r.hdr = ldg16(w.p2 + ((size_t)row * (w.K / 256) + b) * 16);
-    if (FIVE) r.qh = ldg16(w.p1 + (size_t)row * (w.K / 8) + (size_t)b * 32 + (p & 1) * 16);
+    const int kg = p >> 3;
+    r.q = ldg16_stream(plane_chunk<WT, 0>(w, row, kg, p & 7));
+    if constexpr (FIVE) {
+      r.hdr = ldg16(plane_chunk<WT, 2>(w, row, kg, 0));
+      r.qh = ldg16(plane_chunk<WT, 1>(w, row, kg, p & 1));
+    } else {
+      r.hdr = ldg16(plane_chunk<WT, 1>(w, row, kg, 0));
+    }
     return r;
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
@@ -175,13 +185,14 @@ struct TQ6_K {
   struct X { int4 a, b; float da, db; };
   static BARQ_DEV W load_w(const QW& w, int row, int p) {
     W r;
-    int b = p >> 3, q = p & 7, n = q >> 2, c = (q >> 1) & 1, h = q & 1;
-    r.ql = ldg16_stream(w.p0 + (size_t)row * (w.K / 2) + (size_t)p * 16);
-    r.qh = ldg16(w.p1 + (size_t)row * (w.K / 4) + (size_t)b * 64 + 32 * n + 16 * h);
-    const int8_t* sc = reinterpret_cast<const int8_t*>(w.p2) + (size_t)row * (w.K / 16) + (size_t)b * 16;
+    const int kg = p >> 3, q = p & 7, n = q >> 2, c = (q >> 1) & 1, h = q & 1;
+    r.ql = ldg16_stream(plane_chunk<W_Q6_K, 0>(w, row, kg, q));
+    r.qh = ldg16(plane_chunk<W_Q6_K, 1>(w, row, kg, 2 * n + h));
+    const int8_t* sc = reinterpret_cast<const int8_t*>(plane_chunk<W_Q6_K, 2>(w, row, kg, 0));
     int lo = __ldg(sc + 8 * n + 2 * c + h), hi = __ldg(sc + 8 * n + 4 + 2 * c + h);
     r.sc = (uint32_t)(lo & 0xFFFF) | ((uint32_t)hi << 16);
-    r.d = h2f(__ldg(w.d + (size_t)row * (w.K / 256) + b));
+    r.d = h2f(__ldg(reinterpret_cast<const uint16_t*>(chunk_ptr<W_Q6_K>(w, row >> 7, kg) + TileFmt<W_Q6_K>::D_OFF +
+                                                      (row & 127) * 2)));
     return r;
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {

@@ -1,21 +1,6 @@
-// Device-side view of a quantized weight in the planar ("split-plane") layout.
-//
-// A GGUF tensor is a row-major sequence of ggml blocks whose sizes (18, 34, 144, 176, 210 bytes)
-// are not multiples of 16, so rows of Q4_0/Q8_0/Q6_K blocks are not 16-byte aligned.  At load
-// time every weight is split, block by block and without changing a bit, into up to four planes:
-//
-//   type     p0 (quants)        p1 (high bits)   p2 (per-block header)        d (f16 per block)
-//   Q4_0     qs  [N, K/2]       -                -                            d  [N, K/32]
-//   IQ4_NL   qs  [N, K/2]       -                -                            d  [N, K/32]
-//   Q8_0     qs  [N, K]  (i8)   -                -                            d  [N, K/32]
-//   Q4_K     qs  [N, K/2]       -                hdr [N, K/256, 16] (d,dmin,scales[12])
-//   Q5_K     qs  [N, K/2]       qh [N, K/8]      hdr [N, K/256, 16]
-//   Q6_K     ql  [N, K/2]       qh [N, K/4]      sc  [N, K/16] (i8)           d  [N, K/256]
-//   BF16     w   [N, K]  (bf16)
-//
-// The map is a bijection (the Python side re-emits the GGUF blocks from the planes in tests) and
-// every plane row starts on a 16-byte boundary when K is a multiple of 256 (32 for Q4_0/Q8_0/IQ4_NL),
-// which is what both the vector loads of the GEMV kernels and the TMA boxes of the tcgen05 GEMM need.
+// Device-side view of a quantized weight.  Kernels read the tiled layout described in qtile.cuh
+// (p0 = tiled chunk buffer); dense bf16 weights are plain [N, K] rows in p0.  p1/p2/d are unused by
+// the tiled kernels.
 #pragma once
 #include <stdint.h>
 #include <vector_types.h>
