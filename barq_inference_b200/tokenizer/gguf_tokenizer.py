@@ -269,7 +269,11 @@ def synthetic_tokenizer(vocab: int, seed: int = 0) -> GGUFTokenizer:
     base += list("0123456789.,!?;:'\"()-")
     words = ["the", "and", "of", "to", "in", "is", "it", "that", "for", "on", "with", "as", "was", "barq", "model",
              "token", "fast", "gpu", "hello", "world", "json", "true", "false", "null"]
-    extra = [SPIECE + w for w in words] + words
+    extra = []
+    for w in words:  # every prefix, so score-ordered pair merges can reach the whole word
+        for k in range(2, len(w) + 1):
+            extra += [SPIECE + w[:k], w[:k]]
+        extra.append(SPIECE + w[0])
     seen = set(toks)
     for t in base + extra:
         if t not in seen:

@@ -222,6 +222,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemm", &qgemm);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_clear_error", &gemm_clear_error);
+  m.def("gemm_set_trace", [](Tensor t) { barq::gemm_set_trace(t.data_ptr()); });
   m.def("quantize_q8", &quantize_q8);
   m.def("swiglu", &swiglu);
   m.def("rope_kv_write", &rope_kv_write);

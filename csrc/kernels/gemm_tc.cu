@@ -15,17 +15,19 @@
 // and their stage counters run continuously across tiles, and the accumulator is double-buffered in
 // TMEM (2 x BN columns) so the epilogue of one tile overlaps the mainloop of the next.
 //
-// Warp roles (704 threads):
+// Warp roles (736 threads):
 //   warps 0-15  dequant: expand 16 weights each per 64-column stage straight into the UMMA
 //               128B-swizzle K-major layout, fence the async proxy, signal "A full";
 //   warps 16-19 epilogue: tcgen05.ld the finished accumulator -> global (store / residual add /
 //               split-K atomics / SwiGLU);
-//   warp 20     producer: bulk copy of weight chunks, TMA of activation tiles;
-//   warp 21     MMA: one thread issues 4 x tcgen05.mma (K = 16) per stage and commits completion.
+//   warp 20     weight producer: bulk copies of weight chunks, up to SQ chunks ahead;
+//   warp 21     activation producer: TMA of activation tiles, one ring slot behind the MMAs;
+//   warp 22     MMA: one thread issues 4 x tcgen05.mma (K = 16) per stage and commits completion.
 // Every wait is bounded (tc_common.cuh); on expiry the CTA records an error word and unwinds.
 // No load here uses .multicast::cluster.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 #include <unordered_map>
@@ -49,7 +51,16 @@ struct GemmDev {
   int ld_out;
   int k_splits;
   int* err;
+  int exp;  // diagnostics: bit 0 = skip the dequant arithmetic (write zeros), bit 1 = trace CTA 0
+  unsigned long long* trace;  // [kTraceStages][8] globaltimer stamps when tracing
 };
+constexpr int kTraceStages = 256;
+// trace fields per stage: 0 chunk issued, 1 chunk landed (dequant warp 0), 2 A written (dequant 0),
+// 3 act issued, 4 MMA saw A, 5 MMA saw B, 6 MMA issued, 7 consumed observed by dequant 0
+BARQ_DEV void trace(const GemmDev& g, int stage, int field) {
+  if ((g.exp & 2) && blockIdx.x == 0 && stage < kTraceStages && g.trace)
+    g.trace[stage * 8 + field] = globaltimer_ns();
+}
 
 // 1-D bulk copy global -> shared, completion on `bar` (transaction bytes).
 BARQ_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -193,9 +204,10 @@ struct GemmSmem {
 
 constexpr int kDequantWarps = 16;  // 4 per TMEM lane quadrant; each thread expands 16 weights per stage
 constexpr int kEpiWarp0 = kDequantWarps;  // 4 epilogue warps, one per lane quadrant
-constexpr int kTmaWarp = kDequantWarps + 4;
-constexpr int kMmaWarp = kDequantWarps + 5;
-constexpr int kThreads = (kDequantWarps + 6) * 32;
+constexpr int kTmaWarp = kDequantWarps + 4;  // weight chunks (gated only by chunk-slot release)
+constexpr int kActWarp = kDequantWarps + 5;  // activation tiles (gated by MMA progress)
+constexpr int kMmaWarp = kDequantWarps + 6;
+constexpr int kThreads = (kDequantWarps + 7) * 32;
 
 struct TileMap {
   int n_tiles, t_tiles, ks, total;
@@ -263,33 +275,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* err = &err_s;
 
   if (warp == kTmaWarp) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- weight-chunk producer
+    // Runs up to SQ chunks ahead of the dequant warps, independent of MMA progress.
     if (lane == 0) {
-      prefetch_tmap(&tx);
-      int it = 0, qc = 0;
+      int qc = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
         int nt, tt, z, gb, ge;
         tm.decode(u, nt, tt, z);
         grange(z, gb, ge);
         bool ok = true;
-        for (int kg = gb; kg < ge && ok; ++kg, ++qc) {
+        for (int kg = gb; kg < ge; ++kg, ++qc) {
           const int qs = qc % SQ, qph = (qc / SQ) & 1;
           if (qc >= SQ && !mbar_wait(&emptyQ[qs], qph ^ 1, err, 1)) {
             ok = false;
             break;
           }
           mbar_expect_tx(&fullQ[qs], L::Q_BYTES);
+          trace(g, qc * SPG, 0);
           bulk_load(smem + L::OFF_Q + qs * L::Q_BYTES, g.w + ((size_t)nt * KG + kg) * F::CHUNK, L::Q_BYTES,
                     &fullQ[qs]);
-          for (int sub = 0; sub < SPG; ++sub, ++it) {
-            const int s = it % S, ph = (it / S) & 1;
-            if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) {
-              ok = false;
-              break;
-            }
-            mbar_expect_tx(&fullB[s], L::B_BYTES);
-            tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * (kg * SPG + sub), tt * BN, &fullB[s]);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == kActWarp) {
+    // ---------------------------------------------------------------- activation-tile producer
+    if (lane == 0) {
+      prefetch_tmap(&tx);
+      int it = 0;
+      for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
+        int nt, tt, z, gb, ge;
+        tm.decode(u, nt, tt, z);
+        grange(z, gb, ge);
+        bool ok = true;
+        for (int ks = gb * SPG; ks < ge * SPG; ++ks, ++it) {
+          const int s = it % S, ph = (it / S) & 1;
+          if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) {
+            ok = false;
+            break;
           }
+          mbar_expect_tx(&fullB[s], L::B_BYTES);
+          trace(g, it, 3);
+          tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, tt * BN, &fullB[s]);
         }
         if (!ok) break;
       }
@@ -311,10 +338,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nst = (ge - gb) * SPG;
         for (int i = 0; i < nst; ++i, ++it) {
           const int s = it % S, ph = (it / S) & 1;
-          if (!mbar_wait(&fullA[s], ph, err, 3) || !mbar_wait(&fullB[s], ph, err, 4)) {
+          if (!mbar_wait(&fullA[s], ph, err, 3)) {
             ok = false;
             break;
           }
+          trace(g, it, 4);
+          if (!mbar_wait(&fullB[s], ph, err, 4)) {
+            ok = false;
+            break;
+          }
+          trace(g, it, 5);
           tc_fence_after();
           const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
           const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
@@ -322,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k)
             mma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
           mma_commit(&consumed[s]);
+          trace(g, it, 6);
         }
         if (!ok) break;
         mma_commit(&accFull[buf]);
@@ -343,22 +377,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (warp == 0 && lane == 0) trace(g, qc * SPG, 1);
         const uint8_t* ch = smem + L::OFF_Q + qs * L::Q_BYTES;
         for (int sub = 0; sub < SPG; ++sub, ++it) {
           const int s = it % S, ph = (it / S) & 1;
-          const Codes cd = load_codes<WT>(ch, r, qq, sub);
           uint4 ops[2];
-          codes_to_operands<F16>(cd, ops);
+          if (g.exp & 1) {
+            ops[0] = ops[1] = make_uint4(0, 0, 0, 0);
+          } else {
+            const Codes cd = load_codes<WT>(ch, r, qq, sub);
+            codes_to_operands<F16>(cd, ops);
+          }
           if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
             ok = false;
             break;
           }
+          if (warp == 0 && lane == 0) trace(g, it, 7);
           uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
           *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
           *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) mbar_arrive(&fullA[s]);
+          if (warp == 0 && lane == 0) trace(g, it, 2);
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(&emptyQ[qs]);
@@ -520,7 +561,10 @@ static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cud
 template <int WT, bool F16>
 static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   using F = TileFmt<WT>;
-  constexpr int SQ = F::CHUNK > 12000 ? 2 : 4;  // weight chunks in flight
+  // weight chunks in flight per SM: keep >= ~64 KB of loads outstanding to cover DRAM latency
+  constexpr int SQ64 = F::CHUNK > 24000 ? 3 : (F::CHUNK > 12000 ? 4 : 8);
+  constexpr int SQ128 = F::CHUNK > 24000 ? 2 : (F::CHUNK > 12000 ? 3 : 6);
+  constexpr int SQ256 = F::CHUNK > 12000 ? 2 : 4;
   GemmDev g = g0;
   const int bn = g.T <= 64 ? 64 : (g.T <= 128 ? 128 : 256);
   CUtensorMap mx;
@@ -539,9 +583,9 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
     if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)g.N * 4, g.T, st) != cudaSuccess) return -6;
   }
-  if (bn == 64) return launch_gemm<WT, 64, 6, SQ, F16>(mx, g, tiles_t, st);
-  if (bn == 128) return launch_gemm<WT, 128, 4, SQ, F16>(mx, g, tiles_t, st);
-  return launch_gemm<WT, 256, 3, SQ, F16>(mx, g, tiles_t, st);
+  if (bn == 64) return launch_gemm<WT, 64, 4, SQ64, F16>(mx, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, 4, SQ128, F16>(mx, g, tiles_t, st);
+  return launch_gemm<WT, 256, 3, SQ256, F16>(mx, g, tiles_t, st);
 }
 
 template <bool F16>
@@ -556,6 +600,9 @@ static int dispatch_type(int type, const void* x, const GemmDev& g, cudaStream_t
   }
   return -7;
 }
+
+static unsigned long long* g_trace = nullptr;
+void gemm_set_trace(void* p) { g_trace = reinterpret_cast<unsigned long long*>(p); }
 
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
   if (T <= 0) return 0;
@@ -577,6 +624,12 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
   g.ld_out = ep.ld_out;
   g.k_splits = k_splits;
   g.err = device_err_word();
+  static const int exp_flags = [] {
+    const char* e = getenv("BARQ_GEMM_EXP");
+    return e ? atoi(e) : 0;
+  }();
+  g.exp = exp_flags;
+  g.trace = g_trace;
   return x_is_f16 ? dispatch_type<true>(w.type, x, g, st) : dispatch_type<false>(w.type, x, g, st);
 }
 

@@ -29,6 +29,7 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
 int gemm_error_word(int* host_out);
+void gemm_set_trace(void* p);  // diagnostics (BARQ_GEMM_EXP bit 1): [256 stages][8] u64 stamps of CTA 0
 int gemm_clear_error_word();
 
 // Fused (residual add +) RMSNorm.  x: f32 [T, H] residual stream (updated in place when `add`

@@ -1,0 +1,258 @@
+"""Front-end contract tests on CPU: tokenizer, chat templates, grammar/JSON mode, samplers, the
+OpenAI HTTP API (SSE, aliases, CORS, 429), the UDS protocol and the CLI — all on the CPU engine."""
+import json
+import os
+import socket
+import subprocess
+import sys
+import threading
+import time
+
+import pytest
+import torch
+
+from barq_inference_b200.engine.cpu_engine import CPUEngine
+from barq_inference_b200.engine.sampling_params import SamplingParams
+from barq_inference_b200.models import POLICIES, preset, random_tensors
+from barq_inference_b200.sampling import Grammar, JSON_GBNF, schema_to_gbnf, validate_output
+from barq_inference_b200.sampling.host_samplers import HostSampler, sample_chain, top_k_filter, top_p_filter
+from barq_inference_b200.tokenizer import ChatTemplate, GGUFTokenizer, StreamDecoder, synthetic_tokenizer
+from barq_inference_b200.tokenizer.gguf_tokenizer import bytes_to_unicode
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def tiny_engine():
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=0)
+    eng = CPUEngine(cfg, t, max_model_len=256)
+    eng.tokenizer = synthetic_tokenizer(cfg.vocab)
+    return eng
+
+
+# ------------------------------------------------------------------ tokenizer
+def test_spm_roundtrip_and_bytes():
+    tok = synthetic_tokenizer(2000)
+    for text in ["hello world", "the model is fast", "Zyx 123 ü€", "json: {\"a\": true}"]:
+        ids = tok.encode(text, add_special=False)
+        assert tok.decode(ids) == text
+    ids = tok.encode("hello", add_special=True)
+    assert ids[0] == tok.bos_id
+    # merges prefer the highest-scoring token: "▁hello" exists as one piece
+    assert tok.encode("hello", add_special=False) == [tok.vocab["▁hello"]]
+
+
+def test_bpe_byte_level():
+    b2u = bytes_to_unicode()
+    base = [b2u[b] for b in range(256)]
+    merges = ["h e", "l l", "he ll", "hell o", "Ġ w", "Ġw o", "r l", "Ġwo rl", "Ġworl d"]
+    toks = base + ["he", "ll", "hell", "hello", "Ġw", "Ġwo", "rl", "Ġworl", "Ġworld", "<|end|>"]
+    types = [1] * (len(toks) - 1) + [3]
+    tok = GGUFTokenizer(tokens=toks, token_types=types, merges=merges, model="gpt2", add_bos=False, bos_id=None)
+    ids = tok.encode("hello world<|end|>")
+    assert ids == [toks.index("hello"), toks.index("Ġworld"), toks.index("<|end|>")]
+    assert tok.decode(ids) == "hello world"
+    assert tok.decode(tok.encode("héllo ✓")) == "héllo ✓"
+
+
+def test_stream_decoder_utf8():
+    tok = synthetic_tokenizer(600)
+    ids = tok.encode("€", add_special=False)  # space-prefix piece + byte fallback: 3 byte tokens
+    assert all(i in tok.byte_tokens.values() for i in ids[-3:])
+    d = StreamDecoder(tok)
+    assert [d.push(i) for i in ids][-3:] == ["", "", "€"]
+
+
+def test_chat_templates():
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+    assert ChatTemplate("chatml").render(msgs).endswith("<|im_start|>assistant\n")
+    l2 = ChatTemplate("llama").render(msgs)
+    assert l2.startswith("[INST] <<SYS>>\nbe brief\n<</SYS>>\n\nhi [/INST]")
+    l3 = ChatTemplate("llama3").render(msgs)
+    assert l3.startswith("<|begin_of_text|><|start_header_id|>system<|end_header_id|>\n\nbe brief<|eot_id|>")
+    src = "{% for m in messages %}<{{ m.role }}>{{ m.content }}{% endfor %}{% if add_generation_prompt %}<assistant>{% endif %}"
+    assert ChatTemplate("generic", src).render(msgs) == "<system>be brief<user>hi<assistant>"
+    assert ChatTemplate("generic").render([{"role": "weird", "content": "x"}]).startswith("[USER] x")
+
+
+# ------------------------------------------------------------------ grammar / JSON
+def test_json_grammar_and_schema():
+    g = Grammar(JSON_GBNF)
+    ok = g.accept_text(g.initial(), '{"a": [1, -2.5e3, true, null], "b": {"c": "x\\n"}}')
+    assert Grammar.complete(ok)
+    assert not g.accept_text(g.initial(), '{"a": }')
+    sch = {"type": "object", "properties": {"name": {"type": "string"}, "age": {"type": "integer"},
+                                            "tags": {"type": "array", "items": {"type": "string"}}},
+           "required": ["name", "age"]}
+    gs = Grammar(schema_to_gbnf(sch))
+    assert Grammar.complete(gs.accept_text(gs.initial(), '{"name": "bo", "age": 3}'))
+    assert Grammar.complete(gs.accept_text(gs.initial(), '{"name": "bo", "age": 3, "tags": ["a", "b"]}'))
+    assert not gs.accept_text(gs.initial(), '{"age": 3}')
+    g2 = Grammar('root ::= ("ab" | "c")+ [0-9]? # comment\n')
+    assert Grammar.complete(g2.accept_text(g2.initial(), "abcab7"))
+    assert not g2.accept_text(g2.initial(), "abd")
+
+
+def test_json_mode_generation_is_valid(tiny_engine):
+    p = SamplingParams(max_tokens=60, temperature=1.0, top_k=0, top_p=1.0, json_mode=True, seed=5)
+    r = tiny_engine.generate([[1, 5, 9]], p)[0]
+    text = tiny_engine.tokenizer.decode(r.tokens)
+    if r.finish_reason == "stop":
+        assert validate_output(text), text
+    else:  # cut by max_tokens: must still be a valid JSON prefix
+        g = Grammar(JSON_GBNF)
+        assert g.accept_text(g.initial(), text)
+
+
+# ------------------------------------------------------------------ samplers
+def test_host_samplers():
+    torch.manual_seed(0)
+    lg = torch.randn(100)
+    assert (top_k_filter(lg, 5) > -1e30).sum() == 5
+    kept = top_p_filter(lg, 0.5) > -1e30
+    probs = torch.softmax(lg, 0)
+    assert probs[kept].sum() >= 0.5 and kept.sum() <= (probs.sort(descending=True).values.cumsum(0) < 0.5).sum() + 1
+    g = torch.Generator().manual_seed(0)
+    p = SamplingParams(temperature=0.0)
+    assert sample_chain(lg, p, [], g) == int(lg.argmax())
+    for mir in (1, 2):
+        hs = HostSampler(SamplingParams(temperature=1.0, mirostat=mir, seed=1), 100)
+        toks = [hs.sample(lg) for _ in range(50)]
+        assert all(0 <= t < 100 for t in toks)
+    hs = HostSampler(SamplingParams(temperature=1.0, typical_p=0.5, xtc_probability=1.0, xtc_threshold=0.05, seed=2), 100)
+    assert 0 <= hs.sample(lg) < 100
+    rep = SamplingParams(temperature=0.0, repetition_penalty=100.0)
+    top = int(lg.argmax())
+    assert sample_chain(lg, rep, [top], g) != top
+
+
+# ------------------------------------------------------------------ HTTP API
+@pytest.fixture(scope="module")
+def client(tiny_engine):
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.server.openai_api import OpenAIServer
+
+    srv = OpenAIServer(tiny_engine, tiny_engine.tokenizer, model_id="tiny", chat_template=ChatTemplate("chatml"),
+                       rate_limit_rpm=0)
+    with TestClient(srv.app) as c:
+        c.srv = srv
+        yield c
+    srv.aengine.shutdown()
+
+
+def test_http_routes(client):
+    r = client.get("/")
+    assert r.json()["object"] == "server.info"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    assert client.get("/health").json()["status"] == "ok"
+    r = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 5, "temperature": 0})
+    j = r.json()
+    assert j["object"] == "text_completion" and j["id"].startswith("cmpl-")
+    assert j["usage"]["completion_tokens"] <= 5 and j["choices"][0]["finish_reason"] in ("stop", "length")
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4})
+    j = r.json()
+    assert j["object"] == "chat.completion" and j["choices"][0]["message"]["role"] == "assistant"
+    for body in ({"input": "hey"}, {"prompt": "hey"}, {"messages": [{"role": "user", "content": "x"}]}):
+        j = client.post("/v1/responses", json={**body, "max_output_tokens": 3}).json()
+        assert j["object"] == "response" and j["usage"]["completion_tokens"] <= 3
+    assert client.post("/v1/completions", content=b"{bad json").status_code == 400
+    assert client.post("/v1/chat/completions", json={"messages": []}).status_code == 400
+    assert client.get("/nope").status_code == 404
+    assert client.options("/v1/completions").status_code == 204
+    assert "barq_requests_total" in client.get("/metrics").text
+
+
+def test_http_sse_stream(client):
+    with client.stream("POST", "/v1/chat/completions",
+                       json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 6, "stream": True,
+                             "temperature": 0}) as r:
+        events = [ln[6:] for ln in r.iter_lines() if ln.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    chunks = [json.loads(e) for e in events[:-1]]
+    assert chunks[0]["choices"][0]["delta"] == {"role": "assistant"}
+    assert all(c["object"] == "chat.completion.chunk" for c in chunks)
+    assert chunks[-1]["choices"][0]["finish_reason"] in ("stop", "length")
+    with client.stream("POST", "/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 3, "stream": True}) as r:
+        ev = [ln[6:] for ln in r.iter_lines() if ln.startswith("data: ")]
+    assert json.loads(ev[0])["object"] == "text_completion.chunk" and ev[-1] == "[DONE]"
+
+
+def test_http_json_mode(client):
+    j = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "json"}], "max_tokens": 40,
+                                                  "response_format": {"type": "json_object"}, "temperature": 0.7,
+                                                  "seed": 3}).json()
+    text = j["choices"][0]["message"]["content"]
+    g = Grammar(JSON_GBNF)
+    assert g.accept_text(g.initial(), text)
+
+
+def test_rate_limiter():
+    from barq_inference_b200.server.openai_api import RateLimiter
+
+    rl = RateLimiter(2)
+    assert rl.allow("a", 0.0) and rl.allow("a", 0.0) and not rl.allow("a", 0.0)
+    assert rl.allow("b", 0.0)
+    assert rl.allow("a", 30.5)  # one token refilled after 30 s at 2 rpm
+
+
+def test_http_429(tiny_engine):
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.server.openai_api import OpenAIServer
+
+    srv = OpenAIServer(tiny_engine, tiny_engine.tokenizer, rate_limit_rpm=1)
+    with TestClient(srv.app) as c:
+        assert c.post("/v1/completions", json={"prompt": "a", "max_tokens": 1}).status_code == 200
+        r = c.post("/v1/completions", json={"prompt": "a", "max_tokens": 1})
+        assert r.status_code == 429 and r.json()["error"]["type"] == "rate_limit_error"
+    srv.aengine.shutdown()
+
+
+# ------------------------------------------------------------------ UDS
+def test_uds_protocol(tiny_engine, tmp_path):
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSClient, UDSServer, recv_frame, send_frame
+
+    path = str(tmp_path / "barq.sock")
+    ae = AsyncEngine(tiny_engine)
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        cl = UDSClient(path)
+        frames = list(cl.stream("hello", max_tokens=5, temperature=0.0, rid="r1"))
+        assert frames[-1]["done"] and frames[-1]["tokens_generated"] <= 5
+        assert all(f["id"] == "r1" for f in frames)
+        assert all(not f["done"] for f in frames[:-1])
+        # raw framing: 4-byte big-endian length + JSON
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        s.connect(path)
+        send_frame(s, {"id": "x", "prompt": "hi", "max_tokens": 2, "temperature": 0.5})
+        fr = recv_frame(s)
+        assert set(fr) >= {"id", "text", "tokens_generated", "ttft_ms", "total_time_ms", "done"}
+        s.close()
+        cl.close()
+    finally:
+        srv.stop()
+        ae.shutdown()
+
+
+# ------------------------------------------------------------------ CLI
+def _cli(*args, timeout=300):
+    return subprocess.run([sys.executable, "-m", "barq_inference_b200.cli", *args], cwd=ROOT, capture_output=True,
+                          text=True, timeout=timeout)
+
+
+def test_cli_make_info_run_convert(tmp_path):
+    path = str(tmp_path / "tiny.gguf")
+    r = _cli("make-random-gguf", "--arch", "tiny", "--layers", "1", "--output", path, "--device", "cpu")
+    assert r.returncode == 0, r.stderr
+    info = json.loads(_cli("info", "-m", path).stdout)
+    assert info["architecture"] == "llama" and info["tensor_types"]["Q4_0"] > 0
+    r = _cli("run", "-m", path, "--device", "cpu", "-p", "hello", "--max-tokens", "4", "--temperature", "0")
+    assert r.returncode == 0, r.stderr
+    out = str(tmp_path / "q8.gguf")
+    r = _cli("convert", "--input", path, "--output", out, "--quantize", "q8_0", "--device", "cpu")
+    assert r.returncode == 0, r.stderr
+    assert json.loads(_cli("info", "-m", out).stdout)["tensor_types"].get("Q8_0", 0) > 0
+    assert json.loads(_cli("metal-info").stdout)["metal"] == "unavailable"
