@@ -59,7 +59,7 @@ constexpr int kTraceStages = 256;
 // 3 act issued, 4 MMA saw A, 5 MMA saw B, 6 MMA issued, 7 consumed observed by dequant 0
 BARQ_DEV void trace(const GemmDev& g, int stage, int field) {
   if ((g.exp & 2) && blockIdx.x == 0 && stage < kTraceStages && g.trace)
-    g.trace[stage * 8 + field] = globaltimer_ns();
+    g.trace[stage * 32 + field] = clock64();
 }
 
 // 1-D bulk copy global -> shared, completion on `bar` (transaction bytes).
@@ -186,10 +186,12 @@ BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
   out[1] = make_uint4(r[4], r[5], r[6], r[7]);
 }
 
-template <int WT, int BN, int S, int SQ>
+template <int WT, int BN, int S, int SQ, int KS>
 struct GemmSmem {
-  static constexpr int A_BYTES = 128 * 128;       // 128 rows x 64 fp16/bf16
-  static constexpr int B_BYTES = BN * 128;        // BN rows x 64 fp16/bf16
+  static constexpr int A_ATOM = 128 * 128;        // 128 rows x 64 fp16/bf16 (one 128B-swizzle atom column)
+  static constexpr int B_ATOM = BN * 128;         // BN rows x 64 fp16/bf16
+  static constexpr int A_BYTES = BN <= 128 ? 0 : KS * A_ATOM;  // one stage: KS x 64 columns (TS: in TMEM)
+  static constexpr int B_BYTES = KS * B_ATOM;
   static constexpr int Q_BYTES = TileFmt<WT>::CHUNK;
   static constexpr int XCH_BYTES = 4 * 32 * 32 * 4;  // SwiGLU exchange, one 32x32 f32 tile per quadrant
   static constexpr int OFF_A = 0;
@@ -197,7 +199,7 @@ struct GemmSmem {
   static constexpr int OFF_Q = OFF_B + S * B_BYTES;
   static constexpr int OFF_XCH = OFF_Q + ((SQ * Q_BYTES + 1023) / 1024) * 1024;
   static constexpr int OFF_BAR = OFF_XCH + XCH_BYTES;
-  static constexpr int N_BAR = 2 * SQ + 3 * S + 4;
+  static constexpr int N_BAR = 2 * SQ + 2 * S + 4;
   static constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
   static constexpr int TOTAL = OFF_TMEM + 16 + 1024;  // + alignment slack
 };
@@ -206,8 +208,27 @@ constexpr int kDequantWarps = 16;  // 4 per TMEM lane quadrant; each thread expa
 constexpr int kEpiWarp0 = kDequantWarps;  // 4 epilogue warps, one per lane quadrant
 constexpr int kTmaWarp = kDequantWarps + 4;  // weight chunks (gated only by chunk-slot release)
 constexpr int kActWarp = kDequantWarps + 5;  // activation tiles (gated by MMA progress)
-constexpr int kMmaWarp = kDequantWarps + 6;
-constexpr int kThreads = (kDequantWarps + 7) * 32;
+constexpr int kMmaWarp = kDequantWarps + 6;  // MMA issuers: warps kMmaWarp, kMmaWarp + 1
+constexpr int kThreads = (kDequantWarps + 8) * 32;
+// Two MMA-issuing threads alternate the stages of a tile, each accumulating into its own TMEM
+// buffer.  One issuing thread stalls on every tcgen05.mma while the tensor queue is full and then
+// pays its per-stage barrier round (commit + wait, a few hundred cycles) with the tensor pipe idle;
+// with two, one thread's barrier round overlaps the other's queued MMAs, which keeps M=128 x N<=128
+// MMAs near their 64-cycle issue rate.  Wide token tiles (BN = 256) keep one issuer: their MMAs
+// already take 128 cycles each and the TMEM budget (512 columns) holds only two 256-column buffers.
+//
+// Token tiles of up to 128 columns take the weight operand from TMEM ("TS" MMA): dequant warps store
+// the expanded weights with tcgen05.st into their own lane quadrant, so the operand never touches
+// shared memory (no 32 KB/stage of st.shared, no async-proxy fence, no smem reads by the MMA), and
+// the shared memory it frees deepens the activation and weight-chunk rings.  TMEM budget (512
+// columns): accumulators 2 buffers x NI issuers x BN, then S stages x KS x 32 columns of operand.
+template <int BN>
+struct Issuers {
+  static constexpr int NI = BN <= 64 ? 2 : 1;
+  static constexpr bool TS = BN <= 128;
+  static constexpr int ACOL = 2 * NI * BN;            // first TMEM column of the operand stages
+  static constexpr int COLS = TS ? 512 : 2 * NI * BN;
+};
 
 struct TileMap {
   int n_tiles, t_tiles, ks, total;
@@ -219,21 +240,24 @@ struct TileMap {
   }
 };
 
-template <int WT, int BN, int S, int SQ, bool F16>
+template <int WT, int BN, int S, int SQ, int KS, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tx, GemmDev g) {
-  using L = GemmSmem<WT, BN, S, SQ>;
+  using L = GemmSmem<WT, BN, S, SQ, KS>;
   using F = TileFmt<WT>;
-  constexpr int SPG = F::G / 64;  // 64-column stages per weight chunk
+  static_assert(F::G % (64 * KS) == 0, "a stage never straddles two weight chunks");
+  constexpr int SPG = F::G / (64 * KS);  // stages per weight chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* fullQ = bars;                // [SQ] chunk landed
   uint64_t* emptyQ = bars + SQ;          // [SQ] chunk fully expanded
-  uint64_t* fullB = bars + 2 * SQ;       // [S]  activation tile landed
-  uint64_t* fullA = bars + 2 * SQ + S;   // [S]  weight operand written
-  uint64_t* consumed = bars + 2 * SQ + 2 * S;  // [S] MMAs of the stage done
-  uint64_t* accFull = bars + 2 * SQ + 3 * S;   // [2]
+  // full[s]: the stage's weight operand is written (one arrival per dequant warp) AND its activation
+  // tile has landed (the producer's arrive.expect_tx + the TMA transaction bytes) -- one barrier, so
+  // the MMA thread pays a single wait per stage
+  uint64_t* full = bars + 2 * SQ;              // [S]
+  uint64_t* consumed = bars + 2 * SQ + S;      // [S] MMAs of the stage done
+  uint64_t* accFull = bars + 2 * SQ + 2 * S;   // [2]
   uint64_t* accEmpty = accFull + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
   __shared__ int err_s;
@@ -257,17 +281,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&emptyQ[i], kDequantWarps);
     }
     for (int i = 0; i < S; ++i) {
-      mbar_init(&fullB[i], 1);
-      mbar_init(&fullA[i], kDequantWarps);
+      mbar_init(&full[i], kDequantWarps + 1);
       mbar_init(&consumed[i], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&accFull[b], 1);
+      mbar_init(&accFull[b], Issuers<BN>::NI);
       mbar_init(&accEmpty[b], 4);
     }
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) tmem_alloc(tmem_slot, 2 * BN);
+  constexpr int NI = Issuers<BN>::NI;
+  constexpr bool TS = Issuers<BN>::TS;
+  static_assert(!TS || Issuers<BN>::ACOL + S * KS * 32 <= 512, "TMEM budget");
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, Issuers<BN>::COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -314,15 +340,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&fullB[s], L::B_BYTES);
           trace(g, it, 3);
-          tma_load_2d(smem + L::OFF_B + s * L::B_BYTES, &tx, 64 * ks, tt * BN, &fullB[s]);
+          if (g.exp & 8) {  // diagnostics: no activation copy (operand stale), barrier protocol unchanged
+            mbar_arrive(&full[s]);
+          } else {
+            mbar_expect_tx(&full[s], L::B_BYTES);
+#pragma unroll
+            for (int a = 0; a < KS; ++a)
+              tma_load_2d(smem + L::OFF_B + s * L::B_BYTES + a * L::B_ATOM, &tx, 64 * (ks * KS + a), tt * BN, &full[s]);
+          }
         }
         if (!ok) break;
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp >= kMmaWarp && warp < kMmaWarp + NI) {
+    // ---------------------------------------------------------------- MMA issuers
+    // Issuer m takes the stages i of each tile with i % NI == m, accumulating into TMEM columns
+    // [(buf * NI + m) * BN, +BN).  It walks every stage to keep the ring index and phase in step.
+    const int me = warp - kMmaWarp;
     if (lane == 0) {
       constexpr uint32_t idesc = F16 ? idesc_f16(128, BN) : idesc_bf16(128, BN);
       int it = 0, tc = 0;
@@ -331,34 +366,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         tm.decode(u, nt, tt, z);
         grange(z, gb, ge);
         const int buf = tc & 1, use = tc >> 1;
+        const int nst = (ge - gb) * SPG;
         if (tc >= 2 && !mbar_wait(&accEmpty[buf], (use - 1) & 1, err, 8)) break;
         tc_fence_after();
-        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        const uint32_t acc = tmem + (uint32_t)((buf * NI + me) * BN);
         bool ok = true;
-        const int nst = (ge - gb) * SPG;
         for (int i = 0; i < nst; ++i, ++it) {
+          if (i % NI != me) continue;
           const int s = it % S, ph = (it / S) & 1;
-          if (!mbar_wait(&fullA[s], ph, err, 3)) {
+          trace(g, it, 0);
+          if (!mbar_wait(&full[s], ph, err, 3)) {
             ok = false;
             break;
           }
           trace(g, it, 4);
-          if (!mbar_wait(&fullB[s], ph, err, 4)) {
-            ok = false;
-            break;
-          }
-          trace(g, it, 5);
           tc_fence_after();
-          const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
           const uint32_t b0 = smem_addr(smem + L::OFF_B + s * L::B_BYTES);
+          if constexpr (TS) {
+            const uint32_t ta = tmem + (uint32_t)(Issuers<BN>::ACOL + s * KS * 32);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
+            for (int a = 0; a < KS; ++a)
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma_f16_ts(acc, ta + (uint32_t)(a * 32 + k * 8), umma_desc_sw128(b0 + a * L::B_ATOM + 32 * k), idesc,
+                           (i >= NI) | a | k);
+          } else {
+            const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
+#pragma unroll
+            for (int a = 0; a < KS; ++a)
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma_bf16(acc, umma_desc_sw128(a0 + a * L::A_ATOM + 32 * k),
+                         umma_desc_sw128(b0 + a * L::B_ATOM + 32 * k), idesc, (i >= NI) | a | k);
+          }
+          trace(g, it, 1);
           mma_commit(&consumed[s]);
           trace(g, it, 6);
         }
         if (!ok) break;
-        mma_commit(&accFull[buf]);
+        mma_commit(&accFull[buf]);  // every issuer arrives, also one that had no stage in this tile
       }
     }
   } else if (warp < kDequantWarps) {
@@ -377,35 +423,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (warp == 0 && lane == 0) trace(g, qc * SPG, 1);
+
         const uint8_t* ch = smem + L::OFF_Q + qs * L::Q_BYTES;
         for (int sub = 0; sub < SPG; ++sub, ++it) {
           const int s = it % S, ph = (it / S) & 1;
-          uint4 ops[2];
-          if (g.exp & 1) {
-            ops[0] = ops[1] = make_uint4(0, 0, 0, 0);
-          } else {
-            const Codes cd = load_codes<WT>(ch, r, qq, sub);
-            codes_to_operands<F16>(cd, ops);
+          uint4 ops[KS][2];
+#pragma unroll
+          for (int a = 0; a < KS; ++a) {
+            if (g.exp & 1) {
+              ops[a][0] = ops[a][1] = make_uint4(0, 0, 0, 0);
+            } else {
+              const Codes cd = load_codes<WT>(ch, r, qq, sub * KS + a);
+              codes_to_operands<F16>(cd, ops[a]);
+            }
           }
           if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
             ok = false;
             break;
           }
           if (warp == 0 && lane == 0) trace(g, it, 7);
-          uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + r * 128;
-          *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[0];
-          *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[1];
-          fence_proxy_async();
+          if constexpr (TS) {
+            const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(Issuers<BN>::ACOL + s * KS * 32 + qq * 8);
+#pragma unroll
+            for (int a = 0; a < KS; ++a) tmem_st8(ta + (uint32_t)(a * 32), ops[a][0], ops[a][1]);
+            tmem_wait_st();
+            tc_fence_before();
+          } else {
+#pragma unroll
+            for (int a = 0; a < KS; ++a) {
+              uint8_t* arow = smem + L::OFF_A + s * L::A_BYTES + a * L::A_ATOM + r * 128;
+              *reinterpret_cast<uint4*>(arow + (((2 * qq) ^ (r & 7)) << 4)) = ops[a][0];
+              *reinterpret_cast<uint4*>(arow + (((2 * qq + 1) ^ (r & 7)) << 4)) = ops[a][1];
+            }
+            fence_proxy_async();
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&fullA[s]);
+          if (lane == 0) mbar_arrive(&full[s]);
           if (warp == 0 && lane == 0) trace(g, it, 2);
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(&emptyQ[qs]);
       }
     }
-  } else {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ---------------------------------------------------------------- epilogue (4 warps)
     const int quad = warp - kEpiWarp0;
     const int r = quad * 32 + lane;
@@ -415,8 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool atomic = g.k_splits > 1;
     int tc = 0;
     for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
-      int nt, tt, z;
+      int nt, tt, z, gb, ge;
       tm.decode(u, nt, tt, z);
+      grange(z, gb, ge);
+      const int nacc = (ge - gb) * SPG < NI ? (ge - gb) * SPG : NI;  // issuers that wrote this tile
       const int buf = tc & 1, use = tc >> 1;
       mbar_wait(&accFull[buf], use & 1, err, 7);
       tc_fence_after();
@@ -424,10 +486,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (*err) break;
       const int n0 = nt * 128, t0 = tt * BN, n = n0 + r;
-      const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(quad * 32) << 16);
+      const uint32_t acc = tmem + (uint32_t)(buf * NI * BN) + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(acc + (uint32_t)c0, v);
+        for (int m = 1; m < nacc; ++m) {
+          float w[32];
+          tmem_ld32(acc + (uint32_t)(m * BN + c0), w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += w[j];
+        }
         if (g.mode == EPI_SWIGLU_Q8) {
           // rows [32 gate | 32 up] x 2 groups: quadrants 0,2 hold gate rows, 1,3 the matching up rows
           float* mine = xch + quad * 32 * 32;
@@ -476,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, Issuers<BN>::COLS);
   }
   if (threadIdx.x == 0 && err_s && g.err) atomicExch(g.err, err_s);
 }
@@ -546,11 +614,11 @@ static int sm_count() {
   return n;
 }
 
-template <int WT, int BN, int S, int SQ, bool F16>
+template <int WT, int BN, int S, int SQ, int KS, bool F16>
 static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cudaStream_t st) {
-  using L = GemmSmem<WT, BN, S, SQ>;
+  using L = GemmSmem<WT, BN, S, SQ, KS>;
   static_assert(L::TOTAL <= 232448, "shared memory budget");
-  auto kern = qgemm_tc_kernel<WT, BN, S, SQ, F16>;
+  auto kern = qgemm_tc_kernel<WT, BN, S, SQ, KS, F16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   const int total = ((g.N + 127) / 128) * tiles_t * g.k_splits;
   const int n = sm_count();
@@ -558,13 +626,22 @@ static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cud
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
 }
 
+// Weight-chunk ring depth: as many chunks in flight as the shared memory left after the operand
+// rings allows (capped at 8), so each SM keeps tens of KB of weight loads outstanding.
+template <int WT, int BN, int S, int KS>
+constexpr int chunk_slots() {
+  using L = GemmSmem<WT, BN, S, 1, KS>;
+  constexpr int fixed = L::OFF_Q + L::XCH_BYTES + (2 + 2 * S + 4) * 8 + 16 + 1024 + 1024;
+  constexpr int n = (232448 - fixed) / L::Q_BYTES;
+  return n > 8 ? 8 : n;
+}
+
 template <int WT, bool F16>
 static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   using F = TileFmt<WT>;
-  // weight chunks in flight per SM: keep >= ~64 KB of loads outstanding to cover DRAM latency
-  constexpr int SQ64 = F::CHUNK > 24000 ? 3 : (F::CHUNK > 12000 ? 4 : 8);
-  constexpr int SQ128 = F::CHUNK > 24000 ? 2 : (F::CHUNK > 12000 ? 3 : 6);
-  constexpr int SQ256 = F::CHUNK > 12000 ? 2 : 4;
+  // K-quant chunks are 256 columns wide: small token tiles take two 64-column atoms per stage, so
+  // the MMA thread issues 8 MMAs per barrier round instead of 4
+  constexpr int KSW = F::G >= 128 ? 2 : 1;
   GemmDev g = g0;
   const int bn = g.T <= 64 ? 64 : (g.T <= 128 ? 128 : 256);
   CUtensorMap mx;
@@ -583,9 +660,11 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
     if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)g.N * 4, g.T, st) != cudaSuccess) return -6;
   }
-  if (bn == 64) return launch_gemm<WT, 64, 4, SQ64, F16>(mx, g, tiles_t, st);
-  if (bn == 128) return launch_gemm<WT, 128, 4, SQ128, F16>(mx, g, tiles_t, st);
-  return launch_gemm<WT, 256, 3, SQ256, F16>(mx, g, tiles_t, st);
+  // TS tiles: the operand stages fill the TMEM columns left after the accumulators (256 of 512)
+  constexpr int S_TS = 256 / (KSW * 32);
+  if (bn == 64) return launch_gemm<WT, 64, S_TS, chunk_slots<WT, 64, S_TS, KSW>(), KSW, F16>(mx, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, S_TS, chunk_slots<WT, 128, S_TS, KSW>(), KSW, F16>(mx, g, tiles_t, st);
+  return launch_gemm<WT, 256, 3, chunk_slots<WT, 256, 3, 1>(), 1, F16>(mx, g, tiles_t, st);
 }
 
 template <bool F16>

@@ -45,7 +45,19 @@ BARQ_DEV uint64_t globaltimer_ns() {
 // an error, or ~2 s of %globaltimer elapsed; on expiry the error word is set (0x100 | call site)
 // and false is returned so every role can unwind and the kernel returns normally.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+BARQ_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 BARQ_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* err, int site) {
+  if (mbar_test_wait(bar, parity)) return true;  // non-blocking probe: cheaper when already complete
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
@@ -90,6 +102,23 @@ BARQ_DEV void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A's 128 rows are TMEM lanes, its K elements
+// packed two per 32-bit column (even k in the low half).
+BARQ_DEV void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// 32 lanes x 8 consecutive 32-bit columns from registers into TMEM (warp w: lanes 32*(w%4) .. +31).
+BARQ_DEV void tmem_st8(uint32_t taddr, uint4 lo, uint4 hi) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(lo.x),
+               "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+BARQ_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
 BARQ_DEV void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
