@@ -186,6 +186,74 @@ BARQ_DEV void codes_to_operands(const Codes& c, uint4* out) {
   out[1] = make_uint4(r[4], r[5], r[6], r[7]);
 }
 
+// One 32-weight sub-block (row r; 64-column atom sub64 of the staged chunk; its first or second 32
+// columns by h) -> four 16-byte groups of operand pairs.  Q4_K / Q5_K share one (scale, min) over
+// the sub-block, decoded once; other formats expand two 16-weight halves.
+template <int WT, bool F16>
+BARQ_DEV void dequant32(const uint8_t* ch, int r, int sub64, int h, uint4* out) {
+  if constexpr ((WT == W_Q4_K || WT == W_Q5_K) && F16) {
+    // fp16-native scale: (1024 + scl, 1024) - (1024, 1024 + mn) = (scl, -mn) exactly, times the
+    // (d, dmin) pair -> (d*scl, -dmin*mn), each product rounded once, as a float product rounded to
+    // fp16 would be; no int/float conversion instructions.
+    constexpr int HP = WT == W_Q5_K ? 2 : 1;
+    const uint4 hd = *reinterpret_cast<const uint4*>(staged_chunk<WT, HP>(ch, r, 0));
+    int scl, mn;
+    kscale(hd.y, hd.z, hd.w, 2 * sub64 + h, scl, mn);
+    uint32_t ua = 0x64006400u | (uint32_t)scl, ub = 0x64006400u | ((uint32_t)mn << 16);
+    const __half2 t = __hsub2(*reinterpret_cast<__half2*>(&ua), *reinterpret_cast<__half2*>(&ub));
+    uint32_t dd = hd.x;
+    const __half2 sb = __hmul2(*reinterpret_cast<__half2*>(&dd), t);
+    const __half2 sc2 = __low2half2(sb), bi2 = __high2half2(sb);
+    const __half2 off = __float2half2_rn(1024.f);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t w[4];
+      words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, 2 * sub64 + half)), w);
+      uint32_t hb[4] = {0, 0, 0, 0};
+      if constexpr (WT == W_Q5_K) words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 1>(ch, r, half)), hb);
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t v = (h ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
+        if constexpr (WT == W_Q5_K) v |= ((hb[i] >> (2 * sub64 + h)) & 0x01010101u) << 4;
+        uint32_t p0 = __byte_perm(v, 0x64646464u, 0x4140), p1 = __byte_perm(v, 0x64646464u, 0x4342);
+        __half2 h0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p0), off), sc2, bi2);
+        __half2 h1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&p1), off), sc2, bi2);
+        o[2 * i] = *reinterpret_cast<uint32_t*>(&h0);
+        o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h1);
+      }
+      out[2 * half] = make_uint4(o[0], o[1], o[2], o[3]);
+      out[2 * half + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  } else if constexpr (WT == W_Q4_K || WT == W_Q5_K) {
+    constexpr int HP = WT == W_Q5_K ? 2 : 1;
+    const uint4 hd = *reinterpret_cast<const uint4*>(staged_chunk<WT, HP>(ch, r, 0));
+    int scl, mn;
+    kscale(hd.y, hd.z, hd.w, 2 * sub64 + h, scl, mn);
+    Codes c;
+    c.sc = h2f(hd.x & 0xFFFF) * (float)scl;
+    c.bi = -h2f(hd.x >> 16) * (float)mn;
+    c.zp = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t w[4];
+      words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 0>(ch, r, 2 * sub64 + half)), w);
+      uint32_t hb[4] = {0, 0, 0, 0};
+      if constexpr (WT == W_Q5_K) words(*reinterpret_cast<const uint4*>(staged_chunk<WT, 1>(ch, r, half)), hb);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t v = (h ? (w[i] >> 4) : w[i]) & 0x0F0F0F0Fu;
+        if constexpr (WT == W_Q5_K) v |= ((hb[i] >> (2 * sub64 + h)) & 0x01010101u) << 4;
+        c.u[i] = v;
+      }
+      codes_to_operands<F16>(c, out + 2 * half);
+    }
+  } else {
+    codes_to_operands<F16>(load_codes<WT>(ch, r, 2 * h, sub64), out);
+    codes_to_operands<F16>(load_codes<WT>(ch, r, 2 * h + 1, sub64), out + 2);
+  }
+}
+
 template <int WT, int BN, int S, int SQ, int KS>
 struct GemmSmem {
   static constexpr int A_ATOM = 128 * 128;        // 128 rows x 64 fp16/bf16 (one 128B-swizzle atom column)
@@ -425,6 +493,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         const uint8_t* ch = smem + L::OFF_Q + qs * L::Q_BYTES;
+        if constexpr (TS && KS == 2) {
+          // 128-column stages: warp (quad, sb) expands rows quad*32 + lane, stage columns [32 sb, +32)
+#pragma unroll
+          for (int sub = 0; sub < SPG; ++sub, ++it) {
+            const int s = it % S, ph = (it / S) & 1;
+            uint4 ops[4];
+            if (g.exp & 1) {
+              ops[0] = ops[1] = ops[2] = ops[3] = make_uint4(0, 0, 0, 0);
+            } else {
+              dequant32<WT, F16>(ch, r, 2 * sub + (qq >> 1), qq & 1, ops);
+            }
+            if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 6)) {
+              ok = false;
+              break;
+            }
+            if (warp == 0 && lane == 0) trace(g, it, 7);
+            tmem_st16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(Issuers<BN>::ACOL + s * 64 + qq * 16), ops);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
+            if (warp == 0 && lane == 0) trace(g, it, 2);
+          }
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(&emptyQ[qs]);
+        } else {
         for (int sub = 0; sub < SPG; ++sub, ++it) {
           const int s = it % S, ph = (it / S) & 1;
           uint4 ops[KS][2];
@@ -463,6 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(&emptyQ[qs]);
+        }
       }
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {

@@ -117,6 +117,14 @@ BARQ_DEV void tmem_st8(uint32_t taddr, uint4 lo, uint4 hi) {
                "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
                : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns from registers into TMEM.
+BARQ_DEV void tmem_st16(uint32_t taddr, const uint4* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z), "r"(v[1].w),
+      "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z), "r"(v[3].w)
+      : "memory");
+}
 BARQ_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
