@@ -6,6 +6,7 @@ missing or stale extension is an error (``require_ext``): there is no silent PyT
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -96,17 +97,41 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, add: torch.Tensor | No
     return ob, oq
 
 
+# Streaming GEMV workspace, one per device: f32 [8, WS_ROWS] partial sums and int [WS_ROWS/128]
+# tile counters, zero between calls (the kernel clears what it used).  Allocated on first use --
+# before any CUDA-graph capture, since the engine runs eager steps first.
+WS_ROWS = 1 << 18
+_GEMV_WS: dict = {}
+GEMV_STREAM = os.environ.get("BARQ_GEMV_STREAM", "1") != "0"
+
+
+def _gemv_ws(w: QWeight):
+    if not GEMV_STREAM or w.wtype == W_BF16 or w.N > WS_ROWS:
+        return None, None
+    key = w.device
+    ws = _GEMV_WS.get(key)
+    if ws is None:
+        ws = (torch.zeros(8 * WS_ROWS, dtype=torch.float32, device=w.device),
+              torch.zeros(WS_ROWS // 128, dtype=torch.int32, device=w.device))
+        _GEMV_WS[key] = ws
+    return ws
+
+
 def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
          xb: torch.Tensor | None = None, bias: torch.Tensor | None = None, out_q: Q8Act | None = None,
          x2: bool = False):
-    """Decode GEMV for T <= 8 tokens.  Returns ``out`` (allocated if None for store modes)."""
+    """Decode GEMV for T <= 8 tokens.  Returns ``out`` (allocated if None for store modes).
+
+    Quantized weights go through the streaming kernel (persistent, bulk-copy fed, stream-K);
+    dense bf16 weights through the warp-per-row kernel."""
     C = require_ext()
     dev = w.device
+    wa, wc = _gemv_ws(w)
     if mode == EPI_SWIGLU_Q8:
         F = w.N // 2
         if out_q is None:
             out_q = Q8Act.empty(T, F, dev, x2)
-        C.qgemv(*w.args(), *_ins(x), xb, T, mode, None, out, *out_q.outs(), bias, F)
+        C.qgemv(*w.args(), *_ins(x), xb, T, mode, None, out, *out_q.outs(), bias, F, wa, wc)
         _count()
         return out_q
     if out is None:
@@ -115,7 +140,7 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
     ld = out.stride(0)
     f32 = out if out.dtype == torch.float32 else None
     bf = out if out.dtype == torch.bfloat16 else None
-    C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld)
+    C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld, wa, wc)
     _count()
     return out
 

@@ -81,10 +81,11 @@ BARQ_DEV void quant_lane32x2(float v, int8_t& q, int8_t& ql, float& d_out, float
   float d = amax / 127.0f;
   float id = d > 0.f ? 1.0f / d : 0.f;
   int qi = max(-127, min(127, __float2int_rn(v * id)));
+  // The residual (|r| <= d/2) is quantized with the fixed step d/256, so q*256 + ql is a 16-bit code
+  // of v with step d/256: consumers may fold both terms into one integer dot product.
   float r = v - d * (float)qi;
-  float rmax = warp_max(fabsf(r));
-  float dl = rmax / 127.0f;
-  float idl = dl > 0.f ? 1.0f / dl : 0.f;
+  float dl = d * (1.0f / 256.0f);
+  float idl = id * 256.0f;
   int qli = max(-127, min(127, __float2int_rn(r * idl)));
   int sq = warp_sum_int(qi), sql = warp_sum_int(qli);
   q = (int8_t)qi;

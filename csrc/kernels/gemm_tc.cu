@@ -687,6 +687,8 @@ static int* device_err_word() {
   return p;
 }
 
+int* kernel_err_word() { return device_err_word(); }
+
 int gemm_error_word(int* host_out) {
   int* p = device_err_word();
   if (!p) return -1;

@@ -1,0 +1,336 @@
+// K1b: streaming quantized GEMV for decode (1..8 tokens): persistent, bulk-copy fed, stream-K.
+//
+// The reference's decode matmul is a host round trip (backend/src/cuda_quant.rs:104-126); this is
+// the B200 path for the same y = W x with W in GGUF blocks and x as int8 (ActQ8).
+//
+// Why a second GEMV: with K = 4096 a warp-per-row GEMV gives each lane only a few dependent DRAM
+// round trips, so it is latency-bound (~1.5 TB/s).  Here one CTA per SM walks a contiguous range of
+// weight chunks (the tiled layout makes "128 rows x G columns" one contiguous chunk, and a range of
+// chunks one contiguous span of memory):
+//   warp 8 (one thread)  cp.async.bulk of whole chunks into an S-deep shared-memory ring
+//                        (~180 KB in flight per SM, enough to cover DRAM latency at full rate);
+//   warps 0-7            dp4a against the int8 activations: warp w takes rows 32*(w/2) + lane and
+//                        half w%2 of each chunk row (warp-uniform, so no divergence); the two
+//                        halves of a row meet in shared memory once per row tile.
+// Work units are (row tile, K chunk) pairs split evenly over the CTAs ("stream-K"), so every SM
+// streams the same number of bytes.  A row tile finished by one CTA is written directly; a tile
+// shared by two CTAs is combined in an f32 workspace: each adds its partial sums (atomics in L2),
+// the last to arrive (per-tile counter) applies the epilogue and clears the workspace rows and the
+// counter again, so the next call (or CUDA-graph replay) finds them zero.
+// Epilogues: STORE_F32, ADD_F32 (partials go straight to the output with atomics), STORE_BF16,
+// SWIGLU_Q8 (rows interleaved [32 gate | 32 up]; writes silu(g)*u as int8 activations).
+// Every mbarrier wait is bounded; on expiry the CTA records an error word and unwinds.
+#include <cstdlib>
+
+#include "gemv_traits.cuh"
+#include "launch.h"
+#include "tc_common.cuh"
+
+namespace barq {
+
+using namespace tc;
+
+namespace {
+
+constexpr int kRingBytes = 184 * 1024;
+
+// Compute warps per CTA: 16 (each row split over 4 warps) for 1-2 tokens, where latency hiding
+// matters most and registers allow it; 8 (rows split over 2 warps) otherwise and for formats
+// with 64-column chunks (two 32-weight parts per chunk row).
+template <int WT, int BS>
+struct StreamCfg {
+  static constexpr int NP = TileFmt<WT>::G / 32;
+  static constexpr int TPR = (BS <= 2 && NP >= 8) ? 4 : 2;  // warps per row group
+  static constexpr int NW = 4 * TPR;                        // compute warps: 4 row groups of 32
+  static constexpr int THREADS = (NW + 1) * 32;
+};
+
+BARQ_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+template <int NW>
+BARQ_DEV void compute_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
+}
+
+struct StreamWs {
+  float* acc;  // [8, N] f32 partial sums of shared row tiles (zero between calls)
+  int* cnt;    // [N / 128] units accumulated per row tile (zero between calls)
+  int* err;
+  int exp;  // diagnostics: bit 0 = compute warps skip the arithmetic (still wait for and release chunks)
+};
+
+}  // namespace
+
+template <class T, int WT, int BS, bool X2>
+__global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
+    qgemv_stream_kernel(QW w, ActQ8 x, int B, GemvEpi ep, StreamWs ws) {
+  using F = TileFmt<WT>;
+  using Cfg = StreamCfg<WT, BS>;
+  constexpr int CH = F::CHUNK;
+  constexpr int S = kRingBytes / CH > 32 ? 32 : kRingBytes / CH;
+  constexpr int NP = Cfg::NP;     // 32-weight parts per chunk row
+  constexpr int TPR = Cfg::TPR;   // warps sharing a row group
+  constexpr int NW = Cfg::NW;
+  constexpr int PPT = NP / TPR;   // parts per thread
+  static_assert(NP % TPR == 0, "whole parts per thread");
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[S], empty[S];
+  __shared__ float red[128][BS];
+  __shared__ float comb[TPR - 1][128][BS];
+  __shared__ int last_s;
+  __shared__ int err_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KG = w.K / F::G;
+  const int tiles = (w.N + 127) / 128;
+  const int U = tiles * KG;  // < 2^31 for any weight this library loads
+  const int u0 = (int)((long long)U * blockIdx.x / gridDim.x), u1 = (int)((long long)U * (blockIdx.x + 1) / gridDim.x);
+  const int n_units = u1 - u0;
+  const int nparts = w.K >> 5;
+  if (threadIdx.x == 0) {
+    err_s = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* err = &err_s;
+
+  if (warp == NW) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint8_t* src = w.p0 + (size_t)u0 * CH;
+      int issued = 0, s = 0;
+      uint32_t ph = 0;
+      for (int i = 0; i < n_units; ++i) {
+        if (i >= S && !mbar_wait(&empty[s], ph ^ 1, err, 1)) break;
+        mbar_expect_tx(&full[s], CH);
+        bulk_copy(smem + s * CH, src, CH, &full[s]);
+        src += CH;
+        issued = i + 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      // Before the CTA may exit, every copy issued must have landed (normally the compute warps
+      // already saw each one; after an error this waits, bounded, for the ones in flight).
+      for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+        mbar_wait_bounded(&full[i % S], (uint32_t)((i / S) & 1));
+    }
+  } else {
+    // ------------------------------------------------------------------ compute
+    const int half = warp % TPR, r = (warp / TPR) * 32 + lane;  // half: this warp's slice of the row
+    const int tid = threadIdx.x;
+    float acc[BS];
+#pragma unroll
+    for (int b = 0; b < BS; ++b) acc[b] = 0.f;
+    int tile_first = u0;  // first unit of the current tile inside this CTA's range
+    int tile = u0 / KG, kg = u0 - (u0 / KG) * KG, s = 0;
+    uint32_t ph = 0;
+    for (int i = 0; i < n_units; ++i, ++kg) {
+      if (kg == KG) {
+        kg = 0;
+        ++tile;
+      }
+      if (i > 0 && ++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+      const int u = u0 + i;
+      // On an error the loop keeps running (without waiting) so that every compute warp still
+      // reaches each named barrier below; the results are discarded by the host.
+      const bool have = !*err && mbar_wait(&full[s], ph, err, 2);
+      const uint8_t* ch = smem + s * CH;
+      const int row = tile * 128 + r;
+      if (have && !(ws.exp & 1)) {
+        if constexpr (WT == W_Q4_K || WT == W_Q5_K || WT == W_Q6_K) {
+          switch (half) {
+            case 0: T::template chunk_dot<0 * PPT, PPT, BS, X2>(ch, r, kg, x, w.K, nparts, B, acc); break;
+            case 1: T::template chunk_dot<1 * PPT, PPT, BS, X2>(ch, r, kg, x, w.K, nparts, B, acc); break;
+            case 2: T::template chunk_dot<(TPR > 2 ? 2 : 0) * PPT, PPT, BS, X2>(ch, r, kg, x, w.K, nparts, B, acc); break;
+            default: T::template chunk_dot<(TPR > 2 ? 3 : 0) * PPT, PPT, BS, X2>(ch, r, kg, x, w.K, nparts, B, acc); break;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < PPT; ++j) {
+            const int q = half * PPT + j;
+            const typename T::W wq = T::load_s(ch, r, q);
+            const int p = kg * NP + q;
+#pragma unroll
+            for (int b = 0; b < BS; ++b) {
+              if (b < B) {
+                acc[b] += T::dot(wq, T::load_x(x.q + (size_t)b * w.K, x.s + (size_t)b * nparts, p), q);
+                if (X2) acc[b] += T::dot(wq, T::load_x(x.ql + (size_t)b * w.K, x.dl + (size_t)b * nparts, p), q);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (kg != KG - 1 && i != n_units - 1) continue;
+
+      // ---- tile done (or this CTA's range ends inside it)
+      if (half) {
+#pragma unroll
+        for (int b = 0; b < BS; ++b) comb[half - 1][r][b] = acc[b];
+      }
+      compute_sync<NW>();
+      if (!half) {
+#pragma unroll
+        for (int t = 0; t < TPR - 1; ++t)
+#pragma unroll
+          for (int b = 0; b < BS; ++b) acc[b] += comb[t][r][b];
+      }
+      const int tu0 = tile * KG;
+      const bool whole = tile_first == tu0 && u == tu0 + KG - 1;
+      const int covered = (int)(u - tile_first + 1);
+      const bool has_k0 = tile_first == tu0;
+      tile_first = u + 1;
+      const bool valid = row < w.N;
+      bool emit = whole;
+      if (!whole) {
+        if (ep.mode == EPI_ADD_F32) {
+          if (half == 0 && valid)
+#pragma unroll
+            for (int b = 0; b < BS; ++b) {
+              if (b >= B) break;
+              float v = acc[b] + ((has_k0 && ep.bias) ? ep.bias[row] : 0.f);
+              atomicAdd(ep.out_f32 + (size_t)b * ep.ld_out + row, v);
+            }
+        } else {
+          if (half == 0 && valid)
+#pragma unroll
+            for (int b = 0; b < BS; ++b)
+              if (b < B) atomicAdd(ws.acc + (size_t)b * w.N + row, acc[b]);
+          __threadfence();
+          compute_sync<NW>();
+          if (tid == 0) last_s = atomicAdd(ws.cnt + tile, covered) + covered == KG;
+          compute_sync<NW>();
+          emit = last_s != 0;
+          if (emit) {
+            __threadfence();
+            if (half == 0 && valid)
+#pragma unroll
+              for (int b = 0; b < BS; ++b) {
+                if (b >= B) break;
+                float* pw = ws.acc + (size_t)b * w.N + row;
+                acc[b] = __ldcg(pw);
+                *pw = 0.f;
+              }
+            if (tid == 0) ws.cnt[tile] = 0;
+          }
+        }
+      }
+      if (emit) {
+        if (ep.mode == EPI_SWIGLU_Q8) {
+          if (half == 0)
+#pragma unroll
+            for (int b = 0; b < BS; ++b) red[r][b] = acc[b];
+          compute_sync<NW>();
+          if (warp < 2) {  // group `warp`: gate rows 64*warp + [0,32), up rows 64*warp + 32 + [0,32)
+            const int n_out = w.N / 2;
+            const int o = tile * 64 + warp * 32 + lane;
+            for (int b = 0; b < B; ++b) {
+              const float g = red[warp * 64 + lane][b], up = red[warp * 64 + 32 + lane][b];
+              const float h = silu(g) * up;
+              act_store32(ep.out_q, h, (size_t)b * n_out + o, (size_t)b * (n_out / 32) + tile * 2 + warp, lane);
+              if (ep.out_bf16) ep.out_bf16[(size_t)b * ep.ld_out + o] = __float2bfloat16(h);
+            }
+          }
+          compute_sync<NW>();
+        } else if (half == 0 && valid) {
+#pragma unroll
+          for (int b = 0; b < BS; ++b) {
+            if (b >= B) break;
+            float v = acc[b] + (ep.bias ? ep.bias[row] : 0.f);
+            const size_t idx = (size_t)b * ep.ld_out + row;
+            if (ep.mode == EPI_ADD_F32)
+              ep.out_f32[idx] += v;
+            else if (ep.mode == EPI_STORE_F32)
+              ep.out_f32[idx] = v;
+            else
+              ep.out_bf16[idx] = __float2bfloat16(v);
+          }
+        }
+      }
+      compute_sync<NW>();  // comb[] / red[] are free again for the next row tile
+#pragma unroll
+      for (int b = 0; b < BS; ++b) acc[b] = 0.f;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && err_s && ws.err) atomicExch(ws.err, err_s);
+}
+
+namespace {
+
+template <class T, int WT, int BS, bool X2>
+int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
+                  cudaStream_t st) {
+  using F = TileFmt<WT>;
+  constexpr int S = kRingBytes / F::CHUNK > 32 ? 32 : kRingBytes / F::CHUNK;
+  const int smem = S * F::CHUNK;
+  auto kern = qgemv_stream_kernel<T, WT, BS, X2>;
+  constexpr int THREADS = StreamCfg<WT, BS>::THREADS;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const long U = (long)((w.N + 127) / 128) * (w.K / F::G);
+  const int grid = (int)(U < n_sm ? U : n_sm);
+  kern<<<grid, THREADS, smem, st>>>(w, x, B, ep, ws);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
+}
+
+template <class T, int WT, int BS>
+int launch_stream_x(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
+                    cudaStream_t st) {
+  return x.ql ? launch_stream<T, WT, BS, true>(w, x, B, ep, ws, n_sm, st)
+              : launch_stream<T, WT, BS, false>(w, x, B, ep, ws, n_sm, st);
+}
+
+template <class T, int WT>
+int launch_stream_b(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
+                    cudaStream_t st) {
+  if (B <= 1) return launch_stream_x<T, WT, 1>(w, x, B, ep, ws, n_sm, st);
+  if (B <= 2) return launch_stream_x<T, WT, 2>(w, x, B, ep, ws, n_sm, st);
+  if (B <= 4) return launch_stream_x<T, WT, 4>(w, x, B, ep, ws, n_sm, st);
+  return launch_stream_x<T, WT, 8>(w, x, B, ep, ws, n_sm, st);
+}
+
+}  // namespace
+
+int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
+                 cudaStream_t st) {
+  if (B < 1 || B > 8) return -1;
+  if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128)) return -3;
+  if ((reinterpret_cast<uintptr_t>(w.p0) & 15)) return -4;
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  static const int exp_flags = [] {
+    const char* e = getenv("BARQ_GEMV_EXP");
+    return e ? atoi(e) : 0;
+  }();
+  const StreamWs ws{ws_acc, ws_cnt, err, exp_flags};
+  switch (w.type) {
+    case W_Q4_0: if (w.K % 64) return -2; return launch_stream_b<T4Block<false>, W_Q4_0>(w, x, B, ep, ws, n_sm, st);
+    case W_IQ4_NL: if (w.K % 64) return -2; return launch_stream_b<T4Block<true>, W_IQ4_NL>(w, x, B, ep, ws, n_sm, st);
+    case W_Q8_0: if (w.K % 64) return -2; return launch_stream_b<TQ8_0, W_Q8_0>(w, x, B, ep, ws, n_sm, st);
+    case W_Q4_K: if (w.K % 256) return -2; return launch_stream_b<TK45<false>, W_Q4_K>(w, x, B, ep, ws, n_sm, st);
+    case W_Q5_K: if (w.K % 256) return -2; return launch_stream_b<TK45<true>, W_Q5_K>(w, x, B, ep, ws, n_sm, st);
+    case W_Q6_K: if (w.K % 256) return -2; return launch_stream_b<TQ6_K, W_Q6_K>(w, x, B, ep, ws, n_sm, st);
+  }
+  return -5;
+}
+
+}  // namespace barq

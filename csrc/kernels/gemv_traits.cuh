@@ -20,6 +20,21 @@ BARQ_DEV int dot16(int4 w, int4 x) {
   return dp4a(w.w, x.w, s);
 }
 
+// Integer dot of 32 weights (w0: elements 0-15, w1: 16-31) with the activation at xq; with the
+// two-term activation the residual codes ql (step d/256) fold in as 256 * dot(w, q) + dot(w, ql).
+template <bool X2>
+BARQ_DEV int dot32x(int4 w0, int4 w1, const int8_t* xq, const int8_t* xl) {
+  int s = dot16(w0, ld_x16(xq)) + dot16(w1, ld_x16(xq + 16));
+  if (X2) s = (s << 8) + dot16(w0, ld_x16(xl)) + dot16(w1, ld_x16(xl + 16));
+  return s;
+}
+template <bool X2>
+BARQ_DEV int dot16x(int4 w, const int8_t* xq, const int8_t* xl) {
+  int s = dot16(w, ld_x16(xq));
+  if (X2) s = (s << 8) + dot16(w, ld_x16(xl));
+  return s;
+}
+
 BARQ_DEV int4 nib_lo(int4 q) {
   return make_int4(q.x & 0x0F0F0F0F, q.y & 0x0F0F0F0F, q.z & 0x0F0F0F0F, q.w & 0x0F0F0F0F);
 }
@@ -73,6 +88,13 @@ struct T4Block {
                                                       (row & 127) * 4) + bi));
     return r;
   }
+  // Part q (0..1) of row r from a chunk staged in shared memory.
+  static BARQ_DEV W load_s(const uint8_t* ch, int r, int q) {
+    W s;
+    s.q = *reinterpret_cast<const int4*>(staged_chunk<WT, 0>(ch, r, q));
+    s.d = h2f(reinterpret_cast<const uint16_t*>(ch + TileFmt<WT>::D_OFF)[2 * r + q]);
+    return s;
+  }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
     X x;
     x.a = ld_x16(xq + 32 * p);
@@ -110,6 +132,13 @@ struct TQ8_0 {
                                                       (row & 127) * 4) + bi));
     return r;
   }
+  static BARQ_DEV W load_s(const uint8_t* ch, int r, int q) {
+    W s;
+    s.a = *reinterpret_cast<const int4*>(staged_chunk<W_Q8_0, 0>(ch, r, 2 * q));
+    s.b = *reinterpret_cast<const int4*>(staged_chunk<W_Q8_0, 0>(ch, r, 2 * q + 1));
+    s.d = h2f(reinterpret_cast<const uint16_t*>(ch + TileFmt<W_Q8_0>::D_OFF)[2 * r + q]);
+    return s;
+  }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
     X x;
     x.a = ld_x16(xq + 32 * p);
@@ -141,6 +170,71 @@ struct TK45 {
       r.hdr = ldg16(plane_chunk<WT, 1>(w, row, kg, 0));
     }
     return r;
+  }
+  static BARQ_DEV W load_s(const uint8_t* ch, int r, int q) {
+    W s;
+    s.q = *reinterpret_cast<const int4*>(staged_chunk<WT, 0>(ch, r, q));
+    if constexpr (FIVE) {
+      s.hdr = *reinterpret_cast<const int4*>(staged_chunk<WT, 2>(ch, r, 0));
+      s.qh = *reinterpret_cast<const int4*>(staged_chunk<WT, 1>(ch, r, q & 1));
+    } else {
+      s.hdr = *reinterpret_cast<const int4*>(staged_chunk<WT, 1>(ch, r, 0));
+    }
+    return s;
+  }
+  // Parts [Q0, Q0+NQ) (NQ even: whole 32-byte qs pairs j = Q0/2 ..) of row r of a staged chunk
+  // (super-block kg) against BS tokens; scales decoded once and reused for every token.
+  template <int Q0, int NQ, int BS, bool X2>
+  static BARQ_DEV void chunk_dot(const uint8_t* ch, int r, int kg, const ActQ8& x, int K, int nparts, int B,
+                                 float* acc) {
+    static_assert(Q0 % 2 == 0 && NQ % 2 == 0, "whole qs pairs");
+    constexpr int J0 = Q0 / 2, NJ = NQ / 2;
+    constexpr int HP = FIVE ? 2 : 1;
+    const uint4 hd = *reinterpret_cast<const uint4*>(staged_chunk<WT, HP>(ch, r, 0));
+    const float d = h2f(hd.x & 0xFFFF), dmin = h2f(hd.x >> 16);
+    float dsc[2 * NJ], dmn[2 * NJ];
+#pragma unroll
+    for (int i = 0; i < 2 * NJ; ++i) {
+      int sc, m;
+      kscale(hd.y, hd.z, hd.w, 2 * J0 + i, sc, m);
+      dsc[i] = d * (float)sc;
+      dmn[i] = dmin * (float)m;
+    }
+    int4 qh0 = make_int4(0, 0, 0, 0), qh1 = qh0;
+    if constexpr (FIVE) {
+      qh0 = *reinterpret_cast<const int4*>(staged_chunk<WT, 1>(ch, r, 0));
+      qh1 = *reinterpret_cast<const int4*>(staged_chunk<WT, 1>(ch, r, 1));
+    }
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) {
+      const int j = J0 + jj;  // qs bytes [32j, 32j+32): low nibbles sub-block 2j, high 2j+1
+      const int4 q0 = *reinterpret_cast<const int4*>(staged_chunk<WT, 0>(ch, r, 2 * j));
+      const int4 q1 = *reinterpret_cast<const int4*>(staged_chunk<WT, 0>(ch, r, 2 * j + 1));
+      int4 a0 = nib_lo(q0), a1 = nib_lo(q1), b0 = nib_hi(q0), b1 = nib_hi(q1);
+      if constexpr (FIVE) {
+        const int sa = 2 * j, sb = 2 * j + 1;
+        a0 = make_int4(a0.x | (((qh0.x >> sa) & 0x01010101) << 4), a0.y | (((qh0.y >> sa) & 0x01010101) << 4),
+                       a0.z | (((qh0.z >> sa) & 0x01010101) << 4), a0.w | (((qh0.w >> sa) & 0x01010101) << 4));
+        a1 = make_int4(a1.x | (((qh1.x >> sa) & 0x01010101) << 4), a1.y | (((qh1.y >> sa) & 0x01010101) << 4),
+                       a1.z | (((qh1.z >> sa) & 0x01010101) << 4), a1.w | (((qh1.w >> sa) & 0x01010101) << 4));
+        b0 = make_int4(b0.x | (((qh0.x >> sb) & 0x01010101) << 4), b0.y | (((qh0.y >> sb) & 0x01010101) << 4),
+                       b0.z | (((qh0.z >> sb) & 0x01010101) << 4), b0.w | (((qh0.w >> sb) & 0x01010101) << 4));
+        b1 = make_int4(b1.x | (((qh1.x >> sb) & 0x01010101) << 4), b1.y | (((qh1.y >> sb) & 0x01010101) << 4),
+                       b1.z | (((qh1.z >> sb) & 0x01010101) << 4), b1.w | (((qh1.w >> sb) & 0x01010101) << 4));
+      }
+#pragma unroll
+      for (int b = 0; b < BS; ++b) {
+        if (b < B) {
+          const size_t e = (size_t)b * K + 256 * kg + 64 * j;
+          const int sA = dot32x<X2>(a0, a1, x.q + e, X2 ? x.ql + e : nullptr);
+          const int sB = dot32x<X2>(b0, b1, x.q + e + 32, X2 ? x.ql + e + 32 : nullptr);
+          const float2 xa = x.s[(size_t)b * nparts + 8 * kg + 2 * j], xb = x.s[(size_t)b * nparts + 8 * kg + 2 * j + 1];
+          const float f = X2 ? (1.0f / 256.0f) : 1.0f;
+          acc[b] += dsc[2 * jj] * (xa.x * f) * (float)sA + dsc[2 * jj + 1] * (xb.x * f) * (float)sB -
+                    dmn[2 * jj] * xa.y - dmn[2 * jj + 1] * xb.y;
+        }
+      }
+    }
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
     int b = p >> 3, j = (p & 7) >> 1, h = p & 1;
@@ -194,6 +288,55 @@ struct TQ6_K {
     r.d = h2f(__ldg(reinterpret_cast<const uint16_t*>(chunk_ptr<W_Q6_K>(w, row >> 7, kg) + TileFmt<W_Q6_K>::D_OFF +
                                                       (row & 127) * 2)));
     return r;
+  }
+  static BARQ_DEV W load_s(const uint8_t* ch, int r, int q) {
+    W s;
+    const int n = q >> 2, c = (q >> 1) & 1, h = q & 1;
+    s.ql = *reinterpret_cast<const int4*>(staged_chunk<W_Q6_K, 0>(ch, r, q));
+    s.qh = *reinterpret_cast<const int4*>(staged_chunk<W_Q6_K, 1>(ch, r, 2 * n + h));
+    const int8_t* sc = reinterpret_cast<const int8_t*>(staged_chunk<W_Q6_K, 2>(ch, r, 0));
+    int lo = sc[8 * n + 2 * c + h], hi = sc[8 * n + 4 + 2 * c + h];
+    s.sc = (uint32_t)(lo & 0xFFFF) | ((uint32_t)hi << 16);
+    s.d = h2f(reinterpret_cast<const uint16_t*>(ch + TileFmt<W_Q6_K>::D_OFF)[r]);
+    return s;
+  }
+  // Parts [Q0, Q0+NQ) of row r of a staged chunk against BS tokens; part q = 4n + 2c + h.
+  template <int Q0, int NQ, int BS, bool X2>
+  static BARQ_DEV void chunk_dot(const uint8_t* ch, int r, int kg, const ActQ8& x, int K, int nparts, int B,
+                                 float* acc) {
+    const float d = h2f(reinterpret_cast<const uint16_t*>(ch + TileFmt<W_Q6_K>::D_OFF)[r]);
+    const int8_t* scp = reinterpret_cast<const int8_t*>(staged_chunk<W_Q6_K, 2>(ch, r, 0));
+    const int4 sc4 = *reinterpret_cast<const int4*>(scp);  // 16 int8 scales (the plane row is one 16-byte piece)
+    const int8_t* sc = reinterpret_cast<const int8_t*>(&sc4);
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) {
+      {
+        const int q = Q0 + qi, H = q >> 2, c = (q >> 1) & 1, h = q & 1;
+        const int4 ql = *reinterpret_cast<const int4*>(staged_chunk<W_Q6_K, 0>(ch, r, q));
+        const int4 qh = *reinterpret_cast<const int4*>(staged_chunk<W_Q6_K, 1>(ch, r, 2 * H + h));
+        const int s_lo = 2 * c, s_hi = 4 + 2 * c;
+        int4 lo = nib_lo(ql), hi = nib_hi(ql);
+        lo = make_int4(lo.x | (((qh.x >> s_lo) & 0x03030303) << 4), lo.y | (((qh.y >> s_lo) & 0x03030303) << 4),
+                       lo.z | (((qh.z >> s_lo) & 0x03030303) << 4), lo.w | (((qh.w >> s_lo) & 0x03030303) << 4));
+        hi = make_int4(hi.x | (((qh.x >> s_hi) & 0x03030303) << 4), hi.y | (((qh.y >> s_hi) & 0x03030303) << 4),
+                       hi.z | (((qh.z >> s_hi) & 0x03030303) << 4), hi.w | (((qh.w >> s_hi) & 0x03030303) << 4));
+        lo = vsub4(lo, 0x20202020);
+        hi = vsub4(hi, 0x20202020);
+        const float dlo = d * (float)sc[8 * H + 2 * c + h], dhi = d * (float)sc[8 * H + 4 + 2 * c + h];
+#pragma unroll
+        for (int b = 0; b < BS; ++b) {
+          if (b < B) {
+            const size_t e = (size_t)b * K + 256 * kg + 128 * H + 32 * c + 16 * h;
+            const int sL = dot16x<X2>(lo, x.q + e, X2 ? x.ql + e : nullptr);
+            const int sH = dot16x<X2>(hi, x.q + e + 64, X2 ? x.ql + e + 64 : nullptr);
+            const float f = X2 ? (1.0f / 256.0f) : 1.0f;
+            const float xl = x.s[(size_t)b * nparts + 8 * kg + 4 * H + c].x * f;
+            const float xh = x.s[(size_t)b * nparts + 8 * kg + 4 * H + 2 + c].x * f;
+            acc[b] += dlo * xl * (float)sL + dhi * xh * (float)sH;
+          }
+        }
+      }
+    }
   }
   static BARQ_DEV X load_x(const int8_t* xq, const float2* xs, int p) {
     int b = p >> 3, q = p & 7, n = q >> 2, c = (q >> 1) & 1, h = q & 1;

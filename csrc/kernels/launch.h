@@ -29,6 +29,12 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
 int gemm_error_word(int* host_out);
+int* kernel_err_word();  // device error word shared by the bounded-wait kernels (per device)
+// Streaming decode GEMV (1..8 tokens): persistent, bulk-copy fed, stream-K over weight chunks.
+// ws_acc: f32 [8, N] and ws_cnt: int [N/128], both zero before the first call; the kernel leaves
+// them zero.  Calls sharing a workspace must not overlap on the GPU.  err: bounded-wait error word.
+int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
+                 cudaStream_t st);
 void gemm_set_trace(void* p);  // diagnostics (BARQ_GEMM_EXP bit 1): [256 stages][8] u64 stamps of CTA 0
 int gemm_clear_error_word();
 

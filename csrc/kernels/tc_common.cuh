@@ -56,6 +56,14 @@ BARQ_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Wait ignoring the error word (used to drain copies in flight before a CTA exits); bounded.
+BARQ_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
 BARQ_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* err, int site) {
   if (mbar_test_wait(bar, parity)) return true;  // non-blocking probe: cheaper when already complete
   if (mbar_try_wait(bar, parity)) return true;
