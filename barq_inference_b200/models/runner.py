@@ -147,6 +147,22 @@ class LlamaRunner:
                      xb=None if xb is None else xb[t0:t1].contiguous())
         return out
 
+    def _norm_lin(self, w, x: torch.Tensor, norm_w: torch.Tensor, T: int, mode: int, out=None, bias=None):
+        """RMSNorm(x) -> int8 -> GEMV.  For 1-2 tokens on a quantized weight the norm runs inside the
+        streaming GEMV (no separate launch); otherwise RMSNorm then ``_lin_q8``."""
+        eps = self.cfg.rms_eps
+        if isinstance(w, QWeight) and ops.gemv_can_fuse_norm(w, T):
+            if mode == EPI_SWIGLU_Q8:
+                oq = Q8Act.empty(T, w.N // 2, self.device, self.x2)
+                ops.gemv(w, None, T, mode, out_q=oq, x2=self.x2, norm=(x, norm_w, eps))
+                return oq
+            if out is None:
+                out = torch.empty(T, w.N, dtype=torch.float32, device=self.device)
+            ops.gemv(w, None, T, mode, out=out, bias=bias, x2=self.x2, norm=(x, norm_w, eps))
+            return out
+        hb, hq = ops.rmsnorm(x, norm_w, eps, want_q8=True, want_bf16=self._needs_bf16(w), x2=self.x2)
+        return self._lin_q8(w, hq, T, mode, out=out, bias=bias, xb=hb)
+
     def _lin_bf16(self, w, xb: torch.Tensor, T: int, mode: int, out=None, bias=None):
         """Projection of bf16 activations [T, K] on the tcgen05 GEMM (K2)."""
         if isinstance(w, tuple):
@@ -228,9 +244,7 @@ class LlamaRunner:
         x = ops.embed(self.embed_w, inp.ids)
         for li, L in enumerate(self.layers):
             kc, vc = self.kv[li]
-            hb, hq = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.qkv),
-                                 x2=self.x2)
-            qkv = self._lin_q8(L.qkv, hq, T, EPI_STORE_F32, bias=L.qkv_bias, xb=hb)
+            qkv = self._norm_lin(L.qkv, x, L.attn_norm, T, EPI_STORE_F32, bias=L.qkv_bias)
             q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
                                   cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
             if inp.decode:
@@ -246,12 +260,12 @@ class LlamaRunner:
                 L.moe.forward(self, hq, hb, T, x)
                 continue
             down_bf16 = self._needs_bf16(L.down)
-            hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=self._needs_bf16(L.gate_up),
-                                 x2=self.x2)
             if L.gu_interleaved and not down_bf16:
-                h2 = self._lin_q8(L.gate_up, hq, T, EPI_SWIGLU_Q8)
+                h2 = self._norm_lin(L.gate_up, x, L.ffn_norm, T, EPI_SWIGLU_Q8)
                 self._lin_q8(L.down, h2, T, EPI_ADD_F32, out=x)
             else:
+                hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True,
+                                     want_bf16=self._needs_bf16(L.gate_up), x2=self.x2)
                 gu = self._lin_q8(L.gate_up, hq, T, EPI_STORE_F32, xb=hb)
                 if L.gu_interleaved:  # undo the 32-row interleave for the elementwise kernel
                     gu = gu.view(T, -1, 2, 32).transpose(1, 2).reshape(T, -1).contiguous()
@@ -259,5 +273,4 @@ class LlamaRunner:
                                       x2=self.x2)
                 self._lin_q8(L.down, hq2, T, EPI_ADD_F32, out=x, xb=hb2)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
-        _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
-        return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32)
+        return self._norm_lin(self.out_w, xl, self.out_norm, xl.shape[0], EPI_STORE_F32)

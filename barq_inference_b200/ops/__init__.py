@@ -117,21 +117,33 @@ def _gemv_ws(w: QWeight):
     return ws
 
 
+NORM_MAX_K = 4096
+
+
+def gemv_can_fuse_norm(w: QWeight, T: int) -> bool:
+    """Whether ``gemv(..., norm=...)`` (RMSNorm computed inside the GEMV) applies."""
+    return GEMV_STREAM and w.wtype != W_BF16 and T <= 2 and w.K <= NORM_MAX_K and w.N <= WS_ROWS
+
+
 def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: torch.Tensor | None = None,
          xb: torch.Tensor | None = None, bias: torch.Tensor | None = None, out_q: Q8Act | None = None,
-         x2: bool = False):
+         x2: bool = False, norm: tuple | None = None):
     """Decode GEMV for T <= 8 tokens.  Returns ``out`` (allocated if None for store modes).
 
     Quantized weights go through the streaming kernel (persistent, bulk-copy fed, stream-K);
-    dense bf16 weights through the warp-per-row kernel."""
+    dense bf16 weights through the warp-per-row kernel.  ``norm=(h, weight, eps)`` (f32 h [T, K]):
+    the activation is int8(rmsnorm(h) * weight), computed inside the kernel (``x`` unused)."""
     C = require_ext()
     dev = w.device
     wa, wc = _gemv_ws(w)
+    nh, nw, neps = (norm if norm is not None else (None, None, 0.0))
+    if norm is not None and not gemv_can_fuse_norm(w, T):
+        raise ValueError("gemv: fused norm needs a quantized weight, T <= 2 and K <= 4096")
     if mode == EPI_SWIGLU_Q8:
         F = w.N // 2
         if out_q is None:
             out_q = Q8Act.empty(T, F, dev, x2)
-        C.qgemv(*w.args(), *_ins(x), xb, T, mode, None, out, *out_q.outs(), bias, F, wa, wc)
+        C.qgemv(*w.args(), *_ins(x), xb, T, mode, None, out, *out_q.outs(), bias, F, wa, wc, nh, nw, neps, int(x2))
         _count()
         return out_q
     if out is None:
@@ -140,7 +152,8 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
     ld = out.stride(0)
     f32 = out if out.dtype == torch.float32 else None
     bf = out if out.dtype == torch.bfloat16 else None
-    C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld, wa, wc)
+    C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld, wa, wc, nh, nw, neps,
+            int(x2))
     _count()
     return out
 

@@ -45,16 +45,19 @@ barq::QW make_qw(int64_t type, int64_t N, int64_t K, const Tensor& p0, const Opt
 
 void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, OptT xq, OptT xs, OptT xql,
            OptT xdl, OptT xb, int64_t B, int64_t mode, OptT out_f32, OptT out_bf16, OptT out_q, OptT out_s,
-           OptT out_ql, OptT out_dl, OptT bias, int64_t ld_out, OptT ws_acc, OptT ws_cnt) {
+           OptT out_ql, OptT out_dl, OptT bias, int64_t ld_out, OptT ws_acc, OptT ws_cnt, OptT norm_h, OptT norm_w,
+           double norm_eps, int64_t norm_x2) {
   c10::cuda::CUDAGuard g(p0.device());
   barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
   barq::ActQ8 x{optptr<const int8_t>(xq), optptr<const float2>(xs), optptr<const int8_t>(xql),
                 optptr<const float2>(xdl)};
   barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16),
                    act_out(out_q, out_s, out_ql, out_dl), optptr<const float>(bias), (int)ld_out};
+  TORCH_CHECK(!norm_h || (ws_acc && ws_cnt), "qgemv: the fused norm needs the streaming kernel");
   if (ws_acc && ws_cnt && type != barq::W_BF16) {
     TORCH_CHECK(ws_acc->numel() >= 8 * N && ws_cnt->numel() >= (N + 127) / 128, "qgemv: workspace too small");
     check(barq::qgemv_stream(w, x, (int)B, ep, ptr<float>(*ws_acc), ptr<int>(*ws_cnt), barq::kernel_err_word(),
+                             optptr<const float>(norm_h), optptr<const float>(norm_w), (float)norm_eps, (int)norm_x2,
                              cur_stream()),
           "qgemv_stream");
     return;

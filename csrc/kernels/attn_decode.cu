@@ -13,6 +13,7 @@
 // A second kernel merges the splits, normalizes, writes bf16 and the int8 q8 activation of the
 // output projection.
 #include "common.cuh"
+#include "pdl.cuh"
 #include "launch.h"
 
 namespace barq {
@@ -45,6 +46,8 @@ constexpr int kBS = 16;  // tokens per KV page
 
 template <typename TC, int D, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int NW = 4;
   constexpr int CH = D / 8;        // 16-byte chunks per K row
   constexpr int CPH = CH / 2;      // chunks per half-lane
@@ -173,6 +176,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
 // One CTA per (head, batch row); D threads.
 template <int D>
 __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeAttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int G = a.H / a.Hkv, kvh = h / G, g = h % G;
   const size_t base = ((size_t)b * a.Hkv + kvh) * a.splits;
@@ -213,13 +218,13 @@ static int launch_g(const DecodeAttnArgs& a, cudaStream_t st) {
   const int G = a.H / a.Hkv;
   dim3 grid(a.splits, a.Hkv, a.B);
   switch (G) {
-    case 1: decode_attn_kernel<TC, D, 1><<<grid, 128, 0, st>>>(a); break;
-    case 2: decode_attn_kernel<TC, D, 2><<<grid, 128, 0, st>>>(a); break;
-    case 4: decode_attn_kernel<TC, D, 4><<<grid, 128, 0, st>>>(a); break;
-    case 8: decode_attn_kernel<TC, D, 8><<<grid, 128, 0, st>>>(a); break;
+    case 1: launch_pdl(decode_attn_kernel<TC, D, 1>, grid, dim3(128), 0, st, a); break;
+    case 2: launch_pdl(decode_attn_kernel<TC, D, 2>, grid, dim3(128), 0, st, a); break;
+    case 4: launch_pdl(decode_attn_kernel<TC, D, 4>, grid, dim3(128), 0, st, a); break;
+    case 8: launch_pdl(decode_attn_kernel<TC, D, 8>, grid, dim3(128), 0, st, a); break;
     default: return -3;
   }
-  decode_merge_kernel<D><<<dim3(a.H, a.B), D, 0, st>>>(a);
+  launch_pdl(decode_merge_kernel<D>, dim3(a.H, a.B), dim3(D), 0, st, a);
   return 0;
 }
 

@@ -10,6 +10,7 @@
 // CPU FA-2 (advanced/src/flash_attention.rs:169-271); its CUDA flash attention returns
 // Unsupported (backend/src/cuda_flash_attn.rs:165-359).
 #include "common.cuh"
+#include "pdl.cuh"
 #include "launch.h"
 
 namespace barq {
@@ -57,6 +58,8 @@ template <int N> BARQ_DEV void cp_async_wait() { asm volatile("cp.async.wait_gro
 
 template <typename TC, int D>
 __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int BQ = 64, BK = 64, LD = D + 8;  // padded rows (16 B) avoid ldmatrix bank conflicts
   constexpr int NB = BK / 8;                   // S n-blocks per warp
   constexpr int KS = D / 16;                   // k-steps of QK^T
@@ -254,7 +257,7 @@ static int launch_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   size_t smem = (size_t)(64 * LD + 4 * 64 * LD) * sizeof(TC);
   cudaFuncSetAttribute(prefill_attn_kernel<TC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((a.max_q + 63) / 64, a.H, a.S);
-  prefill_attn_kernel<TC, D><<<grid, 128, smem, st>>>(a);
+  launch_pdl(prefill_attn_kernel<TC, D>, grid, dim3(128), smem, st, a);
   return 0;
 }
 

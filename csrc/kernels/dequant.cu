@@ -1,6 +1,7 @@
 // K13 embedding gather straight from quantized rows, and row dequantization to bf16.
 // Element-wise ggml-spec decoding of the tiled device layout described in qtile.cuh.
 #include "common.cuh"
+#include "pdl.cuh"
 #include "launch.h"
 #include "qweight.cuh"
 #include "qtile.cuh"
@@ -74,6 +75,8 @@ BARQ_DEV float deq_elem(const QW& w, int row, int k) {
 }
 
 __global__ void embed_kernel(QW w, const int* __restrict__ ids, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int row = ids[t];
   for (int k = threadIdx.x; k < w.K; k += blockDim.x) out[(size_t)t * w.K + k] = deq_elem(w, row, k);
@@ -81,11 +84,13 @@ __global__ void embed_kernel(QW w, const int* __restrict__ ids, float* __restric
 
 int embed_gather(const QW& table, const int* ids, int T, float* out, cudaStream_t st) {
   if (T <= 0) return 0;
-  embed_kernel<<<T, 256, 0, st>>>(table, ids, out);
+  launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, table, ids, out);
   return 0;
 }
 
 __global__ void dequant_rows_kernel(QW w, int r0, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   for (int k = threadIdx.x; k < w.K; k += blockDim.x)
     out[(size_t)r * w.K + k] = __float2bfloat16(deq_elem(w, r0 + r, k));
@@ -93,7 +98,7 @@ __global__ void dequant_rows_kernel(QW w, int r0, __nv_bfloat16* __restrict__ ou
 
 int dequant_rows(const QW& w, int r0, int n, __nv_bfloat16* out, cudaStream_t st) {
   if (n <= 0) return 0;
-  dequant_rows_kernel<<<n, 256, 0, st>>>(w, r0, out);
+  launch_pdl(dequant_rows_kernel, dim3(n), dim3(256), 0, st, w, r0, out);
   return 0;
 }
 

@@ -4,8 +4,11 @@
 // Parity: the reference's rms_norm / rope / SwiGLU run as separate f32 CPU loops
 // (models/src/transformer.rs:148-172, 378-408, 514-568); here they are fused into the producers
 // and consumers of each GEMV/GEMM so the residual stream is touched once per sub-layer.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.cuh"
 #include "qweight.cuh"
 
 namespace barq {
@@ -16,6 +19,8 @@ constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
                                                       const float* __restrict__ w, float eps, int H,
                                                       void* __restrict__ ob, int ob_f16, ActOut oq) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * H;
   const float* ar = add ? add + (size_t)t * H : nullptr;
@@ -54,12 +59,16 @@ int rmsnorm(float* x, const float* add, const float* w, float eps, int T, int H,
             ActOut out_q, cudaStream_t st) {
   if (out_q.q && (H % 32)) return -1;
   if (T <= 0) return 0;
-  rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, add, w, eps, H, out_act, out_f16, out_q);
-  return 0;
+  return launch_pdl(rmsnorm_kernel, dim3(T), dim3(kNormThreads), 0, st, x, add, w, eps, H, out_act, out_f16, out_q) ==
+                 cudaSuccess
+             ? 0
+             : -20;
 }
 
 template <typename T>
 __global__ void quant_q8_kernel(const T* __restrict__ x, int H, int ldx, ActOut oq) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -73,15 +82,17 @@ int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_
   if (T <= 0) return 0;
   dim3 g((H / 32 + 7) / 8, T);
   if (x_is_bf16)
-    quant_q8_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)x, H, ldx, out_q);
+    launch_pdl(quant_q8_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)x, H, ldx, out_q);
   else
-    quant_q8_kernel<float><<<g, 256, 0, st>>>((const float*)x, H, ldx, out_q);
+    launch_pdl(quant_q8_kernel<float>, g, dim3(256), 0, st, (const float*)x, H, ldx, out_q);
   return 0;
 }
 
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ in, int F, int ld, void* __restrict__ ob, int ob_f16,
                               ActOut oq) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -99,9 +110,9 @@ int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, void* out_ac
   if (T <= 0) return 0;
   dim3 g(((F + 31) / 32 + 7) / 8, T);
   if (in_is_bf16)
-    swiglu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)in, F, ld_in, out_act, out_f16, out_q);
+    launch_pdl(swiglu_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)in, F, ld_in, out_act, out_f16, out_q);
   else
-    swiglu_kernel<float><<<g, 256, 0, st>>>((const float*)in, F, ld_in, out_act, out_f16, out_q);
+    launch_pdl(swiglu_kernel<float>, g, dim3(256), 0, st, (const float*)in, F, ld_in, out_act, out_f16, out_q);
   return 0;
 }
 
@@ -109,6 +120,8 @@ int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, void* out_ac
 // One CTA per token, one warp per head (q heads first, then k heads, then v heads).
 template <typename TIN, typename TC>
 __global__ void __launch_bounds__(256) rope_kv_kernel(RopeKVArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nh = a.H + 2 * a.Hkv;
@@ -202,13 +215,23 @@ int rope_kv_write(const RopeKVArgs& a, cudaStream_t st) {
   const int nh = a.H + 2 * a.Hkv;
   dim3 g(a.T, (nh + 7) / 8 > 4 ? 4 : (nh + 7) / 8);
   if (a.qkv_is_bf16) {
-    if (a.cache_is_bf16) rope_kv_kernel<__nv_bfloat16, __nv_bfloat16><<<g, 256, 0, st>>>(a);
-    else rope_kv_kernel<__nv_bfloat16, __half><<<g, 256, 0, st>>>(a);
+    if (a.cache_is_bf16) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else launch_pdl(rope_kv_kernel<__nv_bfloat16, __half>, g, dim3(256), 0, st, a);
   } else {
-    if (a.cache_is_bf16) rope_kv_kernel<float, __nv_bfloat16><<<g, 256, 0, st>>>(a);
-    else rope_kv_kernel<float, __half><<<g, 256, 0, st>>>(a);
+    if (a.cache_is_bf16) launch_pdl(rope_kv_kernel<float, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else launch_pdl(rope_kv_kernel<float, __half>, g, dim3(256), 0, st, a);
   }
   return 0;
 }
 
+}  // namespace barq
+
+namespace barq {
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("BARQ_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 }  // namespace barq

@@ -34,6 +34,7 @@
 
 #include "gemv_traits.cuh"
 #include "launch.h"
+#include "pdl.cuh"
 #include "qtile.cuh"
 #include "tc_common.cuh"
 
@@ -367,6 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   volatile int* err = &err_s;
+  // Weight chunks, their dequantization and the MMAs on them do not depend on earlier kernels; the
+  // activation producer and the epilogue (which writes, or adds into, the output) wait for them.
+  pdl_trigger();
 
   if (warp == kTmaWarp) {
     // ---------------------------------------------------------------- weight-chunk producer
@@ -394,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kActWarp) {
     // ---------------------------------------------------------------- activation-tile producer
+    pdl_wait();
     if (lane == 0) {
       prefetch_tmap(&tx);
       int it = 0;
@@ -568,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     AT* out_act = reinterpret_cast<AT*>(g.out_act);
     float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);
     const bool atomic = g.k_splits > 1;
+    pdl_wait();
     int tc = 0;
     for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
       int nt, tt, z, gb, ge;
@@ -719,8 +725,8 @@ static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cud
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   const int total = ((g.N + 127) / 128) * tiles_t * g.k_splits;
   const int n = sm_count();
-  kern<<<dim3(total < n ? total : n), kThreads, L::TOTAL, st>>>(tx, g);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
+  return launch_pdl(kern, dim3(total < n ? total : n), dim3(kThreads), (size_t)L::TOTAL, st, tx, g) == cudaSuccess ? 0
+                                                                                                          : -20;
 }
 
 // Weight-chunk ring depth: as many chunks in flight as the shared memory left after the operand

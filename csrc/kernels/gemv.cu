@@ -13,12 +13,15 @@
 //   EPI_SWIGLU_Q8  CTA holds 32 gate rows + 32 matching up rows; writes silu(g)*u for 32 outputs
 //                  straight into the int8 activation layout of the next GEMV (and optionally bf16).
 #include "gemv_traits.cuh"
+#include "pdl.cuh"
 #include "launch.h"
 
 namespace barq {
 
 template <class T, int BS, int RW, int NW, bool X2>
 __global__ void __launch_bounds__(NW * 32) qgemv_kernel(QW w, ActQ8 x, int B, GemvEpi ep) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * NW + warp) * RW;
   const int K = w.K;

@@ -24,6 +24,7 @@
 
 #include "gemv_traits.cuh"
 #include "launch.h"
+#include "pdl.cuh"
 #include "tc_common.cuh"
 
 namespace barq {
@@ -33,6 +34,7 @@ using namespace tc;
 namespace {
 
 constexpr int kRingBytes = 184 * 1024;
+constexpr int kNormMaxK = 4096;  // fused-RMSNorm prologue: longest activation row staged in smem
 
 // Compute warps per CTA: 16 (each row split over 4 warps) for 1-2 tokens, where latency hiding
 // matters most and registers allow it; 8 (rows split over 2 warps) otherwise and for formats
@@ -43,6 +45,10 @@ struct StreamCfg {
   static constexpr int TPR = (BS <= 2 && NP >= 8) ? 4 : 2;  // warps per row group
   static constexpr int NW = 4 * TPR;                        // compute warps: 4 row groups of 32
   static constexpr int THREADS = (NW + 1) * 32;
+  // 1-2 tokens: room for the fused-norm activations (q, ql, s, dl per token) after the ring
+  static constexpr int XS_BYTES = BS <= 2 ? BS * (2 * kNormMaxK + 2 * (kNormMaxK / 32) * 8) : 0;
+  static constexpr int RING = kRingBytes - XS_BYTES;
+  static constexpr int S = RING / TileFmt<WT>::CHUNK > 32 ? 32 : RING / TileFmt<WT>::CHUNK;
 };
 
 BARQ_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -56,6 +62,16 @@ BARQ_DEV void compute_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
 }
 
+// Optional prologue: the activation is rmsnorm(h) * w quantized to int8 inside the kernel (each CTA
+// recomputes it into shared memory while its weight stream is already in flight), replacing a
+// separate RMSNorm launch.  h: f32 [B, K]; null = activations come in x.
+struct NormIn {
+  const float* h;
+  const float* w;
+  float eps;
+  int x2;
+};
+
 struct StreamWs {
   float* acc;  // [8, N] f32 partial sums of shared row tiles (zero between calls)
   int* cnt;    // [N / 128] units accumulated per row tile (zero between calls)
@@ -67,11 +83,11 @@ struct StreamWs {
 
 template <class T, int WT, int BS, bool X2>
 __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
-    qgemv_stream_kernel(QW w, ActQ8 x, int B, GemvEpi ep, StreamWs ws) {
+    qgemv_stream_kernel(QW w, ActQ8 x, int B, GemvEpi ep, StreamWs ws, NormIn ni) {
   using F = TileFmt<WT>;
   using Cfg = StreamCfg<WT, BS>;
   constexpr int CH = F::CHUNK;
-  constexpr int S = kRingBytes / CH > 32 ? 32 : kRingBytes / CH;
+  constexpr int S = Cfg::S;
   constexpr int NP = Cfg::NP;     // 32-weight parts per chunk row
   constexpr int TPR = Cfg::TPR;   // warps sharing a row group
   constexpr int NW = Cfg::NW;
@@ -82,6 +98,7 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
   __shared__ float red[128][BS];
   __shared__ float comb[TPR - 1][128][BS];
   __shared__ int last_s;
+  __shared__ float red_ss[NW];
   __shared__ int err_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,6 +118,9 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
   }
   __syncthreads();
   volatile int* err = &err_s;
+  // Weights do not depend on earlier kernels: the producer streams them at once.  The compute warps
+  // wait for the previous kernel (activations, output buffers, workspace) before their first read.
+  pdl_trigger();
 
   if (warp == NW) {
     // ------------------------------------------------------------------ producer
@@ -126,6 +146,37 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------------ compute
+    pdl_wait();
+    if (Cfg::XS_BYTES > 0 && ni.h) {
+      // fused RMSNorm + int8 quantization of the B activation rows into shared memory
+      const int K = w.K, G32 = w.K / 32;
+      int8_t* sq = reinterpret_cast<int8_t*>(smem + S * CH);
+      int8_t* sql = sq + BS * K;
+      float2* ssc = reinterpret_cast<float2*>(sql + BS * K);
+      float2* sdl = ssc + BS * G32;
+      for (int b = 0; b < B; ++b) {
+        const float* hb = ni.h + (size_t)b * K;
+        float ss = 0.f;
+        for (int k = threadIdx.x; k < K; k += NW * 32) {
+          const float v = hb[k];
+          ss += v * v;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red_ss[warp] = ss;
+        compute_sync<NW>();
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) tot += red_ss[i];
+        const float rstd = rsqrtf(tot / (float)K + ni.eps);
+        const ActOut o{sq + b * K, ssc + b * G32, ni.x2 ? sql + b * K : nullptr, ni.x2 ? sdl + b * G32 : nullptr};
+        for (int g = warp; g < G32; g += NW) {
+          const int k = g * 32 + lane;
+          act_store32(o, hb[k] * rstd * ni.w[k], k, g, lane);
+        }
+        compute_sync<NW>();  // red_ss reused by the next row
+      }
+      x = ActQ8{sq, ssc, ni.x2 ? sql : nullptr, ni.x2 ? sdl : nullptr};
+    }
     const int half = warp % TPR, r = (warp / TPR) * 32 + lane;  // half: this warp's slice of the row
     const int tid = threadIdx.x;
     float acc[BS];
@@ -273,40 +324,42 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
 namespace {
 
 template <class T, int WT, int BS, bool X2>
-int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
-                  cudaStream_t st) {
+int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
+                  int n_sm, cudaStream_t st) {
   using F = TileFmt<WT>;
-  constexpr int S = kRingBytes / F::CHUNK > 32 ? 32 : kRingBytes / F::CHUNK;
-  const int smem = S * F::CHUNK;
+  using Cfg = StreamCfg<WT, BS>;
+  if (ni.h && (Cfg::XS_BYTES == 0 || w.K > kNormMaxK)) return -6;
+  const int smem = Cfg::S * F::CHUNK + Cfg::XS_BYTES;
   auto kern = qgemv_stream_kernel<T, WT, BS, X2>;
   constexpr int THREADS = StreamCfg<WT, BS>::THREADS;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const long U = (long)((w.N + 127) / 128) * (w.K / F::G);
   const int grid = (int)(U < n_sm ? U : n_sm);
-  kern<<<grid, THREADS, smem, st>>>(w, x, B, ep, ws);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : -20;
+  return launch_pdl(kern, dim3(grid), dim3(THREADS), (size_t)smem, st, w, x, B, ep, ws, ni) == cudaSuccess ? 0 : -20;
 }
 
 template <class T, int WT, int BS>
-int launch_stream_x(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
-                    cudaStream_t st) {
-  return x.ql ? launch_stream<T, WT, BS, true>(w, x, B, ep, ws, n_sm, st)
-              : launch_stream<T, WT, BS, false>(w, x, B, ep, ws, n_sm, st);
+int launch_stream_x(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
+                    int n_sm, cudaStream_t st) {
+  const bool x2 = ni.h ? ni.x2 != 0 : x.ql != nullptr;
+  return x2 ? launch_stream<T, WT, BS, true>(w, x, B, ep, ws, ni, n_sm, st)
+            : launch_stream<T, WT, BS, false>(w, x, B, ep, ws, ni, n_sm, st);
 }
 
 template <class T, int WT>
-int launch_stream_b(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, int n_sm,
-                    cudaStream_t st) {
-  if (B <= 1) return launch_stream_x<T, WT, 1>(w, x, B, ep, ws, n_sm, st);
-  if (B <= 2) return launch_stream_x<T, WT, 2>(w, x, B, ep, ws, n_sm, st);
-  if (B <= 4) return launch_stream_x<T, WT, 4>(w, x, B, ep, ws, n_sm, st);
-  return launch_stream_x<T, WT, 8>(w, x, B, ep, ws, n_sm, st);
+int launch_stream_b(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
+                    int n_sm, cudaStream_t st) {
+  if (B <= 1) return launch_stream_x<T, WT, 1>(w, x, B, ep, ws, ni, n_sm, st);
+  if (B <= 2) return launch_stream_x<T, WT, 2>(w, x, B, ep, ws, ni, n_sm, st);
+  if (B <= 4) return launch_stream_x<T, WT, 4>(w, x, B, ep, ws, ni, n_sm, st);
+  return launch_stream_x<T, WT, 8>(w, x, B, ep, ws, ni, n_sm, st);
 }
 
 }  // namespace
 
 int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
-                 cudaStream_t st) {
+                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st) {
+  const NormIn ni{norm_h, norm_w, norm_eps, norm_x2};
   if (B < 1 || B > 8) return -1;
   if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128)) return -3;
   if ((reinterpret_cast<uintptr_t>(w.p0) & 15)) return -4;
@@ -323,12 +376,12 @@ int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* w
   }();
   const StreamWs ws{ws_acc, ws_cnt, err, exp_flags};
   switch (w.type) {
-    case W_Q4_0: if (w.K % 64) return -2; return launch_stream_b<T4Block<false>, W_Q4_0>(w, x, B, ep, ws, n_sm, st);
-    case W_IQ4_NL: if (w.K % 64) return -2; return launch_stream_b<T4Block<true>, W_IQ4_NL>(w, x, B, ep, ws, n_sm, st);
-    case W_Q8_0: if (w.K % 64) return -2; return launch_stream_b<TQ8_0, W_Q8_0>(w, x, B, ep, ws, n_sm, st);
-    case W_Q4_K: if (w.K % 256) return -2; return launch_stream_b<TK45<false>, W_Q4_K>(w, x, B, ep, ws, n_sm, st);
-    case W_Q5_K: if (w.K % 256) return -2; return launch_stream_b<TK45<true>, W_Q5_K>(w, x, B, ep, ws, n_sm, st);
-    case W_Q6_K: if (w.K % 256) return -2; return launch_stream_b<TQ6_K, W_Q6_K>(w, x, B, ep, ws, n_sm, st);
+    case W_Q4_0: if (w.K % 64) return -2; return launch_stream_b<T4Block<false>, W_Q4_0>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_IQ4_NL: if (w.K % 64) return -2; return launch_stream_b<T4Block<true>, W_IQ4_NL>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_Q8_0: if (w.K % 64) return -2; return launch_stream_b<TQ8_0, W_Q8_0>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_Q4_K: if (w.K % 256) return -2; return launch_stream_b<TK45<false>, W_Q4_K>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_Q5_K: if (w.K % 256) return -2; return launch_stream_b<TK45<true>, W_Q5_K>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_Q6_K: if (w.K % 256) return -2; return launch_stream_b<TQ6_K, W_Q6_K>(w, x, B, ep, ws, ni, n_sm, st);
   }
   return -5;
 }

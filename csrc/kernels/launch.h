@@ -33,8 +33,10 @@ int* kernel_err_word();  // device error word shared by the bounded-wait kernels
 // Streaming decode GEMV (1..8 tokens): persistent, bulk-copy fed, stream-K over weight chunks.
 // ws_acc: f32 [8, N] and ws_cnt: int [N/128], both zero before the first call; the kernel leaves
 // them zero.  Calls sharing a workspace must not overlap on the GPU.  err: bounded-wait error word.
+// norm_h (optional, f32 [B, K], K <= 4096, B <= 2): the activation is computed in the kernel as
+// int8(rmsnorm(norm_h) * norm_w) (two-term if norm_x2) instead of being read from x.
 int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
-                 cudaStream_t st);
+                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st);
 void gemm_set_trace(void* p);  // diagnostics (BARQ_GEMM_EXP bit 1): [256 stages][8] u64 stamps of CTA 0
 int gemm_clear_error_word();
 

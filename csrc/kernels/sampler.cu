@@ -13,6 +13,7 @@
 // Random numbers: Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3",
 // SC 2011), keyed by the request seed and counted by (step, token index).
 #include "common.cuh"
+#include "pdl.cuh"
 #include "launch.h"
 
 namespace barq {
@@ -111,6 +112,8 @@ BARQ_DEV void block_argmax(float& v, int& idx, SampleShared& sh) {
 }
 
 __global__ void __launch_bounds__(SNT) sample_kernel(SampleArgs a) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SampleShared& sh = *reinterpret_cast<SampleShared*>(smem_raw);
   const int b = blockIdx.x;
@@ -316,7 +319,7 @@ int sample_tokens(const SampleArgs& a, cudaStream_t st) {
     cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
-  sample_kernel<<<a.B, SNT, smem, st>>>(a);
+  launch_pdl(sample_kernel, dim3(a.B), dim3(SNT), smem, st, a);
   return 0;
 }
 

@@ -88,6 +88,32 @@ def test_gemv_swiglu_epilogue(t, x2):
     assert torch.allclose(hd, h_ref, atol=h_ref.abs().max() / 100, rtol=2e-2)
 
 
+@pytest.mark.parametrize("t", [GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q8_0])
+@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("x2", [False, True])
+def test_gemv_fused_norm(t, B, x2):
+    """RMSNorm inside the streaming GEMV vs the fp32 reference of rmsnorm(h) @ W^T, with the same
+    tolerance as the unfused GEMV (the two paths may round a few activation codes differently)."""
+    N, K = 384, 2048
+    qw, ref, _ = _qw(t, N, K, seed=4)
+    h = torch.randn(B, K, device=DEV) * 3
+    nw = torch.rand(K, device=DEV) + 0.5
+    hn = (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5) * nw).cpu()
+    y_ref = hn @ ref.T
+    tol = y_ref.abs().max() * (2e-3 if x2 else 2e-2)
+    y = ops.gemv(qw, None, B, ops.EPI_STORE_F32, x2=x2, norm=(h, nw, 1e-5)).cpu()
+    assert (y - y_ref).abs().max() <= tol, (y - y_ref).abs().max()
+    _, hq = ops.rmsnorm(h.clone(), nw, 1e-5, want_q8=True, x2=x2)
+    y_unfused = ops.gemv(qw, hq, B, ops.EPI_STORE_F32, x2=x2).cpu()
+    assert (y_unfused - y_ref).abs().max() <= tol
+    if t == GGMLType.Q4_K:
+        g2, ref2, _ = _qw(t, N, K, seed=5)
+        w = ops.interleave_gate_up(qw, g2)
+        hs = _q8_deq(ops.gemv(w, None, B, ops.EPI_SWIGLU_Q8, x2=x2, norm=(h, nw, 1e-5)))
+        hs_ref = torch.nn.functional.silu(hn @ ref.T) * (hn @ ref2.T)
+        assert (hs - hs_ref).abs().max() <= hs_ref.abs().max() / 50
+
+
 def test_bf16_gemv():
     N, K, B = 100, 688, 3
     w = torch.randn(N, K) * 0.02
