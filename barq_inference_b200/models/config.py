@@ -204,6 +204,10 @@ def config_from_gguf(md: dict[str, Any], tensor_names: set[str] | None = None) -
 PRESETS: dict[str, ModelConfig] = {
     "tiny": ModelConfig(arch="llama", n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=688,
                         vocab=32000, rms_eps=1e-5, rope_theta=10000.0, max_ctx=512),
+    # test-sized MoE (Mixtral-style: 4 experts, top-2, softmax gate)
+    "tiny-moe": ModelConfig(arch="llama", n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512,
+                            vocab=4096, rms_eps=1e-5, rope_theta=10000.0, max_ctx=512, n_experts=4,
+                            n_experts_used=2, expert_ffn=256),
     "llama3-8b": ModelConfig(arch="llama", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128,
                              ffn=14336, vocab=128256, rms_eps=1e-5, rope_theta=500000.0, max_ctx=8192,
                              bos_id=128000, eos_ids=(128001, 128009)),

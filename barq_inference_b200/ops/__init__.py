@@ -235,6 +235,56 @@ def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q,
     return out
 
 
+EPI_MOE_COMBINE = 4
+
+
+class MoeRouting:
+    """Device buffers of one MoE routing call for up to ``T`` tokens, ``E`` experts, top-``k``."""
+
+    def __init__(self, T: int, E: int, k: int, H: int, dtype, device):
+        i32 = dict(dtype=torch.int32, device=device)
+        self.T, self.E, self.k = T, E, k
+        self.ids = torch.empty(T, k, **i32)
+        self.weights = torch.empty(T, k, dtype=torch.float32, device=device)
+        self.counts = torch.zeros(E, **i32)  # left zero by the kernels
+        self.cursor = torch.empty(E, **i32)
+        self.off = torch.empty(E + 1, **i32)
+        self.row_tok = torch.empty(T * k, **i32)
+        self.row_w = torch.empty(T * k, dtype=torch.float32, device=device)
+        self.xs = torch.empty(T * k, H, dtype=dtype, device=device)
+
+
+def moe_route(logits: torch.Tensor, x: torch.Tensor, k: int, r: MoeRouting, sigmoid: bool = False,
+              renorm: bool = True, n_group: int = 1, topk_group: int = 1, ser_threshold: float = 0.0,
+              scale: float = 1.0) -> MoeRouting:
+    """Gate + top-k + SER + dispatch of x's rows into expert-major ``r.xs`` (see csrc/kernels/moe.cu)."""
+    T = logits.shape[0]
+    require_ext().moe_route(logits.contiguous(), k, int(sigmoid), int(renorm), n_group, topk_group, ser_threshold,
+                            scale, x.contiguous(), r.ids[:T], r.weights[:T], r.counts, r.cursor, r.off,
+                            r.row_tok, r.row_w, r.xs)
+    _count(3)
+    return r
+
+
+def gemm_grouped(w: QWeight, x: torch.Tensor, off: torch.Tensor, n_groups: int, mode: int,
+                 out: torch.Tensor | None = None, row_tok=None, row_w=None) -> torch.Tensor:
+    """Grouped (per-expert) tcgen05 GEMM over x rows sorted by group (``off`` [n_groups+1] on device).
+    SwiGLU mode returns x.dtype [rows, grows/2]; EPI_MOE_COMBINE adds into ``out`` (f32 [tokens, grows])."""
+    Tr = x.shape[0]
+    grows = w.N // n_groups
+    if mode == EPI_SWIGLU_Q8:
+        if out is None:
+            out = torch.empty(Tr, grows // 2, dtype=x.dtype, device=x.device)
+        act, f32, ld = out, None, out.stride(0)
+    else:
+        if out is None:
+            raise ValueError("gemm_grouped: the combine mode adds into an existing output")
+        act, f32, ld = None, out, out.stride(0)
+    require_ext().qgemm_grouped(*w.args(), x, Tr, mode, f32, act, ld, off, n_groups, grows, row_tok, row_w)
+    _count()
+    return out
+
+
 def embed(w: QWeight, ids: torch.Tensor) -> torch.Tensor:
     out = torch.empty(ids.numel(), w.K, dtype=torch.float32, device=ids.device)
     require_ext().embed_gather(*w.args(), ids, out)

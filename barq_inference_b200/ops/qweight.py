@@ -131,6 +131,20 @@ class QWeight:
         g = lambda x: None if x is None else x.index_select(0, idx).contiguous()  # noqa: E731
         return QWeight(self.wtype, int(idx.numel()), self.K, g(self.p0), g(self.p1), g(self.p2), g(self.d), self.src_type)
 
+    def row_slice(self, r0: int, n: int) -> "QWeight":
+        """Rows [r0, r0+n) as a view of the tiled buffer (r0, n multiples of 128), e.g. one expert of a
+        stacked expert tensor."""
+        if self.wtype == W_BF16:
+            return QWeight(W_BF16, n, self.K, self.p0[r0:r0 + n], None, None, None, self.src_type)
+        if r0 % 128 or n % 128:
+            raise ValueError("row_slice: rows must be multiples of 128")
+        self.finalize()
+        G, _ = TILE_FMT[self.wtype]
+        per_tile = self.tiled.numel() // ((self.N + 127) // 128)
+        q = QWeight(self.wtype, n, self.K, None, None, None, None, self.src_type)
+        q.tiled = self.tiled[(r0 // 128) * per_tile:(r0 + n) // 128 * per_tile]
+        return q
+
     def col_shard(self, k0: int, k1: int) -> "QWeight":
         """Columns [k0, k1) (block-aligned) — row-parallel sharding for tensor parallelism."""
         self = self._planar()

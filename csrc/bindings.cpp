@@ -80,6 +80,51 @@ void qgemm(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT
   check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, (int)k_splits, cur_stream()), "qgemm");
 }
 
+// Grouped (MoE expert) GEMM: w holds ng groups of grows rows; x [Ttot, K] rows sorted by group.
+void qgemm_grouped(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor x, int64_t T,
+                   int64_t mode, OptT out_f32, OptT out_act, int64_t ld_out, Tensor off, int64_t ng, int64_t grows,
+                   OptT row_tok, OptT row_w) {
+  c10::cuda::CUDAGuard g(p0.device());
+  const bool f16 = x.scalar_type() == torch::kHalf;
+  TORCH_CHECK((f16 || x.scalar_type() == torch::kBFloat16) && x.is_contiguous() && x.size(-1) == K,
+              "qgemm_grouped: x must be fp16 or bf16 [T, K]");
+  TORCH_CHECK(off.scalar_type() == torch::kInt32 && off.numel() >= ng + 1, "qgemm_grouped: off must be int32 [ng+1]");
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_act), barq::ActOut{}, nullptr,
+                   (int)ld_out};
+  barq::GemmGroups grp{ptr<const int>(off), (int)ng, (int)grows, optptr<const int>(row_tok),
+                       optptr<const float>(row_w)};
+  check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, 1, cur_stream(), &grp), "qgemm_grouped");
+}
+
+void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_t n_group, int64_t topk_group,
+               double ser_threshold, double scale, Tensor x, Tensor ids, Tensor weights, Tensor counts, Tensor cursor,
+               Tensor off, Tensor row_tok, Tensor row_w, Tensor xs) {
+  c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "moe_route: logits f32 [T, E]");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16, "moe_route: x fp16/bf16");
+  barq::MoeRouteArgs a;
+  a.logits = ptr<const float>(logits);
+  a.T = (int)logits.size(0);
+  a.E = (int)logits.size(1);
+  a.k = (int)k;
+  a.H = (int)x.size(1);
+  a.sigmoid = (int)sigmoid;
+  a.renorm = (int)renorm;
+  a.n_group = (int)n_group;
+  a.topk_group = (int)topk_group;
+  a.ser_threshold = (float)ser_threshold;
+  a.scale = (float)scale;
+  a.ids = ptr<int>(ids);
+  a.weights = ptr<float>(weights);
+  a.counts = ptr<int>(counts);
+  a.cursor = ptr<int>(cursor);
+  a.off = ptr<int>(off);
+  a.row_tok = ptr<int>(row_tok);
+  a.row_w = ptr<float>(row_w);
+  check(barq::moe_route(a, x.data_ptr(), x.scalar_type() == torch::kHalf, xs.data_ptr(), cur_stream()), "moe_route");
+}
+
 int64_t gemm_error() {
   int v = 0;
   TORCH_CHECK(barq::gemm_error_word(&v) == 0, "gemm_error: read failed");
@@ -231,6 +276,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("qgemm", &qgemm);
   m.def("gemm_error", &gemm_error);
+  m.def("qgemm_grouped", &qgemm_grouped);
+  m.def("moe_route", &moe_route);
   m.def("gemm_clear_error", &gemm_clear_error);
   m.def("gemm_set_trace", [](Tensor t) { barq::gemm_set_trace(t.data_ptr()); });
   m.def("quantize_q8", &quantize_q8);

@@ -52,6 +52,14 @@ struct GemmDev {
   int ld_out;
   int k_splits;
   int* err;
+  // Grouped (MoE) mode, ng > 0: the weight holds ng groups of grows rows (one expert each); the
+  // activation rows are sorted by group, group e owning rows [goff[e], goff[e+1]) (device memory,
+  // written by the routing kernels).  Output columns are group-local (0..grows).  EPI_MOE_COMBINE
+  // adds row_w[row] * result into out_f32[row_tok[row], :] with atomics.
+  const int* goff;
+  int ng, grows;
+  const int* row_tok;
+  const float* row_w;
   int exp;  // diagnostics: bit 0 = skip the dequant arithmetic (write zeros), bit 1 = trace CTA 0
   unsigned long long* trace;  // [kTraceStages][8] globaltimer stamps when tracing
 };
@@ -299,13 +307,41 @@ struct Issuers {
   static constexpr int COLS = TS ? 512 : 2 * NI * BN;
 };
 
+constexpr int kMaxGroups = 256;
+
+// One output tile: global weight tile nt, K split z, activation/output rows [row0, row0 + rows),
+// output column base n0.
+struct Tile {
+  int nt, z, row0, rows, n0;
+};
+
+template <int BN>
 struct TileMap {
-  int n_tiles, t_tiles, ks, total;
-  BARQ_DEV void decode(int u, int& nt, int& tt, int& z) const {
-    nt = u % n_tiles;  // weight tiles fastest: concurrent CTAs share one activation tile in L2
-    const int rest = u / n_tiles;
-    z = rest % ks;
-    tt = rest / ks;
+  int n_tiles, t_tiles, ks, total, T;
+  int ng, ntg;                   // grouped: groups, weight tiles per group
+  const int* off;                // [ng+1] activation row offsets (smem)
+  const int* tcum;               // [ng+1] prefix of tiles per group (smem)
+  BARQ_DEV Tile decode(int u) const {
+    Tile t;
+    if (ng == 0) {
+      t.nt = u % n_tiles;  // weight tiles fastest: concurrent CTAs share one activation tile in L2
+      const int rest = u / n_tiles;
+      t.z = rest % ks;
+      const int tt = rest / ks;
+      t.row0 = tt * BN;
+      t.rows = min(BN, T - t.row0);
+      t.n0 = t.nt * 128;
+    } else {
+      int e = 0;
+      while (tcum[e + 1] <= u) ++e;
+      const int local = u - tcum[e], ntl = local % ntg, tt = local / ntg;
+      t.nt = e * ntg + ntl;
+      t.z = 0;
+      t.row0 = off[e] + tt * BN;
+      t.rows = min(BN, off[e + 1] - t.row0);
+      t.n0 = ntl * 128;
+    }
+    return t;
   }
 };
 
@@ -332,11 +368,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int err_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  TileMap tm;
+  __shared__ int goff_s[kMaxGroups + 1], gcum_s[kMaxGroups + 1];
+  TileMap<BN> tm;
   tm.n_tiles = (g.N + 127) / 128;
   tm.t_tiles = (g.T + BN - 1) / BN;
   tm.ks = g.k_splits;
   tm.total = tm.n_tiles * tm.t_tiles * tm.ks;
+  tm.T = g.T;
+  tm.ng = g.ng;
+  tm.ntg = g.grows / 128;
+  tm.off = goff_s;
+  tm.tcum = gcum_s;
+  if (g.ng > 0) {
+    // Grouped: the group offsets come from the previous kernel, so every role waits for it here.
+    pdl_wait();
+    for (int i = threadIdx.x; i <= g.ng; i += blockDim.x) goff_s[i] = g.goff[i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0;
+      for (int e = 0; e < g.ng; ++e) {
+        gcum_s[e] = cum;
+        cum += (goff_s[e + 1] - goff_s[e] + BN - 1) / BN * tm.ntg;
+      }
+      gcum_s[g.ng] = cum;
+    }
+    __syncthreads();
+    tm.total = gcum_s[g.ng];
+  }
   const int KG = g.K / F::G;
   auto grange = [&](int z, int& gb, int& ge) {
     gb = (int)((long)KG * z / g.k_splits);
@@ -378,8 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int qc = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
-        int nt, tt, z, gb, ge;
-        tm.decode(u, nt, tt, z);
+        const Tile tl = tm.decode(u);
+        const int nt = tl.nt, z = tl.z;
+        int gb, ge;
         grange(z, gb, ge);
         bool ok = true;
         for (int kg = gb; kg < ge; ++kg, ++qc) {
@@ -403,8 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tx);
       int it = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
-        int nt, tt, z, gb, ge;
-        tm.decode(u, nt, tt, z);
+        const Tile tl = tm.decode(u);
+        const int nt = tl.nt, z = tl.z;
+        int gb, ge;
         grange(z, gb, ge);
         bool ok = true;
         for (int ks = gb * SPG; ks < ge * SPG; ++ks, ++it) {
@@ -420,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_expect_tx(&full[s], L::B_BYTES);
 #pragma unroll
             for (int a = 0; a < KS; ++a)
-              tma_load_2d(smem + L::OFF_B + s * L::B_BYTES + a * L::B_ATOM, &tx, 64 * (ks * KS + a), tt * BN, &full[s]);
+              tma_load_2d(smem + L::OFF_B + s * L::B_BYTES + a * L::B_ATOM, &tx, 64 * (ks * KS + a), tl.row0, &full[s]);
           }
         }
         if (!ok) break;
@@ -435,8 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = F16 ? idesc_f16(128, BN) : idesc_bf16(128, BN);
       int it = 0, tc = 0;
       for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x, ++tc) {
-        int nt, tt, z, gb, ge;
-        tm.decode(u, nt, tt, z);
+        const Tile tl = tm.decode(u);
+        const int nt = tl.nt, z = tl.z;
+        int gb, ge;
         grange(z, gb, ge);
         const int buf = tc & 1, use = tc >> 1;
         const int nst = (ge - gb) * SPG;
@@ -487,8 +548,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, qc = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < tm.total && ok && !*err; u += gridDim.x) {
-      int nt, tt, z, gb, ge;
-      tm.decode(u, nt, tt, z);
+      const Tile tl = tm.decode(u);
+      const int nt = tl.nt, z = tl.z;
+      int gb, ge;
       grange(z, gb, ge);
       for (int kg = gb; kg < ge && ok; ++kg, ++qc) {
         const int qs = qc % SQ, qph = (qc / SQ) & 1;
@@ -576,8 +638,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     int tc = 0;
     for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
-      int nt, tt, z, gb, ge;
-      tm.decode(u, nt, tt, z);
+      const Tile tl = tm.decode(u);
+      const int nt = tl.nt, z = tl.z;
+      int gb, ge;
       grange(z, gb, ge);
       const int nacc = (ge - gb) * SPG < NI ? (ge - gb) * SPG : NI;  // issuers that wrote this tile
       const int buf = tc & 1, use = tc >> 1;
@@ -586,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // All 128 epilogue threads agree on stopping (the error word only ever grows).
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (*err) break;
-      const int n0 = nt * 128, t0 = tt * BN, n = n0 + r;
+      const int n0 = tl.n0, t0 = tl.row0, t_end = tl.row0 + tl.rows, n = n0 + r;
       const uint32_t acc = tmem + (uint32_t)(buf * NI * BN) + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
@@ -609,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int t = t0 + c0 + j;
-              if (t < g.T && f < g.N / 2)
+              if (t < t_end && f < g.N / 2)
                 out_act[(size_t)t * g.ld_out + f] = from_f<AT>(silu(v[j]) * up[j * 32 + lane]);
             }
           }
@@ -621,10 +684,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int t = t0 + c0 + j;
-            if (t >= g.T) continue;
+            if (t >= t_end) continue;
             const size_t idx = (size_t)t * g.ld_out + n;
             const float val = v[j] + bias;
-            if (g.mode == EPI_STORE_BF16) {
+            if (g.mode == EPI_MOE_COMBINE) {
+              atomicAdd(g.out_f32 + (size_t)g.row_tok[t] * g.ld_out + n, g.row_w[t] * val);
+            } else if (g.mode == EPI_STORE_BF16) {
               out_act[idx] = from_f<AT>(val);
             } else if (atomic) {
               atomicAdd(g.out_f32 + idx, val);
@@ -720,11 +785,11 @@ static int sm_count() {
 template <int WT, int BN, int S, int SQ, int KS, bool F16>
 static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cudaStream_t st) {
   using L = GemmSmem<WT, BN, S, SQ, KS>;
-  static_assert(L::TOTAL <= 232448, "shared memory budget");
+  static_assert(L::TOTAL + 4096 <= 232448, "shared memory budget (dynamic + static)");
   auto kern = qgemm_tc_kernel<WT, BN, S, SQ, KS, F16>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-  const int total = ((g.N + 127) / 128) * tiles_t * g.k_splits;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess) return -21;
   const int n = sm_count();
+  const int total = g.ng ? n : ((g.N + 127) / 128) * tiles_t * g.k_splits;  // grouped: sized on the device
   return launch_pdl(kern, dim3(total < n ? total : n), dim3(kThreads), (size_t)L::TOTAL, st, tx, g) == cudaSuccess ? 0
                                                                                                           : -20;
 }
@@ -734,7 +799,8 @@ static int launch_gemm(const CUtensorMap& tx, const GemmDev& g, int tiles_t, cud
 template <int WT, int BN, int S, int KS>
 constexpr int chunk_slots() {
   using L = GemmSmem<WT, BN, S, 1, KS>;
-  constexpr int fixed = L::OFF_Q + L::XCH_BYTES + (2 + 2 * S + 4) * 8 + 16 + 1024 + 1024;
+  // + static shared memory of the kernel (grouped-GEMM tables, error word): 4 KB reserved
+  constexpr int fixed = L::OFF_Q + L::XCH_BYTES + (2 + 2 * S + 4) * 8 + 16 + 1024 + 1024 + 4096;
   constexpr int n = (232448 - fixed) / L::Q_BYTES;
   return n > 8 ? 8 : n;
 }
@@ -746,7 +812,8 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   // the MMA thread issues 8 MMAs per barrier round instead of 4
   constexpr int KSW = F::G >= 128 ? 2 : 1;
   GemmDev g = g0;
-  const int bn = g.T <= 64 ? 64 : (g.T <= 128 ? 128 : 256);
+  const int rows_per_tile = g.ng ? (g.T + g.ng - 1) / g.ng : g.T;  // grouped: mean rows per group
+  const int bn = rows_per_tile <= 64 ? 64 : (rows_per_tile <= 128 ? 128 : 256);
   CUtensorMap mx;
   int rc = make_act_map(&mx, x, F16, g.K, g.T, bn);
   if (rc) return rc;
@@ -786,16 +853,29 @@ static int dispatch_type(int type, const void* x, const GemmDev& g, cudaStream_t
 static unsigned long long* g_trace = nullptr;
 void gemm_set_trace(void* p) { g_trace = reinterpret_cast<unsigned long long*>(p); }
 
-int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st) {
+int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st,
+             const GemmGroups* grp) {
   if (T <= 0) return 0;
+  if (grp) {
+    if (grp->ng <= 0 || grp->ng > kMaxGroups || grp->grows % 128 || (long)grp->ng * grp->grows != w.N) return -8;
+    if (ep.mode == EPI_MOE_COMBINE && (!grp->row_tok || !grp->row_w)) return -9;
+    k_splits = 1;
+  } else if (ep.mode == EPI_MOE_COMBINE) {
+    return -9;
+  }
   const int G = (w.type == W_Q4_K || w.type == W_Q5_K || w.type == W_Q6_K) ? 256 : 64;
   if (w.K % G) return -2;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w.p0) & 15)) return -3;
-  if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128 || k_splits > 1)) return -4;
+  if (ep.mode == EPI_SWIGLU_Q8 && ((grp ? grp->grows : w.N) % 128 || k_splits > 1)) return -4;
   if (ep.mode == EPI_SWIGLU_Q8 || ep.mode == EPI_STORE_BF16) k_splits = 1;
   if (k_splits < 0) k_splits = 0;
   GemmDev g;
-  g.N = w.N;
+  g.N = grp ? grp->grows : w.N;
+  g.goff = grp ? grp->off : nullptr;
+  g.ng = grp ? grp->ng : 0;
+  g.grows = grp ? grp->grows : 0;
+  g.row_tok = grp ? grp->row_tok : nullptr;
+  g.row_w = grp ? grp->row_w : nullptr;
   g.K = w.K;
   g.T = T;
   g.w = w.p0;

@@ -8,7 +8,7 @@
 
 namespace barq {
 
-enum EpiMode : int { EPI_STORE_F32 = 0, EPI_ADD_F32 = 1, EPI_STORE_BF16 = 2, EPI_SWIGLU_Q8 = 3 };
+enum EpiMode : int { EPI_STORE_F32 = 0, EPI_ADD_F32 = 1, EPI_STORE_BF16 = 2, EPI_SWIGLU_Q8 = 3, EPI_MOE_COMBINE = 4 };
 
 struct GemvEpi {
   int mode;
@@ -27,7 +27,35 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
 // 0 = automatic (f32 modes only; accumulated with atomics).
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
-int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st);
+// MoE routing + dispatch (moe.cu).  logits f32 [T, E] -> ids/weights [T, k]; rows of x (fp16/bf16
+// [T, H]) are copied into xs [T*k, H] sorted by expert, off [E+1] holds each expert's row range, and
+// row_tok / row_w the source token and gate weight of each row.  counts [E] must be zero before the
+// first call (the kernels leave them zero); cursor [E] is scratch.
+struct MoeRouteArgs {
+  const float* logits;
+  int T, E, k, H;
+  int sigmoid, renorm, n_group, topk_group;
+  float ser_threshold, scale;
+  int* ids;
+  float* weights;
+  int* counts;
+  int* cursor;
+  int* off;
+  int* row_tok;
+  float* row_w;
+};
+int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st);
+
+// Grouped (MoE expert) GEMM: the weight is ng stacked groups of grows rows; activation rows sorted by
+// group with device offsets off[ng+1]; EPI_MOE_COMBINE scatters row_w[r] * y[r, :] into out row row_tok[r].
+struct GemmGroups {
+  const int* off;
+  int ng, grows;
+  const int* row_tok;
+  const float* row_w;
+};
+int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st,
+             const GemmGroups* grp = nullptr);
 int gemm_error_word(int* host_out);
 int* kernel_err_word();  // device error word shared by the bounded-wait kernels (per device)
 // Streaming decode GEMV (1..8 tokens): persistent, bulk-copy fed, stream-K over weight chunks.

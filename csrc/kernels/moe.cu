@@ -1,0 +1,203 @@
+// K5 (single-GPU part): MoE routing and dispatch.  The expert GEMMs are the grouped mode of the
+// tcgen05 GEMM (gemm_tc.cu) and the combine is that GEMM's EPI_MOE_COMBINE epilogue.
+//
+// Parity: the reference routes on the CPU (models/src/moe_fused.rs:95-193 top-k + SER,
+// models/src/deepseek.rs:140-163 DeepSeek routing) and runs each expert as a separate matmul;
+// here routing, the token permutation and the weighted combine stay on the device, so a MoE layer is
+// three small kernels plus two grouped GEMMs and needs no device->host copy (CUDA-graph friendly).
+//
+//   moe_route_kernel     one warp per token: gate (softmax | sigmoid) over E logits, optional
+//                        group-limited selection (keep the best topk_group of n_group groups), top-k,
+//                        renormalization, SER drop (weights below a threshold, the top expert is
+//                        always kept), scale; per-expert counts with atomics.
+//   moe_scan_kernel      one block: counts -> row offsets [E+1], cursors, counts cleared.
+//   moe_dispatch_kernel  one block per (token, slot): claims a row of its expert and copies the
+//                        token's activation row there; records (token, weight) for the combine.
+#include "common.cuh"
+#include "launch.h"
+#include "pdl.cuh"
+
+namespace barq {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 8;
+
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= a.T) return;
+  const float* lg = a.logits + (size_t)t * a.E;
+  constexpr int PER = kMaxExperts / 32;
+  float p[PER];
+  // gate probabilities (lane holds experts lane, lane+32, ...)
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = e < a.E ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, p[i]);
+  }
+  if (a.sigmoid) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) p[i] = (lane + 32 * i) < a.E ? 1.f / (1.f + __expf(-p[i])) : -INFINITY;
+  } else {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      p[i] = (lane + 32 * i) < a.E ? __expf(p[i] - mx) : 0.f;
+      sum += p[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) p[i] = (lane + 32 * i) < a.E ? p[i] * inv : -INFINITY;
+  }
+  // group-limited routing: experts outside the best topk_group groups (by their best expert) drop out
+  if (a.n_group > 1 && a.topk_group < a.n_group) {
+    const int gsz = a.E / a.n_group;
+    __shared__ float gbest[8][64];
+    for (int gi = 0; gi < a.n_group; ++gi) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        if (e < a.E && e / gsz == gi) m = fmaxf(m, p[i]);
+      }
+      m = warp_max(m);
+      if (lane == 0) gbest[warp][gi] = m;
+    }
+    __syncwarp();
+    unsigned long long keep = 0;  // groups kept (n_group <= 64)
+    for (int r = 0; r < a.topk_group; ++r) {
+      int best = -1;
+      float bv = -INFINITY;
+      for (int gi = 0; gi < a.n_group; ++gi)
+        if (!((keep >> gi) & 1ull) && gbest[warp][gi] > bv) {
+          bv = gbest[warp][gi];
+          best = gi;
+        }
+      if (best >= 0) keep |= 1ull << best;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e < a.E && !((keep >> (e / gsz)) & 1ull)) p[i] = -INFINITY;
+    }
+  }
+  // top-k by repeated warp argmax (ties: lower expert id)
+  int ids[kMaxTopK];
+  float ws[kMaxTopK];
+  float wsum = 0.f;
+  for (int j = 0; j < a.k; ++j) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (p[i] > bv || (p[i] == bv && e < be)) {
+        bv = p[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    ids[j] = be;
+    ws[j] = bv;
+    wsum += bv;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i == be) p[i] = -INFINITY;
+  }
+  if (a.renorm) {
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    for (int j = 0; j < a.k; ++j) ws[j] *= inv;
+  }
+  if (a.ser_threshold > 0.f) {  // smart expert reduction: drop weak experts, renormalize the rest
+    float s = 0.f;
+    for (int j = 0; j < a.k; ++j) {
+      if (j > 0 && ws[j] < a.ser_threshold) ws[j] = 0.f;
+      s += ws[j];
+    }
+    const float inv = s > 0.f ? 1.f / s : 0.f;
+    for (int j = 0; j < a.k; ++j) ws[j] *= inv;
+  }
+  if (lane == 0) {
+    for (int j = 0; j < a.k; ++j) {
+      const float wj = ws[j] * a.scale;
+      a.ids[(size_t)t * a.k + j] = ids[j];
+      a.weights[(size_t)t * a.k + j] = wj;
+      if (ws[j] > 0.f) atomicAdd(a.counts + ids[j], 1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) moe_scan_kernel(MoeRouteArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int c[kMaxExperts];
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) c[e] = a.counts[e];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < a.E; ++e) {
+      a.off[e] = run;
+      a.cursor[e] = run;
+      run += c[e];
+    }
+    a.off[a.E] = run;
+  }
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.counts[e] = 0;  // ready for the next call
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) moe_dispatch_kernel(MoeRouteArgs a, const T* __restrict__ x,
+                                                           T* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x / a.k, j = blockIdx.x % a.k;
+  const float wj = a.weights[(size_t)t * a.k + j];
+  if (wj == 0.f) return;  // dropped by SER
+  __shared__ int row_s;
+  if (threadIdx.x == 0) {
+    const int e = a.ids[(size_t)t * a.k + j];
+    const int row = atomicAdd(a.cursor + e, 1);
+    a.row_tok[row] = t;
+    a.row_w[row] = wj;
+    row_s = row;
+  }
+  __syncthreads();
+  const int row = row_s;
+  const int4* src = reinterpret_cast<const int4*>(x + (size_t)t * a.H);
+  int4* dst = reinterpret_cast<int4*>(xs + (size_t)row * a.H);
+  for (int i = threadIdx.x; i < a.H * (int)sizeof(T) / 16; i += blockDim.x) dst[i] = src[i];
+}
+
+int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st) {
+  if (a.E <= 0 || a.E > kMaxExperts || a.k <= 0 || a.k > kMaxTopK || a.k > a.E) return -1;
+  if (a.n_group > 64 || (a.n_group > 1 && a.E % a.n_group)) return -2;
+  if ((a.H * 2) % 16) return -3;
+  if (a.T <= 0) return 0;
+  cudaError_t e = launch_pdl(moe_route_kernel, dim3((a.T + 7) / 8), dim3(256), 0, st, a);
+  if (e == cudaSuccess) e = launch_pdl(moe_scan_kernel, dim3(1), dim3(256), 0, st, a);
+  if (e == cudaSuccess) {
+    if (x_is_f16)
+      e = launch_pdl(moe_dispatch_kernel<__half>, dim3(a.T * a.k), dim3(128), 0, st, a,
+                     static_cast<const __half*>(x), static_cast<__half*>(xs));
+    else
+      e = launch_pdl(moe_dispatch_kernel<__nv_bfloat16>, dim3(a.T * a.k), dim3(128), 0, st, a,
+                     static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(xs));
+  }
+  return e == cudaSuccess ? 0 : -20;
+}
+
+}  // namespace barq
