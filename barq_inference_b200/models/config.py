@@ -208,6 +208,12 @@ PRESETS: dict[str, ModelConfig] = {
     "tiny-moe": ModelConfig(arch="llama", n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512,
                             vocab=4096, rms_eps=1e-5, rope_theta=10000.0, max_ctx=512, n_experts=4,
                             n_experts_used=2, expert_ffn=256),
+    # test-sized DeepSeek-V2 (MLA with the real 16 heads / 512 latent / 64 rope; 1 dense + 1 MoE layer)
+    "tiny-ds": ModelConfig(arch="deepseek2", n_layers=2, hidden=256, n_heads=16, n_kv_heads=16, head_dim=192,
+                           ffn=512, vocab=4096, rms_eps=1e-6, rope_theta=10000.0, max_ctx=512, n_experts=4,
+                           n_experts_used=2, expert_ffn=256, n_shared_experts=1, n_dense_layers=1,
+                           expert_weights_norm=False, kv_lora_rank=512, qk_nope_dim=128, qk_rope_dim=64,
+                           v_head_dim=128, bos_id=1, eos_ids=(2,)),
     "llama3-8b": ModelConfig(arch="llama", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128,
                              ffn=14336, vocab=128256, rms_eps=1e-5, rope_theta=500000.0, max_ctx=8192,
                              bos_id=128000, eos_ids=(128001, 128009)),

@@ -47,6 +47,7 @@ class QuantPolicy:
 
 POLICIES = {
     "tiny": QuantPolicy(default=GGMLType.Q4_0, output=GGMLType.Q8_0, embed=GGMLType.Q8_0),
+    "tiny-ds": QuantPolicy(default=GGMLType.Q4_K, attn=GGMLType.Q8_0, output=GGMLType.Q8_0, embed=GGMLType.Q8_0),
     "tiny-moe": QuantPolicy(default=GGMLType.Q4_K, output=GGMLType.Q8_0, embed=GGMLType.Q8_0),
     "llama3-8b": QuantPolicy(default=GGMLType.Q4_K, output=GGMLType.Q6_K),
     "llama3-70b": QuantPolicy(default=GGMLType.Q4_K, attn=GGMLType.Q6_K, output=GGMLType.Q6_K),

@@ -235,6 +235,28 @@ def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q,
     return out
 
 
+def mla_kv_write(kv_a: torch.Tensor, norm_w: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor,
+                 neox: bool, pos: torch.Tensor, slots: torch.Tensor, cache: torch.Tensor, q: torch.Tensor, H: int,
+                 qdim: int, rope_off: int) -> None:
+    """MLA: latent rows (rmsnorm(c) | rope(k_pe)) into the paged cache; q's rope part rotated in place."""
+    require_ext().mla_kv_write(kv_a.contiguous(), norm_w, eps, cos, sin, int(neox), pos, slots, cache, q, H, qdim,
+                               rope_off)
+    _count()
+
+
+def mla_attention(q_lat: torch.Tensor, q: torch.Tensor, qdim: int, rope_off: int, cache: torch.Tensor,
+                  block_tables: torch.Tensor, row_seq: torch.Tensor, row_len: torch.Tensor, H: int, splits: int,
+                  scale: float) -> torch.Tensor:
+    """Absorbed MLA attention (K10): returns o_lat f32 [rows, H, 512]."""
+    C = require_ext()
+    rows = q_lat.shape[0]
+    scratch = torch.empty(C.mla_attn_scratch_floats(rows, splits), dtype=torch.float32, device=q_lat.device)
+    o = torch.empty(rows, H, 512, dtype=torch.float32, device=q_lat.device)
+    C.mla_attention(q_lat, q, qdim, rope_off, cache, block_tables, row_seq, row_len, H, splits, scale, scratch, o)
+    _count(2)
+    return o
+
+
 EPI_MOE_COMBINE = 4
 
 

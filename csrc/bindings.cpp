@@ -125,6 +125,45 @@ void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_
   check(barq::moe_route(a, x.data_ptr(), x.scalar_type() == torch::kHalf, xs.data_ptr(), cur_stream()), "moe_route");
 }
 
+void mla_kv_write(Tensor kv_a, Tensor norm_w, double eps, Tensor cos, Tensor sin, int64_t neox, Tensor pos,
+                  Tensor slots, Tensor cache, Tensor q, int64_t H, int64_t qdim, int64_t rope_off) {
+  c10::cuda::CUDAGuard g(kv_a.device());
+  TORCH_CHECK(kv_a.size(-1) == 576 && cache.size(-1) == 576, "mla_kv_write: latent rows are 576 wide");
+  barq::MlaKvArgs a{ptr<const float>(kv_a), ptr<const float>(norm_w), (float)eps, ptr<const float>(cos),
+                    ptr<const float>(sin), (int)neox, ptr<const int>(pos), ptr<const int64_t>(slots),
+                    cache.data_ptr(), ptr<float>(q), (int)kv_a.size(0), (int)H, (int)qdim, (int)rope_off};
+  check(barq::mla_kv_write(a, cache.scalar_type() == torch::kBFloat16, cur_stream()), "mla_kv_write");
+}
+
+int64_t mla_attn_scratch_floats(int64_t rows, int64_t splits) {
+  return (int64_t)barq::mla_attn_scratch_floats((int)rows, (int)splits);
+}
+
+void mla_attention(Tensor q_lat, Tensor q, int64_t qdim, int64_t rope_off, Tensor cache, Tensor block_tables,
+                   Tensor row_seq, Tensor row_len, int64_t H, int64_t splits, double scale, Tensor scratch,
+                   Tensor o_lat) {
+  c10::cuda::CUDAGuard g(q_lat.device());
+  const int rows = (int)q_lat.size(0);
+  TORCH_CHECK((size_t)scratch.numel() >= barq::mla_attn_scratch_floats(rows, (int)splits), "mla: scratch too small");
+  barq::MlaAttnArgs a;
+  a.q_lat = ptr<const float>(q_lat);
+  a.q_pe = ptr<const float>(q) + rope_off;
+  a.q_pe_stride = (int)qdim;
+  a.cache = cache.data_ptr();
+  a.block_tables = ptr<const int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.row_seq = ptr<const int>(row_seq);
+  a.row_len = ptr<const int>(row_len);
+  a.rows = rows;
+  a.H = (int)H;
+  a.splits = (int)splits;
+  a.scale = (float)scale;
+  a.part_acc = ptr<float>(scratch);
+  a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)rows * splits * H * 512);
+  a.o_lat = ptr<float>(o_lat);
+  check(barq::mla_attention(a, cache.scalar_type() == torch::kBFloat16, cur_stream()), "mla_attention");
+}
+
 int64_t gemm_error() {
   int v = 0;
   TORCH_CHECK(barq::gemm_error_word(&v) == 0, "gemm_error: read failed");
@@ -278,6 +317,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error", &gemm_error);
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
+  m.def("mla_kv_write", &mla_kv_write);
+  m.def("mla_attn_scratch_floats", &mla_attn_scratch_floats);
+  m.def("mla_attention", &mla_attention);
   m.def("gemm_clear_error", &gemm_clear_error);
   m.def("gemm_set_trace", [](Tensor t) { barq::gemm_set_trace(t.data_ptr()); });
   m.def("quantize_q8", &quantize_q8);

@@ -27,6 +27,40 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
 // 0 = automatic (f32 modes only; accumulated with atomics).
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
+// DeepSeek-V2 MLA (mla.cu).  Latent cache rows: [c (512) | k_pe (64)], 16 tokens per page.
+struct MlaKvArgs {
+  const float* kv_a;    // [T, 576] kv_a_mqa projection
+  const float* norm_w;  // [512] attn_kv_a_norm
+  float eps;
+  const float* cos;     // [max_pos, 32] (YaRN mscale folded in)
+  const float* sin;
+  int neox;
+  const int* pos;       // [T]
+  const int64_t* slots; // [T] cache slot = block * 16 + offset
+  void* cache;          // [blocks, 16, 576] fp16 / bf16
+  float* q;             // [T, H, qdim] f32; rope part rotated in place
+  int T, H, qdim, rope_off;
+};
+int mla_kv_write(const MlaKvArgs& a, int cache_is_bf16, cudaStream_t st);
+
+struct MlaAttnArgs {
+  const float* q_lat;  // [rows, H, 512] absorbed queries
+  const float* q_pe;   // rows of [H, q_pe_stride]: rotated rope part at offset 0 (pointer pre-offset)
+  int q_pe_stride;     // floats between consecutive heads' q_pe (qdim)
+  const void* cache;
+  const int* block_tables;  // [S, max_blocks]
+  int max_blocks;
+  const int* row_seq;  // [rows] sequence of each query row
+  const int* row_len;  // [rows] visible cache tokens (causal: position + 1)
+  int rows, H, splits;
+  float scale;
+  float* part_acc;     // scratch [rows, splits, H, 512]
+  float2* part_ml;     // scratch [rows, splits, H]
+  float* o_lat;        // [rows, H, 512]
+};
+size_t mla_attn_scratch_floats(int rows, int splits);
+int mla_attention(const MlaAttnArgs& a, int cache_is_bf16, cudaStream_t st);
+
 // MoE routing + dispatch (moe.cu).  logits f32 [T, E] -> ids/weights [T, k]; rows of x (fp16/bf16
 // [T, H]) are copied into xs [T*k, H] sorted by expert, off [E+1] holds each expert's row range, and
 // row_tok / row_w the source token and gate weight of each row.  counts [E] must be zero before the

@@ -70,3 +70,45 @@ def test_tiny_moe_logits_match_reference(fused):
         pos += 1
         worst = max(worst, (lg - ref_logits[i + 1]).abs().max().item())
     assert worst < 2e-2, worst
+
+
+def test_tiny_deepseek_mla_logits_match_reference():
+    """DeepSeek-V2 runner (latent cache, absorbed MLA kernel, dense + MoE with a shared expert)."""
+    from barq_inference_b200.models.deepseek2 import DeepseekV2Runner
+
+    cfg = preset("tiny-ds")
+    tensors = random_tensors(cfg, POLICIES["tiny-ds"], seed=5)
+    ref = ReferenceModel(cfg, tensors)
+    g = torch.Generator().manual_seed(9)
+    prompt = torch.randint(0, cfg.vocab, (40,), generator=g).tolist()
+    ref_tokens, ref_logits = ref.greedy(prompt, 5)
+    runner = DeepseekV2Runner(cfg, tensors, DEV)
+    runner.allocate_kv(32)
+    table = list(range(1, 10))
+    lg = _run(runner, prompt, 0, table, decode=False)
+    worst = (lg - ref_logits[0]).abs().max().item()
+    pos = len(prompt)
+    for i, t in enumerate(ref_tokens[:-1]):
+        lg = _run(runner, [t], pos, table, decode=True)
+        pos += 1
+        worst = max(worst, (lg - ref_logits[i + 1]).abs().max().item())
+    assert worst < 3e-2, worst
+
+
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-ds"])
+def test_engine_moe_families_graph_vs_eager(name):
+    """Engine end to end on the MoE / MLA families: CUDA-graph decode == eager decode."""
+    from barq_inference_b200.engine.engine import Engine, EngineConfig
+    from barq_inference_b200.engine.sampling_params import SamplingParams
+
+    cfg = preset(name)
+    tensors = random_tensors(cfg, POLICIES[name], seed=11)
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, cfg.vocab, (30,), generator=g).tolist()
+    outs = []
+    for graphs in (False, True):
+        eng = Engine(cfg, tensors, EngineConfig(max_num_seqs=4, max_model_len=256, num_blocks=64, cuda_graphs=graphs))
+        res = eng.generate([prompt, prompt[:9]], SamplingParams.greedy_params(max_tokens=8))
+        outs.append([r.tokens for r in res])
+        assert all(len(r.tokens) == 8 for r in res)
+    assert outs[0] == outs[1]
