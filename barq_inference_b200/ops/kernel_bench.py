@@ -1,0 +1,114 @@
+"""Kernel microbenchmarks on Llama-3-8B shapes (random Q4_K / Q6_K weights), timed with CUDA events
+around a CUDA graph of ``--iters`` launches (device time only, no host gaps).
+
+    python -m barq_inference_b200.ops.kernel_bench gemm_gate_up --tokens 64
+    python -m barq_inference_b200.ops.kernel_bench gemv_gate_up
+    python -m barq_inference_b200.ops.kernel_bench all
+
+Each case prints one line: name, microseconds per launch, GB/s of weight bytes, TFLOP/s.  The same
+cases, run a few times without timing (``--iters 3 --no-graph``), are the profiling targets for ncu.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import EPI_ADD_F32, EPI_STORE_F32, EPI_SWIGLU_Q8, QWeight, gemm, gemv, interleave_gate_up, quantize_q8
+
+
+def _qw(N: int, K: int, t, seed: int = 0) -> QWeight:
+    from ..gguf import quantize
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    return QWeight.from_packed(quantize(w, t), t, N, K, "cuda").finalize()
+
+
+def _time(fn, iters: int, graph: bool) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
+    else:
+        def run():
+            for _ in range(iters):
+                fn()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3
+
+
+def cases(tokens: int):
+    from ..gguf import GGMLType
+
+    def gate_up():
+        return interleave_gate_up(_qw(14336, 4096, GGMLType.Q4_K, 1), _qw(14336, 4096, GGMLType.Q4_K, 2)).finalize()
+
+    def gemm_gate_up():
+        w = gate_up()
+        x = torch.randn(tokens, 4096, device="cuda").half()
+        return w, (lambda: gemm(w, x, EPI_SWIGLU_Q8)), 2.0 * tokens * w.N * w.K
+
+    def gemm_down():
+        w = _qw(4096, 14336, GGMLType.Q4_K, 3)
+        x = torch.randn(tokens, 14336, device="cuda").half()
+        out = torch.zeros(tokens, 4096, device="cuda")
+        return w, (lambda: gemm(w, x, EPI_ADD_F32, out=out)), 2.0 * tokens * w.N * w.K
+
+    def gemv_gate_up():
+        w = gate_up()
+        xa = quantize_q8(torch.randn(1, 4096, device="cuda"), True)
+        return w, (lambda: gemv(w, xa, 1, EPI_SWIGLU_Q8, x2=True)), 2.0 * w.N * w.K
+
+    def gemv_head():
+        w = _qw(128256, 4096, GGMLType.Q6_K, 4)
+        xa = quantize_q8(torch.randn(1, 4096, device="cuda"), True)
+        out = torch.empty(1, w.N, device="cuda")
+        return w, (lambda: gemv(w, xa, 1, EPI_STORE_F32, out=out, x2=True)), 2.0 * w.N * w.K
+
+    def gemv_qkv():
+        w = _qw(6144, 4096, GGMLType.Q4_K, 5)
+        xa = quantize_q8(torch.randn(1, 4096, device="cuda"), True)
+        out = torch.empty(1, w.N, device="cuda")
+        return w, (lambda: gemv(w, xa, 1, EPI_STORE_F32, out=out, x2=True)), 2.0 * w.N * w.K
+
+    return {"gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
+            "gemv_head": gemv_head, "gemv_qkv": gemv_qkv}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("case", help="case name or 'all'")
+    ap.add_argument("--tokens", type=int, default=64, help="token rows for the GEMM cases")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-graph", action="store_true", help="plain launches (for profilers)")
+    a = ap.parse_args(argv)
+    cs = cases(a.tokens)
+    names = list(cs) if a.case == "all" else [a.case]
+    for n in names:
+        w, fn, flops = cs[n]()
+        us = _time(fn, a.iters, not a.no_graph)
+        gbs = w.nbytes() / us / 1e3
+        print(f"{n}: {us:.1f} us  {gbs:.0f} GB/s  {flops / us / 1e6:.1f} TFLOP/s", flush=True)
+        del w, fn
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
