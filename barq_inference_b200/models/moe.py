@@ -34,10 +34,13 @@ def _qw(pt: PackedTensor, device) -> QWeight:
 
 
 class MoEBlock:
-    def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], prefix: str, device):
+    def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], prefix: str, device, expert0: int = 0):
         self.cfg = cfg
         self.device = device
         self.E, self.k = cfg.n_experts, cfg.n_experts_used
+        # expert parallel: this block holds experts [expert0, expert0 + E_local) of the E routed ones
+        self.e0 = expert0
+        self.E_local = tensors[prefix + "ffn_gate_exps.weight"].shape[0]
         self.F = cfg.expert_ffn
         self.router = _dense(tensors[prefix + "ffn_gate_inp.weight"], device)  # [E, H]
         g = _qw(tensors[prefix + "ffn_gate_exps.weight"], device)  # E*F rows
@@ -84,16 +87,18 @@ class MoEBlock:
     def _fused(self, logits, hb, T, x, ser):
         r = ops.MoeRouting(T, self.E, self.k, hb.shape[1], hb.dtype, self.device)
         ops.moe_route(logits, hb, self.k, r, **self._route_args(ser))
-        h = ops.gemm_grouped(self.gate_up, r.xs, r.off, self.E, EPI_SWIGLU_Q8)  # [T*k, F]
-        ops.gemm_grouped(self.down, h, r.off, self.E, EPI_MOE_COMBINE, out=x, row_tok=r.row_tok, row_w=r.row_w)
+        # rows are sorted by expert: the local experts' rows are the window off[e0 .. e0 + E_local]
+        off = r.off[self.e0:self.e0 + self.E_local + 1]
+        h = ops.gemm_grouped(self.gate_up, r.xs, off, self.E_local, EPI_SWIGLU_Q8)  # [T*k, F]
+        ops.gemm_grouped(self.down, h, off, self.E_local, EPI_MOE_COMBINE, out=x, row_tok=r.row_tok, row_w=r.row_w)
 
     def _unfused(self, logits, hb, T, x, ser):
         """Baseline: route on the device, then one expert at a time (host-side token lists)."""
         r = ops.MoeRouting(T, self.E, self.k, hb.shape[1], hb.dtype, self.device)
         ops.moe_route(logits, hb, self.k, r, **self._route_args(ser))
         ids, wts = r.ids[:T].cpu(), r.weights[:T].cpu()
-        for e in range(self.E):
-            sel = (ids == e) & (wts > 0)
+        for e in range(self.E_local):
+            sel = (ids == self.e0 + e) & (wts > 0)
             if not bool(sel.any()):
                 continue
             tok = sel.nonzero()[:, 0]

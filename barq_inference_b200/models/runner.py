@@ -60,8 +60,12 @@ class Layer:
 
 class LlamaRunner:
     def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], device="cuda",
-                 kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None, act_x2: bool = True):
+                 kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None, act_x2: bool = True,
+                 tp=None, comm=None):
         self.cfg = cfg
+        # tensor parallel: ``tp`` (parallel.tp.TPInfo) describes this rank's shard, ``comm``
+        # (parallel.comm.Comm) completes the row-parallel partial sums; None = one GPU
+        self.tp, self.comm = tp, comm
         self.device = torch.device(device)
         self.kv_dtype = kv_dtype
         self.scale = attn_scale(cfg)
@@ -95,7 +99,7 @@ class LlamaRunner:
             if cfg.layer_is_moe(i):
                 from .moe import MoEBlock
 
-                L.moe = MoEBlock(cfg, tensors, p, dev)
+                L.moe = MoEBlock(cfg, tensors, p, dev, expert0=tp.expert0 if tp is not None else 0)
             else:
                 L.moe = None
                 g, u = _qw(tensors[p + "ffn_gate.weight"], dev), _qw(tensors[p + "ffn_up.weight"], dev)
@@ -146,6 +150,37 @@ class LlamaRunner:
             ops.gemv(w, x.rows(t0, t1) if x is not None else None, t1 - t0, mode, out=out[t0:t1], bias=bias,
                      xb=None if xb is None else xb[t0:t1].contiguous())
         return out
+
+    def _row_parallel(self, j: int, fn, x: torch.Tensor) -> None:
+        """Add a row-parallel layer's output into the residual ``x``.  ``fn(mode, out)`` writes this
+        rank's partial with EPI_ADD_F32 (into x) or EPI_STORE_F32 (into a buffer).  One GPU: plain
+        add.  Fused TP: store into the symmetric buffer j, then one kernel adds every rank's partial.
+        NCCL TP: rank 0 adds into x, the others store into x, then an all-reduce."""
+        c = self.comm
+        if c is None or c.world == 1:
+            fn(EPI_ADD_F32, x)
+        elif c.fused:
+            fn(EPI_STORE_F32, c.partial(j, x.shape[0], x.shape[1]))
+            c.allreduce_add(j, x)
+        else:
+            fn(EPI_ADD_F32 if c.rank == 0 else EPI_STORE_F32, x)
+            c.all_reduce(x)
+
+    def _moe_out(self, L, hq, hb, T, x) -> None:
+        def fn(mode, out):
+            if mode == EPI_STORE_F32:
+                out.zero_()
+            L.moe.forward(self, hq, hb, T, out)
+        self._row_parallel(1, fn, x)
+
+    def _gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
+        """Vocab-parallel head: every rank holds a slice of the vocabulary; all-gather the logits."""
+        if self.comm is not None and self.comm.world > 1 and self.tp is not None and self.tp.vocab_local:
+            logits = self.comm.all_gather_cols(logits)
+        return logits
+
+    def _head(self, x_last: torch.Tensor) -> torch.Tensor:
+        return self._gather_logits(self._norm_lin(self.out_w, x_last, self.out_norm, x_last.shape[0], EPI_STORE_F32))
 
     def _norm_lin(self, w, x: torch.Tensor, norm_w: torch.Tensor, T: int, mode: int, out=None, bias=None):
         """RMSNorm(x) -> int8 -> GEMV.  For 1-2 tokens on a quantized weight the norm runs inside the
@@ -218,24 +253,25 @@ class LlamaRunner:
             hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
             qkv = self._lin_bf16(L.qkv, hb, T, EPI_STORE_F32, bias=L.qkv_bias)
             ab, _ = self._attention(L, li, qkv, inp, T, want_q8=False)
-            self._lin_bf16(L.wo, ab, T, EPI_ADD_F32, out=x)
+            self._row_parallel(0, lambda m, o: self._lin_bf16(L.wo, ab, T, m, out=o), x)
             hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_bf16=True,
                                  want_q8=L.moe is not None, x2=self.x2, act_dtype=self.act_dtype)
             if L.moe is not None:
-                L.moe.forward(self, hq, hb, T, x)
+                self._moe_out(L, hq, hb, T, x)
                 continue
             if L.gu_interleaved:
                 h = ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
             else:
                 gu = self._lin_bf16(L.gate_up, hb, T, EPI_STORE_F32)
                 h, _ = ops.swiglu(gu, cfg.ffn, want_bf16=True, act_dtype=self.act_dtype)
-            self._lin_bf16(L.down, h, T, EPI_ADD_F32, out=x)
+            self._row_parallel(1, lambda m, o: self._lin_bf16(L.down, h, T, m, out=o), x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
         ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
         if xl.shape[0] <= GEMV_MAX_T:
             _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
-            return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32, xb=ob.to(torch.bfloat16))
-        return self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32)
+            return self._gather_logits(self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32,
+                                                    xb=ob.to(torch.bfloat16)))
+        return self._gather_logits(self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32))
 
     def _forward_gemv(self, inp: StepInput) -> torch.Tensor:
         cfg = self.cfg
@@ -254,15 +290,15 @@ class LlamaRunner:
                 ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
                                            H, Hkv, D, self.scale, cfg.sliding_window)
                 aq = ops.quantize_q8(ab, self.x2)
-            self._lin_q8(L.wo, aq, T, EPI_ADD_F32, out=x, xb=ab)
+            self._row_parallel(0, lambda m, o: self._lin_q8(L.wo, aq, T, m, out=o, xb=ab), x)
             if L.moe is not None:
                 hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=True, x2=self.x2)
-                L.moe.forward(self, hq, hb, T, x)
+                self._moe_out(L, hq, hb, T, x)
                 continue
             down_bf16 = self._needs_bf16(L.down)
             if L.gu_interleaved and not down_bf16:
                 h2 = self._norm_lin(L.gate_up, x, L.ffn_norm, T, EPI_SWIGLU_Q8)
-                self._lin_q8(L.down, h2, T, EPI_ADD_F32, out=x)
+                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, h2, T, m, out=o), x)
             else:
                 hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True,
                                      want_bf16=self._needs_bf16(L.gate_up), x2=self.x2)
@@ -271,6 +307,6 @@ class LlamaRunner:
                     gu = gu.view(T, -1, 2, 32).transpose(1, 2).reshape(T, -1).contiguous()
                 hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16,
                                       x2=self.x2)
-                self._lin_q8(L.down, hq2, T, EPI_ADD_F32, out=x, xb=hb2)
+                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, hq2, T, m, out=o, xb=hb2), x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
-        return self._norm_lin(self.out_w, xl, self.out_norm, xl.shape[0], EPI_STORE_F32)
+        return self._head(xl)

@@ -1,0 +1,94 @@
+"""Communication backend for tensor / expert parallelism: one process per GPU over NCCL.
+
+Parity: ``NcclCommunicator`` / ``MultiGpuManager`` (``backend/src/cuda_multi_gpu.rs:197-233, 400-453``)
+and ``CommBackend`` (``advanced/src/tensor_parallel.rs:28-37``), all stubs in the reference.
+
+* Bootstrap: ``torch.distributed`` (NCCL backend) from the usual RANK / WORLD_SIZE / MASTER_* env;
+  every collective has the process group's timeout, so a rank that dies makes the others raise
+  instead of waiting forever.
+* Baseline path: ``all_reduce`` / ``all_gather`` through NCCL.
+* Fused path (``fused=True``): a symmetric allocation (every rank maps every peer's buffer over
+  NVLink) holds two partial-sum buffers and the barrier flags; row-parallel layers store their
+  partial into the local buffer and ``allreduce_add`` (csrc/kernels/allreduce.cu) sums the peers'
+  partials into the residual stream in one kernel -- a one-shot all-reduce with the residual add
+  fused, no NCCL launch on the decode path.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..ops import require_ext
+
+
+class Comm:
+    def __init__(self, device: torch.device, fused: bool = True, max_elems: int = 0,
+                 timeout_s: float = 120.0):
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=timeout_s))
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        self.device = device
+        self.fused = fused and self.world > 1
+        self.max_elems = max_elems
+        if self.fused:
+            self._setup_symmetric(max_elems)
+
+    # ------------------------------------------------------------------ fused path
+    def _setup_symmetric(self, n: int) -> None:
+        import torch.distributed._symmetric_memory as symm
+
+        n = (n + 63) // 64 * 64
+        flag_words = 64 * 8  # kArMaxBlocks x kArMaxRanks u32
+        self.buf = symm.empty(2 * n + flag_words, dtype=torch.float32, device=self.device)
+        self.buf.zero_()
+        self.hdl = symm.rendezvous(self.buf, dist.group.WORLD)
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        base = list(self.hdl.buffer_ptrs)
+        self._bufs = [[p + j * n * 4 for p in base] for j in (0, 1)]
+        self._flags = [p + 2 * n * 4 for p in base]
+        self._n = n
+        self.epoch = torch.zeros(64, dtype=torch.int32, device=self.device)
+
+    def partial(self, j: int, T: int, H: int) -> torch.Tensor:
+        """Local partial-sum buffer j (0: attention output, 1: FFN down) viewed as f32 [T, H]."""
+        if T * H > self._n:
+            raise ValueError(f"fused all-reduce buffer holds {self._n} values, {T * H} requested")
+        return self.buf[j * self._n: j * self._n + T * H].view(T, H)
+
+    def allreduce_add(self, j: int, x: torch.Tensor) -> None:
+        """x += sum over ranks of partial buffer j (every rank calls it with its own x)."""
+        n = x.numel()
+        blocks = max(1, min(32, (n // 4 + 255) // 256))
+        require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks)
+
+    # ------------------------------------------------------------------ NCCL baseline
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        dist.all_reduce(x)
+        return x
+
+    def all_gather_cols(self, y: torch.Tensor) -> torch.Tensor:
+        """Concatenate every rank's [T, n_r] along columns (vocab-parallel logits; equal n_r)."""
+        parts = [torch.empty_like(y) for _ in range(self.world)]
+        dist.all_gather(parts, y.contiguous())
+        return torch.cat(parts, 1)
+
+    def barrier(self) -> None:
+        dist.barrier()
+
+    def check(self) -> None:
+        """Raise if a fused all-reduce gave up waiting for a peer (bounded device-side waits)."""
+        from .. import ops
+
+        err = ops.gemm_error()
+        if err & 0xF00 == 0x300:
+            raise RuntimeError(f"fused all-reduce: peer {err & 0xFF} did not arrive within the wait limit")
+
+
+def env_world() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), \
+        int(os.environ.get("LOCAL_RANK", "0"))

@@ -164,6 +164,27 @@ void mla_attention(Tensor q_lat, Tensor q, int64_t qdim, int64_t rope_off, Tenso
   check(barq::mla_attention(a, cache.scalar_type() == torch::kBFloat16, cur_stream()), "mla_attention");
 }
 
+// bufs / flags: device addresses (one per rank) of the partial buffers and flag areas.
+void allreduce_add(Tensor x, std::vector<int64_t> bufs, std::vector<int64_t> flags, Tensor epoch, int64_t rank,
+                   int64_t blocks) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "allreduce_add: x must be contiguous f32");
+  TORCH_CHECK(bufs.size() == flags.size() && bufs.size() <= (size_t)barq::kArMaxRanks, "allreduce_add: ranks");
+  barq::ArArgs a{};
+  a.x = ptr<float>(x);
+  for (size_t r = 0; r < bufs.size(); ++r) {
+    a.bufs[r] = reinterpret_cast<const float*>(bufs[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+  }
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.err = barq::kernel_err_word();
+  a.rank = (int)rank;
+  a.world = (int)bufs.size();
+  a.n = (int)x.numel();
+  a.blocks = (int)blocks;
+  check(barq::allreduce_add(a, cur_stream()), "allreduce_add");
+}
+
 int64_t gemm_error() {
   int v = 0;
   TORCH_CHECK(barq::gemm_error_word(&v) == 0, "gemm_error: read failed");
@@ -318,6 +339,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("mla_kv_write", &mla_kv_write);
+  m.def("allreduce_add", &allreduce_add);
   m.def("mla_attn_scratch_floats", &mla_attn_scratch_floats);
   m.def("mla_attention", &mla_attention);
   m.def("gemm_clear_error", &gemm_clear_error);

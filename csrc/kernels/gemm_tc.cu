@@ -24,7 +24,7 @@
 //   warp 21     activation producer: TMA of activation tiles, one ring slot behind the MMAs;
 //   warp 22     MMA: one thread issues 4 x tcgen05.mma (K = 16) per stage and commits completion.
 // Every wait is bounded (tc_common.cuh); on expiry the CTA records an error word and unwinds.
-// No load here uses .multicast::cluster.
+// Every TMA / bulk copy here has a single destination CTA and reads this GPU's own memory.
 #include <cudaTypedefs.h>
 
 #include <cstdlib>

@@ -27,6 +27,19 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
 // 0 = automatic (f32 modes only; accumulated with atomics).
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
+// One-shot all-reduce + residual add over peer memory (allreduce.cu).
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxBlocks = 64;
+struct ArArgs {
+  float* x;                          // local residual [n], x += sum of partials
+  const float* bufs[kArMaxRanks];    // every rank's partial buffer (peer pointers; bufs[rank] local)
+  uint32_t* flags[kArMaxRanks];      // every rank's flag area [kArMaxBlocks][kArMaxRanks] (peer pointers)
+  uint32_t* epoch;                   // local [kArMaxBlocks] epoch counters (zero-initialized)
+  int* err;                          // error word (0x300 | peer on a barrier timeout)
+  int rank, world, n, blocks;
+};
+int allreduce_add(const ArArgs& a, cudaStream_t st);
+
 // DeepSeek-V2 MLA (mla.cu).  Latent cache rows: [c (512) | k_pe (64)], 16 tokens per page.
 struct MlaKvArgs {
   const float* kv_a;    // [T, 576] kv_a_mqa projection

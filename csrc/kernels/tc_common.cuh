@@ -1,7 +1,7 @@
 // Blackwell (sm_100a) building blocks in inline PTX: mbarriers with bounded waits, TMA tile loads,
 // tcgen05 TMEM allocation / MMA / commit / load, and UMMA shared-memory descriptors.
 //
-// No load here uses .multicast::cluster: every TMA copy reads this GPU's own memory into this CTA.
+// Every TMA copy here reads this GPU's own memory into the issuing CTA only.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>

@@ -1,0 +1,87 @@
+"""Tensor parallel (attention TP x MoE EP) on 2 GPUs vs the same model on one GPU.
+
+Runs 2 NCCL ranks as child processes (skipped with fewer than 2 GPUs); both the fused one-shot
+all-reduce (symmetric memory, csrc/kernels/allreduce.cu) and the NCCL baseline are checked."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+
+def _step(runner, toks, start, table, decode):
+    from barq_inference_b200.models.runner import StepInput
+
+    T = len(toks)
+    pos = list(range(start, start + T))
+    slots = [table[p // 16] * 16 + p % 16 for p in pos]
+    dev = runner.device
+    d = lambda a, dt: torch.tensor(a, dtype=dt, device=dev)  # noqa: E731
+    inp = StepInput(d(toks, torch.int32), d(pos, torch.int32), d(slots, torch.int64), d([table], torch.int32),
+                    d([start + T], torch.int32), d([T - 1], torch.int64), decode,
+                    q_start=d([0, T], torch.int32), max_q=T)
+    return runner.forward(inp)[0].float().cpu()
+
+
+def _logits(runner, prompt, steps=3):
+    table = list(range(1, 10))
+    out = [_step(runner, prompt, 0, table, False)]
+    pos = len(prompt)
+    for _ in range(steps):
+        t = int(out[-1].argmax())
+        out.append(_step(runner, [t], pos, table, True))
+        pos += 1
+    return torch.stack(out)
+
+
+def _worker(rank, world, port, name, fused, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.models.runner import LlamaRunner
+    from barq_inference_b200.parallel.comm import Comm
+    from barq_inference_b200.parallel.tp import shard_config, shard_tensors
+
+    cfg = preset(name)
+    full = random_tensors(cfg, POLICIES["tiny"], seed=4)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
+    comm = Comm(dev, fused=fused, max_elems=64 * cfg.hidden)
+    shard, info = shard_tensors(cfg, full, rank, world)
+    r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
+    r.allocate_kv(32)
+    tp_logits = _logits(r, prompt)
+    comm.check()
+    if rank == 0:
+        ref = LlamaRunner(cfg, full, dev)
+        ref.allocate_kv(32)
+        q.put(("ok", (tp_logits - _logits(ref, prompt)).abs().max().item()))
+    comm.barrier()
+    import torch.distributed as dist
+
+    dist.destroy_process_group()
+
+
+@needs2
+@pytest.mark.parametrize("name", ["tiny", "tiny-moe"])
+@pytest.mark.parametrize("fused", [True, False])
+def test_tp2_matches_single_gpu(name, fused):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, name, fused, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    status, err = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    assert err < 2e-2, err
