@@ -47,6 +47,8 @@ class EngineConfig:
     ser_threshold: float = 0.0      # MoE smart expert reduction (--ser)
     fused_moe: bool = True          # --fmoe
     act_x2: bool = True             # two-term int8 decode activations (False: single int8 term)
+    tp: int = 1                     # tensor parallel degree (one process per GPU, torch.distributed)
+    fused_comm: bool = True         # TP: fused one-shot all-reduce kernel (False: NCCL all-reduce)
 
     @staticmethod
     def preset(name: str, **kw) -> "EngineConfig":
@@ -172,6 +174,9 @@ class Engine:
         self.timings[key + "_s"] += dt
         self.timings[key + "_tokens"] += sum(plan.n_new)
         self.step_count += 1
+        comm = getattr(self.runner, "comm", None)
+        if comm is not None and comm.fused:
+            comm.check()  # a peer that stopped answering raises here instead of slowing every step
         return self._commit(plan, ids)
 
     def _commit(self, plan: ScheduledStep, ids: list[int | None]) -> list[Sequence]:
@@ -410,6 +415,20 @@ class Engine:
 
 
 def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
+    if ec.tp > 1:
+        from ..parallel.comm import Comm
+        from ..parallel.tp import shard_config, shard_tensors
+
+        comm = Comm(torch.device(device), fused=ec.fused_comm,
+                    max_elems=max(ec.max_num_batched_tokens, ec.max_num_seqs) * cfg.hidden)
+        if comm.world != ec.tp:
+            raise ValueError(f"tp={ec.tp} but the process group has {comm.world} ranks")
+        shard, info = shard_tensors(cfg, tensors, comm.rank, comm.world)
+        r = LlamaRunner(shard_config(cfg, comm.world), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info, comm=comm)
+        comm.barrier()  # ranks finish building (tiling) their shards before the first collective
+        r.ser_threshold = ec.ser_threshold
+        r.fused_moe = ec.fused_moe
+        return r
     if cfg.is_mla:
         from ..models.deepseek2 import DeepseekV2Runner
 

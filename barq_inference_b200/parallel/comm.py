@@ -26,12 +26,15 @@ from ..ops import require_ext
 
 class Comm:
     def __init__(self, device: torch.device, fused: bool = True, max_elems: int = 0,
-                 timeout_s: float = 120.0):
+                 timeout_s: float = 120.0, wait_s: float = 20.0):
         if not dist.is_initialized():
             dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=timeout_s))
         self.rank = dist.get_rank()
         self.world = dist.get_world_size()
         self.device = device
+        # device-side barrier limit of the fused all-reduce: ranks may legitimately drift apart by
+        # seconds (graph capture, garbage collection); a longer silence is a failed peer
+        self.wait_s = wait_s
         self.fused = fused and self.world > 1
         self.max_elems = max_elems
         if self.fused:
@@ -64,7 +67,7 @@ class Comm:
         """x += sum over ranks of partial buffer j (every rank calls it with its own x)."""
         n = x.numel()
         blocks = max(1, min(32, (n // 4 + 255) // 256))
-        require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks)
+        require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks, self.wait_s)
 
     # ------------------------------------------------------------------ NCCL baseline
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:

@@ -42,6 +42,11 @@ def parse():
     ap.add_argument("--bs1-steps", type=int, default=64)
     ap.add_argument("--e2e-tokens", type=int, default=32)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
+                    help="dp: one engine replica per GPU (weak scaling, default); tp: one tensor-parallel engine "
+                         "over all GPUs (strong scaling)")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="tp all-reduce: fused one-shot kernel over NVLink peer memory, or NCCL")
     return ap.parse_args()
 
 
@@ -132,13 +137,15 @@ def main():
     max_len = max(max_len, args.ttft_prompt + args.bs1_steps + 16)
     max_len = (max_len + 15) // 16 * 16
     blocks_needed = B * (max_len // 16 + 2) + 64
+    tp = world if args.parallel == "tp" else 1
     ec = EngineConfig(max_num_seqs=max(B, 1), max_num_batched_tokens=8192, max_model_len=max_len,
-                      num_blocks=blocks_needed, cuda_graphs=True)
+                      num_blocks=blocks_needed, cuda_graphs=True, tp=tp, fused_comm=args.comm == "fused")
     eng = Engine(cfg, tensors, ec)
     del tensors
     torch.cuda.empty_cache()
     init_s = time.time() - t_init
-    rng = np.random.default_rng(1 + rank)
+    rng = np.random.default_rng(1 + (rank if tp == 1 else 0))  # TP ranks serve the same requests
+    mult = world if tp == 1 else 1  # DP: aggregate over replicas; TP: one engine
     greedy = lambda n: SamplingParams.greedy_params(max_tokens=n, ignore_eos=True)  # noqa: E731
 
     def ev():
@@ -244,30 +251,31 @@ def main():
     d2h = B * 4
 
     if rank == 0:
-        value = world * B * args.steps / (dec_ms / 1e3)
+        value = mult * B * args.steps / (dec_ms / 1e3)
         out = {
             "metric": METRIC,
             "value": round(value, 2),
-            "unit": "tokens/s (decode, batch %d per GPU, aggregate)" % B,
+            "unit": ("tokens/s (decode, batch %d per GPU, aggregate)" % B) if tp == 1 else
+                    ("tokens/s (decode, batch %d, tensor parallel over %d GPUs)" % (B, world)),
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(dec_ms / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if tp == 1 else "strong",
             "vs_baseline": None,
             "dtype": "bf16/fp32 compute on Q4_K/Q6_K weights, int8 decode activations, fp16 KV",
             "data": "synthetic: random-init N(0,0.02) weights quantized to Q4_K/Q6_K, uniform-random prompt ids",
-            "config": {"model": MODEL + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * world,
-                       "seq_len": P, "parallelism": f"dp{world}",
+            "config": {"model": MODEL + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * mult,
+                       "seq_len": P, "parallelism": f"dp{world}" if tp == 1 else f"tp{world}-{args.comm}",
                        "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)"},
             "extra": {
-                "decode_tok_s_bs1": round(world * 1e3 / bs1_ms, 2),
-                "prefill_tok_s": round(world * B * P / (prefill_ms / 1e3), 1),
+                "decode_tok_s_bs1": round(mult * 1e3 / bs1_ms, 2),
+                "prefill_tok_s": round(mult * B * P / (prefill_ms / 1e3), 1),
                 "ttft_p50_ms_512": round(statistics.median(ttfts), 3) if ttfts else None,
                 "init_s": round(init_s, 1),
             },
-            "e2e": {"value": round(world * e2e_dec, 2), "unit": "tokens/s decode via Engine.generate()",
+            "e2e": {"value": round(mult * e2e_dec, 2), "unit": "tokens/s decode via Engine.generate()",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "wall_s": round(t_e2e, 3), "tokens": sum(len(r.tokens) for r in res)},
             "gpu_launches": launches_per_step * args.steps,

@@ -5,8 +5,9 @@
 // peer's buffer); this kernel then, on every rank,
 //   1. (per block) signals "partial ready" to each peer: a release store of its epoch into the
 //      peer's flag slot [block][my rank], and waits until every peer's flag in its own slots reached
-//      the same epoch (acquire loads, bounded by ~1 s of %globaltimer, then an error word is set
-//      and the block returns);
+//      the same epoch (acquire loads, bounded by a wait limit measured on %globaltimer -- long
+//      enough to absorb host-side skew between ranks such as CUDA-graph capture; on expiry the error
+//      word is set and the block skips the sum but still advances its epoch, keeping ranks aligned);
 //   2. reads the partials of all ranks straight from peer memory (plain per-thread loads over
 //      NVLink, no TMA) and adds their sum into the local residual stream x.
 // Epochs live in device memory (one counter per block, advanced by the kernel), so the kernel is
@@ -23,7 +24,6 @@
 namespace barq {
 
 namespace {
-constexpr uint64_t kArWaitNs = 1000000000ull;  // 1 s
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256) allreduce_add_kernel(ArArgs a) {
     const uint64_t t0 = gtimer();
     for (uint32_t i = 0;; ++i) {
       if ((int)(ld_acquire_sys(mine) - ep) >= 0) break;
-      if ((i & 1023) == 1023 && gtimer() - t0 > kArWaitNs) {
+      if ((i & 1023) == 1023 && gtimer() - t0 > a.wait_ns) {
         fail_s = 1;
         atomicExch(a.err, 0x300 | peer);
         break;
@@ -68,7 +68,10 @@ __global__ void __launch_bounds__(256) allreduce_add_kernel(ArArgs a) {
     }
   }
   __syncthreads();
-  if (fail_s) return;  // a peer never arrived: leave x unchanged, the host reads the error word
+  if (fail_s) {  // a peer never arrived: x is left unchanged, the host raises on the error word
+    if (threadIdx.x == 0) a.epoch[b] = ep;
+    return;
+  }
   // x[i] += sum_r partial_r[i] over this block's grid-stride share, float4 at a time
   const int n4 = a.n / 4;
   for (int i = b * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {

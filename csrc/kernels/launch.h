@@ -37,6 +37,7 @@ struct ArArgs {
   uint32_t* epoch;                   // local [kArMaxBlocks] epoch counters (zero-initialized)
   int* err;                          // error word (0x300 | peer on a barrier timeout)
   int rank, world, n, blocks;
+  unsigned long long wait_ns;        // barrier wait limit
 };
 int allreduce_add(const ArArgs& a, cudaStream_t st);
 
