@@ -154,12 +154,13 @@ class LlamaRunner:
     def _row_parallel(self, j: int, fn, x: torch.Tensor) -> None:
         """Add a row-parallel layer's output into the residual ``x``.  ``fn(mode, out)`` writes this
         rank's partial with EPI_ADD_F32 (into x) or EPI_STORE_F32 (into a buffer).  One GPU: plain
-        add.  Fused TP: store into the symmetric buffer j, then one kernel adds every rank's partial.
-        NCCL TP: rank 0 adds into x, the others store into x, then an all-reduce."""
+        add.  Fused TP (decode-sized messages): store into the symmetric buffer j, then one kernel adds
+        every rank's partial.  NCCL TP (and large messages): rank 0 adds into x, the others store
+        into x, then an all-reduce."""
         c = self.comm
         if c is None or c.world == 1:
             fn(EPI_ADD_F32, x)
-        elif c.fused:
+        elif c.fused and x.numel() <= c.fused_max_elems:  # large (prefill) messages go through NCCL
             fn(EPI_STORE_F32, c.partial(j, x.shape[0], x.shape[1]))
             c.allreduce_add(j, x)
         else:

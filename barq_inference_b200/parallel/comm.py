@@ -36,6 +36,9 @@ class Comm:
         # seconds (graph capture, garbage collection); a longer silence is a failed peer
         self.wait_s = wait_s
         self.fused = fused and self.world > 1
+        # the one-shot kernel wins on latency-bound (decode) messages; NCCL's ring/NVLS algorithms
+        # win on bandwidth-bound ones (prefill), which therefore stay on NCCL
+        self.fused_max_elems = 256 * 1024
         self.max_elems = max_elems
         if self.fused:
             self._setup_symmetric(max_elems)

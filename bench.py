@@ -283,6 +283,13 @@ def main():
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        if tp > 1:
+            # captured CUDA graphs hold NCCL collectives: tearing the communicator down under them can
+            # block; every result is printed, so synchronize the ranks and leave without teardown
+            dist.barrier()
+            torch.cuda.synchronize()
+            sys.stdout.flush()
+            os._exit(0)
         dist.destroy_process_group()
 
 
