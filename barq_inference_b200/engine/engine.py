@@ -48,6 +48,7 @@ class EngineConfig:
     fused_moe: bool = True          # --fmoe
     act_x2: bool = True             # two-term int8 decode activations (False: single int8 term)
     tp: int = 1                     # tensor parallel degree (one process per GPU, torch.distributed)
+    rank_timeout_s: float = 30.0    # TP: a peer without a heartbeat for this long fails the step
     fused_comm: bool = True         # TP: fused one-shot all-reduce kernel (False: NCCL all-reduce)
 
     @staticmethod
@@ -90,6 +91,10 @@ class Engine:
         if nb is None:
             nb = max(64, int(ec.kv_cache_gb * (1 << 30) // self.runner.kv_bytes_per_block(ec.block_size)))
         self.runner.allocate_kv(nb, ec.block_size)
+        from ..utils.trace import StepProfiler
+
+        self._profile = StepProfiler.from_env(self)  # BARQ_PROFILE / BARQ_NVTX
+        self.last_plan = None
         self.blocks = BlockManager(nb, ec.block_size)
         self.dummy_block = self.blocks.allocate(1)[0]  # padding rows of graph batches write here
         self.prefix_cache = None
@@ -128,6 +133,9 @@ class Engine:
                     on_token=None) -> Sequence:
         params = params or SamplingParams()
         seq = Sequence(list(prompt), params, request_id=request_id, on_token=on_token)
+        inj = getattr(self.runner, "injector", None)
+        if inj is not None and inj.active("corrupt", self.step_count):  # fault injection: a bad request
+            seq.prompt.append(self.cfg.vocab)
         if any(t < 0 or t >= self.cfg.vocab for t in seq.prompt):
             raise ValueError("prompt token id out of range")
         if params.grammar or params.json_mode or params.json_schema:
@@ -159,7 +167,20 @@ class Engine:
 
     # ------------------------------------------------------------------ one engine step
     def step(self) -> list[Sequence]:
+        if self._profile is not None:
+            return self._profile.step(self._step)
+        return self._step()
+
+    def _step(self) -> list[Sequence]:
+        health = getattr(self.runner, "health", None)
+        if health is not None:  # tensor parallel: every peer must be alive before a collective
+            inj = self.runner.injector
+            inj.on_step(self.step_count)
+            health.check()
+            if self.runner.comm is not None:
+                self.runner.comm.skip_signal = inj.active("skip_flag", self.step_count)
         plan = self.sched.schedule()
+        self.last_plan = plan
         if plan is None:
             if self.sched.waiting:
                 raise RuntimeError("KV cache too small for the waiting request")
@@ -426,6 +447,12 @@ def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
         shard, info = shard_tensors(cfg, tensors, comm.rank, comm.world)
         r = LlamaRunner(shard_config(cfg, comm.world), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info, comm=comm)
         comm.barrier()  # ranks finish building (tiling) their shards before the first collective
+        from ..parallel.health import FaultInjector, Heartbeat
+        from torch.distributed.distributed_c10d import _get_default_store
+
+        r.injector = FaultInjector(comm.rank)
+        r.health = Heartbeat(_get_default_store(), comm.rank, comm.world, timeout=ec.rank_timeout_s,
+                             injector=r.injector)
         r.ser_threshold = ec.ser_threshold
         r.fused_moe = ec.fused_moe
         return r

@@ -39,6 +39,7 @@ class Comm:
         # the one-shot kernel wins on latency-bound (decode) messages; NCCL's ring/NVLS algorithms
         # win on bandwidth-bound ones (prefill), which therefore stay on NCCL
         self.fused_max_elems = 256 * 1024
+        self.skip_signal = False  # fault injection (BARQ_FAULT skip_flag)
         self.max_elems = max_elems
         if self.fused:
             self._setup_symmetric(max_elems)
@@ -70,7 +71,8 @@ class Comm:
         """x += sum over ranks of partial buffer j (every rank calls it with its own x)."""
         n = x.numel()
         blocks = max(1, min(32, (n // 4 + 255) // 256))
-        require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks, self.wait_s)
+        require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks, self.wait_s,
+                                    int(self.skip_signal))
 
     # ------------------------------------------------------------------ NCCL baseline
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:

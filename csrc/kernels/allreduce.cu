@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(256) allreduce_add_kernel(ArArgs a) {
   if (threadIdx.x < a.world) {
     const int peer = threadIdx.x;
     __threadfence_system();  // this rank's partial (written by the previous kernel) before the flag
-    st_release_sys(a.flags[peer] + b * kArMaxRanks + a.rank, ep);
+    if (!a.skip_signal) st_release_sys(a.flags[peer] + b * kArMaxRanks + a.rank, ep);
     const uint32_t* mine = a.flags[a.rank] + b * kArMaxRanks + peer;
     const uint64_t t0 = gtimer();
     for (uint32_t i = 0;; ++i) {

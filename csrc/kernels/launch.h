@@ -38,6 +38,7 @@ struct ArArgs {
   int* err;                          // error word (0x300 | peer on a barrier timeout)
   int rank, world, n, blocks;
   unsigned long long wait_ns;        // barrier wait limit
+  int skip_signal;                   // fault injection: do not signal the peers (their waits run out)
 };
 int allreduce_add(const ArArgs& a, cudaStream_t st);
 
