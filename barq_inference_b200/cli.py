@@ -27,7 +27,7 @@ log = logging.getLogger("barq")
 # ------------------------------------------------------------------ model loading
 def load(args, need_engine: bool = True):
     """Returns (engine, tokenizer, chat_template, metadata)."""
-    from .gguf import read_gguf
+    from .gguf import read_gguf_split as read_gguf
     from .models.config import config_from_gguf
     from .models.weights import tensors_from_gguf
     from .tokenizer import ChatTemplate, GGUFTokenizer, synthetic_tokenizer
@@ -233,7 +233,7 @@ def cmd_info(args) -> int:
     """Header-only inspection: no tensor is read or dequantized."""
     from collections import Counter
 
-    from .gguf import read_gguf
+    from .gguf import read_gguf_split as read_gguf
     from .models.config import config_from_gguf
 
     g = read_gguf(args.model)

@@ -113,7 +113,7 @@ class Engine:
     # ------------------------------------------------------------------ construction helpers
     @staticmethod
     def from_gguf(path: str, engine_cfg: EngineConfig | None = None, device: str | None = None) -> "Engine":
-        from ..gguf import read_gguf
+        from ..gguf import read_gguf_split as read_gguf
         from ..models.config import config_from_gguf
         from ..models.weights import tensors_from_gguf
 

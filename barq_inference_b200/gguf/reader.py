@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import mmap
 import os
+import re
 import struct
 from dataclasses import dataclass, field
 from typing import Any
@@ -230,6 +231,49 @@ def read_gguf(path: str | os.PathLike) -> GGUFFile:
     g = _parse(mm, path)
     g._mm = mm
     return g
+
+
+_SPLIT_RE = re.compile(r"^(?P<base>.*)-(?P<no>\d{5})-of-(?P<count>\d{5})\.gguf$")
+
+
+def split_paths(path: str | os.PathLike) -> list[str]:
+    """All parts of a split GGUF (``name-00001-of-0000N.gguf``), or ``[path]`` for a single file."""
+    path = os.fspath(path)
+    m = _SPLIT_RE.match(path)
+    if not m:
+        return [path]
+    n = int(m.group("count"))
+    return [f"{m.group('base')}-{i:05d}-of-{n:05d}.gguf" for i in range(1, n + 1)]
+
+
+def read_gguf_split(path: str | os.PathLike) -> GGUFFile:
+    """Open a GGUF that may be split into parts (llama.cpp ``gguf-split`` naming and ``split.*``
+    keys): metadata comes from the first part, tensors from all of them (each part mmap'd)."""
+    parts = split_paths(path)
+    first = read_gguf(parts[0])
+    count = int(first.metadata.get("split.count", len(parts)))
+    if count != len(parts):
+        parts = split_paths(parts[0]) if count == len(parts) else parts
+        if count != len(parts):
+            raise GGUFError(f"{path}: split.count is {count} but {len(parts)} part file(s) were found")
+    if count <= 1:
+        return first
+    maps = [first._mm]
+    for i, p in enumerate(parts[1:], start=2):
+        g = read_gguf(p)
+        no = int(g.metadata.get("split.no", i - 1))
+        if no != i - 1:
+            raise GGUFError(f"{p}: split.no is {no}, expected {i - 1}")
+        dup = set(g.tensors) & set(first.tensors)
+        if dup:
+            raise GGUFError(f"{p}: tensor(s) {sorted(dup)[:3]} already in an earlier part")
+        first.tensors.update(g.tensors)
+        maps.append(g._mm)
+    first._parts = maps  # keep every part mapped while the tensors are in use
+    expected = first.metadata.get("split.tensors.count")
+    if expected is not None and int(expected) != len(first.tensors):
+        raise GGUFError(f"{path}: {len(first.tensors)} tensors across parts, split.tensors.count says {expected}")
+    return first
 
 
 def read_gguf_bytes(data: bytes) -> GGUFFile:

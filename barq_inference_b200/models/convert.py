@@ -11,7 +11,8 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from ..gguf import GGMLType, GGUFWriter, dequantize, quantize, read_gguf
+from ..gguf import GGMLType, GGUFWriter, dequantize, quantize
+from ..gguf import read_gguf_split as read_gguf
 from .weights import fallback_type
 
 KEEP_SUFFIXES = ("_norm.weight", ".bias", "norm.weight")

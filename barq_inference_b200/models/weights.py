@@ -13,7 +13,7 @@ from typing import Iterator
 import numpy as np
 import torch
 
-from ..gguf import GGMLType, GGUFWriter, quantize
+from ..gguf import GGUFValueType, GGMLType, GGUFWriter, quantize
 from .config import ModelConfig
 
 
@@ -224,6 +224,34 @@ def write_gguf(path: str, cfg: ModelConfig, tensors: dict[str, PackedTensor], ex
     for name, pt in tensors.items():
         w.add_tensor(name, pt.data.cpu().numpy(), pt.ggml_type, pt.shape)
     w.write()
+
+
+def write_gguf_split(path: str, cfg: ModelConfig, tensors: dict[str, PackedTensor], n_parts: int,
+                     extra_md: dict | None = None) -> list[str]:
+    """Write ``path`` as ``n_parts`` files ``<base>-0000i-of-0000N.gguf`` (llama.cpp gguf-split layout:
+    every part carries ``split.no`` / ``split.count`` / ``split.tensors.count``, the first one the
+    model metadata, tensors distributed in order).  Returns the part paths."""
+    base = path[:-5] if path.endswith(".gguf") else path
+    names = list(tensors)
+    per = (len(names) + n_parts - 1) // n_parts
+    paths = []
+    for i in range(n_parts):
+        pp = f"{base}-{i + 1:05d}-of-{n_parts:05d}.gguf"
+        w = GGUFWriter(pp)
+        if i == 0:
+            for k, v in config_metadata(cfg).items():
+                w.add(k, v)
+            for k, v in (extra_md or {}).items():
+                w.add(k, v)
+        w.add("split.no", i, GGUFValueType.UINT16)
+        w.add("split.count", n_parts, GGUFValueType.UINT16)
+        w.add("split.tensors.count", len(names), GGUFValueType.INT32)
+        for name in names[i * per:(i + 1) * per]:
+            pt = tensors[name]
+            w.add_tensor(name, pt.data.cpu().numpy(), pt.ggml_type, pt.shape)
+        w.write()
+        paths.append(pp)
+    return paths
 
 
 def tensors_from_gguf(g, device: str | torch.device = "cpu", names: set[str] | None = None) -> dict[str, PackedTensor]:

@@ -101,3 +101,23 @@ def test_cpu_ref_matches_numpy():
         v = torch.randn(2, 512)
         y = _cpu_ref.qgemv(raw.reshape(-1).contiguous(), int(t), 4, 512, v)
         assert torch.allclose(y, v @ torch.from_numpy(b.reshape(4, 512)).T, atol=1e-5)
+
+
+def test_split_gguf_roundtrip(tmp_path):
+    """gguf-split layout: 3 parts, metadata in the first, tensors merged on read."""
+    from barq_inference_b200.gguf import read_gguf_split, split_paths
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.models.weights import tensors_from_gguf, write_gguf_split
+
+    cfg = preset("tiny")
+    t = random_tensors(cfg, POLICIES["tiny"], seed=2)
+    parts = write_gguf_split(str(tmp_path / "m.gguf"), cfg, t, 3)
+    assert split_paths(parts[1]) == parts
+    g = read_gguf_split(parts[0])
+    assert g.metadata["split.count"] == 3 and g.architecture == "llama"
+    back = tensors_from_gguf(g)
+    assert set(back) == set(t)
+    for k in t:
+        assert torch.equal(back[k].data, t[k].data), k
+    # opening any part finds the whole model
+    assert set(read_gguf_split(parts[2]).tensors) == set(t)
