@@ -55,8 +55,21 @@ def load(args, need_engine: bool = True):
         from .engine.engine import Engine, EngineConfig
 
         preset = getattr(args, "preset", None)
+        tp = int(getattr(args, "tp", 1) or 1)
+        if tp > 1:  # one process per GPU under torchrun: this rank's GPU
+            import os
+
+            import torch
+
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            device = f"cuda:{local}"
+        if int(getattr(args, "pp", 1) or 1) > 1:
+            raise SystemExit("--pp: pipeline stages are not built; on one NVSwitch node use --tp (and --ep) instead")
         kw = dict(max_model_len=cfg.max_ctx, device=device, ser_threshold=ser,
-                  fused_moe=getattr(args, "fmoe", True) or True,
+                  fused_moe=not getattr(args, "no_fmoe", False), tp=tp,
+                  fused_comm=getattr(args, "comm", "fused") != "nccl",
+                  block_size=int(getattr(args, "block_size", 16) or 16),
                   kv_dtype=getattr(args, "kv_dtype", "fp16") or "fp16",
                   max_num_seqs=getattr(args, "max_batch", 64) or 64,
                   prefix_caching=bool(getattr(args, "prefix_cache", False)),
@@ -348,6 +361,15 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("--kv-cache-gb", type=float, default=8.0)
         p.add_argument("--max-batch", type=int, default=64)
         p.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
+        p.add_argument("--ep", type=int, default=0,
+                       help="expert-parallel ranks (experts are split over the --tp ranks; must equal --tp)")
+        p.add_argument("--pp", type=int, default=1, help="pipeline stages (not built: use --tp on one node)")
+        p.add_argument("--dp", type=int, default=1,
+                       help="data-parallel replicas: launch one process per GPU, each with its own engine")
+        p.add_argument("--comm", choices=["fused", "nccl"], default="fused",
+                       help="TP all-reduce: fused one-shot kernel over NVLink peer memory, or NCCL")
+        p.add_argument("--block-size", type=int, default=16, help="KV cache page size (tokens)")
+        p.add_argument("--no-fmoe", action="store_true", help="unfused per-expert MoE loop (baseline)")
         p.add_argument("--prefix-cache", action="store_true")
         p.add_argument("--mla", action="store_true", help="DeepSeek MLA latent cache (on for deepseek2 models)")
         p.add_argument("--fmoe", action="store_true", help="fused MoE routing/dispatch (default path)")
