@@ -297,7 +297,7 @@ class Engine:
         bt = np.full((B, self.max_blocks_per_seq), self.dummy_block, np.int32)
         for i, s in enumerate(seqs):
             p = s.n_tokens - 1
-            ids[i] = s.tokens[-1]
+            ids[i] = s.last_token
             pos[i] = p
             slots[i] = self._slot_of(s, p)
             lens[i] = s.n_tokens
@@ -355,7 +355,7 @@ class Engine:
             h = np.full((B, nh), -1, np.int32)
             for i, s in enumerate(seqs):
                 pa[i] = (s.params.repetition_penalty, s.params.frequency_penalty, s.params.presence_penalty)
-                last = s.tokens[-s.params.penalty_last_n:] if s.params.penalty_last_n > 0 else []
+                last = s.last_tokens(s.params.penalty_last_n) if s.params.penalty_last_n > 0 else []
                 h[i, : len(last)] = last
             pen, hist = self._to_dev(pa), self._to_dev(h)
         host = [i for i, s in enumerate(seqs) if s.host_sampler is not None]

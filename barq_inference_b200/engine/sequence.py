@@ -22,7 +22,7 @@ class SeqStatus(enum.Enum):
     FINISHED = "finished"
 
 
-@dataclass
+@dataclass(eq=False)  # identity semantics: membership tests in scheduler lists stay O(1) per item
 class Sequence:
     prompt: list[int]
     params: SamplingParams
@@ -46,6 +46,17 @@ class Sequence:
     @property
     def tokens(self) -> list[int]:
         return self.prompt + self.output
+
+    @property
+    def last_token(self) -> int:
+        return self.output[-1] if self.output else self.prompt[-1]
+
+    def last_tokens(self, n: int) -> list[int]:
+        """The last ``n`` tokens (prompt + output) without building the whole list."""
+        if n <= len(self.output):
+            return self.output[len(self.output) - n:]
+        k = n - len(self.output)
+        return self.prompt[max(0, len(self.prompt) - k):] + self.output
 
     @property
     def n_tokens(self) -> int:

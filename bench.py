@@ -222,6 +222,20 @@ def main():
     barrier()
     ck = clocks.stop()
     dec_ms = max_over_ranks(e0.elapsed_time(e1))
+    # device time of the decode step alone: back-to-back replays of the captured graph (no host work
+    # in between); ms_per_step minus this is the engine's host overhead per step
+    replay_ms = None
+    if eng.graphs:
+        gb = eng.graphs[max(eng.graphs)]
+        gb.graph.replay()
+        barrier()
+        r0, r1 = ev(), ev()
+        r0.record()
+        for _ in range(10):
+            gb.graph.replay()
+        r1.record()
+        torch.cuda.synchronize()
+        replay_ms = max_over_ranks(r0.elapsed_time(r1) / 10)
     while eng.has_work():
         eng.step()
     # kernel launches per decode step: one eager (non-graph) forward of the same batch, counted
@@ -274,6 +288,7 @@ def main():
                 "prefill_tok_s": round(mult * B * P / (prefill_ms / 1e3), 1),
                 "ttft_p50_ms_512": round(statistics.median(ttfts), 3) if ttfts else None,
                 "init_s": round(init_s, 1),
+                "decode_graph_replay_ms": round(replay_ms, 4) if replay_ms is not None else None,
             },
             "e2e": {"value": round(mult * e2e_dec, 2), "unit": "tokens/s decode via Engine.generate()",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
