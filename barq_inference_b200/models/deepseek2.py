@@ -137,6 +137,7 @@ class DeepseekV2Runner(LlamaRunner):
     def forward(self, inp: StepInput) -> torch.Tensor:
         cfg = self.cfg
         T = inp.ids.numel()
+        ops.set_pdl(T <= GEMV_MAX_T)
         x = ops.embed(self.embed_w, inp.ids)
         for li, L in enumerate(self.layers):
             self._mla(L, li, x, inp, T)

@@ -228,6 +228,9 @@ class LlamaRunner:
     def forward(self, inp: StepInput) -> torch.Tensor:
         """Logits (f32) of the last new token of each sequence: [S, vocab]."""
         T = inp.ids.numel()
+        # programmatic dependent launch pays off where launches are short (GEMV-sized steps); next to
+        # the persistent GEMM, early-launched waiting CTAs only take SM resources
+        ops.set_pdl(T <= GEMV_MAX_T)
         if T > GEMV_MAX_T and self.use_gemm is not False:
             return self._forward_gemm(inp)
         return self._forward_gemv(inp)

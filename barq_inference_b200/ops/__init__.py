@@ -176,6 +176,11 @@ def gemm(w: QWeight, x: torch.Tensor, mode: int = EPI_STORE_F32, out: torch.Tens
     return out
 
 
+def set_pdl(on: bool) -> None:
+    """Launch the following kernels with (True) or without programmatic dependent launch."""
+    require_ext().set_pdl_mode(1 if on else 0)
+
+
 def gemm_error() -> int:
     """Sticky device error word of the tcgen05 kernels (0 = ok; 0x100|site = bounded wait expired)."""
     return int(require_ext().gemm_error())

@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "kernels/launch.h"
+#include "kernels/pdl.cuh"
 
 using torch::Tensor;
 using OptT = c10::optional<Tensor>;
@@ -342,6 +343,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("mla_kv_write", &mla_kv_write);
   m.def("allreduce_add", &allreduce_add);
+  m.def("set_pdl_mode", [](int64_t m) { barq::set_pdl_mode((int)m); });
   m.def("mla_attn_scratch_floats", &mla_attn_scratch_floats);
   m.def("mla_attention", &mla_attention);
   m.def("gemm_clear_error", &gemm_clear_error);

@@ -227,11 +227,13 @@ int rope_kv_write(const RopeKVArgs& a, cudaStream_t st) {
 }  // namespace barq
 
 namespace barq {
+static int g_pdl_mode = -1;  // -1: from BARQ_PDL (default on), 0: off, 1: on
 bool pdl_enabled() {
-  static const bool on = [] {
+  static const bool env_on = [] {
     const char* e = getenv("BARQ_PDL");
     return !(e && e[0] == '0');
   }();
-  return on;
+  return env_on && g_pdl_mode != 0;
 }
+void set_pdl_mode(int mode) { g_pdl_mode = mode; }
 }  // namespace barq
