@@ -207,9 +207,10 @@ def rope_kv_write(qkv, pos, slots, cos_t, sin_t, H, Hkv, D, rot, neox, kcache, v
 
 
 def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
-    """KV splits per (sequence, KV head): enough CTAs to cover the SMs, at most 16 (a split of a
-    typical decode context still holds several 16-token pages)."""
-    return max(1, min(16, math.ceil(2 * n_sm / max(1, B * Hkv))))
+    """KV splits per (sequence, KV head): about 4 CTAs per SM (each CTA streams its pages with 4
+    warps, so this keeps ~16 page loads in flight per SM), at most 16 (a split of a typical decode
+    context still holds several 16-token pages)."""
+    return max(1, min(16, math.ceil(4 * n_sm / max(1, B * Hkv))))
 
 
 def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,

@@ -37,12 +37,21 @@ template <> BARQ_DEV void cvt8<__nv_bfloat16>(const int4& raw, float* f) {
     f[2 * i + 1] = v.y;
   }
 }
-template <typename TC> BARQ_DEV void cvt_n(const TC* p, float* f, int n) {
-#pragma unroll
-  for (int i = 0; i < n; ++i) f[i] = to_f(p[i]);
-}
 
 constexpr int kBS = 16;  // tokens per KV page
+
+// This lane's DPL consecutive V elements of one token, kept packed in registers until used.
+template <typename TC, int DPL>
+struct VRow {
+  using R = typename std::conditional<DPL * sizeof(TC) == 8, uint2, uint32_t>::type;
+  R r;
+  BARQ_DEV void load(const TC* p) { r = __ldg(reinterpret_cast<const R*>(p)); }
+  BARQ_DEV void cvt(float* f) const {
+    const TC* e = reinterpret_cast<const TC*>(&r);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) f[i] = to_f(e[i]);
+  }
+};
 
 template <typename TC, int D, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
@@ -91,6 +100,12 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
     const int phys = bt[blk];
     const size_t page = ((size_t)phys * a.Hkv + kvh) * kBS;
     const TC* krow = kc + (page + tok) * D;
+    // The page's V rows are loaded together with K (they do not depend on the scores), so a page
+    // costs one DRAM round trip instead of two.
+    const TC* vpage = vc + page * D;
+    VRow<TC, DPL> vr[kBS];
+#pragma unroll
+    for (int t = 0; t < kBS; ++t) vr[t].load(vpage + (size_t)t * D + lane * DPL);
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) s[g] = 0.f;
@@ -129,11 +144,10 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
 #pragma unroll
       for (int j = 0; j < DPL; ++j) acc[g][j] *= corr;
     }
-    const TC* vpage = vc + page * D;
-#pragma unroll 4
+#pragma unroll
     for (int t = 0; t < kBS; ++t) {
       float vf[DPL];
-      cvt_n<TC>(vpage + (size_t)t * D + lane * DPL, vf, DPL);
+      vr[t].cvt(vf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float pt = __shfl_sync(0xffffffffu, p[g], 2 * t);
