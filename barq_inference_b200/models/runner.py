@@ -26,6 +26,11 @@ from .rope import attn_scale, rope_cos_sin
 from .weights import PackedTensor
 
 GEMV_MAX_T = 8
+# Optional large-T route (env BARQ_DENSE_T = token threshold, 0 = off, the default): a projection
+# dequantizes its whole weight once (csrc dequant_dense) and runs a dense GEMM (a plain library GEMM).
+# Measured on Llama-3-8B prefill (8192-token chunks) it was slower than the fused-dequant tcgen05 GEMM
+# (33k vs 43k tokens/s: the separate SwiGLU / fp16 output passes cost more than the mainloop saves).
+DENSE_T = int(__import__("os").environ.get("BARQ_DENSE_T", "0"))
 
 
 @dataclass
@@ -199,8 +204,36 @@ class LlamaRunner:
         hb, hq = ops.rmsnorm(x, norm_w, eps, want_q8=True, want_bf16=self._needs_bf16(w), x2=self.x2)
         return self._lin_q8(w, hq, T, mode, out=out, bias=bias, xb=hb)
 
+    def _dense_ok(self, w, T: int) -> bool:
+        return DENSE_T > 0 and T >= DENSE_T and isinstance(w, QWeight) and w.wtype != ops.W_BF16
+
+    def _dense_gemm(self, w, xb: torch.Tensor, mode: int, out=None, bias=None):
+        """Large-T projection: dequantize w into a reused scratch, then a dense GEMM."""
+        n = w.N * w.K
+        sc = getattr(self, "_dense_scratch", None)
+        if sc is None or sc.numel() < n or sc.dtype != xb.dtype:
+            sc = self._dense_scratch = torch.empty(n, dtype=xb.dtype, device=self.device)
+        wd = ops.dequant_dense(w, sc[:n].view(w.N, w.K))
+        y = torch.matmul(xb, wd.t())
+        if mode == EPI_SWIGLU_Q8:  # rows interleaved [32 gate | 32 up] per group
+            T = y.shape[0]
+            g4 = y.view(T, -1, 2, 32)
+            return (torch.nn.functional.silu(g4[:, :, 0, :].float()) * g4[:, :, 1, :].float()).reshape(T, -1).to(
+                xb.dtype)
+        if bias is not None:
+            y = y.float() + bias
+        if mode == EPI_ADD_F32:
+            out.add_(y)
+            return out
+        if out is None:
+            return y.float()
+        out.copy_(y)
+        return out
+
     def _lin_bf16(self, w, xb: torch.Tensor, T: int, mode: int, out=None, bias=None):
         """Projection of bf16 activations [T, K] on the tcgen05 GEMM (K2)."""
+        if self._dense_ok(w, T):
+            return self._dense_gemm(w, xb, mode, out=out, bias=bias)
         if isinstance(w, tuple):
             r = torch.cat([self._lin_bf16(wi, xb, T, EPI_STORE_F32) for wi in w], 1)
             if bias is not None:
@@ -263,7 +296,9 @@ class LlamaRunner:
             if L.moe is not None:
                 self._moe_out(L, hq, hb, T, x)
                 continue
-            if L.gu_interleaved:
+            if L.gu_interleaved and self._dense_ok(L.gate_up, T):
+                h = self._dense_gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
+            elif L.gu_interleaved:
                 h = ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
             else:
                 gu = self._lin_bf16(L.gate_up, hb, T, EPI_STORE_F32)

@@ -327,6 +327,15 @@ def dequant_rows(w: QWeight, r0: int = 0, n: int | None = None) -> torch.Tensor:
     return out
 
 
+def dequant_dense(w: QWeight, out: torch.Tensor | None = None, dtype=torch.float16) -> torch.Tensor:
+    """Whole quantized weight -> row-major ``dtype`` [N, K] (fp16 / bf16), one CTA per weight chunk."""
+    if out is None:
+        out = torch.empty(w.N, w.K, dtype=dtype, device=w.device)
+    require_ext().dequant_dense(*w.args(), out)
+    _count()
+    return out
+
+
 def sample(logits, temperature, top_k, top_p, min_p, seeds, steps, allow_mask=None, penalties=None,
            history=None, want_logprob=False):
     B, V = logits.shape

@@ -188,6 +188,15 @@ void allreduce_add(Tensor x, std::vector<int64_t> bufs, std::vector<int64_t> fla
   check(barq::allreduce_add(a, cur_stream()), "allreduce_add");
 }
 
+void dequant_dense(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor out) {
+  c10::cuda::CUDAGuard g(p0.device());
+  TORCH_CHECK(out.is_contiguous() && out.numel() >= N * K &&
+                  (out.scalar_type() == torch::kHalf || out.scalar_type() == torch::kBFloat16),
+              "dequant_dense: out must be contiguous fp16/bf16 [N, K]");
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  check(barq::dequant_dense(w, out.data_ptr(), out.scalar_type() == torch::kHalf, cur_stream()), "dequant_dense");
+}
+
 int64_t gemm_error() {
   int v = 0;
   TORCH_CHECK(barq::gemm_error_word(&v) == 0, "gemm_error: read failed");
@@ -343,6 +352,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("mla_kv_write", &mla_kv_write);
   m.def("allreduce_add", &allreduce_add);
+  m.def("dequant_dense", &dequant_dense);
   m.def("set_pdl_mode", [](int64_t m) { barq::set_pdl_mode((int)m); });
   m.def("mla_attn_scratch_floats", &mla_attn_scratch_floats);
   m.def("mla_attention", &mla_attention);

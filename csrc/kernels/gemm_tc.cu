@@ -715,6 +715,61 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && err_s && g.err) atomicExch(g.err, err_s);
 }
 
+// ------------------------------------------------------------------------------------ dense dequant
+// Whole weight -> row-major fp16/bf16 [N, K], one CTA per tiled chunk (128 rows x G columns): the
+// chunk is staged in shared memory with 16-byte loads, then each thread expands 32-weight
+// sub-blocks with the GEMM's own dequant32 and writes 64 contiguous bytes.  Used for large-T
+// prefill, where dequantizing once and running a dense tensor-core GEMM beats expanding every
+// weight tile inside the GEMM mainloop.
+template <int WT, bool F16>
+__global__ void __launch_bounds__(512) dequant_dense_kernel(const uint8_t* __restrict__ w, int N, int K,
+                                                           void* __restrict__ out) {
+  using F = TileFmt<WT>;
+  __shared__ __align__(16) uint8_t ch[F::CHUNK];
+  const int KG = K / F::G;
+  const int nt = blockIdx.x / KG, kg = blockIdx.x % KG;
+  const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)blockIdx.x * F::CHUNK);
+  for (int i = threadIdx.x; i < F::CHUNK / 16; i += blockDim.x) reinterpret_cast<uint4*>(ch)[i] = src[i];
+  __syncthreads();
+  constexpr int SB = F::G / 32;  // 32-weight sub-blocks per chunk row
+  using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
+  AT* o = reinterpret_cast<AT*>(out);
+  for (int task = threadIdx.x; task < 128 * SB; task += blockDim.x) {
+    const int r = task / SB, j8 = task % SB;
+    const int row = nt * 128 + r;
+    if (row >= N) continue;
+    uint4 v[4];
+    dequant32<WT, F16>(ch, r, j8 >> 1, j8 & 1, v);
+    uint4* dst = reinterpret_cast<uint4*>(o + (size_t)row * K + (size_t)kg * F::G + j8 * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = v[i];
+  }
+}
+
+template <int WT>
+static int launch_dense(const QW& w, void* out, int f16, cudaStream_t st) {
+  using F = TileFmt<WT>;
+  const int blocks = ((w.N + 127) / 128) * (w.K / F::G);
+  cudaError_t e = f16 ? launch_pdl(dequant_dense_kernel<WT, true>, dim3(blocks), dim3(512), 0, st, w.p0, w.N, w.K, out)
+                      : launch_pdl(dequant_dense_kernel<WT, false>, dim3(blocks), dim3(512), 0, st, w.p0, w.N, w.K, out);
+  return e == cudaSuccess ? 0 : -20;
+}
+
+int dequant_dense(const QW& w, void* out, int out_f16, cudaStream_t st) {
+  const int G = (w.type == W_Q4_K || w.type == W_Q5_K || w.type == W_Q6_K) ? 256 : 64;
+  if (w.K % G) return -2;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(w.p0) & 15)) return -3;
+  switch (w.type) {
+    case W_Q4_K: return launch_dense<W_Q4_K>(w, out, out_f16, st);
+    case W_Q5_K: return launch_dense<W_Q5_K>(w, out, out_f16, st);
+    case W_Q6_K: return launch_dense<W_Q6_K>(w, out, out_f16, st);
+    case W_Q8_0: return launch_dense<W_Q8_0>(w, out, out_f16, st);
+    case W_Q4_0: return launch_dense<W_Q4_0>(w, out, out_f16, st);
+    case W_IQ4_NL: return launch_dense<W_IQ4_NL>(w, out, out_f16, st);
+  }
+  return -7;
+}
+
 // ------------------------------------------------------------------------------------ host side
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {

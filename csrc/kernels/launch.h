@@ -105,6 +105,8 @@ struct GemmGroups {
 };
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st,
              const GemmGroups* grp = nullptr);
+// Whole quantized weight (tiled layout) -> row-major fp16 (out_f16) or bf16 [N, K].
+int dequant_dense(const QW& w, void* out, int out_f16, cudaStream_t st);
 int gemm_error_word(int* host_out);
 int* kernel_err_word();  // device error word shared by the bounded-wait kernels (per device)
 // Streaming decode GEMV (1..8 tokens): persistent, bulk-copy fed, stream-K over weight chunks.

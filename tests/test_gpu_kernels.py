@@ -114,6 +114,17 @@ def test_gemv_fused_norm(t, B, x2):
         assert (hs - hs_ref).abs().max() <= hs_ref.abs().max() / 50
 
 
+@pytest.mark.parametrize("t", TYPES)
+def test_dequant_dense_matches_oracle(t):
+    N, K = 300, 512
+    qw, ref, _ = _qw(t, N, K, seed=6)
+    for dt in (torch.float16, torch.bfloat16):
+        d = ops.dequant_dense(qw, dtype=dt).float().cpu()
+        # the GEMM's operand numerics: per-block scale and min rounded to the operand type, one FMA
+        tol = ref.abs().max() * (2e-3 if dt == torch.float16 else 1.6e-2)
+        assert (d - ref).abs().max() <= tol, (t, dt, (d - ref).abs().max())
+
+
 def test_bf16_gemv():
     N, K, B = 100, 688, 3
     w = torch.randn(N, K) * 0.02

@@ -119,3 +119,17 @@ def test_batched_decode_gemm_path_matches_gemv_path():
         outs.append([r.tokens for r in eng.generate(prompts, SamplingParams.greedy_params(max_tokens=6))])
     same = sum(a == b for a, b in zip(outs[0], outs[1]))
     assert same >= 14, same  # bf16 GEMM vs two-term int8 GEMV: random-init logits are near-ties
+
+
+def test_dense_prefill_path_matches_fused(monkeypatch):
+    """Large-T prefill route (dequantize the weight once + dense GEMM) == fused-dequant GEMM route."""
+    import barq_inference_b200.models.runner as rmod
+
+    cfg, tensors, prompt = _tiny()
+    outs = []
+    for dense_t in (0, 16):
+        monkeypatch.setattr(rmod, "DENSE_T", dense_t)
+        runner = LlamaRunner(cfg, tensors, DEV)
+        runner.allocate_kv(64)
+        outs.append(_run(runner, prompt, 0, list(range(1, 10)), decode=False))
+    assert (outs[0] - outs[1]).abs().max().item() < 2e-2
