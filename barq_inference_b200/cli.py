@@ -64,10 +64,19 @@ def load(args, need_engine: bool = True):
             local = int(os.environ.get("LOCAL_RANK", "0"))
             torch.cuda.set_device(local)
             device = f"cuda:{local}"
-        if int(getattr(args, "pp", 1) or 1) > 1:
-            raise SystemExit("--pp: pipeline stages are not built; on one NVSwitch node use --tp (and --ep) instead")
+        pp = int(getattr(args, "pp", 1) or 1)
+        if pp > 1 and tp > 1:
+            raise SystemExit("--pp with --tp: combined pipeline x tensor parallelism is not built; pick one")
+        if pp > 1:
+            import os
+
+            import torch
+
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            device = f"cuda:{local}"
         kw = dict(max_model_len=cfg.max_ctx, device=device, ser_threshold=ser,
-                  fused_moe=not getattr(args, "no_fmoe", False), tp=tp,
+                  fused_moe=not getattr(args, "no_fmoe", False), tp=tp, pp=pp,
                   fused_comm=getattr(args, "comm", "fused") != "nccl",
                   block_size=int(getattr(args, "block_size", 16) or 16),
                   kv_dtype=getattr(args, "kv_dtype", "fp16") or "fp16",
@@ -363,7 +372,7 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
         p.add_argument("--ep", type=int, default=0,
                        help="expert-parallel ranks (experts are split over the --tp ranks; must equal --tp)")
-        p.add_argument("--pp", type=int, default=1, help="pipeline stages (not built: use --tp on one node)")
+        p.add_argument("--pp", type=int, default=1, help="pipeline stages (launch with torchrun; layers split contiguously)")
         p.add_argument("--dp", type=int, default=1,
                        help="data-parallel replicas: launch one process per GPU, each with its own engine")
         p.add_argument("--comm", choices=["fused", "nccl"], default="fused",

@@ -48,6 +48,7 @@ class EngineConfig:
     fused_moe: bool = True          # --fmoe
     act_x2: bool = True             # two-term int8 decode activations (False: single int8 term)
     tp: int = 1                     # tensor parallel degree (one process per GPU, torch.distributed)
+    pp: int = 1                     # pipeline stages (one process per GPU, contiguous layer ranges)
     rank_timeout_s: float = 30.0    # TP: a peer without a heartbeat for this long fails the step
     fused_comm: bool = True         # TP: fused one-shot all-reduce kernel (False: NCCL all-reduce)
 
@@ -436,6 +437,25 @@ class Engine:
 
 
 def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
+    if ec.pp > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from ..parallel.pp import PPInfo, shard_pp, stage_layers
+
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", device_id=torch.device(device), timeout=datetime.timedelta(seconds=120))
+        stage, world = dist.get_rank(), dist.get_world_size()
+        if world != ec.pp:
+            raise ValueError(f"pp={ec.pp} but the process group has {world} ranks")
+        l0, l1 = stage_layers(cfg.n_layers, world)[stage]
+        r = LlamaRunner(cfg, shard_pp(tensors, cfg.n_layers, stage, world), device, kv_dtype, act_x2=ec.act_x2,
+                        pp=PPInfo(stage, world, l0, l1))
+        r.ser_threshold = ec.ser_threshold
+        r.fused_moe = ec.fused_moe
+        dist.barrier()
+        return r
     if ec.tp > 1:
         from ..parallel.comm import Comm
         from ..parallel.tp import shard_config, shard_tensors

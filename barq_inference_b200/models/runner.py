@@ -66,8 +66,11 @@ class Layer:
 class LlamaRunner:
     def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], device="cuda",
                  kv_dtype: torch.dtype = torch.float16, use_gemm: bool | None = None, act_x2: bool = True,
-                 tp=None, comm=None):
+                 tp=None, comm=None, pp=None):
         self.cfg = cfg
+        # pipeline parallel: ``pp`` (parallel.pp.PPInfo) -- this rank runs layers [l0, l1); stage 0
+        # embeds, the last stage computes the logits and broadcasts them
+        self.pp = pp
         # tensor parallel: ``tp`` (parallel.tp.TPInfo) describes this rank's shard, ``comm``
         # (parallel.comm.Comm) completes the row-parallel partial sums; None = one GPU
         self.tp, self.comm = tp, comm
@@ -81,12 +84,13 @@ class LlamaRunner:
         # expansion in the GEMM mainloop) unless the family is known to overflow fp16 (DeepSeek)
         self.act_dtype = torch.bfloat16 if cfg.arch.startswith("deepseek") else torch.float16
         dev = self.device
-        self.embed_w = _qw(tensors["token_embd.weight"], dev)
-        self.out_norm = _f32(tensors["output_norm.weight"], dev)
+        self.embed_w = _qw(tensors["token_embd.weight"], dev) if "token_embd.weight" in tensors else None
+        self.out_norm = _f32(tensors["output_norm.weight"], dev) if "output_norm.weight" in tensors else None
         self.out_w = _qw(tensors["output.weight"], dev) if "output.weight" in tensors else self.embed_w
         self.layers: list[Layer] = []
         F = cfg.ffn
-        for i in range(cfg.n_layers):
+        l0, l1 = (pp.l0, pp.l1) if pp is not None else (0, cfg.n_layers)
+        for i in range(l0, l1):
             p = f"blk.{i}."
             L = Layer()
             L.attn_norm = _f32(tensors[p + "attn_norm.weight"], dev)
@@ -118,15 +122,16 @@ class LlamaRunner:
     # ------------------------------------------------------------------ KV cache
     def allocate_kv(self, num_blocks: int, block_size: int = 16) -> list[tuple[torch.Tensor, torch.Tensor]]:
         cfg = self.cfg
-        shape = (cfg.n_layers, 2, num_blocks, cfg.n_kv_heads, block_size, cfg.head_dim)
+        nl = len(self.layers)  # this rank's layers (all of them unless pipeline parallel)
+        shape = (nl, 2, num_blocks, cfg.n_kv_heads, block_size, cfg.head_dim)
         kv = torch.zeros(shape, dtype=self.kv_dtype, device=self.device)
         self.kv_storage = kv
-        self.kv = [(kv[i, 0], kv[i, 1]) for i in range(cfg.n_layers)]
+        self.kv = [(kv[i, 0], kv[i, 1]) for i in range(nl)]
         return self.kv
 
     def kv_bytes_per_block(self, block_size: int = 16) -> int:
         cfg = self.cfg
-        return cfg.n_layers * 2 * cfg.n_kv_heads * block_size * cfg.head_dim * torch.finfo(self.kv_dtype).bits // 8
+        return len(self.layers) * 2 * cfg.n_kv_heads * block_size * cfg.head_dim * torch.finfo(self.kv_dtype).bits // 8
 
     # ------------------------------------------------------------------ linear layers
     def _lin_q8(self, w, x: Q8Act, T: int, mode: int, out=None, bias=None, xb=None):
@@ -178,6 +183,31 @@ class LlamaRunner:
                 out.zero_()
             L.moe.forward(self, hq, hb, T, out)
         self._row_parallel(1, fn, x)
+
+    # ------------------------------------------------------------------ pipeline stages
+    def _stage_input(self, inp: StepInput) -> torch.Tensor:
+        """Stage 0 (or a single GPU): embeddings.  Later stages: the previous stage's hidden states."""
+        if self.pp is None or self.pp.stage == 0:
+            return ops.embed(self.embed_w, inp.ids)
+        x = torch.empty(inp.ids.numel(), self.cfg.hidden, dtype=torch.float32, device=self.device)
+        self.pp.recv(x)
+        return x
+
+    def _stage_forward(self, x: torch.Tensor, inp: StepInput) -> bool:
+        """True if this stage hands its hidden states on (and computes no logits)."""
+        if self.pp is None or self.pp.is_last:
+            return False
+        self.pp.send(x)
+        return True
+
+    def _stage_logits(self, inp: StepInput, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """Every stage returns the same logits: the last stage broadcasts them."""
+        if self.pp is None:
+            return logits
+        if logits is None:
+            logits = torch.empty(inp.last_idx.numel(), self.cfg.vocab, dtype=torch.float32, device=self.device)
+        self.pp.broadcast_logits(logits)
+        return logits
 
     def _gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
         """Vocab-parallel head: every rank holds a slice of the vocabulary; all-gather the logits."""
@@ -285,7 +315,7 @@ class LlamaRunner:
         """Many tokens (prefill, batched decode): bf16 activations on the tcgen05 GEMM."""
         cfg = self.cfg
         T = inp.ids.numel()
-        x = ops.embed(self.embed_w, inp.ids)
+        x = self._stage_input(inp)
         for li, L in enumerate(self.layers):
             hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
             qkv = self._lin_bf16(L.qkv, hb, T, EPI_STORE_F32, bias=L.qkv_bias)
@@ -304,19 +334,21 @@ class LlamaRunner:
                 gu = self._lin_bf16(L.gate_up, hb, T, EPI_STORE_F32)
                 h, _ = ops.swiglu(gu, cfg.ffn, want_bf16=True, act_dtype=self.act_dtype)
             self._row_parallel(1, lambda m, o: self._lin_bf16(L.down, h, T, m, out=o), x)
+        if self._stage_forward(x, inp):
+            return self._stage_logits(inp)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
         ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
         if xl.shape[0] <= GEMV_MAX_T:
             _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
-            return self._gather_logits(self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32,
-                                                    xb=ob.to(torch.bfloat16)))
-        return self._gather_logits(self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32))
+            return self._stage_logits(inp, self._gather_logits(
+                self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32, xb=ob.to(torch.bfloat16))))
+        return self._stage_logits(inp, self._gather_logits(self._lin_bf16(self.out_w, ob, xl.shape[0], EPI_STORE_F32)))
 
     def _forward_gemv(self, inp: StepInput) -> torch.Tensor:
         cfg = self.cfg
         T = inp.ids.numel()
         H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        x = ops.embed(self.embed_w, inp.ids)
+        x = self._stage_input(inp)
         for li, L in enumerate(self.layers):
             kc, vc = self.kv[li]
             qkv = self._norm_lin(L.qkv, x, L.attn_norm, T, EPI_STORE_F32, bias=L.qkv_bias)
@@ -347,5 +379,7 @@ class LlamaRunner:
                 hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16,
                                       x2=self.x2)
                 self._row_parallel(1, lambda m, o: self._lin_q8(L.down, hq2, T, m, out=o, xb=hb2), x)
+        if self._stage_forward(x, inp):
+            return self._stage_logits(inp)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
-        return self._head(xl)
+        return self._stage_logits(inp, self._head(xl))

@@ -85,3 +85,50 @@ def test_tp2_matches_single_gpu(name, fused):
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in ps)
     assert err < 2e-2, err
+
+
+def _pp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+
+    import torch.distributed as dist
+
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.models.runner import LlamaRunner
+    from barq_inference_b200.parallel.pp import PPInfo, shard_pp, stage_layers
+
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    cfg = preset("tiny")
+    full = random_tensors(cfg, POLICIES["tiny"], seed=4)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
+    l0, l1 = stage_layers(cfg.n_layers, world)[rank]
+    r = LlamaRunner(cfg, shard_pp(full, cfg.n_layers, rank, world), dev, pp=PPInfo(rank, world, l0, l1))
+    r.allocate_kv(32)
+    pp_logits = _logits(r, prompt)
+    if rank == 0:
+        ref = LlamaRunner(cfg, full, dev)
+        ref.allocate_kv(32)
+        q.put(("ok", (pp_logits - _logits(ref, prompt)).abs().max().item()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@needs2
+def test_pp2_matches_single_gpu():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_pp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    status, err = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in ps)
+    assert err < 1e-3, err

@@ -97,3 +97,19 @@ def test_row_parallel_reduction_gloo():
         p.join(timeout=60)
     want = [float(i) + 1 + 2 for i in range(8)]  # residual + sum of partials (1 + 2)
     assert res[0] == want and res[1] == want
+
+
+def test_pipeline_stage_split_and_tensor_filter():
+    from barq_inference_b200.parallel.pp import shard_pp, stage_layers
+
+    assert stage_layers(32, 4) == [(0, 8), (8, 16), (16, 24), (24, 32)]
+    assert stage_layers(5, 2) == [(0, 3), (3, 5)]
+    with pytest.raises(ValueError):
+        stage_layers(2, 3)
+    cfg = preset("tiny")
+    full = random_tensors(cfg, POLICIES["tiny"], seed=1)
+    s0, s1 = (shard_pp(full, cfg.n_layers, s, 2) for s in range(2))
+    assert "token_embd.weight" in s0 and "output_norm.weight" not in s0
+    assert "output_norm.weight" in s1 and "blk.0.attn_q.weight" not in s1
+    assert {k for k in s0 if k.startswith("blk.")} | {k for k in s1 if k.startswith("blk.")} == \
+        {k for k in full if k.startswith("blk.")}
