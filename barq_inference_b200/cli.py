@@ -366,7 +366,7 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("-m", "--model", required=True)
         p.add_argument("--device", choices=["cuda", "cpu"])
         p.add_argument("--context-size", type=int, default=2048)
-        p.add_argument("--kv-dtype", choices=["fp16", "bf16"], default="fp16")
+        p.add_argument("--kv-dtype", choices=["fp16", "bf16", "fp8"], default="fp16")
         p.add_argument("--kv-cache-gb", type=float, default=8.0)
         p.add_argument("--max-batch", type=int, default=64)
         p.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")

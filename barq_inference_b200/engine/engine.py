@@ -38,7 +38,7 @@ class EngineConfig:
     block_size: int = 16
     num_blocks: int | None = None   # None -> sized from kv_cache_gb
     kv_cache_gb: float = 8.0
-    kv_dtype: str = "fp16"          # fp16 | bf16
+    kv_dtype: str = "fp16"          # fp16 | bf16 | fp8 (e4m3, unscaled)
     cuda_graphs: bool = True
     graph_buckets: tuple[int, ...] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
     prefix_caching: bool = False
@@ -85,7 +85,7 @@ class Engine:
         self.cfg = cfg
         self.ecfg = ec = engine_cfg or EngineConfig()
         self.device = torch.device(ec.device)
-        kv_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16}[ec.kv_dtype]
+        kv_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}[ec.kv_dtype]
         self.runner = runner or make_runner(cfg, tensors, self.device, kv_dtype, ec)
         self.max_blocks_per_seq = (ec.max_model_len + ec.block_size - 1) // ec.block_size
         nb = ec.num_blocks

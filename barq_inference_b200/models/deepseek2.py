@@ -35,6 +35,8 @@ class DeepseekV2Runner(LlamaRunner):
                  kv_dtype: torch.dtype = torch.bfloat16, ser_threshold: float = 0.0, act_x2: bool = True):
         if cfg.kv_lora_rank != LAT or cfg.qk_rope_dim != ROPE or cfg.n_heads != 16:
             raise ValueError("DeepseekV2Runner: the MLA kernel is built for 16 heads, latent 512, rope 64")
+        if kv_dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("DeepseekV2Runner: the latent KV cache is float16 or bfloat16 (no fp8 MLA kernel)")
         from .reference import dequant_tensor
 
         self.cfg = cfg

@@ -26,6 +26,12 @@ void check(int rc, const char* what) {
 }
 
 int is_f16(const OptT& t) { return t.has_value() && t->defined() && t->scalar_type() == torch::kHalf; }
+int cache_type_of(const torch::Tensor& c) {
+  if (c.scalar_type() == torch::kBFloat16) return barq::kCacheBF16;
+  if (c.scalar_type() == torch::kFloat8_e4m3fn) return barq::kCacheFP8;
+  TORCH_CHECK(c.scalar_type() == torch::kHalf, "KV cache must be float16, bfloat16 or float8_e4m3fn");
+  return barq::kCacheF16;
+}
 
 barq::ActOut act_out(const OptT& q, const OptT& s, const OptT& ql, const OptT& dl) {
   return barq::ActOut{optptr<int8_t>(q), optptr<float2>(s), optptr<int8_t>(ql), optptr<float2>(dl)};
@@ -250,7 +256,7 @@ void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor co
   a.q_out = ptr<__nv_bfloat16>(q_out);
   a.kcache = kcache.data_ptr();
   a.vcache = vcache.data_ptr();
-  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.cache_type = cache_type_of(kcache);
   a.block_size = (int)kcache.size(-2);
   check(barq::rope_kv_write(a, cur_stream()), "rope_kv_write");
 }
@@ -266,7 +272,7 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.q = ptr<const __nv_bfloat16>(q);
   a.kcache = kcache.data_ptr();
   a.vcache = vcache.data_ptr();
-  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.cache_type = cache_type_of(kcache);
   a.block_tables = ptr<const int>(block_tables);
   a.max_blocks = (int)block_tables.size(1);
   a.seq_lens = ptr<const int>(seq_lens);
@@ -291,7 +297,7 @@ void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tabl
   a.q = ptr<const __nv_bfloat16>(q);
   a.kcache = kcache.data_ptr();
   a.vcache = vcache.data_ptr();
-  a.cache_is_bf16 = kcache.scalar_type() == torch::kBFloat16;
+  a.cache_type = cache_type_of(kcache);
   a.block_tables = ptr<const int>(block_tables);
   a.max_blocks = (int)block_tables.size(1);
   a.q_start = ptr<const int>(q_start);

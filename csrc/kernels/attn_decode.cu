@@ -18,6 +18,10 @@
 
 namespace barq {
 
+// 8 consecutive K elements (one "chunk") of a row as floats: 16-byte loads for 2-byte types, 8-byte
+// loads for fp8.
+template <typename TC>
+BARQ_DEV void load_k8(const TC* row, int chunk, float* f);
 template <typename TC> BARQ_DEV void cvt8(const int4& raw, float* f);
 template <> BARQ_DEV void cvt8<__half>(const int4& raw, float* f) {
   const __half2* h = reinterpret_cast<const __half2*>(&raw);
@@ -38,12 +42,27 @@ template <> BARQ_DEV void cvt8<__nv_bfloat16>(const int4& raw, float* f) {
   }
 }
 
+template <> BARQ_DEV void load_k8<__half>(const __half* row, int chunk, float* f) {
+  cvt8<__half>(__ldg(reinterpret_cast<const int4*>(row) + chunk), f);
+}
+template <> BARQ_DEV void load_k8<__nv_bfloat16>(const __nv_bfloat16* row, int chunk, float* f) {
+  cvt8<__nv_bfloat16>(__ldg(reinterpret_cast<const int4*>(row) + chunk), f);
+}
+template <> BARQ_DEV void load_k8<__nv_fp8_e4m3>(const __nv_fp8_e4m3* row, int chunk, float* f) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(row) + chunk);
+  const __nv_fp8_e4m3* e = reinterpret_cast<const __nv_fp8_e4m3*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = static_cast<float>(e[i]);
+}
+
 constexpr int kBS = 16;  // tokens per KV page
 
 // This lane's DPL consecutive V elements of one token, kept packed in registers until used.
 template <typename TC, int DPL>
 struct VRow {
-  using R = typename std::conditional<DPL * sizeof(TC) == 8, uint2, uint32_t>::type;
+  static constexpr int BYTES = DPL * (int)sizeof(TC);
+  using R = typename std::conditional<BYTES == 8, uint2,
+                                      typename std::conditional<BYTES == 4, uint32_t, unsigned short>::type>::type;
   R r;
   BARQ_DEV void load(const TC* p) { r = __ldg(reinterpret_cast<const R*>(p)); }
   BARQ_DEV void cvt(float* f) const {
@@ -112,9 +131,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
 #pragma unroll
     for (int c = 0; c < CPH; ++c) {
       const int chunk = 2 * c + half;
-      int4 raw = __ldg(reinterpret_cast<const int4*>(krow) + chunk);
       float kf[8];
-      cvt8<TC>(raw, kf);
+      load_k8<TC>(krow, chunk, kf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float4* qv = reinterpret_cast<const float4*>(&q_s[g][chunk * 8]);
@@ -247,8 +265,14 @@ int decode_attention(const DecodeAttnArgs& a, cudaStream_t st) {
   if (a.splits < 1 || a.splits > 64) return -5;
   if (a.H % a.Hkv) return -2;
   if (a.B <= 0) return 0;
-  if (a.D == 128) return a.cache_is_bf16 ? launch_g<__nv_bfloat16, 128>(a, st) : launch_g<__half, 128>(a, st);
-  if (a.D == 64) return a.cache_is_bf16 ? launch_g<__nv_bfloat16, 64>(a, st) : launch_g<__half, 64>(a, st);
+  if (a.D == 128)
+    return a.cache_type == kCacheBF16  ? launch_g<__nv_bfloat16, 128>(a, st)
+           : a.cache_type == kCacheFP8 ? launch_g<__nv_fp8_e4m3, 128>(a, st)
+                                       : launch_g<__half, 128>(a, st);
+  if (a.D == 64)
+    return a.cache_type == kCacheBF16  ? launch_g<__nv_bfloat16, 64>(a, st)
+           : a.cache_type == kCacheFP8 ? launch_g<__nv_fp8_e4m3, 64>(a, st)
+                                       : launch_g<__half, 64>(a, st);
   return -4;
 }
 

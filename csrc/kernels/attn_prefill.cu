@@ -9,6 +9,8 @@
 // The reference's only attention is a per-row CPU loop (models/src/transformer.rs:301-374) and a
 // CPU FA-2 (advanced/src/flash_attention.rs:169-271); its CUDA flash attention returns
 // Unsupported (backend/src/cuda_flash_attn.rs:165-359).
+#include <type_traits>
+
 #include "common.cuh"
 #include "pdl.cuh"
 #include "launch.h"
@@ -56,7 +58,9 @@ BARQ_DEV void cp_async16(void* dst, const void* src, bool pred) {
 BARQ_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N> BARQ_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
 
-template <typename TC, int D>
+// TC: KV cache element type; TM: tensor-core operand type (TC itself for fp16/bf16; fp16 for an
+// fp8 cache, whose pages are converted while being staged in shared memory).
+template <typename TC, typename TM, int D>
 __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -65,9 +69,9 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
   constexpr int KS = D / 16;                   // k-steps of QK^T
   constexpr int ND = D / 8;                    // O n-blocks
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TC* sQ = reinterpret_cast<TC*>(smem_raw);
-  TC* sK = sQ + BQ * LD;           // [2][BK][LD]
-  TC* sV = sK + 2 * BK * LD;       // [2][BK][LD]
+  TM* sQ = reinterpret_cast<TM*>(smem_raw);
+  TM* sK = sQ + BQ * LD;           // [2][BK][LD]
+  TM* sV = sK + 2 * BK * LD;       // [2][BK][LD]
 
   const int s = blockIdx.z, h = blockIdx.y, qt = blockIdx.x;
   const int q_begin = a.q_start[s], n_new = a.q_start[s + 1] - q_begin;
@@ -84,16 +88,16 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
   for (int i = tid; i < BQ * D / 8; i += 128) {
     int r = i / (D / 8), c = (i % (D / 8)) * 8;
     int qi = q0 + r;
-    TC tmp[8];
+    TM tmp[8];
     if (qi < n_new) {
       const __nv_bfloat16* src = a.q + ((size_t)(q_begin + qi) * a.H + h) * D + c;
       int4 raw = *reinterpret_cast<const int4*>(src);
       const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) tmp[j] = from_f<TC>(__bfloat162float(hv[j]));
+      for (int j = 0; j < 8; ++j) tmp[j] = from_f<TM>(__bfloat162float(hv[j]));
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) tmp[j] = from_f<TC>(0.f);
+      for (int j = 0; j < 8; ++j) tmp[j] = from_f<TM>(0.f);
     }
     *reinterpret_cast<int4*>(sQ + r * LD + c) = *reinterpret_cast<int4*>(tmp);
   }
@@ -108,16 +112,36 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
   const TC* vc = reinterpret_cast<const TC*>(a.vcache);
 
   auto load_kv = [&](int tile, int buf) {
-    TC* dk = sK + buf * BK * LD;
-    TC* dv = sV + buf * BK * LD;
+    TM* dk = sK + buf * BK * LD;
+    TM* dv = sV + buf * BK * LD;
     for (int i = tid; i < BK * D / 8; i += 128) {
       int r = i / (D / 8), c = (i % (D / 8)) * 8;
       int pos = tile * BK + r;
       bool ok = pos < kv_end;
       int phys = ok ? bt[pos >> 4] : 0;
       size_t off = (((size_t)phys * a.Hkv + kvh) * 16 + (pos & 15)) * D + c;
-      cp_async16(dk + r * LD + c, kc + off, ok);
-      cp_async16(dv + r * LD + c, vc + off, ok);
+      if constexpr (std::is_same<TC, TM>::value) {
+        cp_async16(dk + r * LD + c, kc + off, ok);
+        cp_async16(dv + r * LD + c, vc + off, ok);
+      } else {  // fp8 cache: 8 elements (8 bytes) -> 8 operands (16 bytes)
+        TM tk[8], tv[8];
+        if (ok) {
+          const uint2 rk = __ldg(reinterpret_cast<const uint2*>(kc + off));
+          const uint2 rv = __ldg(reinterpret_cast<const uint2*>(vc + off));
+          const TC* ek = reinterpret_cast<const TC*>(&rk);
+          const TC* ev = reinterpret_cast<const TC*>(&rv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            tk[j] = from_f<TM>(to_f(ek[j]));
+            tv[j] = from_f<TM>(to_f(ev[j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) tk[j] = tv[j] = from_f<TM>(0.f);
+        }
+        *reinterpret_cast<int4*>(dk + r * LD + c) = *reinterpret_cast<int4*>(tk);
+        *reinterpret_cast<int4*>(dv + r * LD + c) = *reinterpret_cast<int4*>(tv);
+      }
     }
     cp_async_commit();
   };
@@ -150,8 +174,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const TC* k_s = sK + buf * BK * LD;
-    const TC* v_s = sV + buf * BK * LD;
+    const TM* k_s = sK + buf * BK * LD;
+    const TM* v_s = sV + buf * BK * LD;
     float sc[NB][4];
 #pragma unroll
     for (int j = 0; j < NB; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
@@ -163,8 +187,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
         int r = jp * 8 + (lane & 7) + (lane >> 4) * 8;
         int c = kk * 16 + ((lane >> 3) & 1) * 8;
         ldsm_x4(kf, smem_u32(k_s + r * LD + c));
-        MmaT<TC>::mma(sc[jp], qf[kk], kf);
-        MmaT<TC>::mma(sc[jp + 1], qf[kk], kf + 2);
+        MmaT<TM>::mma(sc[jp], qf[kk], kf);
+        MmaT<TM>::mma(sc[jp + 1], qf[kk], kf + 2);
       }
     }
     // mask + online softmax
@@ -215,18 +239,18 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
 #pragma unroll
     for (int kk = 0; kk < BK / 16; ++kk) {
       uint32_t pf[4];
-      pf[0] = MmaT<TC>::pack(sc[2 * kk][0], sc[2 * kk][1]);
-      pf[1] = MmaT<TC>::pack(sc[2 * kk][2], sc[2 * kk][3]);
-      pf[2] = MmaT<TC>::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
-      pf[3] = MmaT<TC>::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+      pf[0] = MmaT<TM>::pack(sc[2 * kk][0], sc[2 * kk][1]);
+      pf[1] = MmaT<TM>::pack(sc[2 * kk][2], sc[2 * kk][3]);
+      pf[2] = MmaT<TM>::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+      pf[3] = MmaT<TM>::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
 #pragma unroll
       for (int jd = 0; jd < ND; jd += 2) {
         uint32_t vf[4];
         int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         int c = jd * 8 + (lane >> 4) * 8;
         ldsm_x4_t(vf, smem_u32(v_s + r * LD + c));
-        MmaT<TC>::mma(o[jd], pf, vf);
-        MmaT<TC>::mma(o[jd + 1], pf, vf + 2);
+        MmaT<TM>::mma(o[jd], pf, vf);
+        MmaT<TM>::mma(o[jd + 1], pf, vf + 2);
       }
     }
     __syncthreads();
@@ -251,21 +275,27 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
   }
 }
 
-template <typename TC, int D>
+template <typename TC, typename TM, int D>
 static int launch_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   constexpr int LD = D + 8;
-  size_t smem = (size_t)(64 * LD + 4 * 64 * LD) * sizeof(TC);
-  cudaFuncSetAttribute(prefill_attn_kernel<TC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  size_t smem = (size_t)(64 * LD + 4 * 64 * LD) * sizeof(TM);
+  cudaFuncSetAttribute(prefill_attn_kernel<TC, TM, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((a.max_q + 63) / 64, a.H, a.S);
-  launch_pdl(prefill_attn_kernel<TC, D>, grid, dim3(128), smem, st, a);
+  launch_pdl(prefill_attn_kernel<TC, TM, D>, grid, dim3(128), smem, st, a);
   return 0;
 }
 
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st) {
   if (a.block_size != 16) return -1;
   if (a.S <= 0 || a.max_q <= 0) return 0;
-  if (a.D == 128) return a.cache_is_bf16 ? launch_prefill<__nv_bfloat16, 128>(a, st) : launch_prefill<__half, 128>(a, st);
-  if (a.D == 64) return a.cache_is_bf16 ? launch_prefill<__nv_bfloat16, 64>(a, st) : launch_prefill<__half, 64>(a, st);
+  if (a.D == 128)
+    return a.cache_type == kCacheBF16  ? launch_prefill<__nv_bfloat16, __nv_bfloat16, 128>(a, st)
+           : a.cache_type == kCacheFP8 ? launch_prefill<__nv_fp8_e4m3, __half, 128>(a, st)
+                                       : launch_prefill<__half, __half, 128>(a, st);
+  if (a.D == 64)
+    return a.cache_type == kCacheBF16  ? launch_prefill<__nv_bfloat16, __nv_bfloat16, 64>(a, st)
+           : a.cache_type == kCacheFP8 ? launch_prefill<__nv_fp8_e4m3, __half, 64>(a, st)
+                                       : launch_prefill<__half, __half, 64>(a, st);
   return -4;
 }
 

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 #include "qweight.cuh"
 
@@ -38,11 +39,14 @@ BARQ_DEV float silu(float x) { return x / (1.0f + __expf(-x)); }
 BARQ_DEV float to_f(float v) { return v; }
 BARQ_DEV float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 BARQ_DEV float to_f(__half v) { return __half2float(v); }
+BARQ_DEV float to_f(__nv_fp8_e4m3 v) { return static_cast<float>(v); }
 
 template <typename T> BARQ_DEV T from_f(float v);
 template <> BARQ_DEV float from_f<float>(float v) { return v; }
 template <> BARQ_DEV __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
 template <> BARQ_DEV __half from_f<__half>(float v) { return __float2half(v); }
+// fp8 e4m3 KV cache: round to nearest, saturating at +-448
+template <> BARQ_DEV __nv_fp8_e4m3 from_f<__nv_fp8_e4m3>(float v) { return __nv_fp8_e4m3(v); }
 
 BARQ_DEV int4 ldg16(const void* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
 // Streaming 16-byte load (no L1 allocation) for weights that are read exactly once per step.

@@ -78,7 +78,7 @@ extern "C" int barq_decode_attention_static(const void* q, const void* kcache, c
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.kcache = kcache;
   a.vcache = vcache;
-  a.cache_is_bf16 = cache_is_bf16;
+  a.cache_type = cache_is_bf16 ? barq::kCacheBF16 : barq::kCacheF16;
   a.block_tables = block_tables;
   a.max_blocks = max_blocks;
   a.seq_lens = seq_lens;

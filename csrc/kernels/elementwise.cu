@@ -215,10 +215,12 @@ int rope_kv_write(const RopeKVArgs& a, cudaStream_t st) {
   const int nh = a.H + 2 * a.Hkv;
   dim3 g(a.T, (nh + 7) / 8 > 4 ? 4 : (nh + 7) / 8);
   if (a.qkv_is_bf16) {
-    if (a.cache_is_bf16) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    if (a.cache_type == kCacheBF16) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else if (a.cache_type == kCacheFP8) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
     else launch_pdl(rope_kv_kernel<__nv_bfloat16, __half>, g, dim3(256), 0, st, a);
   } else {
-    if (a.cache_is_bf16) launch_pdl(rope_kv_kernel<float, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    if (a.cache_type == kCacheBF16) launch_pdl(rope_kv_kernel<float, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else if (a.cache_type == kCacheFP8) launch_pdl(rope_kv_kernel<float, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
     else launch_pdl(rope_kv_kernel<float, __half>, g, dim3(256), 0, st, a);
   }
   return 0;

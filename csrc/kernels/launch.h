@@ -8,6 +8,9 @@
 
 namespace barq {
 
+// KV cache element types
+constexpr int kCacheF16 = 0, kCacheBF16 = 1, kCacheFP8 = 2;
+
 enum EpiMode : int { EPI_STORE_F32 = 0, EPI_ADD_F32 = 1, EPI_STORE_BF16 = 2, EPI_SWIGLU_Q8 = 3, EPI_MOE_COMBINE = 4 };
 
 struct GemvEpi {
@@ -146,7 +149,7 @@ struct RopeKVArgs {
   __nv_bfloat16* q_out;  // [T, H, D]
   void* kcache;          // [num_blocks, Hkv, block_size, D] (fp16 or bf16)
   void* vcache;
-  int cache_is_bf16;
+  int cache_type;           // KV cache element type: kCacheF16, kCacheBF16 or kCacheFP8 (e4m3)
   int block_size;
 };
 int rope_kv_write(const RopeKVArgs& a, cudaStream_t st);
@@ -155,7 +158,7 @@ struct DecodeAttnArgs {
   const __nv_bfloat16* q;   // [B, H, D]
   const void* kcache;       // [num_blocks, Hkv, bs, D]
   const void* vcache;
-  int cache_is_bf16;
+  int cache_type;           // KV cache element type: kCacheF16, kCacheBF16 or kCacheFP8 (e4m3)
   const int* block_tables;  // [B, max_blocks]
   int max_blocks;
   const int* seq_lens;      // [B] tokens in cache including the current one
@@ -176,7 +179,7 @@ struct PrefillAttnArgs {
   const __nv_bfloat16* q;   // [T, H, D]  (rows of all sequences, concatenated)
   const void* kcache;
   const void* vcache;
-  int cache_is_bf16;
+  int cache_type;           // KV cache element type: kCacheF16, kCacheBF16 or kCacheFP8 (e4m3)
   const int* block_tables;  // [S, max_blocks]
   int max_blocks;
   const int* q_start;       // [S+1] prefix sums of new tokens per sequence

@@ -149,8 +149,8 @@ def test_rmsnorm_fused_add():
     assert torch.allclose(_q8_deq(oq), ref.cpu(), atol=ref.abs().max().item() / 5000)
 
 
-@pytest.mark.parametrize("neox", [False, True])
-def test_rope_kv_write(neox):
+@pytest.mark.parametrize("neox,cdt", [(False, torch.float16), (True, torch.float16), (True, torch.float8_e4m3fn)])
+def test_rope_kv_write(neox, cdt):
     from barq_inference_b200.models.config import preset
     from barq_inference_b200.models.rope import rope_cos_sin
 
@@ -160,7 +160,7 @@ def test_rope_kv_write(neox):
     qkv = torch.randn(T, (H + 2 * Hkv) * D, device=DEV)
     pos = torch.tensor([3, 17, 40, 41, 100, 200, 255], dtype=torch.int32, device=DEV)
     nb = 32
-    kc = torch.zeros(nb, Hkv, 16, D, dtype=torch.float16, device=DEV)
+    kc = torch.zeros(nb, Hkv, 16, D, dtype=cdt, device=DEV)
     vc = torch.zeros_like(kc)
     slots = torch.tensor([5, 16 * 3 + 2, 16 * 7 + 15, 1, 16 * 9, 16 * 31 + 4, 16 * 2 + 8], dtype=torch.int64,
                          device=DEV)
@@ -170,10 +170,12 @@ def test_rope_kv_write(neox):
     q_ref = apply_rope_ref(x[:, :H].cpu(), c, s, neox)
     k_ref = apply_rope_ref(x[:, H:H + Hkv].cpu(), c, s, neox)
     assert torch.allclose(q.float().cpu(), q_ref, atol=2e-2, rtol=1e-2)
+    # fp8 e4m3: 3 mantissa bits, so a stored value is within 1/16 relative of the exact one
+    tol = dict(atol=3e-3, rtol=1e-3) if cdt == torch.float16 else dict(atol=2e-3, rtol=0.07)
     for t in range(T):
         blk, off = int(slots[t]) // 16, int(slots[t]) % 16
-        assert torch.allclose(kc[blk, :, off].float().cpu(), k_ref[t], atol=3e-3, rtol=1e-3)
-        assert torch.allclose(vc[blk, :, off].float().cpu(), x[t, H + Hkv:].cpu(), atol=3e-3, rtol=1e-3)
+        assert torch.allclose(kc[blk, :, off].float().cpu(), k_ref[t], **tol)
+        assert torch.allclose(vc[blk, :, off].float().cpu(), x[t, H + Hkv:].cpu(), **tol)
 
 
 def _paged(Ls, Hkv, D, nb_total=256, dtype=torch.float16, seed=0):
@@ -196,11 +198,13 @@ def _gather(cache, bt_row, L):
     return torch.cat([b.transpose(0, 1) for b in blocks], 0)[:L].float().cpu()  # [L, Hkv, D]
 
 
-@pytest.mark.parametrize("D,H,Hkv", [(128, 32, 8), (64, 4, 2), (128, 8, 8)])
+@pytest.mark.parametrize("D,H,Hkv,cdt", [(128, 32, 8, torch.float16), (64, 4, 2, torch.float16),
+                                          (128, 8, 8, torch.float16), (128, 32, 8, torch.float8_e4m3fn),
+                                          (64, 4, 2, torch.float8_e4m3fn), (128, 32, 8, torch.bfloat16)])
 @pytest.mark.parametrize("window", [0, 40])
-def test_decode_attention(D, H, Hkv, window):
+def test_decode_attention(D, H, Hkv, cdt, window):
     Ls = [1, 17, 300, 1024]
-    kc, vc, bt = _paged(Ls, Hkv, D)
+    kc, vc, bt = _paged(Ls, Hkv, D, dtype=cdt)
     B = len(Ls)
     q = torch.randn(B, H, D, device=DEV).bfloat16()
     lens = torch.tensor(Ls, dtype=torch.int32, device=DEV)
@@ -218,13 +222,14 @@ def test_decode_attention(D, H, Hkv, window):
         assert torch.allclose(_q8_deq(oq)[b], o, atol=o.abs().max() / 60)
 
 
-@pytest.mark.parametrize("D,H,Hkv", [(128, 8, 2), (64, 4, 2)])
+@pytest.mark.parametrize("D,H,Hkv,cdt", [(128, 8, 2, torch.bfloat16), (64, 4, 2, torch.bfloat16),
+                                          (128, 8, 2, torch.float8_e4m3fn), (64, 4, 2, torch.float16)])
 @pytest.mark.parametrize("window", [0, 100])
-def test_prefill_attention(D, H, Hkv, window):
+def test_prefill_attention(D, H, Hkv, cdt, window):
     # (n_new, ctx): first chunk, a later chunk of a long prompt, a one-token row
     spec = [(70, 70), (130, 300), (1, 45), (256, 256)]
     Ls = [c for _, c in spec]
-    kc, vc, bt = _paged(Ls, Hkv, D, seed=3, dtype=torch.bfloat16)
+    kc, vc, bt = _paged(Ls, Hkv, D, seed=3, dtype=cdt)
     T = sum(n for n, _ in spec)
     q = torch.randn(T, H, D, device=DEV).bfloat16()
     qs = [0]

@@ -133,3 +133,28 @@ def test_dense_prefill_path_matches_fused(monkeypatch):
         runner.allocate_kv(64)
         outs.append(_run(runner, prompt, 0, list(range(1, 10)), decode=False))
     assert (outs[0] - outs[1]).abs().max().item() < 2e-2
+
+
+def test_fp8_kv_cache_logits_close_to_fp16():
+    """fp8 (e4m3) KV cache: prefill + teacher-forced decode logits stay close to the fp16-cache run,
+    and the engine's graph and eager paths agree token for token."""
+    cfg, tensors, prompt = _tiny()
+    table = list(range(1, 10))
+    logits = {}
+    for dt in (torch.float16, torch.float8_e4m3fn):
+        runner = LlamaRunner(cfg, tensors, DEV, kv_dtype=dt)
+        runner.allocate_kv(64)
+        out = [_run(runner, prompt, 0, table, decode=False)]
+        for i, t in enumerate(prompt[:16]):
+            out.append(_run(runner, [t], len(prompt) + i, table, decode=True))
+        logits[dt] = torch.stack(out)
+    a, b = logits[torch.float16], logits[torch.float8_e4m3fn]
+    rel = ((a - b).norm(dim=-1) / a.norm(dim=-1)).max().item()
+    assert rel < 0.1, rel
+    outs = []
+    for graphs in (False, True):
+        eng = Engine(cfg, tensors, EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=128,
+                                                cuda_graphs=graphs, kv_dtype="fp8"))
+        outs.append([r.tokens for r in eng.generate([prompt, prompt[:20]],
+                                                    SamplingParams.greedy_params(max_tokens=12))])
+    assert outs[0] == outs[1]
