@@ -276,8 +276,27 @@ def cmd_convert(args) -> int:
     from .gguf import QUANT_NAME_TO_TYPE
     from .models.convert import convert_gguf
 
-    t = QUANT_NAME_TO_TYPE[args.quantize.lower()]
-    convert_gguf(args.input, args.output, t, keep_output_type=args.output_type, device=args.device)
+    from .gguf.ikq import IKQ_NAMES, gguf_to_ikq, ikq_to_gguf
+
+    q = args.quantize.lower()
+    src = args.input
+    if src.endswith(".ikq"):  # IKQ1 archive in: unpack to GGUF first
+        if q == "keep":
+            ikq_to_gguf(src, args.output)
+            print(f"wrote {args.output}")
+            return 0
+        import tempfile
+
+        tmp = tempfile.NamedTemporaryFile(suffix=".gguf", delete=False).name
+        ikq_to_gguf(src, tmp)
+        src = tmp
+    if q == "q4_k_r4" or args.output.endswith(".ikq"):  # the reference's archive (CPU repack / ik types)
+        if q not in IKQ_NAMES:
+            raise SystemExit(f"IKQ archives hold {sorted(IKQ_NAMES)}, not {q}")
+        gguf_to_ikq(src, args.output, q, device=args.device)
+    else:
+        convert_gguf(src, args.output, QUANT_NAME_TO_TYPE[q], keep_output_type=args.output_type,
+                     device=args.device)
     print(f"wrote {args.output}")
     return 0
 
@@ -430,7 +449,8 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("convert", help="requantize a GGUF file")
     p.add_argument("--input", required=True)
     p.add_argument("--output", required=True)
-    p.add_argument("--quantize", default="q4_k")
+    p.add_argument("--quantize", default="q4_k",
+                   help="ggml type (q4_k, q6_k, ..., iq4_ks, iq3_ks, iq2_ks), q4_k_r4 (IKQ archive) or keep")
     p.add_argument("--output-type", default=None, help="type for output.weight (default: keep)")
     p.add_argument("--device", default=None)
     p.set_defaults(fn=cmd_convert)

@@ -61,12 +61,18 @@ class GGMLType(enum.IntEnum):
     F64 = 28
     IQ1_M = 29
     BF16 = 30
+    # ik_llama.cpp extension types (its ``ggml_type`` numbering).  Their rows start with a row
+    # scale (``row_meta`` bytes) before the blocks.
+    IQ4_KS = 144
+    IQ2_KS = 145
+    IQ3_KS = 156
 
 
 @dataclass(frozen=True)
 class TypeTraits:
     block_size: int  # elements per block
     type_size: int  # bytes per block
+    row_meta: int = 0  # bytes at the start of every row (ik_llama row scale), 0 for ggml types
 
 
 QK_K = 256
@@ -94,7 +100,17 @@ TYPE_TRAITS: dict[GGMLType, TypeTraits] = {
     GGMLType.Q8_K: TypeTraits(QK_K, 4 + 256 + 32),
     GGMLType.IQ4_NL: TypeTraits(32, 2 + 16),
     GGMLType.IQ4_XS: TypeTraits(QK_K, 2 + 2 + 4 + 128),
+    GGMLType.IQ4_KS: TypeTraits(QK_K, 8 + 128, 4),  # f32 row scale; scales[8], qs[128]
+    GGMLType.IQ2_KS: TypeTraits(QK_K, 2 + 4 + 64, 2),  # f16 row scale; extra, scales[4], qs[64]
+    GGMLType.IQ3_KS: TypeTraits(QK_K, 2 + 4 + 64 + 32, 2),  # f16 row scale; extra, scales[4], qs[64], qh[32]
 }
+
+# ik_llama non-linear codebooks (published format tables): a base half and a shifted half,
+# selected per 32-element block.
+KVALUES_IQ4K = (-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113,
+                -123, -100, -79, -61, -45, -31, -18, -6, 5, 17, 29, 42, 57, 73, 93, 117)
+KVALUES_IQ2NL = (-31, -13, 1, 17, -26, -8, 6, 22)
+KVALUES_IQ3NL = (-63, -40, -23, -10, 1, 13, 28, 47, -59, -36, -19, -6, 5, 17, 32, 51)
 
 # IQ4_NL / IQ4_XS non-linear 4-bit codebook (published ggml GGUF format table).
 KVALUES_IQ4NL = (-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113)
@@ -118,13 +134,29 @@ QUANT_NAME_TO_TYPE: dict[str, GGMLType] = {
     "q8_k": GGMLType.Q8_K,
     "iq4_nl": GGMLType.IQ4_NL,
     "iq4_xs": GGMLType.IQ4_XS,
+    "iq4_ks": GGMLType.IQ4_KS,
+    "iq3_ks": GGMLType.IQ3_KS,
+    "iq2_ks": GGMLType.IQ2_KS,
 }
 
 
-def type_nbytes(t: GGMLType, n_elements: int) -> int:
+def row_nbytes(t: GGMLType, ne0: int) -> int:
+    """Bytes of one row of ``ne0`` elements (row scale included for ik_llama types)."""
+    tr = TYPE_TRAITS[GGMLType(t)]
+    if ne0 % tr.block_size:
+        raise ValueError(f"{GGMLType(t).name}: row of {ne0} elements not a multiple of block {tr.block_size}")
+    return tr.row_meta + ne0 // tr.block_size * tr.type_size
+
+
+def type_nbytes(t: GGMLType, n_elements: int, ne0: int | None = None) -> int:
+    """Bytes of ``n_elements`` values; row-scaled types also need the row length ``ne0``."""
     tr = TYPE_TRAITS[GGMLType(t)]
     if n_elements % tr.block_size:
         raise ValueError(f"{GGMLType(t).name}: {n_elements} elements not a multiple of block {tr.block_size}")
+    if tr.row_meta:
+        if ne0 is None:
+            raise ValueError(f"{GGMLType(t).name}: row length needed (per-row scale)")
+        return n_elements // ne0 * row_nbytes(t, ne0)
     return n_elements // tr.block_size * tr.type_size
 
 

@@ -283,10 +283,17 @@ def dequantize(raw: np.ndarray, t: GGMLType, shape: tuple[int, ...] | None = Non
         out = r.view(np.uint8).view(dt).astype(np.float32)
     elif t in _DQ:
         out = _DQ[t](r).reshape(-1)
+    elif TYPE_TRAITS.get(t) is not None and TYPE_TRAITS[t].row_meta:
+        from .ik_quants import DQ_IK
+
+        if shape is None:
+            raise ValueError(f"dequantize: {t.name} has a per-row scale, pass the shape")
+        out = DQ_IK[t](r, int(shape[-1])).reshape(-1)
     else:
         raise NotImplementedError(f"dequantize: {t.name}")
     return out.reshape(shape) if shape is not None else out
 
 
 def supported_dequant_types() -> list[GGMLType]:
-    return [GGMLType.F32, GGMLType.F16, GGMLType.BF16, *list(_DQ)]
+    return [GGMLType.F32, GGMLType.F16, GGMLType.BF16, *list(_DQ), GGMLType.IQ4_KS, GGMLType.IQ3_KS,
+            GGMLType.IQ2_KS]

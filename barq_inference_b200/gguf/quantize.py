@@ -227,6 +227,15 @@ QUANTIZERS = {
 }
 
 
+def _ik_quantizers():
+    from .ik_quants import Q_IK
+
+    QUANTIZERS.update(Q_IK)
+
+
+_ik_quantizers()
+
+
 def quantize(x: torch.Tensor, t: GGMLType) -> torch.Tensor:
     t = GGMLType(t)
     if t not in QUANTIZERS:

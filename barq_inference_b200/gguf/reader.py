@@ -23,6 +23,7 @@ from .constants import (
     TYPE_TRAITS,
     GGMLType,
     GGUFValueType,
+    row_nbytes,
 )
 
 _SCALAR_FMT = {
@@ -75,8 +76,7 @@ class TensorInfo:
 
     @property
     def nbytes(self) -> int:
-        tr = TYPE_TRAITS[self.ggml_type]
-        return self.n_elements // tr.block_size * tr.type_size
+        return self.n_elements // self.shape[0] * row_nbytes(self.ggml_type, self.shape[0])
 
     @property
     def torch_shape(self) -> tuple[int, ...]:
@@ -85,9 +85,7 @@ class TensorInfo:
 
     def rows(self) -> np.ndarray:
         """Packed bytes as ``[n_rows, row_bytes]`` where a row is ``ne0`` elements."""
-        tr = TYPE_TRAITS[self.ggml_type]
-        row_bytes = self.shape[0] // tr.block_size * tr.type_size
-        return self.data.reshape(-1, row_bytes)
+        return self.data.reshape(-1, row_nbytes(self.ggml_type, self.shape[0]))
 
 
 @dataclass

@@ -12,7 +12,7 @@ from typing import Any, Iterable
 
 import numpy as np
 
-from .constants import GGUF_DEFAULT_ALIGNMENT, GGUF_MAGIC, GGUF_VERSION, TYPE_TRAITS, GGMLType, GGUFValueType
+from .constants import GGUF_DEFAULT_ALIGNMENT, GGUF_MAGIC, GGUF_VERSION, TYPE_TRAITS, GGMLType, GGUFValueType, row_nbytes
 
 
 def _infer_vt(v: Any) -> GGUFValueType:
@@ -120,7 +120,7 @@ class GGUFWriter:
         if ne[0] % tr.block_size:
             raise ValueError(f"{name}: row length {ne[0]} not a multiple of {tr.block_size}")
         raw = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
-        want = n // tr.block_size * tr.type_size
+        want = n // ne[0] * row_nbytes(ggml_type, ne[0]) if ne else tr.type_size
         if raw.size != want:
             raise ValueError(f"{name}: {raw.size} bytes given, {want} expected for {ggml_type.name}{shape}")
         self.tensors.append((name, ne, GGMLType(ggml_type), raw))

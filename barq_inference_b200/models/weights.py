@@ -14,6 +14,7 @@ import numpy as np
 import torch
 
 from ..gguf import GGUFValueType, GGMLType, GGUFWriter, quantize
+from ..gguf.ik_quants import IK_TYPES
 from .config import ModelConfig
 
 
@@ -64,7 +65,8 @@ def fallback_type(t: GGMLType, row_len: int) -> GGMLType:
     if row_len % TYPE_TRAITS[t].block_size == 0:
         return t
     if row_len % 32 == 0:
-        return {GGMLType.Q6_K: GGMLType.Q8_0, GGMLType.Q5_K: GGMLType.Q5_0}.get(t, GGMLType.Q4_0 if t != GGMLType.Q8_0 else t)
+        return {GGMLType.Q6_K: GGMLType.Q8_0, GGMLType.Q5_K: GGMLType.Q5_0, GGMLType.IQ4_KS: GGMLType.IQ4_NL}.get(
+            t, GGMLType.Q4_0 if t != GGMLType.Q8_0 else t)
     return GGMLType.F16
 
 
@@ -254,6 +256,17 @@ def write_gguf_split(path: str, cfg: ModelConfig, tensors: dict[str, PackedTenso
     return paths
 
 
+def import_ik(rows, t, shape, device="cpu"):
+    """Packed ik_llama rows -> (import type, its packed rows), via the fp32 values."""
+    from ..gguf import dequantize, quantize
+    from ..gguf.ik_quants import import_type
+
+    tt = import_type(t)
+    x = torch.from_numpy(dequantize(np.asarray(rows), t, (int(np.prod(shape[:-1])), shape[-1])))
+    q = quantize(x.to(device), tt)
+    return tt, q.reshape(x.shape[0], -1)
+
+
 def tensors_from_gguf(g, device: str | torch.device = "cpu", names: set[str] | None = None) -> dict[str, PackedTensor]:
     """Wrap every tensor of a parsed GGUF as a PackedTensor (upload to ``device``)."""
     out = {}
@@ -262,6 +275,10 @@ def tensors_from_gguf(g, device: str | torch.device = "cpu", names: set[str] | N
             continue
         shape = ti.torch_shape
         rows = ti.rows()
+        if ti.ggml_type in IK_TYPES:  # ik_llama row-scaled types: requantize to a streamed type
+            tt, data = import_ik(rows, ti.ggml_type, shape, device)
+            out[name] = PackedTensor(name, tt, shape, data)
+            continue
         data = torch.from_numpy(np.array(rows, copy=True)).to(device)
         out[name] = PackedTensor(name, ti.ggml_type, shape, data)
     return out

@@ -16,6 +16,7 @@ import numpy as np
 import torch
 
 from ..gguf import TYPE_TRAITS, GGMLType, dequantize
+from ..gguf.ik_quants import IK_TYPES
 
 NATIVE = {GGMLType.Q4_0, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q5_K, GGMLType.Q6_K, GGMLType.IQ4_NL}
 W_BF16 = 0
@@ -77,6 +78,11 @@ class QWeight:
         t = GGMLType(t)
         dev = torch.device(device) if device is not None else raw.device
         raw = raw.to(dev)
+        if t in IK_TYPES:  # ik_llama row-scaled type: requantize to a type the kernels stream
+            from ..models.weights import import_ik
+
+            tt, q = import_ik(raw.cpu().numpy(), t, (N, K), dev)
+            return QWeight.from_packed(q, tt, N, K, dev)
         if t not in NATIVE or K % TILE_FMT[int(t)][0]:
             if t == GGMLType.BF16:
                 w = raw.contiguous().view(torch.bfloat16).reshape(N, K)
