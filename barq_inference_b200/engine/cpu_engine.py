@@ -35,7 +35,7 @@ class CPUEngine:
         self.timings = {"prefill_s": 0.0, "decode_s": 0.0, "prefill_tokens": 0, "decode_tokens": 0}
 
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, request_id: str = "",
-                    on_token=None) -> Sequence:
+                    on_token=None, embeds: tuple[int, torch.Tensor] | None = None) -> Sequence:
         params = params or SamplingParams()
         if not prompt:
             raise ValueError("empty prompt")
@@ -44,6 +44,11 @@ class CPUEngine:
         if len(prompt) >= self.max_model_len:
             raise ValueError("prompt exceeds max_model_len")
         seq = Sequence(list(prompt), params, request_id=request_id, on_token=on_token)
+        if embeds is not None:
+            st, e = embeds
+            if e.dim() != 2 or e.shape[1] != self.cfg.hidden or st < 0 or st + e.shape[0] > len(prompt):
+                raise ValueError("embeds: need [n, hidden] rows inside the prompt")
+            seq.embeds = (int(st), e.float().cpu())
         if params.grammar or params.json_mode or params.json_schema:
             from ..sampling.grammar_engine import make_grammar_state
 
@@ -78,7 +83,7 @@ class CPUEngine:
             t0 = time.perf_counter()
             cache = self.caches[s.seq_id]
             if getattr(s, "pending_prefill", False):
-                logits = self.model.forward(s.tokens, cache)[-1]
+                logits = self.model.forward(s.tokens, cache, embeds=s.embeds)[-1]
                 s.pending_prefill = False
                 key = "prefill"
                 n = s.n_tokens
@@ -127,5 +132,8 @@ class CPUEngine:
         seqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
         while self.has_work():
             self.step()
-        return [GenerationResult(s.prompt, s.output, s.finish_reason or "", s.ttft,
-                                 (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs) for s in seqs]
+        return [self._result(s) for s in seqs]
+
+    def _result(self, s: Sequence) -> GenerationResult:
+        return GenerationResult(s.prompt, s.output, s.finish_reason or "", s.ttft,
+                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs)

@@ -131,9 +131,16 @@ class Engine:
 
     # ------------------------------------------------------------------ request API
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, request_id: str = "",
-                    on_token=None) -> Sequence:
+                    on_token=None, embeds: tuple[int, torch.Tensor] | None = None) -> Sequence:
+        """``embeds``: (first position, [n, hidden] tensor) input embeddings that replace the token
+        embeddings of prompt positions first..first+n-1 (image patches of a multimodal prompt)."""
         params = params or SamplingParams()
         seq = Sequence(list(prompt), params, request_id=request_id, on_token=on_token)
+        if embeds is not None:
+            st, e = embeds
+            if e.dim() != 2 or e.shape[1] != self.cfg.hidden or st < 0 or st + e.shape[0] > len(prompt):
+                raise ValueError("embeds: need [n, hidden] rows inside the prompt")
+            seq.embeds = (int(st), e.to(self.device, torch.float32))
         inj = getattr(self.runner, "injector", None)
         if inj is not None and inj.active("corrupt", self.step_count):  # fault injection: a bad request
             seq.prompt.append(self.cfg.vocab)
@@ -264,9 +271,17 @@ class Engine:
 
     def _run_prefill(self, plan: ScheduledStep) -> list[int | None]:
         ids, pos, slots, last = [], [], [], []
+        e_rows, e_vals = [], []
         q_start = [0]
         for s, n in zip(plan.seqs, plan.n_new):
             toks = s.tokens
+            if s.embeds is not None:  # image rows of this chunk
+                st, e = s.embeds
+                lo, hi = max(st, s.n_cached), min(st + e.shape[0], s.n_cached + n)
+                if lo < hi:
+                    base = len(ids) - s.n_cached
+                    e_rows.extend(range(base + lo, base + hi))
+                    e_vals.append(e[lo - st: hi - st])
             for p in range(s.n_cached, s.n_cached + n):
                 ids.append(toks[p])
                 pos.append(p)
@@ -283,6 +298,9 @@ class Engine:
                         self._to_dev(np.array(slots, np.int64)), self._to_dev(bt), self._to_dev(seq_lens),
                         self._to_dev(np.array(last, np.int64)), False,
                         q_start=self._to_dev(np.array(q_start, np.int32)), max_q=max(plan.n_new))
+        if e_rows:
+            inp.embed_rows = self._to_dev(np.array(e_rows, np.int64))
+            inp.embed_vals = torch.cat(e_vals)
         logits = self.runner.forward(inp)
         complete = [s.n_cached + n >= s.n_tokens for s, n in zip(plan.seqs, plan.n_new)]
         out = self._sample(logits, plan.seqs)

@@ -71,7 +71,7 @@ class Scheduler:
     def finish(self, seq: Sequence, reason: str) -> None:
         seq.status = SeqStatus.FINISHED
         seq.finish_reason = reason
-        if self.prefix_cache is not None:
+        if self.prefix_cache is not None and seq.embeds is None:
             self.prefix_cache.insert(seq.tokens[: seq.n_cached], seq.block_table)
         self._free(seq)
         if seq in self.running:
@@ -108,7 +108,7 @@ class Scheduler:
         # 2) admit waiting sequences
         while self.waiting and budget > 0 and len(self.running) < cfg.max_num_seqs:
             s = self.waiting[0]
-            if self.prefix_cache is not None and not s.block_table:
+            if self.prefix_cache is not None and not s.block_table and s.embeds is None:
                 hit_blocks, hit_tokens = self.prefix_cache.match(s.tokens[:-1])
                 if hit_blocks:
                     self.blocks.retain(hit_blocks)

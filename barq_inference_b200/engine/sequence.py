@@ -42,6 +42,9 @@ class Sequence:
     on_token: Callable[["Sequence", int], None] | None = None
     grammar_state: Any = None
     host_sampler: Any = None
+    # (first position, f32 [n, hidden] device tensor): prompt positions whose input embedding is
+    # given instead of the token's (multimodal prompts); such prompts bypass the prefix cache
+    embeds: Any = None
 
     @property
     def tokens(self) -> list[int]:

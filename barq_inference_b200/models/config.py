@@ -22,10 +22,12 @@ ARCH_FAMILY = {
     "qwen3moe": "llama",
     "deepseek": "llama",
     "deepseek2": "deepseek2",
+    "llava": "llama",  # the language half of a LLaVA checkpoint
+    "qwen2vl": "llama",  # the language half of a Qwen2-VL checkpoint (qwen2 layers)
 }
 
 # RoPE pairing: ggml "normal" (adjacent pairs) vs NeoX (split halves).
-NEOX_ARCHES = {"qwen", "qwen2", "qwen2moe", "qwen3", "qwen3moe"}
+NEOX_ARCHES = {"qwen", "qwen2", "qwen2moe", "qwen3", "qwen3moe", "qwen2vl"}
 
 
 @dataclass

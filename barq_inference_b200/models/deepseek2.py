@@ -24,7 +24,7 @@ from ..ops import EPI_ADD_F32, EPI_STORE_F32, EPI_SWIGLU_Q8
 from .config import ModelConfig
 from .moe import MoEBlock
 from .rope import attn_scale, rope_cos_sin
-from .runner import GEMV_MAX_T, Layer, LlamaRunner, StepInput, _f32, _qw
+from .runner import GEMV_MAX_T, Layer, LlamaRunner, StepInput, _f32, _qw, apply_embed_overrides
 from .weights import PackedTensor
 
 LAT, ROPE = 512, 64
@@ -140,7 +140,7 @@ class DeepseekV2Runner(LlamaRunner):
         cfg = self.cfg
         T = inp.ids.numel()
         ops.set_pdl(T <= GEMV_MAX_T)
-        x = ops.embed(self.embed_w, inp.ids)
+        x = apply_embed_overrides(ops.embed(self.embed_w, inp.ids), inp)
         for li, L in enumerate(self.layers):
             self._mla(L, li, x, inp, T)
             hb, hq = self._norm(x, L.ffn_norm, T)

@@ -98,8 +98,10 @@ class ReferenceModel:
             out += (F.silu(g) * u) @ w[p + "ffn_down_shexp.weight"].T
         return out
 
-    def forward(self, ids: list[int] | torch.Tensor, cache: dict | None = None) -> torch.Tensor:
-        """Logits for every position of ``ids``.  ``cache`` (dict) carries K/V across calls."""
+    def forward(self, ids: list[int] | torch.Tensor, cache: dict | None = None,
+                embeds: tuple[int, torch.Tensor] | None = None) -> torch.Tensor:
+        """Logits for every position of ``ids``.  ``cache`` (dict) carries K/V across calls.
+        ``embeds`` = (first row, [n, hidden]) replaces those rows' token embeddings."""
         cfg, w = self.cfg, self.w
         ids = torch.as_tensor(ids, dtype=torch.long)
         if cache is None:
@@ -107,6 +109,9 @@ class ReferenceModel:
         T0 = cache.get("pos", 0)
         T = ids.numel()
         x = w["token_embd.weight"][ids]
+        if embeds is not None:
+            x = x.clone()
+            x[embeds[0]: embeds[0] + embeds[1].shape[0]] = embeds[1].to(x.dtype).cpu()
         cos, sin = self.cos[T0 : T0 + T], self.sin[T0 : T0 + T]
         for i in range(cfg.n_layers):
             p = f"blk.{i}."

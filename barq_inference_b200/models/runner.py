@@ -46,6 +46,16 @@ class StepInput:
     decode: bool               # every sequence has exactly one new token (T == S)
     q_start: torch.Tensor | None = None  # int32 [S+1] (prefill)
     max_q: int = 1
+    # input-embedding overrides (multimodal prompts): rows of the step whose embedding is given
+    embed_rows: torch.Tensor | None = None  # int64 [n]
+    embed_vals: torch.Tensor | None = None  # f32 [n, hidden]
+
+
+def apply_embed_overrides(x: torch.Tensor, inp: StepInput) -> torch.Tensor:
+    """Replace the token embeddings of ``inp.embed_rows`` by ``inp.embed_vals`` (image patches)."""
+    if inp.embed_rows is not None and inp.embed_rows.numel():
+        x.index_copy_(0, inp.embed_rows, inp.embed_vals.to(x.dtype))
+    return x
 
 
 def _qw(pt: PackedTensor, device) -> QWeight:
@@ -188,7 +198,7 @@ class LlamaRunner:
     def _stage_input(self, inp: StepInput) -> torch.Tensor:
         """Stage 0 (or a single GPU): embeddings.  Later stages: the previous stage's hidden states."""
         if self.pp is None or self.pp.stage == 0:
-            return ops.embed(self.embed_w, inp.ids)
+            return apply_embed_overrides(ops.embed(self.embed_w, inp.ids), inp)
         x = torch.empty(inp.ids.numel(), self.cfg.hidden, dtype=torch.float32, device=self.device)
         self.pp.recv(x)
         return x

@@ -158,3 +158,23 @@ def test_fp8_kv_cache_logits_close_to_fp16():
         outs.append([r.tokens for r in eng.generate([prompt, prompt[:20]],
                                                     SamplingParams.greedy_params(max_tokens=12))])
     assert outs[0] == outs[1]
+
+
+def test_multimodal_prompt_embeds_on_gpu():
+    """Image-patch embeddings replace placeholder rows on the device path (whole and chunked
+    prefill), matching the fp32 reference forward given the same embeddings."""
+    from barq_inference_b200.models.vision import ImageInput, LlavaModel
+
+    cfg, tensors, prompt = _tiny()
+    img = ImageInput.solid_rgb(224, 224, [10, 200, 30])
+    toks = []
+    for budget in (8192, 40):
+        eng = Engine(cfg, tensors, EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=128,
+                                                max_num_batched_tokens=budget, cuda_graphs=False))
+        vlm = LlavaModel(eng)
+        toks.append(vlm.generate(prompt[:8], img, SamplingParams.greedy_params(max_tokens=4)).tokens)
+    assert toks[0] == toks[1]
+    e = vlm.image_embeddings(img).cpu()
+    ref = ReferenceModel(cfg, tensors)
+    lg = ref.forward(prompt[:8] + [0] * e.shape[0], {}, embeds=(8, e))[-1]
+    assert toks[0][0] == int(lg.argmax())
