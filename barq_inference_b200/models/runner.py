@@ -171,15 +171,19 @@ class LlamaRunner:
                      xb=None if xb is None else xb[t0:t1].contiguous())
         return out
 
-    def _row_parallel(self, j: int, fn, x: torch.Tensor) -> None:
+    def _row_parallel(self, j: int, fn, x: torch.Tensor, gemv=None) -> None:
         """Add a row-parallel layer's output into the residual ``x``.  ``fn(mode, out)`` writes this
         rank's partial with EPI_ADD_F32 (into x) or EPI_STORE_F32 (into a buffer).  One GPU: plain
         add.  Fused TP (decode-sized messages): store into the symmetric buffer j, then one kernel adds
         every rank's partial.  NCCL TP (and large messages): rank 0 adds into x, the others store
-        into x, then an all-reduce."""
+        into x, then an all-reduce.  ``gemv=(w, act, bias)``: the layer is one streaming GEMV, so with
+        the fused communicator its all-reduce runs inside that GEMV (``ops.gemv_allreduce``)."""
         c = self.comm
         if c is None or c.world == 1:
             fn(EPI_ADD_F32, x)
+        elif (c.fused and gemv is not None and not isinstance(gemv[0], tuple) and x.shape[0] <= GEMV_MAX_T
+              and c.push_ok(x.shape[0], x.shape[1]) and ops.gemv_can_allreduce(gemv[0], x.shape[0])):
+            ops.gemv_allreduce(gemv[0], gemv[1], x.shape[0], x, c.push_args, j, bias=gemv[2])
         elif c.fused and x.numel() <= c.fused_max_elems:  # large (prefill) messages go through NCCL
             fn(EPI_STORE_F32, c.partial(j, x.shape[0], x.shape[1]))
             c.allreduce_add(j, x)
@@ -371,7 +375,7 @@ class LlamaRunner:
                 ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
                                            H, Hkv, D, self.scale, cfg.sliding_window)
                 aq = ops.quantize_q8(ab, self.x2)
-            self._row_parallel(0, lambda m, o: self._lin_q8(L.wo, aq, T, m, out=o, xb=ab), x)
+            self._row_parallel(0, lambda m, o: self._lin_q8(L.wo, aq, T, m, out=o, xb=ab), x, gemv=(L.wo, aq, None))
             if L.moe is not None:
                 hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True, want_bf16=True, x2=self.x2)
                 self._moe_out(L, hq, hb, T, x)
@@ -379,7 +383,7 @@ class LlamaRunner:
             down_bf16 = self._needs_bf16(L.down)
             if L.gu_interleaved and not down_bf16:
                 h2 = self._norm_lin(L.gate_up, x, L.ffn_norm, T, EPI_SWIGLU_Q8)
-                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, h2, T, m, out=o), x)
+                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, h2, T, m, out=o), x, gemv=(L.down, h2, None))
             else:
                 hb, hq = ops.rmsnorm(x, L.ffn_norm, cfg.rms_eps, want_q8=True,
                                      want_bf16=self._needs_bf16(L.gate_up), x2=self.x2)
@@ -388,7 +392,8 @@ class LlamaRunner:
                     gu = gu.view(T, -1, 2, 32).transpose(1, 2).reshape(T, -1).contiguous()
                 hb2, hq2 = ops.swiglu(gu, cfg.ffn, want_bf16=down_bf16, want_q8=cfg.ffn % 32 == 0 and not down_bf16,
                                       x2=self.x2)
-                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, hq2, T, m, out=o, xb=hb2), x)
+                self._row_parallel(1, lambda m, o: self._lin_q8(L.down, hq2, T, m, out=o, xb=hb2), x,
+                                   gemv=(L.down, hq2, None) if hq2 is not None else None)
         if self._stage_forward(x, inp):
             return self._stage_logits(inp)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x

@@ -21,6 +21,7 @@ else:
     _IMPORT_ERROR = None
 
 EPI_STORE_F32, EPI_ADD_F32, EPI_STORE_BF16, EPI_SWIGLU_Q8 = 0, 1, 2, 3
+EPI_AR_PUSH = 5  # row-parallel GEMV with the tensor-parallel all-reduce fused in (gemv_allreduce)
 
 # Number of kernel launches issued through these wrappers (bench.py reports launches per step).
 LAUNCHES = [0]
@@ -154,6 +155,25 @@ def gemv(w: QWeight, x: Q8Act | None, T: int, mode: int = EPI_STORE_F32, out: to
     bf = out if out.dtype == torch.bfloat16 else None
     C.qgemv(*w.args(), *_ins(x), xb, T, mode, f32, bf, None, None, None, None, bias, ld, wa, wc, nh, nw, neps,
             int(x2))
+    _count()
+    return out
+
+
+def gemv_can_allreduce(w: QWeight, T: int) -> bool:
+    """Whether :func:`gemv_allreduce` (all-reduce fused into the streaming GEMV) applies."""
+    return GEMV_STREAM and w.wtype != W_BF16 and T <= 8 and w.N % 128 == 0 and w.N <= WS_ROWS
+
+
+def gemv_allreduce(w: QWeight, x: Q8Act, T: int, out: torch.Tensor, push, j: int, bias=None) -> torch.Tensor:
+    """out (f32 [T, N], the replicated residual) += sum over tensor-parallel ranks of W_r x_r, in
+    one kernel: tiles are pushed to every rank over NVLink as they finish.  ``push``: the
+    communicator's fused-push state (``Comm.push_args``)."""
+    if not gemv_can_allreduce(w, T):
+        raise ValueError("gemv_allreduce: needs a quantized weight, T <= 8 and N % 128 == 0")
+    wa, wc = _gemv_ws(w)
+    bufs, flags, epoch, done, rank, wait_s, skip = push(j, T, w.N)
+    require_ext().qgemv_ar(*w.args(), *_ins(x), T, bias, wa, wc, out, bufs, flags, epoch, done, j, rank, wait_s,
+                           int(skip))
     _count()
     return out
 

@@ -20,25 +20,9 @@
 #include "common.cuh"
 #include "launch.h"
 #include "pdl.cuh"
+#include "sysflags.cuh"
 
 namespace barq {
-
-namespace {
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-}  // namespace
 
 __global__ void __launch_bounds__(256) allreduce_add_kernel(ArArgs a) {
   pdl_wait();

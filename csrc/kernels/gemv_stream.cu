@@ -18,13 +18,20 @@
 // the last to arrive (per-tile counter) applies the epilogue and clears the workspace rows and the
 // counter again, so the next call (or CUDA-graph replay) finds them zero.
 // Epilogues: STORE_F32, ADD_F32 (partials go straight to the output with atomics), STORE_BF16,
-// SWIGLU_Q8 (rows interleaved [32 gate | 32 up]; writes silu(g)*u as int8 activations).
+// SWIGLU_Q8 (rows interleaved [32 gate | 32 up]; writes silu(g)*u as int8 activations), and
+// AR_PUSH: the tensor-parallel all-reduce of a row-parallel layer fused into the GEMV.  Every
+// finished 128-row tile is stored at once into all ranks' receive buffers (slot = this rank) by
+// plain stores over NVLink, so the transfer overlaps the remaining tiles' weight streaming; a
+// system-scope counter finds the CTA that finishes the rank's last tile, which releases a flag to
+// every peer, waits (bounded by %globaltimer) for the peers' flags and adds the world's slots into
+// the residual stream.  No separate all-reduce launch and no NCCL call on the decode path.
 // Every mbarrier wait is bounded; on expiry the CTA records an error word and unwinds.
 #include <cstdlib>
 
 #include "gemv_traits.cuh"
 #include "launch.h"
 #include "pdl.cuh"
+#include "sysflags.cuh"
 #include "tc_common.cuh"
 
 namespace barq {
@@ -83,7 +90,7 @@ struct StreamWs {
 
 template <class T, int WT, int BS, bool X2>
 __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
-    qgemv_stream_kernel(QW w, ActQ8 x, int B, GemvEpi ep, StreamWs ws, NormIn ni) {
+    qgemv_stream_kernel(QW w, ActQ8 x, int B, GemvEpi ep, StreamWs ws, NormIn ni, ArPush ar) {
   using F = TileFmt<WT>;
   using Cfg = StreamCfg<WT, BS>;
   constexpr int CH = F::CHUNK;
@@ -98,6 +105,8 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
   __shared__ float red[128][BS];
   __shared__ float comb[TPR - 1][128][BS];
   __shared__ int last_s;
+  __shared__ int ar_last_s, ar_fail_s;
+  __shared__ uint32_t ar_ep_s;
   __shared__ float red_ss[NW];
   __shared__ int err_s;
 
@@ -303,12 +312,67 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
             if (b >= B) break;
             float v = acc[b] + (ep.bias ? ep.bias[row] : 0.f);
             const size_t idx = (size_t)b * ep.ld_out + row;
-            if (ep.mode == EPI_ADD_F32)
+            if (ep.mode == EPI_AR_PUSH) {
+              const size_t o = ((size_t)ar.rank * B + b) * w.N + row;
+              for (int q = 0; q < ar.world; ++q) ar.dst[q][o] = v;  // NVLink stores (own slot: local)
+            } else if (ep.mode == EPI_ADD_F32)
               ep.out_f32[idx] += v;
             else if (ep.mode == EPI_STORE_F32)
               ep.out_f32[idx] = v;
             else
               ep.out_bf16[idx] = __float2bfloat16(v);
+          }
+        }
+        if (ep.mode == EPI_AR_PUSH) {
+          // release this tile's stores system-wide, then count it; the CTA that counts the last
+          // tile of the layer runs the exchange (the other CTAs never wait on anything)
+          if (half == 0) __threadfence_system();
+          compute_sync<NW>();
+          if (tid == 0) ar_last_s = atomicAdd_system(ar.done, 1) == tiles - 1;
+          compute_sync<NW>();
+          if (ar_last_s) {
+            if (tid == 0) {
+              __threadfence_system();  // acquire side of the counter: every CTA's stores before ours
+              *ar.done = 0;
+              ar_ep_s = *ar.epoch + 1;
+              ar_fail_s = 0;
+            }
+            compute_sync<NW>();
+            const uint32_t aep = ar_ep_s;
+            if (tid < ar.world) {
+              const int peer = tid;
+              __threadfence_system();
+              if (!ar.skip_signal) st_release_sys(ar.flags[peer] + ar.j * kArMaxRanks + ar.rank, aep);
+              if (!wait_epoch_sys(ar.flags[ar.rank] + ar.j * kArMaxRanks + peer, aep, ar.wait_ns)) {
+                ar_fail_s = 1;
+                atomicExch(ws.err, 0x300 | peer);
+              }
+            }
+            compute_sync<NW>();
+            if (!ar_fail_s) {  // x[b, n] += sum over ranks of slot r (all in this GPU's memory)
+              const int n4 = w.N / 4;
+              const float4* src = reinterpret_cast<const float4*>(ar.dst[ar.rank]);
+              for (int i = tid; i < B * n4; i += NW * 32) {
+                const int b = i / n4, c = i - b * n4;
+                float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < ar.world; ++q) {
+                  const float4 v = __ldcg(src + ((size_t)q * B + b) * n4 + c);
+                  acc4.x += v.x;
+                  acc4.y += v.y;
+                  acc4.z += v.z;
+                  acc4.w += v.w;
+                }
+                float4* px = reinterpret_cast<float4*>(ar.x + (size_t)b * ar.ld_x) + c;
+                float4 xv = *px;
+                xv.x += acc4.x;
+                xv.y += acc4.y;
+                xv.z += acc4.z;
+                xv.w += acc4.w;
+                *px = xv;
+              }
+            }
+            compute_sync<NW>();
+            if (tid == 0) *ar.epoch = aep;  // advanced on failure too, so the ranks stay aligned
           }
         }
       }
@@ -325,7 +389,7 @@ namespace {
 
 template <class T, int WT, int BS, bool X2>
 int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
-                  int n_sm, cudaStream_t st) {
+                  const ArPush& ar, int n_sm, cudaStream_t st) {
   using F = TileFmt<WT>;
   using Cfg = StreamCfg<WT, BS>;
   if (ni.h && (Cfg::XS_BYTES == 0 || w.K > kNormMaxK)) return -6;
@@ -335,31 +399,41 @@ int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const S
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const long U = (long)((w.N + 127) / 128) * (w.K / F::G);
   const int grid = (int)(U < n_sm ? U : n_sm);
-  return launch_pdl(kern, dim3(grid), dim3(THREADS), (size_t)smem, st, w, x, B, ep, ws, ni) == cudaSuccess ? 0 : -20;
+  return launch_pdl(kern, dim3(grid), dim3(THREADS), (size_t)smem, st, w, x, B, ep, ws, ni, ar) == cudaSuccess ? 0 : -20;
 }
 
 template <class T, int WT, int BS>
 int launch_stream_x(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
-                    int n_sm, cudaStream_t st) {
+                    const ArPush& ar, int n_sm, cudaStream_t st) {
   const bool x2 = ni.h ? ni.x2 != 0 : x.ql != nullptr;
-  return x2 ? launch_stream<T, WT, BS, true>(w, x, B, ep, ws, ni, n_sm, st)
-            : launch_stream<T, WT, BS, false>(w, x, B, ep, ws, ni, n_sm, st);
+  return x2 ? launch_stream<T, WT, BS, true>(w, x, B, ep, ws, ni, ar, n_sm, st)
+            : launch_stream<T, WT, BS, false>(w, x, B, ep, ws, ni, ar, n_sm, st);
 }
 
 template <class T, int WT>
 int launch_stream_b(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const StreamWs& ws, const NormIn& ni,
-                    int n_sm, cudaStream_t st) {
-  if (B <= 1) return launch_stream_x<T, WT, 1>(w, x, B, ep, ws, ni, n_sm, st);
-  if (B <= 2) return launch_stream_x<T, WT, 2>(w, x, B, ep, ws, ni, n_sm, st);
-  if (B <= 4) return launch_stream_x<T, WT, 4>(w, x, B, ep, ws, ni, n_sm, st);
-  return launch_stream_x<T, WT, 8>(w, x, B, ep, ws, ni, n_sm, st);
+                    const ArPush& ar, int n_sm, cudaStream_t st) {
+  if (B <= 1) return launch_stream_x<T, WT, 1>(w, x, B, ep, ws, ni, ar, n_sm, st);
+  if (B <= 2) return launch_stream_x<T, WT, 2>(w, x, B, ep, ws, ni, ar, n_sm, st);
+  if (B <= 4) return launch_stream_x<T, WT, 4>(w, x, B, ep, ws, ni, ar, n_sm, st);
+  return launch_stream_x<T, WT, 8>(w, x, B, ep, ws, ni, ar, n_sm, st);
 }
 
 }  // namespace
 
 int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
-                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st) {
+                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st,
+                 const ArPush* ar) {
   const NormIn ni{norm_h, norm_w, norm_eps, norm_x2};
+  ArPush arp{};
+  if (ep.mode == EPI_AR_PUSH) {
+    if (!ar || ar->world < 1 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || !ar->x ||
+        !ar->epoch || !ar->done || (w.N % 128) || (ar->ld_x % 4) || (reinterpret_cast<uintptr_t>(ar->x) & 15))
+      return -7;
+    for (int q = 0; q < ar->world; ++q)
+      if (!ar->dst[q] || !ar->flags[q] || (reinterpret_cast<uintptr_t>(ar->dst[q]) & 15)) return -7;
+    arp = *ar;
+  }
   if (B < 1 || B > 8) return -1;
   if (ep.mode == EPI_SWIGLU_Q8 && (w.N % 128)) return -3;
   if ((reinterpret_cast<uintptr_t>(w.p0) & 15)) return -4;
@@ -376,12 +450,12 @@ int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* w
   }();
   const StreamWs ws{ws_acc, ws_cnt, err, exp_flags};
   switch (w.type) {
-    case W_Q4_0: if (w.K % 64) return -2; return launch_stream_b<T4Block<false>, W_Q4_0>(w, x, B, ep, ws, ni, n_sm, st);
-    case W_IQ4_NL: if (w.K % 64) return -2; return launch_stream_b<T4Block<true>, W_IQ4_NL>(w, x, B, ep, ws, ni, n_sm, st);
-    case W_Q8_0: if (w.K % 64) return -2; return launch_stream_b<TQ8_0, W_Q8_0>(w, x, B, ep, ws, ni, n_sm, st);
-    case W_Q4_K: if (w.K % 256) return -2; return launch_stream_b<TK45<false>, W_Q4_K>(w, x, B, ep, ws, ni, n_sm, st);
-    case W_Q5_K: if (w.K % 256) return -2; return launch_stream_b<TK45<true>, W_Q5_K>(w, x, B, ep, ws, ni, n_sm, st);
-    case W_Q6_K: if (w.K % 256) return -2; return launch_stream_b<TQ6_K, W_Q6_K>(w, x, B, ep, ws, ni, n_sm, st);
+    case W_Q4_0: if (w.K % 64) return -2; return launch_stream_b<T4Block<false>, W_Q4_0>(w, x, B, ep, ws, ni, arp, n_sm, st);
+    case W_IQ4_NL: if (w.K % 64) return -2; return launch_stream_b<T4Block<true>, W_IQ4_NL>(w, x, B, ep, ws, ni, arp, n_sm, st);
+    case W_Q8_0: if (w.K % 64) return -2; return launch_stream_b<TQ8_0, W_Q8_0>(w, x, B, ep, ws, ni, arp, n_sm, st);
+    case W_Q4_K: if (w.K % 256) return -2; return launch_stream_b<TK45<false>, W_Q4_K>(w, x, B, ep, ws, ni, arp, n_sm, st);
+    case W_Q5_K: if (w.K % 256) return -2; return launch_stream_b<TK45<true>, W_Q5_K>(w, x, B, ep, ws, ni, arp, n_sm, st);
+    case W_Q6_K: if (w.K % 256) return -2; return launch_stream_b<TQ6_K, W_Q6_K>(w, x, B, ep, ws, ni, arp, n_sm, st);
   }
   return -5;
 }

@@ -11,7 +11,14 @@ namespace barq {
 // KV cache element types
 constexpr int kCacheF16 = 0, kCacheBF16 = 1, kCacheFP8 = 2;
 
-enum EpiMode : int { EPI_STORE_F32 = 0, EPI_ADD_F32 = 1, EPI_STORE_BF16 = 2, EPI_SWIGLU_Q8 = 3, EPI_MOE_COMBINE = 4 };
+enum EpiMode : int {
+  EPI_STORE_F32 = 0,
+  EPI_ADD_F32 = 1,
+  EPI_STORE_BF16 = 2,
+  EPI_SWIGLU_Q8 = 3,
+  EPI_MOE_COMBINE = 4,
+  EPI_AR_PUSH = 5,  // streaming GEMV only: tensor-parallel all-reduce fused into the epilogue (ArPush)
+};
 
 struct GemvEpi {
   int mode;
@@ -117,8 +124,21 @@ int* kernel_err_word();  // device error word shared by the bounded-wait kernels
 // them zero.  Calls sharing a workspace must not overlap on the GPU.  err: bounded-wait error word.
 // norm_h (optional, f32 [B, K], K <= 4096, B <= 2): the activation is computed in the kernel as
 // int8(rmsnorm(norm_h) * norm_w) (two-term if norm_x2) instead of being read from x.
+// Fused GEMV + all-reduce (EPI_AR_PUSH): each finished output tile is stored straight into every
+// rank's receive buffer (slot = this rank) over NVLink; the CTA that finishes the rank's last tile
+// signals the peers, waits (bounded) for theirs and adds the world's slots into the residual x.
+struct ArPush {
+  float* dst[kArMaxRanks];       // receive buffer j of every rank: [world][B][N] f32
+  uint32_t* flags[kArMaxRanks];  // every rank's push flag words [2][kArMaxRanks] (buffer-major)
+  uint32_t* epoch;               // this rank's epoch of buffer j (device)
+  int* done;                     // this rank's finished-tile counter for buffer j (zero between calls)
+  float* x;                      // residual stream [B, ld_x]
+  int ld_x, j, rank, world, skip_signal;
+  unsigned long long wait_ns;
+};
 int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
-                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st);
+                 const float* norm_h, const float* norm_w, float norm_eps, int norm_x2, cudaStream_t st,
+                 const ArPush* ar = nullptr);
 void gemm_set_trace(void* p);  // diagnostics (BARQ_GEMM_EXP bit 1): [256 stages][8] u64 stamps of CTA 0
 int gemm_clear_error_word();
 

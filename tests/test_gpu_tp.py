@@ -1,7 +1,8 @@
 """Tensor parallel (attention TP x MoE EP) on 2 GPUs vs the same model on one GPU.
 
-Runs 2 NCCL ranks as child processes (skipped with fewer than 2 GPUs); both the fused one-shot
-all-reduce (symmetric memory, csrc/kernels/allreduce.cu) and the NCCL baseline are checked."""
+Runs 2 NCCL ranks as child processes (skipped with fewer than 2 GPUs).  Three communication modes:
+"push" (decode: the all-reduce fused into the row-parallel streaming GEMV; otherwise the one-shot
+kernel), "oneshot" (symmetric memory, csrc/kernels/allreduce.cu) and the NCCL baseline."""
 import os
 import socket
 
@@ -38,7 +39,7 @@ def _logits(runner, prompt, steps=3):
     return torch.stack(out)
 
 
-def _worker(rank, world, port, name, fused, q):
+def _worker(rank, world, port, name, mode, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -52,12 +53,15 @@ def _worker(rank, world, port, name, fused, q):
     full = random_tensors(cfg, POLICIES["tiny"], seed=4)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
-    comm = Comm(dev, fused=fused, max_elems=64 * cfg.hidden)
+    comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden, hidden=cfg.hidden if mode == "push" else 0)
     shard, info = shard_tensors(cfg, full, rank, world)
     r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
     r.allocate_kv(32)
     tp_logits = _logits(r, prompt)
     comm.check()
+    pushes = int(comm.push_epoch.sum()) if mode == "push" else -1
+    if mode == "push":  # the fused GEMV all-reduce ran on the decode steps (epochs advance per call)
+        assert pushes > 0, pushes
     if rank == 0:
         ref = LlamaRunner(cfg, full, dev)
         ref.allocate_kv(32)
@@ -70,14 +74,14 @@ def _worker(rank, world, port, name, fused, q):
 
 @needs2
 @pytest.mark.parametrize("name", ["tiny", "tiny-moe"])
-@pytest.mark.parametrize("fused", [True, False])
-def test_tp2_matches_single_gpu(name, fused):
+@pytest.mark.parametrize("mode", ["push", "oneshot", "nccl"])
+def test_tp2_matches_single_gpu(name, mode):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, name, fused, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, name, mode, q)) for r in range(2)]
     for p in ps:
         p.start()
     status, err = q.get(timeout=300)
