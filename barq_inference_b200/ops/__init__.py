@@ -167,13 +167,13 @@ def gemv_can_allreduce(w: QWeight, T: int) -> bool:
 def gemv_allreduce(w: QWeight, x: Q8Act, T: int, out: torch.Tensor, push, j: int, bias=None) -> torch.Tensor:
     """out (f32 [T, N], the replicated residual) += sum over tensor-parallel ranks of W_r x_r, in
     one kernel: tiles are pushed to every rank over NVLink as they finish.  ``push``: the
-    communicator's fused-push state (``Comm.push_args``)."""
+    communicator's fused-push state (``Comm.push_args``: int64 device table of the ranks' receive
+    buffers for call site j, epoch and counter tensors, rank, wait limit, fault-injection flag)."""
     if not gemv_can_allreduce(w, T):
         raise ValueError("gemv_allreduce: needs a quantized weight, T <= 8 and N % 128 == 0")
     wa, wc = _gemv_ws(w)
-    bufs, flags, epoch, done, rank, wait_s, skip = push(j, T, w.N)
-    require_ext().qgemv_ar(*w.args(), *_ins(x), T, bias, wa, wc, out, bufs, flags, epoch, done, j, rank, wait_s,
-                           int(skip))
+    bufs, epoch, done, rank, wait_s, skip = push(j, T, w.N)
+    require_ext().qgemv_ar(*w.args(), *_ins(x), T, bias, wa, wc, out, bufs, epoch, done, j, rank, wait_s, int(skip))
     _count()
     return out
 

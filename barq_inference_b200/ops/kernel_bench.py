@@ -88,8 +88,39 @@ def cases(tokens: int):
         out = torch.empty(1, w.N, device="cuda")
         return w, (lambda: gemv(w, xa, 1, EPI_STORE_F32, out=out, x2=True)), 2.0 * w.N * w.K
 
-    return {"gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
-            "gemv_head": gemv_head, "gemv_qkv": gemv_qkv}
+    def gemv_o_tp2(push: bool):
+        # attention output of one rank under TP=2 (K halved); push: the all-reduce fused in, as a
+        # world of one (the exchange protocol runs against this GPU's own flag)
+        def make():
+            from . import gemv_allreduce
+
+            w = _qw(4096, 2048, GGMLType.Q4_K, 6)
+            xa = quantize_q8(torch.randn(1, 2048, device="cuda"), True)
+            x = torch.zeros(1, 4096, device="cuda")
+            if not push:
+                return w, (lambda: gemv(w, xa, 1, EPI_ADD_F32, out=x, x2=True)), 2.0 * w.N * w.K
+            buf = torch.zeros(4096, dtype=torch.int64, device="cuda")
+            ctr = torch.zeros(2, dtype=torch.int32, device="cuda"), torch.zeros(2, dtype=torch.int32, device="cuda")
+            tab = torch.tensor([buf.data_ptr()], dtype=torch.int64, device="cuda")
+            args = lambda j, T, H: (tab, ctr[0], ctr[1], 0, 5.0, 0)  # noqa: E731
+            return w, (lambda: gemv_allreduce(w, xa, 1, x, args, 0)), 2.0 * w.N * w.K
+        return make
+
+    def allreduce_w1():
+        # the separate one-shot all-reduce kernel on a decode-sized message, as a world of one
+        from . import require_ext
+
+        x = torch.zeros(1, 4096, device="cuda")
+        buf = torch.zeros(4096, device="cuda")
+        flags = torch.zeros(64 * 8, dtype=torch.int32, device="cuda")
+        epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
+        C = require_ext()
+        fn = lambda: C.allreduce_add(x, [buf.data_ptr()], [flags.data_ptr()], epoch, 0, 4, 5.0, 0)  # noqa: E731
+        return _qw(128, 256, GGMLType.Q4_K, 7), fn, 0.0
+
+    return {"allreduce_w1": allreduce_w1, "gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
+            "gemv_head": gemv_head, "gemv_qkv": gemv_qkv, "gemv_o_tp2": gemv_o_tp2(False),
+            "gemv_o_tp2_push": gemv_o_tp2(True)}
 
 
 def main(argv=None):

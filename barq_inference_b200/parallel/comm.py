@@ -13,9 +13,9 @@ and ``CommBackend`` (``advanced/src/tensor_parallel.rs:28-37``), all stubs in th
   partials into the residual stream in one kernel -- a one-shot all-reduce with the residual add
   fused, no NCCL launch on the decode path.
 * Fused GEMV + all-reduce (decode, up to ``push_rows`` tokens): the same allocation also holds two
-  receive buffers of ``world`` slots each; the row-parallel streaming GEMV itself stores every
-  finished tile into all ranks' slot for this rank and performs the exchange
-  (``ops.gemv_allreduce``), so the all-reduce costs no launch of its own.
+  receive buffers of ``world`` slots of 64-bit (epoch, value) words; the row-parallel streaming
+  GEMV itself stores every finished tile into all peers' slot for this rank and adds the peers'
+  tiles as they arrive (``ops.gemv_allreduce``), so the all-reduce costs no launch of its own.
 """
 from __future__ import annotations
 
@@ -45,7 +45,7 @@ class Comm:
         self.fused_max_elems = 256 * 1024
         self.skip_signal = False  # fault injection (BARQ_FAULT skip_flag)
         self.max_elems = max_elems
-        # fused GEMV + all-reduce receive buffers: [2][world][push_rows * hidden] f32
+        # fused GEMV + all-reduce receive buffers: [2][world][push_rows * hidden] 64-bit words
         self.push_elems = push_rows * hidden if (self.fused and hidden) else 0
         self.push_fused = self.push_elems > 0 and os.environ.get("BARQ_AR_PUSH", "1") != "0"
         if self.fused:
@@ -57,10 +57,8 @@ class Comm:
 
         n = (n + 63) // 64 * 64
         flag_words = 64 * 8  # kArMaxBlocks x kArMaxRanks u32
-        push_flag_words = 64  # [2][kArMaxRanks] u32, padded to 256 bytes
         pe = self.push_elems
-        self.buf = symm.empty(2 * n + flag_words + push_flag_words + 2 * self.world * pe, dtype=torch.float32,
-                              device=self.device)
+        self.buf = symm.empty(2 * n + flag_words + 2 * self.world * pe * 2, dtype=torch.float32, device=self.device)
         self.buf.zero_()
         self.hdl = symm.rendezvous(self.buf, dist.group.WORLD)
         torch.cuda.synchronize(self.device)
@@ -70,9 +68,9 @@ class Comm:
         self._flags = [p + 2 * n * 4 for p in base]
         self._n = n
         self.epoch = torch.zeros(64, dtype=torch.int32, device=self.device)
-        off = 2 * n + flag_words
-        self._push_flags = [p + off * 4 for p in base]
-        self._push_bufs = [[p + (off + push_flag_words + j * self.world * pe) * 4 for p in base] for j in (0, 1)]
+        off = 2 * n + flag_words  # a multiple of 64 floats: the words are 8-byte aligned
+        self._push_bufs = [torch.tensor([p + (off + j * self.world * pe * 2) * 4 for p in base], dtype=torch.int64,
+                                        device=self.device) for j in (0, 1)]
         self.push_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.push_done = torch.zeros(2, dtype=torch.int32, device=self.device)
 
@@ -83,8 +81,7 @@ class Comm:
         """Arguments of ``ops.gemv_allreduce`` for call site j (0: attention output, 1: FFN down)."""
         if not self.push_ok(T, H):
             raise ValueError(f"fused GEMV all-reduce buffers hold {self.push_elems} values, {T * H} requested")
-        return (self._push_bufs[j], self._push_flags, self.push_epoch, self.push_done, self.rank, self.wait_s,
-                self.skip_signal)
+        return self._push_bufs[j], self.push_epoch, self.push_done, self.rank, self.wait_s, self.skip_signal
 
     def partial(self, j: int, T: int, H: int) -> torch.Tensor:
         """Local partial-sum buffer j (0: attention output, 1: FFN down) viewed as f32 [T, H]."""

@@ -195,16 +195,17 @@ void allreduce_add(Tensor x, std::vector<int64_t> bufs, std::vector<int64_t> fla
 }
 
 // Row-parallel GEMV with the tensor-parallel all-reduce fused in (EPI_AR_PUSH): x += sum over ranks
-// of W_r a_r.  bufs: every rank's receive buffer for this call site ([world][B][N] f32); flags:
-// every rank's push flag words; epoch / done: this rank's int32 [2] counters, indexed by j.
+// of W_r a_r.  bufs: int64 device tensor [world] of every rank's receive-buffer address for this
+// call site (each [world][B][N] 64-bit words);
+// epoch / done: this rank's int32 [2] counters, indexed by j.
 void qgemv_ar(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, OptT xq, OptT xs, OptT xql,
-              OptT xdl, int64_t B, OptT bias, Tensor ws_acc, Tensor ws_cnt, Tensor x, std::vector<int64_t> bufs,
-              std::vector<int64_t> flags, Tensor epoch, Tensor done, int64_t j, int64_t rank, double wait_s,
-              int64_t skip_signal) {
+              OptT xdl, int64_t B, OptT bias, Tensor ws_acc, Tensor ws_cnt, Tensor x, Tensor bufs, Tensor epoch,
+              Tensor done, int64_t j, int64_t rank, double wait_s, int64_t skip_signal) {
   c10::cuda::CUDAGuard g(p0.device());
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.stride(1) == 1 && x.size(0) >= B && x.size(1) == N,
               "qgemv_ar: x must be f32 [B, N] with unit column stride");
-  TORCH_CHECK(bufs.size() == flags.size() && bufs.size() <= (size_t)barq::kArMaxRanks && j >= 0 && j < 2,
+  TORCH_CHECK(bufs.is_cuda() && bufs.scalar_type() == torch::kInt64 && bufs.numel() >= 1 &&
+                  bufs.numel() <= barq::kArMaxRanks && j >= 0 && j < 2,
               "qgemv_ar: ranks / buffer index");
   TORCH_CHECK(epoch.scalar_type() == torch::kInt32 && done.scalar_type() == torch::kInt32 && epoch.numel() >= 2 &&
                   done.numel() >= 2, "qgemv_ar: epoch / done must be int32 [2]");
@@ -214,17 +215,13 @@ void qgemv_ar(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, O
                  optptr<const float2>(xdl)};
   barq::GemvEpi ep{barq::EPI_AR_PUSH, nullptr, nullptr, barq::ActOut{}, optptr<const float>(bias), (int)N};
   barq::ArPush ar{};
-  for (size_t r = 0; r < bufs.size(); ++r) {
-    ar.dst[r] = reinterpret_cast<float*>(bufs[r]);
-    ar.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
-  }
+  ar.dst = reinterpret_cast<uint64_t* const*>(bufs.data_ptr());
   ar.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>()) + j;
   ar.done = done.data_ptr<int>() + j;
   ar.x = ptr<float>(x);
   ar.ld_x = (int)x.stride(0);
-  ar.j = (int)j;
   ar.rank = (int)rank;
-  ar.world = (int)bufs.size();
+  ar.world = (int)bufs.numel();
   ar.skip_signal = (int)skip_signal;
   ar.wait_ns = (unsigned long long)(wait_s * 1e9);
   check(barq::qgemv_stream(w, xa, (int)B, ep, ptr<float>(ws_acc), ptr<int>(ws_cnt), barq::kernel_err_word(), nullptr,

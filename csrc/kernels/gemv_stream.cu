@@ -19,12 +19,14 @@
 // counter again, so the next call (or CUDA-graph replay) finds them zero.
 // Epilogues: STORE_F32, ADD_F32 (partials go straight to the output with atomics), STORE_BF16,
 // SWIGLU_Q8 (rows interleaved [32 gate | 32 up]; writes silu(g)*u as int8 activations), and
-// AR_PUSH: the tensor-parallel all-reduce of a row-parallel layer fused into the GEMV.  Every
-// finished 128-row tile is stored at once into all ranks' receive buffers (slot = this rank) by
-// plain stores over NVLink, so the transfer overlaps the remaining tiles' weight streaming; a
-// system-scope counter finds the CTA that finishes the rank's last tile, which releases a flag to
-// every peer, waits (bounded by %globaltimer) for the peers' flags and adds the world's slots into
-// the residual stream.  No separate all-reduce launch and no NCCL call on the decode path.
+// AR_PUSH: the tensor-parallel all-reduce of a row-parallel layer fused into the GEMV.  The CTA
+// that finishes a 128-row tile stores it at once into every peer's receive buffer (slot = this
+// rank) over NVLink, each value packed with the call's epoch into one 64-bit store, so no memory
+// fence or flag is needed: a reader that sees the epoch sees the value (the low-latency protocol
+// of NCCL's LL mode).  It then waits for the same tile of every peer in its own receive buffer
+// (bounded by %globaltimer) and adds the world's sum into the residual stream.  Every rank splits
+// the work identically, so tile t's exchange only waits on the peers' tile t; no separate
+// all-reduce launch and no NCCL call on the decode path.
 // Every mbarrier wait is bounded; on expiry the CTA records an error word and unwinds.
 #include <cstdlib>
 
@@ -83,7 +85,8 @@ struct StreamWs {
   float* acc;  // [8, N] f32 partial sums of shared row tiles (zero between calls)
   int* cnt;    // [N / 128] units accumulated per row tile (zero between calls)
   int* err;
-  int exp;  // diagnostics: bit 0 = compute warps skip the arithmetic (still wait for and release chunks)
+  int exp;  // diagnostics: bit 0 = compute warps skip the arithmetic (still wait for and release chunks);
+            // AR_PUSH: bit 1 = skip the flag exchange, bit 2 = skip the final reduction
 };
 
 }  // namespace
@@ -105,8 +108,6 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
   __shared__ float red[128][BS];
   __shared__ float comb[TPR - 1][128][BS];
   __shared__ int last_s;
-  __shared__ int ar_last_s, ar_fail_s;
-  __shared__ uint32_t ar_ep_s;
   __shared__ float red_ss[NW];
   __shared__ int err_s;
 
@@ -186,6 +187,8 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
       }
       x = ActQ8{sq, ssc, ni.x2 ? sql : nullptr, ni.x2 ? sdl : nullptr};
     }
+    uint32_t ar_ep = 0;  // AR_PUSH: this call's epoch (the counter is advanced by the last CTA out)
+    if (ep.mode == EPI_AR_PUSH) ar_ep = *ar.epoch + 1;
     const int half = warp % TPR, r = (warp / TPR) * 32 + lane;  // half: this warp's slice of the row
     const int tid = threadIdx.x;
     float acc[BS];
@@ -313,8 +316,13 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
             float v = acc[b] + (ep.bias ? ep.bias[row] : 0.f);
             const size_t idx = (size_t)b * ep.ld_out + row;
             if (ep.mode == EPI_AR_PUSH) {
+              // (epoch, value) in one 64-bit store: a peer that sees the epoch sees the value
               const size_t o = ((size_t)ar.rank * B + b) * w.N + row;
-              for (int q = 0; q < ar.world; ++q) ar.dst[q][o] = v;  // NVLink stores (own slot: local)
+              const uint64_t pk = ((uint64_t)ar_ep << 32) | __float_as_uint(v);
+              if (!ar.skip_signal)
+                for (int q = 0; q < ar.world; ++q)
+                  if (q != ar.rank) st_relaxed_sys_u64(ar.dst[q] + o, pk);  // NVLink store
+              red[r][b] = v;
             } else if (ep.mode == EPI_ADD_F32)
               ep.out_f32[idx] += v;
             else if (ep.mode == EPI_STORE_F32)
@@ -322,63 +330,40 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
             else
               ep.out_bf16[idx] = __float2bfloat16(v);
           }
-        }
-        if (ep.mode == EPI_AR_PUSH) {
-          // release this tile's stores system-wide, then count it; the CTA that counts the last
-          // tile of the layer runs the exchange (the other CTAs never wait on anything)
-          if (half == 0) __threadfence_system();
-          compute_sync<NW>();
-          if (tid == 0) ar_last_s = atomicAdd_system(ar.done, 1) == tiles - 1;
-          compute_sync<NW>();
-          if (ar_last_s) {
-            if (tid == 0) {
-              __threadfence_system();  // acquire side of the counter: every CTA's stores before ours
-              *ar.done = 0;
-              ar_ep_s = *ar.epoch + 1;
-              ar_fail_s = 0;
-            }
-            compute_sync<NW>();
-            const uint32_t aep = ar_ep_s;
-            if (tid < ar.world) {
-              const int peer = tid;
-              __threadfence_system();
-              if (!ar.skip_signal) st_release_sys(ar.flags[peer] + ar.j * kArMaxRanks + ar.rank, aep);
-              if (!wait_epoch_sys(ar.flags[ar.rank] + ar.j * kArMaxRanks + peer, aep, ar.wait_ns)) {
-                ar_fail_s = 1;
-                atomicExch(ws.err, 0x300 | peer);
+          if (ep.mode == EPI_AR_PUSH) {
+            // the same tile of every peer: wait for its (epoch, value) words in this GPU's
+            // receive buffer, then add the world's sum into the residual stream
+            const uint64_t* own = ar.dst[ar.rank];
+            for (int b = 0; b < B; ++b) {
+              float sum = red[r][b];
+              bool ok = true;
+              for (int q = 0; q < ar.world && ok; ++q) {
+                if (q == ar.rank) continue;
+                uint64_t pk = 0;
+                ok = wait_pair_sys(own + ((size_t)q * B + b) * w.N + row, ar_ep, ar.wait_ns, ws.err,
+                                   pk);
+                if (ok)
+                  sum += __uint_as_float((uint32_t)pk);
+                else
+                  atomicExch(ws.err, 0x300 | q);
               }
+              if (ok) ar.x[(size_t)b * ar.ld_x + row] += sum;
             }
-            compute_sync<NW>();
-            if (!ar_fail_s) {  // x[b, n] += sum over ranks of slot r (all in this GPU's memory)
-              const int n4 = w.N / 4;
-              const float4* src = reinterpret_cast<const float4*>(ar.dst[ar.rank]);
-              for (int i = tid; i < B * n4; i += NW * 32) {
-                const int b = i / n4, c = i - b * n4;
-                float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int q = 0; q < ar.world; ++q) {
-                  const float4 v = __ldcg(src + ((size_t)q * B + b) * n4 + c);
-                  acc4.x += v.x;
-                  acc4.y += v.y;
-                  acc4.z += v.z;
-                  acc4.w += v.w;
-                }
-                float4* px = reinterpret_cast<float4*>(ar.x + (size_t)b * ar.ld_x) + c;
-                float4 xv = *px;
-                xv.x += acc4.x;
-                xv.y += acc4.y;
-                xv.z += acc4.z;
-                xv.w += acc4.w;
-                *px = xv;
-              }
-            }
-            compute_sync<NW>();
-            if (tid == 0) *ar.epoch = aep;  // advanced on failure too, so the ranks stay aligned
           }
         }
       }
       compute_sync<NW>();  // comb[] / red[] are free again for the next row tile
 #pragma unroll
       for (int b = 0; b < BS; ++b) acc[b] = 0.f;
+    }
+    if (ep.mode == EPI_AR_PUSH) {
+      // every CTA has read the epoch (program order before its acq_rel count): the last one out
+      // advances it and clears the counter for the next call / graph replay
+      compute_sync<NW>();
+      if (tid == 0 && atom_add_acq_rel_gpu(ar.done, 1) == (int)gridDim.x - 1) {
+        *ar.done = 0;
+        *ar.epoch = ar_ep;
+      }
     }
   }
   __syncthreads();
@@ -430,8 +415,7 @@ int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* w
     if (!ar || ar->world < 1 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || !ar->x ||
         !ar->epoch || !ar->done || (w.N % 128) || (ar->ld_x % 4) || (reinterpret_cast<uintptr_t>(ar->x) & 15))
       return -7;
-    for (int q = 0; q < ar->world; ++q)
-      if (!ar->dst[q] || !ar->flags[q] || (reinterpret_cast<uintptr_t>(ar->dst[q]) & 15)) return -7;
+    if (!ar->dst) return -7;
     arp = *ar;
   }
   if (B < 1 || B > 8) return -1;

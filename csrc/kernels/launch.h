@@ -124,16 +124,17 @@ int* kernel_err_word();  // device error word shared by the bounded-wait kernels
 // them zero.  Calls sharing a workspace must not overlap on the GPU.  err: bounded-wait error word.
 // norm_h (optional, f32 [B, K], K <= 4096, B <= 2): the activation is computed in the kernel as
 // int8(rmsnorm(norm_h) * norm_w) (two-term if norm_x2) instead of being read from x.
-// Fused GEMV + all-reduce (EPI_AR_PUSH): each finished output tile is stored straight into every
-// rank's receive buffer (slot = this rank) over NVLink; the CTA that finishes the rank's last tile
-// signals the peers, waits (bounded) for theirs and adds the world's slots into the residual x.
+// Fused GEMV + all-reduce (EPI_AR_PUSH): the CTA that finishes an output tile stores it into every
+// peer's receive buffer (slot = this rank) over NVLink as (epoch, value) 64-bit words, then waits
+// (bounded) for the peers' words of the same tile and adds the world's sum into the residual x.
 struct ArPush {
-  float* dst[kArMaxRanks];       // receive buffer j of every rank: [world][B][N] f32
-  uint32_t* flags[kArMaxRanks];  // every rank's push flag words [2][kArMaxRanks] (buffer-major)
+  uint64_t* const* dst;          // device table: receive buffer j of every rank, [world][B][N] words
+                                 // (epoch << 32 | f32 bits); a table in memory, not a parameter
+                                 // array, so that indexing it by rank needs no local-memory copy
   uint32_t* epoch;               // this rank's epoch of buffer j (device)
-  int* done;                     // this rank's finished-tile counter for buffer j (zero between calls)
+  int* done;                     // this rank's CTA-exit counter for buffer j (zero between calls)
   float* x;                      // residual stream [B, ld_x]
-  int ld_x, j, rank, world, skip_signal;
+  int ld_x, rank, world, skip_signal;
   unsigned long long wait_ns;
 };
 int qgemv_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, float* ws_acc, int* ws_cnt, int* err,
