@@ -105,19 +105,60 @@ class _Seq:
 
 
 def _probs(logits: torch.Tensor, p: SamplingParams) -> torch.Tensor:
+    """Sampling distribution of every row of ``logits`` [R, V] (temperature, top-k, top-p, min-p in
+    that order, as the host samplers apply them), computed on the logits' device for all rows at
+    once.  Greedy: one-hot argmax."""
     if p.temperature <= 0:
         out = torch.zeros_like(logits)
         out.scatter_(-1, logits.argmax(-1, keepdim=True), 1.0)
         return out
-    from ..sampling.host_samplers import min_p_filter, top_k_filter, top_p_filter
+    lg = logits.float() / p.temperature
+    V = lg.shape[-1]
+    if 0 < p.top_k < V:
+        th = torch.topk(lg, p.top_k, dim=-1).values[:, -1:]
+        lg = lg.masked_fill(lg < th, -float("inf"))
+    if p.top_p < 1.0:
+        sl, si = torch.sort(lg, dim=-1, descending=True)
+        pr = torch.softmax(sl, -1)
+        remove = (pr.cumsum(-1) - pr) >= p.top_p
+        remove[:, 0] = False
+        lg = lg.scatter(-1, si, sl.masked_fill(remove, -float("inf")))
+    if p.min_p > 0.0:
+        pr = torch.softmax(lg, -1)
+        lg = lg.masked_fill(pr < p.min_p * pr.amax(-1, keepdim=True), -float("inf"))
+    return torch.softmax(lg, -1)
 
-    rows = []
-    for lg in logits:
-        lg = top_k_filter(lg / p.temperature, p.top_k)
-        lg = top_p_filter(lg, p.top_p)
-        lg = min_p_filter(lg, p.min_p)
-        rows.append(torch.softmax(lg, -1))
-    return torch.stack(rows)
+
+def verify_drafts(ps: torch.Tensor, qs: torch.Tensor, drafts: torch.Tensor, greedy: bool,
+                  gen: torch.Generator | None = None) -> tuple[int, list[int]]:
+    """Rejection step of speculative decoding for k drafted tokens, on the device of ``ps``.
+
+    ps: target distributions [k+1, V] (rows for the positions of d1..dk and the bonus position);
+    qs: draft distributions [k, V]; drafts: int64 [k].  Returns (number accepted, tokens to append):
+    the accepted prefix plus either the correction sampled from norm(max(0, p - q)) at the first
+    rejection or the bonus token sampled from the last target row.  Greedy: accept while the
+    target's argmax agrees, then append the target's argmax.  One host synchronization."""
+    k = drafts.numel()
+    ar = torch.arange(k, device=ps.device)
+    if greedy:
+        tgt = ps.argmax(-1)  # [k+1]
+        ok = tgt[:k] == drafts
+    else:
+        px = ps[ar, drafts]
+        qx = qs[ar, drafts].clamp_min(1e-20)
+        u = torch.rand(k, generator=gen, device=ps.device) if gen is not None else torch.rand(k, device=ps.device)
+        ok = u < torch.clamp(px / qx, max=1.0)
+    n_acc = int(torch.cumprod(ok.to(torch.int32), 0).sum()) if k else 0
+    acc = drafts[:n_acc].tolist()
+    if greedy:
+        return n_acc, acc + [int(tgt[n_acc])]
+    if n_acc < k:
+        r = (ps[n_acc] - qs[n_acc]).clamp_min(0)
+        tot = r.sum()
+        r = r / tot if float(tot) > 0 else ps[n_acc]
+    else:
+        r = ps[k]
+    return n_acc, acc + [int(torch.multinomial(r, 1, generator=gen))]
 
 
 class SpeculativeDecoder:
@@ -133,7 +174,9 @@ class SpeculativeDecoder:
     @torch.no_grad()
     def generate(self, prompt: list[int], params: SamplingParams) -> SpecResult:
         t0 = time.perf_counter()
-        gen = torch.Generator(device="cpu").manual_seed(params.seed or 1234)
+        dev = self.t.device
+        gen = torch.Generator(device=dev).manual_seed(params.seed or 1234)
+        greedy = params.temperature <= 0
         ts, ds = _Seq(self.t), _Seq(self.d)
         try:
             # invariant: the target cache holds every token but the last; the draft may lag behind
@@ -150,39 +193,16 @@ class SpeculativeDecoder:
                 drafts, qs = [], []
                 feed = tokens[ds.len:]
                 for _ in range(k):
-                    ql = ds.forward(feed, False)[-1:]
-                    q = _probs(ql.cpu(), params)[0]
-                    cur = int(torch.argmax(q)) if params.temperature <= 0 else int(torch.multinomial(q, 1, generator=gen))
+                    q = _probs(ds.forward(feed, False)[-1:], params)  # [1, V] on the device
+                    cur = int(q.argmax()) if greedy else int(torch.multinomial(q[0], 1, generator=gen))
                     drafts.append(cur)
                     qs.append(q)
                     feed = [cur]
                 # 2) target scores [last, d1..dk] in one forward -> k+1 distributions
-                pl = ts.forward([last] + drafts, True).cpu()
-                ps = _probs(pl, params)
-                # 3) accept / reject
-                n_acc = 0
-                new = []
-                for i, x in enumerate(drafts):
-                    p, q = ps[i], qs[i]
-                    if params.temperature <= 0:
-                        ok = int(torch.argmax(p)) == x
-                    else:
-                        ok = torch.rand((), generator=gen).item() < min(1.0, float(p[x] / max(float(q[x]), 1e-20)))
-                    if ok:
-                        new.append(x)
-                        n_acc += 1
-                        continue
-                    if params.temperature <= 0:
-                        new.append(int(torch.argmax(p)))
-                    else:
-                        r = (p - q).clamp_min(0)
-                        r = r / r.sum() if r.sum() > 0 else p
-                        new.append(int(torch.multinomial(r, 1, generator=gen)))
-                    break
-                else:
-                    p = ps[k]
-                    bonus = int(torch.argmax(p)) if params.temperature <= 0 else int(torch.multinomial(p, 1, generator=gen))
-                    new.append(bonus)
+                ps = _probs(ts.forward([last] + drafts, True), params)
+                # 3) accept / reject on the device (one host synchronization)
+                n_acc, new = verify_drafts(ps, torch.cat(qs), torch.tensor(drafts, device=ps.device), greedy, gen)
+                if n_acc == k:
                     self.stats.bonus += 1
                 self.stats.drafted += k
                 self.stats.accepted += n_acc

@@ -178,3 +178,50 @@ def test_multimodal_prompt_embeds_on_gpu():
     ref = ReferenceModel(cfg, tensors)
     lg = ref.forward(prompt[:8] + [0] * e.shape[0], {}, embeds=(8, e))[-1]
     assert toks[0][0] == int(lg.argmax())
+
+
+def test_long_context_32k_yarn_prefill_vs_decode():
+    """A 32k-token context (YaRN x4 over an 8k original window): the last token's logits from the
+    decode path (split-KV decode attention over 2048 pages) match the prefill path's (paged prefill
+    attention) for the same position."""
+    import dataclasses
+
+    cfg = dataclasses.replace(preset("tiny", max_ctx=32768), rope_scaling="yarn", rope_factor=4.0,
+                              rope_orig_ctx=8192)
+    tensors = random_tensors(cfg, POLICIES["tiny"], seed=0)
+    L = 32768 - 8
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, cfg.vocab, (L,), generator=g).tolist()
+    runner = LlamaRunner(cfg, tensors, DEV)
+    runner.allocate_kv(L // 16 + 8)
+    table = list(range(1, L // 16 + 2))
+    for s in range(0, L - 1, 4096):
+        _run(runner, prompt[s:min(s + 4096, L - 1)], s, table, decode=False)
+    dec = _run(runner, [prompt[L - 1]], L - 1, table, decode=True)
+    pre = _run(runner, prompt[L - 4096:], L - 4096, table, decode=False)  # recompute the last chunk
+    assert torch.isfinite(dec).all()
+    rel = ((dec - pre).norm() / pre.norm()).item()
+    assert rel < 2e-2, rel
+    assert int(dec.argmax()) == int(pre.argmax())
+
+
+def test_speculative_greedy_matches_plain_greedy():
+    """Draft + target (one batched verify forward per round): greedy output is token-for-token the
+    target's plain greedy output, whatever the draft; a draft identical to the target is always
+    accepted."""
+    from barq_inference_b200.engine.speculative import SpeculativeConfig, SpeculativeDecoder
+
+    cfg, tensors, prompt = _tiny()
+    ec = lambda: EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=128, cuda_graphs=False)  # noqa: E731
+    target = Engine(cfg, tensors, ec())
+    plain = target.generate([prompt[:24]], SamplingParams.greedy_params(max_tokens=20))[0].tokens
+    other = Engine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=7), ec())
+    out = SpeculativeDecoder(target, other, SpeculativeConfig(4)).generate(
+        prompt[:24], SamplingParams.greedy_params(max_tokens=20))
+    assert out.tokens == plain
+    same = SpeculativeDecoder(target, Engine(cfg, tensors, ec()), SpeculativeConfig(4, adaptive=False)).generate(
+        prompt[:24], SamplingParams.greedy_params(max_tokens=20))
+    assert same.tokens == plain and same.acceptance_rate > 0.99
+    sampled = SpeculativeDecoder(target, other, SpeculativeConfig(3)).generate(
+        prompt[:24], SamplingParams(temperature=0.8, top_k=40, max_tokens=16, seed=5, ignore_eos=True))
+    assert len(sampled.tokens) == 16 and all(0 <= t < cfg.vocab for t in sampled.tokens)
