@@ -77,7 +77,7 @@ class GenerationResult:
 
 
 class _GraphBucket:
-    __slots__ = ("B", "graph", "out_ids")
+    __slots__ = ("B", "graph", "out_ids", "packed")
 
 
 class Engine:
@@ -106,7 +106,6 @@ class Engine:
         self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
                                                ec.chunked_prefill), self.blocks, self.prefix_cache)
         self.graphs: dict[int, _GraphBucket] = {}
-        self._static = None
         self.metrics = None
         self.step_count = 0
         self.timings = {"prefill_s": 0.0, "decode_s": 0.0, "prefill_tokens": 0, "decode_tokens": 0}
@@ -393,65 +392,73 @@ class Engine:
         return out
 
     # ------------------------------------------------------------------ CUDA graphs
-    def _static_buffers(self):
-        if self._static is None:
-            Bm = max(self.ecfg.graph_buckets)
-            d = self.device
-            self._static = {
-                "ids": torch.zeros(Bm, dtype=torch.int32, device=d),
-                "pos": torch.zeros(Bm, dtype=torch.int32, device=d),
-                "slots": torch.zeros(Bm, dtype=torch.int64, device=d),
-                "lens": torch.ones(Bm, dtype=torch.int32, device=d),
-                "bt": torch.zeros(Bm, self.max_blocks_per_seq, dtype=torch.int32, device=d),
-                "last": torch.arange(Bm, dtype=torch.int64, device=d),
-                "temp": torch.zeros(Bm, dtype=torch.float32, device=d),
-                "topk": torch.zeros(Bm, dtype=torch.int32, device=d),
-                "topp": torch.ones(Bm, dtype=torch.float32, device=d),
-                "minp": torch.zeros(Bm, dtype=torch.float32, device=d),
-                "seeds": torch.zeros(Bm, dtype=torch.int64, device=d),
-                "steps": torch.zeros(Bm, dtype=torch.int32, device=d),
-                # one pinned host staging row holding every per-step input, copied with one H2D
-                "host": torch.zeros(0),
-            }
-        return self._static
-
-    def _graph_forward(self, B: int):
-        st = self._static
-        inp = StepInput(st["ids"][:B], st["pos"][:B], st["slots"][:B], st["bt"][:B], st["lens"][:B],
-                        st["last"][:B], True)
+    def _graph_forward(self, pk: "_Packed"):
+        d = pk.d
+        inp = StepInput(d["ids"], d["pos"], d["slots"], d["bt"], d["lens"], pk.last, True)
         logits = self.runner.forward(inp)
-        ids, _ = ops.sample(logits, st["temp"][:B], st["topk"][:B], st["topp"][:B], st["minp"][:B],
-                            st["seeds"][:B], st["steps"][:B])
+        ids, _ = ops.sample(logits, d["temp"], d["topk"], d["topp"], d["minp"], d["seeds"], d["steps"])
         return ids
 
     def _capture(self, B: int) -> _GraphBucket:
-        self._static_buffers()
+        pk = _Packed(B, self.max_blocks_per_seq, self.device)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):  # warm up allocations and lazily-set kernel attributes
-                self._graph_forward(B)
+                self._graph_forward(pk)
         torch.cuda.current_stream(self.device).wait_stream(s)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=getattr(self, "_graph_pool", None)):
-            out = self._graph_forward(B)
+            out = self._graph_forward(pk)
         self._graph_pool = g.pool()
         gb = _GraphBucket()
-        gb.B, gb.graph, gb.out_ids = B, g, out
+        gb.B, gb.graph, gb.out_ids, gb.packed = B, g, out, pk
         return gb
 
     def _decode_graph(self, seqs: list[Sequence], B: int) -> list[int]:
         gb = self.graphs.get(B)
         if gb is None:
             gb = self.graphs[B] = self._capture(B)
-        st = self._static
+        pk = gb.packed
         ids, pos, slots, lens, bt, n = self._decode_arrays(seqs, B)
         temp, topk, topp, minp, seeds, steps = self._sampling_tensors(seqs, B)
+        h = pk.h
         for k, a in (("ids", ids), ("pos", pos), ("slots", slots), ("lens", lens), ("bt", bt), ("temp", temp),
                      ("topk", topk), ("topp", topp), ("minp", minp), ("seeds", seeds), ("steps", steps)):
-            st[k][:B].copy_(self._stage(k, a), non_blocking=True)
+            h[k][...] = a
+        pk.upload()  # every per-step input in one host->device copy
         gb.graph.replay()
         return gb.out_ids[:n].cpu().tolist()
+
+
+class _Packed:
+    """Per-step inputs of a B-row decode graph packed into ONE device buffer (and one pinned host
+    mirror), so a step uploads everything with a single copy.  Each field is a contiguous typed
+    view at a 16-byte aligned offset."""
+
+    FIELDS = (("ids", torch.int32, 0), ("pos", torch.int32, 0), ("lens", torch.int32, 0),
+              ("topk", torch.int32, 0), ("steps", torch.int32, 0), ("temp", torch.float32, 0),
+              ("topp", torch.float32, 0), ("minp", torch.float32, 0), ("slots", torch.int64, 0),
+              ("seeds", torch.int64, 0), ("bt", torch.int32, 1))
+
+    def __init__(self, B: int, max_blocks: int, device):
+        lay, off = {}, 0
+        for k, dt, is_bt in self.FIELDS:
+            n = B * (max_blocks if is_bt else 1) * torch.tensor([], dtype=dt).element_size()
+            lay[k] = (off, n, dt, (B, max_blocks) if is_bt else (B,))
+            off += (n + 15) // 16 * 16
+        self.nbytes = off
+        self.dev = torch.zeros(off, dtype=torch.uint8, device=device)
+        self.host = torch.zeros(off, dtype=torch.uint8, pin_memory=torch.device(device).type == "cuda")
+        self.d = {k: self.dev[o:o + n].view(dt).view(shape) for k, (o, n, dt, shape) in lay.items()}
+        self.h = {k: self.host[o:o + n].view(dt).view(shape).numpy() for k, (o, n, dt, shape) in lay.items()}
+        self.h["lens"][...] = 1
+        self.h["topp"][...] = 1.0
+        self.upload()
+        self.last = torch.arange(B, dtype=torch.int64, device=device)
+
+    def upload(self) -> None:
+        self.dev.copy_(self.host, non_blocking=True)
 
 
 def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):

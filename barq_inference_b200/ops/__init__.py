@@ -244,10 +244,27 @@ def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale
                               device=q.device)
     out = torch.empty(B, H * D, dtype=act_dtype, device=q.device)
     oq = Q8Act.empty(B, H * D, q.device, x2) if want_q8 else None
+    cnt = _attn_counters(q.device, B * Hkv)
     C.decode_attention(q, kcache, vcache, block_tables, seq_lens, B, H, Hkv, D, scale, window, splits, scratch,
-                       out, *_outs(oq))
-    _count(2)
+                       out, *_outs(oq), cnt)
+    _count(1 if cnt is not None else 2)
     return out, oq
+
+
+# Split-merge arrival counters of decode attention, one zeroed int per (sequence, KV head), per
+# device; the kernel resets what it used.  Allocated on first use, before any CUDA-graph capture.
+_ATTN_CNT: dict = {}
+ATTN_FUSED_MERGE = os.environ.get("BARQ_ATTN_MERGE_KERNEL", "0") == "0"
+
+
+def _attn_counters(device, n: int):
+    if not ATTN_FUSED_MERGE:
+        return None
+    c = _ATTN_CNT.get(device)
+    if c is None or c.numel() < n:
+        c = torch.zeros(max(n, 4096), dtype=torch.int32, device=device)
+        _ATTN_CNT[device] = c
+    return c
 
 
 def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0,

@@ -192,6 +192,18 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     bs1_ms = max_over_ranks(e0.elapsed_time(e1) / max(1, n1))
+    bs1_replay_ms = None
+    if 1 in eng.graphs:  # device time of the batch-1 step alone (back-to-back graph replays)
+        g1 = eng.graphs[1].graph
+        g1.replay()
+        barrier()
+        r0, r1 = ev(), ev()
+        r0.record()
+        for _ in range(10):
+            g1.replay()
+        r1.record()
+        torch.cuda.synchronize()
+        bs1_replay_ms = max_over_ranks(r0.elapsed_time(r1) / 10)
     while eng.has_work():
         eng.step()
 
@@ -260,8 +272,10 @@ def main():
     t_e2e = time.perf_counter() - t0
     e2e_dec = eng.timings["decode_tokens"] / max(1e-9, eng.timings["decode_s"])
     e2e_dec = max_over_ranks(-e2e_dec) * -1 if world > 1 else e2e_dec  # slowest rank
-    mb = eng.max_blocks_per_seq
-    h2d = B * (4 + 4 + 8 + 4 + 4 * mb + 4 + 4 + 4 + 4 + 8 + 4)
+    # per decode step: ONE host->device copy of the packed inputs of the graph bucket, one read of
+    # the sampled ids
+    gbB = eng.graphs.get(next((b for b in eng.ecfg.graph_buckets if b >= B), B))
+    h2d = gbB.packed.nbytes if gbB is not None else B * (40 + 4 * eng.max_blocks_per_seq)
     d2h = B * 4
 
     if rank == 0:
@@ -289,6 +303,7 @@ def main():
                 "ttft_p50_ms_512": round(statistics.median(ttfts), 3) if ttfts else None,
                 "init_s": round(init_s, 1),
                 "decode_graph_replay_ms": round(replay_ms, 4) if replay_ms is not None else None,
+                "bs1_graph_replay_ms": round(bs1_replay_ms, 4) if bs1_replay_ms is not None else None,
             },
             "e2e": {"value": round(mult * e2e_dec, 2), "unit": "tokens/s decode via Engine.generate()",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

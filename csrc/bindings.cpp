@@ -298,9 +298,11 @@ void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor co
 
 void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor seq_lens, int64_t B,
                       int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window, int64_t splits, Tensor scratch,
-                      Tensor out, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl) {
+                      Tensor out, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl, OptT counters) {
   c10::cuda::CUDAGuard g(q.device());
   TORCH_CHECK(scratch.scalar_type() == torch::kFloat32, "scratch must be f32");
+  TORCH_CHECK(!counters || (counters->scalar_type() == torch::kInt32 && counters->numel() >= B * Hkv),
+              "decode_attention: counters must be int32 [>= B * Hkv] (zero)");
   size_t need = barq::decode_attention_scratch_floats((int)B, (int)H, (int)Hkv, (int)D, (int)splits);
   TORCH_CHECK((size_t)scratch.numel() >= need, "decode_attention: scratch too small (", scratch.numel(), " < ", need, ")");
   barq::DecodeAttnArgs a;
@@ -321,6 +323,7 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.out = out.data_ptr();
   a.out_f16 = out.scalar_type() == torch::kHalf;
   a.out_q = act_out(out_q, out_s, out_ql, out_dl);
+  a.counters = optptr<int>(counters);
   check(barq::decode_attention(a, cur_stream()), "decode_attention");
 }
 

@@ -10,8 +10,9 @@
 // which keeps both the page loads coalesced and the shared-memory q reads conflict-free); for PV
 // each lane owns D/32 output dims and receives the probabilities by shuffle.  Each warp keeps an
 // online-softmax state; the CTA merges its 4 warps and writes an unnormalized partial per split.
-// A second kernel merges the splits, normalizes, writes bf16 and the int8 q8 activation of the
-// output projection.
+// The splits are then merged (normalized, written as bf16/fp16 and as the int8 q8 activation of
+// the output projection) by the last split CTA of each (sequence, KV head) to arrive -- a counter
+// per (b, kv head) finds it, and it resets the counter -- or, without counters, by a second kernel.
 #include "common.cuh"
 #include "pdl.cuh"
 #include "launch.h"
@@ -203,6 +204,49 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
     a.part_acc[(pbase + g) * D + d] = A;
     if (d == 0) a.part_ml[pbase + g] = make_float2(M, L);
   }
+  if (!a.counters) return;
+  // ---- in-kernel merge by the last split CTA of this (b, kv head)
+  __shared__ int last_s;
+  __threadfence();  // this CTA's partial before its arrival
+  __syncthreads();
+  int* cnt = a.counters + (size_t)b * a.Hkv + kvh;
+  if (threadIdx.x == 0) last_s = atomicAdd(cnt, 1) == a.splits - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();  // every other split's partial (they fenced before arriving) before the reads
+  const size_t sbase = ((size_t)b * a.Hkv + kvh) * a.splits;
+  // per-split weights exp2(m_s - M) and 1 / L once per head, then one pass over the accumulators
+  __shared__ float2 ml_x[G][64];
+  __shared__ float fw_s[G][64], inv_s[G];
+  for (int i = threadIdx.x; i < G * a.splits; i += blockDim.x) {
+    const int g = i / a.splits, sp = i - g * a.splits;
+    ml_x[g][sp] = __ldcg(&a.part_ml[(sbase + sp) * G + g]);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -1e30f, L = 0.f;
+    for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, ml_x[g][sp].x);
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float f = exp2f(ml_x[g][sp].x - M);
+      fw_s[g][sp] = f;
+      L += ml_x[g][sp].y * f;
+    }
+    inv_s[g] = L > 0.f ? 1.f / L : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {  // warp-uniform: G * D is a multiple of 32
+    const int g = i / D, d = i % D;
+    const float* pa = a.part_acc + (sbase * G + g) * D + d;
+    float A = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < a.splits; ++sp) A += __ldcg(pa + (size_t)sp * G * D) * fw_s[g][sp];
+    const float o = A * inv_s[g];
+    const size_t oi = (size_t)b * a.H * D + (size_t)(kvh * G + g) * D + d;
+    store_act(a.out, oi, o, a.out_f16);
+    if (a.out_q.q) act_store32(a.out_q, o, oi, oi / 32, d & 31);
+  }
+  if (threadIdx.x == 0) *cnt = 0;  // ready for the next call / graph replay
 }
 
 // One CTA per (head, batch row); D threads.
@@ -256,7 +300,7 @@ static int launch_g(const DecodeAttnArgs& a, cudaStream_t st) {
     case 8: launch_pdl(decode_attn_kernel<TC, D, 8>, grid, dim3(128), 0, st, a); break;
     default: return -3;
   }
-  launch_pdl(decode_merge_kernel<D>, dim3(a.H, a.B), dim3(D), 0, st, a);
+  if (!a.counters) launch_pdl(decode_merge_kernel<D>, dim3(a.H, a.B), dim3(D), 0, st, a);
   return 0;
 }
 

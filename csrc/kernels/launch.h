@@ -192,6 +192,9 @@ struct DecodeAttnArgs {
   void* out;                // [B, H*D] activation dtype
   int out_f16;
   ActOut out_q;             // optional q8 of out (q == null: none)
+  // optional [B * Hkv] zeroed arrival counters: the last split CTA of a (b, kv head) merges the
+  // splits itself (no second launch); null = a separate merge kernel
+  int* counters = nullptr;
 };
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
 size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits);
