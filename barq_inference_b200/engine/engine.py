@@ -104,7 +104,9 @@ class Engine:
 
             self.prefix_cache = RadixPrefixCache(self.blocks)
         self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
-                                               ec.chunked_prefill), self.blocks, self.prefix_cache)
+                                               ec.chunked_prefill, sliding_window=cfg.sliding_window),
+                               self.blocks, self.prefix_cache)
+        self.sched.dummy_block = self.dummy_block
         self.graphs: dict[int, _GraphBucket] = {}
         self.metrics = None
         self.step_count = 0

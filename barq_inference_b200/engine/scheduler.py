@@ -25,6 +25,9 @@ class SchedulerConfig:
     max_num_batched_tokens: int = 8192
     max_model_len: int = 8192
     chunked_prefill: bool = True
+    # sliding-window attention: KV blocks that fall entirely out of every future query's window are
+    # returned to the pool as a sequence advances (0 = no window)
+    sliding_window: int = 0
 
     @staticmethod
     def low_latency() -> "SchedulerConfig":
@@ -50,6 +53,11 @@ class Scheduler:
         self.running: list[Sequence] = []
         self.prefix_cache = prefix_cache
         self.n_preemptions = 0
+        # block id written into the table entries of blocks freed by the sliding window (the
+        # attention kernels never read them, but every entry must name a valid block); None
+        # disables window trimming
+        self.dummy_block: int | None = None
+        self.n_window_freed = 0
 
     def add(self, seq: Sequence) -> None:
         if len(seq.prompt) == 0:
@@ -64,14 +72,30 @@ class Scheduler:
 
     def _free(self, seq: Sequence) -> None:
         if seq.block_table:
-            self.blocks.release(seq.block_table)
+            self.blocks.release([b for i, b in enumerate(seq.block_table) if i >= seq.window_freed])
         seq.block_table = []
         seq.n_cached = 0
+        seq.window_freed = 0
+
+    def _trim_window(self, seq: Sequence) -> None:
+        """Release the blocks no future query of ``seq`` can attend to: the next query position is
+        n_cached and attends to [n_cached - W + 1, n_cached], so blocks wholly below that are dead."""
+        W = self.cfg.sliding_window
+        if W <= 0 or self.dummy_block is None:
+            return
+        dead = min(max(0, seq.n_cached - W + 1) // self.blocks.block_size, len(seq.block_table))
+        if dead <= seq.window_freed:
+            return
+        freed = seq.block_table[seq.window_freed:dead]
+        self.blocks.release(freed)
+        seq.block_table[seq.window_freed:dead] = [self.dummy_block] * len(freed)
+        seq.window_freed = dead
+        self.n_window_freed += len(freed)
 
     def finish(self, seq: Sequence, reason: str) -> None:
         seq.status = SeqStatus.FINISHED
         seq.finish_reason = reason
-        if self.prefix_cache is not None and seq.embeds is None:
+        if self.prefix_cache is not None and seq.embeds is None and not seq.window_freed:
             self.prefix_cache.insert(seq.tokens[: seq.n_cached], seq.block_table)
         self._free(seq)
         if seq in self.running:
@@ -92,6 +116,9 @@ class Scheduler:
 
     def schedule(self) -> ScheduledStep | None:
         cfg = self.cfg
+        if cfg.sliding_window > 0:
+            for s in self.running:
+                self._trim_window(s)
         # 1) continue chunked prefills of running sequences first
         pre = [s for s in self.running if s.n_uncached > 1]
         budget = cfg.max_num_batched_tokens

@@ -45,6 +45,7 @@ class Sequence:
     # (first position, f32 [n, hidden] device tensor): prompt positions whose input embedding is
     # given instead of the token's (multimodal prompts); such prompts bypass the prefix cache
     embeds: Any = None
+    window_freed: int = 0  # leading block-table entries released by the sliding window
 
     @property
     def tokens(self) -> list[int]:

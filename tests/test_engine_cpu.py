@@ -79,3 +79,32 @@ def test_reference_tiny_deterministic():
         m.forward([tok], cache)
     inc = m.forward([a[2]], cache)[-1]
     assert torch.allclose(full, inc, atol=1e-4)
+
+
+def test_scheduler_sliding_window_frees_dead_blocks():
+    """With a 32-token window, blocks wholly behind every future query's window go back to the pool
+    (their table entries name the dummy block); a long generation keeps a bounded block count."""
+    bm = BlockManager(64)
+    dummy = bm.allocate(1)[0]
+    s = Scheduler(SchedulerConfig(max_num_seqs=2, max_num_batched_tokens=48, max_model_len=4096, sliding_window=32), bm)
+    s.dummy_block = dummy
+    q = Sequence(list(range(100)), SamplingParams())
+    s.add(q)
+    peak = 0
+    for step in range(300):
+        st = s.schedule()
+        assert st is not None
+        for x, n in zip(st.seqs, st.n_new):
+            x.n_cached += n
+            if x.n_cached >= x.n_tokens:
+                x.output.append(7)
+        peak = max(peak, bm.n_used)
+        live = [b for b in q.block_table[q.window_freed:]]
+        assert dummy not in live and all(b == dummy for b in q.block_table[:q.window_freed])
+        # every position a future query can attend to is still backed by a live block
+        first_needed = max(0, q.n_cached - 32 + 1)
+        assert q.window_freed <= first_needed // 16
+    assert q.n_tokens > 350 and s.n_window_freed >= 18
+    assert peak <= 1 + (48 + 32) // 16 + 2, peak  # dummy + window + one prefill chunk, not the sequence
+    s.finish(q, "length")
+    assert bm.n_used == 1  # only the dummy block: no double free, nothing leaked

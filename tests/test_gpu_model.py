@@ -225,3 +225,23 @@ def test_speculative_greedy_matches_plain_greedy():
     sampled = SpeculativeDecoder(target, other, SpeculativeConfig(3)).generate(
         prompt[:24], SamplingParams(temperature=0.8, top_k=40, max_tokens=16, seed=5, ignore_eos=True))
     assert len(sampled.tokens) == 16 and all(0 <= t < cfg.vocab for t in sampled.tokens)
+
+
+def test_sliding_window_engine_frees_blocks():
+    """A 40-token sliding window: the engine returns dead blocks to the pool while generating, and
+    its greedy tokens are identical to the same engine keeping every block (freed blocks are never
+    read), with and without CUDA graphs."""
+    import dataclasses
+
+    cfg0, tensors, prompt = _tiny()
+    cfg = dataclasses.replace(cfg0, sliding_window=40)
+    outs = []
+    for graphs in (False, True):
+        for trim in (True, False):
+            eng = Engine(cfg, tensors, EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=64,
+                                                    max_num_batched_tokens=32, cuda_graphs=graphs))
+            if not trim:
+                eng.sched.dummy_block = None  # window trimming off
+            outs.append(eng.generate([prompt], SamplingParams.greedy_params(max_tokens=48))[0].tokens)
+            assert (eng.sched.n_window_freed >= 3) if trim else eng.sched.n_window_freed == 0
+    assert outs[0] == outs[1] == outs[2] == outs[3]
