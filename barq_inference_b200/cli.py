@@ -325,13 +325,35 @@ def cmd_make_random(args) -> int:
     return 0
 
 
+def _dp_front(args):
+    """``--dp N``: N engine replicas (one process per GPU) behind the least-outstanding-work router.
+    Returns (front, tokenizer, chat_template)."""
+    from .parallel.dp import DataParallelEngine, GGUFEngineFactory, default_devices
+
+    if int(getattr(args, "tp", 1) or 1) > 1 or int(getattr(args, "pp", 1) or 1) > 1:
+        raise SystemExit("--dp with --tp/--pp: replicas are single-GPU engines here; pick one")
+    _, tok, tmpl, md = load(args, need_engine=False)
+    from .models.config import config_from_gguf
+
+    cfg = config_from_gguf(md, set())
+    a = {k: v for k, v in vars(args).items() if k != "fn"}
+    devices = ["cpu"] * args.dp if getattr(args, "device", None) == "cpu" else default_devices(args.dp)
+    front = DataParallelEngine(GGUFEngineFactory(a), devices, cfg=cfg, tokenizer=tok)
+    log.info("data parallel: %d replicas on %s", front.n_alive, ", ".join(devices))
+    return front, tok, tmpl
+
+
 def cmd_server(args) -> int:
     from .server.async_engine import AsyncEngine
     from .server.uds import UDSServer
 
-    eng, tok, _, _ = load(args)
     path = args.socket or f"/tmp/barq-inference-{args.port}.sock"
-    srv = UDSServer(AsyncEngine(eng), tok, path)
+    if int(getattr(args, "dp", 1) or 1) > 1:
+        front, tok, _ = _dp_front(args)
+        srv = UDSServer(front, tok, path)
+    else:
+        eng, tok, _, _ = load(args)
+        srv = UDSServer(AsyncEngine(eng), tok, path)
     print(f"barq UDS server listening on {path}")
     srv.start(background=False)
     return 0
@@ -340,9 +362,14 @@ def cmd_server(args) -> int:
 def cmd_http_server(args) -> int:
     from .server.openai_api import OpenAIServer, serve
 
-    eng, tok, tmpl, md = load(args)
-    srv = OpenAIServer(eng, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
-                       rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch)
+    if int(getattr(args, "dp", 1) or 1) > 1:
+        front, tok, tmpl = _dp_front(args)
+        srv = OpenAIServer(front, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
+                           rate_limit_rpm=args.rate_limit_rpm, arch=front.cfg.arch, aengine=front)
+    else:
+        eng, tok, tmpl, md = load(args)
+        srv = OpenAIServer(eng, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
+                           rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch)
     serve(srv, args.host, args.port)
     return 0
 
@@ -393,7 +420,8 @@ def build_parser() -> argparse.ArgumentParser:
                        help="expert-parallel ranks (experts are split over the --tp ranks; must equal --tp)")
         p.add_argument("--pp", type=int, default=1, help="pipeline stages (launch with torchrun; layers split contiguously)")
         p.add_argument("--dp", type=int, default=1,
-                       help="data-parallel replicas: launch one process per GPU, each with its own engine")
+                       help="data-parallel replicas for server/http-server: one engine process per GPU behind a "
+                            "least-outstanding-work request router")
         p.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                        help="TP all-reduce: fused one-shot kernel over NVLink peer memory, or NCCL")
         p.add_argument("--block-size", type=int, default=16, help="KV cache page size (tokens)")

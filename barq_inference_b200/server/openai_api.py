@@ -85,9 +85,11 @@ def _params(body: dict, max_key: str = "max_tokens") -> SamplingParams:
 
 class OpenAIServer:
     def __init__(self, engine, tokenizer, model_id: str = "barq", chat_template: ChatTemplate | None = None,
-                 rate_limit_rpm: int = 0, arch: str = "llama"):
+                 rate_limit_rpm: int = 0, arch: str = "llama", aengine=None):
         self.metrics = InferenceMetrics()
-        self.aengine = AsyncEngine(engine, self.metrics)
+        # ``aengine``: a ready front with the AsyncEngine caller API (e.g. the data-parallel replica
+        # router, whose ``engine`` argument is then itself)
+        self.aengine = aengine if aengine is not None else AsyncEngine(engine, self.metrics)
         self.engine = engine
         self.tok = tokenizer
         self.model_id = model_id
