@@ -114,6 +114,8 @@ class GGUFFile:
     def close(self) -> None:
         for t in self.tensors.values():
             t.data = None
+        if self._mm is not None and not hasattr(self._mm, "close"):  # native map: freed with its views
+            self._mm = None
         if self._mm is not None:
             try:
                 self._mm.close()
@@ -218,9 +220,54 @@ def _parse(buf, path: str) -> GGUFFile:
     return GGUFFile(path, version, md, mdt, infos, alignment, data_offset)
 
 
-def read_gguf(path: str | os.PathLike) -> GGUFFile:
-    """Memory-map ``path`` and parse its header; tensor data stays in the page cache."""
+def _native():
+    if os.environ.get("BARQ_GGUF_NATIVE", "1") == "0":
+        return None
+    try:
+        from .. import _native as nat
+
+        return nat
+    except ImportError:
+        return None
+
+
+def _from_native(head, path: str) -> GGUFFile:
+    version, md, mdt, tlist, alignment, data_offset, file_t = head
+    mdt = {k: GGUFValueType(v) for k, v in mdt.items()}
+    buf = file_t.numpy()  # zero-copy: the array keeps the mapping alive
+    buf.flags.writeable = False  # the pages are mapped read-only
+    infos: dict[str, TensorInfo] = {}
+    for name, shape, tt, off in tlist:
+        infos[name] = TensorInfo(name, tuple(shape), GGMLType(tt), off)
+    for t in infos.values():
+        if t.ggml_type not in TYPE_TRAITS:
+            raise GGUFError(f"tensor {t.name}: unsupported ggml type {t.ggml_type.name}")
+        start = data_offset + t.offset
+        if start + t.nbytes > buf.shape[0]:
+            raise GGUFError(f"tensor {t.name} extends past end of file")
+        t.data = buf[start: start + t.nbytes]
+    return GGUFFile(path, version, md, mdt, infos, int(alignment), int(data_offset), _mm=file_t)
+
+
+def read_gguf(path: str | os.PathLike, native: bool | None = None) -> GGUFFile:
+    """Memory-map ``path`` and parse its header; tensor data stays in the page cache.  The header is
+    parsed by the C++ parser (``_native.gguf_parse``) when it is built, else in Python;
+    ``native=False`` or ``BARQ_GGUF_NATIVE=0`` forces the Python parser."""
     path = os.fspath(path)
+    nat = _native() if native is not False else None
+    if native and nat is None:
+        raise ImportError("barq_inference_b200._native is not built (python setup.py build_ext --inplace)")
+    if nat is not None:
+        try:
+            head = nat.gguf_parse(path)
+        except ValueError as e:
+            raise GGUFError(f"{path}: {e}") from None
+        try:
+            return _from_native(head, path)
+        except ValueError as e:
+            if isinstance(e, GGUFError):
+                raise
+            raise GGUFError(f"{path}: {e}") from None
     with open(path, "rb") as f:
         size = os.fstat(f.fileno()).st_size
         if size < 24:

@@ -6,7 +6,7 @@ import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -28,6 +28,11 @@ ext_modules = [
         name="barq_inference_b200._cpu_ref",
         sources=sorted(glob.glob(os.path.join("csrc", "cpu_ref", "*.cpp"))),
         extra_compile_args={"cxx": CXX, "nvcc": NVCC},
+    ),
+    CppExtension(
+        name="barq_inference_b200._native",
+        sources=sorted(glob.glob(os.path.join("csrc", "native", "*.cpp"))),
+        extra_compile_args={"cxx": CXX},
     ),
 ]
 
