@@ -405,6 +405,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--cuda-graphs", dest="cuda_graphs", action="store_true", default=None)
     ap.add_argument("--no-cuda-graphs", dest="cuda_graphs", action="store_false")
     ap.add_argument("--flash-attn", action="store_true", help="always on (paged flash attention kernels)")
+    ap.add_argument("--log-format", choices=["text", "json"], default="text",
+                    help="json: one structured object per line with request ids (production logging)")
+    ap.add_argument("--log-file", default=None)
     ap.add_argument("--preset", choices=["max-speed", "balanced", "max-quality", "cpu", "gpu"])
     sub = ap.add_subparsers(dest="cmd", required=True)
 
@@ -515,6 +518,11 @@ def build_parser() -> argparse.ArgumentParser:
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     logging.basicConfig(level=logging.DEBUG if args.verbose else logging.INFO, format="%(message)s")
+    if args.log_format == "json" or args.log_file:
+        from .utils.logging import LoggingConfig, init_logger
+
+        init_logger(LoggingConfig(min_level=logging.DEBUG if args.verbose else logging.INFO,
+                                  json_format=args.log_format == "json", log_file=args.log_file))
     try:
         import torch
 

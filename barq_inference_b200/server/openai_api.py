@@ -14,6 +14,7 @@ from __future__ import annotations
 import json
 import threading
 import time
+import uuid
 from typing import Any
 
 from fastapi import FastAPI, Request
@@ -21,6 +22,7 @@ from fastapi.responses import JSONResponse, PlainTextResponse, Response, Streami
 
 from ..engine.sampling_params import SamplingParams
 from ..tokenizer import ChatTemplate, StreamDecoder
+from ..utils.logging import request_logger
 from .async_engine import AsyncEngine
 from .metrics import InferenceMetrics, context_health
 
@@ -271,6 +273,18 @@ class OpenAIServer:
             return PlainTextResponse(srv.metrics.prometheus(srv.engine), media_type="text/plain; version=0.0.4")
 
         async def handle(request: Request, kind: str):
+            rid = request.headers.get("x-request-id") or uuid.uuid4().hex[:16]
+            rlog = request_logger(rid)
+            t0 = time.perf_counter()
+            resp = await _handle(request, kind)
+            ctx = {"endpoint": request.url.path, "status": resp.status_code,
+                   "latency_ms": round((time.perf_counter() - t0) * 1000, 3),
+                   "stream": isinstance(resp, StreamingResponse)}
+            rlog.info("request %s", "accepted" if ctx["stream"] else "completed", extra={"context": ctx})
+            resp.headers["x-request-id"] = rid
+            return resp
+
+        async def _handle(request: Request, kind: str):
             lim = srv._limit(request)
             if lim is not None:
                 return lim
