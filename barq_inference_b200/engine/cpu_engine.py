@@ -33,6 +33,8 @@ class CPUEngine:
         self.tokenizer = None
         self.step_count = 0
         self.timings = {"prefill_s": 0.0, "decode_s": 0.0, "prefill_tokens": 0, "decode_tokens": 0}
+        # imported KV sessions (engine.session.import_session): (tokens, reference-forward cache)
+        self.sessions: list[tuple[list[int], dict]] = []
 
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, request_id: str = "",
                     on_token=None, embeds: tuple[int, torch.Tensor] | None = None) -> Sequence:
@@ -83,10 +85,11 @@ class CPUEngine:
             t0 = time.perf_counter()
             cache = self.caches[s.seq_id]
             if getattr(s, "pending_prefill", False):
-                logits = self.model.forward(s.tokens, cache, embeds=s.embeds)[-1]
+                start = self._resume(s, cache)
+                logits = self.model.forward(s.tokens[start:], cache, embeds=s.embeds)[-1]
                 s.pending_prefill = False
                 key = "prefill"
-                n = s.n_tokens
+                n = s.n_tokens - start
             else:
                 logits = self.model.forward([s.tokens[-1]], cache)[-1]
                 key = "decode"
@@ -125,6 +128,21 @@ class CPUEngine:
                     s.on_token(s, -1)
         self.step_count += 1
         return done
+
+    def _resume(self, s: Sequence, cache: dict) -> int:
+        """Seeds ``cache`` from the longest imported session that is a strict prefix of the prompt;
+        returns the number of positions that need no prefill."""
+        if s.embeds is not None or not self.sessions:
+            return 0
+        toks = s.tokens
+        best = None
+        for st, c in self.sessions:
+            if len(st) < len(toks) and toks[: len(st)] == st and (best is None or len(st) > len(best[0])):
+                best = (st, c)
+        if best is None:
+            return 0
+        cache.update(best[1])  # the forward concatenates new rows into fresh tensors
+        return len(best[0])
 
     def generate(self, prompts: list[list[int]], params=None) -> list[GenerationResult]:
         if params is None or isinstance(params, SamplingParams):
