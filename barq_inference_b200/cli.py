@@ -28,13 +28,13 @@ log = logging.getLogger("barq")
 def load(args, need_engine: bool = True):
     """Returns (engine, tokenizer, chat_template, metadata)."""
     from .gguf import read_gguf_split as read_gguf
-    from .models.config import config_from_gguf
+    from .models.config import attach_rope_factors, config_from_gguf
     from .models.weights import tensors_from_gguf
     from .tokenizer import ChatTemplate, GGUFTokenizer, synthetic_tokenizer
 
     g = read_gguf(args.model)
     md = g.metadata
-    cfg = config_from_gguf(md, set(g.tensors))
+    cfg = attach_rope_factors(config_from_gguf(md, set(g.tensors)), g)
     if getattr(args, "context_size", None):
         cfg.max_ctx = min(cfg.max_ctx, int(args.context_size)) if cfg.max_ctx else int(args.context_size)
     try:

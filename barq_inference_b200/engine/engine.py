@@ -116,11 +116,11 @@ class Engine:
     @staticmethod
     def from_gguf(path: str, engine_cfg: EngineConfig | None = None, device: str | None = None) -> "Engine":
         from ..gguf import read_gguf_split as read_gguf
-        from ..models.config import config_from_gguf
+        from ..models.config import attach_rope_factors, config_from_gguf
         from ..models.weights import tensors_from_gguf
 
         g = read_gguf(path)
-        cfg = config_from_gguf(g.metadata, set(g.tensors))
+        cfg = attach_rope_factors(config_from_gguf(g.metadata, set(g.tensors)), g)
         ec = engine_cfg or EngineConfig()
         if device:
             ec.device = device

@@ -50,6 +50,10 @@ class ModelConfig:
     yarn_beta_fast: float = 32.0
     yarn_beta_slow: float = 1.0
     yarn_log_mul: float = 0.0  # deepseek2 rope.scaling.yarn_log_multiplier
+    # per-dimension divisors of the RoPE inverse frequencies (rot_dim/2 values): the GGUF
+    # ``rope_freqs.weight`` tensor (Llama-3.1-style scaling) or LongRoPE's long/short factor list
+    rope_freq_factors: tuple = ()
+    rope_attn_factor: float = 0.0  # cos/sin magnitude (LongRoPE attention factor); 0 -> derived
     max_ctx: int = 4096
     sliding_window: int = 0
     qkv_bias: bool = False
@@ -162,6 +166,7 @@ def config_from_gguf(md: dict[str, Any], tensor_names: set[str] | None = None) -
         rope_factor=float(_g(md, arch, "rope.scaling.factor", 1.0) or 1.0),
         rope_orig_ctx=int(_g(md, arch, "rope.scaling.original_context_length", 0) or 0),
         yarn_log_mul=float(_g(md, arch, "rope.scaling.yarn_log_multiplier", 0.0) or 0.0),
+        rope_attn_factor=float(_g(md, arch, "rope.scaling.attn_factor", 0.0) or 0.0),
         max_ctx=int(_g(md, arch, "context_length", 4096)),
         sliding_window=int(_g(md, arch, "attention.sliding_window", 0) or 0),
         n_experts=int(_g(md, arch, "expert_count", 0) or 0),
@@ -240,3 +245,29 @@ def preset(name: str, **overrides) -> ModelConfig:
     if name not in PRESETS:
         raise KeyError(f"unknown preset {name!r}; known: {sorted(PRESETS)}")
     return replace(PRESETS[name], **overrides)
+
+
+def attach_rope_factors(cfg: ModelConfig, g) -> ModelConfig:
+    """Reads per-dimension RoPE frequency factors from a parsed GGUF file into ``cfg``:
+    ``rope_freqs.weight`` (Llama-3.1-style) or LongRoPE's ``rope_factors_long.weight`` /
+    ``rope_factors_short.weight`` (long factors when the context exceeds the original one)."""
+    import numpy as np
+
+    def vec(name):
+        t = g.tensors.get(name)
+        if t is None:
+            return None
+        return tuple(float(x) for x in np.frombuffer(bytes(t.data), dtype=np.float32))
+
+    ff = vec("rope_freqs.weight")
+    long_f, short_f = vec("rope_factors_long.weight"), vec("rope_factors_short.weight")
+    if long_f is not None or short_f is not None:
+        cfg.rope_scaling = "longrope"
+        orig = cfg.rope_orig_ctx or cfg.max_ctx
+        use_long = long_f is not None and (cfg.max_ctx > orig or short_f is None)
+        ff = long_f if use_long else short_f
+    if ff is not None:
+        if len(ff) != cfg.rot_dim // 2:
+            raise ValueError(f"RoPE factor tensor has {len(ff)} values, expected rot_dim/2 = {cfg.rot_dim // 2}")
+        cfg.rope_freq_factors = ff
+    return cfg

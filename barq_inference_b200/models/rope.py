@@ -6,6 +6,11 @@ These tables follow the published definitions instead:
 
 * linear: positions divided by ``factor``;
 * NTK-aware: ``base' = base * factor^(d/(d-2))``;
+* per-dimension frequency factors (GGUF ``rope_freqs.weight``, Llama-3.1 style): each inverse
+  frequency divided by its factor, in any mode;
+* LongRoPE (Ding et al. 2024, the Phi-3 scheme): long or short per-dimension factors as above, and
+  the attention factor ``sqrt(1 + ln(s) / ln(orig_ctx))`` (s = context / original context) or the
+  GGUF ``rope.scaling.attn_factor`` folded into cos/sin;
 * YaRN (Peng et al. 2023): per-dimension ramp between interpolated and extrapolated angles over the
   correction range given by ``beta_fast``/``beta_slow``, and the attention temperature
   ``mscale = 1 + 0.1 ln(factor)`` folded into cos/sin.
@@ -36,7 +41,17 @@ def rope_angles(cfg: ModelConfig, max_pos: int) -> tuple[torch.Tensor, float]:
     if cfg.rope_scaling == "ntk" and cfg.rope_factor > 1:
         base = base * cfg.rope_factor ** (d / (d - 2))
     inv = base ** (-2.0 * i / d)
+    if cfg.rope_freq_factors:
+        inv = inv / torch.tensor(cfg.rope_freq_factors, dtype=torch.float64)
     theta_ext = pos * inv
+    if cfg.rope_scaling == "longrope":
+        orig = cfg.rope_orig_ctx or cfg.max_ctx
+        s = cfg.max_ctx / orig
+        if cfg.rope_attn_factor > 0:
+            mscale = cfg.rope_attn_factor
+        elif s > 1:
+            mscale = math.sqrt(1.0 + math.log(s) / math.log(orig))
+        return theta_ext, mscale
     if cfg.rope_scaling == "linear" and cfg.rope_factor > 1:
         return theta_ext / cfg.rope_factor, mscale
     if cfg.rope_scaling == "yarn" and cfg.rope_factor > 1:
