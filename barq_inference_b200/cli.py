@@ -354,6 +354,14 @@ def cmd_server(args) -> int:
     else:
         eng, tok, _, _ = load(args)
         srv = UDSServer(AsyncEngine(eng), tok, path)
+    if getattr(args, "metrics_port", 0):
+        from .server.metrics import InferenceMetrics
+        from .server.metrics_server import MetricsServer, MetricsServerConfig
+
+        srv.metrics = InferenceMetrics()
+        ms = MetricsServer(srv.metrics, MetricsServerConfig(port=args.metrics_port),
+                           health_fn=lambda: (srv.ae.healthy, srv.ae.last_error)).start()
+        print(f"barq metrics on :{ms.port} (/metrics, /metrics.json, /health)")
     print(f"barq UDS server listening on {path}")
     srv.start(background=False)
     return 0
@@ -500,6 +508,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--host", default="127.0.0.1")
     p.add_argument("--port", type=int, default=8080)
     p.add_argument("--socket", default=None)
+    p.add_argument("--metrics-port", type=int, default=0, help="serve /metrics and /health on this port (e.g. 9090; 0: off)")
     p.set_defaults(fn=cmd_server)
 
     p = sub.add_parser("http-server", help="OpenAI-compatible HTTP server")

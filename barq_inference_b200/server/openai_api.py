@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import json
 import threading
+from collections import OrderedDict
 import time
 import uuid
 from typing import Any
@@ -98,6 +99,10 @@ class OpenAIServer:
         self.arch = arch
         self.template = chat_template or ChatTemplate("generic")
         self.limiter = RateLimiter(rate_limit_rpm) if rate_limit_rpm > 0 else None
+        self._tok_cache: OrderedDict[str, tuple[int, ...]] = OrderedDict()
+        self._tok_lock = threading.Lock()
+        self.tok_cache_size = 1024
+        self.tok_cache_hits = 0
         self.app = self._build()
 
     # ------------------------------------------------------------------ helpers
@@ -220,9 +225,21 @@ class OpenAIServer:
                 guard.fail()
 
     def _encode(self, text: str) -> list[int]:
+        """Tokenize with an LRU of recent prompts (repeated system prompts / retries skip the
+        tokenizer; the role of the reference's prompt-processing cache, ``barq_core`` context)."""
+        with self._tok_lock:
+            hit = self._tok_cache.get(text)
+            if hit is not None:
+                self._tok_cache.move_to_end(text)
+                self.tok_cache_hits += 1
+                return list(hit)
         ids = self.tok.encode(text, add_special=True)
         if not ids:
             raise ValueError("empty prompt")
+        with self._tok_lock:
+            self._tok_cache[text] = tuple(ids)
+            if len(self._tok_cache) > self.tok_cache_size:
+                self._tok_cache.popitem(last=False)
         return ids
 
     def _chat_prompt(self, messages: Any) -> list[int]:

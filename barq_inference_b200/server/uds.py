@@ -54,8 +54,10 @@ def recv_frame(sock: socket.socket) -> dict | None:
 
 
 class UDSServer:
-    def __init__(self, aengine, tokenizer, socket_path: str = "/tmp/barq-inference.sock", queue_size: int = 100):
+    def __init__(self, aengine, tokenizer, socket_path: str = "/tmp/barq-inference.sock", queue_size: int = 100,
+                 metrics=None):
         self.ae = aengine
+        self.metrics = metrics  # InferenceMetrics: per-request counters / TTFT for the metrics server
         self.tok = tokenizer
         self.path = socket_path
         self.sem = threading.BoundedSemaphore(queue_size)
@@ -75,21 +77,33 @@ class UDSServer:
             return
         dec = StreamDecoder(self.tok)
         n, ttft = 0, None
+        guard = self.metrics.begin() if self.metrics is not None else None
         try:
             for item in self.ae.generate_blocking(ids, params, rid):
                 now = time.perf_counter()
                 if item.token is None:
+                    if guard is not None:
+                        guard.complete(len(ids), n)
+                        guard = None
                     send_frame(conn, {"id": rid, "text": dec.flush(), "tokens_generated": n,
                                       "ttft_ms": int(ttft or 0), "total_time_ms": int((now - t0) * 1e3), "done": True})
                     return
                 n += 1
                 if ttft is None:
                     ttft = (now - t0) * 1e3
+                    if guard is not None:
+                        guard.first_token()
                 send_frame(conn, {"id": rid, "text": dec.push(item.token), "tokens_generated": n,
                                   "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
         except ValueError as e:
+            if guard is not None:
+                guard.fail()
+                guard = None
             send_frame(conn, {"id": rid, "text": "", "tokens_generated": n, "ttft_ms": 0,
                               "total_time_ms": int((time.perf_counter() - t0) * 1e3), "done": True, "error": str(e)})
+        finally:
+            if guard is not None:  # client went away mid-stream
+                guard.fail()
 
     def start(self, background: bool = True):
         if os.path.exists(self.path):

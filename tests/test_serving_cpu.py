@@ -256,3 +256,55 @@ def test_cli_make_info_run_convert(tmp_path):
     assert r.returncode == 0, r.stderr
     assert json.loads(_cli("info", "-m", out).stdout)["tensor_types"].get("Q8_0", 0) > 0
     assert json.loads(_cli("metal-info").stdout)["metal"] == "unavailable"
+
+
+def test_metrics_server_with_uds(tiny_engine, tmp_path):
+    """Standalone metrics endpoint next to the UDS server: Prometheus text, JSON snapshot, health."""
+    import json as _json
+    import urllib.error
+    import urllib.request
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.metrics import InferenceMetrics
+    from barq_inference_b200.server.metrics_server import MetricsServer, MetricsServerConfig
+    from barq_inference_b200.server.uds import UDSClient, UDSServer
+
+    m = InferenceMetrics()
+    ae = AsyncEngine(tiny_engine)
+    srv = UDSServer(ae, tiny_engine.tokenizer, str(tmp_path / "m.sock"), metrics=m).start()
+    ms = MetricsServer(m, MetricsServerConfig(host="127.0.0.1", port=0), engine=tiny_engine,
+                       health_fn=lambda: (ae.healthy, ae.last_error)).start()
+    try:
+        cl = UDSClient(str(tmp_path / "m.sock"))
+        frames = list(cl.stream("hello", max_tokens=3, temperature=0.0, rid="a"))
+        cl.close()
+        base = f"http://127.0.0.1:{ms.port}"
+        text = urllib.request.urlopen(base + "/metrics").read().decode()
+        assert "barq_requests_total 1" in text and "barq_requests_successful 1" in text
+        snap = _json.loads(urllib.request.urlopen(base + "/metrics.json").read())
+        assert snap["tokens_generated"] == frames[-1]["tokens_generated"] and snap["requests_active"] == 0
+        h = _json.loads(urllib.request.urlopen(base + "/health").read())
+        assert h["status"] == "healthy" and h["metrics"]["requests_successful"] == 1
+        with pytest.raises(urllib.error.HTTPError) as e:
+            urllib.request.urlopen(base + "/nope")
+        assert e.value.code == 404
+    finally:
+        ms.stop()
+        srv.stop()
+        ae.shutdown()
+
+
+def test_prompt_tokenization_lru(tiny_engine):
+    from barq_inference_b200.server.openai_api import OpenAIServer
+
+    srv = OpenAIServer(tiny_engine, tiny_engine.tokenizer)
+    try:
+        srv.tok_cache_size = 2
+        a = srv._encode("alpha beta")
+        assert srv._encode("alpha beta") == a and srv.tok_cache_hits == 1
+        srv._encode("gamma")
+        srv._encode("delta")  # evicts "alpha beta" (least recently used)
+        srv._encode("alpha beta")
+        assert srv.tok_cache_hits == 1 and len(srv._tok_cache) == 2
+    finally:
+        srv.aengine.shutdown()
