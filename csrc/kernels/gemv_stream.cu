@@ -335,10 +335,15 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
             // receive buffer, then add the world's sum into the residual stream
             const uint64_t* own = ar.dst[ar.rank];
             for (int b = 0; b < B; ++b) {
-              float sum = red[r][b];
+              // summed in rank order on every rank, so the replicated residual stays bit-identical
+              // across ranks for any world size (own-value-first order differs per rank from 3 on)
+              float sum = 0.f;
               bool ok = true;
               for (int q = 0; q < ar.world && ok; ++q) {
-                if (q == ar.rank) continue;
+                if (q == ar.rank) {
+                  sum += red[r][b];
+                  continue;
+                }
                 uint64_t pk = 0;
                 ok = wait_pair_sys(own + ((size_t)q * B + b) * w.N + row, ar_ep, ar.wait_ns, ws.err,
                                    pk);
