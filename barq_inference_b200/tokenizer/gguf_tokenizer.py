@@ -15,6 +15,7 @@ Special / control tokens written literally in the text are split out first and m
 from __future__ import annotations
 
 import heapq
+import os
 from dataclasses import dataclass, field
 from functools import lru_cache
 
@@ -78,6 +79,7 @@ class GGUFTokenizer:
                     self.byte_tokens[int(t[3:5], 16)] = i
                 except ValueError:
                     pass
+        self._native = _make_native(self)
         if self.model == "gpt2":
             self.ranks = {}
             for r, m in enumerate(self.merges):
@@ -137,6 +139,14 @@ class GGUFTokenizer:
         if self.add_space_prefix and first and not text.startswith(" "):
             text = " " + text
         text = text.replace(" ", SPIECE)
+        if self._native is not None:
+            try:
+                return self._native.spm(text)
+            except UnicodeEncodeError:  # lone surrogates: not UTF-8 encodable, use the Python path
+                pass
+        return self._spm_py(text)
+
+    def _spm_py(self, text: str) -> list[int]:
         syms = list(text)
         if not syms:
             return []
@@ -197,6 +207,12 @@ class GGUFTokenizer:
         return parts
 
     def _encode_bpe(self, text: str) -> list[int]:
+        if self._native is not None:
+            words = ["".join(self.b2u[b] for b in m.encode("utf-8")) for m in self.pre_re.findall(text)]
+            return self._native.bpe(words)
+        return self._bpe_py(text)
+
+    def _bpe_py(self, text: str) -> list[int]:
         out = []
         for m in self.pre_re.findall(text):
             word = "".join(self.b2u[b] for b in m.encode("utf-8"))
@@ -259,6 +275,25 @@ class StreamDecoder:
         s = self.pending.decode("utf-8", errors="replace")
         self.pending = b""
         return s
+
+
+def _make_native(tok: "GGUFTokenizer"):
+    """The C++ merge loops (``_native.NativeTokenizer``) for this vocabulary, or None when the
+    extension is not built or ``BARQ_NATIVE_TOKENIZER=0``."""
+    if os.environ.get("BARQ_NATIVE_TOKENIZER", "1") == "0":
+        return None
+    try:
+        import torch  # noqa: F401  (loads the libraries the extension links against)
+
+        from .. import _native
+    except ImportError:
+        return None
+    byte_ids = [tok.byte_tokens.get(b, -1) for b in range(256)]
+    try:
+        return _native.NativeTokenizer(list(tok.tokens), [float(x) for x in tok.scores], list(tok.merges) if tok.model == "gpt2" else [],
+                                       byte_ids, int(tok.vocab.get("<unk>", 0)))
+    except (UnicodeError, TypeError):
+        return None
 
 
 def synthetic_tokenizer(vocab: int, seed: int = 0) -> GGUFTokenizer:
