@@ -198,6 +198,36 @@ class _Parser:
                         seq.append(RuleRef(rid))
                     else:
                         seq.extend(last + [RuleRef(rid)])
+            elif self.i < len(self.s) and self.s[self.i] == "{":
+                # bounded repetition {m}, {m,}, {m,n}: m copies, then a star rule or n-m nested optionals
+                close = self.s.find("}", self.i)
+                if close < 0:
+                    raise GrammarError("unterminated repetition count")
+                body = self.s[self.i + 1: close].replace(" ", "")
+                self.i = close + 1
+                try:
+                    if "," in body:
+                        lo_s, hi_s = body.split(",", 1)
+                        lo, hi = int(lo_s), (int(hi_s) if hi_s else None)
+                    else:
+                        lo = hi = int(body)
+                except ValueError:
+                    raise GrammarError(f"bad repetition count {{{body}}}") from None
+                if lo < 0 or (hi is not None and hi < lo):
+                    raise GrammarError(f"bad repetition count {{{body}}}")
+                last = seq[start:]
+                del seq[start:]
+                for _ in range(lo):
+                    seq.extend(last)
+                if hi is None:
+                    rid = self.new_rule([])
+                    self.rules[rid] = [last + [RuleRef(rid)], []]
+                    seq.append(RuleRef(rid))
+                elif hi > lo:
+                    tail: list = []
+                    for _ in range(hi - lo):  # R ::= last R_prev | (empty)
+                        tail = [RuleRef(self.new_rule([last + tail, []]))]
+                    seq.extend(tail)
         return seq
 
 

@@ -236,10 +236,12 @@ py::tuple parse_bytes(py::bytes b) {
 }  // namespace
 
 void register_tokenizer(py::module_& m);  // tokenizer_native.cpp
+void register_grammar(py::module_& m);    // grammar_native.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.doc() = "barq native runtime pieces (GGUF parser, tokenizer merge loops)";
+  m.doc() = "barq native runtime pieces (GGUF parser, tokenizer merge loops, grammar recognizer)";
   register_tokenizer(m);
+  register_grammar(m);
   m.def("gguf_parse", &parse, "memory-map and parse a GGUF file");
   m.def("gguf_parse_bytes", &parse_bytes, "parse a GGUF header held in memory (no tensor data view)");
 }
