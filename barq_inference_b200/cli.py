@@ -82,7 +82,8 @@ def load(args, need_engine: bool = True):
                   kv_dtype=getattr(args, "kv_dtype", "fp16") or "fp16",
                   max_num_seqs=getattr(args, "max_batch", 64) or 64,
                   prefix_caching=bool(getattr(args, "prefix_cache", False)),
-                  kv_cache_gb=float(getattr(args, "kv_cache_gb", 8.0) or 8.0))
+                  kv_cache_gb=float(getattr(args, "kv_cache_gb", 8.0) or 8.0),
+                  max_waiting=int(getattr(args, "max_waiting", 0) or 0))
         if getattr(args, "cuda_graphs", None) is not None:
             kw["cuda_graphs"] = bool(args.cuda_graphs)
         ec = EngineConfig.preset(preset, **kw) if preset else EngineConfig(**kw)
@@ -438,6 +439,8 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("--block-size", type=int, default=16, help="KV cache page size (tokens)")
         p.add_argument("--no-fmoe", action="store_true", help="unfused per-expert MoE loop (baseline)")
         p.add_argument("--prefix-cache", action="store_true")
+        p.add_argument("--max-waiting", type=int, default=0,
+                       help="admission control: refuse requests (HTTP 503) beyond this many waiting (0: no limit)")
         p.add_argument("--mla", action="store_true", help="DeepSeek MLA latent cache (on for deepseek2 models)")
         p.add_argument("--fmoe", action="store_true", help="fused MoE routing/dispatch (default path)")
         p.add_argument("--ser", action="store_true", help="smart expert reduction: drop experts with gate < 0.2")

@@ -22,10 +22,12 @@ from .sequence import Sequence, SeqStatus
 
 
 class CPUEngine:
-    def __init__(self, cfg: ModelConfig, tensors, max_model_len: int = 2048, ser_threshold: float = 0.0):
+    def __init__(self, cfg: ModelConfig, tensors, max_model_len: int = 2048, ser_threshold: float = 0.0,
+                 max_waiting: int = 0):
         self.cfg = cfg
         self.model = ReferenceModel(cfg, tensors, ser_threshold=ser_threshold)
         self.max_model_len = min(max_model_len, cfg.max_ctx)
+        self.max_waiting = max_waiting  # admission control (0: no limit), as in the scheduler
         self.waiting: list[Sequence] = []
         self.running: list[Sequence] = []
         self.caches: dict[int, dict] = {}
@@ -45,6 +47,10 @@ class CPUEngine:
             raise ValueError("prompt token id out of range")
         if len(prompt) >= self.max_model_len:
             raise ValueError("prompt exceeds max_model_len")
+        if self.max_waiting and len(self.waiting) >= self.max_waiting:
+            from .scheduler import Overloaded
+
+            raise Overloaded(f"{len(self.waiting)} requests already waiting; retry later")
         seq = Sequence(list(prompt), params, request_id=request_id, on_token=on_token)
         if embeds is not None:
             st, e = embeds

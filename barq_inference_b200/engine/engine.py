@@ -51,6 +51,7 @@ class EngineConfig:
     pp: int = 1                     # pipeline stages (one process per GPU, contiguous layer ranges)
     rank_timeout_s: float = 30.0    # TP: a peer without a heartbeat for this long fails the step
     fused_comm: bool = True         # TP: fused one-shot all-reduce kernel (False: NCCL all-reduce)
+    max_waiting: int = 0            # admission control: refuse requests beyond this queue depth (0: off)
 
     @staticmethod
     def preset(name: str, **kw) -> "EngineConfig":
@@ -104,7 +105,8 @@ class Engine:
 
             self.prefix_cache = RadixPrefixCache(self.blocks)
         self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
-                                               ec.chunked_prefill, sliding_window=cfg.sliding_window),
+                                               ec.chunked_prefill, sliding_window=cfg.sliding_window,
+                                               max_waiting=ec.max_waiting),
                                self.blocks, self.prefix_cache)
         self.sched.dummy_block = self.dummy_block
         self.graphs: dict[int, _GraphBucket] = {}

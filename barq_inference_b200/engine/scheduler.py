@@ -19,6 +19,10 @@ from .kv_cache import BlockManager
 from .sequence import Sequence, SeqStatus
 
 
+class Overloaded(RuntimeError):
+    """Admission control refused a request (the waiting queue is full); servers answer 503."""
+
+
 @dataclass
 class SchedulerConfig:
     max_num_seqs: int = 64
@@ -28,6 +32,8 @@ class SchedulerConfig:
     # sliding-window attention: KV blocks that fall entirely out of every future query's window are
     # returned to the pool as a sequence advances (0 = no window)
     sliding_window: int = 0
+    # admission control: requests beyond this many waiting are refused with Overloaded (0 = no limit)
+    max_waiting: int = 0
 
     @staticmethod
     def low_latency() -> "SchedulerConfig":
@@ -64,6 +70,13 @@ class Scheduler:
             raise ValueError("empty prompt")
         if len(seq.prompt) >= self.cfg.max_model_len:
             raise ValueError(f"prompt of {len(seq.prompt)} tokens exceeds max_model_len {self.cfg.max_model_len}")
+        # a prompt whose KV pages exceed the whole pool would wait forever: refuse it up front
+        usable = self.blocks.num_blocks - (1 if self.dummy_block is not None else 0)
+        need = self.blocks.blocks_for(len(seq.prompt) + 1)
+        if need > usable:
+            raise ValueError(f"prompt of {len(seq.prompt)} tokens needs {need} KV pages; the pool has {usable}")
+        if self.cfg.max_waiting and len(self.waiting) >= self.cfg.max_waiting:
+            raise Overloaded(f"{len(self.waiting)} requests already waiting; retry later")
         self.waiting.append(seq)
 
     @property

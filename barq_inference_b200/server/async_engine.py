@@ -37,6 +37,14 @@ class Submission:
     accepted: threading.Event = field(default_factory=threading.Event)
 
 
+def _refusal(e: Exception) -> Exception:
+    """What the caller sees for a request the engine did not accept: admission-control refusals
+    keep their type (servers answer 503), anything else is a bad request (ValueError)."""
+    from ..engine.scheduler import Overloaded
+
+    return e if isinstance(e, Overloaded) else ValueError(str(e))
+
+
 class AsyncEngine:
     def __init__(self, engine, metrics=None, idle_sleep: float = 0.002):
         self.engine = engine
@@ -90,7 +98,7 @@ class AsyncEngine:
             seq = self.engine.add_request(sub.prompt, sub.params, sub.request_id, on_token=on_token)
             sub.seq = seq
         except Exception as e:
-            sub.error.append(str(e))
+            sub.error.append(e)
             self._deliver(sub, StreamItem(None, "error"))
         sub.accepted.set()
 
@@ -119,7 +127,7 @@ class AsyncEngine:
         while True:
             item = await sub.aqueue.get()
             if item.token is None and item.finish_reason == "error" and sub.error:
-                raise ValueError(sub.error[0])
+                raise _refusal(sub.error[0])
             yield item
             if item.token is None:
                 return
@@ -131,7 +139,7 @@ class AsyncEngine:
         while True:
             item = sub.sink.get(timeout=timeout)
             if item.token is None and item.finish_reason == "error" and sub.error:
-                raise ValueError(sub.error[0])
+                raise _refusal(sub.error[0])
             yield item
             if item.token is None:
                 return

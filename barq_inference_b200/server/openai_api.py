@@ -22,6 +22,7 @@ from fastapi import FastAPI, Request
 from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
 
 from ..engine.sampling_params import SamplingParams
+from ..engine.scheduler import Overloaded
 from ..tokenizer import ChatTemplate, StreamDecoder
 from ..utils.logging import request_logger
 from .async_engine import AsyncEngine
@@ -338,6 +339,8 @@ class OpenAIServer:
                 return JSONResponse(await srv._complete(ids, params, stops, kind, model))
             except ValueError as e:
                 return _err(400, str(e))
+            except Overloaded as e:  # admission control: queue full
+                return _err(503, str(e), "overloaded_error")
             except Exception as e:  # engine failure
                 return _err(500, f"{type(e).__name__}: {e}", "server_error")
 

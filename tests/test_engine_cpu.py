@@ -108,3 +108,42 @@ def test_scheduler_sliding_window_frees_dead_blocks():
     assert peak <= 1 + (48 + 32) // 16 + 2, peak  # dummy + window + one prefill chunk, not the sequence
     s.finish(q, "length")
     assert bm.n_used == 1  # only the dummy block: no double free, nothing leaked
+
+
+def test_scheduler_admission_control():
+    """Refused up front: a prompt larger than the whole KV pool (it could never be scheduled), and
+    requests beyond the waiting-queue limit (Overloaded, which servers turn into 503)."""
+    import pytest
+
+    from barq_inference_b200.engine.scheduler import Overloaded
+
+    bm = BlockManager(8)
+    s = Scheduler(SchedulerConfig(max_num_seqs=2, max_num_batched_tokens=64, max_model_len=4096, max_waiting=2), bm)
+    s.dummy_block = bm.allocate(1)[0]
+    with pytest.raises(ValueError, match="KV pages"):
+        s.add(Sequence(list(range(7 * 16)), SamplingParams()))  # needs 8 pages, 7 usable
+    s.add(Sequence([1, 2, 3], SamplingParams()))
+    s.add(Sequence([1, 2, 3], SamplingParams()))
+    with pytest.raises(Overloaded):
+        s.add(Sequence([1, 2, 3], SamplingParams()))
+    s.schedule()  # admits the waiting ones; the queue has room again
+    s.add(Sequence([4, 5], SamplingParams()))
+
+
+def test_http_503_when_overloaded():
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.engine.cpu_engine import CPUEngine
+    from barq_inference_b200.server.openai_api import OpenAIServer
+    from barq_inference_b200.tokenizer.gguf_tokenizer import synthetic_tokenizer
+
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
+    eng = CPUEngine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=0), max_model_len=256, max_waiting=1)
+    eng.waiting.append(Sequence([1, 2], SamplingParams()))  # a request already queued ...
+    eng.has_work = lambda: False  # ... that the engine thread leaves there
+    srv = OpenAIServer(eng, synthetic_tokenizer(cfg.vocab))
+    try:
+        r = TestClient(srv.app).post("/v1/completions", json={"prompt": "hi", "max_tokens": 2})
+        assert r.status_code == 503 and r.json()["error"]["type"] == "overloaded_error"
+    finally:
+        srv.aengine.shutdown()
