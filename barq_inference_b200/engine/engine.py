@@ -424,12 +424,7 @@ class Engine:
         if gb is None:
             gb = self.graphs[B] = self._capture(B)
         pk = gb.packed
-        ids, pos, slots, lens, bt, n = self._decode_arrays(seqs, B)
-        temp, topk, topp, minp, seeds, steps = self._sampling_tensors(seqs, B)
-        h = pk.h
-        for k, a in (("ids", ids), ("pos", pos), ("slots", slots), ("lens", lens), ("bt", bt), ("temp", temp),
-                     ("topk", topk), ("topp", topp), ("minp", minp), ("seeds", seeds), ("steps", steps)):
-            h[k][...] = a
+        n = pk.fill(seqs, self.ecfg.block_size, self.dummy_block)
         pk.upload()  # every per-step input in one host->device copy
         gb.graph.replay()
         return gb.out_ids[:n].cpu().tolist()
@@ -460,6 +455,54 @@ class _Packed:
         self.h["topp"][...] = 1.0
         self.upload()
         self.last = torch.arange(B, dtype=torch.int64, device=device)
+        self.B = B
+        # what each host row holds: (seq_id, bt_gen, block-table length) or None for a padding row
+        self.rows: list = [None] * B
+        self.n_prev = B  # rows [n, n_prev) are reset to padding on the next fill
+
+    def fill(self, seqs, block_size: int, dummy: int) -> int:
+        """Write a decode step's inputs into the pinned host mirror, touching only what changed: a
+        row that holds the same sequence as in this bucket's previous step gets its per-token
+        fields and the block-table entries appended since then; a new occupant gets its whole row;
+        rows no longer used become padding (dummy page, length 1).  Equal, byte for byte, to
+        rewriting every array each step."""
+        h, rows, n = self.h, self.rows, len(seqs)
+        lens = [s.n_tokens for s in seqs]
+        pos = [x - 1 for x in lens]
+        h["ids"][:n] = [s.last_token for s in seqs]
+        h["pos"][:n] = pos
+        h["lens"][:n] = lens
+        h["slots"][:n] = [s.block_table[p // block_size] * block_size + p % block_size for s, p in zip(seqs, pos)]
+        h["steps"][:n] = [len(s.output) for s in seqs]
+        bt = h["bt"]
+        for i, s in enumerate(seqs):
+            tbl = s.block_table
+            nb = len(tbl)
+            key = rows[i]
+            if key is not None and key[0] == s.seq_id and key[1] == s.bt_gen and key[2] <= nb:
+                if nb > key[2]:
+                    bt[i, key[2]:nb] = tbl[key[2]:]
+            else:
+                bt[i, :nb] = tbl
+                bt[i, nb:] = dummy
+                p = s.params
+                h["temp"][i] = p.temperature
+                h["topk"][i] = p.top_k
+                h["topp"][i] = p.top_p
+                h["minp"][i] = p.min_p
+                h["seeds"][i] = p.seed * 1000003 + s.seq_id if p.seed == 0 else p.seed
+            rows[i] = (s.seq_id, s.bt_gen, nb)
+        if self.n_prev > n:
+            lo, hi = n, self.n_prev
+            for k, v in (("ids", 0), ("pos", 0), ("lens", 1), ("topk", 0), ("steps", 0), ("temp", 0.0),
+                         ("topp", 1.0), ("minp", 0.0), ("seeds", 0)):
+                h[k][lo:hi] = v
+            h["slots"][lo:hi] = dummy * block_size
+            bt[lo:hi] = dummy
+            for i in range(lo, hi):
+                rows[i] = None
+        self.n_prev = n
+        return n
 
     def upload(self) -> None:
         self.dev.copy_(self.host, non_blocking=True)

@@ -87,6 +87,7 @@ class Scheduler:
         if seq.block_table:
             self.blocks.release([b for i, b in enumerate(seq.block_table) if i >= seq.window_freed])
         seq.block_table = []
+        seq.bt_gen += 1
         seq.n_cached = 0
         seq.window_freed = 0
 
@@ -102,6 +103,7 @@ class Scheduler:
         freed = seq.block_table[seq.window_freed:dead]
         self.blocks.release(freed)
         seq.block_table[seq.window_freed:dead] = [self.dummy_block] * len(freed)
+        seq.bt_gen += 1
         seq.window_freed = dead
         self.n_window_freed += len(freed)
 
@@ -153,6 +155,7 @@ class Scheduler:
                 if hit_blocks:
                     self.blocks.retain(hit_blocks)
                     s.block_table = list(hit_blocks)
+                    s.bt_gen += 1
                     s.n_cached = hit_tokens
                     s.prefix_hit = hit_tokens
             total = s.n_uncached

@@ -46,6 +46,9 @@ class Sequence:
     # given instead of the token's (multimodal prompts); such prompts bypass the prefix cache
     embeds: Any = None
     window_freed: int = 0  # leading block-table entries released by the sliding window
+    # bumped whenever block_table is replaced or rewritten (not when it only grows), so that packed
+    # decode inputs can re-send only the entries appended since the previous step
+    bt_gen: int = 0
 
     @property
     def tokens(self) -> list[int]:

@@ -147,3 +147,59 @@ def test_http_503_when_overloaded():
         assert r.status_code == 503 and r.json()["error"]["type"] == "overloaded_error"
     finally:
         srv.aengine.shutdown()
+
+
+def test_incremental_decode_packing_equals_full_rewrite():
+    """The decode graph's packed host inputs, written incrementally (only appended block-table
+    entries for a row whose sequence is unchanged), are byte-identical to rewriting every array each
+    step — across joins, departures, preemption (table replaced), window trimming and growth."""
+    import random
+    import types
+
+    import numpy as np
+
+    from barq_inference_b200.engine.engine import Engine, _Packed
+
+    rng = random.Random(0)
+    B, mb, bs, dummy = 8, 32, 16, 0
+    eng = Engine.__new__(Engine)
+    eng.ecfg = types.SimpleNamespace(block_size=bs)
+    eng.dummy_block, eng.max_blocks_per_seq = dummy, mb
+    inc, ref = _Packed(B, mb, "cpu"), _Packed(B, mb, "cpu")
+    pool = []
+    nxt = iter(range(1, 10**6))
+
+    def new_seq():
+        s = Sequence([rng.randrange(100) for _ in range(rng.randint(1, 40))],
+                     SamplingParams(temperature=rng.choice([0.0, 0.7]), top_k=rng.choice([0, 40]), seed=rng.randint(0, 3)))
+        s.block_table = [next(nxt) for _ in range((s.n_tokens + bs - 1) // bs)]
+        return s
+
+    for step in range(400):
+        if len(pool) < B and rng.random() < 0.3:
+            pool.insert(rng.randrange(len(pool) + 1), new_seq())
+        if pool and rng.random() < 0.1:
+            pool.pop(rng.randrange(len(pool)))
+        for s in pool:
+            s.output.append(rng.randrange(100))
+            while len(s.block_table) * bs < s.n_tokens:
+                s.block_table.append(next(nxt))
+        if pool and rng.random() < 0.05:  # preempted and readmitted: a new table of the same length
+            s = rng.choice(pool)
+            s.block_table = [next(nxt) for _ in s.block_table]
+            s.bt_gen += 1
+        if pool and rng.random() < 0.05:  # sliding window: leading entries point at the dummy page
+            s = rng.choice(pool)
+            k = rng.randint(0, len(s.block_table) - 1)
+            s.block_table[:k] = [dummy] * k
+            s.bt_gen += 1
+        if not pool:
+            continue
+        n = inc.fill(pool, bs, dummy)
+        ids, pos, slots, lens, bt, _ = eng._decode_arrays(pool, B)
+        temp, topk, topp, minp, seeds, steps = eng._sampling_tensors(pool, B)
+        for k, a in (("ids", ids), ("pos", pos), ("slots", slots), ("lens", lens), ("bt", bt), ("temp", temp),
+                     ("topk", topk), ("topp", topp), ("minp", minp), ("seeds", seeds), ("steps", steps)):
+            ref.h[k][...] = a
+        assert n == len(pool)
+        assert np.array_equal(inc.host.numpy(), ref.host.numpy()), step
