@@ -135,7 +135,7 @@ class Scheduler:
             for s in self.running:
                 self._trim_window(s)
         # 1) continue chunked prefills of running sequences first
-        pre = [s for s in self.running if s.n_uncached > 1]
+        pre = [s for s in self.running if len(s.prompt) + len(s.output) - s.n_cached > 1]  # = n_uncached > 1
         budget = cfg.max_num_batched_tokens
         seqs, n_new = [], []
         for s in pre:
@@ -182,12 +182,16 @@ class Scheduler:
         if not self.running:
             return None
         dec = []
+        p0 = self.n_preemptions
+        cap = self.blocks.block_size
         for s in sorted(self.running, key=lambda s: s.arrival):
-            if s not in self.running:
-                continue  # preempted below
-            if self._reserve(s, s.n_tokens):
+            if self.n_preemptions != p0 and s.status is not SeqStatus.RUNNING:
+                continue  # preempted to make room for an older sequence
+            nt = len(s.prompt) + len(s.output)
+            if nt <= len(s.block_table) * cap or self._reserve(s, nt):  # fast path: the page has room
                 dec.append(s)
-        dec = [s for s in dec if s in self.running]
+        if self.n_preemptions != p0:
+            dec = [s for s in dec if s.status is SeqStatus.RUNNING]
         if not dec:
             return None
         return ScheduledStep("decode", dec, [1] * len(dec))
