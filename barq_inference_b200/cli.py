@@ -81,7 +81,7 @@ def load(args, need_engine: bool = True):
                   block_size=int(getattr(args, "block_size", 16) or 16),
                   kv_dtype=getattr(args, "kv_dtype", "fp16") or "fp16",
                   max_num_seqs=getattr(args, "max_batch", 64) or 64,
-                  prefix_caching=bool(getattr(args, "prefix_cache", False)),
+                  prefix_caching=bool(getattr(args, "prefix_cache", False) or getattr(args, "prompt_cache", None)),
                   kv_cache_gb=float(getattr(args, "kv_cache_gb", 8.0) or 8.0),
                   max_waiting=int(getattr(args, "max_waiting", 0) or 0))
         if getattr(args, "cuda_graphs", None) is not None:
@@ -135,6 +135,14 @@ def cmd_run(args) -> int:
         sys.stdout.write(tok.decode(out.tokens) + "\n")
         log.info("speculative: acceptance %.2f", out.acceptance_rate)
         return 0
+    pc = getattr(args, "prompt_cache", None)
+    if pc and os.path.exists(pc):
+        from .engine.session import import_session
+
+        try:
+            log.info("prompt cache %s: %d tokens reusable", pc, import_session(eng, pc))
+        except (ValueError, NotImplementedError) as e:
+            log.warning("prompt cache %s not used: %s", pc, e)
     dec = StreamDecoder(tok)
     t0 = time.perf_counter()
     first = [None]
@@ -160,6 +168,14 @@ def cmd_run(args) -> int:
     n = len(seq.output)
     log.info("%d prompt tokens, %d generated in %.2fs (%.1f tok/s, TTFT %.1f ms)", len(ids), n, dt, n / max(dt, 1e-9),
              ((first[0] or t0) - t0) * 1e3)
+    if pc:
+        from .engine.session import export_session
+
+        try:
+            export_session(eng, ids, pc)
+            log.info("prompt cache written to %s", pc)
+        except (ValueError, NotImplementedError) as e:
+            log.warning("prompt cache not written: %s", e)
     return 0
 
 
@@ -459,6 +475,8 @@ def build_parser() -> argparse.ArgumentParser:
     sampling_args(p)
     p.add_argument("-p", "--prompt", default="Hello")
     p.add_argument("--prompt-ids", default="", help="comma-separated token ids (bypasses the tokenizer)")
+    p.add_argument("--prompt-cache", default=None,
+                   help="KV session file: reused when present (prompt prefix skips prefill), written after the run")
     p.add_argument("--chat-format", action="store_true")
     p.add_argument("--json", action="store_true", help="constrain output to JSON")
     p.add_argument("--speculative", action="store_true")

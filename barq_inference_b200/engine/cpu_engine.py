@@ -141,14 +141,23 @@ class CPUEngine:
         if s.embeds is not None or not self.sessions:
             return 0
         toks = s.tokens
-        best = None
+        best_k, best_c = 0, None
         for st, c in self.sessions:
-            if len(st) < len(toks) and toks[: len(st)] == st and (best is None or len(st) > len(best[0])):
-                best = (st, c)
-        if best is None:
+            # usable length: the whole session if it is a strict prefix of the prompt, else the prompt
+            # minus its last token when the session covers that (the last position must run for logits)
+            if len(st) < len(toks) and toks[: len(st)] == st:
+                k = len(st)
+            elif len(st) >= len(toks) - 1 and st[: len(toks) - 1] == toks[:-1]:
+                k = len(toks) - 1
+            else:
+                continue
+            if k > best_k:
+                best_k, best_c = k, c
+        if best_c is None:
             return 0
-        cache.update(best[1])  # the forward concatenates new rows into fresh tensors
-        return len(best[0])
+        for key, t in best_c.items():  # the forward concatenates new rows into fresh tensors
+            cache[key] = t[:best_k] if isinstance(key, tuple) else best_k
+        return best_k
 
     def generate(self, prompts: list[list[int]], params=None) -> list[GenerationResult]:
         if params is None or isinstance(params, SamplingParams):

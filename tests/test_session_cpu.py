@@ -27,6 +27,9 @@ def test_cpu_session_roundtrip(tmp_path):
     got = eng.generate([prompt], p)[0].tokens
     assert got == want
     assert eng.timings["prefill_tokens"] == 3  # only the new suffix was prefilled
+    again = eng.generate([system], p)[0].tokens  # the exact session prompt: only its last token runs
+    assert again == CPUEngine(cfg, t, max_model_len=256).generate([system], p)[0].tokens
+    assert eng.timings["prefill_tokens"] == 4
     other = preset("tiny", n_layers=1, vocab=500, max_ctx=256)
     with pytest.raises(ValueError):
         import_session(CPUEngine(other, random_tensors(other, POLICIES["tiny"], seed=0)), path)
@@ -81,3 +84,22 @@ def test_paged_session_fp8_pages():
     assert import_session(b, st) == 16
     blocks, _ = b.prefix_cache.match(toks + [0])
     assert torch.equal(b.runner.kv[1][0][blocks[0]], a.runner.kv[1][0][tbl[0]].to(torch.float16))
+
+
+def test_cli_prompt_cache(tmp_path, caplog):
+    """``run --prompt-cache``: the first run writes the session, the second reuses it (CPU engine)."""
+    import logging
+
+    from barq_inference_b200.cli import main
+
+    path = str(tmp_path / "m.gguf")
+    pc = str(tmp_path / "p.session")
+    assert main(["make-random-gguf", "--arch", "tiny", "--layers", "1", "--output", path, "--device", "cpu"]) == 0
+    argv = ["run", "-m", path, "--device", "cpu", "--prompt-ids", ",".join(str(i) for i in range(5, 45)),
+            "--max-tokens", "3", "--temperature", "0", "--prompt-cache", pc]
+    assert main(argv) == 0
+    st = load_session(pc)
+    assert st["tokens"].tolist() == list(range(5, 45))
+    with caplog.at_level(logging.INFO, logger="barq"):
+        assert main(argv) == 0
+    assert any("40 tokens reusable" in r.getMessage() for r in caplog.records)
