@@ -59,6 +59,8 @@ class MoEBlock:
         self.sigmoid = cfg.expert_gating == "sigmoid"
         self.renorm = cfg.arch != "deepseek2" or cfg.expert_weights_norm
         self.stats = {"tokens": 0, "dispatched": 0}
+        self.load = None  # models.moe_stats.ExpertLoad when expert-load counting is on
+        self.layer_index = 0
 
     # ------------------------------------------------------------------ forward
     def forward(self, runner, hq, hb: torch.Tensor, T: int, x: torch.Tensor) -> None:
@@ -89,6 +91,8 @@ class MoEBlock:
         ops.moe_route(logits, hb, self.k, r, **self._route_args(ser))
         # rows are sorted by expert: the local experts' rows are the window off[e0 .. e0 + E_local]
         off = r.off[self.e0:self.e0 + self.E_local + 1]
+        if self.load is not None:  # rows routed to each of the E experts (sorted-row offsets)
+            self.load.add(self.layer_index, r.off[1:self.E + 1] - r.off[:self.E])
         h = ops.gemm_grouped(self.gate_up, r.xs, off, self.E_local, EPI_SWIGLU_Q8)  # [T*k, F]
         ops.gemm_grouped(self.down, h, off, self.E_local, EPI_MOE_COMBINE, out=x, row_tok=r.row_tok, row_w=r.row_w)
 

@@ -83,6 +83,9 @@ class ReferenceModel:
         cfg, w = self.cfg, self.w
         logits = x @ w[p + "ffn_gate_inp.weight"].T
         ids, wt = moe_route(logits, cfg, self.ser)
+        load = getattr(self, "expert_load", None)
+        if load is not None:
+            load.add(int(p.split(".")[1]), torch.bincount(ids.reshape(-1), minlength=cfg.n_experts))
         out = torch.zeros_like(x)
         G, U, D = w[p + "ffn_gate_exps.weight"], w[p + "ffn_up_exps.weight"], w[p + "ffn_down_exps.weight"]
         for t in range(x.shape[0]):

@@ -128,6 +128,11 @@ class LlamaRunner:
                 L.down = _qw(tensors[p + "ffn_down.weight"], dev)
             self.layers.append(L)
         self.cos, self.sin = rope_cos_sin(cfg, cfg.max_ctx, dev)
+        if cfg.is_moe:
+            from .moe_stats import enable, enabled_by_env
+
+            if enabled_by_env():  # BARQ_MOE_STATS=1: per-expert routed-row counters on the device
+                enable(self, dev)
 
     # ------------------------------------------------------------------ KV cache
     def allocate_kv(self, num_blocks: int, block_size: int = 16) -> list[tuple[torch.Tensor, torch.Tensor]]:

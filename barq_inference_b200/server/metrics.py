@@ -122,6 +122,13 @@ class InferenceMetrics:
             spec = getattr(engine, "spec_stats", None)
             if spec is not None:
                 g("barq_spec_acceptance_rate", spec.acceptance_rate, "gauge")
+            load = getattr(getattr(engine, "runner", None), "expert_load", None) or getattr(
+                getattr(engine, "model", None), "expert_load", None)
+            if load is not None:  # MoE expert-load counters (BARQ_MOE_STATS=1)
+                ms = load.summary()
+                g("barq_moe_tokens_routed_total", ms["tokens_routed"])
+                g("barq_moe_load_max_over_mean", ms["max_over_mean"], "gauge")
+                g("barq_moe_load_cv", ms["cv"], "gauge")
         lines.append("# TYPE barq_ttft_seconds histogram")
         lines += self.ttft.lines("barq_ttft_seconds")
         lines.append("# TYPE barq_tpot_seconds histogram")
