@@ -65,9 +65,7 @@ def load(args, need_engine: bool = True):
             torch.cuda.set_device(local)
             device = f"cuda:{local}"
         pp = int(getattr(args, "pp", 1) or 1)
-        if pp > 1 and tp > 1:
-            raise SystemExit("--pp with --tp: combined pipeline x tensor parallelism is not built; pick one")
-        if pp > 1:
+        if pp > 1:  # (with --tp too: a tp x pp grid, global rank = stage * tp + tensor rank)
             import os
 
             import torch

@@ -508,7 +508,43 @@ class _Packed:
         self.dev.copy_(self.host, non_blocking=True)
 
 
+def _attach_health(r, comm, global_rank: int, global_world: int, ec: "EngineConfig") -> None:
+    from torch.distributed.distributed_c10d import _get_default_store
+
+    from ..parallel.health import FaultInjector, Heartbeat
+
+    r.injector = FaultInjector(global_rank)
+    r.health = Heartbeat(_get_default_store(), global_rank, global_world, timeout=ec.rank_timeout_s,
+                         injector=r.injector)
+
+
 def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
+    if ec.pp > 1 and ec.tp > 1:
+        # tp x pp grid: each pipeline stage is a tensor-parallel group (global rank = stage * tp + t)
+        import datetime
+
+        import torch.distributed as dist
+
+        from ..parallel.comm import Comm
+        from ..parallel.pp import PPInfo, grid_groups, shard_pp, stage_layers
+        from ..parallel.tp import shard_config, shard_tensors
+
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", device_id=torch.device(device), timeout=datetime.timedelta(seconds=120))
+        stage, t, tp_group, pp_group = grid_groups(ec.tp, ec.pp)
+        l0, l1 = stage_layers(cfg.n_layers, ec.pp)[stage]
+        comm = Comm(torch.device(device), fused=ec.fused_comm,
+                    max_elems=max(ec.max_num_batched_tokens, ec.max_num_seqs) * cfg.hidden, hidden=cfg.hidden,
+                    group=tp_group)
+        stage_tensors = shard_pp(tensors, cfg.n_layers, stage, ec.pp)
+        shard, info = shard_tensors(cfg, stage_tensors, t, ec.tp)
+        r = LlamaRunner(shard_config(cfg, ec.tp), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info, comm=comm,
+                        pp=PPInfo(stage, ec.pp, l0, l1, tp=ec.tp, tp_rank=t, group=pp_group))
+        _attach_health(r, comm, dist.get_rank(), dist.get_world_size(), ec)
+        r.ser_threshold = ec.ser_threshold
+        r.fused_moe = ec.fused_moe
+        dist.barrier()
+        return r
     if ec.pp > 1:
         import datetime
 
@@ -539,12 +575,7 @@ def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
         shard, info = shard_tensors(cfg, tensors, comm.rank, comm.world)
         r = LlamaRunner(shard_config(cfg, comm.world), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info, comm=comm)
         comm.barrier()  # ranks finish building (tiling) their shards before the first collective
-        from ..parallel.health import FaultInjector, Heartbeat
-        from torch.distributed.distributed_c10d import _get_default_store
-
-        r.injector = FaultInjector(comm.rank)
-        r.health = Heartbeat(_get_default_store(), comm.rank, comm.world, timeout=ec.rank_timeout_s,
-                             injector=r.injector)
+        _attach_health(r, comm, comm.rank, comm.world, ec)
         r.ser_threshold = ec.ser_threshold
         r.fused_moe = ec.fused_moe
         return r

@@ -30,11 +30,14 @@ from ..ops import require_ext
 
 class Comm:
     def __init__(self, device: torch.device, fused: bool = True, max_elems: int = 0,
-                 timeout_s: float = 120.0, wait_s: float = 20.0, hidden: int = 0, push_rows: int = 8):
+                 timeout_s: float = 120.0, wait_s: float = 20.0, hidden: int = 0, push_rows: int = 8, group=None):
+        """``group``: the tensor-parallel process group (None = every rank; a subgroup when tensor
+        parallelism is combined with pipeline stages).  ``rank`` / ``world`` are group-local."""
         if not dist.is_initialized():
             dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=timeout_s))
-        self.rank = dist.get_rank()
-        self.world = dist.get_world_size()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
         self.device = device
         # device-side barrier limit of the fused all-reduce: ranks may legitimately drift apart by
         # seconds (graph capture, garbage collection); a longer silence is a failed peer
@@ -60,9 +63,9 @@ class Comm:
         pe = self.push_elems
         self.buf = symm.empty(2 * n + flag_words + 2 * self.world * pe * 2, dtype=torch.float32, device=self.device)
         self.buf.zero_()
-        self.hdl = symm.rendezvous(self.buf, dist.group.WORLD)
+        self.hdl = symm.rendezvous(self.buf, self.group if self.group is not None else dist.group.WORLD)
         torch.cuda.synchronize(self.device)
-        dist.barrier()
+        dist.barrier(group=self.group)
         base = list(self.hdl.buffer_ptrs)
         self._bufs = [[p + j * n * 4 for p in base] for j in (0, 1)]
         self._flags = [p + 2 * n * 4 for p in base]
@@ -98,17 +101,17 @@ class Comm:
 
     # ------------------------------------------------------------------ NCCL baseline
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
-        dist.all_reduce(x)
+        dist.all_reduce(x, group=self.group)
         return x
 
     def all_gather_cols(self, y: torch.Tensor) -> torch.Tensor:
         """Concatenate every rank's [T, n_r] along columns (vocab-parallel logits; equal n_r)."""
         parts = [torch.empty_like(y) for _ in range(self.world)]
-        dist.all_gather(parts, y.contiguous())
+        dist.all_gather(parts, y.contiguous(), group=self.group)
         return torch.cat(parts, 1)
 
     def barrier(self) -> None:
-        dist.barrier()
+        dist.barrier(group=self.group)
 
     def check(self) -> None:
         """Raise if a fused all-reduce gave up waiting for a peer (bounded device-side waits)."""

@@ -54,26 +54,58 @@ def shard_pp(tensors: dict[str, PackedTensor], n_layers: int, stage: int, world:
 
 @dataclass
 class PPInfo:
+    """This rank's pipeline stage.  With tensor parallelism inside each stage (``tp`` > 1) the
+    global rank of (stage s, tensor rank t) is ``s * tp + t``: hidden states go to the rank with the
+    same tensor rank in the next stage, and the last stage's rank broadcasts the (already gathered)
+    logits over ``group``, the ranks sharing this tensor rank."""
     stage: int
     world: int
     l0: int
     l1: int
+    tp: int = 1
+    tp_rank: int = 0
+    group: object = None
 
     @property
     def is_last(self) -> bool:
         return self.stage == self.world - 1
 
+    def global_rank(self, stage: int) -> int:
+        return stage * self.tp + self.tp_rank
+
     def send(self, x: torch.Tensor) -> None:
         import torch.distributed as dist
 
-        dist.send(x.contiguous(), self.stage + 1)
+        dist.send(x.contiguous(), self.global_rank(self.stage + 1))
 
     def recv(self, x: torch.Tensor) -> None:
         import torch.distributed as dist
 
-        dist.recv(x, self.stage - 1)
+        dist.recv(x, self.global_rank(self.stage - 1))
 
     def broadcast_logits(self, logits: torch.Tensor) -> None:
         import torch.distributed as dist
 
-        dist.broadcast(logits, self.world - 1)
+        dist.broadcast(logits, self.global_rank(self.world - 1), group=self.group)
+
+
+def grid_groups(tp: int, pp: int):
+    """Process groups of a tp x pp grid (global rank = stage * tp + tensor rank): returns
+    (stage, tensor rank, this rank's tensor-parallel group, this rank's pipeline group).  Every
+    rank creates every group, in the same order, as ``new_group`` requires."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if world != tp * pp:
+        raise ValueError(f"tp={tp} x pp={pp} needs {tp * pp} ranks, the process group has {world}")
+    stage, t = divmod(rank, tp)
+    tp_group = pp_group = None
+    for s in range(pp):
+        g = dist.new_group([s * tp + i for i in range(tp)])
+        if s == stage:
+            tp_group = g
+    for i in range(tp):
+        g = dist.new_group([s * tp + i for s in range(pp)])
+        if i == t:
+            pp_group = g
+    return stage, t, tp_group, pp_group

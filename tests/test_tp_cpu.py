@@ -113,3 +113,42 @@ def test_pipeline_stage_split_and_tensor_filter():
     assert "output_norm.weight" in s1 and "blk.0.attn_q.weight" not in s1
     assert {k for k in s0 if k.startswith("blk.")} | {k for k in s1 if k.startswith("blk.")} == \
         {k for k in full if k.startswith("blk.")}
+
+
+def _grid_worker(rank, world, port, out_path):
+    from barq_inference_b200.parallel.pp import PPInfo, grid_groups
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    stage, t, tpg, ppg = grid_groups(2, 2)
+    x = torch.tensor([float(rank)])
+    dist.all_reduce(x, group=tpg)  # sum over the two tensor ranks of this stage
+    info = PPInfo(stage, 2, 0, 1, tp=2, tp_rank=t, group=ppg)
+    logits = torch.tensor([100.0 + rank]) if info.is_last else torch.zeros(1)
+    info.broadcast_logits(logits)  # from the last stage's rank with the same tensor rank
+    h = torch.tensor([10.0 * rank])
+    if stage == 0:
+        info.send(h)
+    else:
+        info.recv(h)
+    torch.save({"stage": stage, "t": t, "tp_sum": x.item(), "logits": logits.item(), "h": h.item(),
+                "dst": info.global_rank(1)}, f"{out_path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_tp_pp_grid_groups(tmp_path):
+    """tp=2 x pp=2 over 4 gloo ranks: rank = stage * tp + t; tensor-parallel sums stay inside a stage,
+    hidden states go to the same tensor rank of the next stage, logits come from the last stage."""
+    import socket as _s
+
+    with _s.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    path = str(tmp_path / "g")
+    mp.spawn(_grid_worker, args=(4, port, path), nprocs=4, join=True)
+    r = [torch.load(f"{path}.{i}") for i in range(4)]
+    assert [(x["stage"], x["t"]) for x in r] == [(0, 0), (0, 1), (1, 0), (1, 1)]
+    assert [x["tp_sum"] for x in r] == [1.0, 1.0, 5.0, 5.0]
+    assert [x["logits"] for x in r] == [102.0, 103.0, 102.0, 103.0]
+    assert [x["h"] for x in r] == [0.0, 10.0, 0.0, 10.0]  # stage 1 received its stage-0 peer's states
