@@ -1,4 +1,5 @@
-"""Tokenizers built from GGUF metadata: SentencePiece-style BPE ("llama") and byte-level BPE ("gpt2").
+"""Tokenizers built from GGUF metadata: SentencePiece-style BPE ("llama"), byte-level BPE ("gpt2"),
+WordPiece ("bert") and Unigram ("t5").
 
 Parity: ``GgufTokenizer`` (``vocab/src/gguf_tokenizer.rs:76-566``).  The reference tokenizes
 SPM vocabularies with a greedy longest match (``tokenize_greedy``, ``:416-468``) and builds GPT-2 BPE by
@@ -9,6 +10,15 @@ writing temp files for an external crate.  Here both follow the published algori
   ``<0xNN>`` byte tokens.
 * byte-level BPE: pre-tokenize with the GPT-2 / Llama-3 regex, map bytes to printable characters,
   merge by rank from ``tokenizer.ggml.merges``.
+* WordPiece (BERT; the reference's ``WpmTokenizer`` returns "not yet implemented"): NFD, lower case,
+  accents stripped, split on whitespace with punctuation and CJK characters as words of their own;
+  each word, prefixed with "▁" (GGUF BERT vocabularies mark word starts that way instead of "##"
+  continuations), is cut greedily into the longest vocabulary pieces; a word that cannot be covered
+  becomes the unknown token.
+* Unigram (T5 / SentencePiece unigram; the reference's ``UgmTokenizer`` is a stub): spaces become
+  "▁" (plus a leading one), then a Viterbi pass picks the segmentation with the highest total
+  score (log-probability) over the vocabulary; characters no piece covers cost the unknown
+  token's score minus 10.
 
 Special / control tokens written literally in the text are split out first and mapped directly.
 """
@@ -105,7 +115,7 @@ class GGUFTokenizer:
             scores=[float(x) for x in scores] if scores is not None else [],
             token_types=[int(x) for x in types] if types is not None else [],
             merges=list(merges) if merges is not None else [],
-            model="gpt2" if model == "gpt2" else "llama",
+            model=model if model in ("gpt2", "bert", "t5") else "llama",
             pre=str(md.get("tokenizer.ggml.pre", "default")),
             bos_id=md.get("tokenizer.ggml.bos_token_id"),
             eos_id=md.get("tokenizer.ggml.eos_token_id"),
@@ -131,7 +141,14 @@ class GGUFTokenizer:
                 out.append(self.vocab[p])
                 first = False
                 continue
-            out.extend(self._encode_spm(p, first) if self.model == "llama" else self._encode_bpe(p))
+            if self.model == "llama":
+                out.extend(self._encode_spm(p, first))
+            elif self.model == "bert":
+                out.extend(self._encode_wpm(p))
+            elif self.model == "t5":
+                out.extend(self._encode_ugm(p, first))
+            else:
+                out.extend(self._encode_bpe(p))
             first = False
         return out
 
@@ -227,13 +244,96 @@ class GGUFTokenizer:
                     out.append(tid)
         return out
 
+    def _encode_wpm(self, text: str) -> list[int]:
+        import unicodedata
+
+        unk = self.vocab.get("[UNK]", self.vocab.get("<unk>", 0))
+        norm = "".join(c for c in unicodedata.normalize("NFD", text.lower()) if unicodedata.category(c) != "Mn")
+        words, cur = [], []
+        for ch in norm:
+            cp = ord(ch)
+            if ch.isspace():
+                if cur:
+                    words.append("".join(cur))
+                    cur = []
+            elif unicodedata.category(ch).startswith("P") or (33 <= cp <= 47 or 58 <= cp <= 64 or 91 <= cp <= 96
+                                                               or 123 <= cp <= 126) or _is_cjk(cp):
+                if cur:
+                    words.append("".join(cur))
+                    cur = []
+                words.append(ch)
+            else:
+                cur.append(ch)
+        if cur:
+            words.append("".join(cur))
+        out: list[int] = []
+        for w in words:
+            w = SPIECE + w
+            pieces, i, ok = [], 0, True
+            while i < len(w):
+                j = len(w)
+                while j > i and w[i:j] not in self.vocab:
+                    j -= 1
+                if j == i:
+                    ok = False
+                    break
+                pieces.append(self.vocab[w[i:j]])
+                i = j
+            out.extend(pieces if ok else [unk])
+        return out
+
+    def _encode_ugm(self, text: str, first: bool) -> list[int]:
+        text = regex.sub(" +", " ", text)  # runs of spaces collapse (SentencePiece normalization)
+        if self.add_space_prefix and first and not text.startswith(" "):
+            text = " " + text
+        text = text.replace(" ", SPIECE)
+        n = len(text)
+        if n == 0:
+            return []
+        unk = self.vocab.get("<unk>", self.vocab.get("[UNK]", 0))
+        if not hasattr(self, "_ugm_maxlen"):
+            self._ugm_maxlen = max((len(t) for t in self.tokens), default=1)
+            normal = [sc for sc, ty in zip(self.scores, self.token_types) if ty == TT_NORMAL]
+            self._ugm_unk_score = (min(normal) if normal else 0.0) - 10.0
+        best = [float("-inf")] * (n + 1)
+        back: list[tuple[int, int]] = [(0, -1)] * (n + 1)
+        best[0] = 0.0
+        for i in range(n):
+            if best[i] == float("-inf"):
+                continue
+            covered = False
+            for j in range(i + 1, min(n, i + self._ugm_maxlen) + 1):
+                tid = self.vocab.get(text[i:j])
+                if tid is None or self.token_types[tid] not in (TT_NORMAL, TT_USER_DEFINED):
+                    continue
+                covered = covered or j == i + 1
+                sc = best[i] + (0.0 if self.token_types[tid] == TT_USER_DEFINED else self.scores[tid])
+                if sc > best[j]:
+                    best[j], back[j] = sc, (i, tid)
+            if not covered:  # no single-character piece: this character costs the unknown token
+                sc = best[i] + self._ugm_unk_score
+                if sc > best[i + 1]:
+                    best[i + 1], back[i + 1] = sc, (i, unk)
+        out: list[int] = []
+        j = n
+        while j > 0:
+            i, tid = back[j]
+            out.append(tid)
+            j = i
+        out.reverse()
+        merged: list[int] = []  # consecutive unknown characters collapse into one unknown token
+        for t in out:
+            if not (t == unk and merged and merged[-1] == unk):
+                merged.append(t)
+        return merged
+
     # ------------------------------------------------------------------ decode
     def token_bytes(self, tid: int) -> bytes:
         t = self.tokens[tid]
         ty = self.token_types[tid] if tid < len(self.token_types) else TT_NORMAL
         if ty == TT_CONTROL:
             return b""
-        if self.model == "llama":
+        if self.model in ("llama", "bert", "t5"):
             if ty == TT_BYTE or (len(t) == 6 and t.startswith("<0x") and t.endswith(">")):
                 try:
                     return bytes([int(t[3:5], 16)])
@@ -247,7 +347,9 @@ class GGUFTokenizer:
     def decode(self, ids: list[int], skip_special: bool = True) -> str:
         buf = b"".join(self.token_bytes(i) for i in ids if 0 <= i < len(self.tokens))
         s = buf.decode("utf-8", errors="replace")
-        if self.model == "llama" and self.add_space_prefix and s.startswith(" "):
+        if self.model in ("llama", "t5") and self.add_space_prefix and s.startswith(" "):
+            s = s[1:]
+        elif self.model == "bert" and s.startswith(" "):  # every word starts with "▁"
             s = s[1:]
         return s
 
@@ -275,6 +377,12 @@ class StreamDecoder:
         s = self.pending.decode("utf-8", errors="replace")
         self.pending = b""
         return s
+
+
+def _is_cjk(cp: int) -> bool:
+    return (0x4E00 <= cp <= 0x9FFF or 0x3400 <= cp <= 0x4DBF or 0x20000 <= cp <= 0x2A6DF or 0x2A700 <= cp <= 0x2B73F
+            or 0x2B740 <= cp <= 0x2B81F or 0x2B820 <= cp <= 0x2CEAF or 0xF900 <= cp <= 0xFAFF
+            or 0x2F800 <= cp <= 0x2FA1F)
 
 
 def _make_native(tok: "GGUFTokenizer"):
