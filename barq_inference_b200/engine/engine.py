@@ -272,35 +272,47 @@ class Engine:
         bs = self.ecfg.block_size
         return s.block_table[pos // bs] * bs + pos % bs
 
-    def _run_prefill(self, plan: ScheduledStep) -> list[int | None]:
-        ids, pos, slots, last = [], [], [], []
+    def _prefill_arrays(self, plan: ScheduledStep):
+        """Token ids, positions, KV slots, query starts, last rows, block tables and lengths of a
+        prefill step, built per sequence with array slices (no per-token Python work), plus the
+        rows / values of image embeddings that replace token embeddings."""
+        bs = self.ecfg.block_size
+        ids_p, pos_p, slot_p = [], [], []
         e_rows, e_vals = [], []
         q_start = [0]
+        total = 0
         for s, n in zip(plan.seqs, plan.n_new):
-            toks = s.tokens
+            c = s.n_cached
             if s.embeds is not None:  # image rows of this chunk
                 st, e = s.embeds
-                lo, hi = max(st, s.n_cached), min(st + e.shape[0], s.n_cached + n)
+                lo, hi = max(st, c), min(st + e.shape[0], c + n)
                 if lo < hi:
-                    base = len(ids) - s.n_cached
+                    base = total - c
                     e_rows.extend(range(base + lo, base + hi))
                     e_vals.append(e[lo - st: hi - st])
-            for p in range(s.n_cached, s.n_cached + n):
-                ids.append(toks[p])
-                pos.append(p)
-                slots.append(self._slot_of(s, p))
-            q_start.append(len(ids))
-            last.append(len(ids) - 1)
+            p = np.arange(c, c + n, dtype=np.int64)
+            toks = s.prompt[c:c + n] if c + n <= len(s.prompt) else s.tokens[c:c + n]
+            ids_p.append(np.asarray(toks, dtype=np.int32))
+            pos_p.append(p)
+            tbl = np.asarray(s.block_table, dtype=np.int64)
+            slot_p.append(tbl[p // bs] * bs + p % bs)
+            total += n
+            q_start.append(total)
         S = len(plan.seqs)
         mb = max(len(s.block_table) for s in plan.seqs)
         bt = np.zeros((S, mb), np.int32)
         for i, s in enumerate(plan.seqs):
             bt[i, : len(s.block_table)] = s.block_table
         seq_lens = np.array([s.n_cached + n for s, n in zip(plan.seqs, plan.n_new)], np.int32)
-        inp = StepInput(self._to_dev(np.array(ids, np.int32)), self._to_dev(np.array(pos, np.int32)),
-                        self._to_dev(np.array(slots, np.int64)), self._to_dev(bt), self._to_dev(seq_lens),
-                        self._to_dev(np.array(last, np.int64)), False,
-                        q_start=self._to_dev(np.array(q_start, np.int32)), max_q=max(plan.n_new))
+        qs = np.array(q_start, np.int32)
+        return (np.concatenate(ids_p), np.concatenate(pos_p).astype(np.int32), np.concatenate(slot_p), qs,
+                (qs[1:] - 1).astype(np.int64), bt, seq_lens, e_rows, e_vals)
+
+    def _run_prefill(self, plan: ScheduledStep) -> list[int | None]:
+        ids, pos, slots, q_start, last, bt, seq_lens, e_rows, e_vals = self._prefill_arrays(plan)
+        inp = StepInput(self._to_dev(ids), self._to_dev(pos), self._to_dev(slots), self._to_dev(bt),
+                        self._to_dev(seq_lens), self._to_dev(last), False,
+                        q_start=self._to_dev(q_start), max_q=max(plan.n_new))
         if e_rows:
             inp.embed_rows = self._to_dev(np.array(e_rows, np.int64))
             inp.embed_vals = torch.cat(e_vals)

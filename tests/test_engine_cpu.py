@@ -203,3 +203,45 @@ def test_incremental_decode_packing_equals_full_rewrite():
             ref.h[k][...] = a
         assert n == len(pool)
         assert np.array_equal(inc.host.numpy(), ref.host.numpy()), step
+
+
+def test_prefill_arrays_match_per_token_construction():
+    import random
+    import types
+
+    import numpy as np
+
+    from barq_inference_b200.engine.engine import Engine
+    from barq_inference_b200.engine.scheduler import ScheduledStep
+
+    rng = random.Random(1)
+    eng = Engine.__new__(Engine)
+    eng.ecfg = types.SimpleNamespace(block_size=16)
+    for trial in range(50):
+        seqs, n_new = [], []
+        for _ in range(rng.randint(1, 5)):
+            s = Sequence([rng.randrange(1000) for _ in range(rng.randint(1, 90))], SamplingParams())
+            s.output = [rng.randrange(1000) for _ in range(rng.choice([0, 0, 3]))]
+            s.n_cached = rng.randint(0, s.n_tokens - 1)
+            n = rng.randint(1, s.n_tokens - s.n_cached)
+            s.block_table = rng.sample(range(1, 500), (s.n_cached + n + 15) // 16)
+            if rng.random() < 0.3:
+                st = rng.randrange(len(s.prompt))
+                s.embeds = (st, torch.randn(min(5, len(s.prompt) - st), 8))
+            seqs.append(s)
+            n_new.append(n)
+        ids, pos, slots, qs, last, bt, lens, e_rows, e_vals = eng._prefill_arrays(ScheduledStep("prefill", seqs, n_new))
+        want_ids, want_pos, want_slots, want_rows = [], [], [], []
+        for s, n in zip(seqs, n_new):
+            if s.embeds is not None:
+                st, e = s.embeds
+                for p in range(max(st, s.n_cached), min(st + e.shape[0], s.n_cached + n)):
+                    want_rows.append(len(want_ids) + p - s.n_cached)
+            for p in range(s.n_cached, s.n_cached + n):
+                want_ids.append(s.tokens[p])
+                want_pos.append(p)
+                want_slots.append(s.block_table[p // 16] * 16 + p % 16)
+        assert ids.dtype == np.int32 and pos.dtype == np.int32 and slots.dtype == np.int64
+        assert ids.tolist() == want_ids and pos.tolist() == want_pos and slots.tolist() == want_slots
+        assert qs.tolist() == [0] + list(np.cumsum(n_new)) and last.tolist() == [q - 1 for q in qs.tolist()[1:]]
+        assert e_rows == want_rows and lens.tolist() == [s.n_cached + n for s, n in zip(seqs, n_new)]
