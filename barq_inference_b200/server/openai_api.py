@@ -6,16 +6,20 @@ limiting (429 ``rate_limit_error``), request defaults (max_tokens 128, temperatu
 top_p 0.95), ``/v1/responses`` accepting ``input`` / ``prompt`` / ``messages`` and
 ``max_output_tokens``, ids ``cmpl-`` / ``chatcmpl-`` / ``resp-<unix ts>``, SSE chunk objects
 ``text_completion.chunk``, ``chat.completion.chunk`` (role delta first) and ``response.chunk``,
-``data: [DONE]``.  Added: ``/health``, ``/metrics`` (Prometheus), ``response_format`` JSON mode,
-``stop``, ``seed``, and continuous batching across concurrent requests.
+``data: [DONE]``.  Added: ``/health``, ``/metrics`` (Prometheus), ``response_format`` JSON mode /
+JSON schema, ``grammar`` (GBNF), ``stop``, ``seed``, ``n`` choices, ``stream_options.include_usage``,
+per-request log lines with ``x-request-id``, 503 from admission control, and continuous batching
+across concurrent requests.
 """
 from __future__ import annotations
 
+import asyncio
+import dataclasses
 import json
 import threading
-from collections import OrderedDict
 import time
 import uuid
+from collections import OrderedDict
 from typing import Any
 
 from fastapi import FastAPI, Request
@@ -168,35 +172,44 @@ class OpenAIServer:
         return StreamingResponse(wrap(), media_type="text/event-stream",
                                  headers={**CORS, "Cache-Control": "no-cache"})
 
-    async def _complete(self, prompt_ids, params, stops, kind: str, model: str):
+    async def _complete(self, prompt_ids, params, stops, kind: str, model: str, n_choices: int = 1):
         guard = self.metrics.begin()
         created = int(time.time())
         rid = {"text": "cmpl", "chat": "chatcmpl", "resp": "resp"}[kind] + f"-{created}{id(guard) % 100000}"
-        parts, reason, n = [], "stop", 0
-        try:
-            async for delta, fin in self._run(prompt_ids, params, stops):
+
+        async def one(i: int):
+            # choice i samples with its own seed (a 0 seed already differs per request)
+            p = dataclasses.replace(params, seed=params.seed + i) if (i and params.seed) else params
+            parts, reason, n = [], "stop", 0
+            async for delta, fin in self._run(prompt_ids, p, stops):
                 if delta:
                     guard.first_token()
                     parts.append(delta)
                     n += 1
                 if fin:
                     reason = fin
+            return "".join(parts), reason, n
+
+        try:
+            outs = await asyncio.gather(*(one(i) for i in range(n_choices)))
         except Exception:
             guard.fail()
             raise
-        guard.complete(len(prompt_ids), n)
-        text = "".join(parts)
-        usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": n, "total_tokens": len(prompt_ids) + n}
+        n_tok = sum(o[2] for o in outs)
+        guard.complete(len(prompt_ids), n_tok)
+        usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": n_tok, "total_tokens": len(prompt_ids) + n_tok}
         if kind == "text":
             return {"id": rid, "object": "text_completion", "created": created, "model": model,
-                    "choices": [{"index": 0, "text": text, "finish_reason": reason}], "usage": usage}
+                    "choices": [{"index": i, "text": t, "finish_reason": r} for i, (t, r, _) in enumerate(outs)],
+                    "usage": usage}
         if kind == "chat":
             return {"id": rid, "object": "chat.completion", "created": created, "model": model,
-                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                                 "finish_reason": reason}], "usage": usage}
-        return {"id": rid, "object": "response", "created": created, "model": model, "output": text, "usage": usage}
+                    "choices": [{"index": i, "message": {"role": "assistant", "content": t}, "finish_reason": r}
+                                for i, (t, r, _) in enumerate(outs)], "usage": usage}
+        return {"id": rid, "object": "response", "created": created, "model": model, "output": outs[0][0],
+                "usage": usage}
 
-    async def _stream(self, prompt_ids, params, stops, kind: str, model: str):
+    async def _stream(self, prompt_ids, params, stops, kind: str, model: str, include_usage: bool = False):
         guard = self.metrics.begin()
         created = int(time.time())
         rid = {"text": "cmpl", "chat": "chatcmpl", "resp": "resp"}[kind] + f"-{created}{id(guard) % 100000}"
@@ -221,6 +234,11 @@ class OpenAIServer:
                 else:
                     yield {"id": rid, "object": "response.chunk", "created": created, "model": model, "output": delta}
             guard.complete(len(prompt_ids), n)
+            if include_usage:  # stream_options.include_usage: a final chunk with usage and no choices
+                yield {"id": rid, "object": "chat.completion.chunk" if kind == "chat" else "text_completion.chunk",
+                       "created": created, "model": model, "choices": [],
+                       "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": n,
+                                 "total_tokens": len(prompt_ids) + n}}
         finally:
             if not guard.done:
                 guard.fail()
@@ -334,9 +352,16 @@ class OpenAIServer:
                             raise ValueError("input (or prompt / messages) is required")
                     params = _params(body, "max_output_tokens")
                 stops = srv._stops(body)
+                n_choices = int(body.get("n", 1) or 1)
+                if not 1 <= n_choices <= 16:
+                    raise ValueError("n must be between 1 and 16")
                 if body.get("stream"):
-                    return srv._sse(srv._stream(ids, params, stops, kind, model))
-                return JSONResponse(await srv._complete(ids, params, stops, kind, model))
+                    if n_choices > 1:
+                        raise ValueError("n > 1 is not supported with stream")
+                    so = body.get("stream_options") or {}
+                    inc = bool(so.get("include_usage")) if isinstance(so, dict) else False
+                    return srv._sse(srv._stream(ids, params, stops, kind, model, include_usage=inc))
+                return JSONResponse(await srv._complete(ids, params, stops, kind, model, n_choices))
             except ValueError as e:
                 return _err(400, str(e))
             except Overloaded as e:  # admission control: queue full

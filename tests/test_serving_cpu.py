@@ -308,3 +308,21 @@ def test_prompt_tokenization_lru(tiny_engine):
         assert srv.tok_cache_hits == 1 and len(srv._tok_cache) == 2
     finally:
         srv.aengine.shutdown()
+
+
+def test_http_n_choices_and_stream_usage(client):
+    r = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 4, "n": 3, "temperature": 0.9,
+                                             "seed": 5})
+    assert r.status_code == 200, r.text
+    ch = r.json()["choices"]
+    assert [c["index"] for c in ch] == [0, 1, 2]
+    assert r.json()["usage"]["completion_tokens"] >= 3
+    assert client.post("/v1/completions", json={"prompt": "hi", "n": 2, "stream": True}).status_code == 400
+    with client.stream("POST", "/v1/chat/completions",
+                       json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "stream": True,
+                             "stream_options": {"include_usage": True}}) as resp:
+        lines = [ln for ln in resp.iter_lines() if ln.startswith("data: ")]
+    import json as _json
+
+    last = _json.loads(lines[-2][6:])  # the chunk before [DONE]
+    assert last["choices"] == [] and last["usage"]["prompt_tokens"] > 0
