@@ -61,6 +61,8 @@ class GGMLType(enum.IntEnum):
     F64 = 28
     IQ1_M = 29
     BF16 = 30
+    TQ1_0 = 34
+    TQ2_0 = 35
     # ik_llama.cpp extension types (its ``ggml_type`` numbering).  Their rows start with a row
     # scale (``row_meta`` bytes) before the blocks.
     IQ4_KS = 144
@@ -100,6 +102,8 @@ TYPE_TRAITS: dict[GGMLType, TypeTraits] = {
     GGMLType.Q8_K: TypeTraits(QK_K, 4 + 256 + 32),
     GGMLType.IQ4_NL: TypeTraits(32, 2 + 16),
     GGMLType.IQ4_XS: TypeTraits(QK_K, 2 + 2 + 4 + 128),
+    GGMLType.TQ1_0: TypeTraits(QK_K, 48 + 4 + 2),
+    GGMLType.TQ2_0: TypeTraits(QK_K, 64 + 2),
     GGMLType.IQ4_KS: TypeTraits(QK_K, 8 + 128, 4),  # f32 row scale; scales[8], qs[128]
     GGMLType.IQ2_KS: TypeTraits(QK_K, 2 + 4 + 64, 2),  # f16 row scale; extra, scales[4], qs[64]
     GGMLType.IQ3_KS: TypeTraits(QK_K, 2 + 4 + 64 + 32, 2),  # f16 row scale; extra, scales[4], qs[64], qh[32]
@@ -134,6 +138,8 @@ QUANT_NAME_TO_TYPE: dict[str, GGMLType] = {
     "q8_k": GGMLType.Q8_K,
     "iq4_nl": GGMLType.IQ4_NL,
     "iq4_xs": GGMLType.IQ4_XS,
+    "tq1_0": GGMLType.TQ1_0,
+    "tq2_0": GGMLType.TQ2_0,
     "iq4_ks": GGMLType.IQ4_KS,
     "iq3_ks": GGMLType.IQ3_KS,
     "iq2_ks": GGMLType.IQ2_KS,

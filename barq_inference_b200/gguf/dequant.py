@@ -265,6 +265,18 @@ _DQ = {
 }
 
 
+def _tq(name):
+    def f(raw):
+        from . import ternary
+
+        return getattr(ternary, name)(raw)
+    return f
+
+
+_DQ[GGMLType.TQ1_0] = _tq("dq_tq1_0")
+_DQ[GGMLType.TQ2_0] = _tq("dq_tq2_0")
+
+
 def dequantize(raw: np.ndarray, t: GGMLType, shape: tuple[int, ...] | None = None) -> np.ndarray:
     """Packed GGUF bytes of type ``t`` -> float32 (reshaped to row-major ``shape`` if given)."""
     t = GGMLType(t)

@@ -233,6 +233,25 @@ def _ik_quantizers():
     QUANTIZERS.update(Q_IK)
 
 
+def _ternary(name: str):
+    """TQ1_0 / TQ2_0 quantizers (numpy, ``gguf/ternary.py``) with the torch signature used here:
+    [..., K] float -> [..., row bytes] uint8."""
+    def q(x: torch.Tensor) -> torch.Tensor:
+        from . import ternary
+
+        k = x.shape[-1]
+        if k % 256:
+            raise ValueError(f"{name}: row length {k} is not a multiple of 256")
+        lead = x.shape[:-1]
+        packed = getattr(ternary, name)(x.detach().float().cpu().numpy().reshape(-1, k))
+        return torch.from_numpy(packed.reshape(*lead, -1)).to(x.device)
+    return q
+
+
+QUANTIZERS[GGMLType.TQ1_0] = _ternary("q_tq1_0")
+QUANTIZERS[GGMLType.TQ2_0] = _ternary("q_tq2_0")
+
+
 _ik_quantizers()
 
 

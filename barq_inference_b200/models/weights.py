@@ -279,6 +279,12 @@ def tensors_from_gguf(g, device: str | torch.device = "cpu", names: set[str] | N
             tt, data = import_ik(rows, ti.ggml_type, shape, device)
             out[name] = PackedTensor(name, tt, shape, data)
             continue
+        if ti.ggml_type in (GGMLType.TQ1_0, GGMLType.TQ2_0):  # ternary: lossless repack to Q4_0
+            from ..gguf.ternary import to_q4_0
+
+            q4 = to_q4_0(np.asarray(rows), ti.ggml_type == GGMLType.TQ1_0).reshape(rows.shape[0], -1)
+            out[name] = PackedTensor(name, GGMLType.Q4_0, shape, torch.from_numpy(q4).to(device))
+            continue
         data = torch.from_numpy(np.array(rows, copy=True)).to(device)
         out[name] = PackedTensor(name, ti.ggml_type, shape, data)
     return out
