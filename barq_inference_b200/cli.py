@@ -194,7 +194,9 @@ def cmd_chat(args) -> int:
         if not line.strip() or line.strip() in ("/exit", "/quit"):
             break
         history.append({"role": "user", "content": line})
-        ids = tok.encode(tmpl.render(history, add_generation_prompt=True))
+        text = tmpl.render(history, add_generation_prompt=True)
+        # a template that writes the BOS text itself must not get a second BOS id
+        ids = tok.encode(text, add_special=not text.startswith(getattr(tmpl, "bos_token", "") or "\0"))
         dec = StreamDecoder(tok)
         out = []
 

@@ -326,3 +326,18 @@ def test_http_n_choices_and_stream_usage(client):
 
     last = _json.loads(lines[-2][6:])  # the chunk before [DONE]
     assert last["choices"] == [] and last["usage"]["prompt_tokens"] > 0
+
+
+def test_cli_chat_and_benchmark(tmp_path):
+    path = str(tmp_path / "m.gguf")
+    assert _cli("make-random-gguf", "--arch", "tiny", "--layers", "1", "--output", path, "--device", "cpu").returncode == 0
+    r = subprocess.run([sys.executable, "-m", "barq_inference_b200.cli", "chat", "-m", path, "--device", "cpu",
+                        "--max-tokens", "4", "--temperature", "0"], cwd=ROOT, input="hello there\nand again\n/exit\n",
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.count("> ") >= 3  # two turns answered, then /exit at the third prompt
+    r = _cli("benchmark", "-m", path, "--device", "cpu", "--iterations", "2", "--prompt-length", "8",
+             "--gen-length", "4", "--batch", "2", "--json-out")
+    assert r.returncode == 0, r.stderr[-2000:]
+    summary = json.loads(r.stdout.strip().splitlines()[-1])
+    assert summary["batch"] == 2 and summary["decode_tok_s"] > 0 and summary["ttft_p99_ms"] >= summary["ttft_p50_ms"]
