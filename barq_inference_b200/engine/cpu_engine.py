@@ -69,6 +69,12 @@ class CPUEngine:
     def has_work(self) -> bool:
         return bool(self.waiting or self.running)
 
+    def embed(self, prompts: list[list[int]], normalize: bool = True) -> torch.Tensor:
+        """Mean-pooled final-norm hidden states of each prompt ([N, hidden], fp32)."""
+        from .embeddings import embed_cpu
+
+        return embed_cpu(self, prompts, normalize)
+
     def _finish(self, s: Sequence, reason: str) -> None:
         s.status = SeqStatus.FINISHED
         s.finish_reason = reason

@@ -163,6 +163,12 @@ class Engine:
     def has_work(self) -> bool:
         return self.sched.has_work
 
+    def embed(self, prompts: list[list[int]], normalize: bool = True) -> torch.Tensor:
+        """Mean-pooled final-norm hidden states of each prompt ([N, hidden], fp32, on the CPU)."""
+        from .embeddings import embed_gpu
+
+        return embed_gpu(self, prompts, normalize)
+
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
                  ) -> list[GenerationResult]:
         if params is None or isinstance(params, SamplingParams):

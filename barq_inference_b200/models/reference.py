@@ -102,7 +102,7 @@ class ReferenceModel:
         return out
 
     def forward(self, ids: list[int] | torch.Tensor, cache: dict | None = None,
-                embeds: tuple[int, torch.Tensor] | None = None) -> torch.Tensor:
+                embeds: tuple[int, torch.Tensor] | None = None, hidden: bool = False) -> torch.Tensor:
         """Logits for every position of ``ids``.  ``cache`` (dict) carries K/V across calls.
         ``embeds`` = (first row, [n, hidden]) replaces those rows' token embeddings."""
         cfg, w = self.cfg, self.w
@@ -147,8 +147,10 @@ class ReferenceModel:
             hN = rms_norm(x, w[p + "ffn_norm.weight"], cfg.rms_eps)
             x = x + (self._moe(hN, p) if cfg.layer_is_moe(i) else self._ffn(hN, p))
         x = rms_norm(x, w["output_norm.weight"], cfg.rms_eps)
-        head = w.get("output.weight", w["token_embd.weight"])
         cache["pos"] = T0 + T
+        if hidden:  # final-norm hidden states instead of logits (embeddings)
+            return x
+        head = w.get("output.weight", w["token_embd.weight"])
         return x @ head.T
 
     def _mla(self, x, p, i, cache, cos, sin, T0):

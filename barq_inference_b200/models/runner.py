@@ -49,6 +49,9 @@ class StepInput:
     # input-embedding overrides (multimodal prompts): rows of the step whose embedding is given
     embed_rows: torch.Tensor | None = None  # int64 [n]
     embed_vals: torch.Tensor | None = None  # f32 [n, hidden]
+    # embeddings: when set (f32 [T, hidden]), the final residual stream of every row is copied here
+    # before the output norm and head
+    hidden_out: torch.Tensor | None = None
 
 
 def apply_embed_overrides(x: torch.Tensor, inp: StepInput) -> torch.Tensor:
@@ -355,6 +358,8 @@ class LlamaRunner:
             self._row_parallel(1, lambda m, o: self._lin_bf16(L.down, h, T, m, out=o), x)
         if self._stage_forward(x, inp):
             return self._stage_logits(inp)
+        if inp.hidden_out is not None:
+            inp.hidden_out.copy_(x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
         ob, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)
         if xl.shape[0] <= GEMV_MAX_T:
@@ -401,5 +406,7 @@ class LlamaRunner:
                                    gemv=(L.down, hq2, None) if hq2 is not None else None)
         if self._stage_forward(x, inp):
             return self._stage_logits(inp)
+        if inp.hidden_out is not None:
+            inp.hidden_out.copy_(x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
         return self._stage_logits(inp, self._head(xl))

@@ -45,6 +45,15 @@ def _refusal(e: Exception) -> Exception:
     return e if isinstance(e, Overloaded) else ValueError(str(e))
 
 
+@dataclass
+class _Call:
+    """A function to run on the engine thread between steps (e.g. embeddings)."""
+    fn: object
+    done: threading.Event = field(default_factory=threading.Event)
+    result: object = None
+    error: BaseException | None = None
+
+
 class AsyncEngine:
     def __init__(self, engine, metrics=None, idle_sleep: float = 0.002):
         self.engine = engine
@@ -73,7 +82,14 @@ class AsyncEngine:
             try:
                 while True:
                     sub = self.inbox.get_nowait()
-                    self._admit(sub)
+                    if isinstance(sub, _Call):
+                        try:
+                            sub.result = sub.fn(self.engine)
+                        except BaseException as e:  # noqa: BLE001 - handed to the caller
+                            sub.error = e
+                        sub.done.set()
+                    else:
+                        self._admit(sub)
             except queue.Empty:
                 pass
             if not self.engine.has_work():
@@ -131,6 +147,21 @@ class AsyncEngine:
             yield item
             if item.token is None:
                 return
+
+    def call_sync(self, fn, timeout: float | None = None):
+        """Run ``fn(engine)`` on the engine thread (between steps) and return its result."""
+        c = _Call(fn)
+        self.inbox.put(c)
+        if not c.done.wait(timeout):
+            raise TimeoutError("engine call timed out")
+        if c.error is not None:
+            raise c.error
+        return c.result
+
+    async def call(self, fn):
+        """Async form of ``call_sync``."""
+        loop = asyncio.get_running_loop()
+        return await loop.run_in_executor(None, self.call_sync, fn)
 
     def generate_blocking(self, prompt: list[int], params: SamplingParams, request_id: str = "", timeout=None):
         """Iterator of StreamItem for synchronous callers (UDS server, CLI)."""

@@ -288,6 +288,7 @@ class OpenAIServer:
         async def root():
             return {"object": "server.info", "model": srv.model_id, "architecture": srv.arch,
                     "endpoints": ["/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions",
+                                  "/v1/embeddings",
                                   "/health", "/metrics"]}
 
         @app.get("/v1/models")
@@ -368,6 +369,41 @@ class OpenAIServer:
                 return _err(503, str(e), "overloaded_error")
             except Exception as e:  # engine failure
                 return _err(500, f"{type(e).__name__}: {e}", "server_error")
+
+        @app.post("/v1/embeddings")
+        async def embeddings(request: Request):
+            lim = srv._limit(request)
+            if lim is not None:
+                return lim
+            try:
+                body = await srv._body(request)
+                inp = body.get("input")
+                if isinstance(inp, str):
+                    batch = [srv._encode(inp)]
+                elif isinstance(inp, list) and inp and all(isinstance(t, int) for t in inp):
+                    batch = [list(inp)]
+                elif isinstance(inp, list) and inp and all(isinstance(x, str) for x in inp):
+                    batch = [srv._encode(x) for x in inp]
+                elif isinstance(inp, list) and inp and all(isinstance(x, list) for x in inp):
+                    batch = [list(x) for x in inp]
+                else:
+                    raise ValueError("input must be a string, a list of strings or token-id list(s)")
+                if any(not b for b in batch) or any(t < 0 or t >= srv.engine.cfg.vocab for b in batch for t in b):
+                    raise ValueError("input token ids out of range")
+                if not hasattr(srv.aengine, "call"):
+                    raise ValueError("embeddings are not served by this front end")
+                vecs = await srv.aengine.call(lambda eng: eng.embed(batch))
+            except ValueError as e:
+                return _err(400, str(e))
+            except NotImplementedError as e:
+                return _err(400, str(e))
+            except Exception as e:  # engine failure
+                return _err(500, f"{type(e).__name__}: {e}", "server_error")
+            n_tok = sum(len(b) for b in batch)
+            return JSONResponse({"object": "list", "model": body.get("model") or srv.model_id,
+                                 "data": [{"object": "embedding", "index": i, "embedding": v.tolist()}
+                                          for i, v in enumerate(vecs)],
+                                 "usage": {"prompt_tokens": n_tok, "total_tokens": n_tok}}, headers=CORS)
 
         @app.post("/v1/completions")
         async def completions(request: Request):

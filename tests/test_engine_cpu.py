@@ -245,3 +245,40 @@ def test_prefill_arrays_match_per_token_construction():
         assert ids.tolist() == want_ids and pos.tolist() == want_pos and slots.tolist() == want_slots
         assert qs.tolist() == [0] + list(np.cumsum(n_new)) and last.tolist() == [q - 1 for q in qs.tolist()[1:]]
         assert e_rows == want_rows and lens.tolist() == [s.n_cached + n for s, n in zip(seqs, n_new)]
+
+
+def test_embed_gpu_plumbing_with_stub_runner():
+    """The GPU engine's embedding path (chunked prefill on borrowed pages, hidden-row tap, output norm,
+    mean pooling) driven by a stub runner on CPU tensors: pages go back to the pool, chunking does not
+    change the result, StepInputs carry consistent positions and slots."""
+    import types
+
+    from barq_inference_b200.engine.embeddings import embed_gpu
+    from barq_inference_b200.models.runner import LlamaRunner
+
+    H = 8
+    seen = []
+
+    def fwd(inp):
+        seen.append((inp.pos.tolist(), inp.slots.tolist(), inp.block_tables.tolist()))
+        ids = inp.ids.to(torch.float32)
+        inp.hidden_out.copy_(torch.stack([ids * (k + 1) + 1.0 for k in range(H)], 1))
+
+    r = LlamaRunner.__new__(LlamaRunner)
+    r.pp, r.comm, r.out_norm = None, None, torch.full((H,), 2.0)
+    r.forward = fwd
+    bm = BlockManager(16, 4)
+    res = []
+    for step in (3, 100):
+        eng = types.SimpleNamespace(runner=r, cfg=types.SimpleNamespace(hidden=H, rms_eps=1e-6), blocks=bm,
+                                    prefix_cache=None, device=torch.device("cpu"),
+                                    ecfg=types.SimpleNamespace(block_size=4, max_model_len=64, max_num_batched_tokens=step))
+        res.append(embed_gpu(eng, [[1, 2, 3, 4, 5, 6, 7], [9]]))
+        assert bm.n_used == 0
+    assert torch.allclose(res[0], res[1], atol=1e-6)
+    x = torch.stack([torch.tensor([1., 2, 3, 4, 5, 6, 7]) * (k + 1) + 1 for k in range(H)], 1)
+    h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * 2.0
+    want = h.mean(0) / h.mean(0).norm()
+    assert torch.allclose(res[1][0], want, atol=1e-6)
+    pos, slots, bt = seen[1]  # second chunk of the first prompt with step 3: positions 3..5
+    assert pos == [3, 4, 5] and slots == [bt[0][p // 4] * 4 + p % 4 for p in pos]

@@ -341,3 +341,21 @@ def test_cli_chat_and_benchmark(tmp_path):
     assert r.returncode == 0, r.stderr[-2000:]
     summary = json.loads(r.stdout.strip().splitlines()[-1])
     assert summary["batch"] == 2 and summary["decode_tok_s"] > 0 and summary["ttft_p99_ms"] >= summary["ttft_p50_ms"]
+
+
+def test_embeddings_cpu_engine_and_http(tiny_engine, client):
+    import torch
+
+    e = tiny_engine.embed([[1, 2, 3], [4, 5, 6, 7]])
+    assert e.shape == (2, tiny_engine.cfg.hidden)
+    assert torch.allclose(e.norm(dim=1), torch.ones(2), atol=1e-5)
+    h = tiny_engine.model.forward([1, 2, 3], {}, hidden=True).mean(0)
+    assert torch.allclose(e[0], h / h.norm(), atol=1e-6)
+    r = client.post("/v1/embeddings", json={"input": ["hello world", "the model"]})
+    assert r.status_code == 200, r.text
+    d = r.json()
+    assert [x["index"] for x in d["data"]] == [0, 1] and len(d["data"][0]["embedding"]) == tiny_engine.cfg.hidden
+    assert d["usage"]["prompt_tokens"] > 0
+    r = client.post("/v1/embeddings", json={"input": [[1, 2], [3]]})
+    assert r.status_code == 200 and len(r.json()["data"]) == 2
+    assert client.post("/v1/embeddings", json={"input": 5}).status_code == 400
