@@ -1,0 +1,173 @@
+"""The CUDA engine's host logic end to end on CPU: ``Engine`` (scheduler, chunked prefill, paged-KV
+slots and block tables, preemption, prefix cache, sliding-window page freeing, sampling plumbing)
+driving a paged fp32 runner that stores K/V at exactly the slots the engine hands it and attends
+through the block tables.  Its greedy tokens must follow the contiguous fp32 reference forward: a
+wrong slot, position or block table shows up as different logits."""
+import dataclasses
+
+import pytest
+import torch
+
+import barq_inference_b200.engine.engine as engine_mod
+from barq_inference_b200.engine.engine import Engine, EngineConfig
+from barq_inference_b200.engine.sampling_params import SamplingParams
+from barq_inference_b200.models import POLICIES, preset, random_tensors
+from barq_inference_b200.models.reference import ReferenceModel, rms_norm
+from barq_inference_b200.models.rope import apply_rope_ref
+
+
+class PagedRefRunner:
+    """fp32 forward over a paged K/V store, following the reference model's math."""
+
+    def __init__(self, cfg, tensors):
+        self.cfg = cfg
+        self.ref = ReferenceModel(cfg, tensors)
+        self.w = self.ref.w
+
+    def kv_bytes_per_block(self, block_size=16):
+        c = self.cfg
+        return c.n_layers * 2 * c.n_kv_heads * block_size * c.head_dim * 4
+
+    def allocate_kv(self, num_blocks, block_size=16):
+        c = self.cfg
+        self.bs = block_size
+        self.kc = torch.full((c.n_layers, num_blocks * block_size, c.n_kv_heads, c.head_dim), float("nan"))
+        self.vc = torch.full_like(self.kc, float("nan"))  # unwritten slots are NaN: reading one poisons logits
+        return None
+
+    def forward(self, inp):
+        cfg, w, ref = self.cfg, self.w, self.ref
+        ids = inp.ids.long()
+        pos = inp.pos.long()
+        slots = inp.slots.long()
+        T = ids.numel()
+        S = inp.seq_lens.numel()
+        if inp.decode:
+            rows = [(s, s + 1) for s in range(S)]
+        else:
+            qs = inp.q_start.tolist()
+            rows = [(qs[s], qs[s + 1]) for s in range(S)]
+        x = w["token_embd.weight"][ids]
+        cos, sin = ref.cos[pos], ref.sin[pos]
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            h = rms_norm(x, w[p + "attn_norm.weight"], cfg.rms_eps)
+            q = (h @ w[p + "attn_q.weight"].T).view(T, cfg.n_heads, cfg.head_dim)
+            k = (h @ w[p + "attn_k.weight"].T).view(T, cfg.n_kv_heads, cfg.head_dim)
+            v = (h @ w[p + "attn_v.weight"].T).view(T, cfg.n_kv_heads, cfg.head_dim)
+            r = cfg.rot_dim
+            q = torch.cat([apply_rope_ref(q[..., :r], cos, sin, cfg.rope_neox), q[..., r:]], -1)
+            k = torch.cat([apply_rope_ref(k[..., :r], cos, sin, cfg.rope_neox), k[..., r:]], -1)
+            self.kc[i, slots] = k
+            self.vc[i, slots] = v
+            o = torch.empty(T, cfg.n_heads, cfg.head_dim)
+            for s, (a, b) in enumerate(rows):
+                L = int(inp.seq_lens[s])
+                kp = torch.arange(L)
+                if cfg.sliding_window:  # only positions some query of the chunk can attend to are read
+                    kp = kp[kp >= int(pos[a]) - cfg.sliding_window + 1]
+                bt = inp.block_tables[s].long()
+                ks = bt[kp // self.bs] * self.bs + kp % self.bs
+                kk, vv = self.kc[i, ks], self.vc[i, ks]
+                qpos = pos[a:b][:, None]
+                rep = cfg.n_heads // cfg.n_kv_heads
+                kk, vv = kk.repeat_interleave(rep, 1), vv.repeat_interleave(rep, 1)
+                sc = torch.einsum("thd,shd->hts", q[a:b], kk) * ref.scale
+                mask = kp[None, :] > qpos
+                if cfg.sliding_window:
+                    mask |= kp[None, :] <= qpos - cfg.sliding_window
+                sc = sc.masked_fill(mask[None], float("-inf"))
+                o[a:b] = torch.einsum("hts,shd->thd", torch.softmax(sc, -1), vv)
+            x = x + o.reshape(T, -1) @ w[p + "attn_output.weight"].T
+            h = rms_norm(x, w[p + "ffn_norm.weight"], cfg.rms_eps)
+            x = x + (ref._moe(h, p) if cfg.layer_is_moe(i) else ref._ffn(h, p))
+        xl = x[inp.last_idx.long()] if not inp.decode else x
+        xl = rms_norm(xl, w["output_norm.weight"], cfg.rms_eps)
+        return xl @ w.get("output.weight", w["token_embd.weight"]).T
+
+
+def _greedy_sample(logits, temp, topk, topp, minp, seeds, steps, allow_mask=None, penalties=None, history=None,
+                   want_logprob=False):
+    lg = logits.float().clone()
+    if allow_mask is not None:
+        bits = ((allow_mask.view(torch.int32).long()[:, :, None] >> torch.arange(32)) & 1).reshape(lg.shape[0], -1)
+        lg = lg.masked_fill(bits[:, : lg.shape[1]] == 0, float("-inf"))
+    return lg.argmax(-1).to(torch.int32), None
+
+
+@pytest.fixture(autouse=True)
+def _cpu_sampler(monkeypatch):
+    monkeypatch.setattr(engine_mod.ops, "sample", _greedy_sample)
+
+
+def _follows_reference(ref: ReferenceModel, prompt, tokens, tol=1e-3):
+    """True if ``tokens`` is the reference's greedy continuation, allowing a switch only where the
+    reference's top two logits are within ``tol`` (a near-tie that rounding may flip)."""
+    cache: dict = {}
+    logits = ref.forward(prompt, cache)[-1]
+    for t in tokens:
+        best = int(logits.argmax())
+        if t != best:
+            return bool(logits[best] - logits[t] < tol)
+        logits = ref.forward([t], cache)[-1]
+    return True
+
+
+def _engine(cfg, tensors, **kw):
+    ec = EngineConfig(device="cpu", cuda_graphs=False, max_model_len=256, **kw)
+    return Engine(cfg, tensors, ec, runner=PagedRefRunner(cfg, tensors))
+
+
+def _prompts(cfg, n, seed, lo=5, hi=70, shared=0):
+    g = torch.Generator().manual_seed(seed)
+    base = torch.randint(0, cfg.vocab, (shared,), generator=g).tolist()
+    return [base + torch.randint(0, cfg.vocab, (int(torch.randint(lo, hi, (1,), generator=g)),), generator=g).tolist()
+            for _ in range(n)]
+
+
+def test_continuous_batching_chunked_prefill_matches_reference():
+    cfg = preset("tiny", n_layers=2, vocab=500, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=0)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=24, max_num_seqs=3)
+    prompts = _prompts(cfg, 5, 1)
+    res = eng.generate(prompts, SamplingParams.greedy_params(max_tokens=12))
+    for p, r in zip(prompts, res):
+        assert len(r.tokens) == 12 and _follows_reference(ref, p, r.tokens)
+
+
+def test_preemption_under_a_small_pool_matches_reference():
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=2)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=12, max_num_batched_tokens=64, max_num_seqs=4)
+    prompts = _prompts(cfg, 4, 3, lo=30, hi=50)
+    res = eng.generate(prompts, SamplingParams.greedy_params(max_tokens=30))
+    assert eng.sched.n_preemptions > 0
+    for p, r in zip(prompts, res):
+        assert len(r.tokens) == 30 and _follows_reference(ref, p, r.tokens)
+
+
+def test_prefix_cache_reuse_matches_reference():
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=4)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=128, max_num_seqs=4, prefix_caching=True)
+    prompts = _prompts(cfg, 4, 5, lo=3, hi=10, shared=40)
+    first = eng.generate(prompts[:1], SamplingParams.greedy_params(max_tokens=6))
+    rest = eng.generate(prompts[1:], SamplingParams.greedy_params(max_tokens=6))
+    assert eng.prefix_cache.hits >= 3
+    for p, r in zip(prompts, first + rest):
+        assert _follows_reference(ref, p, r.tokens)
+
+
+def test_sliding_window_page_freeing_matches_reference():
+    cfg = dataclasses.replace(preset("tiny", n_layers=1, vocab=400, max_ctx=256), sliding_window=24)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=6)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=20, max_num_batched_tokens=16, max_num_seqs=2)
+    prompts = _prompts(cfg, 2, 7, lo=40, hi=60)
+    res = eng.generate(prompts, SamplingParams.greedy_params(max_tokens=60))
+    assert eng.sched.n_window_freed > 0
+    for p, r in zip(prompts, res):
+        assert _follows_reference(ref, p, r.tokens)
