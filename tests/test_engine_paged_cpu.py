@@ -33,7 +33,10 @@ class PagedRefRunner:
         self.bs = block_size
         self.kc = torch.full((c.n_layers, num_blocks * block_size, c.n_kv_heads, c.head_dim), float("nan"))
         self.vc = torch.full_like(self.kc, float("nan"))  # unwritten slots are NaN: reading one poisons logits
-        return None
+        # the device runner's page layout [blocks, kv heads, block_size, head_dim], as strided views
+        pages = lambda t: t.view(num_blocks, block_size, c.n_kv_heads, c.head_dim).permute(0, 2, 1, 3)  # noqa: E731
+        self.kv = [(pages(self.kc[i]), pages(self.vc[i])) for i in range(c.n_layers)]
+        return self.kv
 
     def forward(self, inp):
         cfg, w, ref = self.cfg, self.w, self.ref
@@ -47,7 +50,9 @@ class PagedRefRunner:
         else:
             qs = inp.q_start.tolist()
             rows = [(qs[s], qs[s + 1]) for s in range(S)]
-        x = w["token_embd.weight"][ids]
+        x = w["token_embd.weight"][ids].clone()
+        if inp.embed_rows is not None and inp.embed_rows.numel():  # multimodal rows
+            x[inp.embed_rows.long()] = inp.embed_vals.float()
         cos, sin = ref.cos[pos], ref.sin[pos]
         for i in range(cfg.n_layers):
             p = f"blk.{i}."
@@ -171,3 +176,59 @@ def test_sliding_window_page_freeing_matches_reference():
     assert eng.sched.n_window_freed > 0
     for p, r in zip(prompts, res):
         assert _follows_reference(ref, p, r.tokens)
+
+
+def test_kv_session_export_import_through_the_engine(tmp_path):
+    from barq_inference_b200.engine.session import export_session, import_session
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=8)
+    ref = ReferenceModel(cfg, t)
+    system = _prompts(cfg, 1, 9, lo=40, hi=41)[0]
+    a = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=128, prefix_caching=True)
+    path = str(tmp_path / "s.pt")
+    st = export_session(a, system, path)
+    assert st["tokens"].numel() == 32  # whole pages of the cached prefix
+    b = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=128, prefix_caching=True)
+    assert import_session(b, path) == 32
+    prompt = system + [7, 8, 9]
+    r = b.generate([prompt], SamplingParams.greedy_params(max_tokens=8))[0]
+    assert b.prefix_cache.hits >= 1 and b.timings["prefill_tokens"] == len(prompt) - 32
+    assert _follows_reference(ref, prompt, r.tokens)
+
+
+def test_multimodal_embedding_rows_through_the_engine():
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=10)
+    ref = ReferenceModel(cfg, t)
+    prompt = _prompts(cfg, 1, 11, lo=30, hi=31)[0]
+    rows = torch.randn(6, cfg.hidden, generator=torch.Generator().manual_seed(12)) * 0.5
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=16)  # the image rows straddle two chunks
+    seq = eng.add_request(prompt, SamplingParams.greedy_params(max_tokens=6), embeds=(12, rows))
+    while eng.has_work():
+        eng.step()
+    cache: dict = {}
+    logits = ref.forward(prompt, cache, embeds=(12, rows))[-1]
+    for tok in seq.output:
+        best = int(logits.argmax())
+        assert tok == best or logits[best] - logits[tok] < 1e-3
+        if tok != best:
+            break
+        logits = ref.forward([tok], cache)[-1]
+
+
+def test_json_mode_mask_plumbing_through_the_engine():
+    import json as _json
+
+    from barq_inference_b200.tokenizer.gguf_tokenizer import synthetic_tokenizer
+
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=12)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=64)
+    eng.tokenizer = synthetic_tokenizer(cfg.vocab)
+    r = eng.generate([[1, 5, 9]], SamplingParams(max_tokens=64, temperature=0.0, json_mode=True))[0]
+    text = eng.tokenizer.decode([x for x in r.tokens if x not in cfg.eos_ids])
+    if r.finish_reason == "stop":
+        _json.loads(text)
+    else:  # ran out of tokens: still a valid JSON prefix under the grammar
+        assert text.lstrip().startswith("{")
