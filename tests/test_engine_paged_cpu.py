@@ -232,3 +232,24 @@ def test_json_mode_mask_plumbing_through_the_engine():
         _json.loads(text)
     else:  # ran out of tokens: still a valid JSON prefix under the grammar
         assert text.lstrip().startswith("{")
+
+
+@pytest.mark.parametrize("same_draft", [True, False])
+def test_speculative_greedy_follows_target_reference(same_draft):
+    """Speculative decoding through the real engines' paged state: greedy output is the target's
+    greedy continuation whatever the draft; an identical draft is (almost) always accepted."""
+    from barq_inference_b200.engine.speculative import SpeculativeConfig, SpeculativeDecoder
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=13)
+    d = t if same_draft else random_tensors(cfg, POLICIES["tiny"], seed=14)
+    ref = ReferenceModel(cfg, t)
+    target = _engine(cfg, t, num_blocks=64)
+    draft = _engine(cfg, d, num_blocks=64)
+    prompt = _prompts(cfg, 1, 15, lo=20, hi=21)[0]
+    res = SpeculativeDecoder(target, draft, SpeculativeConfig(4)).generate(
+        prompt, SamplingParams.greedy_params(max_tokens=20))
+    assert len(res.tokens) == 20 and _follows_reference(ref, prompt, res.tokens)
+    if same_draft:
+        assert res.acceptance_rate > 0.9
+    assert target.blocks.n_used == 1 and draft.blocks.n_used == 1  # pages released (dummy page only)
