@@ -253,3 +253,31 @@ def test_speculative_greedy_follows_target_reference(same_draft):
     if same_draft:
         assert res.acceptance_rate > 0.9
     assert target.blocks.n_used == 1 and draft.blocks.n_used == 1  # pages released (dummy page only)
+
+
+def test_openai_server_over_the_engine():
+    """The HTTP server with the CUDA engine's host side (AsyncEngine thread, KV gauges, health)."""
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.server.openai_api import OpenAIServer
+    from barq_inference_b200.tokenizer.gguf_tokenizer import synthetic_tokenizer
+
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=16)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=64)
+    tok = synthetic_tokenizer(cfg.vocab)
+    eng.tokenizer = tok
+    srv = OpenAIServer(eng, tok)
+    try:
+        c = TestClient(srv.app)
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hello"}],
+                                                  "max_tokens": 5, "temperature": 0})
+        assert r.status_code == 200 and r.json()["choices"][0]["finish_reason"] in ("length", "stop")
+        with c.stream("POST", "/v1/completions", json={"prompt": "the model", "max_tokens": 4, "stream": True}) as s:
+            assert [ln for ln in s.iter_lines() if ln.startswith("data: ")][-1] == "data: [DONE]"
+        h = c.get("/health").json()
+        assert h["status"] == "ok" and 0 <= h["kv_usage"] <= 1
+        m = c.get("/metrics").text
+        assert "barq_kv_blocks_total 64" in m and "barq_requests_successful 2" in m
+    finally:
+        srv.aengine.shutdown()
