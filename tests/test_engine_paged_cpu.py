@@ -281,3 +281,35 @@ def test_openai_server_over_the_engine():
         assert "barq_kv_blocks_total 64" in m and "barq_requests_successful 2" in m
     finally:
         srv.aengine.shutdown()
+
+
+def test_engine_step_failure_fails_in_flight_requests_and_recovers():
+    """A step that raises (injected on the host, no device involved) fails the requests in flight;
+    the engine thread keeps serving and the next request completes."""
+    from barq_inference_b200.server.async_engine import AsyncEngine
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=17)
+    eng = _engine(cfg, t, num_blocks=64)
+    real = eng.runner.forward
+    calls = {"n": 0}
+
+    def flaky(inp):
+        calls["n"] += 1
+        if calls["n"] == 2:
+            raise RuntimeError("injected step failure")
+        return real(inp)
+
+    eng.runner.forward = flaky
+    ae = AsyncEngine(eng)
+    try:
+        p = SamplingParams.greedy_params(max_tokens=5)
+        items = list(ae.generate_blocking([1, 2, 3], p, timeout=60))
+        assert items[-1].token is None and items[-1].finish_reason == "error"
+        assert not ae.healthy and "injected" in ae.last_error
+        assert eng.blocks.n_used == 1  # the failed sequence's pages went back to the pool
+        items = list(ae.generate_blocking([4, 5, 6], p, timeout=60))
+        assert [i.token is not None for i in items].count(True) == 5 and items[-1].finish_reason == "length"
+        assert ae.healthy
+    finally:
+        ae.shutdown()
