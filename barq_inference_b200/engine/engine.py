@@ -27,7 +27,7 @@ from ..models.runner import LlamaRunner, StepInput
 from .kv_cache import BlockManager
 from .scheduler import ScheduledStep, Scheduler, SchedulerConfig
 from .sampling_params import SamplingParams
-from .sequence import Sequence, SeqStatus
+from .sequence import Sequence
 
 
 @dataclass

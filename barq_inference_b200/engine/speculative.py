@@ -14,9 +14,8 @@ target's argmax agrees, so their output is identical to plain greedy decoding.
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
-import numpy as np
 import torch
 
 from ..models.runner import StepInput

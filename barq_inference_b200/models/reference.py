@@ -9,7 +9,6 @@ CUDA path is checked against it.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 import torch

@@ -19,7 +19,6 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
-from ..gguf import GGMLType
 from ..ops import EPI_ADD_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU_Q8, Q8Act, QWeight
 from .config import ModelConfig
 from .rope import attn_scale, rope_cos_sin

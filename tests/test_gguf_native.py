@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from barq_inference_b200.gguf import GGMLType, GGUFError, GGUFValueType, GGUFWriter, quantize, read_gguf
+from barq_inference_b200.gguf import GGMLType, GGUFValueType, GGUFWriter, quantize, read_gguf
 
 nat = pytest.importorskip("barq_inference_b200._native")
 

@@ -47,7 +47,8 @@ def test_silent_rank_times_out_and_epochs_stay_aligned():
 
     def rank_fn(r, rng):
         x = np.zeros((B, N), np.float32)
-        fab.push_allreduce(r, 0, p1[r], x, wait_s=0.2, skip_signal=(r == 2))
+        # the silent rank waits longer: its peers' later tiles only come after their own timeouts
+        fab.push_allreduce(r, 0, p1[r], x, wait_s=0.2 if r != 2 else 3.0, skip_signal=(r == 2))
         after1 = x.copy()
         err1 = fab.err[r]
         fab.err[r] = 0

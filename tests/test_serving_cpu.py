@@ -5,8 +5,6 @@ import os
 import socket
 import subprocess
 import sys
-import threading
-import time
 
 import pytest
 import torch
