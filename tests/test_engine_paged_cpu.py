@@ -313,3 +313,38 @@ def test_engine_step_failure_fails_in_flight_requests_and_recovers():
         assert ae.healthy
     finally:
         ae.shutdown()
+
+
+def test_decode_graph_path_host_side_matches_reference():
+    """The CUDA-graph decode path without the graph: packed per-step inputs (incremental
+    ``_Packed.fill``), padding rows, bucket sizes and the captured forward run eagerly on CPU."""
+    import types
+
+    from barq_inference_b200.engine.engine import _GraphBucket, _Packed
+
+    class GraphOnCPU(Engine):
+        def _run_decode(self, plan):
+            B = next(b for b in self.ecfg.graph_buckets if b >= len(plan.seqs))
+            return self._decode_graph(plan.seqs, B)
+
+        def _capture(self, B):
+            pk = _Packed(B, self.max_blocks_per_seq, self.device)
+            gb = _GraphBucket()
+            gb.B, gb.packed = B, pk
+            gb.out_ids = torch.zeros(B, dtype=torch.int32)
+            gb.graph = types.SimpleNamespace(replay=lambda: gb.out_ids.copy_(self._graph_forward(pk)))
+            self.captured = getattr(self, "captured", 0) + 1
+            return gb
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=18)
+    ref = ReferenceModel(cfg, t)
+    ec = EngineConfig(device="cpu", cuda_graphs=True, max_model_len=256, num_blocks=96, max_num_batched_tokens=48,
+                      max_num_seqs=6, graph_buckets=(1, 2, 4, 8))
+    eng = GraphOnCPU(cfg, t, ec, runner=PagedRefRunner(cfg, t))
+    prompts = _prompts(cfg, 6, 19, lo=5, hi=40)
+    params = [SamplingParams.greedy_params(max_tokens=n) for n in (3, 9, 17, 25, 6, 12)]  # rows leave at different steps
+    res = eng.generate(prompts, params)
+    assert eng.captured >= 3  # several buckets used as the batch shrinks
+    for p, r, sp in zip(prompts, res, params):
+        assert len(r.tokens) == sp.max_tokens and _follows_reference(ref, p, r.tokens)
