@@ -315,9 +315,11 @@ def test_engine_step_failure_fails_in_flight_requests_and_recovers():
         ae.shutdown()
 
 
-def test_decode_graph_path_host_side_matches_reference():
+@pytest.mark.parametrize("window", [0, 24])
+def test_decode_graph_path_host_side_matches_reference(window):
     """The CUDA-graph decode path without the graph: packed per-step inputs (incremental
-    ``_Packed.fill``), padding rows, bucket sizes and the captured forward run eagerly on CPU."""
+    ``_Packed.fill``, rewritten rows after window trimming), padding rows, bucket sizes and the
+    captured forward run eagerly on CPU."""
     import types
 
     from barq_inference_b200.engine.engine import _GraphBucket, _Packed
@@ -336,7 +338,7 @@ def test_decode_graph_path_host_side_matches_reference():
             self.captured = getattr(self, "captured", 0) + 1
             return gb
 
-    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    cfg = dataclasses.replace(preset("tiny", n_layers=1, vocab=400, max_ctx=256), sliding_window=window)
     t = random_tensors(cfg, POLICIES["tiny"], seed=18)
     ref = ReferenceModel(cfg, t)
     ec = EngineConfig(device="cpu", cuda_graphs=True, max_model_len=256, num_blocks=96, max_num_batched_tokens=48,
@@ -346,5 +348,6 @@ def test_decode_graph_path_host_side_matches_reference():
     params = [SamplingParams.greedy_params(max_tokens=n) for n in (3, 9, 17, 25, 6, 12)]  # rows leave at different steps
     res = eng.generate(prompts, params)
     assert eng.captured >= 3  # several buckets used as the batch shrinks
+    assert (eng.sched.n_window_freed > 0) == bool(window)
     for p, r, sp in zip(prompts, res, params):
         assert len(r.tokens) == sp.max_tokens and _follows_reference(ref, p, r.tokens)
