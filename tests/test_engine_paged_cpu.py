@@ -351,3 +351,28 @@ def test_decode_graph_path_host_side_matches_reference(window):
     assert (eng.sched.n_window_freed > 0) == bool(window)
     for p, r, sp in zip(prompts, res, params):
         assert len(r.tokens) == sp.max_tokens and _follows_reference(ref, p, r.tokens)
+
+
+@pytest.mark.parametrize("kind", ["engine", "cpu"])
+def test_model_context_encode_decode_truncate(kind):
+    from barq_inference_b200.engine.context import ModelContext
+    from barq_inference_b200.engine.cpu_engine import CPUEngine
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=20)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=32) if kind == "engine" else CPUEngine(cfg, t, max_model_len=256)
+    prompt = _prompts(cfg, 1, 21, lo=20, hi=21)[0]
+    want = ref.forward(prompt)
+    with ModelContext(eng) as ctx:
+        allg = ctx.encode(prompt, all_logits=True)
+        assert allg.shape == (len(prompt), cfg.vocab) and (allg - want).abs().max() < 1e-3
+        tok = ctx.sample(allg[-1:], temperature=0.0)
+        assert tok == int(want[-1].argmax())
+        lg = ctx.decode(tok)
+        assert (lg[0] - ref.forward(prompt + [tok])[-1]).abs().max() < 1e-3
+        ctx.truncate(10)  # roll back and continue differently
+        lg = ctx.encode([5, 6])
+        assert (lg[0] - ref.forward(prompt[:10] + [5, 6])[-1]).abs().max() < 1e-3 and ctx.n_past == 12
+    if kind == "engine":
+        assert eng.blocks.n_used == 1  # pages returned
