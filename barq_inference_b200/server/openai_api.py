@@ -7,7 +7,8 @@ top_p 0.95), ``/v1/responses`` accepting ``input`` / ``prompt`` / ``messages`` a
 ``max_output_tokens``, ids ``cmpl-`` / ``chatcmpl-`` / ``resp-<unix ts>``, SSE chunk objects
 ``text_completion.chunk``, ``chat.completion.chunk`` (role delta first) and ``response.chunk``,
 ``data: [DONE]``.  Added: ``/health``, ``/metrics`` (Prometheus), ``response_format`` JSON mode /
-JSON schema, ``grammar`` (GBNF), ``stop``, ``seed``, ``n`` choices, ``stream_options.include_usage``,
+JSON schema, ``grammar`` (GBNF), ``tools`` / ``tool_choice`` (function calls constrained by the
+tools' parameter schemas), ``stop``, ``seed``, ``n`` choices, ``stream_options.include_usage``,
 per-request log lines with ``x-request-id``, 503 from admission control, and continuous batching
 across concurrent requests.
 """
@@ -89,6 +90,62 @@ def _params(body: dict, max_key: str = "max_tokens") -> SamplingParams:
     if body.get("grammar"):
         p.grammar = str(body["grammar"])
     return p
+
+
+def _tool_setup(body: dict) -> dict | None:
+    """OpenAI ``tools`` / ``tool_choice``: a system prompt describing the functions, and (when a call
+    is required or a function is named) a JSON schema that constrains the reply to
+    ``{"name": ..., "arguments": {...}}`` for one of them."""
+    tools = body.get("tools")
+    if not tools:
+        return None
+    if not isinstance(tools, list):
+        raise ValueError("tools must be a list")
+    fns = []
+    for t in tools:
+        f = t.get("function", t) if isinstance(t, dict) else None
+        if not isinstance(f, dict) or not f.get("name"):
+            raise ValueError("each tool needs a function with a name")
+        fns.append(f)
+    choice = body.get("tool_choice", "auto")
+    if choice == "none":
+        return None
+    if isinstance(choice, dict):
+        name = (choice.get("function") or {}).get("name")
+        fns_c = [f for f in fns if f["name"] == name]
+        if not fns_c:
+            raise ValueError(f"tool_choice names an unknown function {name!r}")
+    else:
+        fns_c = fns
+    forced = choice == "required" or isinstance(choice, dict)
+    schema = None
+    if forced:
+        alts = [{"type": "object", "properties": {"name": {"const": f["name"]},
+                                                  "arguments": f.get("parameters") or {"type": "object"}},
+                 "required": ["name", "arguments"]} for f in fns_c]
+        schema = alts[0] if len(alts) == 1 else {"anyOf": alts}
+    desc = json.dumps([{"name": f["name"], "description": f.get("description", ""),
+                        "parameters": f.get("parameters", {})} for f in fns])
+    prompt = ("You can call these functions. To call one, reply with only a JSON object "
+              '{"name": <function name>, "arguments": <arguments object>}.\nFunctions: ' + desc)
+    return {"prompt": prompt, "schema": schema, "names": {f["name"] for f in fns}}
+
+
+def _tool_calls(out: dict, body: dict) -> None:
+    """Turn chat choices whose text is a function-call object into OpenAI ``tool_calls``."""
+    names = {(t.get("function", t) or {}).get("name") for t in body.get("tools") or [] if isinstance(t, dict)}
+    for i, ch in enumerate(out.get("choices", [])):
+        text = (ch.get("message") or {}).get("content") or ""
+        try:
+            obj = json.loads(text)
+        except ValueError:
+            continue
+        if isinstance(obj, dict) and obj.get("name") in names and isinstance(obj.get("arguments"), dict):
+            ch["message"] = {"role": "assistant", "content": None,
+                             "tool_calls": [{"id": f"call_{out['id']}_{i}", "type": "function",
+                                             "function": {"name": obj["name"],
+                                                          "arguments": json.dumps(obj["arguments"])}}]}
+            ch["finish_reason"] = "tool_calls"
 
 
 class OpenAIServer:
@@ -264,10 +321,19 @@ class OpenAIServer:
     def _chat_prompt(self, messages: Any) -> list[int]:
         if not isinstance(messages, list) or not messages:
             raise ValueError("messages must be a non-empty list")
+        msgs = []
         for m in messages:
-            if not isinstance(m, dict) or "content" not in m:
+            if not isinstance(m, dict) or ("content" not in m and "tool_calls" not in m):
                 raise ValueError("each message needs role and content")
-        text = self.template.render(messages, add_generation_prompt=True)
+            m = dict(m)
+            if m.get("content") is None and m.get("tool_calls"):  # an earlier assistant tool call
+                m["content"] = json.dumps([c.get("function", c) for c in m["tool_calls"]])
+            if m.get("role") == "tool":  # a tool's result goes back to the model as a user turn
+                m = {"role": "user", "content": f"Tool result ({m.get('name') or m.get('tool_call_id', 'tool')}): "
+                                                f"{m.get('content', '')}"}
+            m["content"] = m.get("content") or ""
+            msgs.append(m)
+        text = self.template.render(msgs, add_generation_prompt=True)
         return self.tok.encode(text, add_special=not text.startswith(getattr(self.template, "bos_token", "") or "\0"))
 
     # ------------------------------------------------------------------ app
@@ -338,8 +404,14 @@ class OpenAIServer:
                         raise ValueError("prompt must be a string or a list of token ids")
                     params = _params(body)
                 elif kind == "chat":
-                    ids = srv._chat_prompt(body.get("messages"))
+                    tools = _tool_setup(body)
+                    msgs = body.get("messages")
+                    if tools is not None and isinstance(msgs, list):
+                        msgs = [{"role": "system", "content": tools["prompt"]}] + list(msgs)
+                    ids = srv._chat_prompt(msgs)
                     params = _params(body)
+                    if tools is not None and tools["schema"] is not None:  # a tool call is required
+                        params.json_schema, params.json_mode = tools["schema"], True
                 else:
                     if body.get("messages") is not None:
                         ids = srv._chat_prompt(body["messages"])
@@ -359,10 +431,15 @@ class OpenAIServer:
                 if body.get("stream"):
                     if n_choices > 1:
                         raise ValueError("n > 1 is not supported with stream")
+                    if kind == "chat" and body.get("tools"):
+                        raise ValueError("stream with tools is not supported; send stream=false")
                     so = body.get("stream_options") or {}
                     inc = bool(so.get("include_usage")) if isinstance(so, dict) else False
                     return srv._sse(srv._stream(ids, params, stops, kind, model, include_usage=inc))
-                return JSONResponse(await srv._complete(ids, params, stops, kind, model, n_choices))
+                out = await srv._complete(ids, params, stops, kind, model, n_choices)
+                if kind == "chat" and body.get("tools"):
+                    _tool_calls(out, body)
+                return JSONResponse(out)
             except ValueError as e:
                 return _err(400, str(e))
             except Overloaded as e:  # admission control: queue full

@@ -357,3 +357,41 @@ def test_embeddings_cpu_engine_and_http(tiny_engine, client):
     r = client.post("/v1/embeddings", json={"input": [[1, 2], [3]]})
     assert r.status_code == 200 and len(r.json()["data"]) == 2
     assert client.post("/v1/embeddings", json={"input": 5}).status_code == 400
+
+
+def test_chat_tool_calls():
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.server.openai_api import OpenAIServer
+
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=2048)  # room for the tool description prompt
+    eng = CPUEngine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=0), max_model_len=2048)
+    eng.tokenizer = synthetic_tokenizer(cfg.vocab)
+    srv = OpenAIServer(eng, eng.tokenizer, chat_template=ChatTemplate("chatml"))
+    client = TestClient(srv.app)
+    tools = [{"type": "function", "function": {"name": "get_weather", "description": "weather for a city",
+                                                "parameters": {"type": "object",
+                                                               "properties": {"city": {"type": "string"}},
+                                                               "required": ["city"]}}}]
+    body = {"messages": [{"role": "user", "content": "weather in Paris?"}], "tools": tools, "max_tokens": 60,
+            "tool_choice": {"type": "function", "function": {"name": "get_weather"}}, "temperature": 0.7, "seed": 2}
+    r = client.post("/v1/chat/completions", json=body)
+    assert r.status_code == 200, r.text
+    ch = r.json()["choices"][0]
+    if ch["finish_reason"] == "tool_calls":  # completed within max_tokens: a well-formed call
+        call = ch["message"]["tool_calls"][0]
+        assert call["function"]["name"] == "get_weather" and "city" in json.loads(call["function"]["arguments"])
+    else:  # cut by max_tokens: still the prefix of a call
+        assert ch["message"]["content"].lstrip().startswith("{")
+    # the tool result goes back as a message; an assistant turn with tool_calls and no content is accepted
+    body2 = {"messages": [{"role": "user", "content": "weather in Paris?"},
+                          {"role": "assistant", "content": None,
+                           "tool_calls": [{"id": "c1", "type": "function",
+                                           "function": {"name": "get_weather", "arguments": "{\"city\": \"Paris\"}"}}]},
+                          {"role": "tool", "tool_call_id": "c1", "content": "sunny"}],
+             "tools": tools, "max_tokens": 5}
+    assert client.post("/v1/chat/completions", json=body2).status_code == 200
+    bad = dict(body, tool_choice={"type": "function", "function": {"name": "nope"}})
+    assert client.post("/v1/chat/completions", json=bad).status_code == 400
+    assert client.post("/v1/chat/completions", json=dict(body, stream=True)).status_code == 400
+    srv.aengine.shutdown()
