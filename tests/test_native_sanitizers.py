@@ -1,0 +1,110 @@
+"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer) built with
+AddressSanitizer + UndefinedBehaviorSanitizer and driven with fuzzed and random inputs, CPU only.
+
+compute-sanitizer is not available for the device code on this pool; the host-side native code gets
+ASan/UBSan instead.  The build takes a minute or two, so the test runs when ``BARQ_SANITIZE=1``:
+
+    BARQ_SANITIZE=1 python -m pytest tests/test_native_sanitizers.py -q
+"""
+import os
+import shutil
+import subprocess
+import sys
+import textwrap
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+DRIVER = textwrap.dedent(r'''
+    import os, random, sys, tempfile
+    import numpy as np
+    import torch
+    from torch.utils.cpp_extension import load
+
+    root = sys.argv[1]
+    flags = ["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined", "-fno-sanitize-recover=undefined",
+             "-std=c++17"]
+    nat = load(name="_native_asan", sources=[os.path.join(root, "csrc/native", f) for f in
+                                              ("gguf_native.cpp", "tokenizer_native.cpp", "grammar_native.cpp")],
+               extra_cflags=flags, extra_ldflags=["-fsanitize=address,undefined"],
+               build_directory=tempfile.mkdtemp(prefix="barq-asan-"), verbose=False)
+    sys.path.insert(0, root)
+    from barq_inference_b200.gguf import GGMLType, GGUFValueType, GGUFWriter, quantize
+    from barq_inference_b200.sampling.grammar import Grammar
+    from barq_inference_b200.sampling.grammar_engine import native_rules, token_strings
+    from barq_inference_b200.sampling.json_mode import JSON_GBNF
+    from barq_inference_b200.tokenizer.gguf_tokenizer import synthetic_tokenizer
+
+    rng = random.Random(0)
+    # 1) GGUF parser on a valid file and on truncated / byte-flipped copies
+    d = tempfile.mkdtemp()
+    p = os.path.join(d, "t.gguf")
+    w = GGUFWriter(p, arch="llama")
+    w.add("s", "héllo"); w.add("arr_s", ["a", "bb"]); w.add("long", np.arange(500, dtype=np.float32))
+    w.add("nested", [[1, 2], [3]], GGUFValueType.ARRAY, GGUFValueType.ARRAY)
+    w.add_tensor("w", quantize(torch.randn(4, 256), GGMLType.Q4_K).numpy(), GGMLType.Q4_K, (4, 256))
+    w.write()
+    raw = open(p, "rb").read()
+    nat.gguf_parse(p)
+    q = os.path.join(d, "f.gguf")
+    n_bad = 0
+    for i in range(2000):
+        b = bytearray(raw[: rng.randint(24, len(raw))] if i % 3 == 0 else raw)
+        for _ in range(rng.randint(1, 6)):
+            b[rng.randrange(min(len(b), 600))] = rng.randrange(256)
+        open(q, "wb").write(bytes(b))
+        try:
+            nat.gguf_parse(q)
+        except (ValueError, OverflowError, MemoryError):
+            n_bad += 1
+        try:
+            nat.gguf_parse_bytes(bytes(b))
+        except (ValueError, OverflowError, MemoryError):
+            pass
+    # 2) tokenizer merge loops on random multilingual text
+    tok = synthetic_tokenizer(3000)
+    t = nat.NativeTokenizer(list(tok.tokens), [float(x) for x in tok.scores], [], [tok.byte_tokens.get(i, -1) for i in range(256)], 0)
+    alphabet = list("abcdefgh ijkl  ,.!") + ["é", "中", "😀", "▁"]
+    for _ in range(500):
+        s = "".join(rng.choice(alphabet) for _ in range(rng.randint(0, 80)))
+        t.spm(s.replace(" ", "▁"))
+    bt = nat.NativeTokenizer(["a", "b", "ab", "abc", "c", "Ġ"], [0.0] * 6, ["a b", "ab c", "Ġ a", "x"], [-1] * 256, 0)
+    for _ in range(500):
+        bt.bpe(["".join(rng.choice("abcĠ") for _ in range(rng.randint(0, 20))) for _ in range(5)])
+    # 3) grammar recognizer: random token walks under the JSON grammar
+    strs = token_strings(tok, 3000)
+    g = Grammar(JSON_GBNF)
+    ng, trie = nat.NativeGrammar(native_rules(g), g.root), nat.NativeTrie(strs)
+    for _ in range(20):
+        m = nat.NativeMatcher(ng, trie, [2])
+        for _ in range(30):
+            ids = m.allowed_ids()
+            if not ids:
+                break
+            m.accept(rng.choice(ids))
+            m.allowed_mask(94)
+            if m.done():
+                break
+    print("SANITIZED RUN OK", n_bad)
+''')
+
+
+@pytest.mark.skipif(os.environ.get("BARQ_SANITIZE") != "1", reason="set BARQ_SANITIZE=1 (builds with ASan/UBSan)")
+def test_native_code_under_asan_ubsan(tmp_path):
+    gxx = shutil.which("g++", path="/usr/bin") or shutil.which("g++")
+    asan = subprocess.run([gxx, "-print-file-name=libasan.so"], capture_output=True, text=True).stdout.strip()
+    ubsan = subprocess.run([gxx, "-print-file-name=libubsan.so"], capture_output=True, text=True).stdout.strip()
+    if not os.path.isabs(asan):
+        pytest.skip("no libasan for this compiler")
+    script = tmp_path / "driver.py"
+    script.write_text(DRIVER)
+    # alloc_dealloc_mismatch is off: pybind11 objects created in torch's uninstrumented libraries are
+    # freed in ours (and the reverse), which ASan reports although the pairs match
+    env = {**os.environ, "CXX": gxx, "LD_PRELOAD": f"{asan}:{ubsan}",
+           "ASAN_OPTIONS": "detect_leaks=0:abort_on_error=1:verify_asan_link_order=0:alloc_dealloc_mismatch=0",
+           "UBSAN_OPTIONS": "halt_on_error=1:print_stacktrace=1"}
+    r = subprocess.run([sys.executable, str(script), ROOT], env=env, capture_output=True, text=True, timeout=1800)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0 and "SANITIZED RUN OK" in r.stdout, out[-4000:]
+    assert "runtime error" not in out and "AddressSanitizer" not in out, out[-4000:]
