@@ -159,6 +159,8 @@ torch::Tensor qgemv(torch::Tensor raw, int64_t type, int64_t N, int64_t K, torch
   TORCH_CHECK(x.dtype() == torch::kFloat32 && x.dim() == 2 && x.size(1) == K, "x: [B, K] f32");
   int ts = type_size((int)type), be = block_elems((int)type);
   TORCH_CHECK(ts > 0 && K % be == 0, "unsupported type/shape");
+  TORCH_CHECK(raw.dtype() == torch::kUInt8 && raw.is_contiguous() && !raw.is_cuda(), "raw: contiguous CPU uint8");
+  TORCH_CHECK(N >= 0 && raw.numel() >= N * (K / be * ts), "qgemv: raw holds fewer than N rows of K values");
   auto xc = x.contiguous();
   int64_t B = x.size(0);
   auto out = torch::zeros({B, N}, torch::kFloat32);

@@ -1,4 +1,4 @@
-"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer) built with
+"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, dequant oracle) built with
 AddressSanitizer + UndefinedBehaviorSanitizer and driven with fuzzed and random inputs, CPU only.
 
 compute-sanitizer is not available for the device code on this pool; the host-side native code gets
@@ -86,6 +86,19 @@ DRIVER = textwrap.dedent(r'''
             m.allowed_mask(94)
             if m.done():
                 break
+    # 4) the C++ dequant / GEMV oracle on random blocks of every type it reads
+    ref = load(name="_cpu_ref_asan", sources=[os.path.join(root, "csrc/cpu_ref/cpu_ref.cpp")], extra_cflags=flags,
+               extra_ldflags=["-fsanitize=address,undefined"], build_directory=tempfile.mkdtemp(prefix="barq-asan-"))
+    for ty, ts, be in ((2, 18, 32), (20, 18, 32), (8, 34, 32), (12, 144, 256), (13, 176, 256), (14, 210, 256)):
+        raw = torch.randint(0, 256, (4 * 2 * ts,), dtype=torch.uint8)
+        raw.view(-1, ts)[:, :2] = torch.tensor([0x00, 0x3C], dtype=torch.uint8)  # finite fp16 scales (1.0)
+        ref.dequantize(raw, ty, 8 * be)
+        ref.qgemv(raw, ty, 4, 2 * be, torch.randn(3, 2 * be))
+        try:
+            ref.qgemv(raw[:ts], ty, 4, 2 * be, torch.randn(3, 2 * be))  # too short: must be refused
+            raise SystemExit("short raw accepted")
+        except RuntimeError:
+            pass
     print("SANITIZED RUN OK", n_bad)
 ''')
 
