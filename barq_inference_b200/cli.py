@@ -360,6 +360,27 @@ def _dp_front(args):
     return front, tok, tmpl
 
 
+def _lockstep(eng, args):
+    """Multi-rank engines (--tp / --pp under torchrun): rank 0 serves through a LockstepLeader, the
+    other ranks replay its steps and return None here once it stops."""
+    if int(getattr(args, "tp", 1) or 1) <= 1 and int(getattr(args, "pp", 1) or 1) <= 1:
+        return eng
+    import torch.distributed as dist
+    from torch.distributed.distributed_c10d import _get_default_store
+
+    from .parallel.lockstep import LockstepLeader, follower_loop
+
+    store = _get_default_store()
+    if dist.get_rank() != 0:
+        follower_loop(eng, store)
+        return None
+    lead = LockstepLeader(eng, store)
+    import atexit
+
+    atexit.register(lead.stop)
+    return lead
+
+
 def cmd_server(args) -> int:
     from .server.async_engine import AsyncEngine
     from .server.uds import UDSServer
@@ -370,6 +391,9 @@ def cmd_server(args) -> int:
         srv = UDSServer(front, tok, path)
     else:
         eng, tok, _, _ = load(args)
+        eng = _lockstep(eng, args)
+        if eng is None:  # a follower rank: rank 0 has stopped serving
+            return 0
         srv = UDSServer(AsyncEngine(eng), tok, path)
     if getattr(args, "metrics_port", 0):
         from .server.metrics import InferenceMetrics
@@ -393,6 +417,9 @@ def cmd_http_server(args) -> int:
                            rate_limit_rpm=args.rate_limit_rpm, arch=front.cfg.arch, aengine=front)
     else:
         eng, tok, tmpl, md = load(args)
+        eng = _lockstep(eng, args)
+        if eng is None:  # a follower rank: rank 0 has stopped serving
+            return 0
         srv = OpenAIServer(eng, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
                            rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch)
     serve(srv, args.host, args.port)
