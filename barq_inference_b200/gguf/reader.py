@@ -261,7 +261,8 @@ def read_gguf(path: str | os.PathLike, native: bool | None = None) -> GGUFFile:
         try:
             head = nat.gguf_parse(path)
         except ValueError as e:
-            raise GGUFError(f"{path}: {e}") from None
+            msg = str(e)
+            raise GGUFError(msg if msg.startswith(path) else f"{path}: {msg}") from None
         try:
             return _from_native(head, path)
         except ValueError as e:
