@@ -33,7 +33,7 @@ def _run(runner, toks, start, table, decode):
 
 
 def test_tiny_logits_match_reference():
-    """BASELINE tiny config check: logits within 1e-2 of the fp32 dequantized reference."""
+    """Tiny config check: logits within 1e-2 of the fp32 dequantized reference."""
     cfg, tensors, prompt = _tiny()
     ref = ReferenceModel(cfg, tensors)
     ref_tokens, ref_logits = ref.greedy(prompt, 64)
