@@ -69,6 +69,16 @@ class CPUEngine:
     def has_work(self) -> bool:
         return bool(self.waiting or self.running)
 
+    def abort(self, seq: Sequence) -> bool:
+        """Stop generating for ``seq`` (e.g. its client disconnected)."""
+        seq.on_token = None
+        if seq in self.waiting:
+            self.waiting.remove(seq)
+        elif seq not in self.running:
+            return False
+        self._finish(seq, "abort")
+        return True
+
     def embed(self, prompts: list[list[int]], normalize: bool = True) -> torch.Tensor:
         """Mean-pooled final-norm hidden states of each prompt ([N, hidden], fp32)."""
         from .embeddings import embed_cpu

@@ -163,6 +163,11 @@ class Engine:
     def has_work(self) -> bool:
         return self.sched.has_work
 
+    def abort(self, seq: Sequence) -> bool:
+        """Stop generating for ``seq`` (e.g. its client disconnected); no further tokens are sent."""
+        seq.on_token = None
+        return self.sched.abort(seq)
+
     def embed(self, prompts: list[list[int]], normalize: bool = True) -> torch.Tensor:
         """Mean-pooled final-norm hidden states of each prompt ([N, hidden], fp32, on the CPU)."""
         from .embeddings import embed_gpu

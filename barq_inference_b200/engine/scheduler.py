@@ -116,6 +116,20 @@ class Scheduler:
         if seq in self.running:
             self.running.remove(seq)
 
+    def abort(self, seq: Sequence) -> bool:
+        """Drop a request whose client went away: a waiting one leaves the queue, a running one
+        finishes with reason ``abort`` (its pages return to the pool).  False if already finished."""
+        if seq.status is SeqStatus.FINISHED:
+            return False
+        if seq in self.waiting:
+            self.waiting.remove(seq)
+            seq.status = SeqStatus.FINISHED
+            seq.finish_reason = "abort"
+            self._free(seq)
+            return True
+        self.finish(seq, "abort")
+        return True
+
     def _preempt_youngest(self, protect: Sequence | None = None) -> bool:
         cands = [s for s in self.running if s is not protect]
         if not cands:

@@ -73,7 +73,10 @@ class AsyncEngine:
     # ------------------------------------------------------------------ engine thread
     def _deliver(self, sub: Submission, item: StreamItem) -> None:
         if sub.aqueue is not None and sub.loop is not None:
-            sub.loop.call_soon_threadsafe(sub.aqueue.put_nowait, item)
+            try:
+                sub.loop.call_soon_threadsafe(sub.aqueue.put_nowait, item)
+            except RuntimeError:  # the consumer's event loop is gone; its abort is on the way
+                pass
         elif sub.sink is not None:
             sub.sink.put(item)
 
@@ -140,13 +143,28 @@ class AsyncEngine:
         loop = asyncio.get_running_loop()
         sub = Submission(prompt, params, request_id, loop=loop, aqueue=asyncio.Queue())
         self.inbox.put(sub)
-        while True:
-            item = await sub.aqueue.get()
-            if item.token is None and item.finish_reason == "error" and sub.error:
-                raise _refusal(sub.error[0])
-            yield item
-            if item.token is None:
-                return
+        done = False
+        try:
+            while True:
+                item = await sub.aqueue.get()
+                if item.token is None and item.finish_reason == "error" and sub.error:
+                    done = True
+                    raise _refusal(sub.error[0])
+                yield item
+                if item.token is None:
+                    done = True
+                    return
+        finally:
+            if not done:  # the consumer stopped early (client disconnected): stop generating for it
+                self._abort(sub)
+
+    def _abort(self, sub: Submission) -> None:
+        def fn(eng, sub=sub):
+            seq = getattr(sub, "seq", None)
+            if seq is not None and hasattr(eng, "abort"):
+                eng.abort(seq)
+
+        self.inbox.put(_Call(fn))
 
     def call_sync(self, fn, timeout: float | None = None):
         """Run ``fn(engine)`` on the engine thread (between steps) and return its result."""

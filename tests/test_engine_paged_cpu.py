@@ -376,3 +376,34 @@ def test_model_context_encode_decode_truncate(kind):
         assert (lg[0] - ref.forward(prompt[:10] + [5, 6])[-1]).abs().max() < 1e-3 and ctx.n_past == 12
     if kind == "engine":
         assert eng.blocks.n_used == 1  # pages returned
+
+
+def test_stream_consumer_going_away_aborts_the_request():
+    """An async stream closed early (a disconnected HTTP client) aborts its request on the engine
+    thread: it stops generating and its pages return to the pool."""
+    import asyncio
+    import time
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=22)
+    eng = _engine(cfg, t, num_blocks=64)
+    ae = AsyncEngine(eng)
+
+    async def consume_two():
+        agen = ae.stream([1, 2, 3], SamplingParams(max_tokens=200, temperature=0.0, ignore_eos=True))
+        got = [await agen.__anext__(), await agen.__anext__()]
+        await agen.aclose()
+        return got
+
+    try:
+        got = asyncio.run(consume_two())
+        assert all(g.token is not None for g in got)
+        deadline = time.monotonic() + 30
+        while (eng.sched.running or eng.sched.waiting) and time.monotonic() < deadline:
+            time.sleep(0.01)
+        assert not eng.sched.running and eng.blocks.n_used == 1
+        assert eng.step_count < 150  # stopped long before its 200 tokens
+    finally:
+        ae.shutdown()
