@@ -396,11 +396,27 @@ class DataParallelEngine:
         """Async generator of StreamItem; the last item has token None."""
         loop = asyncio.get_running_loop()
         req = self._submit(prompt, params, request_id, loop=loop, aqueue=asyncio.Queue())
-        while True:
-            item = self._check(await req.aqueue.get())
-            yield item
-            if item.token is None:
+        done = False
+        try:
+            while True:
+                item = await req.aqueue.get()
+                done = item.token is None
+                yield self._check(item)
+                if done:
+                    return
+        finally:
+            if not done:  # the consumer went away: the replica stops generating for it
+                self.cancel(req.rid)
+
+    def cancel(self, rid: str) -> None:
+        with self._lock:
+            req = self._reqs.pop(rid, None)
+            if req is None:
                 return
+            r = self.replicas[req.replica]
+            r.load -= req.cost
+        if r.alive:
+            r.inq.put(("cancel", rid))
 
     def generate_blocking(self, prompt: list[int], params: SamplingParams, request_id: str = "", timeout=None):
         """Iterator of StreamItem for synchronous callers (UDS server, CLI)."""

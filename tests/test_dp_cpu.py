@@ -110,3 +110,22 @@ def test_cli_dp_front_from_gguf(tmp_path):
         assert [len(o) for o in outs] == [3, 3, 3]
     finally:
         front.shutdown()
+
+
+def test_dp_stream_closed_early_cancels_on_the_replica(dp):
+    import asyncio
+    import time
+
+    async def two():
+        agen = dp.stream([1, 2, 3, 4], SamplingParams(max_tokens=200, temperature=0.0, ignore_eos=True))
+        got = [await agen.__anext__(), await agen.__anext__()]
+        await agen.aclose()
+        return got
+
+    got = asyncio.run(two())
+    assert all(g.token is not None for g in got)
+    deadline = time.monotonic() + 30
+    while any(r["load"] for r in dp.replica_info()) and time.monotonic() < deadline:
+        time.sleep(0.05)
+    assert all(r["load"] == 0 for r in dp.replica_info())
+    assert not dp._reqs  # nothing left in flight
