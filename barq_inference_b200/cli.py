@@ -345,17 +345,27 @@ def cmd_make_random(args) -> int:
 def _dp_front(args):
     """``--dp N``: N engine replicas (one process per GPU) behind the least-outstanding-work router.
     Returns (front, tokenizer, chat_template)."""
-    from .parallel.dp import DataParallelEngine, GGUFEngineFactory, default_devices
+    from .parallel.dp import DataParallelEngine, GGUFEngineFactory, GGUFTPBuilder, TPReplicaFactory, default_devices
 
-    if int(getattr(args, "tp", 1) or 1) > 1 or int(getattr(args, "pp", 1) or 1) > 1:
-        raise SystemExit("--dp with --tp/--pp: replicas are single-GPU engines here; pick one")
+    if int(getattr(args, "pp", 1) or 1) > 1:
+        raise SystemExit("--dp with --pp: replicas are single-GPU or tensor-parallel engines; drop --pp")
+    tp = int(getattr(args, "tp", 1) or 1)
     _, tok, tmpl, md = load(args, need_engine=False)
     from .models.config import config_from_gguf
 
     cfg = config_from_gguf(md, set())
     a = {k: v for k, v in vars(args).items() if k != "fn"}
-    devices = ["cpu"] * args.dp if getattr(args, "device", None) == "cpu" else default_devices(args.dp)
-    front = DataParallelEngine(GGUFEngineFactory(a), devices, cfg=cfg, tokenizer=tok)
+    if tp > 1:  # each replica is a tensor-parallel group on GPUs [r*tp, (r+1)*tp)
+        import torch
+
+        if not torch.cuda.is_available() or torch.cuda.device_count() < args.dp * tp:
+            raise SystemExit(f"--dp {args.dp} --tp {tp} needs {args.dp * tp} GPUs")
+        devices = [f"cuda:{r * tp}" for r in range(args.dp)]
+        factory = TPReplicaFactory(GGUFTPBuilder(a), tp)
+    else:
+        devices = ["cpu"] * args.dp if getattr(args, "device", None) == "cpu" else default_devices(args.dp)
+        factory = GGUFEngineFactory(a)
+    front = DataParallelEngine(factory, devices, cfg=cfg, tokenizer=tok)
     log.info("data parallel: %d replicas on %s", front.n_alive, ", ".join(devices))
     return front, tok, tmpl
 

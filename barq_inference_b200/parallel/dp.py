@@ -100,6 +100,10 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
         torch.cuda.set_device(torch.device(device))
     try:
         eng = factory(device)
+        if hasattr(eng, "stop"):  # a multi-rank replica: its follower ranks exit with this process
+            import atexit
+
+            atexit.register(eng.stop)
     except Exception as e:  # report and exit; the front end marks the replica dead
         outq.put((idx, "fatal", f"{type(e).__name__}: {e}"))
         return
@@ -145,6 +149,8 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
                 if msg[0] == "stop":
                     if events:
                         outq.put((idx, "events", events))
+                    if hasattr(eng, "stop"):  # release the follower ranks of a multi-rank replica
+                        eng.stop()
                     return
                 if msg[0] == "req":
                     admit(msg[1], msg[2], msg[3])
@@ -221,8 +227,10 @@ class DataParallelEngine:
         self.replicas = [ReplicaState(i, d) for i, d in enumerate(devices)]
         for r in self.replicas:
             r.inq = ctx.Queue()
+            # not daemonic: a replica may start processes of its own (the other ranks of a
+            # multi-GPU replica); shutdown() stops and joins every replica
             r.proc = ctx.Process(target=_replica_main, args=(r.idx, r.device, factory, r.inq, self._outq, stats_every),
-                                 name=f"barq-dp{r.idx}", daemon=True)
+                                 name=f"barq-dp{r.idx}", daemon=False)
             r.proc.start()
         self._lock = threading.Lock()
         self._reqs: dict[str, _Request] = {}
@@ -230,6 +238,9 @@ class DataParallelEngine:
         self._ids = itertools.count()
         self._stop = threading.Event()
         self.last_error: str | None = None
+        import atexit
+
+        atexit.register(self.shutdown)  # replica processes are not daemonic: stop them at exit
         self._wait_ready(start_timeout)
         self._router = threading.Thread(target=self._route_loop, name="barq-dp-router", daemon=True)
         self._router.start()
@@ -457,3 +468,77 @@ def default_devices(n: int) -> list[str]:
     except Exception:
         pass
     return ["cpu"] * n
+
+
+# ------------------------------------------------------------------ replicas that span several GPUs
+
+
+def _tp_follower(rank: int, tp: int, port: int, backend: str, device: str, builder) -> None:
+    import torch.distributed as dist
+
+    from .lockstep import follower_loop
+
+    if device != "cpu":
+        import torch
+
+        torch.cuda.set_device(torch.device(device))
+    dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=tp)
+    eng = builder(device, rank, tp)
+    from torch.distributed.distributed_c10d import _get_default_store
+
+    follower_loop(eng, _get_default_store())
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@dataclass
+class TPReplicaFactory:
+    """A data-parallel replica that is itself a tensor-parallel group of ``tp`` ranks: the replica
+    process becomes rank 0 (wrapped in a ``LockstepLeader``) and starts ranks 1..tp-1, which replay
+    its steps.  ``builder(device, rank, world)`` returns one rank's engine after the process group
+    is up (``GGUFTPBuilder`` for a GGUF file).  A replica given ``cuda:k`` uses GPUs k..k+tp-1."""
+    builder: Callable
+    tp: int
+
+    def __call__(self, device: str):
+        import torch.distributed as dist
+        from torch.distributed.distributed_c10d import _get_default_store
+
+        from .lockstep import LockstepLeader
+
+        backend = "gloo" if device == "cpu" else "nccl"
+        base = 0 if device == "cpu" else int(device.split(":")[1])
+        devs = ["cpu"] * self.tp if device == "cpu" else [f"cuda:{base + i}" for i in range(self.tp)]
+        port = _free_port()
+        ctx = mp.get_context("spawn")
+        self.procs = [ctx.Process(target=_tp_follower, args=(i, self.tp, port, backend, devs[i], self.builder),
+                                  daemon=True) for i in range(1, self.tp)]
+        for p in self.procs:
+            p.start()
+        dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=self.tp)
+        eng = self.builder(devs[0], 0, self.tp)
+        return LockstepLeader(eng, _get_default_store())
+
+
+@dataclass
+class GGUFTPBuilder:
+    """One rank of a tensor-parallel engine built from CLI arguments (``cli.load`` with ``--tp``)."""
+    args: dict
+
+    def __call__(self, device: str, rank: int, world: int):
+        import argparse
+        import os as _os
+
+        from ..cli import load
+
+        _os.environ["LOCAL_RANK"] = device.split(":")[1] if ":" in device else "0"
+        a = dict(self.args)
+        a.update(device="cuda", tp=world, pp=1, dp=1)
+        eng, _, _, _ = load(argparse.Namespace(**a))
+        return eng

@@ -407,3 +407,30 @@ def test_stream_consumer_going_away_aborts_the_request():
         assert eng.step_count < 150  # stopped long before its 200 tokens
     finally:
         ae.shutdown()
+
+
+class PagedBuilder:
+    """One rank's engine for multi-rank replica tests (picklable; patches the CPU sampler in the
+    process it runs in)."""
+
+    def __call__(self, device, rank, world):
+        engine_mod.ops.sample = _greedy_sample
+        cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+        return _engine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=23), num_blocks=64)
+
+
+def test_data_parallel_replicas_of_two_rank_groups():
+    """--dp with --tp: each replica is a 2-rank lockstep group (rank 0 serves, rank 1 replays)."""
+    from barq_inference_b200.parallel.dp import DataParallelEngine, TPReplicaFactory
+
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    ref = ReferenceModel(cfg, random_tensors(cfg, POLICIES["tiny"], seed=23))
+    front = DataParallelEngine(TPReplicaFactory(PagedBuilder(), 2), ["cpu", "cpu"], cfg=cfg, start_timeout=300)
+    try:
+        prompts = _prompts(cfg, 4, 24, lo=5, hi=20)
+        outs = front.generate(prompts, SamplingParams.greedy_params(max_tokens=6))
+        assert all(len(o) == 6 for o in outs)
+        assert all(_follows_reference(ref, p, o) for p, o in zip(prompts, outs))
+        assert all(r["served"] > 0 for r in front.replica_info())
+    finally:
+        front.shutdown()
