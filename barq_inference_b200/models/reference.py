@@ -54,6 +54,12 @@ class ReferenceModel:
         self.cos, self.sin = rope_cos_sin(cfg, cfg.max_ctx)
         self.scale = attn_scale(cfg)
 
+    def to(self, device) -> "ReferenceModel":
+        """Move the dequantized weights and RoPE tables (e.g. to a GPU for context-parallel prefill)."""
+        self.w = {k: v.to(device) for k, v in self.w.items()}
+        self.cos, self.sin = self.cos.to(device), self.sin.to(device)
+        return self
+
     def _attn(self, q, k, v, T0: int):
         """q: [T,H,d], k/v: [S,Hkv,d] with the last T rows new; causal (+SWA) mask."""
         cfg = self.cfg

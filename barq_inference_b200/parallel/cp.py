@@ -139,8 +139,9 @@ def cp_prefill(model, prompt: list[int], group=None):
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     T = len(prompt)
-    idx = zigzag_indices(T, world, rank)
-    ids = torch.as_tensor(prompt, dtype=torch.long)[idx]
+    dev = w["token_embd.weight"].device  # CPU, or a GPU after ``model.to(...)`` (NCCL ring)
+    idx = zigzag_indices(T, world, rank).to(dev)
+    ids = torch.as_tensor(prompt, dtype=torch.long, device=dev)[idx]
     n = ids.numel()
     x = w["token_embd.weight"][ids]
     cos, sin = model.cos[idx], model.sin[idx]
@@ -168,7 +169,7 @@ def cp_prefill(model, prompt: list[int], group=None):
         hN = rms_norm(x, w[p + "ffn_norm.weight"], cfg.rms_eps)
         x = x + (model._moe(hN, p) if cfg.layer_is_moe(i) else model._ffn(hN, p))
     # position T-1 is the last row of rank 0's second chunk
-    last = torch.zeros(cfg.hidden, dtype=x.dtype)
+    last = torch.zeros(cfg.hidden, dtype=x.dtype, device=dev)
     if rank == 0:
         last = x[-1].clone()
     if world > 1:
