@@ -395,3 +395,15 @@ def test_chat_tool_calls():
     assert client.post("/v1/chat/completions", json=bad).status_code == 400
     assert client.post("/v1/chat/completions", json=dict(body, stream=True)).status_code == 400
     srv.aengine.shutdown()
+
+
+def test_every_subcommand_has_help():
+    from barq_inference_b200.cli import build_parser
+
+    ap = build_parser()
+    sub = next(a for a in ap._actions if a.dest == "cmd")
+    for name in sub.choices:
+        r = _cli(name, "--help", timeout=120)
+        assert r.returncode == 0 and "usage" in r.stdout.lower(), (name, r.stderr[-500:])
+    assert {"run", "chat", "benchmark", "info", "convert", "server", "http-server", "metal-info",
+            "wasm-info"} <= set(sub.choices)
