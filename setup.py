@@ -43,5 +43,5 @@ setup(
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     # the reference's binary name, so scripts written for it keep working after a pip install
-    entry_points={"console_scripts": ["barq-inference=barq_inference_b200.cli:main"]},
+    entry_points={"console_scripts": ["barq-inference=barq_inference_b200.cli:main", "barq=barq_inference_b200.cli:main"]},
 )
