@@ -8,7 +8,8 @@ token on the CPU; here the whole layer stays on the device:
     router logits (small matmul) -> moe_route (gate, group-limited top-k, renorm, SER, counts,
     offsets, dispatch of token rows into expert-major order) -> grouped tcgen05 GEMM over the
     stacked gate|up experts with the SwiGLU epilogue -> grouped GEMM over the stacked down experts
-    whose epilogue adds gate_weight * y into the residual stream (the combine).
+    whose epilogue stores gate_weight * y per sorted row -> moe_combine, which adds each token's
+    rows into the residual stream in slot order (deterministic: no floating-point atomics).
 
 No step depends on host-side expert counts, so MoE decode steps are CUDA-graph capturable.
 ``fused=False`` (the CLI's ``--fmoe off``) runs the experts one by one instead, as the baseline.
@@ -94,7 +95,8 @@ class MoEBlock:
         if self.load is not None:  # rows routed to each of the E experts (sorted-row offsets)
             self.load.add(self.layer_index, r.off[1:self.E + 1] - r.off[:self.E])
         h = ops.gemm_grouped(self.gate_up, r.xs, off, self.E_local, EPI_SWIGLU_Q8)  # [T*k, F]
-        ops.gemm_grouped(self.down, h, off, self.E_local, EPI_MOE_COMBINE, out=x, row_tok=r.row_tok, row_w=r.row_w)
+        ys = ops.gemm_grouped(self.down, h, off, self.E_local, EPI_MOE_COMBINE, row_tok=r.row_tok, row_w=r.row_w)
+        ops.moe_combine(ys, r, T, off[0:1], off[self.E_local:self.E_local + 1], x)
 
     def _unfused(self, logits, hb, T, x, ser):
         """Baseline: route on the device, then one expert at a time (host-side token lists)."""

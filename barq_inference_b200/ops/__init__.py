@@ -98,8 +98,9 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, add: torch.Tensor | No
     return ob, oq
 
 
-# Streaming GEMV workspace, one per device: f32 [8, WS_ROWS] partial sums and int [WS_ROWS/128]
-# tile counters, zero between calls (the kernel clears what it used).  Allocated on first use --
+# Streaming GEMV workspace, one per device: f32 partial-sum slots ([WS_ROWS/128 + 256] x 8 x 128, one
+# slot per piece of a row tile that several CTAs share) and int [WS_ROWS/128] tile counters, zero
+# between calls (the kernel clears what it used).  Allocated on first use --
 # before any CUDA-graph capture, since the engine runs eager steps first.
 WS_ROWS = 1 << 18
 _GEMV_WS: dict = {}
@@ -112,7 +113,7 @@ def _gemv_ws(w: QWeight):
     key = w.device
     ws = _GEMV_WS.get(key)
     if ws is None:
-        ws = (torch.zeros(8 * WS_ROWS, dtype=torch.float32, device=w.device),
+        ws = (torch.zeros((WS_ROWS // 128 + 256) * 8 * 128, dtype=torch.float32, device=w.device),
               torch.zeros(WS_ROWS // 128, dtype=torch.int32, device=w.device))
         _GEMV_WS[key] = ws
     return ws
@@ -182,7 +183,8 @@ def gemm(w: QWeight, x: torch.Tensor, mode: int = EPI_STORE_F32, out: torch.Tens
          bias: torch.Tensor | None = None, k_splits: int = 0) -> torch.Tensor:
     """tcgen05 quantized GEMM: x fp16/bf16 [T, K] -> out (f32 or x.dtype [T, N]; SwiGLU: x.dtype [T, N/2]).
 
-    ``k_splits`` 0 = automatic split-K for the f32 modes (accumulated with atomics)."""
+    ``k_splits`` 0 = automatic split-K for the f32 modes (partial tiles summed in split order by the
+    last split to finish, so results are deterministic)."""
     T = x.shape[0]
     if mode == EPI_SWIGLU_Q8:
         if out is None:
@@ -192,7 +194,7 @@ def gemm(w: QWeight, x: torch.Tensor, mode: int = EPI_STORE_F32, out: torch.Tens
     f32 = out if out.dtype == torch.float32 else None
     bf = out if out.dtype != torch.float32 else None
     require_ext().qgemm(*w.args(), x, T, mode, f32, bf, bias, out.stride(0), k_splits)
-    _count(2 if (k_splits != 1 and mode == EPI_STORE_F32) else 1)
+    _count()
     return out
 
 
@@ -316,6 +318,7 @@ class MoeRouting:
         self.off = torch.empty(E + 1, **i32)
         self.row_tok = torch.empty(T * k, **i32)
         self.row_w = torch.empty(T * k, dtype=torch.float32, device=device)
+        self.tok_row = torch.empty(T * k, **i32)
         self.xs = torch.empty(T * k, H, dtype=dtype, device=device)
 
 
@@ -326,7 +329,7 @@ def moe_route(logits: torch.Tensor, x: torch.Tensor, k: int, r: MoeRouting, sigm
     T = logits.shape[0]
     require_ext().moe_route(logits.contiguous(), k, int(sigmoid), int(renorm), n_group, topk_group, ser_threshold,
                             scale, x.contiguous(), r.ids[:T], r.weights[:T], r.counts, r.cursor, r.off,
-                            r.row_tok, r.row_w, r.xs)
+                            r.row_tok, r.row_w, r.tok_row, r.xs)
     _count(3)
     return r
 
@@ -334,7 +337,8 @@ def moe_route(logits: torch.Tensor, x: torch.Tensor, k: int, r: MoeRouting, sigm
 def gemm_grouped(w: QWeight, x: torch.Tensor, off: torch.Tensor, n_groups: int, mode: int,
                  out: torch.Tensor | None = None, row_tok=None, row_w=None) -> torch.Tensor:
     """Grouped (per-expert) tcgen05 GEMM over x rows sorted by group (``off`` [n_groups+1] on device).
-    SwiGLU mode returns x.dtype [rows, grows/2]; EPI_MOE_COMBINE adds into ``out`` (f32 [tokens, grows])."""
+    SwiGLU mode returns x.dtype [rows, grows/2]; EPI_MOE_COMBINE stores row_w[r] * y[r] into ``out``
+    (f32 [rows, grows], indexed by sorted row; :func:`moe_combine` then adds each token's rows)."""
     Tr = x.shape[0]
     grows = w.N // n_groups
     if mode == EPI_SWIGLU_Q8:
@@ -343,11 +347,20 @@ def gemm_grouped(w: QWeight, x: torch.Tensor, off: torch.Tensor, n_groups: int, 
         act, f32, ld = out, None, out.stride(0)
     else:
         if out is None:
-            raise ValueError("gemm_grouped: the combine mode adds into an existing output")
+            out = torch.empty(Tr, grows, dtype=torch.float32, device=x.device)
         act, f32, ld = None, out, out.stride(0)
     require_ext().qgemm_grouped(*w.args(), x, Tr, mode, f32, act, ld, off, n_groups, grows, row_tok, row_w)
     _count()
     return out
+
+
+def moe_combine(ys: torch.Tensor, r: "MoeRouting", T: int, lo: torch.Tensor, hi: torch.Tensor,
+                x: torch.Tensor) -> torch.Tensor:
+    """x[t] += sum over slots j (slot order) of ys[tok_row[t, j]] for rows in [lo, hi) (device int32
+    scalars: this rank's window of the expert-sorted rows).  Fixed order: deterministic."""
+    require_ext().moe_combine(ys, r.tok_row, lo, hi, T, r.k, x)
+    _count()
+    return x
 
 
 def embed(w: QWeight, ids: torch.Tensor) -> torch.Tensor:

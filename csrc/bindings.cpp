@@ -62,7 +62,7 @@ void qgemv(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT
                    act_out(out_q, out_s, out_ql, out_dl), optptr<const float>(bias), (int)ld_out};
   TORCH_CHECK(!norm_h || (ws_acc && ws_cnt), "qgemv: the fused norm needs the streaming kernel");
   if (ws_acc && ws_cnt && type != barq::W_BF16) {
-    TORCH_CHECK(ws_acc->numel() >= 8 * N && ws_cnt->numel() >= (N + 127) / 128, "qgemv: workspace too small");
+    TORCH_CHECK(ws_acc->numel() >= barq::qgemv_stream_ws_floats((int)N) && ws_cnt->numel() >= (N + 127) / 128, "qgemv: workspace too small");
     check(barq::qgemv_stream(w, x, (int)B, ep, ptr<float>(*ws_acc), ptr<int>(*ws_cnt), barq::kernel_err_word(),
                              optptr<const float>(norm_h), optptr<const float>(norm_w), (float)norm_eps, (int)norm_x2,
                              cur_stream()),
@@ -106,7 +106,7 @@ void qgemm_grouped(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT 
 
 void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_t n_group, int64_t topk_group,
                double ser_threshold, double scale, Tensor x, Tensor ids, Tensor weights, Tensor counts, Tensor cursor,
-               Tensor off, Tensor row_tok, Tensor row_w, Tensor xs) {
+               Tensor off, Tensor row_tok, Tensor row_w, Tensor tok_row, Tensor xs) {
   c10::cuda::CUDAGuard g(logits.device());
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "moe_route: logits f32 [T, E]");
   TORCH_CHECK(x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16, "moe_route: x fp16/bf16");
@@ -129,7 +129,19 @@ void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_
   a.off = ptr<int>(off);
   a.row_tok = ptr<int>(row_tok);
   a.row_w = ptr<float>(row_w);
+  TORCH_CHECK(tok_row.scalar_type() == torch::kInt32 && tok_row.numel() >= (int64_t)a.T * a.k, "moe_route: tok_row int32 [T*k]");
+  a.tok_row = ptr<int>(tok_row);
   check(barq::moe_route(a, x.data_ptr(), x.scalar_type() == torch::kHalf, xs.data_ptr(), cur_stream()), "moe_route");
+}
+
+void moe_combine(Tensor ys, Tensor tok_row, Tensor lo, Tensor hi, int64_t T, int64_t k, Tensor x) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(ys.scalar_type() == torch::kFloat32 && x.scalar_type() == torch::kFloat32, "moe_combine: f32 ys and x");
+  TORCH_CHECK(ys.stride(-1) == 1 && x.stride(-1) == 1 && ys.size(-1) >= x.size(-1), "moe_combine: row-major ys / x");
+  TORCH_CHECK(tok_row.scalar_type() == torch::kInt32 && tok_row.numel() >= T * k, "moe_combine: tok_row int32 [T*k]");
+  barq::MoeCombineArgs a{ptr<const float>(ys), (int)ys.stride(0), ptr<const int>(tok_row), ptr<const int>(lo),
+                         ptr<const int>(hi), (int)T, (int)k, (int)x.size(1), ptr<float>(x), (int)x.stride(0)};
+  check(barq::moe_combine(a, cur_stream()), "moe_combine");
 }
 
 void mla_kv_write(Tensor kv_a, Tensor norm_w, double eps, Tensor cos, Tensor sin, int64_t neox, Tensor pos,
@@ -209,7 +221,7 @@ void qgemv_ar(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, O
               "qgemv_ar: ranks / buffer index");
   TORCH_CHECK(epoch.scalar_type() == torch::kInt32 && done.scalar_type() == torch::kInt32 && epoch.numel() >= 2 &&
                   done.numel() >= 2, "qgemv_ar: epoch / done must be int32 [2]");
-  TORCH_CHECK(ws_acc.numel() >= 8 * N && ws_cnt.numel() >= (N + 127) / 128, "qgemv_ar: workspace too small");
+  TORCH_CHECK(ws_acc.numel() >= barq::qgemv_stream_ws_floats((int)N) && ws_cnt.numel() >= (N + 127) / 128, "qgemv_ar: workspace too small");
   barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
   barq::ActQ8 xa{optptr<const int8_t>(xq), optptr<const float2>(xs), optptr<const int8_t>(xql),
                  optptr<const float2>(xdl)};
@@ -394,6 +406,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error", &gemm_error);
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
+  m.def("moe_combine", &moe_combine);
   m.def("mla_kv_write", &mla_kv_write);
   m.def("allreduce_add", &allreduce_add);
   m.def("qgemv_ar", &qgemv_ar);

@@ -293,14 +293,16 @@ template <typename TC, int D>
 static int launch_g(const DecodeAttnArgs& a, cudaStream_t st) {
   const int G = a.H / a.Hkv;
   dim3 grid(a.splits, a.Hkv, a.B);
+  cudaError_t e;
   switch (G) {
-    case 1: launch_pdl(decode_attn_kernel<TC, D, 1>, grid, dim3(128), 0, st, a); break;
-    case 2: launch_pdl(decode_attn_kernel<TC, D, 2>, grid, dim3(128), 0, st, a); break;
-    case 4: launch_pdl(decode_attn_kernel<TC, D, 4>, grid, dim3(128), 0, st, a); break;
-    case 8: launch_pdl(decode_attn_kernel<TC, D, 8>, grid, dim3(128), 0, st, a); break;
+    case 1: e = launch_pdl(decode_attn_kernel<TC, D, 1>, grid, dim3(128), 0, st, a); break;
+    case 2: e = launch_pdl(decode_attn_kernel<TC, D, 2>, grid, dim3(128), 0, st, a); break;
+    case 4: e = launch_pdl(decode_attn_kernel<TC, D, 4>, grid, dim3(128), 0, st, a); break;
+    case 8: e = launch_pdl(decode_attn_kernel<TC, D, 8>, grid, dim3(128), 0, st, a); break;
     default: return -3;
   }
-  if (!a.counters) launch_pdl(decode_merge_kernel<D>, dim3(a.H, a.B), dim3(D), 0, st, a);
+  if (e != cudaSuccess) return -20;
+  if (!a.counters && launch_pdl(decode_merge_kernel<D>, dim3(a.H, a.B), dim3(D), 0, st, a) != cudaSuccess) return -20;
   return 0;
 }
 

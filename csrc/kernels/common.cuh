@@ -9,7 +9,16 @@
 
 #define BARQ_DEV __device__ __forceinline__
 
+// Diagnostic switches inside the GEMM / streaming-GEMV mainloops (skip the dequant arithmetic, skip
+// the activation copy, trace stage timestamps).  Compiled out unless built with -DBARQ_DIAG=1, so
+// the product kernels carry no runtime branch for them.
+#ifndef BARQ_DIAG
+#define BARQ_DIAG 0
+#endif
+
 namespace barq {
+
+constexpr bool kDiag = BARQ_DIAG != 0;
 
 
 BARQ_DEV float warp_sum(float v) {

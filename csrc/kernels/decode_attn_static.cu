@@ -65,8 +65,13 @@ extern "C" int barq_decode_attention_static(const void* q, const void* kcache, c
                                             const int* block_tables, int max_blocks, const int* seq_lens, int B,
                                             int H, int Hkv, int D, int block_size, float scale, int window,
                                             int splits, void* out, int out_f16, void* stream) {
+  g_last_cuda_error = cudaSuccess;
   if (!q || !kcache || !vcache || !block_tables || !seq_lens || !out || B <= 0 || H <= 0 || Hkv <= 0 || D <= 0 ||
       splits <= 0 || max_blocks <= 0)
+    return BARQ_STATIC_E_ARGS;
+  // the launcher's own limits, checked here so that an unsupported shape is an argument error
+  const int G = H % Hkv == 0 ? H / Hkv : 0;
+  if (block_size != 16 || (D != 64 && D != 128) || splits > 64 || (G != 1 && G != 2 && G != 4 && G != 8))
     return BARQ_STATIC_E_ARGS;
   if (barq_decode_attention_static_need(B, H, D, splits) > BARQ_DECODE_STATIC_SCRATCH_BYTES)
     return BARQ_STATIC_E_SCRATCH;
@@ -96,14 +101,16 @@ extern "C" int barq_decode_attention_static(const void* q, const void* kcache, c
   a.out = out;
   a.out_f16 = out_f16;
   a.out_q = barq::ActOut{};  // no int8 copy of the output on this entry point
-  if (barq::decode_attention(a, static_cast<cudaStream_t>(stream)) != 0) return BARQ_STATIC_E_LAUNCH;
-  const cudaError_t e = cudaPeekAtLastError();
-  if (e != cudaSuccess) {
-    g_last_cuda_error = e;
+  // Each launch's own return code decides (the launcher checks them): a pending error that earlier,
+  // unrelated work left on this thread is not reported as this call's failure.
+  if (barq::decode_attention(a, static_cast<cudaStream_t>(stream)) != 0) {
+    g_last_cuda_error = cudaGetLastError();
     return BARQ_STATIC_E_LAUNCH;
   }
   return BARQ_STATIC_OK;
 }
+
+extern "C" int barq_static_last_cuda_error(void) { return (int)g_last_cuda_error; }
 
 extern "C" const char* barq_static_strerror(int code) {
   switch (code) {
@@ -111,10 +118,12 @@ extern "C" const char* barq_static_strerror(int code) {
     case BARQ_STATIC_E_SCRATCH:
       return "decode attention: the shape needs more scratch than the 8 MiB static array "
              "(4*(B*H*splits*D + 2*B*H*splits) bytes); use fewer splits or a smaller batch";
-    case BARQ_STATIC_E_SETUP: return "decode attention: cudaGetSymbolAddress of the static scratch failed";
-    case BARQ_STATIC_E_ARGS: return "decode attention: null pointer or non-positive size";
-    case BARQ_STATIC_E_LAUNCH:
-      return "decode attention: unsupported shape (block_size 16, D 64/128, splits 1..64, H % Hkv == 0) or launch error";
+    case BARQ_STATIC_E_SETUP:
+      return "decode attention: cudaGetSymbolAddress of the static scratch failed (barq_static_last_cuda_error)";
+    case BARQ_STATIC_E_ARGS:
+      return "decode attention: null pointer, non-positive size or unsupported shape (block_size 16, D 64 or 128, "
+             "splits 1..64, H / Hkv in {1, 2, 4, 8})";
+    case BARQ_STATIC_E_LAUNCH: return "decode attention: a kernel launch failed (barq_static_last_cuda_error)";
   }
   return "unknown code";
 }

@@ -33,14 +33,16 @@ extern "C" {
 
 #define BARQ_STATIC_OK 0
 #define BARQ_STATIC_E_SCRATCH (-101)  // the shape needs more scratch than the static array holds
-#define BARQ_STATIC_E_SETUP (-102)    // cudaGetSymbolAddress failed (the CUDA error is kept)
-#define BARQ_STATIC_E_ARGS (-103)     // bad pointers or shapes
-#define BARQ_STATIC_E_LAUNCH (-104)   // the attention launcher refused the shape or a launch failed
+#define BARQ_STATIC_E_SETUP (-102)    // cudaGetDevice / cudaGetSymbolAddress failed: see barq_static_last_cuda_error
+#define BARQ_STATIC_E_ARGS (-103)     // null pointer, non-positive size or unsupported shape
+#define BARQ_STATIC_E_LAUNCH (-104)   // a kernel launch failed: see barq_static_last_cuda_error
 
 // q: bf16 [B, H, D]; kcache / vcache: fp16 (cache_is_bf16 = 0) or bf16 [num_blocks, Hkv, block_size, D];
 // block_tables: int32 [B, max_blocks]; seq_lens: int32 [B] (tokens in the cache, current one
 // included); out: [B, H*D] fp16 (out_f16 = 1) or bf16.  block_size must be 16, D 64 or 128,
-// 1 <= splits <= 64, H a multiple of Hkv.  window > 0 limits attention to the last `window` tokens.
+// 1 <= splits <= 64, H a multiple of Hkv with H / Hkv in {1, 2, 4, 8} (other shapes return
+// BARQ_STATIC_E_ARGS before anything is launched).  window > 0 limits attention to the last
+// `window` tokens.
 // stream: a cudaStream_t (0 = legacy default stream).  Returns BARQ_STATIC_OK or a negative code.
 __attribute__((visibility("default"))) int barq_decode_attention_static(
     const void* q, const void* kcache, const void* vcache, int cache_is_bf16, const int* block_tables, int max_blocks,
@@ -50,6 +52,10 @@ __attribute__((visibility("default"))) int barq_decode_attention_static(
 // Bytes of static scratch a call with this shape needs (alignment padding included).
 __attribute__((visibility("default"))) unsigned long long barq_decode_attention_static_need(int B, int H, int D,
                                                                                             int splits);
+
+// The CUDA error behind the calling thread's last BARQ_STATIC_E_SETUP or BARQ_STATIC_E_LAUNCH
+// (cudaSuccess when its last call succeeded), as a cudaError_t value.
+__attribute__((visibility("default"))) int barq_static_last_cuda_error(void);
 
 // A one-line description of a return code of barq_decode_attention_static.
 __attribute__((visibility("default"))) const char* barq_static_strerror(int code);

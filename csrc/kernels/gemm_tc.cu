@@ -60,14 +60,18 @@ struct GemmDev {
   int ng, grows;
   const int* row_tok;
   const float* row_w;
-  int exp;  // diagnostics: bit 0 = skip the dequant arithmetic (write zeros), bit 1 = trace CTA 0
+  // Split-K (k_splits > 1): each split stores its partial tile in split_ws; the last split of a
+  // tile to arrive (split_cnt, one zeroed counter per output tile) sums them in split order.
+  float* split_ws;
+  int* split_cnt;
+  int exp;  // diagnostics (built with BARQ_DIAG): bit 0 = skip the dequant arithmetic (write zeros), bit 1 = trace CTA 0
   unsigned long long* trace;  // [kTraceStages][8] globaltimer stamps when tracing
 };
 constexpr int kTraceStages = 256;
 // trace fields per stage: 0 chunk issued, 1 chunk landed (dequant warp 0), 2 A written (dequant 0),
 // 3 act issued, 4 MMA saw A, 5 MMA saw B, 6 MMA issued, 7 consumed observed by dequant 0
 BARQ_DEV void trace(const GemmDev& g, int stage, int field) {
-  if ((g.exp & 2) && blockIdx.x == 0 && stage < kTraceStages && g.trace)
+  if ((kDiag && (g.exp & 2)) && blockIdx.x == 0 && stage < kTraceStages && g.trace)
     g.trace[stage * 32 + field] = clock64();
 }
 
@@ -474,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           trace(g, it, 3);
-          if (g.exp & 8) {  // diagnostics: no activation copy (operand stale), barrier protocol unchanged
+          if (kDiag && (g.exp & 8)) {  // diagnostics: no activation copy (operand stale), barrier protocol unchanged
             mbar_arrive(&full[s]);
           } else {
             mbar_expect_tx(&full[s], L::B_BYTES);
@@ -566,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int sub = 0; sub < SPG; ++sub, ++it) {
             const int s = it % S, ph = (it / S) & 1;
             uint4 ops[4];
-            if (g.exp & 1) {
+            if (kDiag && (g.exp & 1)) {
               ops[0] = ops[1] = ops[2] = ops[3] = make_uint4(0, 0, 0, 0);
             } else {
               dequant32<WT, F16>(ch, r, 2 * sub + (qq >> 1), qq & 1, ops);
@@ -591,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 ops[KS][2];
 #pragma unroll
           for (int a = 0; a < KS; ++a) {
-            if (g.exp & 1) {
+            if (kDiag && (g.exp & 1)) {
               ops[a][0] = ops[a][1] = make_uint4(0, 0, 0, 0);
             } else {
               const Codes cd = load_codes<WT>(ch, r, qq, sub * KS + a);
@@ -634,7 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     using AT = typename std::conditional<F16, __half, __nv_bfloat16>::type;
     AT* out_act = reinterpret_cast<AT*>(g.out_act);
     float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);
-    const bool atomic = g.k_splits > 1;
+    const bool atomic = g.k_splits > 1;  // split-K: partial tiles combined in a fixed order
+    __shared__ int split_last_s;
     pdl_wait();
     int tc = 0;
     for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
@@ -650,6 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (*err) break;
       const int n0 = tl.n0, t0 = tl.row0, t_end = tl.row0 + tl.rows, n = n0 + r;
+      const int split_tile = nt + tm.n_tiles * (t0 / BN);  // output tile id (split-K only)
       const uint32_t acc = tmem + (uint32_t)(buf * NI * BN) + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
@@ -681,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (n < g.N) {
           const float bias = (g.bias && z == 0) ? g.bias[n] : 0.f;
+          float* part = atomic ? g.split_ws + ((size_t)split_tile * g.k_splits + z) * BN * 128 : nullptr;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int t = t0 + c0 + j;
@@ -688,11 +695,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const size_t idx = (size_t)t * g.ld_out + n;
             const float val = v[j] + bias;
             if (g.mode == EPI_MOE_COMBINE) {
-              atomicAdd(g.out_f32 + (size_t)g.row_tok[t] * g.ld_out + n, g.row_w[t] * val);
+              // weighted expert output of sorted row t; moe_combine sums a token's rows in slot order
+              g.out_f32[idx] = g.row_w[t] * val;
             } else if (g.mode == EPI_STORE_BF16) {
               out_act[idx] = from_f<AT>(val);
             } else if (atomic) {
-              atomicAdd(g.out_f32 + idx, val);
+              part[(size_t)(c0 + j) * 128 + r] = val;
             } else if (g.mode == EPI_ADD_F32) {
               g.out_f32[idx] += val;
             } else {
@@ -704,6 +712,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accEmpty[buf]);
+      if (atomic) {
+        // the accumulator is released; combine the splits of this tile if this split is the last
+        __threadfence();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (quad == 0 && lane == 0) split_last_s = atomicAdd(g.split_cnt + split_tile, 1) == g.k_splits - 1;
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (split_last_s) {
+          __threadfence();
+          if (n < g.N) {
+            const float* base = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128 + r;
+            for (int c = 0; c < t_end - t0; ++c) {
+              float sum = 0.f;
+              for (int zz = 0; zz < g.k_splits; ++zz) sum += __ldcg(base + ((size_t)zz * BN + c) * 128);
+              const size_t idx = (size_t)(t0 + c) * g.ld_out + n;
+              if (g.mode == EPI_ADD_F32)
+                g.out_f32[idx] += sum;
+              else
+                g.out_f32[idx] = sum;
+            }
+          }
+          if (quad == 0 && lane == 0) g.split_cnt[split_tile] = 0;
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");  // split_last_s is read before the next tile
+      }
     }
   }
   tc_fence_before();
@@ -815,6 +847,32 @@ static int* device_err_word() {
 
 int* kernel_err_word() { return device_err_word(); }
 
+// Split-K workspace, one per device, allocated on the first split call (before any graph capture:
+// the engine runs eager steps first).  The counters are left zero by the kernel.
+constexpr long kSplitWsFloats = 160L * 128 * 256;  // 20 MiB
+constexpr int kSplitCounters = 4096;
+struct SplitWs {
+  float* ws;
+  int* cnt;
+};
+
+static const SplitWs* device_split_ws() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::unordered_map<int, SplitWs> bufs;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = bufs.find(dev);
+  if (it != bufs.end()) return &it->second;
+  SplitWs w{nullptr, nullptr};
+  if (cudaMalloc(&w.ws, kSplitWsFloats * sizeof(float)) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&w.cnt, kSplitCounters * sizeof(int)) != cudaSuccess || cudaMemset(w.cnt, 0, kSplitCounters * sizeof(int)) != cudaSuccess) {
+    cudaFree(w.ws);
+    return nullptr;
+  }
+  return &(bufs[dev] = w);
+}
+
 int gemm_error_word(int* host_out) {
   int* p = device_err_word();
   if (!p) return -1;
@@ -882,8 +940,16 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
     g.k_splits = ks;
   }
   if (g.k_splits > KG) g.k_splits = KG;
-  if (g.k_splits > 1 && g.mode == EPI_STORE_F32) {
-    if (cudaMemset2DAsync(g.out_f32, (size_t)g.ld_out * 4, 0, (size_t)g.N * 4, g.T, st) != cudaSuccess) return -6;
+  if (g.k_splits > 1) {
+    const long tiles = (long)((g.N + 127) / 128) * tiles_t;
+    // the split workspace holds kSplitWsFloats; fewer splits when a call would need more
+    while (g.k_splits > 1 && (tiles * g.k_splits * bn * 128 > kSplitWsFloats || tiles > kSplitCounters)) g.k_splits /= 2;
+    if (g.k_splits > 1) {
+      const SplitWs* w = device_split_ws();
+      if (!w) return -6;
+      g.split_ws = w->ws;
+      g.split_cnt = w->cnt;
+    }
   }
   // TS tiles: the operand stages fill the TMEM columns left after the accumulators (256 of 512)
   constexpr int S_TS = 256 / (KSW * 32);
@@ -940,6 +1006,8 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
   g.bias = ep.bias;
   g.ld_out = ep.ld_out;
   g.k_splits = k_splits;
+  g.split_ws = nullptr;
+  g.split_cnt = nullptr;
   g.err = device_err_word();
   static const int exp_flags = [] {
     const char* e = getenv("BARQ_GEMM_EXP");

@@ -14,10 +14,11 @@
 //                        halves of a row meet in shared memory once per row tile.
 // Work units are (row tile, K chunk) pairs split evenly over the CTAs ("stream-K"), so every SM
 // streams the same number of bytes.  A row tile finished by one CTA is written directly; a tile
-// shared by two CTAs is combined in an f32 workspace: each adds its partial sums (atomics in L2),
-// the last to arrive (per-tile counter) applies the epilogue and clears the workspace rows and the
-// counter again, so the next call (or CUDA-graph replay) finds them zero.
-// Epilogues: STORE_F32, ADD_F32 (partials go straight to the output with atomics), STORE_BF16,
+// shared by several CTAs is combined in an f32 workspace: each stores its partial sums in a slot of
+// its own, the last to arrive (per-tile counter) adds the slots in a fixed order, applies the
+// epilogue and clears the counter again (the next call or CUDA-graph replay finds it zero).  No
+// floating-point atomics: a decode step gives the same bits on every run.
+// Epilogues: STORE_F32, ADD_F32, STORE_BF16,
 // SWIGLU_Q8 (rows interleaved [32 gate | 32 up]; writes silu(g)*u as int8 activations), and
 // AR_PUSH: the tensor-parallel all-reduce of a row-parallel layer fused into the GEMV.  The CTA
 // that finishes a 128-row tile stores it at once into every peer's receive buffer (slot = this
@@ -43,7 +44,8 @@ using namespace tc;
 namespace {
 
 constexpr int kRingBytes = 184 * 1024;
-constexpr int kNormMaxK = 4096;  // fused-RMSNorm prologue: longest activation row staged in smem
+constexpr int kNormMaxK = 4096;
+constexpr int kSlotFloats = 8 * 128;  // one partial row tile (up to 8 tokens) per workspace slot  // fused-RMSNorm prologue: longest activation row staged in smem
 
 // Compute warps per CTA: 16 (each row split over 4 warps) for 1-2 tokens, where latency hiding
 // matters most and registers allow it; 8 (rows split over 2 warps) otherwise and for formats
@@ -82,7 +84,7 @@ struct NormIn {
 };
 
 struct StreamWs {
-  float* acc;  // [8, N] f32 partial sums of shared row tiles (zero between calls)
+  float* acc;  // [grid + tiles][8 * 128] f32 partial sums of shared row tiles (slot per CTA piece)
   int* cnt;    // [N / 128] units accumulated per row tile (zero between calls)
   int* err;
   int exp;  // diagnostics: bit 0 = compute warps skip the arithmetic (still wait for and release chunks);
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
       const bool have = !*err && mbar_wait(&full[s], ph, err, 2);
       const uint8_t* ch = smem + s * CH;
       const int row = tile * 128 + r;
-      if (have && !(ws.exp & 1)) {
+      if (have && !(kDiag && (ws.exp & 1))) {
         if constexpr (WT == W_Q4_K || WT == W_Q5_K || WT == W_Q6_K) {
           switch (half) {
             case 0: T::template chunk_dot<0 * PPT, PPT, BS, X2>(ch, r, kg, x, w.K, nparts, B, acc); break;
@@ -255,41 +257,36 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
       const int tu0 = tile * KG;
       const bool whole = tile_first == tu0 && u == tu0 + KG - 1;
       const int covered = (int)(u - tile_first + 1);
-      const bool has_k0 = tile_first == tu0;
       tile_first = u + 1;
       const bool valid = row < w.N;
       bool emit = whole;
       if (!whole) {
-        if (ep.mode == EPI_ADD_F32) {
+        // Shared tile: every contributing CTA stores its partial sums in its own workspace slot
+        // (slot = CTA + tile, unique because both grow along the unit sequence); the last CTA to
+        // arrive sums the slots in CTA order, so the result does not depend on arrival order.
+        if (half == 0 && valid)
+#pragma unroll
+          for (int b = 0; b < BS; ++b)
+            if (b < B) ws.acc[(size_t)(blockIdx.x + tile) * kSlotFloats + b * 128 + r] = acc[b];
+        __threadfence();
+        compute_sync<NW>();
+        if (tid == 0) last_s = atomicAdd(ws.cnt + tile, covered) + covered == KG;
+        compute_sync<NW>();
+        emit = last_s != 0;
+        if (emit) {
+          __threadfence();
+          const long long G = gridDim.x;
+          const int c_first = (int)(((long long)(tu0 + 1) * G + U - 1) / U) - 1;
+          const int c_last = (int)(((long long)(tu0 + KG) * G + U - 1) / U) - 1;
           if (half == 0 && valid)
 #pragma unroll
             for (int b = 0; b < BS; ++b) {
               if (b >= B) break;
-              float v = acc[b] + ((has_k0 && ep.bias) ? ep.bias[row] : 0.f);
-              atomicAdd(ep.out_f32 + (size_t)b * ep.ld_out + row, v);
+              float sum = 0.f;
+              for (int c = c_first; c <= c_last; ++c) sum += __ldcg(ws.acc + (size_t)(c + tile) * kSlotFloats + b * 128 + r);
+              acc[b] = sum;
             }
-        } else {
-          if (half == 0 && valid)
-#pragma unroll
-            for (int b = 0; b < BS; ++b)
-              if (b < B) atomicAdd(ws.acc + (size_t)b * w.N + row, acc[b]);
-          __threadfence();
-          compute_sync<NW>();
-          if (tid == 0) last_s = atomicAdd(ws.cnt + tile, covered) + covered == KG;
-          compute_sync<NW>();
-          emit = last_s != 0;
-          if (emit) {
-            __threadfence();
-            if (half == 0 && valid)
-#pragma unroll
-              for (int b = 0; b < BS; ++b) {
-                if (b >= B) break;
-                float* pw = ws.acc + (size_t)b * w.N + row;
-                acc[b] = __ldcg(pw);
-                *pw = 0.f;
-              }
-            if (tid == 0) ws.cnt[tile] = 0;
-          }
+          if (tid == 0) ws.cnt[tile] = 0;
         }
       }
       if (emit) {
@@ -388,7 +385,8 @@ int launch_stream(const QW& w, const ActQ8& x, int B, const GemvEpi& ep, const S
   constexpr int THREADS = StreamCfg<WT, BS>::THREADS;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const long U = (long)((w.N + 127) / 128) * (w.K / F::G);
-  const int grid = (int)(U < n_sm ? U : n_sm);
+  int grid = (int)(U < n_sm ? U : n_sm);
+  if (grid > 256) grid = 256;  // workspace slots: CTA + tile < 256 + tiles (qgemv_stream_ws_floats)
   return launch_pdl(kern, dim3(grid), dim3(THREADS), (size_t)smem, st, w, x, B, ep, ws, ni, ar) == cudaSuccess ? 0 : -20;
 }
 

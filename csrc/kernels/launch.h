@@ -102,11 +102,27 @@ struct MoeRouteArgs {
   int* off;
   int* row_tok;
   float* row_w;
+  int* tok_row;  // [T * k] sorted row of (token, slot), -1 when SER dropped the slot
 };
 int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st);
 
+// K7 combine: x[t, :] += sum over slots j (in slot order) of ys[tok_row[t*k+j], :], counting only
+// rows inside [*lo, *hi) (this rank's experts; device pointers into the routing offsets).
+struct MoeCombineArgs {
+  const float* ys;
+  int ld_ys;
+  const int* tok_row;
+  const int* lo;
+  const int* hi;
+  int T, k, H;
+  float* x;
+  int ld_x;
+};
+int moe_combine(const MoeCombineArgs& a, cudaStream_t st);
+
 // Grouped (MoE expert) GEMM: the weight is ng stacked groups of grows rows; activation rows sorted by
-// group with device offsets off[ng+1]; EPI_MOE_COMBINE scatters row_w[r] * y[r, :] into out row row_tok[r].
+// group with device offsets off[ng+1]; EPI_MOE_COMBINE stores row_w[r] * y[r, :] into out row r (the
+// sorted row), and moe_combine then sums each token's rows in a fixed order.
 struct GemmGroups {
   const int* off;
   int ng, grows;
@@ -119,6 +135,8 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
 int dequant_dense(const QW& w, void* out, int out_f16, cudaStream_t st);
 int gemm_error_word(int* host_out);
 int* kernel_err_word();  // device error word shared by the bounded-wait kernels (per device)
+// f32 workspace floats the streaming GEMV needs for N output rows (one 8 x 128 slot per CTA piece).
+inline long qgemv_stream_ws_floats(int N) { return ((long)(N + 127) / 128 + 256) * 8 * 128; }
 // Streaming decode GEMV (1..8 tokens): persistent, bulk-copy fed, stream-K over weight chunks.
 // ws_acc: f32 [8, N] and ws_cnt: int [N/128], both zero before the first call; the kernel leaves
 // them zero.  Calls sharing a workspace must not overlap on the GPU.  err: bounded-wait error word.

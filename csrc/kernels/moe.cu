@@ -13,6 +13,10 @@
 //   moe_scan_kernel      one block: counts -> row offsets [E+1], cursors, counts cleared.
 //   moe_dispatch_kernel  one block per (token, slot): claims a row of its expert and copies the
 //                        token's activation row there; records (token, weight) for the combine.
+//   moe_combine_kernel   K7: the down GEMM stores weight * y per sorted row; each token then adds
+//                        its rows in slot order into the residual stream.  The fixed order keeps the
+//                        sum deterministic (no floating-point atomics), whatever order the rows
+//                        were claimed in.
 #include "common.cuh"
 #include "launch.h"
 #include "pdl.cuh"
@@ -166,13 +170,17 @@ __global__ void __launch_bounds__(128) moe_dispatch_kernel(MoeRouteArgs a, const
   pdl_trigger();
   const int t = blockIdx.x / a.k, j = blockIdx.x % a.k;
   const float wj = a.weights[(size_t)t * a.k + j];
-  if (wj == 0.f) return;  // dropped by SER
+  if (wj == 0.f) {  // dropped by SER
+    if (threadIdx.x == 0) a.tok_row[(size_t)t * a.k + j] = -1;
+    return;
+  }
   __shared__ int row_s;
   if (threadIdx.x == 0) {
     const int e = a.ids[(size_t)t * a.k + j];
     const int row = atomicAdd(a.cursor + e, 1);
     a.row_tok[row] = t;
     a.row_w[row] = wj;
+    a.tok_row[(size_t)t * a.k + j] = row;
     row_s = row;
   }
   __syncthreads();
@@ -180,6 +188,41 @@ __global__ void __launch_bounds__(128) moe_dispatch_kernel(MoeRouteArgs a, const
   const int4* src = reinterpret_cast<const int4*>(x + (size_t)t * a.H);
   int4* dst = reinterpret_cast<int4*>(xs + (size_t)row * a.H);
   for (int i = threadIdx.x; i < a.H * (int)sizeof(T) / 16; i += blockDim.x) dst[i] = src[i];
+}
+
+// grid (T, ceil(H / 512)), 128 threads, 4 columns per thread
+__global__ void __launch_bounds__(128) moe_combine_kernel(MoeCombineArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int n = (blockIdx.y * 128 + threadIdx.x) * 4;
+  if (n >= a.H) return;
+  const int lo = *a.lo, hi = *a.hi;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < a.k; ++j) {
+    const int row = a.tok_row[(size_t)t * a.k + j];
+    if (row < lo || row >= hi) continue;
+    const float4 y = *reinterpret_cast<const float4*>(a.ys + (size_t)row * a.ld_ys + n);
+    s.x += y.x;
+    s.y += y.y;
+    s.z += y.z;
+    s.w += y.w;
+  }
+  float4* px = reinterpret_cast<float4*>(a.x + (size_t)t * a.ld_x + n);
+  float4 v = *px;
+  v.x += s.x;
+  v.y += s.y;
+  v.z += s.z;
+  v.w += s.w;
+  *px = v;
+}
+
+int moe_combine(const MoeCombineArgs& a, cudaStream_t st) {
+  if (a.H % 4 || a.ld_ys % 4 || a.ld_x % 4 || (reinterpret_cast<uintptr_t>(a.ys) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.x) & 15))
+    return -1;
+  if (a.T <= 0) return 0;
+  return launch_pdl(moe_combine_kernel, dim3(a.T, (a.H + 511) / 512), dim3(128), 0, st, a) == cudaSuccess ? 0 : -20;
 }
 
 int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st) {

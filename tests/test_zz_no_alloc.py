@@ -17,6 +17,7 @@ DEV = "cuda"
 BS = 16
 STATIC_BYTES = 8 * 1024 * 1024
 E_SCRATCH = -101
+E_ARGS = -103
 
 
 def _lib():
@@ -91,3 +92,18 @@ def test_static_scratch_rejects_oversized_shape():
     rc, _ = _call_static(f, q, kc, vc, bt, lens, H, Hkv, D, 0.1, 0, splits)
     assert rc == E_SCRATCH
     assert b"static array" in err(rc)
+
+
+def test_static_rejects_unsupported_group_size_before_launch():
+    """H / Hkv = 16 is outside the kernels' {1, 2, 4, 8}: an argument error, nothing launched, and
+    the thread's recorded CUDA error stays cudaSuccess."""
+    import barq_inference_b200._C as C
+
+    f, need, err = _lib()
+    last = ctypes.CDLL(C.__file__).barq_static_last_cuda_error
+    last.restype = ctypes.c_int
+    q, kc, vc, bt, lens = _case([40, 7], 64, 4, 128, seed=9)
+    rc, _ = _call_static(f, q, kc, vc, bt, lens, 64, 4, 128, 0.1, 0, 2)
+    assert rc == E_ARGS
+    assert b"{1, 2, 4, 8}" in err(rc)
+    assert last() == 0
