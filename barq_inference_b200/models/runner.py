@@ -332,10 +332,65 @@ class LlamaRunner:
                                    H, Hkv, D, self.scale, cfg.sliding_window, act_dtype=self.act_dtype)
         return ab, (ops.quantize_q8(ab, self.x2) if want_q8 else None)
 
+    def _sp_ok(self, T: int) -> bool:
+        """Whether this step runs sequence-parallel with the collectives fused into the GEMMs
+        (tensor parallel over NVLink, every projection a quantized tcgen05 GEMM)."""
+        c = self.comm
+        if c is None or c.world == 1 or self.pp is not None or not c.sp_ok(T) or c.sp_act_dtype != self.act_dtype:
+            return False
+        ok = getattr(self, "_sp_layers_ok", None)
+        if ok is None:
+            q = lambda w: isinstance(w, QWeight) and w.wtype != ops.W_BF16  # noqa: E731
+            ok = self._sp_layers_ok = self.embed_w is not None and q(self.out_w) and all(
+                L.moe is None and L.gu_interleaved and q(L.qkv) and q(L.wo) and q(L.gate_up) and q(L.down)
+                and L.wo.N == self.cfg.hidden and L.down.N == self.cfg.hidden for L in self.layers)
+        return ok
+
+    def _forward_sp(self, inp: StepInput) -> torch.Tensor:
+        """Tensor parallel, sequence-parallel residual: this rank keeps token rows [a, b) of the
+        residual stream.  Per layer: qkv GEMM on the gathered normalized rows (waiting per token
+        tile), attention on this rank's heads, o_proj GEMM whose epilogue reduce-scatters into the
+        owners, owner-side residual add + RMSNorm + all-gather, gate|up GEMM, down GEMM with the same
+        reduce-scatter, and the next norm.  No NCCL call and no separate all-reduce kernel."""
+        cfg, c = self.cfg, self.comm
+        T = inp.ids.numel()
+        eps = cfg.rms_eps
+        chunk, a, b = c.sp_rows(T)
+        x = apply_embed_overrides(ops.embed(self.embed_w, inp.ids), inp)[a:b].contiguous()
+        c.sp_reduce_norm_ag(1, x, T, self.layers[0].attn_norm, eps, reduce=False)
+        for li, L in enumerate(self.layers):
+            qkv = c.sp_gemm_ag(L.qkv, 1, T, EPI_STORE_F32, bias=L.qkv_bias)
+            ab, _ = self._attention(L, li, qkv, inp, T, want_q8=False)
+            c.sp_gemm_rs(L.wo, ab, 0)
+            c.sp_reduce_norm_ag(0, x, T, L.ffn_norm, eps)
+            h = c.sp_gemm_ag(L.gate_up, 0, T, EPI_SWIGLU_Q8)
+            c.sp_gemm_rs(L.down, h, 1)
+            nxt = self.layers[li + 1].attn_norm if li + 1 < len(self.layers) else self.out_norm
+            c.sp_reduce_norm_ag(1, x, T, nxt, eps)
+        if inp.hidden_out is not None:  # embeddings: the whole residual stream (rare; NCCL gather)
+            import torch.distributed as dist
+
+            pad = torch.zeros(chunk, cfg.hidden, dtype=torch.float32, device=self.device)
+            pad[:b - a] = x
+            full = torch.empty(chunk * c.world, cfg.hidden, dtype=torch.float32, device=self.device)
+            dist.all_gather_into_tensor(full, pad, group=c.group)
+            inp.hidden_out.copy_(full[:T])
+        ob = c.sp_gathered(1, T)  # out_norm(x) of every row
+        xl = ob.index_select(0, inp.last_idx) if not inp.decode else ob
+        S = xl.shape[0]
+        if S <= GEMV_MAX_T:
+            xq = ops.quantize_q8(xl.float(), self.x2)
+            logits = self._lin_q8(self.out_w, xq, S, EPI_STORE_F32, xb=xl.to(torch.bfloat16))
+        else:
+            logits = self._lin_bf16(self.out_w, xl.contiguous(), S, EPI_STORE_F32)
+        return self._stage_logits(inp, self._gather_logits(logits))
+
     def _forward_gemm(self, inp: StepInput) -> torch.Tensor:
         """Many tokens (prefill, batched decode): bf16 activations on the tcgen05 GEMM."""
         cfg = self.cfg
         T = inp.ids.numel()
+        if self._sp_ok(T):
+            return self._forward_sp(inp)
         x = self._stage_input(inp)
         for li, L in enumerate(self.layers):
             hb, _ = ops.rmsnorm(x, L.attn_norm, cfg.rms_eps, want_bf16=True, act_dtype=self.act_dtype)

@@ -118,31 +118,40 @@ def cases(tokens: int):
         fn = lambda: C.allreduce_add(x, [buf.data_ptr()], [flags.data_ptr()], epoch, 0, 4, 5.0, 0)  # noqa: E731
         return _qw(128, 256, GGMLType.Q4_K, 7), fn, 0.0
 
-    def decode_step_bs1():
-        # one whole batch-1 decode step of Llama-3-8B (random Q4_K / Q6_K weights, 64-token context),
-        # eager launches: the launch-list target for "where does a decode step's time go"
-        from ..models import POLICIES, preset, random_tensors
-        from ..models.runner import LlamaRunner, StepInput
+    def decode_step(B: int, ctx: int):
+        # one whole decode step of Llama-3-8B (random Q4_K / Q6_K weights) over B sequences of
+        # ctx cached tokens each, eager launches: the launch-list target for "where does a decode
+        # step's time go"
+        def make():
+            from ..models import POLICIES, preset, random_tensors
+            from ..models.runner import LlamaRunner, StepInput
 
-        cfg = preset("llama3-8b")
-        r = LlamaRunner(cfg, random_tensors(cfg, POLICIES["llama3-8b"], seed=0, device="cuda"), "cuda")
-        r.allocate_kv(64)
-        table = list(range(1, 17))
+            cfg = preset("llama3-8b")
+            r = LlamaRunner(cfg, random_tensors(cfg, POLICIES["llama3-8b"], seed=0, device="cuda"), "cuda")
+            pages = ctx // 16 + 2
+            r.allocate_kv(1 + B * pages)
+            tables = torch.arange(1, 1 + B * pages, dtype=torch.int32, device="cuda").view(B, pages)
 
-        def inp(toks, start, decode):
-            T = len(toks)
-            pos = list(range(start, start + T))
-            d = lambda a, dt: torch.tensor(a, dtype=dt, device="cuda")  # noqa: E731
-            return StepInput(d(toks, torch.int32), d(pos, torch.int32),
-                             d([table[p // 16] * 16 + p % 16 for p in pos], torch.int64), d([table], torch.int32),
-                             d([start + T], torch.int32), d([T - 1], torch.int64), decode,
-                             q_start=d([0, T], torch.int32), max_q=T)
+            def inp(seqs, start, T):
+                pos = torch.arange(start, start + T, dtype=torch.int32, device="cuda").repeat(len(seqs))
+                sq = torch.tensor(seqs, device="cuda").repeat_interleave(T)
+                bt = tables[sq.unique_consecutive()]
+                row = torch.arange(len(seqs), device="cuda").repeat_interleave(T)
+                slots = bt[row, pos.long() // 16].long() * 16 + pos.long() % 16
+                ids = torch.randint(0, cfg.vocab, (len(seqs) * T,), device="cuda", dtype=torch.int32)
+                return StepInput(ids, pos, slots, bt.contiguous(),
+                                 torch.full((len(seqs),), start + T, dtype=torch.int32, device="cuda"),
+                                 (torch.arange(len(seqs), device="cuda") + 1) * T - 1, T == 1,
+                                 q_start=torch.arange(len(seqs) + 1, dtype=torch.int32, device="cuda") * T, max_q=T)
 
-        r.forward(inp(list(range(1, 65)), 0, False))
-        step = inp([5], 64, True)  # rewrites the same position each call
-        return _qw(128, 256, GGMLType.Q4_K, 8), (lambda: r.forward(step)), 0.0
+            for b0 in range(0, B, 8):  # prefill the contexts 8 sequences at a time
+                r.forward(inp(list(range(b0, min(B, b0 + 8))), 0, ctx))
+            step = inp(list(range(B)), ctx, 1)  # rewrites the same positions each call
+            return _qw(128, 256, GGMLType.Q4_K, 8), (lambda: r.forward(step)), 0.0
+        return make
 
-    return {"allreduce_w1": allreduce_w1, "decode_step_bs1": decode_step_bs1, "gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
+    return {"allreduce_w1": allreduce_w1, "decode_step_bs1": decode_step(1, 64),
+            "decode_step_bs32": decode_step(32, 1024), "decode_step_bs64": decode_step(64, 1024), "gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
             "gemv_head": gemv_head, "gemv_qkv": gemv_qkv, "gemv_o_tp2": gemv_o_tp2(False),
             "gemv_o_tp2_push": gemv_o_tp2(True)}
 

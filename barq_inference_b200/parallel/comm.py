@@ -16,6 +16,12 @@ and ``CommBackend`` (``advanced/src/tensor_parallel.rs:28-37``), all stubs in th
   receive buffers of ``world`` slots of 64-bit (epoch, value) words; the row-parallel streaming
   GEMV itself stores every finished tile into all peers' slot for this rank and adds the peers'
   tiles as they arrive (``ops.gemv_allreduce``), so the all-reduce costs no launch of its own.
+* Sequence-parallel GEMM path (``sp_tokens``, more than 8 tokens: prefill and batched decode): a second
+  symmetric allocation holds per-rank receive slots, two gather buffers and their flags.  The
+  row-parallel tcgen05 GEMM pushes each output tile into its owner's slots (reduce-scatter fused into
+  the GEMM epilogue), the owner's ``sp_reduce_norm_ag`` kernel adds the partials into its rows of the
+  residual stream, normalizes them and pushes the rows to every rank (all-gather), and the next
+  column-parallel GEMM waits per token tile for those rows (csrc/kernels/tp_fused.cu).
 """
 from __future__ import annotations
 
@@ -30,7 +36,8 @@ from ..ops import require_ext
 
 class Comm:
     def __init__(self, device: torch.device, fused: bool = True, max_elems: int = 0,
-                 timeout_s: float = 120.0, wait_s: float = 20.0, hidden: int = 0, push_rows: int = 8, group=None):
+                 timeout_s: float = 120.0, wait_s: float = 20.0, hidden: int = 0, push_rows: int = 8, group=None,
+                 sp_tokens: int = 0, act_dtype=torch.float16):
         """``group``: the tensor-parallel process group (None = every rank; a subgroup when tensor
         parallelism is combined with pipeline stages).  ``rank`` / ``world`` are group-local."""
         if not dist.is_initialized():
@@ -53,6 +60,10 @@ class Comm:
         self.push_fused = self.push_elems > 0 and os.environ.get("BARQ_AR_PUSH", "1") != "0"
         if self.fused:
             self._setup_symmetric(max_elems)
+        # sequence-parallel buffers: up to sp_tokens rows per step on the fused GEMM path
+        self.sp_tokens = sp_tokens if (self.fused and hidden and os.environ.get("BARQ_SP", "1") != "0") else 0
+        if self.sp_tokens:
+            self._setup_sp(self.sp_tokens, hidden, act_dtype)
 
     # ------------------------------------------------------------------ fused path
     def _setup_symmetric(self, n: int) -> None:
@@ -76,6 +87,99 @@ class Comm:
                                         device=self.device) for j in (0, 1)]
         self.push_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.push_done = torch.zeros(2, dtype=torch.int32, device=self.device)
+
+    def _setup_sp(self, T_max: int, H: int, act_dtype) -> None:
+        import torch.distributed._symmetric_memory as symm
+
+        W = self.world
+        chunk = -(-T_max // W)
+        max_tiles = -(-H // 128) * -(-T_max // 64)
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731  (byte offsets kept 256-aligned)
+        o_slots = 0
+        o_ag = o_slots + al(W * chunk * H * 4)
+        o_rsf = o_ag + 2 * al(T_max * H * 2)
+        o_agf = o_rsf + 2 * al(W * max_tiles * 4)
+        total = o_agf + 2 * al(T_max * 4)
+        self.sp_buf = symm.empty(total, dtype=torch.uint8, device=self.device)
+        self.sp_buf.zero_()
+        self.sp_hdl = symm.rendezvous(self.sp_buf, self.group if self.group is not None else dist.group.WORLD)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        base = list(self.sp_hdl.buffer_ptrs)
+        self.sp_H, self.sp_max_tiles, self.sp_act_dtype = H, max_tiles, act_dtype
+        self._sp_slots = [p + o_slots for p in base]
+        self._sp_rsf = [[p + o_rsf + j * al(W * max_tiles * 4) for p in base] for j in (0, 1)]
+        self._sp_ag = [[p + o_ag + j * al(T_max * H * 2) for p in base] for j in (0, 1)]
+        self._sp_agf = [[p + o_agf + j * al(T_max * 4) for p in base] for j in (0, 1)]
+        b = self.sp_buf
+        self.sp_slots = b[o_slots:o_slots + W * chunk * H * 4].view(torch.float32)
+        self.sp_rs_flags = [b[o_rsf + j * al(W * max_tiles * 4):][:W * max_tiles * 4].view(torch.int32) for j in (0, 1)]
+        self.sp_ag = [b[o_ag + j * al(T_max * H * 2):][:T_max * H * 2].view(act_dtype).view(T_max, H) for j in (0, 1)]
+        self.sp_ag_flags = [b[o_agf + j * al(T_max * 4):][:T_max * 4].view(torch.int32) for j in (0, 1)]
+        self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.sp_done = torch.zeros(2, dtype=torch.int32, device=self.device)
+
+    # ------------------------------------------------------------------ sequence-parallel path
+    def sp_ok(self, T: int) -> bool:
+        return bool(self.sp_tokens) and 8 < T <= self.sp_tokens
+
+    def sp_rows(self, T: int) -> tuple[int, int, int]:
+        """(chunk, first, end): this rank owns token rows [first, end) of a T-row step."""
+        chunk = -(-T // self.world)
+        a = min(T, self.rank * chunk)
+        return chunk, a, min(T, a + chunk)
+
+    def sp_gemm_rs(self, w, x: torch.Tensor, site: int, bias=None) -> None:
+        """Row-parallel GEMM whose epilogue pushes every output tile into its owner's slots."""
+        from .. import ops
+
+        T = x.shape[0]
+        chunk = -(-T // self.world)
+        require_ext().qgemm_sp(*w.args(), x, T, ops.EPI_RS_PUSH, None, None, bias, w.N, self._sp_slots,
+                               self._sp_rsf[site], self.sp_epoch[site:site + 1], self.rank, chunk, self.sp_max_tiles,
+                               None, None, self.wait_s)
+        ops._count()
+
+    def sp_gemm_ag(self, w, site: int, T: int, mode: int, out=None, bias=None) -> torch.Tensor:
+        """Column-parallel GEMM on the gathered rows of site ``site``, loading each token tile as soon
+        as its rows have arrived."""
+        from .. import ops
+
+        x = self.sp_ag[site][:T]
+        if mode == ops.EPI_SWIGLU_Q8:
+            out = torch.empty(T, w.N // 2, dtype=x.dtype, device=x.device) if out is None else out
+            f32, act = None, out
+        else:
+            out = torch.empty(T, w.N, dtype=torch.float32, device=x.device) if out is None else out
+            f32, act = out, None
+        require_ext().qgemm_sp(*w.args(), x, T, mode, f32, act, bias, out.stride(0), [], [], None, self.rank, 0, 0,
+                               self.sp_ag_flags[site], self.sp_epoch[site:site + 1], self.wait_s)
+        ops._count()
+        return out
+
+    def sp_reduce_norm_ag(self, site: int, x_loc: torch.Tensor, T: int, norm_w: torch.Tensor, eps: float,
+                          reduce: bool = True, bias=None) -> None:
+        """Owner side of site ``site``: x_loc += the received partials (``reduce``), then RMSNorm rows
+        pushed to every rank's gather buffer ``site``."""
+        from .. import ops
+
+        C = require_ext()
+        chunk = -(-T // self.world)
+        H = x_loc.shape[1]
+        C.sp_reduce_norm_ag(x_loc, T, self.rank, chunk, self.sp_slots if reduce else None,
+                            self.sp_rs_flags[site] if reduce else None, self.world if reduce else 0,
+                            self.sp_max_tiles, C.gemm_tile_rows(T), -(-H // 128), bias, norm_w, eps,
+                            self._sp_ag[site], self._sp_agf[site], self.sp_epoch[site:site + 1],
+                            self.sp_done[site:site + 1], self.wait_s, int(self.sp_act_dtype == torch.float16))
+        ops._count()
+
+    def sp_gathered(self, site: int, T: int) -> torch.Tensor:
+        """The gathered rows of site ``site`` once every rank's push has landed (device-side wait)."""
+        from .. import ops
+
+        require_ext().sp_ag_wait(self.sp_ag_flags[site], self.sp_epoch[site:site + 1], T, self.wait_s)
+        ops._count()
+        return self.sp_ag[site][:T]
 
     def push_ok(self, T: int, H: int) -> bool:
         return self.push_fused and T * H <= self.push_elems
@@ -118,8 +222,13 @@ class Comm:
         from .. import ops
 
         err = ops.gemm_error()
-        if err & 0xF00 == 0x300:
+        kind = err & 0xF00
+        if kind == 0x300:
             raise RuntimeError(f"fused all-reduce: peer {err & 0xFF} did not arrive within the wait limit")
+        if kind == 0x500:
+            raise RuntimeError(f"fused reduce-scatter: rank {err & 0xFF}'s tiles did not arrive within the wait limit")
+        if kind in (0x400, 0x600):
+            raise RuntimeError("fused all-gather: a peer's rows did not arrive within the wait limit")
 
 
 def env_world() -> tuple[int, int, int]:

@@ -1,15 +1,22 @@
-"""Headline benchmark: Llama-3-8B (Q4_K, Q6_K head), decode tok/s at batch 64 with 1024-token prompts,
-plus prefill tok/s, batch-1 decode tok/s and p50 TTFT of a 512-token prompt — on random-init weights
-and uniform-random prompt ids (no checkpoint or dataset is available offline).
+"""Headline benchmark on the Llama-3-8B architecture (Q4_K, Q6_K head), random-init weights and
+uniform-random prompt ids (no checkpoint or dataset is available offline):
+
+  (b) the value: decode tok/s of 32 concurrent requests with 1024-token prompts, 256 decode tokens
+      each, paged KV in 16-token fp16 blocks (W warm-up steps, then K timed steps);
+  (a) extra: batch 1 with a 512-token prompt and 256 greedy decode tokens (decode tok/s), and the
+      p50 time to first token of that prompt;
+  plus the prefill tok/s of the 32 x 1024 prompts.
 
     python bench.py --gpus N --steps K --warmup W           (N > 1: one process per GPU via torchrun)
     python bench.py --impl reference ...                     (reference arm)
 
-Multi-GPU: every rank is an independent data-parallel engine replica (weak scaling: per-GPU work is
-fixed); the reported value is the whole-job aggregate, timed on the device with CUDA events as the
-max over ranks.  A "step" is one continuous-batching decode step of the engine's public ``step()``
-API: it includes the host->device copy of the step's inputs from pinned memory, the CUDA-graph
-replay (embedding .. sampling) and the device->host read of the sampled ids.
+Multi-GPU (default ``--parallel tp``): ONE engine tensor-parallel over all N GPUs (strong scaling:
+the same requests, the row-parallel all-reduces fused into the GEMV / GEMM kernels over NVLink);
+``--parallel dp`` runs an independent replica per GPU instead (weak scaling).  Times are taken on
+the device with CUDA events, max over ranks.  A "step" is one continuous-batching decode step of
+the engine's public ``step()`` API: it includes the host->device copy of the step's inputs from
+pinned memory, the CUDA-graph replay (embedding .. sampling) and the device->host read of the
+sampled ids.
 """
 from __future__ import annotations
 
@@ -25,26 +32,30 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (bs1, bs64) + prefill tok/s + p50 TTFT at 1/2/4/8 B200, max over ranks"
-MODEL = "Llama-3-8B (Q4_K, Q6_K output), random-init"
+MODELS = {"llama3-8b": "Llama-3-8B (Q4_K, Q6_K output), random-init",
+          "llama3-70b": "Llama-3-70B (Q4_K, Q6_K attention and output, YaRN x4), random-init",
+          "mixtral-8x7b": "Mixtral-8x7B (Q4_K, Q6_K output), random-init",
+          "deepseek-v2-lite": "DeepSeek-V2-Lite (Q4_K experts, Q8_0 attention), random-init"}
+DECODE_TOKENS = 256  # decode tokens per request in every BASELINE workload
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=240)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="barq", choices=["barq", "reference"])
     ap.add_argument("--model", default="llama3-8b")
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--prompt-len", type=int, default=1024)
     ap.add_argument("--ttft-prompt", type=int, default=512)
     ap.add_argument("--ttft-reps", type=int, default=5)
-    ap.add_argument("--bs1-steps", type=int, default=64)
+    ap.add_argument("--bs1-steps", type=int, default=DECODE_TOKENS)
     ap.add_argument("--e2e-tokens", type=int, default=32)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
-    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
-                    help="dp: one engine replica per GPU (weak scaling, default); tp: one tensor-parallel engine "
-                         "over all GPUs (strong scaling)")
+    ap.add_argument("--parallel", default="tp", choices=["dp", "tp"],
+                    help="tp: one tensor-parallel engine over all GPUs (strong scaling, default); dp: one engine "
+                         "replica per GPU (weak scaling)")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="tp all-reduce: fused one-shot kernel over NVLink peer memory, or NCCL")
     return ap.parse_args()
@@ -208,7 +219,7 @@ def main():
         eng.step()
 
     # ---- (2) batch-B prefill of P-token prompts
-    seqs = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), greedy(args.warmup + args.steps + 4))
+    seqs = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), greedy(max(DECODE_TOKENS, args.warmup + args.steps + 4)))
             for _ in range(B)]
     barrier()
     e0, e1 = ev(), ev()
@@ -292,9 +303,11 @@ def main():
             "higher_is_better": True,
             "scaling": "weak" if tp == 1 else "strong",
             "vs_baseline": None,
-            "dtype": "bf16/fp32 compute on Q4_K/Q6_K weights, int8 decode activations, fp16 KV",
+            "dtype": "Q4_K/Q6_K weights dequantized in-kernel; decode GEMV activations two-term int8 (~15-bit: "
+                     "x = d*q + dl*ql), prefill / batched GEMM activations bf16 on tcgen05; fp32 accumulation and "
+                     "residual stream; fp16 KV",
             "data": "synthetic: random-init N(0,0.02) weights quantized to Q4_K/Q6_K, uniform-random prompt ids",
-            "config": {"model": MODEL + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * mult,
+            "config": {"model": MODELS.get(args.model, args.model) + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * mult,
                        "seq_len": P, "parallelism": f"dp{world}" if tp == 1 else f"tp{world}-{args.comm}",
                        "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)"},
             "extra": {

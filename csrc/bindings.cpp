@@ -87,6 +87,99 @@ void qgemm(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT
   check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, (int)k_splits, cur_stream()), "qgemm");
 }
 
+// Sequence-parallel TP GEMM (tp_fused.cu): mode EPI_RS_PUSH pushes each output tile into its owner's
+// receive slots (rs_slots / rs_flags: int64 device addresses [world]); ag_flags (optional): the token
+// tiles of x are loaded only after their gather flags reached *ag_epoch.
+void qgemm_sp(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor x, int64_t T,
+              int64_t mode, OptT out_f32, OptT out_bf16, OptT bias, int64_t ld_out, std::vector<int64_t> rs_slots,
+              std::vector<int64_t> rs_flags, OptT rs_epoch, int64_t rank, int64_t chunk, int64_t max_tiles,
+              OptT ag_flags, OptT ag_epoch, double wait_s) {
+  c10::cuda::CUDAGuard g(p0.device());
+  const bool f16 = x.scalar_type() == torch::kHalf;
+  TORCH_CHECK((f16 || x.scalar_type() == torch::kBFloat16) && x.stride(-1) == 1 && x.size(-1) == K &&
+                  (x.dim() == 1 || x.stride(0) == K),
+              "qgemm_sp: x must be fp16 or bf16 [T, K], row-major");
+  barq::QW w = make_qw(type, N, K, p0, p1, p2, d);
+  barq::GemvEpi ep{(int)mode, optptr<float>(out_f32), optptr<__nv_bfloat16>(out_bf16), barq::ActOut{},
+                   optptr<const float>(bias), (int)ld_out};
+  barq::SpPush rs{};
+  const barq::SpPush* prs = nullptr;
+  if (mode == barq::EPI_RS_PUSH) {
+    TORCH_CHECK(rs_slots.size() == rs_flags.size() && !rs_slots.empty() && rs_slots.size() <= (size_t)barq::kSpMaxRanks &&
+                    rs_epoch.has_value(), "qgemm_sp: RS targets");
+    for (size_t q = 0; q < rs_slots.size(); ++q) {
+      rs.slots[q] = reinterpret_cast<float*>(rs_slots[q]);
+      rs.flags[q] = reinterpret_cast<uint32_t*>(rs_flags[q]);
+    }
+    rs.epoch = reinterpret_cast<const uint32_t*>(rs_epoch->data_ptr());
+    rs.rank = (int)rank;
+    rs.world = (int)rs_slots.size();
+    rs.chunk = (int)chunk;
+    rs.max_tiles = (int)max_tiles;
+    prs = &rs;
+  }
+  barq::SpWait agw{};
+  const barq::SpWait* pagw = nullptr;
+  if (ag_flags.has_value() && ag_flags->defined()) {
+    TORCH_CHECK(ag_epoch.has_value(), "qgemm_sp: ag_epoch");
+    agw.flags = reinterpret_cast<const uint32_t*>(ag_flags->data_ptr());
+    agw.epoch = reinterpret_cast<const uint32_t*>(ag_epoch->data_ptr());
+    agw.wait_ns = (unsigned long long)(wait_s * 1e9);
+    pagw = &agw;
+  }
+  check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, 1, cur_stream(), nullptr, prs, pagw), "qgemm_sp");
+}
+
+// Owner side of a sequence-parallel site: x (this rank's residual rows, f32 [rows, H]) += sum over the
+// received slots; RMSNorm -> bf16 rows pushed into every rank's gather buffer (ag / ag_flags:
+// int64 device addresses [world]).  epoch / done: this site's int32 counters (one element each).
+void sp_reduce_norm_ag(Tensor x, int64_t T, int64_t rank, int64_t chunk, OptT slots, OptT rs_flags, int64_t n_src,
+                       int64_t max_tiles, int64_t gemm_bn, int64_t n_tiles, OptT bias, Tensor norm_w, double eps,
+                       std::vector<int64_t> ag, std::vector<int64_t> ag_flags, Tensor epoch, Tensor done,
+                       double wait_s, int64_t out_f16) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "sp_reduce_norm_ag: x f32 contiguous");
+  TORCH_CHECK(ag.size() == ag_flags.size() && !ag.empty() && ag.size() <= (size_t)barq::kSpMaxRanks,
+              "sp_reduce_norm_ag: ranks");
+  TORCH_CHECK(norm_w.scalar_type() == torch::kFloat32 && norm_w.numel() == x.size(-1), "sp_reduce_norm_ag: norm_w");
+  barq::SpReduceArgs a{};
+  a.slots = optptr<const float>(slots);
+  a.rs_flags = optptr<const uint32_t>(rs_flags);
+  a.n_src = (int)n_src;
+  a.max_tiles = (int)max_tiles;
+  a.gemm_bn = (int)gemm_bn;
+  a.n_tiles = (int)n_tiles;
+  a.bias = optptr<const float>(bias);
+  a.x = ptr<float>(x);
+  a.T = (int)T;
+  a.W = (int)ag.size();
+  a.rank = (int)rank;
+  a.chunk = (int)chunk;
+  a.H = (int)x.size(-1);
+  a.norm_w = ptr<const float>(norm_w);
+  a.eps = (float)eps;
+  a.out_f16 = (int)out_f16;
+  for (size_t q = 0; q < ag.size(); ++q) {
+    a.ag[q] = reinterpret_cast<void*>(ag[q]);
+    a.ag_flags[q] = reinterpret_cast<uint32_t*>(ag_flags[q]);
+  }
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.done = ptr<int>(done);
+  a.err = barq::kernel_err_word();
+  a.wait_ns = (unsigned long long)(wait_s * 1e9);
+  check(barq::sp_reduce_norm_ag(a, cur_stream()), "sp_reduce_norm_ag");
+}
+
+void sp_ag_wait(Tensor flags, Tensor epoch, int64_t T, double wait_s) {
+  c10::cuda::CUDAGuard g(flags.device());
+  check(barq::sp_ag_wait(reinterpret_cast<const uint32_t*>(flags.data_ptr()),
+                         reinterpret_cast<const uint32_t*>(epoch.data_ptr()), (int)T, barq::kernel_err_word(),
+                         (unsigned long long)(wait_s * 1e9), cur_stream()),
+        "sp_ag_wait");
+}
+
+int64_t gemm_tile_rows(int64_t T) { return barq::gemm_tile_rows((int)T); }
+
 // Grouped (MoE expert) GEMM: w holds ng groups of grows rows; x [Ttot, K] rows sorted by group.
 void qgemm_grouped(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, OptT d, Tensor x, int64_t T,
                    int64_t mode, OptT out_f32, OptT out_act, int64_t ld_out, Tensor off, int64_t ng, int64_t grows,
@@ -407,6 +500,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("moe_combine", &moe_combine);
+  m.def("qgemm_sp", &qgemm_sp);
+  m.def("sp_reduce_norm_ag", &sp_reduce_norm_ag);
+  m.def("sp_ag_wait", &sp_ag_wait);
+  m.def("gemm_tile_rows", &gemm_tile_rows);
   m.def("mla_kv_write", &mla_kv_write);
   m.def("allreduce_add", &allreduce_add);
   m.def("qgemv_ar", &qgemv_ar);

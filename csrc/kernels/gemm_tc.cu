@@ -36,6 +36,7 @@
 #include "launch.h"
 #include "pdl.cuh"
 #include "qtile.cuh"
+#include "sysflags.cuh"
 #include "tc_common.cuh"
 
 namespace barq {
@@ -64,6 +65,10 @@ struct GemmDev {
   // tile to arrive (split_cnt, one zeroed counter per output tile) sums them in split order.
   float* split_ws;
   int* split_cnt;
+  // Sequence-parallel tensor parallelism: EPI_RS_PUSH target (rs), and the all-gather flags the
+  // activation producer waits on before loading a token tile (agw.flags non-null).
+  SpPush rs;
+  SpWait agw;
   int exp;  // diagnostics (built with BARQ_DIAG): bit 0 = skip the dequant arithmetic (write zeros), bit 1 = trace CTA 0
   unsigned long long* trace;  // [kTraceStages][8] globaltimer stamps when tracing
 };
@@ -462,15 +467,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kActWarp) {
     // ---------------------------------------------------------------- activation-tile producer
     pdl_wait();
-    if (lane == 0) {
-      prefetch_tmap(&tx);
-      int it = 0;
-      for (int u = blockIdx.x; u < tm.total && !*err; u += gridDim.x) {
-        const Tile tl = tm.decode(u);
-        const int nt = tl.nt, z = tl.z;
-        int gb, ge;
-        grange(z, gb, ge);
-        bool ok = true;
+    const uint32_t ag_ep = g.agw.flags ? *g.agw.epoch : 0u;
+    int ag_row = 0;  // rows [0, ag_row) of the gathered activation are known to have arrived
+    if (lane == 0) prefetch_tmap(&tx);
+    int it = 0;
+    for (int u = blockIdx.x; u < tm.total; u += gridDim.x) {
+      if (__shfl_sync(0xffffffffu, *err != 0, 0)) break;  // warp-uniform stop
+      const Tile tl = tm.decode(u);
+      const int z = tl.z;
+      int gb, ge;
+      grange(z, gb, ge);
+      bool ok = true;
+      if (g.agw.flags && tl.row0 + tl.rows > ag_row) {
+        // all-gather consumer: the warp polls the row flags of this token tile (written by the
+        // owners' reduce kernels over NVLink), then orders the async proxy (TMA) after them
+        bool arrived = true;
+        for (int rr = tl.row0 + lane; rr < tl.row0 + tl.rows; rr += 32)
+          arrived = arrived && wait_epoch_sys(g.agw.flags + rr, ag_ep, g.agw.wait_ns);
+        arrived = __all_sync(0xffffffffu, arrived);
+        // A peer that never delivered: record it in the global error word (the host raises) but
+        // finish the tile on whatever the buffer holds, so the kernel takes no early-exit path with
+        // copies in flight.
+        if (!arrived && lane == 0 && g.err) atomicExch(g.err, 0x400);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        ag_row = tl.row0 + tl.rows;  // token tiles of a CTA come in non-decreasing row order
+      }
+      if (lane == 0) {
         for (int ks = gb * SPG; ks < ge * SPG; ++ks, ++it) {
           const int s = it % S, ph = (it / S) & 1;
           if (it >= S && !mbar_wait(&consumed[s], ph ^ 1, err, 2)) {
@@ -487,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(smem + L::OFF_B + s * L::B_BYTES + a * L::B_ATOM, &tx, 64 * (ks * KS + a), tl.row0, &full[s]);
           }
         }
-        if (!ok) break;
       }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     }
   } else if (warp >= kMmaWarp && warp < kMmaWarp + NI) {
     // ---------------------------------------------------------------- MMA issuers
@@ -641,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool atomic = g.k_splits > 1;  // split-K: partial tiles combined in a fixed order
     __shared__ int split_last_s;
     pdl_wait();
+    const uint32_t rs_ep = g.mode == EPI_RS_PUSH ? *g.rs.epoch + 1 : 0u;
     int tc = 0;
     for (int u = blockIdx.x; u < tm.total; u += gridDim.x, ++tc) {
       const Tile tl = tm.decode(u);
@@ -655,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (*err) break;
       const int n0 = tl.n0, t0 = tl.row0, t_end = tl.row0 + tl.rows, n = n0 + r;
-      const int split_tile = nt + tm.n_tiles * (t0 / BN);  // output tile id (split-K only)
+      const int split_tile = nt + tm.n_tiles * (t0 / BN);  // output tile id (split-K, RS flags)
       const uint32_t acc = tmem + (uint32_t)(buf * NI * BN) + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
@@ -699,6 +722,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               g.out_f32[idx] = g.row_w[t] * val;
             } else if (g.mode == EPI_STORE_BF16) {
               out_act[idx] = from_f<AT>(val);
+            } else if (g.mode == EPI_RS_PUSH) {
+              // reduce-scatter: this rank's partial of row t goes straight into its owner's slot
+              const int o = t / g.rs.chunk;
+              g.rs.slots[o][((size_t)g.rs.rank * g.rs.chunk + (t - o * g.rs.chunk)) * g.N + n] = val;
             } else if (atomic) {
               part[(size_t)(c0 + j) * 128 + r] = val;
             } else if (g.mode == EPI_ADD_F32) {
@@ -712,6 +739,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accEmpty[buf]);
+      if (g.mode == EPI_RS_PUSH) {
+        // every thread's stores reach the owners before the tile's flag (release at system scope)
+        __threadfence_system();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (quad == 0 && lane < g.rs.world) {
+          const int o = lane;
+          if (o * g.rs.chunk < t_end && (o + 1) * g.rs.chunk > t0)
+            st_release_sys(g.rs.flags[o] + (size_t)g.rs.rank * g.rs.max_tiles + split_tile, rs_ep);
+        }
+      }
       if (atomic) {
         // the accumulator is released; combine the splits of this tile if this split is the last
         __threadfence();
@@ -722,14 +759,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           __threadfence();
           if (n < g.N) {
             const float* base = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128 + r;
-            for (int c = 0; c < t_end - t0; ++c) {
-              float sum = 0.f;
-              for (int zz = 0; zz < g.k_splits; ++zz) sum += __ldcg(base + ((size_t)zz * BN + c) * 128);
-              const size_t idx = (size_t)(t0 + c) * g.ld_out + n;
-              if (g.mode == EPI_ADD_F32)
-                g.out_f32[idx] += sum;
-              else
-                g.out_f32[idx] = sum;
+            const int ncol = t_end - t0;
+            for (int c0 = 0; c0 < ncol; c0 += 8) {
+              // splits in order; the 8 loads of one split are issued together
+              float sum[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) sum[j] = 0.f;
+              for (int zz = 0; zz < g.k_splits; ++zz) {
+                const float* src = base + ((size_t)zz * BN + c0) * 128;
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = c0 + j < ncol ? __ldcg(src + j * 128) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sum[j] += v[j];
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (c0 + j >= ncol) break;
+                const size_t idx = (size_t)(t0 + c0 + j) * g.ld_out + n;
+                if (g.mode == EPI_ADD_F32)
+                  g.out_f32[idx] += sum[j];
+                else
+                  g.out_f32[idx] = sum[j];
+              }
             }
           }
           if (quad == 0 && lane == 0) g.split_cnt[split_tile] = 0;
@@ -926,7 +978,7 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   constexpr int KSW = F::G >= 128 ? 2 : 1;
   GemmDev g = g0;
   const int rows_per_tile = g.ng ? (g.T + g.ng - 1) / g.ng : g.T;  // grouped: mean rows per group
-  const int bn = rows_per_tile <= 64 ? 64 : (rows_per_tile <= 128 ? 128 : 256);
+  const int bn = gemm_tile_rows(rows_per_tile);
   CUtensorMap mx;
   int rc = make_act_map(&mx, x, F16, g.K, g.T, bn);
   if (rc) return rc;
@@ -975,8 +1027,17 @@ static unsigned long long* g_trace = nullptr;
 void gemm_set_trace(void* p) { g_trace = reinterpret_cast<unsigned long long*>(p); }
 
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st,
-             const GemmGroups* grp) {
+             const GemmGroups* grp, const SpPush* rs, const SpWait* agw) {
   if (T <= 0) return 0;
+  if (ep.mode == EPI_RS_PUSH) {
+    if (!rs || grp || rs->world < 1 || rs->world > kSpMaxRanks || rs->rank < 0 || rs->rank >= rs->world ||
+        rs->chunk * rs->world < T || !rs->epoch)
+      return -12;
+    const int tiles = ((w.N + 127) / 128) * ((T + gemm_tile_rows(T) - 1) / gemm_tile_rows(T));
+    if (tiles > rs->max_tiles) return -13;
+    k_splits = 1;
+  }
+  if (agw && (grp || !agw->flags || !agw->epoch)) return -14;
   if (grp) {
     if (grp->ng <= 0 || grp->ng > kMaxGroups || grp->grows % 128 || (long)grp->ng * grp->grows != w.N) return -8;
     if (ep.mode == EPI_MOE_COMBINE && (!grp->row_tok || !grp->row_w)) return -9;
@@ -1008,6 +1069,8 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
   g.k_splits = k_splits;
   g.split_ws = nullptr;
   g.split_cnt = nullptr;
+  g.rs = rs ? *rs : SpPush{};
+  g.agw = agw ? *agw : SpWait{};
   g.err = device_err_word();
   static const int exp_flags = [] {
     const char* e = getenv("BARQ_GEMM_EXP");

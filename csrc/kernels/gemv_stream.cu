@@ -278,14 +278,19 @@ __global__ void __launch_bounds__(StreamCfg<WT, BS>::THREADS, 1)
           const long long G = gridDim.x;
           const int c_first = (int)(((long long)(tu0 + 1) * G + U - 1) / U) - 1;
           const int c_last = (int)(((long long)(tu0 + KG) * G + U - 1) / U) - 1;
-          if (half == 0 && valid)
+          if (half == 0 && valid) {
+            // pieces in CTA order; the BS loads of one piece are issued together
 #pragma unroll
-            for (int b = 0; b < BS; ++b) {
-              if (b >= B) break;
-              float sum = 0.f;
-              for (int c = c_first; c <= c_last; ++c) sum += __ldcg(ws.acc + (size_t)(c + tile) * kSlotFloats + b * 128 + r);
-              acc[b] = sum;
+            for (int b = 0; b < BS; ++b) acc[b] = 0.f;
+            for (int c = c_first; c <= c_last; ++c) {
+              const float* slot = ws.acc + (size_t)(c + tile) * kSlotFloats + r;
+              float v[BS];
+#pragma unroll
+              for (int b = 0; b < BS; ++b) v[b] = b < B ? __ldcg(slot + b * 128) : 0.f;
+#pragma unroll
+              for (int b = 0; b < BS; ++b) acc[b] += v[b];
             }
+          }
           if (tid == 0) ws.cnt[tile] = 0;
         }
       }

@@ -18,6 +18,7 @@ enum EpiMode : int {
   EPI_SWIGLU_Q8 = 3,
   EPI_MOE_COMBINE = 4,
   EPI_AR_PUSH = 5,  // streaming GEMV only: tensor-parallel all-reduce fused into the epilogue (ArPush)
+  EPI_RS_PUSH = 6,  // tcgen05 GEMM only: reduce-scatter fused into the epilogue (SpPush)
 };
 
 struct GemvEpi {
@@ -35,8 +36,59 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 
 // K2 tcgen05 quantized GEMM: out[t, n] (+)= x[t, :] . W[n, :], x bf16 [T, K] (row pitch K).
 // Modes as GemvEpi (EPI_SWIGLU_Q8 here writes bf16 silu(g)*u to out_bf16).  k_splits: 1 = none,
-// 0 = automatic (f32 modes only; accumulated with atomics).
+// 0 = automatic (f32 modes only; the last split of a tile sums the splits in order).
 // x is fp16 (x_is_f16) or bf16; EPI_STORE_BF16 / EPI_SWIGLU_Q8 outputs use the same type as x.
+// ---- Sequence-parallel tensor parallelism (tp_fused.cu, the EPI_RS_PUSH / AG-wait modes of the GEMM)
+// T token rows are split over W ranks in contiguous chunks of `chunk` = ceil(T / W) rows; rank r owns
+// rows [r * chunk, min(T, (r + 1) * chunk)) of the residual stream.
+constexpr int kSpMaxRanks = 8;
+// Token-tile height of the non-grouped tcgen05 GEMM for T rows (the RS flags are per GEMM tile).
+inline int gemm_tile_rows(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
+
+// Row-parallel GEMM -> reduce-scatter: every finished output tile is stored (plain f32 stores over
+// NVLink) into the owner rank's receive slots [src rank][chunk][N], then flagged there with the
+// call's epoch (flags [src rank][max_tiles], tile id = n tile + n_tiles * token tile).
+struct SpPush {
+  float* slots[kSpMaxRanks];
+  uint32_t* flags[kSpMaxRanks];
+  const uint32_t* epoch;  // this site's call counter (advanced by sp_reduce_norm_ag)
+  int rank, world, chunk, max_tiles;
+};
+
+// All-gather consumer: before loading token tile rows [t0, t1) of its activation, the GEMM waits for
+// flags[t0 .. t1) (one per row, written by the owner's sp_reduce_norm_ag) to reach *epoch.
+struct SpWait {
+  const uint32_t* flags;
+  const uint32_t* epoch;
+  unsigned long long wait_ns;
+};
+
+// Owner side: x[own rows] += sum over source ranks (rank order) of the received slots (+ bias), then
+// RMSNorm(x) * norm_w -> bf16 rows pushed into every rank's gather buffer ag[q][row] with a flag per
+// row.  n_src = 0: no reduce (the first layer's norm after the embedding).
+struct SpReduceArgs {
+  const float* slots;          // this rank's receive slots [W][chunk][H]
+  const uint32_t* rs_flags;    // [W][max_tiles]
+  int n_src, max_tiles, gemm_bn, n_tiles;
+  const float* bias;           // [H] or null (row-parallel bias, added once)
+  float* x;                    // residual rows of this rank [rows][H] (row pitch H)
+  int T, W, rank, chunk, H;
+  const float* norm_w;
+  float eps;
+  int out_f16;                 // gather buffers hold fp16 (1) or bf16 (0) rows
+  void* ag[kSpMaxRanks];       // every rank's gather buffer [T][H]
+  uint32_t* ag_flags[kSpMaxRanks];  // every rank's row flags [T]
+  uint32_t* epoch;             // this site's call counter: ep = *epoch + 1, advanced by the last CTA
+  int* done;                   // CTA arrival counter (zero between calls)
+  int* err;
+  unsigned long long wait_ns;
+};
+int sp_reduce_norm_ag(const SpReduceArgs& a, cudaStream_t st);
+// Wait (on the device) until the gather flags of rows [0, T) reach *epoch: orders later plain kernels
+// (torch ops) after the remote pushes.
+int sp_ag_wait(const uint32_t* flags, const uint32_t* epoch, int T, int* err, unsigned long long wait_ns,
+               cudaStream_t st);
+
 // One-shot all-reduce + residual add over peer memory (allreduce.cu).
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxBlocks = 64;
@@ -130,7 +182,7 @@ struct GemmGroups {
   const float* row_w;
 };
 int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep, int k_splits, cudaStream_t st,
-             const GemmGroups* grp = nullptr);
+             const GemmGroups* grp = nullptr, const SpPush* rs = nullptr, const SpWait* agw = nullptr);
 // Whole quantized weight (tiled layout) -> row-major fp16 (out_f16) or bf16 [N, K].
 int dequant_dense(const QW& w, void* out, int out_f16, cudaStream_t st);
 int gemm_error_word(int* host_out);

@@ -2,7 +2,11 @@
 
 Runs 2 NCCL ranks as child processes (skipped with fewer than 2 GPUs).  Three communication modes:
 "push" (decode: the all-reduce fused into the row-parallel streaming GEMV; otherwise the one-shot
-kernel), "oneshot" (symmetric memory, csrc/kernels/allreduce.cu) and the NCCL baseline."""
+kernel), "oneshot" (symmetric memory, csrc/kernels/allreduce.cu), "sp" (prefill: sequence-parallel
+residual with the reduce-scatter fused into the row-parallel tcgen05 GEMM and the all-gather into
+the next column-parallel GEMM, csrc/kernels/tp_fused.cu; decode: as "push") and the NCCL baseline.
+"tiny-sp" is the tiny config widened to 8 heads / 8 KV heads (shardable up to TP=8) with an FFN width
+that keeps gate|up interleaved after sharding, which the sequence-parallel path needs."""
 import os
 import socket
 
@@ -49,19 +53,25 @@ def _worker(rank, world, port, name, mode, q):
     from barq_inference_b200.parallel.comm import Comm
     from barq_inference_b200.parallel.tp import shard_config, shard_tensors
 
-    cfg = preset(name)
+    import dataclasses
+
+    cfg = (dataclasses.replace(preset("tiny"), hidden=512, n_heads=8, n_kv_heads=8, head_dim=64, ffn=1024)
+           if name == "tiny-sp" else preset(name))
     full = random_tensors(cfg, POLICIES["tiny"], seed=4)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
-    comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden, hidden=cfg.hidden if mode == "push" else 0)
+    comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden,
+                hidden=cfg.hidden if mode in ("push", "sp") else 0, sp_tokens=64 if mode == "sp" else 0)
     shard, info = shard_tensors(cfg, full, rank, world)
     r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
     r.allocate_kv(32)
     tp_logits = _logits(r, prompt)
     comm.check()
     pushes = int(comm.push_epoch.sum()) if mode == "push" else -1
-    if mode == "push":  # the fused GEMV all-reduce ran on the decode steps (epochs advance per call)
+    if mode in ("push", "sp"):  # the fused GEMV all-reduce ran on the decode steps (epochs advance per call)
         assert pushes > 0, pushes
+    if mode == "sp":  # the 20-token prefill ran sequence-parallel: both sites advanced once per layer
+        assert int(comm.sp_epoch[0]) == cfg.n_layers and int(comm.sp_epoch[1]) == cfg.n_layers + 1, comm.sp_epoch
     if rank == 0:
         ref = LlamaRunner(cfg, full, dev)
         ref.allocate_kv(32)
@@ -72,16 +82,13 @@ def _worker(rank, world, port, name, mode, q):
     dist.destroy_process_group()
 
 
-@needs2
-@pytest.mark.parametrize("name", ["tiny", "tiny-moe"])
-@pytest.mark.parametrize("mode", ["push", "oneshot", "nccl"])
-def test_tp2_matches_single_gpu(name, mode):
+def _run_tp(world, name, mode):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, name, mode, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, name, mode, q)) for r in range(world)]
     for p in ps:
         p.start()
     status, err = q.get(timeout=300)
@@ -89,6 +96,20 @@ def test_tp2_matches_single_gpu(name, mode):
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in ps)
     assert err < 2e-2, err
+
+
+@needs2
+@pytest.mark.parametrize("name", ["tiny", "tiny-moe"])
+@pytest.mark.parametrize("mode", ["push", "oneshot", "nccl"])
+def test_tp2_matches_single_gpu(name, mode):
+    _run_tp(2, name, mode)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_sequence_parallel_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_tp(world, "tiny-sp", "sp")
 
 
 def _pp_worker(rank, world, port, q):
