@@ -22,6 +22,7 @@ else:
 
 EPI_STORE_F32, EPI_ADD_F32, EPI_STORE_BF16, EPI_SWIGLU_Q8 = 0, 1, 2, 3
 EPI_AR_PUSH = 5  # row-parallel GEMV with the tensor-parallel all-reduce fused in (gemv_allreduce)
+EPI_RS_PUSH = 6  # row-parallel GEMM with the reduce-scatter fused in (parallel.comm.Comm.sp_gemm_rs)
 
 # Number of kernel launches issued through these wrappers (bench.py reports launches per step).
 LAUNCHES = [0]

@@ -317,6 +317,9 @@ struct Issuers {
 };
 
 constexpr int kMaxGroups = 256;
+// Split-K: at most this many K splits per output tile (the last split to finish reads every
+// split's partial tile, so more splits lengthen the kernel's tail more than they add parallelism).
+constexpr int kMaxAutoSplits = 4;
 
 // One output tile: global weight tile nt, K split z, activation/output rows [row0, row0 + rows),
 // output column base n0.
@@ -757,30 +760,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (split_last_s) {
           __threadfence();
-          if (n < g.N) {
-            const float* base = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128 + r;
-            const int ncol = t_end - t0;
-            for (int c0 = 0; c0 < ncol; c0 += 8) {
-              // splits in order; the 8 loads of one split are issued together
-              float sum[8];
+          // thread (quad, lane): rows 4*lane .. 4*lane+3 of the tile, columns quad, quad+4, ...;
+          // float4 loads of every split of two columns are issued together, summed in split order
+          const int r4 = lane * 4, n4 = n0 + r4;
+          const int ncol = t_end - t0;
+          const float* base = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128 + r4;
+          if (n4 < g.N) {
+            for (int c = quad; c < ncol; c += 8) {
+              float4 v[2][kMaxAutoSplits];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) sum[j] = 0.f;
-              for (int zz = 0; zz < g.k_splits; ++zz) {
-                const float* src = base + ((size_t)zz * BN + c0) * 128;
-                float v[8];
+              for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = c0 + j < ncol ? __ldcg(src + j * 128) : 0.f;
+                for (int zz = 0; zz < kMaxAutoSplits; ++zz)
+                  v[h][zz] = (zz < g.k_splits && c + 4 * h < ncol)
+                                 ? __ldcg(reinterpret_cast<const float4*>(base + ((size_t)zz * BN + c + 4 * h) * 128))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sum[j] += v[j];
-              }
+              for (int h = 0; h < 2; ++h) {
+                if (c + 4 * h >= ncol) break;
+                float4 s4 = v[h][0];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (c0 + j >= ncol) break;
-                const size_t idx = (size_t)(t0 + c0 + j) * g.ld_out + n;
-                if (g.mode == EPI_ADD_F32)
-                  g.out_f32[idx] += sum[j];
-                else
-                  g.out_f32[idx] = sum[j];
+                for (int zz = 1; zz < kMaxAutoSplits; ++zz) {
+                  if (zz >= g.k_splits) break;
+                  s4.x += v[h][zz].x;
+                  s4.y += v[h][zz].y;
+                  s4.z += v[h][zz].z;
+                  s4.w += v[h][zz].w;
+                }
+                float4* o = reinterpret_cast<float4*>(g.out_f32 + (size_t)(t0 + c + 4 * h) * g.ld_out + n4);
+                if (g.mode == EPI_ADD_F32) {
+                  const float4 prev = *o;
+                  s4.x += prev.x;
+                  s4.y += prev.y;
+                  s4.z += prev.z;
+                  s4.w += prev.w;
+                }
+                *o = s4;
               }
             }
           }
@@ -987,11 +1002,13 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   if (g.k_splits == 0) {  // automatic split-K so that small token counts still fill the SMs
     const int tiles = ((g.N + 127) / 128) * tiles_t, n = sm_count();
     int ks = 1;
-    if (g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32)
-      while (tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
+    if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32) && g.ld_out % 4 == 0 && g.N % 4 == 0)
+      while (ks < kMaxAutoSplits && tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
     g.k_splits = ks;
   }
   if (g.k_splits > KG) g.k_splits = KG;
+  if (g.k_splits > kMaxAutoSplits) g.k_splits = kMaxAutoSplits;
+  if (g.k_splits > 1 && (g.ld_out % 4 || g.N % 4 || (reinterpret_cast<uintptr_t>(g.out_f32) & 15))) g.k_splits = 1;
   if (g.k_splits > 1) {
     const long tiles = (long)((g.N + 127) / 128) * tiles_t;
     // the split workspace holds kSplitWsFloats; fewer splits when a call would need more
