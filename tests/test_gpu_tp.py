@@ -67,7 +67,7 @@ def _worker(rank, world, port, name, mode, q):
     r.allocate_kv(32)
     tp_logits = _logits(r, prompt)
     comm.check()
-    pushes = int(comm.push_epoch.sum()) if mode == "push" else -1
+    pushes = int(comm.push_epoch.sum()) if mode in ("push", "sp") else -1
     if mode in ("push", "sp"):  # the fused GEMV all-reduce ran on the decode steps (epochs advance per call)
         assert pushes > 0, pushes
     if mode == "sp":  # the 20-token prefill ran sequence-parallel: both sites advanced once per layer
