@@ -594,7 +594,8 @@ def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
         comm = Comm(torch.device(device), fused=ec.fused_comm,
                     max_elems=max(ec.max_num_batched_tokens, ec.max_num_seqs) * cfg.hidden, hidden=cfg.hidden,
                     sp_tokens=max(ec.max_num_batched_tokens, ec.max_num_seqs),
-                    act_dtype=torch.bfloat16 if cfg.arch.startswith("deepseek") else torch.float16)
+                    act_dtype=torch.bfloat16 if cfg.arch.startswith("deepseek") else torch.float16,
+                    ep_experts=cfg.n_experts if ec.fused_moe else 0, ep_topk=cfg.n_experts_used)
         if comm.world != ec.tp:
             raise ValueError(f"tp={ec.tp} but the process group has {comm.world} ranks")
         shard, info = shard_tensors(cfg, tensors, comm.rank, comm.world)

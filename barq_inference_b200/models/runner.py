@@ -341,9 +341,11 @@ class LlamaRunner:
         ok = getattr(self, "_sp_layers_ok", None)
         if ok is None:
             q = lambda w: isinstance(w, QWeight) and w.wtype != ops.W_BF16  # noqa: E731
+            dense_ok = lambda L: L.gu_interleaved and q(L.gate_up) and q(L.down) and \
+                L.down.N == self.cfg.hidden  # noqa: E731
             ok = self._sp_layers_ok = self.embed_w is not None and q(self.out_w) and all(
-                L.moe is None and L.gu_interleaved and q(L.qkv) and q(L.wo) and q(L.gate_up) and q(L.down)
-                and L.wo.N == self.cfg.hidden and L.down.N == self.cfg.hidden for L in self.layers)
+                (c.ep_ok(L.moe) if L.moe is not None else dense_ok(L)) and q(L.qkv) and q(L.wo)
+                and L.wo.N == self.cfg.hidden for L in self.layers)
         return ok
 
     def _forward_sp(self, inp: StepInput) -> torch.Tensor:
@@ -351,7 +353,9 @@ class LlamaRunner:
         residual stream.  Per layer: qkv GEMM on the gathered normalized rows (waiting per token
         tile), attention on this rank's heads, o_proj GEMM whose epilogue reduce-scatters into the
         owners, owner-side residual add + RMSNorm + all-gather, gate|up GEMM, down GEMM with the same
-        reduce-scatter, and the next norm.  No NCCL call and no separate all-reduce kernel."""
+        reduce-scatter, and the next norm.  MoE layers instead send this rank's normalized rows to the
+        experts' ranks and gather the weighted outputs back (``Comm.ep_moe``).  No NCCL call and no
+        separate all-reduce kernel."""
         cfg, c = self.cfg, self.comm
         T = inp.ids.numel()
         eps = cfg.rms_eps
@@ -362,10 +366,15 @@ class LlamaRunner:
             qkv = c.sp_gemm_ag(L.qkv, 1, T, EPI_STORE_F32, bias=L.qkv_bias)
             ab, _ = self._attention(L, li, qkv, inp, T, want_q8=False)
             c.sp_gemm_rs(L.wo, ab, 0)
+            nxt = self.layers[li + 1].attn_norm if li + 1 < len(self.layers) else self.out_norm
+            if L.moe is not None:  # expert parallel: this rank's rows go to the experts' ranks and back
+                c.sp_reduce_norm_ag(0, x, T, L.ffn_norm, eps, self_only=True)
+                c.ep_moe(L.moe, c.sp_ag[0][a:b], x, getattr(self, "ser_threshold", 0.0))
+                c.sp_reduce_norm_ag(1, x, T, nxt, eps, reduce=False)
+                continue
             c.sp_reduce_norm_ag(0, x, T, L.ffn_norm, eps)
             h = c.sp_gemm_ag(L.gate_up, 0, T, EPI_SWIGLU_Q8)
             c.sp_gemm_rs(L.down, h, 1)
-            nxt = self.layers[li + 1].attn_norm if li + 1 < len(self.layers) else self.out_norm
             c.sp_reduce_norm_ag(1, x, T, nxt, eps)
         if inp.hidden_out is not None:  # embeddings: the whole residual stream (rare; NCCL gather)
             import torch.distributed as dist

@@ -37,7 +37,7 @@ from ..ops import require_ext
 class Comm:
     def __init__(self, device: torch.device, fused: bool = True, max_elems: int = 0,
                  timeout_s: float = 120.0, wait_s: float = 20.0, hidden: int = 0, push_rows: int = 8, group=None,
-                 sp_tokens: int = 0, act_dtype=torch.float16):
+                 sp_tokens: int = 0, act_dtype=torch.float16, ep_experts: int = 0, ep_topk: int = 0):
         """``group``: the tensor-parallel process group (None = every rank; a subgroup when tensor
         parallelism is combined with pipeline stages).  ``rank`` / ``world`` are group-local."""
         if not dist.is_initialized():
@@ -64,6 +64,10 @@ class Comm:
         self.sp_tokens = sp_tokens if (self.fused and hidden and os.environ.get("BARQ_SP", "1") != "0") else 0
         if self.sp_tokens:
             self._setup_sp(self.sp_tokens, hidden, act_dtype)
+        # expert-parallel all-to-all buffers (MoE models on the sequence-parallel path)
+        self.ep_experts = ep_experts if (self.sp_tokens and ep_experts and ep_experts % self.world == 0) else 0
+        if self.ep_experts:
+            self._setup_ep(ep_experts, ep_topk, self.sp_tokens, hidden, act_dtype)
 
     # ------------------------------------------------------------------ fused path
     def _setup_symmetric(self, n: int) -> None:
@@ -119,6 +123,71 @@ class Comm:
         self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.sp_done = torch.zeros(2, dtype=torch.int32, device=self.device)
 
+    def _setup_ep(self, E: int, k: int, T_max: int, H: int, act_dtype) -> None:
+        import torch.distributed._symmetric_memory as symm
+
+        W = self.world
+        chunk = -(-T_max // W)
+        cap = W * chunk * k  # every routed row of every rank could land on one rank
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        o_cnt = 0
+        o_cf = o_cnt + al(W * E * 4)
+        o_df = o_cf + al(W * 4)
+        o_yf = o_df + al(W * 4)
+        o_rx = o_yf + al(W * 4)
+        o_ys = o_rx + al(cap * H * 2)
+        total = o_ys + al(cap * H * 4)
+        self.ep_buf = symm.empty(total, dtype=torch.uint8, device=self.device)
+        self.ep_buf.zero_()
+        self.ep_hdl = symm.rendezvous(self.ep_buf, self.group if self.group is not None else dist.group.WORLD)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        base = list(self.ep_hdl.buffer_ptrs)
+        self._ep = {n: [p + o for p in base] for n, o in
+                    (("cnt", o_cnt), ("cf", o_cf), ("df", o_df), ("yf", o_yf), ("rx", o_rx), ("ys", o_ys))}
+        b = self.ep_buf
+        self.ep_recv_x = b[o_rx:o_rx + cap * H * 2].view(act_dtype).view(cap, H)
+        self.ep_ys = b[o_ys:o_ys + cap * H * 4].view(torch.float32).view(cap, H)
+        self.ep_cap, self.ep_topk = cap, k
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.ep_epoch = torch.zeros(1, **i32)
+        self.ep_done = torch.zeros(2, **i32)
+        self.ep_counts = torch.zeros(E, **i32)   # left zero by the dispatch kernel
+        self.ep_cursor = torch.zeros(E, **i32)
+        self.ep_recv_off = torch.zeros(E // W + 1, **i32)
+        self.ep_ids = torch.zeros(chunk, k, **i32)
+        self.ep_w = torch.zeros(chunk, k, dtype=torch.float32, device=self.device)
+        self.ep_pos = torch.zeros(chunk * k * 2, **i32)
+        self._ep_dummy = torch.zeros(max(E + 1, chunk * k), **i32)
+        self._ep_dummy_f = torch.zeros(max(E + 1, chunk * k), dtype=torch.float32, device=self.device)
+
+    def ep_ok(self, moe) -> bool:
+        return bool(self.ep_experts) and moe.E == self.ep_experts and moe.k == self.ep_topk and \
+            moe.E_local * self.world == moe.E and moe.shared is None
+
+    def ep_moe(self, moe, hb: torch.Tensor, x: torch.Tensor, ser: float = 0.0) -> None:
+        """Expert-parallel MoE FFN of this rank's token rows: x (f32 [rows, H]) += sum over the routed
+        experts of gate_weight * expert(hb), with the rows sent to and gathered from the experts'
+        ranks over NVLink (moe.cu ep_* kernels; no NCCL, no replicated routing)."""
+        from .. import ops
+
+        C = require_ext()
+        rows = hb.shape[0]
+        logits = hb.float() @ moe.router.T
+        ids, wts, d = self.ep_ids[:rows], self.ep_w[:rows], self._ep_dummy
+        ra = moe._route_args(ser)
+        C.moe_route(logits.contiguous(), moe.k, int(ra["sigmoid"]), int(ra["renorm"]), ra["n_group"],
+                    ra["topk_group"], ra["ser_threshold"], ra["scale"], hb, ids, wts, self.ep_counts, d, d, d, self._ep_dummy_f,
+                    d, None)
+        ep = self._ep
+        args = (self.rank, moe.E, moe.E_local, moe.k, rows, ids, wts, self.ep_counts, self.ep_cursor, ep["cnt"],
+                ep["cf"], hb, ep["rx"], ep["df"], self.ep_pos, self.ep_recv_off, ep["ys"], ep["yf"])
+        C.ep_call(0, *args, None, self.ep_epoch, self.ep_done, self.ep_cap, self.wait_s)
+        h = ops.gemm_grouped(moe.gate_up, self.ep_recv_x, self.ep_recv_off, moe.E_local, ops.EPI_SWIGLU_Q8)
+        ops.gemm_grouped(moe.down, h, self.ep_recv_off, moe.E_local, ops.EPI_STORE_F32, out=self.ep_ys)
+        C.ep_call(1, *args, x, self.ep_epoch, self.ep_done, self.ep_cap, self.wait_s)
+        ops._count(5)
+
     # ------------------------------------------------------------------ sequence-parallel path
     def sp_ok(self, T: int) -> bool:
         return bool(self.sp_tokens) and 8 < T <= self.sp_tokens
@@ -158,9 +227,9 @@ class Comm:
         return out
 
     def sp_reduce_norm_ag(self, site: int, x_loc: torch.Tensor, T: int, norm_w: torch.Tensor, eps: float,
-                          reduce: bool = True, bias=None) -> None:
+                          reduce: bool = True, bias=None, self_only: bool = False) -> None:
         """Owner side of site ``site``: x_loc += the received partials (``reduce``), then RMSNorm rows
-        pushed to every rank's gather buffer ``site``."""
+        pushed to every rank's gather buffer ``site`` (``self_only``: only into this rank's)."""
         from .. import ops
 
         C = require_ext()
@@ -170,7 +239,8 @@ class Comm:
                             self.sp_rs_flags[site] if reduce else None, self.world if reduce else 0,
                             self.sp_max_tiles, C.gemm_tile_rows(T), -(-H // 128), bias, norm_w, eps,
                             self._sp_ag[site], self._sp_agf[site], self.sp_epoch[site:site + 1],
-                            self.sp_done[site:site + 1], self.wait_s, int(self.sp_act_dtype == torch.float16))
+                            self.sp_done[site:site + 1], self.wait_s, int(self.sp_act_dtype == torch.float16),
+                            int(self_only))
         ops._count()
 
     def sp_gathered(self, site: int, T: int) -> torch.Tensor:
@@ -229,6 +299,8 @@ class Comm:
             raise RuntimeError(f"fused reduce-scatter: rank {err & 0xFF}'s tiles did not arrive within the wait limit")
         if kind in (0x400, 0x600):
             raise RuntimeError("fused all-gather: a peer's rows did not arrive within the wait limit")
+        if kind in (0x700, 0x800, 0x900):
+            raise RuntimeError(f"expert all-to-all: rank {err & 0xFF} did not arrive within the wait limit")
 
 
 def env_world() -> tuple[int, int, int]:

@@ -136,7 +136,7 @@ void qgemm_sp(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT p2, O
 void sp_reduce_norm_ag(Tensor x, int64_t T, int64_t rank, int64_t chunk, OptT slots, OptT rs_flags, int64_t n_src,
                        int64_t max_tiles, int64_t gemm_bn, int64_t n_tiles, OptT bias, Tensor norm_w, double eps,
                        std::vector<int64_t> ag, std::vector<int64_t> ag_flags, Tensor epoch, Tensor done,
-                       double wait_s, int64_t out_f16) {
+                       double wait_s, int64_t out_f16, int64_t self_only) {
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "sp_reduce_norm_ag: x f32 contiguous");
   TORCH_CHECK(ag.size() == ag_flags.size() && !ag.empty() && ag.size() <= (size_t)barq::kSpMaxRanks,
@@ -159,6 +159,7 @@ void sp_reduce_norm_ag(Tensor x, int64_t T, int64_t rank, int64_t chunk, OptT sl
   a.norm_w = ptr<const float>(norm_w);
   a.eps = (float)eps;
   a.out_f16 = (int)out_f16;
+  a.self_only = (int)self_only;
   for (size_t q = 0; q < ag.size(); ++q) {
     a.ag[q] = reinterpret_cast<void*>(ag[q]);
     a.ag_flags[q] = reinterpret_cast<uint32_t*>(ag_flags[q]);
@@ -199,7 +200,7 @@ void qgemm_grouped(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT 
 
 void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_t n_group, int64_t topk_group,
                double ser_threshold, double scale, Tensor x, Tensor ids, Tensor weights, Tensor counts, Tensor cursor,
-               Tensor off, Tensor row_tok, Tensor row_w, Tensor tok_row, Tensor xs) {
+               Tensor off, Tensor row_tok, Tensor row_w, Tensor tok_row, OptT xs) {
   c10::cuda::CUDAGuard g(logits.device());
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "moe_route: logits f32 [T, E]");
   TORCH_CHECK(x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16, "moe_route: x fp16/bf16");
@@ -224,7 +225,7 @@ void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_
   a.row_w = ptr<float>(row_w);
   TORCH_CHECK(tok_row.scalar_type() == torch::kInt32 && tok_row.numel() >= (int64_t)a.T * a.k, "moe_route: tok_row int32 [T*k]");
   a.tok_row = ptr<int>(tok_row);
-  check(barq::moe_route(a, x.data_ptr(), x.scalar_type() == torch::kHalf, xs.data_ptr(), cur_stream()), "moe_route");
+  check(barq::moe_route(a, x.data_ptr(), x.scalar_type() == torch::kHalf, optptr<void>(xs), cur_stream()), "moe_route");
 }
 
 void moe_combine(Tensor ys, Tensor tok_row, Tensor lo, Tensor hi, int64_t T, int64_t k, Tensor x) {
@@ -235,6 +236,58 @@ void moe_combine(Tensor ys, Tensor tok_row, Tensor lo, Tensor hi, int64_t T, int
   barq::MoeCombineArgs a{ptr<const float>(ys), (int)ys.stride(0), ptr<const int>(tok_row), ptr<const int>(lo),
                          ptr<const int>(hi), (int)T, (int)k, (int)x.size(1), ptr<float>(x), (int)x.stride(0)};
   check(barq::moe_combine(a, cur_stream()), "moe_combine");
+}
+
+// Expert-parallel all-to-all (moe.cu): which = 0 dispatch (counts exchange + row dispatch), 1 combine
+// (signal + weighted gather into out).  Address lists hold every rank's buffer ([world] int64).
+void ep_call(int64_t which, int64_t rank, int64_t E, int64_t E_local, int64_t k, int64_t rows, Tensor ids,
+             Tensor weights, Tensor counts, Tensor cursor, std::vector<int64_t> cnt_all, std::vector<int64_t> cnt_flags,
+             Tensor x, std::vector<int64_t> recv_x, std::vector<int64_t> disp_flags, Tensor disp_pos, Tensor recv_off,
+             std::vector<int64_t> ys, std::vector<int64_t> ys_flags, OptT out, Tensor epoch, Tensor done, int64_t cap,
+             double wait_s) {
+  c10::cuda::CUDAGuard g(x.device());
+  const size_t W = cnt_all.size();
+  TORCH_CHECK(W >= 1 && W <= (size_t)barq::kSpMaxRanks && cnt_flags.size() == W && recv_x.size() == W &&
+                  disp_flags.size() == W && ys.size() == W && ys_flags.size() == W, "ep_call: ranks");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32 && weights.scalar_type() == torch::kFloat32 &&
+                  ids.numel() >= rows * k && weights.numel() >= rows * k, "ep_call: routing");
+  TORCH_CHECK(disp_pos.scalar_type() == torch::kInt32 && disp_pos.numel() >= 2 * rows * k, "ep_call: disp_pos");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16, "ep_call: x fp16/bf16");
+  barq::EpArgs a{};
+  a.rank = (int)rank;
+  a.W = (int)W;
+  a.E = (int)E;
+  a.E_local = (int)E_local;
+  a.k = (int)k;
+  a.H = (int)x.size(-1);
+  a.rows = (int)rows;
+  a.ids = ptr<const int>(ids);
+  a.weights = ptr<const float>(weights);
+  a.counts = ptr<int>(counts);
+  a.cursor = ptr<int>(cursor);
+  for (size_t q = 0; q < W; ++q) {
+    a.cnt_all[q] = reinterpret_cast<int*>(cnt_all[q]);
+    a.cnt_flags[q] = reinterpret_cast<uint32_t*>(cnt_flags[q]);
+    a.recv_x[q] = reinterpret_cast<void*>(recv_x[q]);
+    a.disp_flags[q] = reinterpret_cast<uint32_t*>(disp_flags[q]);
+    a.ys[q] = reinterpret_cast<const float*>(ys[q]);
+    a.ys_flags[q] = reinterpret_cast<uint32_t*>(ys_flags[q]);
+  }
+  a.x = x.data_ptr();
+  a.disp_pos = reinterpret_cast<int2*>(disp_pos.data_ptr());
+  a.recv_off = ptr<int>(recv_off);
+  a.out = optptr<float>(out);
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.done = ptr<int>(done);
+  a.cap = (int)cap;
+  a.err = barq::kernel_err_word();
+  a.wait_ns = (unsigned long long)(wait_s * 1e9);
+  if (which == 0)
+    check(barq::ep_dispatch(a, x.scalar_type() == torch::kHalf, cur_stream()), "ep_dispatch");
+  else {
+    TORCH_CHECK(a.out && out->scalar_type() == torch::kFloat32 && out->is_contiguous(), "ep_combine: out f32");
+    check(barq::ep_combine(a, cur_stream()), "ep_combine");
+  }
 }
 
 void mla_kv_write(Tensor kv_a, Tensor norm_w, double eps, Tensor cos, Tensor sin, int64_t neox, Tensor pos,
@@ -500,6 +553,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
   m.def("moe_combine", &moe_combine);
+  m.def("ep_call", &ep_call);
   m.def("qgemm_sp", &qgemm_sp);
   m.def("sp_reduce_norm_ag", &sp_reduce_norm_ag);
   m.def("sp_ag_wait", &sp_ag_wait);

@@ -76,6 +76,7 @@ struct SpReduceArgs {
   const float* norm_w;
   float eps;
   int out_f16;                 // gather buffers hold fp16 (1) or bf16 (0) rows
+  int self_only;               // 1: write only this rank's gather buffer (the rows feed a local op)
   void* ag[kSpMaxRanks];       // every rank's gather buffer [T][H]
   uint32_t* ag_flags[kSpMaxRanks];  // every rank's row flags [T]
   uint32_t* epoch;             // this site's call counter: ep = *epoch + 1, advanced by the last CTA
@@ -157,6 +158,37 @@ struct MoeRouteArgs {
   int* tok_row;  // [T * k] sorted row of (token, slot), -1 when SER dropped the slot
 };
 int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st);
+
+// ---- Expert parallelism: all-to-all dispatch / combine over NVLink peer memory (moe.cu).
+// Each rank routes its own token rows (sequence-parallel residual), sends every (token, slot) row to
+// the rank that holds the expert, and later gathers the expert outputs back.  Receive layout on
+// rank q: its E_local experts in order, each expert's rows grouped by source rank in rank order.
+struct EpArgs {
+  int rank, W, E, E_local, k, H, rows;  // rows: token rows of this rank
+  const int* ids;          // [rows, k] expert of each slot (routing of this rank's rows)
+  const float* weights;    // [rows, k] gate weight (0: slot dropped by SER)
+  int* counts;             // [E] rows of this rank per expert (from the routing kernel; cleared here)
+  int* cursor;             // [E] zeroed claim counters (left zero)
+  int* cnt_all[kSpMaxRanks];        // every rank's count matrix [W][E]
+  uint32_t* cnt_flags[kSpMaxRanks];  // every rank's count flags [W]
+  const void* x;           // this rank's normalized rows [rows, H] (fp16 / bf16)
+  void* recv_x[kSpMaxRanks];          // every rank's receive rows [cap, H]
+  uint32_t* disp_flags[kSpMaxRanks];  // every rank's dispatch flags [W]
+  int2* disp_pos;          // [rows, k] (dest rank, receive row) of each slot; dest -1: dropped
+  int* recv_off;           // [E_local + 1] receive-row offsets of this rank's experts (written here)
+  const float* ys[kSpMaxRanks];       // every rank's expert outputs [cap, H] f32
+  uint32_t* ys_flags[kSpMaxRanks];    // every rank's "outputs ready" flags [W]
+  float* out;              // this rank's residual rows [rows, H] (combine adds into it)
+  uint32_t* epoch;         // EP call counter (advanced by the combine's last CTA)
+  int* done;               // [2] CTA arrival counters (zero between calls)
+  int cap;                 // receive rows per rank
+  int* err;
+  unsigned long long wait_ns;
+};
+// route counts of this rank -> every rank's count matrix; then dispatch rows; grouped GEMMs on the
+// receive rows run in between; then signal + combine.
+int ep_dispatch(const EpArgs& a, int x_is_f16, cudaStream_t st);
+int ep_combine(const EpArgs& a, cudaStream_t st);
 
 // K7 combine: x[t, :] += sum over slots j (in slot order) of ys[tok_row[t*k+j], :], counting only
 // rows inside [*lo, *hi) (this rank's experts; device pointers into the routing offsets).

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "pdl.cuh"
+#include "sysflags.cuh"
 
 namespace barq {
 
@@ -231,6 +232,7 @@ int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cuda
   if ((a.H * 2) % 16) return -3;
   if (a.T <= 0) return 0;
   cudaError_t e = launch_pdl(moe_route_kernel, dim3((a.T + 7) / 8), dim3(256), 0, st, a);
+  if (!xs) return e == cudaSuccess ? 0 : -20;  // routing only (expert parallel: ep_dispatch follows)
   if (e == cudaSuccess) e = launch_pdl(moe_scan_kernel, dim3(1), dim3(256), 0, st, a);
   if (e == cudaSuccess) {
     if (x_is_f16)
@@ -241,6 +243,191 @@ int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cuda
                      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(xs));
   }
   return e == cudaSuccess ? 0 : -20;
+}
+
+// ------------------------------------------------------------------ expert parallel (K5 / K7 across ranks)
+// All-to-all over NVLink peer memory, no NCCL:
+//   ep_counts_kernel    this rank's per-expert row counts -> every rank's count matrix, then a flag;
+//   ep_dispatch_kernel  waits for every rank's counts, places each (token, slot) in the expert
+//                       owner's receive rows (expert-major, then source rank) and copies the token
+//                       row there with plain 16-byte stores; its last CTA flags every rank, waits
+//                       for every rank's flag and writes this rank's receive offsets for the
+//                       grouped expert GEMMs;
+//   (grouped gate|up and down GEMMs on the received rows, outputs unweighted f32)
+//   ep_signal_kernel    "my expert outputs are complete" to every rank;
+//   ep_combine_kernel   each token row adds gate_weight * output of its slots, read from the expert
+//                       owners over NVLink, in slot order (deterministic), into the residual stream.
+// Buffer reuse needs no barrier: a peer writes this rank's receive rows or count row for the next
+// layer only after its combine of this layer, which waited for this rank's outputs, which this
+// rank computed after reading its receive rows.
+namespace {
+
+BARQ_DEV uint32_t ep_cur(const EpArgs& a) { return *a.epoch + 1; }
+
+// receive row of the first row that source `src` sends to expert e (on e's owner)
+BARQ_DEV int ep_base(const int* cm, int W, int E, int E_local, int e, int src) {
+  const int e0 = (e / E_local) * E_local;
+  int b = 0;
+  for (int x = e0; x < e; ++x)
+    for (int r = 0; r < W; ++r) b += cm[r * E + x];
+  for (int r = 0; r < src; ++r) b += cm[r * E + e];
+  return b;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256) ep_counts_kernel(EpArgs a) {
+  const uint32_t ep = ep_cur(a);
+  for (int i = threadIdx.x; i < a.W * a.E; i += blockDim.x) {
+    const int q = i / a.E, e = i - q * a.E;
+    a.cnt_all[q][a.rank * a.E + e] = a.counts[e];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < a.W) st_release_sys(a.cnt_flags[threadIdx.x] + a.rank, ep);
+}
+
+// grid: one CTA per own token row (at least 1), 128 threads
+template <typename T>
+__global__ void __launch_bounds__(128) ep_dispatch_kernel(EpArgs a) {
+  const uint32_t ep = ep_cur(a);
+  __shared__ int cm[kSpMaxRanks * kMaxExperts];
+  __shared__ int pos_s[kMaxTopK], dst_s[kMaxTopK];
+  __shared__ int last_s;
+  // every rank's counts (the local row was written by ep_counts_kernel before this launch)
+  if (threadIdx.x < a.W && !wait_epoch_sys(a.cnt_flags[a.rank] + threadIdx.x, ep, a.wait_ns))
+    atomicExch(a.err, 0x700 | threadIdx.x);
+  __syncthreads();
+  const int* own = a.cnt_all[a.rank];
+  for (int i = threadIdx.x; i < a.W * a.E; i += blockDim.x) cm[i] = __ldcg(own + i);
+  __syncthreads();
+  const int t = blockIdx.x;
+  if (t < a.rows) {
+    if (threadIdx.x < a.k) {
+      const int j = threadIdx.x;
+      const int e = a.ids[(size_t)t * a.k + j];
+      int dst = -1, pos = 0;
+      if (a.weights[(size_t)t * a.k + j] > 0.f) {
+        dst = e / a.E_local;
+        pos = ep_base(cm, a.W, a.E, a.E_local, e, a.rank) + atomicAdd(a.cursor + e, 1);
+      }
+      pos_s[j] = pos;
+      dst_s[j] = dst;
+      a.disp_pos[(size_t)t * a.k + j] = make_int2(dst, pos);
+    }
+    __syncthreads();
+    const int4* src = reinterpret_cast<const int4*>(static_cast<const T*>(a.x) + (size_t)t * a.H);
+    const int n16 = a.H * (int)sizeof(T) / 16;
+    for (int j = 0; j < a.k; ++j) {
+      if (dst_s[j] < 0) continue;
+      int4* d = reinterpret_cast<int4*>(static_cast<T*>(a.recv_x[dst_s[j]]) + (size_t)pos_s[j] * a.H);
+      for (int i = threadIdx.x; i < n16; i += blockDim.x) d[i] = src[i];  // NVLink stores
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atom_add_acq_rel_gpu(a.done, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last_s) return;
+  // last CTA: every row of this rank is out; flag every rank, then wait for every rank's rows
+  if (threadIdx.x < a.E) {
+    a.cursor[threadIdx.x] = 0;
+    a.counts[threadIdx.x] = 0;
+  }
+  for (int e = threadIdx.x + 128; e < a.E; e += 128) {
+    a.cursor[e] = 0;
+    a.counts[e] = 0;
+  }
+  if (threadIdx.x < a.W) st_release_sys(a.disp_flags[threadIdx.x] + a.rank, ep);
+  if (threadIdx.x <= a.E_local) {
+    const int e = a.rank * a.E_local + threadIdx.x;
+    a.recv_off[threadIdx.x] = threadIdx.x == a.E_local
+                                  ? ep_base(cm, a.W, a.E, a.E_local, e - 1, a.W)
+                                  : ep_base(cm, a.W, a.E, a.E_local, e, 0);
+  }
+  if (threadIdx.x < a.W && !wait_epoch_sys(a.disp_flags[a.rank] + threadIdx.x, ep, a.wait_ns))
+    atomicExch(a.err, 0x800 | threadIdx.x);
+  if (threadIdx.x == 0) *a.done = 0;
+}
+
+__global__ void __launch_bounds__(32) ep_signal_kernel(EpArgs a) {
+  const uint32_t ep = ep_cur(a);
+  __threadfence_system();  // this rank's expert outputs (previous kernel) before the flags
+  if (threadIdx.x < a.W) st_release_sys(a.ys_flags[threadIdx.x] + a.rank, ep);
+}
+
+// grid: (one CTA per own token row (at least 1), ceil(H / 512)), 128 threads, 4 columns each
+__global__ void __launch_bounds__(128) ep_combine_kernel(EpArgs a) {
+  const uint32_t ep = ep_cur(a);
+  __shared__ int last_s;
+  if (threadIdx.x < a.W && !wait_epoch_sys(a.ys_flags[a.rank] + threadIdx.x, ep, a.wait_ns))
+    atomicExch(a.err, 0x900 | threadIdx.x);
+  __syncthreads();
+  const int t = blockIdx.x, n = (blockIdx.y * 128 + threadIdx.x) * 4;
+  if (t < a.rows && n < a.H) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < a.k; ++j) {  // slot order: the same bits whatever order rows arrived in
+      const int2 dp = a.disp_pos[(size_t)t * a.k + j];
+      if (dp.x < 0) continue;
+      const float w = a.weights[(size_t)t * a.k + j];
+      const float4 y = __ldcg(reinterpret_cast<const float4*>(a.ys[dp.x] + (size_t)dp.y * a.H + n));
+      s.x += w * y.x;
+      s.y += w * y.y;
+      s.z += w * y.z;
+      s.w += w * y.w;
+    }
+    float4* px = reinterpret_cast<float4*>(a.out + (size_t)t * a.H + n);
+    float4 v = *px;
+    v.x += s.x;
+    v.y += s.y;
+    v.z += s.z;
+    v.w += s.w;
+    *px = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atom_add_acq_rel_gpu(a.done + 1, 1) == (int)(gridDim.x * gridDim.y) - 1;
+  __syncthreads();
+  if (last_s && threadIdx.x == 0) {
+    a.done[1] = 0;
+    *a.epoch = ep;
+  }
+}
+
+static bool ep_ok(const EpArgs& a) {
+  if (a.W < 1 || a.W > kSpMaxRanks || a.rank < 0 || a.rank >= a.W || a.E <= 0 || a.E > kMaxExperts ||
+      a.E_local * a.W != a.E || a.E_local > 127 || a.k <= 0 || a.k > kMaxTopK || a.H % 8 || a.rows < 0)
+    return false;
+  for (int q = 0; q < a.W; ++q)
+    if (!a.cnt_all[q] || !a.cnt_flags[q] || !a.recv_x[q] || !a.disp_flags[q] || !a.ys[q] || !a.ys_flags[q] ||
+        (reinterpret_cast<uintptr_t>(a.recv_x[q]) & 15) || (reinterpret_cast<uintptr_t>(a.ys[q]) & 15))
+      return false;
+  return true;
+}
+
+int ep_dispatch(const EpArgs& a, int x_is_f16, cudaStream_t st) {
+  if (!ep_ok(a) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(256);
+  if (cudaLaunchKernelEx(&cfg, ep_counts_kernel, a) != cudaSuccess) return -20;
+  cfg.gridDim = dim3(a.rows > 0 ? a.rows : 1);
+  cfg.blockDim = dim3(128);
+  const cudaError_t e = x_is_f16 ? cudaLaunchKernelEx(&cfg, ep_dispatch_kernel<__half>, a)
+                                 : cudaLaunchKernelEx(&cfg, ep_dispatch_kernel<__nv_bfloat16>, a);
+  return e == cudaSuccess ? 0 : -20;
+}
+
+int ep_combine(const EpArgs& a, cudaStream_t st) {
+  if (!ep_ok(a) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  if (cudaLaunchKernelEx(&cfg, ep_signal_kernel, a) != cudaSuccess) return -20;
+  cfg.gridDim = dim3(a.rows > 0 ? a.rows : 1, (a.H + 511) / 512);
+  cfg.blockDim = dim3(128);
+  return cudaLaunchKernelEx(&cfg, ep_combine_kernel, a) == cudaSuccess ? 0 : -20;
 }
 
 }  // namespace barq

@@ -122,13 +122,15 @@ __global__ void __launch_bounds__(kRedThreads) sp_reduce_norm_ag_kernel(SpReduce
           pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
         }
         for (int q = 0; q < a.W; ++q)  // all-gather: this row into every rank's buffer (NVLink stores)
-          *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.ag[q]) + (size_t)grow * a.H + k) = pk;
+          if (!a.self_only || q == a.rank)
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.ag[q]) + (size_t)grow * a.H + k) = pk;
       }
       __threadfence_system();
     }
     // flagged even after a failed wait (the error word is set): peers then stop waiting at once
     __syncthreads();
-    if (threadIdx.x < a.W) st_release_sys(a.ag_flags[threadIdx.x] + grow, ep);
+    if (threadIdx.x < a.W && (!a.self_only || (int)threadIdx.x == a.rank))
+      st_release_sys(a.ag_flags[threadIdx.x] + grow, ep);
   }
   // the last CTA out advances the epoch and clears the arrival counter for the next call
   __syncthreads();

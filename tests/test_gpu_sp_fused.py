@@ -63,7 +63,7 @@ def test_rs_reduce_norm_ag_gemm_matches_fp32(W, T, dt):
         xl = x0[a:b].clone().to(DEV)
         C.sp_reduce_norm_ag(xl, T, o, chunk, slots[o], rsf[o], W, max_tiles, C.gemm_tile_rows(T), -(-H // 128), None,
                             nw.to(DEV), 1e-5, [g.data_ptr() for g in ag], [f.data_ptr() for f in agf],
-                            epoch[o][site:site + 1], done[o][site:site + 1], 5.0, int(dt == torch.float16))
+                            epoch[o][site:site + 1], done[o][site:site + 1], 5.0, int(dt == torch.float16), 0)
         xloc.append(xl)
     torch.cuda.synchronize()
     assert ops.gemm_error() == 0
@@ -101,3 +101,50 @@ def test_ag_wait_times_out_on_missing_rows():
     assert ops.gemm_error() == 0
     torch.zeros(1, device=DEV).add_(1)  # the context still runs work
     torch.cuda.synchronize()
+
+
+def test_expert_parallel_all_to_all_world_of_one_matches_fused_moe():
+    """The expert-parallel dispatch / grouped GEMMs / combine (moe.cu ep_* kernels) as a world of one
+    rank holding every expert, against the single-GPU fused MoE block on the same rows."""
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.models.moe import MoEBlock
+
+    C = ops.require_ext()
+    cfg = preset("tiny-moe")
+    tensors = random_tensors(cfg, POLICIES["tiny-moe"], seed=2)
+    moe = MoEBlock(cfg, tensors, "blk.0.", DEV)
+    rows, H, E, k = 37, cfg.hidden, moe.E, moe.k
+    g = torch.Generator().manual_seed(8)
+    hb = torch.randn(rows, H, generator=g).half().to(DEV)
+    x0 = torch.randn(rows, H, generator=g).to(DEV)
+
+    class _R:  # what MoEBlock.forward reads from its runner
+        ser_threshold, fused_moe, x2 = 0.0, True, True
+
+    ref = x0.clone()
+    moe.forward(_R(), None, hb, rows, ref)
+    i32 = lambda n: torch.zeros(n, dtype=torch.int32, device=DEV)  # noqa: E731
+    cap = rows * k
+    cnt, cf, df, yf = i32(E), i32(1), i32(1), i32(1)
+    rx = torch.zeros(cap, H, dtype=torch.float16, device=DEV)
+    ys = torch.zeros(cap, H, device=DEV)
+    counts, cursor, off, pos = i32(E), i32(E), i32(E + 1), i32(rows * k * 2)
+    ids, wts = i32(rows * k).view(rows, k), torch.zeros(rows, k, device=DEV)
+    epoch, done, d = i32(1), i32(2), i32(cap + E)
+    for call in range(2):  # two layers' worth: the epoch and the zeroed counters carry over
+        logits = hb.float() @ moe.router.T
+        ra = moe._route_args(0.0)
+        C.moe_route(logits.contiguous(), k, int(ra["sigmoid"]), int(ra["renorm"]), ra["n_group"], ra["topk_group"],
+                    0.0, ra["scale"], hb, ids, wts, counts, d, d, d, d.float(), d, None)
+        args = (0, E, E, k, rows, ids, wts, counts, cursor, [cnt.data_ptr()], [cf.data_ptr()], hb, [rx.data_ptr()],
+                [df.data_ptr()], pos, off, [ys.data_ptr()], [yf.data_ptr()])
+        C.ep_call(0, *args, None, epoch, done, cap, 5.0)
+        h = ops.gemm_grouped(moe.gate_up, rx, off, E, ops.EPI_SWIGLU_Q8)
+        ops.gemm_grouped(moe.down, h, off, E, ops.EPI_STORE_F32, out=ys)
+        out = x0.clone()
+        C.ep_call(1, *args, out, epoch, done, cap, 5.0)
+        torch.cuda.synchronize()
+        assert ops.gemm_error() == 0
+        assert int(epoch) == call + 1 and int(counts.abs().sum()) == 0 and int(cursor.abs().sum()) == 0
+        assert int(off[-1]) == int((wts > 0).sum())
+        assert torch.allclose(out, ref, atol=2e-3 * ref.abs().max().item(), rtol=1e-3), (out - ref).abs().max()

@@ -55,13 +55,15 @@ def _worker(rank, world, port, name, mode, q):
 
     import dataclasses
 
-    cfg = (dataclasses.replace(preset("tiny"), hidden=512, n_heads=8, n_kv_heads=8, head_dim=64, ffn=1024)
-           if name == "tiny-sp" else preset(name))
+    wide = dict(hidden=512, n_heads=8, n_kv_heads=8, head_dim=64, ffn=1024)
+    cfg = (dataclasses.replace(preset("tiny"), **wide) if name == "tiny-sp" else
+           dataclasses.replace(preset("tiny-moe"), n_experts=8, **wide) if name == "tiny-moe-sp" else preset(name))
     full = random_tensors(cfg, POLICIES["tiny"], seed=4)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
     comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden,
-                hidden=cfg.hidden if mode in ("push", "sp") else 0, sp_tokens=64 if mode == "sp" else 0)
+                hidden=cfg.hidden if mode in ("push", "sp") else 0, sp_tokens=64 if mode == "sp" else 0,
+                ep_experts=cfg.n_experts if mode == "sp" else 0, ep_topk=cfg.n_experts_used)
     shard, info = shard_tensors(cfg, full, rank, world)
     r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
     r.allocate_kv(32)
@@ -72,6 +74,8 @@ def _worker(rank, world, port, name, mode, q):
         assert pushes > 0, pushes
     if mode == "sp":  # the 20-token prefill ran sequence-parallel: both sites advanced once per layer
         assert int(comm.sp_epoch[0]) == cfg.n_layers and int(comm.sp_epoch[1]) == cfg.n_layers + 1, comm.sp_epoch
+        if cfg.n_experts:  # ... and every MoE layer went through the expert all-to-all
+            assert int(comm.ep_epoch[0]) == cfg.n_layers, comm.ep_epoch
     if rank == 0:
         ref = LlamaRunner(cfg, full, dev)
         ref.allocate_kv(32)
@@ -110,6 +114,13 @@ def test_tp_sequence_parallel_matches_single_gpu(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     _run_tp(world, "tiny-sp", "sp")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_expert_parallel_all_to_all_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_tp(world, "tiny-moe-sp", "sp")
 
 
 def _pp_worker(rank, world, port, q):
