@@ -97,7 +97,7 @@ class Comm:
 
         W = self.world
         chunk = -(-T_max // W)
-        max_tiles = -(-H // 128) * -(-T_max // 64)
+        max_tiles = -(-H // 128) * -(-T_max // 32)
         al = lambda n: (n + 255) // 256 * 256  # noqa: E731  (byte offsets kept 256-aligned)
         o_slots = 0
         o_ag = o_slots + al(W * chunk * H * 4)

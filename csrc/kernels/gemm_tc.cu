@@ -272,11 +272,18 @@ BARQ_DEV void dequant32(const uint8_t* ch, int r, int sub64, int h, uint4* out) 
   }
 }
 
+// Whether token tiles of up to 128 rows take the weight operand from TMEM (1) or from shared memory
+// (0); see Issuers below.
+#ifndef BARQ_GEMM_TS
+#define BARQ_GEMM_TS 1
+#endif
+constexpr bool kGemmTS = BARQ_GEMM_TS != 0;
+
 template <int WT, int BN, int S, int SQ, int KS>
 struct GemmSmem {
   static constexpr int A_ATOM = 128 * 128;        // 128 rows x 64 fp16/bf16 (one 128B-swizzle atom column)
   static constexpr int B_ATOM = BN * 128;         // BN rows x 64 fp16/bf16
-  static constexpr int A_BYTES = BN <= 128 ? 0 : KS * A_ATOM;  // one stage: KS x 64 columns (TS: in TMEM)
+  static constexpr int A_BYTES = (kGemmTS && BN <= 128) ? 0 : KS * A_ATOM;  // one stage: KS x 64 columns (TS: in TMEM)
   static constexpr int B_BYTES = KS * B_ATOM;
   static constexpr int Q_BYTES = TileFmt<WT>::CHUNK;
   static constexpr int XCH_BYTES = 4 * 32 * 32 * 4;  // SwiGLU exchange, one 32x32 f32 tile per quadrant
@@ -311,7 +318,7 @@ constexpr int kThreads = (kDequantWarps + 8) * 32;
 template <int BN>
 struct Issuers {
   static constexpr int NI = BN <= 64 ? 2 : 1;
-  static constexpr bool TS = BN <= 128;
+  static constexpr bool TS = kGemmTS && BN <= 128;
   static constexpr int ACOL = 2 * NI * BN;            // first TMEM column of the operand stages
   static constexpr int COLS = TS ? 512 : 2 * NI * BN;
 };
@@ -725,12 +732,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               g.out_f32[idx] = g.row_w[t] * val;
             } else if (g.mode == EPI_STORE_BF16) {
               out_act[idx] = from_f<AT>(val);
+            } else if (atomic) {
+              part[(size_t)(c0 + j) * 128 + r] = val;
             } else if (g.mode == EPI_RS_PUSH) {
               // reduce-scatter: this rank's partial of row t goes straight into its owner's slot
               const int o = t / g.rs.chunk;
               g.rs.slots[o][((size_t)g.rs.rank * g.rs.chunk + (t - o * g.rs.chunk)) * g.N + n] = val;
-            } else if (atomic) {
-              part[(size_t)(c0 + j) * 128 + r] = val;
             } else if (g.mode == EPI_ADD_F32) {
               g.out_f32[idx] += val;
             } else {
@@ -742,16 +749,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accEmpty[buf]);
-      if (g.mode == EPI_RS_PUSH) {
-        // every thread's stores reach the owners before the tile's flag (release at system scope)
-        __threadfence_system();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (quad == 0 && lane < g.rs.world) {
-          const int o = lane;
-          if (o * g.rs.chunk < t_end && (o + 1) * g.rs.chunk > t0)
-            st_release_sys(g.rs.flags[o] + (size_t)g.rs.rank * g.rs.max_tiles + split_tile, rs_ep);
-        }
-      }
       if (atomic) {
         // the accumulator is released; combine the splits of this tile if this split is the last
         __threadfence();
@@ -787,7 +784,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                   s4.z += v[h][zz].z;
                   s4.w += v[h][zz].w;
                 }
-                float4* o = reinterpret_cast<float4*>(g.out_f32 + (size_t)(t0 + c + 4 * h) * g.ld_out + n4);
+                const int t = t0 + c + 4 * h;
+                if (g.mode == EPI_RS_PUSH) {  // the summed tile goes to its owner (reduce-scatter)
+                  const int ow = t / g.rs.chunk;
+                  *reinterpret_cast<float4*>(g.rs.slots[ow] + ((size_t)g.rs.rank * g.rs.chunk + (t - ow * g.rs.chunk)) *
+                                                                  g.N + n4) = s4;
+                  continue;
+                }
+                float4* o = reinterpret_cast<float4*>(g.out_f32 + (size_t)t * g.ld_out + n4);
                 if (g.mode == EPI_ADD_F32) {
                   const float4 prev = *o;
                   s4.x += prev.x;
@@ -802,6 +806,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (quad == 0 && lane == 0) g.split_cnt[split_tile] = 0;
         }
         asm volatile("bar.sync 2, 128;" ::: "memory");  // split_last_s is read before the next tile
+      }
+      if (g.mode == EPI_RS_PUSH && (!atomic || split_last_s)) {
+        // (split-K: only the split that summed the tile pushed it)
+        // every thread's stores reach the owners before the tile's flag (release at system scope)
+        __threadfence_system();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (quad == 0 && lane < g.rs.world) {
+          const int o = lane;
+          if (o * g.rs.chunk < t_end && (o + 1) * g.rs.chunk > t0)
+            st_release_sys(g.rs.flags[o] + (size_t)g.rs.rank * g.rs.max_tiles + split_tile, rs_ep);
+        }
       }
     }
   }
@@ -1002,13 +1017,16 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   if (g.k_splits == 0) {  // automatic split-K so that small token counts still fill the SMs
     const int tiles = ((g.N + 127) / 128) * tiles_t, n = sm_count();
     int ks = 1;
-    if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32) && g.ld_out % 4 == 0 && g.N % 4 == 0)
+    if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32 || g.mode == EPI_RS_PUSH) && g.ld_out % 4 == 0 &&
+        g.N % 4 == 0)
       while (ks < kMaxAutoSplits && tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
     g.k_splits = ks;
   }
   if (g.k_splits > KG) g.k_splits = KG;
   if (g.k_splits > kMaxAutoSplits) g.k_splits = kMaxAutoSplits;
-  if (g.k_splits > 1 && (g.ld_out % 4 || g.N % 4 || (reinterpret_cast<uintptr_t>(g.out_f32) & 15))) g.k_splits = 1;
+  if (g.k_splits > 1 && (g.ld_out % 4 || g.N % 4 ||
+                         (g.mode != EPI_RS_PUSH && (reinterpret_cast<uintptr_t>(g.out_f32) & 15))))
+    g.k_splits = 1;
   if (g.k_splits > 1) {
     const long tiles = (long)((g.N + 127) / 128) * tiles_t;
     // the split workspace holds kSplitWsFloats; fewer splits when a call would need more
@@ -1022,8 +1040,14 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   }
   // TS tiles: the operand stages fill the TMEM columns left after the accumulators (256 of 512)
   constexpr int S_TS = 256 / (KSW * 32);
-  if (bn == 64) return launch_gemm<WT, 64, S_TS, chunk_slots<WT, 64, S_TS, KSW>(), KSW, F16>(mx, g, tiles_t, st);
-  if (bn == 128) return launch_gemm<WT, 128, S_TS, chunk_slots<WT, 128, S_TS, KSW>(), KSW, F16>(mx, g, tiles_t, st);
+  // 32-row token tiles (<= 32 tokens): half the MMA width of a 64-row tile, and the TMEM the smaller
+  // accumulators leave free holds 6 operand stages instead of 4
+  constexpr int S32 = kGemmTS ? (512 - 2 * Issuers<32>::NI * 32) / (KSW * 32) : 4;
+  constexpr int S64 = kGemmTS ? S_TS : 3;
+  constexpr int S128 = kGemmTS ? S_TS : 2;
+  if (bn == 32) return launch_gemm<WT, 32, S32, chunk_slots<WT, 32, S32, KSW>(), KSW, F16>(mx, g, tiles_t, st);
+  if (bn == 64) return launch_gemm<WT, 64, S64, chunk_slots<WT, 64, S64, KSW>(), KSW, F16>(mx, g, tiles_t, st);
+  if (bn == 128) return launch_gemm<WT, 128, S128, chunk_slots<WT, 128, S128, KSW>(), KSW, F16>(mx, g, tiles_t, st);
   return launch_gemm<WT, 256, 3, chunk_slots<WT, 256, 3, 1>(), 1, F16>(mx, g, tiles_t, st);
 }
 
@@ -1052,7 +1076,8 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
       return -12;
     const int tiles = ((w.N + 127) / 128) * ((T + gemm_tile_rows(T) - 1) / gemm_tile_rows(T));
     if (tiles > rs->max_tiles) return -13;
-    k_splits = 1;
+    for (int q = 0; q < rs->world; ++q)
+      if (reinterpret_cast<uintptr_t>(rs->slots[q]) & 15) return -12;
   }
   if (agw && (grp || !agw->flags || !agw->epoch)) return -14;
   if (grp) {

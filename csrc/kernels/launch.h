@@ -43,7 +43,7 @@ int qgemv(const QW& w, const ActQ8& x, const __nv_bfloat16* xb, int ldxb, int B,
 // rows [r * chunk, min(T, (r + 1) * chunk)) of the residual stream.
 constexpr int kSpMaxRanks = 8;
 // Token-tile height of the non-grouped tcgen05 GEMM for T rows (the RS flags are per GEMM tile).
-inline int gemm_tile_rows(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
+inline int gemm_tile_rows(int T) { return T <= 32 ? 32 : T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
 
 // Row-parallel GEMM -> reduce-scatter: every finished output tile is stored (plain f32 stores over
 // NVLink) into the owner rank's receive slots [src rank][chunk][N], then flagged there with the

@@ -12,6 +12,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v"
                if os.environ.get("BARQ_PTXAS_V") else "-DBARQ_QUIET=1"]
+# BARQ_DIAG=1: compile the mainloop diagnostic switches (BARQ_GEMM_EXP / BARQ_GEMV_EXP) in
+if os.environ.get("BARQ_DIAG"):
+    NVCC.append("-DBARQ_DIAG=1")
+if os.environ.get("BARQ_GEMM_TS"):  # 0: weight operand through shared memory for every tile size
+    NVCC.append("-DBARQ_GEMM_TS=" + os.environ["BARQ_GEMM_TS"])
 CXX = ["-O3", "-std=c++17"]
 
 kernels = sorted(glob.glob(os.path.join("csrc", "kernels", "*.cu")))

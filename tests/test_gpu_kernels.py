@@ -321,7 +321,7 @@ GEMM_TYPES = [GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q5_K, GGMLType.Q8_0, GGMLTy
 
 
 @pytest.mark.parametrize("t", GEMM_TYPES)
-@pytest.mark.parametrize("T", [1, 37, 64, 200, 300])
+@pytest.mark.parametrize("T", [1, 16, 32, 37, 64, 200, 300])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 def test_gemm_tc(t, T, dt):
     N, K = 384, 1024

@@ -37,7 +37,7 @@ def test_rs_reduce_norm_ag_gemm_matches_fp32(W, T, dt):
     C = ops.require_ext()
     H, Kr, N2 = 512, 256, 384  # hidden, per-rank K of the row-parallel GEMM, next GEMM's rows
     chunk = -(-T // W)
-    max_tiles = -(-H // 128) * -(-T // 64)
+    max_tiles = -(-H // 128) * -(-T // 32)
     ws = [_qw(H, Kr, 10 + r) for r in range(W)]          # rank r's row-parallel shard
     xs = [torch.randn(T, Kr, generator=torch.Generator().manual_seed(20 + r)).to(dt) for r in range(W)]
     x0 = torch.randn(T, H, generator=torch.Generator().manual_seed(3))  # residual stream before the add
