@@ -230,10 +230,11 @@ def rope_kv_write(qkv, pos, slots, cos_t, sin_t, H, Hkv, D, rot, neox, kcache, v
 
 
 def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
-    """KV splits per (sequence, KV head): about 4 CTAs per SM (each CTA streams its pages with 4
-    warps, so this keeps ~16 page loads in flight per SM), at most 16 (a split of a typical decode
-    context still holds several 16-token pages)."""
-    return max(1, min(16, math.ceil(4 * n_sm / max(1, B * Hkv))))
+    """KV splits per (sequence, KV head): just enough CTAs to give every SM one (at most 16).  Each
+    decode-attention CTA streams its pages through a deep shared-memory ring, so longer page ranges
+    per CTA beat more CTAs: measured on B200 at 32 sequences x 1024 tokens x 8 KV heads, 1 split
+    (256 CTAs) runs 39.6 us, 3 splits 44.3 us, 16 splits 76.4 us."""
+    return max(1, min(16, -(-n_sm // max(1, B * Hkv))))
 
 
 def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,

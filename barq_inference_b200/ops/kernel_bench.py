@@ -11,6 +11,7 @@ cases, run a few times without timing (``--iters 3 --no-graph``), are the profil
 from __future__ import annotations
 
 import argparse
+import os
 
 import torch
 
@@ -150,7 +151,32 @@ def cases(tokens: int):
             return _qw(128, 256, GGMLType.Q4_K, 8), (lambda: r.forward(step)), 0.0
         return make
 
-    return {"allreduce_w1": allreduce_w1, "decode_step_bs1": decode_step(1, 64),
+    def attn_decode(B: int, ctx: int):
+        # one layer's decode attention of Llama-3-8B shapes: B sequences of ctx tokens, 32 query /
+        # 8 KV heads of 128, fp16 paged KV (16-token pages, scattered); bytes = the K/V stream
+        def make():
+            from . import decode_attention
+
+            H, Hkv, D = 32, 8, 128
+            pages = (ctx + 15) // 16
+            nb = B * pages + 1
+            kc = torch.randn(nb, Hkv, 16, D, device="cuda").half()
+            vc = torch.randn(nb, Hkv, 16, D, device="cuda").half()
+            bt = (torch.randperm(nb - 1, device="cuda")[: B * pages] + 1).int().view(B, pages)
+            lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+            q = torch.randn(B, H, D, device="cuda").bfloat16()
+
+            class _W:  # bytes streamed per call, for the GB/s column
+                @staticmethod
+                def nbytes():
+                    return B * ctx * Hkv * D * 2 * 2
+            sp = int(os.environ.get("BARQ_BENCH_SPLITS", "0")) or None  # sweep knob of this case
+            return _W, (lambda: decode_attention(q, kc, vc, bt, lens, H, Hkv, D, D ** -0.5, splits=sp)), \
+                4.0 * B * H * ctx * D
+        return make
+
+    return {"allreduce_w1": allreduce_w1, "attn_decode_bs32": attn_decode(32, 1024),
+            "attn_decode_bs1": attn_decode(1, 1024), "decode_step_bs1": decode_step(1, 64),
             "decode_step_bs32": decode_step(32, 1024), "decode_step_bs64": decode_step(64, 1024), "gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
             "gemv_head": gemv_head, "gemv_qkv": gemv_qkv, "gemv_o_tp2": gemv_o_tp2(False),
             "gemv_o_tp2_push": gemv_o_tp2(True)}

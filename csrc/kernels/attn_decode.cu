@@ -4,96 +4,80 @@
 // (backend/src/cuda_flash_attn.rs:165-359) and the CPU path loops over heads and query rows
 // (models/src/transformer.rs:301-374).
 //
-// Grid (splits, Hkv, B), 4 warps per CTA.  All G = H/Hkv query heads of a KV head share one CTA,
-// so every K/V page (16 tokens x D, fp16/bf16) is read from HBM once per step.  A warp takes one
-// page at a time: for QK^T two lanes share a token (each half of D in interleaved 16-byte chunks,
-// which keeps both the page loads coalesced and the shared-memory q reads conflict-free); for PV
-// each lane owns D/32 output dims and receives the probabilities by shuffle.  Each warp keeps an
-// online-softmax state; the CTA merges its 4 warps and writes an unnormalized partial per split.
+// Grid (splits, Hkv, B), 4 compute warps + 1 copy warp per CTA.  All G = H/Hkv query heads of a KV
+// head share one CTA, so every K/V page (16 tokens x D) is read from HBM once per step.  The copy
+// warp streams the CTA's pages (cp.async, 16-byte pieces into rows padded for conflict-free
+// ldmatrix; an fp8 cache is widened to fp16 on the way) into a 6-slot shared-memory ring ahead of
+// the compute warps, which signal per slot through mbarriers.  Compute warp w takes pages w, w+4,
+// ...: S = Q K^T for the G query heads (MMA rows, padded to 16) x 16 tokens on the tensor cores
+// (mma.m16n8k16, fp32 accumulate, 2 x D/16 MMAs), online softmax in the log2 domain on the
+// accumulator fragments, O += P V (D/8 MMAs) with P taken straight from the S fragments.  The CTA
+// merges its 4 warps and writes an unnormalized partial per split.
 // The splits are then merged (normalized, written as bf16/fp16 and as the int8 q8 activation of
 // the output projection) by the last split CTA of each (sequence, KV head) to arrive -- a counter
 // per (b, kv head) finds it, and it resets the counter -- or, without counters, by a second kernel.
 #include "common.cuh"
 #include "pdl.cuh"
 #include "launch.h"
+#include "tc_common.cuh"
+#include "mma_sync.cuh"
+
+#include <type_traits>
 
 namespace barq {
 
-// 8 consecutive K elements (one "chunk") of a row as floats: 16-byte loads for 2-byte types, 8-byte
-// loads for fp8.
-template <typename TC>
-BARQ_DEV void load_k8(const TC* row, int chunk, float* f);
-template <typename TC> BARQ_DEV void cvt8(const int4& raw, float* f);
-template <> BARQ_DEV void cvt8<__half>(const int4& raw, float* f) {
-  const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 v = __half22float2(h[i]);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
-}
-template <> BARQ_DEV void cvt8<__nv_bfloat16>(const int4& raw, float* f) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 v = __bfloat1622float2(h[i]);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
-}
-
-template <> BARQ_DEV void load_k8<__half>(const __half* row, int chunk, float* f) {
-  cvt8<__half>(__ldg(reinterpret_cast<const int4*>(row) + chunk), f);
-}
-template <> BARQ_DEV void load_k8<__nv_bfloat16>(const __nv_bfloat16* row, int chunk, float* f) {
-  cvt8<__nv_bfloat16>(__ldg(reinterpret_cast<const int4*>(row) + chunk), f);
-}
-template <> BARQ_DEV void load_k8<__nv_fp8_e4m3>(const __nv_fp8_e4m3* row, int chunk, float* f) {
-  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(row) + chunk);
-  const __nv_fp8_e4m3* e = reinterpret_cast<const __nv_fp8_e4m3*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = static_cast<float>(e[i]);
-}
-
 constexpr int kBS = 16;  // tokens per KV page
 
-// This lane's DPL consecutive V elements of one token, kept packed in registers until used.
-template <typename TC, int DPL>
-struct VRow {
-  static constexpr int BYTES = DPL * (int)sizeof(TC);
-  using R = typename std::conditional<BYTES == 8, uint2,
-                                      typename std::conditional<BYTES == 4, uint32_t, unsigned short>::type>::type;
-  R r;
-  BARQ_DEV void load(const TC* p) { r = __ldg(reinterpret_cast<const R*>(p)); }
-  BARQ_DEV void cvt(float* f) const {
-    const TC* e = reinterpret_cast<const TC*>(&r);
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) f[i] = to_f(e[i]);
-  }
+constexpr int kAttnRing = 6;       // shared-memory page slots per CTA (3 CTAs per SM fit)
+constexpr int kAttnThreads = 160;  // 4 compute warps + 1 copy warp
+
+// Ring layout: per slot one K page and one V page of 16 tokens x D operands (fp16 / bf16; an fp8
+// cache is widened to fp16 by the copy warp), rows padded to D + 8 elements so that ldmatrix reads
+// are bank-conflict free.
+template <typename TM, int D>
+struct AttnRing {
+  static constexpr int LD = D + 8;
+  static constexpr int PAGE = kBS * LD * (int)sizeof(TM);
+  static constexpr int SLOT = 2 * PAGE;
+  static constexpr int QBYTES = 16 * LD * (int)sizeof(TM);  // the (padded) query heads, after the ring
+  static constexpr int BYTES = kAttnRing * SLOT + QBYTES;
 };
 
-template <typename TC, int D, int G>
-__global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
+// TC: cache element type; TM: tensor-core operand type (TC for fp16 / bf16, fp16 for fp8).
+template <typename TC, typename TM, int D, int G>
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArgs a) {
   pdl_wait();
   pdl_trigger();
   constexpr int NW = 4;
-  constexpr int CH = D / 8;        // 16-byte chunks per K row
-  constexpr int CPH = CH / 2;      // chunks per half-lane
-  constexpr int DPL = D / 32;      // output dims per lane
+  constexpr int KS = D / 16;  // k-steps of QK^T
+  constexpr int ND = D / 8;   // O n-blocks
+  using R = AttnRing<TM, D>;
+  constexpr int LD = R::LD;
+  static_assert(G <= 8, "query heads of a KV head fit the first 8 MMA rows");
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float LOG2E = 1.4426950408889634f;
+  const float sl2 = a.scale * 1.4426950408889634f;
 
-  __shared__ float q_s[G][D];
+  extern __shared__ __align__(128) uint8_t ring[];
+  TM* sQ = reinterpret_cast<TM*>(ring + kAttnRing * R::SLOT);
+  __shared__ __align__(8) uint64_t full[kAttnRing], empty[kAttnRing];
   __shared__ float m_s[NW][G], l_s[NW][G];
-  __shared__ float acc_s[NW][G][D];
+  __shared__ int err_s;
 
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    int g = i / D, d = i % D;
-    q_s[g][d] = __bfloat162float(a.q[((size_t)b * a.H + kvh * G + g) * D + d]) * a.scale * LOG2E;
+  if (threadIdx.x == 0) {
+    err_s = 0;
+    for (int i = 0; i < kAttnRing; ++i) {
+      tc::mbar_init(&full[i], 32);  // one arrival per copy-warp lane
+      tc::mbar_init(&empty[i], 1);
+    }
+    tc::fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 16 * D; i += blockDim.x) {  // query heads as MMA rows 0..G-1
+    const int r = i / D, d = i % D;
+    sQ[r * LD + d] = from_f<TM>(r < G ? __bfloat162float(a.q[((size_t)b * a.H + kvh * G + r) * D + d]) : 0.f);
   }
   __syncthreads();
+  volatile int* err = &err_s;
 
   const int seq_len = a.seq_lens[b];
   const int first_tok = a.window > 0 ? max(0, seq_len - a.window) : 0;
@@ -101,92 +85,158 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   const int nblk = (seq_len + kBS - 1) / kBS - blk0;
   const int per = (nblk + a.splits - 1) / a.splits;
   const int sb = blk0 + split * per;
-  const int se = min(blk0 + nblk, sb + per);
-
-  float m[G], l[G], acc[G][DPL];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -1e30f;
-    l[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) acc[g][j] = 0.f;
-  }
-  const int tok = lane >> 1, half = lane & 1;
+  const int npg = max(0, min(blk0 + nblk, sb + per) - sb);  // pages of this CTA
   const int* bt = a.block_tables + (size_t)b * a.max_blocks;
-  const TC* kc = reinterpret_cast<const TC*>(a.kcache);
-  const TC* vc = reinterpret_cast<const TC*>(a.vcache);
 
-  for (int blk = sb + warp; blk < se; blk += NW) {
-    const int phys = bt[blk];
-    const size_t page = ((size_t)phys * a.Hkv + kvh) * kBS;
-    const TC* krow = kc + (page + tok) * D;
-    // The page's V rows are loaded together with K (they do not depend on the scores), so a page
-    // costs one DRAM round trip instead of two.
-    const TC* vpage = vc + page * D;
-    VRow<TC, DPL> vr[kBS];
+  const int g = lane >> 2, tig = lane & 3;
+  float o[ND][4];
 #pragma unroll
-    for (int t = 0; t < kBS; ++t) vr[t].load(vpage + (size_t)t * D + lane * DPL);
-    float s[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = 0.f;
-#pragma unroll
-    for (int c = 0; c < CPH; ++c) {
-      const int chunk = 2 * c + half;
-      float kf[8];
-      load_k8<TC>(krow, chunk, kf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4* qv = reinterpret_cast<const float4*>(&q_s[g][chunk * 8]);
-        float4 q0 = qv[0], q1 = qv[1];
-        s[g] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
-                q1.z * kf[6] + q1.w * kf[7];
+  for (int j = 0; j < ND; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float mrow = -1e30f, lrow = 0.f;  // row g (rows g + 8 are padding)
+
+  if (warp == NW) {
+    // ---------------------------------------------------------------- copy warp
+    // Every lane copies 1/32 of each page pair (16-byte pieces into the padded rows) and arrives on
+    // the slot's barrier once its copies have landed.
+    const TC* kc = static_cast<const TC*>(a.kcache);
+    const TC* vc = static_cast<const TC*>(a.vcache);
+    constexpr int PIECES = kBS * D / 8;  // 8-element pieces per page
+    int pg = 0;  // physical page of entry (i & ~31) + lane: block-table entries fetched 32 at a time
+    for (int i = 0; i < npg; ++i) {
+      const int s = i % kAttnRing;
+      if ((i & 31) == 0) pg = i + lane < npg ? bt[sb + i + lane] : 0;
+      const int phys = __shfl_sync(0xffffffffu, pg, i & 31);
+      bool ok = true;
+      if (i >= kAttnRing) {
+        if (lane == 0) ok = tc::mbar_wait(&empty[s], ((i / kAttnRing) - 1) & 1, err, 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
       }
-    }
-    const int tpos = blk * kBS + tok;
-    const bool valid = tpos < seq_len && tpos >= first_tok;
+      if (!ok) break;
+      const size_t page = ((size_t)phys * a.Hkv + kvh) * kBS * D;
+      TM* dk = reinterpret_cast<TM*>(ring + s * R::SLOT);
+      TM* dv = reinterpret_cast<TM*>(ring + s * R::SLOT + R::PAGE);
+      for (int pc = lane; pc < PIECES; pc += 32) {
+        const int r = pc / (D / 8), c = (pc % (D / 8)) * 8;
+        if constexpr (std::is_same<TC, TM>::value) {
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dk + r * LD + c)),
+                       "l"(kc + page + r * D + c));
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dv + r * LD + c)),
+                       "l"(vc + page + r * D + c));
+        } else {  // fp8 cache: 8 elements -> 8 fp16 operands
+          const uint2 rk = __ldg(reinterpret_cast<const uint2*>(kc + page + r * D + c));
+          const uint2 rv = __ldg(reinterpret_cast<const uint2*>(vc + page + r * D + c));
+          const TC* ek = reinterpret_cast<const TC*>(&rk);
+          const TC* ev = reinterpret_cast<const TC*>(&rv);
+          TM tk[8], tv[8];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s[g] += __shfl_xor_sync(0xffffffffu, s[g], 1);
-      if (!valid) s[g] = -INFINITY;
-    }
-    // online softmax update (scores already in log2 units)
-    float p[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mx = warp_max(s[g]);
-      float mn = fmaxf(m[g], mx);
-      float corr = exp2f(m[g] - mn);
-      p[g] = exp2f(s[g] - mn);
-      float ps = warp_sum(half == 0 ? p[g] : 0.f);
-      l[g] = l[g] * corr + ps;
-      m[g] = mn;
-#pragma unroll
-      for (int j = 0; j < DPL; ++j) acc[g][j] *= corr;
-    }
-#pragma unroll
-    for (int t = 0; t < kBS; ++t) {
-      float vf[DPL];
-      vr[t].cvt(vf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float pt = __shfl_sync(0xffffffffu, p[g], 2 * t);
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) acc[g][j] += pt * vf[j];
+          for (int j = 0; j < 8; ++j) {
+            tk[j] = from_f<TM>(to_f(ek[j]));
+            tv[j] = from_f<TM>(to_f(ev[j]));
+          }
+          *reinterpret_cast<int4*>(dk + r * LD + c) = *reinterpret_cast<int4*>(tk);
+          *reinterpret_cast<int4*>(dv + r * LD + c) = *reinterpret_cast<int4*>(tv);
+        }
       }
+      if constexpr (std::is_same<TC, TM>::value)
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
+      else
+        tc::mbar_arrive(&full[s]);
+    }
+    // copies in flight land before the ring is reused or the CTA exits
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else {
+    // ---------------------------------------------------------------- compute warps (mma.m16n8k16)
+    uint32_t qf[KS][4];
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = kk * 16 + (lane >> 4) * 8;
+      ldsm_x4(qf[kk], smem_u32(sQ + r * LD + c));
+    }
+    for (int i = warp; i < npg; i += NW) {
+      const int s = i % kAttnRing;
+      if (*err || !tc::mbar_wait(&full[s], (uint32_t)((i / kAttnRing) & 1), err, 2)) break;
+      const TM* k_s = reinterpret_cast<const TM*>(ring + s * R::SLOT);
+      const TM* v_s = reinterpret_cast<const TM*>(ring + s * R::SLOT + R::PAGE);
+      // S = Q K^T: 16 (head) rows x 16 tokens
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t kf[4];
+        const int r = (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(kf, smem_u32(k_s + r * LD + c));
+        MmaT<TM>::mma(sc[0], qf[kk], kf);
+        MmaT<TM>::mma(sc[1], qf[kk], kf + 2);
+      }
+      // mask + online softmax of row g (log2 domain)
+      float mnew = mrow;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kpos = (sb + i) * kBS + j * 8 + 2 * tig + e;
+          const bool ok = kpos < seq_len && kpos >= first_tok;
+          const float v = ok ? sc[j][e] * sl2 : -INFINITY;
+          sc[j][e] = v;
+          mnew = fmaxf(mnew, v);
+        }
+      mnew = fmaxf(mnew, __shfl_xor_sync(0xffffffffu, mnew, 1));
+      mnew = fmaxf(mnew, __shfl_xor_sync(0xffffffffu, mnew, 2));
+      const float corr = exp2f(mrow - mnew);
+      float psum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float p = exp2f(sc[j][e] - mnew);
+          sc[j][e] = p;
+          psum += p;
+        }
+        sc[j][2] = sc[j][3] = 0.f;  // padding rows g + 8
+      }
+      psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+      lrow = lrow * corr + psum;
+      mrow = mnew;
+#pragma unroll
+      for (int j = 0; j < ND; ++j) {
+        o[j][0] *= corr;
+        o[j][1] *= corr;
+      }
+      // O += P V (16 tokens = one k-step)
+      uint32_t pf[4];
+      pf[0] = MmaT<TM>::pack(sc[0][0], sc[0][1]);
+      pf[1] = MmaT<TM>::pack(sc[0][2], sc[0][3]);
+      pf[2] = MmaT<TM>::pack(sc[1][0], sc[1][1]);
+      pf[3] = MmaT<TM>::pack(sc[1][2], sc[1][3]);
+#pragma unroll
+      for (int jd = 0; jd < ND; jd += 2) {
+        uint32_t vf[4];
+        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = jd * 8 + (lane >> 4) * 8;
+        ldsm_x4_t(vf, smem_u32(v_s + r * LD + c));
+        MmaT<TM>::mma(o[jd], pf, vf);
+        MmaT<TM>::mma(o[jd + 1], pf, vf + 2);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
   }
-  // merge the 4 warps of this CTA
-  if (lane == 0) {
+  __syncthreads();  // the ring is free: every page was consumed and the copies drained
+  float(*acc_s)[G][D] = reinterpret_cast<float(*)[G][D]>(ring);  // [NW][G][D], aliases the ring
+  // merge the 4 compute warps of this CTA: rows g < G of each warp's O, m and l
+  if (warp < NW && g < G) {
+    if (tig == 0) {
+      m_s[warp][g] = mrow;
+      l_s[warp][g] = lrow;
+    }
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      m_s[warp][g] = m[g];
-      l_s[warp][g] = l[g];
+    for (int j = 0; j < ND; ++j) {
+      acc_s[warp][g][j * 8 + 2 * tig] = o[j][0];
+      acc_s[warp][g][j * 8 + 2 * tig + 1] = o[j][1];
     }
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) acc_s[warp][g][lane * DPL + j] = acc[g][j];
   __syncthreads();
   const size_t pbase = (((size_t)b * a.Hkv + kvh) * a.splits + split) * G;
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
@@ -289,16 +339,26 @@ size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits)
   return (size_t)B * H * splits * D + (size_t)B * H * splits * 2;
 }
 
+template <typename TC, int D, int G>
+static cudaError_t launch_attn(const DecodeAttnArgs& a, dim3 grid, cudaStream_t st) {
+  using TM = typename std::conditional<std::is_same<TC, __nv_fp8_e4m3>::value, __half, TC>::type;
+  auto kern = decode_attn_kernel<TC, TM, D, G>;
+  constexpr int smem = AttnRing<TM, D>::BYTES;
+  static const cudaError_t attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (attr != cudaSuccess) return attr;
+  return launch_pdl(kern, grid, dim3(kAttnThreads), (size_t)smem, st, a);
+}
+
 template <typename TC, int D>
 static int launch_g(const DecodeAttnArgs& a, cudaStream_t st) {
   const int G = a.H / a.Hkv;
   dim3 grid(a.splits, a.Hkv, a.B);
   cudaError_t e;
   switch (G) {
-    case 1: e = launch_pdl(decode_attn_kernel<TC, D, 1>, grid, dim3(128), 0, st, a); break;
-    case 2: e = launch_pdl(decode_attn_kernel<TC, D, 2>, grid, dim3(128), 0, st, a); break;
-    case 4: e = launch_pdl(decode_attn_kernel<TC, D, 4>, grid, dim3(128), 0, st, a); break;
-    case 8: e = launch_pdl(decode_attn_kernel<TC, D, 8>, grid, dim3(128), 0, st, a); break;
+    case 1: e = launch_attn<TC, D, 1>(a, grid, st); break;
+    case 2: e = launch_attn<TC, D, 2>(a, grid, st); break;
+    case 4: e = launch_attn<TC, D, 4>(a, grid, st); break;
+    case 8: e = launch_attn<TC, D, 8>(a, grid, st); break;
     default: return -3;
   }
   if (e != cudaSuccess) return -20;
