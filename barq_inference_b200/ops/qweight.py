@@ -19,6 +19,34 @@ from ..gguf.ik_quants import IK_TYPES
 
 NATIVE = {GGMLType.Q4_0, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q5_K, GGMLType.Q6_K, GGMLType.IQ4_NL}
 W_BF16 = 0
+# block-quantized GGUF types that are imported to the device by requantization to Q8_0
+_REQUANT = {GGMLType.Q5_0, GGMLType.Q5_1, GGMLType.Q4_1, GGMLType.Q2_K, GGMLType.Q3_K, GGMLType.IQ4_XS}
+
+
+def requant_q8_0(raw: torch.Tensor, t: GGMLType, N: int, K: int) -> torch.Tensor:
+    """GGUF rows of a block type without a kernel format -> Q8_0 rows (uint8 [N, K/32*34]).
+
+    Q5_0 is exact: its block (fp16 d, 5-bit q) maps to Q8_0's block (the same d, q - 16 as int8).
+    The others are dequantized (the ggml-spec oracle) and requantized to Q8_0, whose 255 levels
+    per 32 values add about 1/254 of each block's largest magnitude (plus the fp16 rounding of its scale) -- against the 4..16 levels
+    per (sub-)block of the source types.  Costs 8.5 bits per weight on the device instead of 2.6..6."""
+    dev = raw.device
+    nb = K // 32
+    if t == GGMLType.Q5_0:
+        b = raw.reshape(N, nb, 22)
+        d = b[..., 0:2]
+        qh = b[..., 2:6].to(torch.int64)
+        qh = qh[..., 0] | (qh[..., 1] << 8) | (qh[..., 2] << 16) | (qh[..., 3] << 24)
+        qs = b[..., 6:22].to(torch.int16)
+        j = torch.arange(16, device=dev)
+        lo = (qs & 0x0F) | (((qh[..., None] >> j) & 1) << 4).to(torch.int16)
+        hi = (qs >> 4) | (((qh[..., None] >> (j + 16)) & 1) << 4).to(torch.int16)
+        q = (torch.cat([lo, hi], -1) - 16).to(torch.int8).view(torch.uint8)
+        return torch.cat([d, q], -1).reshape(N, nb * 34).contiguous()
+    from ..gguf import quantize
+
+    w = torch.from_numpy(dequantize(raw.cpu().numpy(), t, (N, K))).to(dev, torch.float32)
+    return quantize(w, GGMLType.Q8_0).reshape(N, nb * 34)
 
 
 def _blocks(raw: torch.Tensor, N: int, t: GGMLType) -> torch.Tensor:
@@ -82,6 +110,10 @@ class QWeight:
 
             tt, q = import_ik(raw.cpu().numpy(), t, (N, K), dev)
             return QWeight.from_packed(q, tt, N, K, dev)
+        if t not in NATIVE and t in _REQUANT and K % 64 == 0:
+            # block types without a tiled kernel format (Q5_0, Q2_K, Q3_K, Q4_1, ...): import as Q8_0,
+            # which the GEMV / tcgen05 GEMM stream (exact for Q5_0, near-lossless otherwise)
+            return QWeight.from_packed(requant_q8_0(raw, t, N, K), GGMLType.Q8_0, N, K, dev)
         if t not in NATIVE or K % TILE_FMT[int(t)][0]:
             if t == GGMLType.BF16:
                 w = raw.contiguous().view(torch.bfloat16).reshape(N, K)

@@ -1,0 +1,48 @@
+"""Import of block types without a kernel format (Q5_0, Q2_K, Q3_K, Q4_1, Q5_1) as Q8_0 rows.
+
+Q5_0 maps exactly (same block size and scale); the others are requantized with an error of about
+one Q8_0 step (1/254 of each 32-value block's largest magnitude, plus the fp16 rounding of its
+scale).  Random block bytes with a fixed, finite fp16 scale are valid blocks of every type."""
+import numpy as np
+import pytest
+import torch
+
+from barq_inference_b200.gguf import GGMLType, dequantize, quantize
+from barq_inference_b200.ops.qweight import W_BF16, QWeight, requant_q8_0
+
+N, K = 8, 512
+LAYOUT = {GGMLType.Q3_K: (256, 110, [108]), GGMLType.Q2_K: (256, 84, [80, 82]),
+          GGMLType.Q4_1: (32, 20, [0, 2]), GGMLType.Q5_1: (32, 24, [0, 2]), GGMLType.Q5_0: (32, 22, [0])}
+
+
+def _random_blocks(t, seed=0):
+    qk, bs, doffs = LAYOUT[t]
+    raw = np.random.default_rng(seed).integers(0, 256, (N, K // qk, bs), dtype=np.uint8)
+    for o in doffs:
+        raw[..., o:o + 2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    return torch.from_numpy(raw.reshape(N, -1).copy())
+
+
+def test_q5_0_is_exact():
+    w = torch.randn(N, K, generator=torch.Generator().manual_seed(1))
+    raw = quantize(w, GGMLType.Q5_0)
+    q8 = requant_q8_0(raw, GGMLType.Q5_0, N, K)
+    assert np.array_equal(dequantize(q8.numpy(), GGMLType.Q8_0, (N, K)), dequantize(raw.numpy(), GGMLType.Q5_0, (N, K)))
+    assert np.array_equal(dequantize(requant_q8_0(_random_blocks(GGMLType.Q5_0), GGMLType.Q5_0, N, K).numpy(),
+                                     GGMLType.Q8_0, (N, K)),
+                          dequantize(_random_blocks(GGMLType.Q5_0).numpy(), GGMLType.Q5_0, (N, K)))
+
+
+@pytest.mark.parametrize("t", [GGMLType.Q3_K, GGMLType.Q2_K, GGMLType.Q4_1, GGMLType.Q5_1])
+def test_requantized_within_one_q8_step(t):
+    raw = _random_blocks(t)
+    ref = dequantize(raw.numpy(), t, (N, K))
+    got = dequantize(requant_q8_0(raw, t, N, K).numpy(), GGMLType.Q8_0, (N, K))
+    # half a Q8_0 step (max/254) plus the fp16 rounding of the scale (127 steps x 2^-11 of a step)
+    bound = np.abs(ref.reshape(N, -1, 32)).max(-1, keepdims=True) / 220
+    assert (np.abs(got - ref).reshape(N, -1, 32) <= bound).all()
+
+
+def test_loader_streams_requantized_types():
+    w = QWeight.from_packed(_random_blocks(GGMLType.Q3_K), GGMLType.Q3_K, N, K, "cpu")
+    assert w.wtype == int(GGMLType.Q8_0) and w.wtype != W_BF16
