@@ -83,6 +83,12 @@ def _paged_kv(engine):
     return kv
 
 
+def _scales(engine, layer: int):
+    """(K scales, V scales) [num_blocks, Hkv, block_size] of a scaled fp8 cache, else None."""
+    sc = getattr(engine.runner, "kv_scales", None)
+    return sc[layer] if sc else None
+
+
 def _bytes(t: torch.Tensor) -> torch.Tensor:
     """1-byte element types (fp8) viewed as uint8 for gathers and scatters."""
     return t.view(torch.uint8) if t.element_size() == 1 else t
@@ -105,6 +111,9 @@ def _gpu_export(engine, tokens: list[int]) -> dict:
         for name, P in (("k", K), ("v", V)):
             pg = _bytes(P).index_select(0, idx).view(P.dtype)  # fp8 pages move as bytes
             out[f"{name}.{i}"] = pg.permute(0, 2, 1, 3).reshape(-1, pg.shape[1], pg.shape[3]).cpu()
+        sc = _scales(engine, i)
+        for name, S in (() if sc is None else (("ks", sc[0]), ("vs", sc[1]))):  # fp8: per-row scales
+            out[f"{name}.{i}"] = S.index_select(0, idx).permute(0, 2, 1).reshape(-1, S.shape[1]).cpu()
     return {**_meta(engine.cfg), "tokens": torch.tensor(list(tokens)[:n], dtype=torch.int64), "kv": out}
 
 
@@ -124,6 +133,13 @@ def _gpu_import(engine, state: dict) -> int:
             rows = state["kv"][f"{name}.{i}"][: nb * bs]
             pg = rows.to(P.dtype).reshape(nb, bs, rows.shape[1], rows.shape[2]).permute(0, 2, 1, 3).contiguous()
             _bytes(P).index_copy_(0, idx, _bytes(pg).to(P.device))
+        sc = _scales(engine, i)
+        for name, S in (() if sc is None else (("ks", sc[0]), ("vs", sc[1]))):
+            rows = state["kv"].get(f"{name}.{i}")
+            if rows is None:
+                raise ValueError("the session has no per-row scales for this fp8 KV cache")
+            pg = rows[: nb * bs].to(S.dtype).reshape(nb, bs, S.shape[1]).permute(0, 2, 1).contiguous()
+            S.index_copy_(0, idx, pg.to(S.device))
     engine.prefix_cache.insert(toks[: nb * bs], blocks)  # the cache takes its own reference
     engine.blocks.release(blocks)
     return nb * bs

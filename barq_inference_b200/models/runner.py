@@ -144,6 +144,13 @@ class LlamaRunner:
         kv = torch.zeros(shape, dtype=self.kv_dtype, device=self.device)
         self.kv_storage = kv
         self.kv = [(kv[i, 0], kv[i, 1]) for i in range(nl)]
+        # fp8 cache: one f32 scale per stored row (K and V), [layer][2][block][kv head][slot]
+        self.kv_scale_storage = None
+        self.kv_scales = [None] * nl
+        if self.kv_dtype == torch.float8_e4m3fn:
+            sc = torch.ones(shape[:-1], dtype=torch.float32, device=self.device)
+            self.kv_scale_storage = sc
+            self.kv_scales = [(sc[i, 0], sc[i, 1]) for i in range(nl)]
         return self.kv
 
     def kv_bytes_per_block(self, block_size: int = 16) -> int:
@@ -323,13 +330,16 @@ class LlamaRunner:
         cfg = self.cfg
         H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         kc, vc = self.kv[li]
+        ks = self.kv_scales[li]
         q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
-                              cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
+                              cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps, kv_scales=ks)
         if inp.decode:
             return ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
-                                        cfg.sliding_window, want_q8=want_q8, x2=self.x2, act_dtype=self.act_dtype)
+                                        cfg.sliding_window, want_q8=want_q8, x2=self.x2, act_dtype=self.act_dtype,
+                                        kv_scales=ks)
         ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
-                                   H, Hkv, D, self.scale, cfg.sliding_window, act_dtype=self.act_dtype)
+                                   H, Hkv, D, self.scale, cfg.sliding_window, act_dtype=self.act_dtype,
+                                   kv_scales=ks)
         return ab, (ops.quantize_q8(ab, self.x2) if want_q8 else None)
 
     def _sp_ok(self, T: int) -> bool:
@@ -439,14 +449,15 @@ class LlamaRunner:
         for li, L in enumerate(self.layers):
             kc, vc = self.kv[li]
             qkv = self._norm_lin(L.qkv, x, L.attn_norm, T, EPI_STORE_F32, bias=L.qkv_bias)
+            ks = self.kv_scales[li]
             q = ops.rope_kv_write(qkv, inp.pos, inp.slots, self.cos, self.sin, H, Hkv, D, cfg.rot_dim,
-                                  cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps)
+                                  cfg.rope_neox, kc, vc, L.q_norm, L.k_norm, cfg.rms_eps, kv_scales=ks)
             if inp.decode:
                 ab, aq = ops.decode_attention(q, kc, vc, inp.block_tables, inp.seq_lens, H, Hkv, D, self.scale,
-                                              cfg.sliding_window, x2=self.x2)
+                                              cfg.sliding_window, x2=self.x2, kv_scales=ks)
             else:
                 ab = ops.prefill_attention(q, kc, vc, inp.block_tables, inp.q_start, inp.seq_lens, inp.max_q,
-                                           H, Hkv, D, self.scale, cfg.sliding_window)
+                                           H, Hkv, D, self.scale, cfg.sliding_window, kv_scales=ks)
                 aq = ops.quantize_q8(ab, self.x2)
             self._row_parallel(0, lambda m, o: self._lin_q8(L.wo, aq, T, m, out=o, xb=ab), x, gemv=(L.wo, aq, None))
             if L.moe is not None:

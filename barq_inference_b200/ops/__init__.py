@@ -220,11 +220,14 @@ def swiglu(gu: torch.Tensor, F: int, want_bf16: bool = True, want_q8: bool = Fal
 
 
 def rope_kv_write(qkv, pos, slots, cos_t, sin_t, H, Hkv, D, rot, neox, kcache, vcache,
-                  q_norm=None, k_norm=None, norm_eps=1e-6):
+                  q_norm=None, k_norm=None, norm_eps=1e-6, kv_scales=None):
+    """RoPE of q / k and the K/V cache write.  ``kv_scales`` (fp8 cache): f32 ``(kscale, vscale)``
+    [num_blocks, Hkv, block_size] -- each row is stored as e4m3(x / s) with s = max|x| / 448."""
     T = qkv.shape[0]
+    ks, vs = kv_scales if kv_scales is not None else (None, None)
     q_out = torch.empty(T, H, D, dtype=torch.bfloat16, device=qkv.device)
     require_ext().rope_kv_write(qkv, qkv.stride(0), pos, slots, cos_t, sin_t, q_norm, k_norm, norm_eps,
-                                T, H, Hkv, D, rot, neox, q_out, kcache, vcache)
+                                T, H, Hkv, D, rot, neox, q_out, kcache, vcache, ks, vs)
     _count()
     return q_out
 
@@ -238,7 +241,7 @@ def decode_splits(B: int, Hkv: int, n_sm: int = 148) -> int:
 
 
 def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale, window=0, splits=None,
-                     want_q8=True, scratch=None, x2=False, act_dtype=torch.bfloat16):
+                     want_q8=True, scratch=None, x2=False, act_dtype=torch.bfloat16, kv_scales=None):
     B = q.shape[0]
     C = require_ext()
     if splits is None:
@@ -250,7 +253,7 @@ def decode_attention(q, kcache, vcache, block_tables, seq_lens, H, Hkv, D, scale
     oq = Q8Act.empty(B, H * D, q.device, x2) if want_q8 else None
     cnt = _attn_counters(q.device, B * Hkv)
     C.decode_attention(q, kcache, vcache, block_tables, seq_lens, B, H, Hkv, D, scale, window, splits, scratch,
-                       out, *_outs(oq), cnt)
+                       out, *_outs(oq), cnt, *(kv_scales if kv_scales is not None else (None, None)))
     _count(1 if cnt is not None else 2)
     return out, oq
 
@@ -272,12 +275,12 @@ def _attn_counters(device, n: int):
 
 
 def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0,
-                      act_dtype=torch.bfloat16):
+                      act_dtype=torch.bfloat16, kv_scales=None):
     T = q.shape[0]
     S = block_tables.shape[0]
     out = torch.empty(T, H * D, dtype=act_dtype, device=q.device)
     require_ext().prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, S, max_q, H, Hkv, D,
-                                    scale, window, out)
+                                    scale, window, out, *(kv_scales if kv_scales is not None else (None, None)))
     _count()
     return out
 

@@ -189,8 +189,14 @@ class Comm:
         ops._count(5)
 
     # ------------------------------------------------------------------ sequence-parallel path
+    # Fewest tokens per step that run sequence-parallel.  Below it (batched decode) the partials
+    # go through the one-shot all-reduce kernel: at 32 tokens on 2 B200 the per-site reduce kernel
+    # and flag round trips of the sequence-parallel path cost more than they save (6.65 vs 5.25 ms
+    # per Llama-3-8B step), while prefill gains (76k vs 53k tok/s).
+    sp_min_tokens = int(os.environ.get("BARQ_SP_MIN_TOKENS", "128"))
+
     def sp_ok(self, T: int) -> bool:
-        return bool(self.sp_tokens) and 8 < T <= self.sp_tokens
+        return bool(self.sp_tokens) and max(9, self.sp_min_tokens) <= T <= self.sp_tokens
 
     def sp_rows(self, T: int) -> tuple[int, int, int]:
         """(chunk, first, end): this rank owns token rows [first, end) of a T-row step."""

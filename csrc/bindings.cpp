@@ -432,7 +432,7 @@ void swiglu(Tensor in, int64_t T, int64_t F, int64_t ld_in, OptT out_bf16, OptT 
 
 void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor cos_t, Tensor sin_t, OptT q_norm,
                    OptT k_norm, double norm_eps, int64_t T, int64_t H, int64_t Hkv, int64_t D, int64_t rot,
-                   bool neox, Tensor q_out, Tensor kcache, Tensor vcache) {
+                   bool neox, Tensor q_out, Tensor kcache, Tensor vcache, OptT kscale, OptT vscale) {
   c10::cuda::CUDAGuard g(qkv.device());
   barq::RopeKVArgs a;
   a.qkv = qkv.data_ptr();
@@ -451,12 +451,15 @@ void rope_kv_write(Tensor qkv, int64_t ld_qkv, Tensor pos, OptT slots, Tensor co
   a.vcache = vcache.data_ptr();
   a.cache_type = cache_type_of(kcache);
   a.block_size = (int)kcache.size(-2);
+  a.kscale = optptr<float>(kscale);
+  a.vscale = optptr<float>(vscale);
   check(barq::rope_kv_write(a, cur_stream()), "rope_kv_write");
 }
 
 void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor seq_lens, int64_t B,
                       int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window, int64_t splits, Tensor scratch,
-                      Tensor out, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl, OptT counters) {
+                      Tensor out, OptT out_q, OptT out_s, OptT out_ql, OptT out_dl, OptT counters, OptT kscale,
+                      OptT vscale) {
   c10::cuda::CUDAGuard g(q.device());
   TORCH_CHECK(scratch.scalar_type() == torch::kFloat32, "scratch must be f32");
   TORCH_CHECK(!counters || (counters->scalar_type() == torch::kInt32 && counters->numel() >= B * Hkv),
@@ -478,6 +481,8 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.splits = (int)splits;
   a.part_acc = ptr<float>(scratch);
   a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)B * H * splits * D);
+  a.kscale = optptr<const float>(kscale);
+  a.vscale = optptr<const float>(vscale);
   a.out = out.data_ptr();
   a.out_f16 = out.scalar_type() == torch::kHalf;
   a.out_q = act_out(out_q, out_s, out_ql, out_dl);
@@ -487,7 +492,7 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
 
 void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor q_start, Tensor ctx_lens,
                        int64_t S, int64_t max_q, int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window,
-                       Tensor out) {
+                       Tensor out, OptT kscale, OptT vscale) {
   c10::cuda::CUDAGuard g(q.device());
   barq::PrefillAttnArgs a;
   a.q = ptr<const __nv_bfloat16>(q);
@@ -504,6 +509,8 @@ void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tabl
   a.window = (int)window;
   a.out = out.data_ptr();
   a.out_f16 = out.scalar_type() == torch::kHalf;
+  a.kscale = optptr<const float>(kscale);
+  a.vscale = optptr<const float>(vscale);
   check(barq::prefill_attention(a, cur_stream()), "prefill_attention");
 }
 

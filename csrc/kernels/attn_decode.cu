@@ -127,11 +127,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
           const uint2 rv = __ldg(reinterpret_cast<const uint2*>(vc + page + r * D + c));
           const TC* ek = reinterpret_cast<const TC*>(&rk);
           const TC* ev = reinterpret_cast<const TC*>(&rv);
+          const size_t srow = ((size_t)phys * a.Hkv + kvh) * kBS + r;  // per-row scales (or unscaled)
+          const float ks = a.kscale ? a.kscale[srow] : 1.f, vs = a.vscale ? a.vscale[srow] : 1.f;
           TM tk[8], tv[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            tk[j] = from_f<TM>(to_f(ek[j]));
-            tv[j] = from_f<TM>(to_f(ev[j]));
+            tk[j] = from_f<TM>(to_f(ek[j]) * ks);
+            tv[j] = from_f<TM>(to_f(ev[j]) * vs);
           }
           *reinterpret_cast<int4*>(dk + r * LD + c) = *reinterpret_cast<int4*>(tk);
           *reinterpret_cast<int4*>(dv + r * LD + c) = *reinterpret_cast<int4*>(tv);

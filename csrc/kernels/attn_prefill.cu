@@ -97,10 +97,12 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
           const uint2 rv = __ldg(reinterpret_cast<const uint2*>(vc + off));
           const TC* ek = reinterpret_cast<const TC*>(&rk);
           const TC* ev = reinterpret_cast<const TC*>(&rv);
+          const size_t srow = ((size_t)phys * a.Hkv + kvh) * 16 + (pos & 15);  // per-row scales
+          const float ks = a.kscale ? a.kscale[srow] : 1.f, vs = a.vscale ? a.vscale[srow] : 1.f;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            tk[j] = from_f<TM>(to_f(ek[j]));
-            tv[j] = from_f<TM>(to_f(ev[j]));
+            tk[j] = from_f<TM>(to_f(ek[j]) * ks);
+            tv[j] = from_f<TM>(to_f(ev[j]) * vs);
           }
         } else {
 #pragma unroll

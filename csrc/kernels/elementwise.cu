@@ -199,11 +199,24 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeKVArgs a) {
       const int kvh = is_k ? h - a.H : h - a.H - a.Hkv;
       const int64_t blk = slot / a.block_size, off = slot % a.block_size;
       TC* cache = reinterpret_cast<TC*>(is_k ? a.kcache : a.vcache);
-      TC* dst = cache + (((size_t)blk * a.Hkv + kvh) * a.block_size + off) * D;
+      const size_t ri = ((size_t)blk * a.Hkv + kvh) * a.block_size + off;  // stored row
+      TC* dst = cache + ri * D;
+      float* sc = is_k ? a.kscale : a.vscale;
+      float inv = 1.f;
+      if (sc) {  // scaled fp8: the row's largest magnitude maps to e4m3's 448
+        float mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (lane + 32 * j < D) mx = fmaxf(mx, fabsf(o[j]));
+        mx = warp_max(mx);
+        const float s = mx > 0.f ? mx / 448.f : 1.f;
+        inv = 1.f / s;
+        if (lane == 0) sc[ri] = s;
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         int i = lane + 32 * j;
-        if (i < D) dst[i] = from_f<TC>(o[j]);
+        if (i < D) dst[i] = from_f<TC>(o[j] * inv);
       }
     }
   }

@@ -274,6 +274,10 @@ struct RopeKVArgs {
   void* vcache;
   int cache_type;           // KV cache element type: kCacheF16, kCacheBF16 or kCacheFP8 (e4m3)
   int block_size;
+  // fp8 cache: one f32 scale per stored row ([num_blocks, Hkv, block_size]); the row holds
+  // e4m3(x / scale) with scale = max|x| / 448.  Null: unscaled e4m3.
+  float* kscale = nullptr;
+  float* vscale = nullptr;
 };
 int rope_kv_write(const RopeKVArgs& a, cudaStream_t st);
 
@@ -297,6 +301,8 @@ struct DecodeAttnArgs {
   // optional [B * Hkv] zeroed arrival counters: the last split CTA of a (b, kv head) merges the
   // splits itself (no second launch); null = a separate merge kernel
   int* counters = nullptr;
+  const float* kscale = nullptr;  // fp8 cache: per-row scales (RopeKVArgs), null = unscaled
+  const float* vscale = nullptr;
 };
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
 size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits);
@@ -315,6 +321,8 @@ struct PrefillAttnArgs {
   int window;
   void* out;                // [T, H*D] activation dtype
   int out_f16;
+  const float* kscale = nullptr;  // fp8 cache: per-row scales (RopeKVArgs), null = unscaled
+  const float* vscale = nullptr;
 };
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st);
 

@@ -64,6 +64,8 @@ def _worker(rank, world, port, name, mode, q):
     comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden,
                 hidden=cfg.hidden if mode in ("push", "sp") else 0, sp_tokens=64 if mode == "sp" else 0,
                 ep_experts=cfg.n_experts if mode == "sp" else 0, ep_topk=cfg.n_experts_used)
+    if mode == "sp":
+        comm.sp_min_tokens = 9  # the 20-token prompt runs sequence-parallel
     shard, info = shard_tensors(cfg, full, rank, world)
     r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
     r.allocate_kv(32)
