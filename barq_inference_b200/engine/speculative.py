@@ -129,15 +129,28 @@ def _probs(logits: torch.Tensor, p: SamplingParams) -> torch.Tensor:
 
 
 def verify_drafts(ps: torch.Tensor, qs: torch.Tensor, drafts: torch.Tensor, greedy: bool,
-                  gen: torch.Generator | None = None) -> tuple[int, list[int]]:
+                  gen: torch.Generator | None = None, seed: int | None = None, step: int = 0) -> tuple[int, list[int]]:
     """Rejection step of speculative decoding for k drafted tokens, on the device of ``ps``.
 
     ps: target distributions [k+1, V] (rows for the positions of d1..dk and the bonus position);
     qs: draft distributions [k, V]; drafts: int64 [k].  Returns (number accepted, tokens to append):
     the accepted prefix plus either the correction sampled from norm(max(0, p - q)) at the first
     rejection or the bonus token sampled from the last target row.  Greedy: accept while the
-    target's argmax agrees, then append the target's argmax.  One host synchronization."""
+    target's argmax agrees, then append the target's argmax.  One host synchronization.
+
+    On a GPU with ``seed`` given, the whole step is one kernel (K14, csrc/kernels/sampler.cu; its
+    uniforms come from Philox keyed by ``seed`` at counter ``step``) and the result is one 4*(k+2)-byte
+    read; otherwise the torch ops below (CPU engine, or a caller-supplied torch.Generator)."""
     k = drafts.numel()
+    if ps.is_cuda and seed is not None:
+        from ..ops import require_ext
+
+        out = torch.empty(k + 2, dtype=torch.int32, device=ps.device)
+        require_ext().spec_verify(ps.float().contiguous(), None if greedy else qs.float().contiguous(),
+                                  drafts.to(torch.int64), int(greedy), int(seed) & ((1 << 63) - 1), int(step), out)
+        res = out.tolist()
+        n_acc = res[0]
+        return n_acc, res[1:n_acc + 2]
     ar = torch.arange(k, device=ps.device)
     if greedy:
         tgt = ps.argmax(-1)  # [k+1]
@@ -200,7 +213,8 @@ class SpeculativeDecoder:
                 # 2) target scores [last, d1..dk] in one forward -> k+1 distributions
                 ps = _probs(ts.forward([last] + drafts, True), params)
                 # 3) accept / reject on the device (one host synchronization)
-                n_acc, new = verify_drafts(ps, torch.cat(qs), torch.tensor(drafts, device=ps.device), greedy, gen)
+                n_acc, new = verify_drafts(ps, torch.cat(qs), torch.tensor(drafts, device=ps.device), greedy, gen,
+                                           seed=params.seed or 1234, step=len(out))
                 if n_acc == k:
                     self.stats.bonus += 1
                 self.stats.drafted += k

@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--parallel", default="tp", choices=["dp", "tp"],
                     help="tp: one tensor-parallel engine over all GPUs (strong scaling, default); dp: one engine "
                          "replica per GPU (weak scaling)")
+    ap.add_argument("--ser", type=float, default=0.0,
+                    help="MoE smart expert reduction: drop a routed expert whose gate weight is below this")
+    ap.add_argument("--no-fmoe", action="store_true", help="MoE: per-expert loop instead of the fused path")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="tp all-reduce: fused one-shot kernel over NVLink peer memory, or NCCL")
     return ap.parse_args()
@@ -150,7 +153,8 @@ def main():
     blocks_needed = B * (max_len // 16 + 2) + 64
     tp = world if args.parallel == "tp" else 1
     ec = EngineConfig(max_num_seqs=max(B, 1), max_num_batched_tokens=8192, max_model_len=max_len,
-                      num_blocks=blocks_needed, cuda_graphs=True, tp=tp, fused_comm=args.comm == "fused")
+                      num_blocks=blocks_needed, cuda_graphs=True, tp=tp, fused_comm=args.comm == "fused",
+                      ser_threshold=args.ser, fused_moe=not args.no_fmoe)
     eng = Engine(cfg, tensors, ec)
     del tensors
     torch.cuda.empty_cache()
@@ -308,7 +312,8 @@ def main():
                      "residual stream; fp16 KV",
             "data": "synthetic: random-init N(0,0.02) weights quantized to Q4_K/Q6_K, uniform-random prompt ids",
             "config": {"model": MODELS.get(args.model, args.model) + (f" ({cfg.n_layers} layers)" if args.layers else ""), "global_batch": B * mult,
-                       "seq_len": P, "parallelism": f"dp{world}" if tp == 1 else f"tp{world}-{args.comm}",
+                       "seq_len": P, "parallelism": (f"dp{world}" if tp == 1 else f"tp{world}-{args.comm}") +
+                       (f"-ser{args.ser}" if args.ser else "") + ("-nofmoe" if args.no_fmoe else ""),
                        "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)"},
             "extra": {
                 "decode_tok_s_bs1": round(mult * 1e3 / bs1_ms, 2),

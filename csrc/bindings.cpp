@@ -290,6 +290,19 @@ void ep_call(int64_t which, int64_t rank, int64_t E, int64_t E_local, int64_t k,
   }
 }
 
+void spec_verify(Tensor ps, OptT qs, Tensor drafts, int64_t greedy, int64_t seed, int64_t step, Tensor out) {
+  c10::cuda::CUDAGuard g(ps.device());
+  TORCH_CHECK(ps.scalar_type() == torch::kFloat32 && ps.is_contiguous() && ps.dim() == 2, "spec_verify: ps f32 [k+1, V]");
+  const int64_t k = drafts.numel();
+  TORCH_CHECK(ps.size(0) == k + 1 && drafts.scalar_type() == torch::kInt64, "spec_verify: ps rows / drafts");
+  TORCH_CHECK(greedy || (qs.has_value() && qs->is_contiguous() && qs->scalar_type() == torch::kFloat32 &&
+                         qs->size(0) >= k && qs->size(1) == ps.size(1)), "spec_verify: qs f32 [k, V]");
+  TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= k + 2, "spec_verify: out int32 [k+2]");
+  check(barq::spec_verify(ptr<const float>(ps), optptr<const float>(qs), ptr<const int64_t>(drafts), (int)k,
+                          (int)ps.size(1), (int)greedy, (uint64_t)seed, (uint32_t)step, ptr<int>(out), cur_stream()),
+        "spec_verify");
+}
+
 void mla_kv_write(Tensor kv_a, Tensor norm_w, double eps, Tensor cos, Tensor sin, int64_t neox, Tensor pos,
                   Tensor slots, Tensor cache, Tensor q, int64_t H, int64_t qdim, int64_t rope_off) {
   c10::cuda::CUDAGuard g(kv_a.device());
@@ -561,6 +574,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("moe_combine", &moe_combine);
   m.def("ep_call", &ep_call);
+  m.def("spec_verify", &spec_verify);
   m.def("qgemm_sp", &qgemm_sp);
   m.def("sp_reduce_norm_ag", &sp_reduce_norm_ag);
   m.def("sp_ag_wait", &sp_ag_wait);

@@ -326,7 +326,7 @@ struct Issuers {
 constexpr int kMaxGroups = 256;
 // Split-K: at most this many K splits per output tile (the last split to finish reads every
 // split's partial tile, so more splits lengthen the kernel's tail more than they add parallelism).
-constexpr int kMaxAutoSplits = 4;
+constexpr int kMaxAutoSplits = 8;
 
 // One output tile: global weight tile nt, K split z, activation/output rows [row0, row0 + rows),
 // output column base n0.
@@ -699,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += w[j];
         }
-        if (g.mode == EPI_SWIGLU_Q8) {
+        if (g.mode == EPI_SWIGLU_Q8 && !atomic) {
           // rows [32 gate | 32 up] x 2 groups: quadrants 0,2 hold gate rows, 1,3 the matching up rows
           float* mine = xch + quad * 32 * 32;
 #pragma unroll
@@ -757,33 +757,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (split_last_s) {
           __threadfence();
-          // thread (quad, lane): rows 4*lane .. 4*lane+3 of the tile, columns quad, quad+4, ...;
-          // float4 loads of every split of two columns are issued together, summed in split order
-          const int r4 = lane * 4, n4 = n0 + r4;
           const int ncol = t_end - t0;
-          const float* base = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128 + r4;
-          if (n4 < g.N) {
-            for (int c = quad; c < ncol; c += 8) {
-              float4 v[2][kMaxAutoSplits];
+          const float* bz = g.split_ws + (size_t)split_tile * g.k_splits * BN * 128;
+          if (g.mode == EPI_SWIGLU_Q8) {
+            // thread -> output feature f (rows: gate 64*(f/32) + f%32, up 32 rows later) and every
+            // other column; splits summed in order, then silu(gate) * up
+            const int tid = quad * 32 + lane, f = tid & 63, rg = (f >> 5) * 64 + (f & 31);
+            const int fo = n0 / 2 + f;
+            for (int c = tid >> 6; c < ncol && fo < g.N / 2; c += 2) {
+              float sg = 0.f, su = 0.f;
+              for (int zb = 0; zb < g.k_splits; zb += 4) {
+                float vg[4], vu[4];
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
+                for (int zz = 0; zz < 4; ++zz) {
+                  const bool in = zb + zz < g.k_splits;
+                  const float* src = bz + ((size_t)(zb + zz) * BN + c) * 128;
+                  vg[zz] = in ? __ldcg(src + rg) : 0.f;
+                  vu[zz] = in ? __ldcg(src + rg + 32) : 0.f;
+                }
 #pragma unroll
-                for (int zz = 0; zz < kMaxAutoSplits; ++zz)
-                  v[h][zz] = (zz < g.k_splits && c + 4 * h < ncol)
-                                 ? __ldcg(reinterpret_cast<const float4*>(base + ((size_t)zz * BN + c + 4 * h) * 128))
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int zz = 0; zz < 4; ++zz) {
+                  sg += vg[zz];
+                  su += vu[zz];
+                }
+              }
+              out_act[(size_t)(t0 + c) * g.ld_out + fo] = from_f<AT>(silu(sg) * su);
+            }
+          } else {
+            // thread (quad, lane): rows 4*lane .. 4*lane+3 of the tile, columns quad, quad+4, ...;
+            // float4 loads of 4 splits of two columns are issued together, summed in split order
+            const int r4 = lane * 4, n4 = n0 + r4;
+            const float* base = bz + r4;
+            for (int c = quad; c < ncol && n4 < g.N; c += 8) {
+              float4 acc2[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+              for (int zb = 0; zb < g.k_splits; zb += 4) {
+                float4 v[2][4];
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                  for (int zz = 0; zz < 4; ++zz)
+                    v[h][zz] = (zb + zz < g.k_splits && c + 4 * h < ncol)
+                                   ? __ldcg(reinterpret_cast<const float4*>(base + ((size_t)(zb + zz) * BN + c + 4 * h) * 128))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                  for (int zz = 0; zz < 4; ++zz) {
+                    acc2[h].x += v[h][zz].x;
+                    acc2[h].y += v[h][zz].y;
+                    acc2[h].z += v[h][zz].z;
+                    acc2[h].w += v[h][zz].w;
+                  }
+              }
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 if (c + 4 * h >= ncol) break;
-                float4 s4 = v[h][0];
-#pragma unroll
-                for (int zz = 1; zz < kMaxAutoSplits; ++zz) {
-                  if (zz >= g.k_splits) break;
-                  s4.x += v[h][zz].x;
-                  s4.y += v[h][zz].y;
-                  s4.z += v[h][zz].z;
-                  s4.w += v[h][zz].w;
-                }
+                float4 s4 = acc2[h];
                 const int t = t0 + c + 4 * h;
                 if (g.mode == EPI_RS_PUSH) {  // the summed tile goes to its owner (reduce-scatter)
                   const int ow = t / g.rs.chunk;
@@ -1017,15 +1046,16 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
   if (g.k_splits == 0) {  // automatic split-K so that small token counts still fill the SMs
     const int tiles = ((g.N + 127) / 128) * tiles_t, n = sm_count();
     int ks = 1;
-    if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32 || g.mode == EPI_RS_PUSH) && g.ld_out % 4 == 0 &&
-        g.N % 4 == 0)
+    if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32 || g.mode == EPI_RS_PUSH || g.mode == EPI_SWIGLU_Q8) &&
+        g.ld_out % 4 == 0 && g.N % 4 == 0)
       while (ks < kMaxAutoSplits && tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
     g.k_splits = ks;
   }
   if (g.k_splits > KG) g.k_splits = KG;
   if (g.k_splits > kMaxAutoSplits) g.k_splits = kMaxAutoSplits;
   if (g.k_splits > 1 && (g.ld_out % 4 || g.N % 4 ||
-                         (g.mode != EPI_RS_PUSH && (reinterpret_cast<uintptr_t>(g.out_f32) & 15))))
+                         (g.mode != EPI_RS_PUSH && g.mode != EPI_SWIGLU_Q8 &&
+                          (reinterpret_cast<uintptr_t>(g.out_f32) & 15))))
     g.k_splits = 1;
   if (g.k_splits > 1) {
     const long tiles = (long)((g.N + 127) / 128) * tiles_t;
@@ -1090,8 +1120,8 @@ int qgemm_tc(const QW& w, const void* x, int x_is_f16, int T, const GemvEpi& ep,
   const int G = (w.type == W_Q4_K || w.type == W_Q5_K || w.type == W_Q6_K) ? 256 : 64;
   if (w.K % G) return -2;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w.p0) & 15)) return -3;
-  if (ep.mode == EPI_SWIGLU_Q8 && ((grp ? grp->grows : w.N) % 128 || k_splits > 1)) return -4;
-  if (ep.mode == EPI_SWIGLU_Q8 || ep.mode == EPI_STORE_BF16) k_splits = 1;
+  if (ep.mode == EPI_SWIGLU_Q8 && (grp ? grp->grows : w.N) % 128) return -4;
+  if (ep.mode == EPI_STORE_BF16) k_splits = 1;
   if (k_splits < 0) k_splits = 0;
   GemmDev g;
   g.N = grp ? grp->grows : w.N;

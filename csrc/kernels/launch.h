@@ -351,4 +351,8 @@ struct SampleArgs {
 };
 int sample_tokens(const SampleArgs& a, cudaStream_t st);
 
+// K14: speculative-decoding rejection step on the device (sampler.cu); out int32 [k + 2].
+int spec_verify(const float* ps, const float* qs, const int64_t* drafts, int k, int V, int greedy, uint64_t seed,
+                uint32_t step, int* out, cudaStream_t st);
+
 }  // namespace barq

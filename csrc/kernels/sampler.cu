@@ -324,3 +324,177 @@ int sample_tokens(const SampleArgs& a, cudaStream_t st) {
 }
 
 }  // namespace barq
+
+// ------------------------------------------------------------------------------------ K14
+// Speculative-decoding verification on the device: one CTA, no host round trip until the result.
+// ps: target distributions [k+1, V] (f32, rows for the k drafted positions and the bonus position);
+// qs: draft distributions [k, V]; drafts: int64 [k].  Sampled: draft i is accepted while
+// u_i < p_i(d_i) / q_i(d_i) (u_i from Philox keyed by seed, counter (step, i)); at the first
+// rejection n the correction is drawn from norm(max(0, p_n - q_n)) (p_n itself if that is all
+// zero), after k acceptances the bonus token from p_k -- the standard rejection rule, so the
+// output follows the target distribution.  Greedy: accept while argmax(p_i) == d_i, then append
+// argmax(p_n).  out: int32 [k + 2] = (n accepted, tokens[0..n]).
+namespace barq {
+namespace {
+constexpr int VT = 1024;
+
+BARQ_DEV float vblock_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < VT / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  t = red[32];
+  __syncthreads();
+  return t;
+}
+
+// argmax of a row (ties: lowest index)
+BARQ_DEV int vblock_argmax(const float* row, int V, float* redv, int* redi) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += VT) {
+    const float x = row[i];
+    if (x > bv) {
+      bv = x;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    redv[threadIdx.x >> 5] = bv;
+    redi[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    bv = redv[threadIdx.x];
+    bi = redi[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) redi[32] = bi;
+  }
+  __syncthreads();
+  const int r = redi[32];
+  __syncthreads();
+  return r;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(VT) spec_verify_kernel(const float* ps, const float* qs, const int64_t* drafts,
+                                                         int k, int V, int greedy, uint64_t seed, uint32_t step,
+                                                         int* out) {
+  __shared__ float redv[33];
+  __shared__ int redi[33];
+  __shared__ float csum[VT];
+  __shared__ int n_s;
+  const uint2 key = make_uint2((uint32_t)(seed & 0xffffffffu), (uint32_t)(seed >> 32));
+  if (threadIdx.x == 0) {
+    int n = 0;
+    if (!greedy) {
+      for (; n < k; ++n) {
+        const int64_t d = drafts[n];
+        const float px = ps[(size_t)n * V + d], qx = fmaxf(qs[(size_t)n * V + d], 1e-20f);
+        const uint4 r = philox4x32_10(make_uint4(step, (uint32_t)n, 0u, 0x7e57u), key);
+        if (!(u01(r.x) < fminf(px / qx, 1.f))) break;
+      }
+    }
+    n_s = n;
+  }
+  __syncthreads();
+  int n = n_s;
+  if (greedy) {  // accept while the target's argmax agrees with the draft
+    for (n = 0; n < k; ++n)
+      if (vblock_argmax(ps + (size_t)n * V, V, redv, redi) != (int)drafts[n]) break;
+    const int tok = vblock_argmax(ps + (size_t)n * V, V, redv, redi);
+    if (threadIdx.x == 0) {
+      out[0] = n;
+      for (int i = 0; i < n; ++i) out[1 + i] = (int)drafts[i];
+      out[1 + n] = tok;
+    }
+    return;
+  }
+  // residual (or bonus) distribution r, sampled by inverse CDF over contiguous chunks
+  const float* p = ps + (size_t)n * V;
+  const float* q = n < k ? qs + (size_t)n * V : nullptr;
+  const int per = (V + VT - 1) / VT, c0 = threadIdx.x * per, c1 = min(V, c0 + per);
+  float s = 0.f;
+  for (int i = c0; i < c1; ++i) s += q ? fmaxf(p[i] - q[i], 0.f) : p[i];
+  float tot = vblock_sum(s, redv);
+  bool use_p = q && !(tot > 0.f);  // p == q exactly: fall back to p
+  if (use_p) {
+    s = 0.f;
+    for (int i = c0; i < c1; ++i) s += p[i];
+    tot = vblock_sum(s, redv);
+  }
+  csum[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive prefix of the chunk sums (in place), then the target mass
+    float run = 0.f;
+    for (int i = 0; i < VT; ++i) {
+      const float v = csum[i];
+      csum[i] = run;
+      run += v;
+    }
+    const uint4 r = philox4x32_10(make_uint4(step, (uint32_t)k, 1u, 0x7e57u), key);
+    redv[32] = u01(r.x) * run;
+  }
+  __syncthreads();
+  const float target = redv[32];
+  if (threadIdx.x == 0) redi[32] = -1;
+  __syncthreads();
+  const float lo = csum[threadIdx.x];
+  const float hi = threadIdx.x + 1 < VT ? csum[threadIdx.x + 1] : INFINITY;
+  if (target >= lo && target < hi && c0 < c1) {
+    float acc = lo;
+    int pick = c1 - 1;
+    for (int i = c0; i < c1; ++i) {
+      acc += (q && !use_p) ? fmaxf(p[i] - q[i], 0.f) : p[i];
+      if (target < acc) {
+        pick = i;
+        break;
+      }
+    }
+    redi[32] = pick;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tok = redi[32];
+    if (tok < 0) tok = V - 1;  // the target fell past the last mass by rounding
+    out[0] = n;
+    for (int i = 0; i < n; ++i) out[1 + i] = (int)drafts[i];
+    out[1 + n] = tok;
+  }
+}
+
+int spec_verify(const float* ps, const float* qs, const int64_t* drafts, int k, int V, int greedy, uint64_t seed,
+                uint32_t step, int* out, cudaStream_t st) {
+  if (k < 0 || V <= 0) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(VT);
+  cfg.stream = st;
+  return cudaLaunchKernelEx(&cfg, spec_verify_kernel, ps, qs, drafts, k, V, greedy, seed, step, out) == cudaSuccess
+             ? 0
+             : -20;
+}
+}  // namespace barq

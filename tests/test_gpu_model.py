@@ -262,3 +262,35 @@ def test_sliding_window_decode_matches_reference_and_skips_dead_pages():
     out = eng.generate([prompt], SamplingParams.greedy_params(max_tokens=48))[0].tokens
     assert len(out) == 48 and eng.sched.n_window_freed >= 3
     assert eng.blocks.n_used == 1  # only the engine's own dummy page is still held
+
+
+def test_fp8_kv_row_scales_keep_values_beyond_e4m3_range():
+    """K/V rows with magnitudes in the thousands (e4m3 saturates at 448): the per-row scales of the
+    fp8 cache keep decode and prefill attention within a few percent of the fp16-cache result."""
+    from barq_inference_b200 import ops
+    from barq_inference_b200.models.rope import rope_cos_sin
+
+    cfg = preset("tiny")
+    H, Hkv, D, T = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, 40
+    g = torch.Generator().manual_seed(3)
+    qkv = (torch.randn(T, (H + 2 * Hkv) * D, generator=g) * 1000).to(DEV)
+    cos, sin = rope_cos_sin(cfg, 512, DEV)
+    pos = torch.arange(T, dtype=torch.int32, device=DEV)
+    slots = (torch.arange(T, device=DEV) + 16).long()  # pages 1..3
+    bt = torch.tensor([[1, 2, 3, 0]], dtype=torch.int32, device=DEV)
+    outs = {}
+    for dt in (torch.float16, torch.float8_e4m3fn):
+        kc = torch.zeros(5, Hkv, 16, D, device=DEV).to(dt)
+        vc = torch.zeros(5, Hkv, 16, D, device=DEV).to(dt)
+        sc = (torch.ones(5, Hkv, 16, device=DEV), torch.ones(5, Hkv, 16, device=DEV)) if dt != torch.float16 else None
+        q = ops.rope_kv_write(qkv, pos, slots, cos, sin, H, Hkv, D, cfg.rot_dim, cfg.rope_neox, kc, vc, kv_scales=sc)
+        q = (q.float() / 1000).bfloat16()  # keep the scores in a sane range; K/V stay large
+        lens = torch.tensor([T], dtype=torch.int32, device=DEV)
+        dec, _ = ops.decode_attention(q[-1:].contiguous(), kc, vc, bt, lens, H, Hkv, D, D ** -0.5, want_q8=False,
+                                      act_dtype=torch.float16, kv_scales=sc)
+        pre = ops.prefill_attention(q, kc, vc, bt, torch.tensor([0, T], dtype=torch.int32, device=DEV), lens, T,
+                                    H, Hkv, D, D ** -0.5, act_dtype=torch.float16, kv_scales=sc)
+        outs[dt] = (dec.float().cpu(), pre.float().cpu())
+    for a, b in zip(outs[torch.float16], outs[torch.float8_e4m3fn]):
+        rel = ((a - b).norm() / a.norm()).item()
+        assert rel < 0.06, rel
