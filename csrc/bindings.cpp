@@ -496,6 +496,8 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
   a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)B * H * splits * D);
   a.kscale = optptr<const float>(kscale);
   a.vscale = optptr<const float>(vscale);
+  a.num_blocks = (int)kcache.size(0);
+  a.err = barq::kernel_err_word();
   a.out = out.data_ptr();
   a.out_f16 = out.scalar_type() == torch::kHalf;
   a.out_q = act_out(out_q, out_s, out_ql, out_dl);

@@ -105,7 +105,11 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
     for (int i = 0; i < npg; ++i) {
       const int s = i % kAttnRing;
       if ((i & 31) == 0) pg = i + lane < npg ? bt[sb + i + lane] : 0;
-      const int phys = __shfl_sync(0xffffffffu, pg, i & 31);
+      int phys = __shfl_sync(0xffffffffu, pg, i & 31);
+      if (a.num_blocks > 0 && (phys < 0 || phys >= a.num_blocks)) {  // bad block-table entry
+        if (lane == 0 && a.err) atomicExch(a.err, 0xA00);
+        phys = 0;
+      }
       bool ok = true;
       if (i >= kAttnRing) {
         if (lane == 0) ok = tc::mbar_wait(&empty[s], ((i / kAttnRing) - 1) & 1, err, 1);

@@ -74,18 +74,23 @@ BARQ_DEV float deq_elem(const QW& w, int row, int k) {
   return 0.f;
 }
 
-__global__ void embed_kernel(QW w, const int* __restrict__ ids, float* __restrict__ out) {
+// A token id outside [0, vocab) is recorded in the device error word (0xB00) and its row reads as
+// zeros: the gather never reads outside the table.
+__global__ void embed_kernel(QW w, const int* __restrict__ ids, float* __restrict__ out, int* err) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
   const int row = ids[t];
-  for (int k = threadIdx.x; k < w.K; k += blockDim.x) out[(size_t)t * w.K + k] = deq_elem(w, row, k);
+  const bool ok = row >= 0 && row < w.N;
+  if (!ok && threadIdx.x == 0 && err) atomicExch(err, 0xB00);
+  for (int k = threadIdx.x; k < w.K; k += blockDim.x) out[(size_t)t * w.K + k] = ok ? deq_elem(w, row, k) : 0.f;
 }
 
 int embed_gather(const QW& table, const int* ids, int T, float* out, cudaStream_t st) {
   if (T <= 0) return 0;
-  launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, table, ids, out);
-  return 0;
+  return launch_pdl(embed_kernel, dim3(T), dim3(256), 0, st, table, ids, out, kernel_err_word()) == cudaSuccess
+             ? 0
+             : -20;
 }
 
 __global__ void dequant_rows_kernel(QW w, int r0, __nv_bfloat16* __restrict__ out) {

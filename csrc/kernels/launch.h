@@ -303,6 +303,10 @@ struct DecodeAttnArgs {
   int* counters = nullptr;
   const float* kscale = nullptr;  // fp8 cache: per-row scales (RopeKVArgs), null = unscaled
   const float* vscale = nullptr;
+  // pages in the cache; a block-table entry outside [0, num_blocks) is recorded in *err (0xA00)
+  // and read as page 0 instead.  0 = unchecked.
+  int num_blocks = 0;
+  int* err = nullptr;
 };
 int decode_attention(const DecodeAttnArgs& a, cudaStream_t st);
 size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits);

@@ -359,3 +359,33 @@ def test_gemm_tc_swiglu_and_ragged_n(T, dt):
     y = ops.gemm(qw, x).cpu()
     y_ref = xf @ ref.to(dt).float().T
     assert torch.allclose(y, y_ref, atol=y_ref.abs().max().item() * 2e-3, rtol=1e-2)
+
+
+def test_spec_verify_kernel_preserves_target_distribution():
+    """K14 on the device: the first emitted token of the rejection step follows the target
+    distribution p_0 whatever the draft proposed (the speculative-sampling guarantee); greedy
+    accepts exactly the prefix that matches the target's argmax."""
+    C = ops.require_ext()
+    g = torch.Generator().manual_seed(4)
+    V, k = 12, 3
+    ps = torch.softmax(torch.randn(k + 1, V, generator=g) * 2, -1).to(DEV)
+    qs = torch.softmax(torch.randn(k, V, generator=g) * 2, -1).to(DEV)
+    out = torch.empty(k + 2, dtype=torch.int32, device=DEV)
+    counts = torch.zeros(V)
+    n = 6000
+    dg = torch.Generator().manual_seed(9)
+    for step in range(n):
+        d = torch.multinomial(qs.cpu(), 1, generator=dg)[:, 0]  # drafts sampled from q
+        C.spec_verify(ps, qs, d.to(DEV), 0, 77, step, out)
+        r = out.cpu()
+        assert 0 <= int(r[0]) <= k
+        counts[int(r[1])] += 1
+    emp = counts / n
+    assert (emp - ps[0].cpu()).abs().max().item() < 0.025, (emp, ps[0])
+    # greedy: drafts = target argmax for the first two positions, then a mismatch
+    tgt = ps.argmax(-1).cpu()
+    d = tgt[:k].clone()
+    d[2] = (d[2] + 1) % V
+    C.spec_verify(ps, None, d.to(DEV), 1, 0, 0, out)
+    r = out.cpu().tolist()
+    assert r[0] == 2 and r[1:4] == [int(tgt[0]), int(tgt[1]), int(tgt[2])]
