@@ -175,7 +175,88 @@ def cases(tokens: int):
                 4.0 * B * H * ctx * D
         return make
 
+    class _Bytes:  # bytes an op must move, for the GB/s column of cases without a weight
+        def __init__(self, n):
+            self.n = n
+
+        def nbytes(self):
+            return self.n
+
+    def rope_kv(T: int):
+        # RoPE + K/V cache write of one Llama-3-8B layer for T tokens (qkv f32 in, q bf16 + K/V fp16 out)
+        def make():
+            from . import rope_kv_write
+            from ..models import preset
+            from ..models.rope import rope_cos_sin
+
+            cfg = preset("llama3-8b")
+            H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+            qkv = torch.randn(T, (H + 2 * Hkv) * D, device="cuda")
+            cos, sin = rope_cos_sin(cfg, 4096, "cuda")
+            pos = torch.arange(T, dtype=torch.int32, device="cuda") + 1000
+            slots = torch.arange(T, device="cuda") * 16 + 16  # one page per token row
+            kc = torch.zeros(T + 2, Hkv, 16, D, device="cuda").half()
+            vc = torch.zeros_like(kc)
+            nb = qkv.numel() * 4 + T * H * D * 2 + 2 * T * Hkv * D * 2
+            return _Bytes(nb), (lambda: rope_kv_write(qkv, pos, slots, cos, sin, H, Hkv, D, cfg.rot_dim,
+                                                      cfg.rope_neox, kc, vc)), 0.0
+        return make
+
+    def sampler(B: int):
+        # fused sampler over a 128256-token vocabulary: top-k 40, top-p 0.95, temperature 0.8
+        def make():
+            from . import sample
+
+            V = 128256
+            lg = torch.randn(B, V, device="cuda")
+            f = lambda v, dt=torch.float32: torch.full((B,), v, dtype=dt, device="cuda")  # noqa: E731
+            args = (f(0.8), f(40, torch.int32), f(0.95), f(0.0), f(7, torch.int64), f(0, torch.int32))
+            return _Bytes(lg.numel() * 4), (lambda: sample(lg, *args)), 0.0
+        return make
+
+    def prefill_attn(T: int):
+        # causal prefill attention of one Llama-3-8B layer over a T-token prompt (fp16 paged KV)
+        def make():
+            from . import prefill_attention
+
+            H, Hkv, D = 32, 8, 128
+            pages = (T + 15) // 16
+            kc = torch.randn(pages + 1, Hkv, 16, D, device="cuda").half()
+            vc = torch.randn_like(kc)
+            bt = torch.arange(1, pages + 1, dtype=torch.int32, device="cuda").view(1, pages)
+            q = torch.randn(T, H, D, device="cuda").bfloat16()
+            qs = torch.tensor([0, T], dtype=torch.int32, device="cuda")
+            cl = torch.tensor([T], dtype=torch.int32, device="cuda")
+            flops = 4.0 * H * D * T * T / 2
+            return _Bytes(2 * T * Hkv * D * 2 + 2 * T * H * D * 2), (lambda: prefill_attention(
+                q, kc, vc, bt, qs, cl, T, H, Hkv, D, D ** -0.5)), flops
+        return make
+
+    def moe_layer(T: int):
+        # one Mixtral-shaped MoE FFN (8 experts of 4096 -> 14336, top-2, Q4_K) for T tokens on one GPU:
+        # router matmul, routing kernels, grouped gate|up and down tcgen05 GEMMs, combine
+        def make():
+            import dataclasses
+
+            from ..models import POLICIES, preset, random_tensors
+            from ..models.moe import MoEBlock
+
+            cfg = dataclasses.replace(preset("mixtral-8x7b"), n_layers=1)
+            tensors = random_tensors(cfg, POLICIES["mixtral-8x7b"], seed=0, device="cuda")
+            blk = MoEBlock(cfg, tensors, "blk.0.", "cuda")
+            del tensors
+            hb = torch.randn(T, cfg.hidden, device="cuda").half()
+            x = torch.zeros(T, cfg.hidden, device="cuda")
+
+            class _R:
+                ser_threshold, fused_moe, x2 = 0.0, True, True
+            nb = blk.gate_up.nbytes() + blk.down.nbytes()
+            return _Bytes(nb), (lambda: blk.forward(_R(), None, hb, T, x)), 2.0 * T * 2 * 3 * 4096 * 14336
+        return make
+
     return {"allreduce_w1": allreduce_w1, "attn_decode_bs32": attn_decode(32, 1024),
+            "rope_kv_t32": rope_kv(32), "sampler_bs32": sampler(32), "prefill_attn_t2048": prefill_attn(2048),
+            "moe_mixtral_t64": moe_layer(64),
             "attn_decode_bs1": attn_decode(1, 1024), "decode_step_bs1": decode_step(1, 64),
             "decode_step_bs32": decode_step(32, 1024), "decode_step_bs64": decode_step(64, 1024), "gemm_gate_up": gemm_gate_up, "gemm_down": gemm_down, "gemv_gate_up": gemv_gate_up,
             "gemv_head": gemv_head, "gemv_qkv": gemv_qkv, "gemv_o_tp2": gemv_o_tp2(False),

@@ -285,7 +285,8 @@ void ep_call(int64_t which, int64_t rank, int64_t E, int64_t E_local, int64_t k,
   if (which == 0)
     check(barq::ep_dispatch(a, x.scalar_type() == torch::kHalf, cur_stream()), "ep_dispatch");
   else {
-    TORCH_CHECK(a.out && out->scalar_type() == torch::kFloat32 && out->is_contiguous(), "ep_combine: out f32");
+    TORCH_CHECK(out.has_value() && out->scalar_type() == torch::kFloat32 && out->is_contiguous() &&
+                    (rows == 0 || a.out), "ep_combine: out f32 [rows, H]");
     check(barq::ep_combine(a, cur_stream()), "ep_combine");
   }
 }

@@ -57,15 +57,22 @@ __global__ void __launch_bounds__(256) allreduce_add_kernel(ArArgs a) {
     return;
   }
   // x[i] += sum_r partial_r[i] over this block's grid-stride share, float4 at a time
+  // every rank's float4 is loaded before any is added (all peers' NVLink reads in flight at once),
+  // then summed in rank order
   const int n4 = a.n / 4;
   for (int i = b * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    float4 v[kArMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kArMaxRanks; ++r)
+      v[r] = r < a.world ? __ldcg(reinterpret_cast<const float4*>(a.bufs[r]) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 acc = reinterpret_cast<float4*>(a.x)[i];
-    for (int r = 0; r < a.world; ++r) {
-      const float4 v = reinterpret_cast<const float4*>(a.bufs[r])[i];
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+#pragma unroll
+    for (int r = 0; r < kArMaxRanks; ++r) {
+      if (r >= a.world) break;
+      acc.x += v[r].x;
+      acc.y += v[r].y;
+      acc.z += v[r].z;
+      acc.w += v[r].w;
     }
     reinterpret_cast<float4*>(a.x)[i] = acc;
   }
