@@ -319,11 +319,7 @@ template <int BN>
 struct Issuers {
   static constexpr int NI = BN <= 64 ? 2 : 1;
   static constexpr bool TS = kGemmTS && BN <= 128;
-  // accumulators per issuer: with 32-row token tiles each issuer alternates its MMAs between two
-  // accumulators (even / odd K steps), so twice as many independent accumulation chains are in
-  // flight; the epilogue adds them
-  static constexpr int SUB = (TS && BN <= 32) ? 2 : 1;
-  static constexpr int ACOL = 2 * NI * SUB * BN;      // first TMEM column of the operand stages
+  static constexpr int ACOL = 2 * NI * BN;            // first TMEM column of the operand stages
   static constexpr int COLS = TS ? 512 : 2 * NI * BN;
 };
 
@@ -543,8 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nst = (ge - gb) * SPG;
         if (tc >= 2 && !mbar_wait(&accEmpty[buf], (use - 1) & 1, err, 8)) break;
         tc_fence_after();
-        constexpr int SUB = Issuers<BN>::SUB;
-        const uint32_t acc = tmem + (uint32_t)((buf * NI + me) * SUB * BN);
+        const uint32_t acc = tmem + (uint32_t)((buf * NI + me) * BN);
         bool ok = true;
         for (int i = 0; i < nst; ++i, ++it) {
           if (i % NI != me) continue;
@@ -563,9 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int a = 0; a < KS; ++a)
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                mma_f16_ts(acc + (uint32_t)((SUB > 1 ? (k & 1) : 0) * BN), ta + (uint32_t)(a * 32 + k * 8),
-                           umma_desc_sw128(b0 + a * L::B_ATOM + 32 * k), idesc,
-                           (i >= NI) | a | (SUB > 1 ? (k >> 1) : k));
+                mma_f16_ts(acc, ta + (uint32_t)(a * 32 + k * 8), umma_desc_sw128(b0 + a * L::B_ATOM + 32 * k), idesc,
+                           (i >= NI) | a | k);
           } else {
             const uint32_t a0 = smem_addr(smem + L::OFF_A + s * L::A_BYTES);
 #pragma unroll
@@ -686,8 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nt = tl.nt, z = tl.z;
       int gb, ge;
       grange(z, gb, ge);
-      // accumulators written for this tile: SUB per issuer that had a stage of it
-      const int nacc = ((ge - gb) * SPG < NI ? (ge - gb) * SPG : NI) * Issuers<BN>::SUB;
+      const int nacc = (ge - gb) * SPG < NI ? (ge - gb) * SPG : NI;  // issuers that wrote this tile
       const int buf = tc & 1, use = tc >> 1;
       mbar_wait(&accFull[buf], use & 1, err, 7);
       tc_fence_after();
@@ -696,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*err) break;
       const int n0 = tl.n0, t0 = tl.row0, t_end = tl.row0 + tl.rows, n = n0 + r;
       const int split_tile = nt + tm.n_tiles * (t0 / BN);  // output tile id (split-K, RS flags)
-      const uint32_t acc = tmem + (uint32_t)(buf * NI * Issuers<BN>::SUB * BN) + ((uint32_t)(quad * 32) << 16);
+      const uint32_t acc = tmem + (uint32_t)(buf * NI * BN) + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(acc + (uint32_t)c0, v);

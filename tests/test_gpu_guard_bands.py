@@ -14,7 +14,7 @@ from barq_inference_b200.gguf import GGMLType, quantize
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 G = 4096  # guard elements on each side
-SENT = -12345.0
+SENT = -4096.0  # exact in fp16, bf16 and f32
 
 
 def _guarded(n, dtype=torch.float32):
