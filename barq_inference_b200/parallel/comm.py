@@ -275,7 +275,7 @@ class Comm:
     def allreduce_add(self, j: int, x: torch.Tensor) -> None:
         """x += sum over ranks of partial buffer j (every rank calls it with its own x)."""
         n = x.numel()
-        blocks = max(1, min(64, (n // 4 + 255) // 256))
+        blocks = max(1, min(32, (n // 4 + 255) // 256))
         require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks, self.wait_s,
                                     int(self.skip_signal))
 
