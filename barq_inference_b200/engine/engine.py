@@ -599,7 +599,14 @@ def make_runner(cfg: ModelConfig, tensors, device, kv_dtype, ec: EngineConfig):
         if comm.world != ec.tp:
             raise ValueError(f"tp={ec.tp} but the process group has {comm.world} ranks")
         shard, info = shard_tensors(cfg, tensors, comm.rank, comm.world)
-        r = LlamaRunner(shard_config(cfg, comm.world), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info, comm=comm)
+        if cfg.is_mla:
+            from ..models.deepseek2 import DeepseekV2Runner
+
+            r = DeepseekV2Runner(cfg, shard, device, kv_dtype, ser_threshold=ec.ser_threshold, act_x2=ec.act_x2,
+                                 tp=info, comm=comm)
+        else:
+            r = LlamaRunner(shard_config(cfg, comm.world), shard, device, kv_dtype, act_x2=ec.act_x2, tp=info,
+                            comm=comm)
         comm.barrier()  # ranks finish building (tiling) their shards before the first collective
         _attach_health(r, comm, comm.rank, comm.world, ec)
         r.ser_threshold = ec.ser_threshold

@@ -9,7 +9,12 @@ rope/nope split, shared + routed experts, first ``n_dense_layers`` dense) and th
 * queries are absorbed: ``q_lat = q_nope . W_UK`` (per-head 128x512 blocks of ``attn_kv_b``), so the
   attention kernel (K10, ``csrc/kernels/mla.cu``) scores ``q_lat . c + q_pe . k_pe`` directly on the
   cached latents and returns ``o_lat = softmax . c``; ``o_lat . W_UV^T`` gives the head outputs;
-* expert FFNs are :class:`MoEBlock` (group-limited top-k, shared experts), the first layer is dense.
+* expert FFNs are :class:`MoEBlock` (group-limited top-k, shared experts), the first layer is dense;
+* tensor parallel (``tp`` / ``comm``): each rank holds the query projection, W_UK / W_UV and the
+  output-projection columns of H / tp heads, the latent path (q_a, kv_a, cache) replicated; the
+  attention kernel runs the 16-head layout with this rank's heads in place (the others' queries
+  zero, their outputs unused), and the output projection's partial sums are all-reduced like the
+  dense models' row-parallel layers.  Experts are split by expert.
 
 Activations in the tensor-core GEMMs are bf16 (DeepSeek overflows fp16).
 """
@@ -32,7 +37,8 @@ LAT, ROPE = 512, 64
 
 class DeepseekV2Runner(LlamaRunner):
     def __init__(self, cfg: ModelConfig, tensors: dict[str, PackedTensor], device="cuda",
-                 kv_dtype: torch.dtype = torch.bfloat16, ser_threshold: float = 0.0, act_x2: bool = True):
+                 kv_dtype: torch.dtype = torch.bfloat16, ser_threshold: float = 0.0, act_x2: bool = True,
+                 tp=None, comm=None):
         if cfg.kv_lora_rank != LAT or cfg.qk_rope_dim != ROPE or cfg.n_heads != 16:
             raise ValueError("DeepseekV2Runner: the MLA kernel is built for 16 heads, latent 512, rope 64")
         if kv_dtype not in (torch.float16, torch.bfloat16):
@@ -40,6 +46,9 @@ class DeepseekV2Runner(LlamaRunner):
         from .reference import dequant_tensor
 
         self.cfg = cfg
+        self.tp, self.comm, self.pp = tp, comm, None
+        self.h0 = tp.head0 if tp is not None else 0
+        self.Hl = tp.n_heads_local if tp is not None else cfg.n_heads  # heads held by this rank
         self.device = torch.device(device)
         self.kv_dtype = kv_dtype
         self.scale = attn_scale(cfg)
@@ -69,12 +78,13 @@ class DeepseekV2Runner(LlamaRunner):
                 L.wq = _qw(tensors[p + "attn_q.weight"], dev)
             L.kv_a = _qw(tensors[p + "attn_kv_a_mqa.weight"], dev)
             L.kv_a_norm = _f32(tensors[p + "attn_kv_a_norm.weight"], dev)
-            kvb = dequant_tensor(tensors[p + "attn_kv_b.weight"]).view(H, dn + dv, LAT).float()
+            kvb = dequant_tensor(tensors[p + "attn_kv_b.weight"]).view(self.Hl, dn + dv, LAT).float()
             L.w_uk = kvb[:, :dn, :].contiguous().to(dev)  # [H, dn, 512]
             L.w_uv = kvb[:, dn:, :].contiguous().to(dev)  # [H, dv, 512]
             L.wo = _qw(tensors[p + "attn_output.weight"], dev)
             if cfg.layer_is_moe(i):
-                L.moe = MoEBlock(cfg, tensors, p, dev)
+                L.moe = MoEBlock(cfg, tensors, p, dev, expert0=tp.expert0 if tp is not None else 0)
+                L.moe.shared_here = tp is None or tp.rank == 0  # shared experts are replicated under TP
             else:
                 L.moe = None
                 g, u = _qw(tensors[p + "ffn_gate.weight"], dev), _qw(tensors[p + "ffn_up.weight"], dev)
@@ -105,6 +115,18 @@ class DeepseekV2Runner(LlamaRunner):
         return ops.rmsnorm(x, w, self.cfg.rms_eps, want_q8=T <= GEMV_MAX_T, want_bf16=True, x2=self.x2,
                            act_dtype=self.act_dtype)
 
+    def _dense_ffn(self, L, hq, hb, T, mode, out):
+        """The leading dense FFN, replicated under tensor parallelism: rank 0 adds (or stores) it,
+        the other ranks contribute zeros to the all-reduce."""
+        if self.tp is not None and self.tp.rank != 0:
+            if mode == EPI_STORE_F32:
+                out.zero_()
+            return
+        if T <= GEMV_MAX_T:
+            self._lin_q8(L.down, self._lin_q8(L.gate_up, hq, T, EPI_SWIGLU_Q8), T, mode, out=out)
+        else:
+            ops.gemm(L.down, ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8), mode, out=out)
+
     def _mla(self, L, li, x, inp: StepInput, T):
         cfg = self.cfg
         H = cfg.n_heads
@@ -117,10 +139,18 @@ class DeepseekV2Runner(LlamaRunner):
         else:
             q = self._proj(L.wq, hq, hb, T)  # f32 [T, H*qdim]
         kva = self._proj(L.kv_a, hq, hb, T)  # f32 [T, 576]
+        Hl, h0 = self.Hl, self.h0
         ops.mla_kv_write(kva, L.kv_a_norm, cfg.rms_eps, self.cos, self.sin, cfg.rope_neox, inp.pos, inp.slots,
-                         self.kv[li], q, H, self.qdim, cfg.qk_nope_dim)
-        q3 = q.view(T, H, self.qdim)
-        q_lat = torch.einsum("thd,hdl->thl", q3[..., :cfg.qk_nope_dim], L.w_uk).contiguous()  # [T, H, 512]
+                         self.kv[li], q, Hl, self.qdim, cfg.qk_nope_dim)
+        q3 = q.view(T, Hl, self.qdim)
+        q_lat = torch.einsum("thd,hdl->thl", q3[..., :cfg.qk_nope_dim], L.w_uk)  # [T, Hl, 512]
+        if Hl != H:  # tensor parallel: this rank's heads in the kernel's 16-head layout
+            ql = torch.zeros(T, H, LAT, dtype=q_lat.dtype, device=self.device)
+            ql[:, h0:h0 + Hl] = q_lat
+            qf = torch.zeros(T, H, self.qdim, dtype=q.dtype, device=self.device)
+            qf[:, h0:h0 + Hl] = q3
+            q_lat, q = ql, qf.view(T, H * self.qdim)
+        q_lat = q_lat.contiguous()
         if inp.decode:
             row_seq = torch.arange(T, dtype=torch.int32, device=self.device)
         else:
@@ -130,11 +160,13 @@ class DeepseekV2Runner(LlamaRunner):
         splits = max(1, min(32, math.ceil(2 * 148 / T)))
         o_lat = ops.mla_attention(q_lat, q, self.qdim, cfg.qk_nope_dim, self.kv[li], inp.block_tables, row_seq,
                                   row_len, H, splits, self.scale)
-        o = torch.einsum("thl,hvl->thv", o_lat, L.w_uv).reshape(T, H * cfg.v_head_dim)
+        o = torch.einsum("thl,hvl->thv", o_lat[:, h0:h0 + Hl], L.w_uv).reshape(T, Hl * cfg.v_head_dim)
         if T <= GEMV_MAX_T:
-            self._lin_q8(L.wo, ops.quantize_q8(o, self.x2), T, EPI_ADD_F32, out=x)
+            oq = ops.quantize_q8(o, self.x2)
+            self._row_parallel(0, lambda m, out: self._lin_q8(L.wo, oq, T, m, out=out), x)
         else:
-            self._lin_bf16(L.wo, o.to(self.act_dtype), T, EPI_ADD_F32, out=x)
+            ob = o.to(self.act_dtype)
+            self._row_parallel(0, lambda m, out: self._lin_bf16(L.wo, ob, T, m, out=out), x)
 
     def forward(self, inp: StepInput) -> torch.Tensor:
         cfg = self.cfg
@@ -145,13 +177,9 @@ class DeepseekV2Runner(LlamaRunner):
             self._mla(L, li, x, inp, T)
             hb, hq = self._norm(x, L.ffn_norm, T)
             if L.moe is not None:
-                L.moe.forward(self, hq, hb, T, x)
-            elif T <= GEMV_MAX_T:
-                h2 = self._lin_q8(L.gate_up, hq, T, EPI_SWIGLU_Q8)
-                self._lin_q8(L.down, h2, T, EPI_ADD_F32, out=x)
+                self._moe_out(L, hq, hb, T, x)
             else:
-                h = ops.gemm(L.gate_up, hb, EPI_SWIGLU_Q8)
-                ops.gemm(L.down, h, EPI_ADD_F32, out=x)
+                self._row_parallel(1, lambda m, out: self._dense_ffn(L, hq, hb, T, m, out), x)
         xl = x.index_select(0, inp.last_idx) if not inp.decode else x
         _, oq = ops.rmsnorm(xl, self.out_norm, cfg.rms_eps, want_q8=True, x2=self.x2)
-        return self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32)
+        return self._gather_logits(self._lin_q8(self.out_w, oq, xl.shape[0], EPI_STORE_F32))

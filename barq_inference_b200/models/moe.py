@@ -59,6 +59,9 @@ class MoEBlock:
             self.shared = (ops.interleave_gate_up(sg, su).finalize(), sd.finalize())
         self.sigmoid = cfg.expert_gating == "sigmoid"
         self.renorm = cfg.arch != "deepseek2" or cfg.expert_weights_norm
+        # tensor parallel with replicated shared experts: only one rank adds their output to the
+        # partial sums the all-reduce completes
+        self.shared_here = True
         self.stats = {"tokens": 0, "dispatched": 0}
         self.load = None  # models.moe_stats.ExpertLoad when expert-load counting is on
         self.layer_index = 0
@@ -72,7 +75,7 @@ class MoEBlock:
             self._fused(logits, hb, T, x, ser)
         else:
             self._unfused(logits, hb, T, x, ser)
-        if self.shared is not None:
+        if self.shared is not None and self.shared_here:
             gu, down = self.shared
             if T <= 8 and hq is not None:
                 h2 = ops.gemv(gu, hq, T, EPI_SWIGLU_Q8, x2=runner.x2)

@@ -33,6 +33,8 @@ class TPInfo:
     n_experts_local: int = 0
     vocab0: int = 0        # first vocabulary row of this rank's head shard
     vocab_local: int = 0
+    head0: int = 0         # MLA: first attention head of this rank
+    n_heads_local: int = 0
 
 
 def _rows(pt: PackedTensor, r0: int, n: int, shape: tuple[int, ...]) -> PackedTensor:
@@ -67,7 +69,7 @@ def shard_tensors(cfg: ModelConfig, tensors: dict[str, PackedTensor], rank: int,
                   ) -> tuple[dict[str, PackedTensor], TPInfo]:
     """This rank's tensors for tensor parallelism of degree ``world`` (attention TP x MoE EP)."""
     if cfg.is_mla:
-        raise ValueError("tensor parallel MLA is not implemented (DeepSeek runs expert parallel on one GPU)")
+        return _shard_mla(cfg, tensors, rank, world)
     H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     _split(H, world, rank, "attention heads")
     _split(Hkv, world, rank, "KV heads")
@@ -109,4 +111,47 @@ def shard_tensors(cfg: ModelConfig, tensors: dict[str, PackedTensor], rank: int,
                 out["output.weight"] = _rows(pt, v0, vn, (vn,) + tuple(pt.shape[1:]))
         else:
             out[name] = pt
+    return out, info
+
+
+def _shard_mla(cfg: ModelConfig, tensors: dict[str, PackedTensor], rank: int, world: int
+               ) -> tuple[dict[str, PackedTensor], TPInfo]:
+    """DeepSeek-V2 (MLA): attention heads split over the ranks, the latent path replicated.
+
+    Per rank: the query projection rows and the per-head ``attn_kv_b`` blocks (W_UK / W_UV) of its
+    heads; ``attn_output`` columns of its heads (row-parallel, completed by the all-reduce);
+    ``attn_q_a`` / ``attn_kv_a_mqa`` and their norms whole, so every rank writes the same latent
+    cache rows.  Routed experts split by expert and the head by vocabulary as for the dense models;
+    the dense FFN and the shared experts replicated (added by rank 0 only)."""
+    H, dn, dv, dr = cfg.n_heads, cfg.qk_nope_dim, cfg.v_head_dim, cfg.qk_rope_dim
+    h0, hn = _split(H, world, rank, "attention heads")
+    info = TPInfo(rank, world)
+    out: dict[str, PackedTensor] = {}
+    rest: dict[str, PackedTensor] = {}
+    for name, pt in tensors.items():
+        short = name.split(".", 2)[-1] if name.startswith("blk.") else name
+        if short in ("attn_q.weight", "attn_q_b.weight"):
+            qd = dn + dr
+            out[name] = _rows(pt, h0 * qd, hn * qd, (hn * qd,) + tuple(pt.shape[1:]))
+        elif short == "attn_kv_b.weight":
+            kd = dn + dv
+            out[name] = _rows(pt, h0 * kd, hn * kd, (hn * kd,) + tuple(pt.shape[1:]))
+        elif short == "attn_output.weight":
+            out[name] = _cols(pt, h0 * dv, (h0 + hn) * dv)
+        elif short.startswith("attn_"):
+            out[name] = pt  # q_a / kv_a projections, norms: replicated latent path
+        elif short in ("ffn_gate.weight", "ffn_up.weight", "ffn_down.weight", "ffn_gate_shexp.weight",
+                       "ffn_up_shexp.weight", "ffn_down_shexp.weight"):
+            # the leading dense FFN and the shared experts stay whole (their widths, e.g. 10944 / 8,
+            # do not split into the GEMM's 128-row tiles); rank 0 alone adds them to the partial sums
+            out[name] = pt
+        else:
+            rest[name] = pt
+    # FFNs (dense, shared experts, routed experts) and the vocabulary-parallel head: the dense rules
+    dense_cfg = dataclasses.replace(cfg, kv_lora_rank=0, n_heads=world, n_kv_heads=world, head_dim=1)
+    ffn, finfo = shard_tensors(dense_cfg, rest, rank, world)
+    out.update(ffn)
+    info.expert0, info.n_experts_local = finfo.expert0, finfo.n_experts_local
+    info.vocab0, info.vocab_local = finfo.vocab0, finfo.vocab_local
+    info.head0, info.n_heads_local = h0, hn
     return out, info

@@ -58,7 +58,7 @@ def _worker(rank, world, port, name, mode, q):
     wide = dict(hidden=512, n_heads=8, n_kv_heads=8, head_dim=64, ffn=1024)
     cfg = (dataclasses.replace(preset("tiny"), **wide) if name == "tiny-sp" else
            dataclasses.replace(preset("tiny-moe"), n_experts=8, **wide) if name == "tiny-moe-sp" else preset(name))
-    full = random_tensors(cfg, POLICIES["tiny"], seed=4)
+    full = random_tensors(cfg, POLICIES["tiny-ds" if cfg.is_mla else "tiny"], seed=4)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (20,), generator=g).tolist()
     comm = Comm(dev, fused=mode != "nccl", max_elems=64 * cfg.hidden,
@@ -67,7 +67,12 @@ def _worker(rank, world, port, name, mode, q):
     if mode == "sp":
         comm.sp_min_tokens = 9  # the 20-token prompt runs sequence-parallel
     shard, info = shard_tensors(cfg, full, rank, world)
-    r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
+    if cfg.is_mla:  # DeepSeek-V2: heads split, latent path replicated
+        from barq_inference_b200.models.deepseek2 import DeepseekV2Runner
+
+        r = DeepseekV2Runner(cfg, shard, dev, tp=info, comm=comm)
+    else:
+        r = LlamaRunner(shard_config(cfg, world), shard, dev, tp=info, comm=comm)
     r.allocate_kv(32)
     tp_logits = _logits(r, prompt)
     comm.check()
@@ -79,7 +84,12 @@ def _worker(rank, world, port, name, mode, q):
         if cfg.n_experts:  # ... and every MoE layer went through the expert all-to-all
             assert int(comm.ep_epoch[0]) == cfg.n_layers, comm.ep_epoch
     if rank == 0:
-        ref = LlamaRunner(cfg, full, dev)
+        if cfg.is_mla:
+            from barq_inference_b200.models.deepseek2 import DeepseekV2Runner
+
+            ref = DeepseekV2Runner(cfg, full, dev)
+        else:
+            ref = LlamaRunner(cfg, full, dev)
         ref.allocate_kv(32)
         q.put(("ok", (tp_logits - _logits(ref, prompt)).abs().max().item()))
     comm.barrier()
@@ -125,6 +135,13 @@ def test_tp_expert_parallel_all_to_all_matches_single_gpu(world):
     _run_tp(world, "tiny-moe-sp", "sp")
 
 
+@needs2
+@pytest.mark.parametrize("mode", ["oneshot", "nccl"])
+def test_tp2_deepseek_mla_matches_single_gpu(mode):
+    """DeepSeek-V2 (MLA + shared / routed experts) with its 16 heads split over 2 ranks."""
+    _run_tp(2, "tiny-ds", mode)
+
+
 def _pp_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       NCCL_NVLS_ENABLE="0")
@@ -148,7 +165,12 @@ def _pp_worker(rank, world, port, q):
     r.allocate_kv(32)
     pp_logits = _logits(r, prompt)
     if rank == 0:
-        ref = LlamaRunner(cfg, full, dev)
+        if cfg.is_mla:
+            from barq_inference_b200.models.deepseek2 import DeepseekV2Runner
+
+            ref = DeepseekV2Runner(cfg, full, dev)
+        else:
+            ref = LlamaRunner(cfg, full, dev)
         ref.allocate_kv(32)
         q.put(("ok", (pp_logits - _logits(ref, prompt)).abs().max().item()))
     dist.barrier()

@@ -152,3 +152,27 @@ def test_tp_pp_grid_groups(tmp_path):
     assert [x["tp_sum"] for x in r] == [1.0, 1.0, 5.0, 5.0]
     assert [x["logits"] for x in r] == [102.0, 103.0, 102.0, 103.0]
     assert [x["h"] for x in r] == [0.0, 10.0, 0.0, 10.0]  # stage 1 received its stage-0 peer's states
+
+
+def test_mla_shards_heads_and_keeps_latent_path_whole():
+    """DeepSeek-V2 tensor parallel: query / kv_b rows and output columns by head, the latent
+    projections, dense FFN and shared experts whole, routed experts by expert; the shards' query
+    rows and output columns reassemble the full tensors."""
+    import torch
+
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.parallel.tp import shard_tensors
+
+    cfg = preset("tiny-ds")
+    full = random_tensors(cfg, POLICIES["tiny-ds"], seed=4)
+    shards = [shard_tensors(cfg, full, r, 2) for r in range(2)]
+    for r, (sh, info) in enumerate(shards):
+        assert (info.head0, info.n_heads_local) == (8 * r, 8)
+        assert sh["blk.1.attn_kv_a_mqa.weight"] is full["blk.1.attn_kv_a_mqa.weight"]
+        assert sh["blk.0.ffn_down.weight"] is full["blk.0.ffn_down.weight"]
+        assert sh["blk.1.ffn_down_shexp.weight"] is full["blk.1.ffn_down_shexp.weight"]
+        assert sh["blk.1.ffn_gate_exps.weight"].shape[0] == 2 and info.expert0 == 2 * r
+    q = torch.cat([shards[r][0]["blk.1.attn_q.weight"].data for r in range(2)])
+    assert torch.equal(q, full["blk.1.attn_q.weight"].data)
+    o = torch.cat([shards[r][0]["blk.1.attn_output.weight"].data for r in range(2)], 1)
+    assert torch.equal(o, full["blk.1.attn_output.weight"].data)
