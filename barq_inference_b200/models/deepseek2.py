@@ -8,7 +8,9 @@ rope/nope split, shared + routed experts, first ``n_dense_layers`` dense) and th
   and the shared rotary key ``k_pe`` (64) -- 8x less cache than materialized per-head K/V;
 * queries are absorbed: ``q_lat = q_nope . W_UK`` (per-head 128x512 blocks of ``attn_kv_b``), so the
   attention kernel (K10, ``csrc/kernels/mla.cu``) scores ``q_lat . c + q_pe . k_pe`` directly on the
-  cached latents and returns ``o_lat = softmax . c``; ``o_lat . W_UV^T`` gives the head outputs;
+  cached latents and returns ``o_lat = softmax . c``; ``o_lat . W_UV^T`` gives the head outputs.
+  Both absorptions run as grouped tcgen05 GEMMs (one group per head, Q8_0 weights, bf16
+  activations) -- no cuBLAS on the attention path;
 * expert FFNs are :class:`MoEBlock` (group-limited top-k, shared experts), the first layer is dense;
 * tensor parallel (``tp`` / ``comm``): each rank holds the query projection, W_UK / W_UV and the
   output-projection columns of H / tp heads, the latent path (q_a, kv_a, cache) replicated; the
@@ -33,6 +35,14 @@ from .runner import GEMV_MAX_T, Layer, LlamaRunner, StepInput, _f32, _qw, apply_
 from .weights import PackedTensor
 
 LAT, ROPE = 512, 64
+
+
+def _q8_grouped(w: torch.Tensor, dev) -> ops.QWeight:
+    """f32 [rows, K] -> Q8_0 QWeight on ``dev`` (rows are whole 128-row groups of a grouped GEMM)."""
+    from ..gguf import GGMLType, quantize
+
+    w = w.to(dev).contiguous()
+    return ops.QWeight.from_packed(quantize(w, GGMLType.Q8_0), GGMLType.Q8_0, w.shape[0], w.shape[1], dev).finalize()
 
 
 class DeepseekV2Runner(LlamaRunner):
@@ -79,8 +89,10 @@ class DeepseekV2Runner(LlamaRunner):
             L.kv_a = _qw(tensors[p + "attn_kv_a_mqa.weight"], dev)
             L.kv_a_norm = _f32(tensors[p + "attn_kv_a_norm.weight"], dev)
             kvb = dequant_tensor(tensors[p + "attn_kv_b.weight"]).view(self.Hl, dn + dv, LAT).float()
-            L.w_uk = kvb[:, :dn, :].contiguous().to(dev)  # [H, dn, 512]
-            L.w_uv = kvb[:, dn:, :].contiguous().to(dev)  # [H, dv, 512]
+            # absorption weights as grouped tcgen05 GEMM operands (one group per head, Q8_0):
+            # W_UK^T [Hl * 512, dn] maps q_nope to q_lat, W_UV [Hl * dv, 512] maps o_lat to the head outputs
+            L.uk = _q8_grouped(kvb[:, :dn, :].transpose(1, 2).reshape(self.Hl * LAT, dn), dev)
+            L.uv = _q8_grouped(kvb[:, dn:, :].reshape(self.Hl * dv, LAT), dev)
             L.wo = _qw(tensors[p + "attn_output.weight"], dev)
             if cfg.layer_is_moe(i):
                 L.moe = MoEBlock(cfg, tensors, p, dev, expert0=tp.expert0 if tp is not None else 0)
@@ -115,6 +127,15 @@ class DeepseekV2Runner(LlamaRunner):
         return ops.rmsnorm(x, w, self.cfg.rms_eps, want_q8=T <= GEMV_MAX_T, want_bf16=True, x2=self.x2,
                            act_dtype=self.act_dtype)
 
+    def _per_head(self, w, x: torch.Tensor, n_out: int) -> torch.Tensor:
+        """Per-head projection x [T, Hl, K] -> [T, Hl, n_out] as one grouped tcgen05 GEMM (group h =
+        head h's rows of ``w``; the activations in head-major order, bf16)."""
+        T, Hl, K = x.shape
+        xs = x.permute(1, 0, 2).reshape(Hl * T, K).to(self.act_dtype).contiguous()
+        off = torch.arange(0, (Hl + 1) * T, T, dtype=torch.int32, device=self.device)
+        y = ops.gemm_grouped(w, xs, off, Hl, EPI_STORE_F32)  # [Hl * T, n_out]
+        return y.view(Hl, T, n_out).permute(1, 0, 2).contiguous()
+
     def _dense_ffn(self, L, hq, hb, T, mode, out):
         """The leading dense FFN, replicated under tensor parallelism: rank 0 adds (or stores) it,
         the other ranks contribute zeros to the all-reduce."""
@@ -143,7 +164,7 @@ class DeepseekV2Runner(LlamaRunner):
         ops.mla_kv_write(kva, L.kv_a_norm, cfg.rms_eps, self.cos, self.sin, cfg.rope_neox, inp.pos, inp.slots,
                          self.kv[li], q, Hl, self.qdim, cfg.qk_nope_dim)
         q3 = q.view(T, Hl, self.qdim)
-        q_lat = torch.einsum("thd,hdl->thl", q3[..., :cfg.qk_nope_dim], L.w_uk)  # [T, Hl, 512]
+        q_lat = self._per_head(L.uk, q3[..., :cfg.qk_nope_dim], LAT)  # [T, Hl, 512]
         if Hl != H:  # tensor parallel: this rank's heads in the kernel's 16-head layout
             ql = torch.zeros(T, H, LAT, dtype=q_lat.dtype, device=self.device)
             ql[:, h0:h0 + Hl] = q_lat
@@ -160,7 +181,7 @@ class DeepseekV2Runner(LlamaRunner):
         splits = max(1, min(32, math.ceil(2 * 148 / T)))
         o_lat = ops.mla_attention(q_lat, q, self.qdim, cfg.qk_nope_dim, self.kv[li], inp.block_tables, row_seq,
                                   row_len, H, splits, self.scale)
-        o = torch.einsum("thl,hvl->thv", o_lat[:, h0:h0 + Hl], L.w_uv).reshape(T, Hl * cfg.v_head_dim)
+        o = self._per_head(L.uv, o_lat[:, h0:h0 + Hl], cfg.v_head_dim).reshape(T, Hl * cfg.v_head_dim)
         if T <= GEMV_MAX_T:
             oq = ops.quantize_q8(o, self.x2)
             self._row_parallel(0, lambda m, out: self._lin_q8(L.wo, oq, T, m, out=out), x)
