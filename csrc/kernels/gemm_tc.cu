@@ -1048,7 +1048,8 @@ static int dispatch_bn(const void* x, const GemmDev& g0, cudaStream_t st) {
     int ks = 1;
     if ((g.mode == EPI_STORE_F32 || g.mode == EPI_ADD_F32 || g.mode == EPI_RS_PUSH || g.mode == EPI_SWIGLU_Q8) &&
         g.ld_out % 4 == 0 && g.N % 4 == 0)
-      while (ks < kMaxAutoSplits && tiles * ks * 2 <= 2 * n && KG / (ks * 2) >= 2) ks *= 2;
+      // more splits only while the work units still fit one wave of CTAs
+      while (ks < kMaxAutoSplits && tiles * ks * 2 <= n && KG / (ks * 2) >= 2) ks *= 2;
     g.k_splits = ks;
   }
   if (g.k_splits > KG) g.k_splits = KG;
