@@ -389,3 +389,19 @@ def test_spec_verify_kernel_preserves_target_distribution():
     C.spec_verify(ps, None, d.to(DEV), 1, 0, 0, out)
     r = out.cpu().tolist()
     assert r[0] == 2 and r[1:4] == [int(tgt[0]), int(tgt[1]), int(tgt[2])]
+
+
+def test_sampler_topk_ties_and_short_rows():
+    """Top-k selection on a 128256-token row: of 40 tokens tied at the top, exactly k = 20 stay in
+    play (ties go to the lower index), and a row with fewer than k tokens within 80 of the max
+    samples among those only."""
+    V = 128256
+    g = torch.Generator().manual_seed(2)
+    lg = torch.randn(V, generator=g)
+    lg[100:140] = 9.0  # 40 tokens tied at the top, k = 20
+    ids, _ = _sample(lg.to(DEV).repeat(2000, 1), 1.0, k=20)
+    assert set(ids.tolist()) == set(range(100, 120))
+    short = torch.full((V,), -1000.0)
+    short[[7, 70000, 128000]] = torch.tensor([1.0, 0.5, 0.0])
+    ids, _ = _sample(short.to(DEV).repeat(1000, 1), 1.0, k=50)
+    assert set(ids.tolist()) <= {7, 70000, 128000} and len(set(ids.tolist())) == 3
