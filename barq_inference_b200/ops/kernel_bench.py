@@ -254,7 +254,50 @@ def cases(tokens: int):
             return _Bytes(nb), (lambda: blk.forward(_R(), None, hb, T, x)), 2.0 * T * 2 * 3 * 4096 * 14336
         return make
 
+    def mla_decode(B: int, ctx: int):
+        # DeepSeek-V2-Lite MLA decode attention: B rows of ctx cached latents (576-wide bf16 rows), 16 heads
+        def make():
+            from . import mla_attention
+
+            H, qdim = 16, 192
+            pages = (ctx + 15) // 16
+            cache = torch.randn(B * pages + 1, 16, 576, device="cuda").bfloat16()
+            bt = (torch.arange(B * pages, dtype=torch.int32, device="cuda") + 1).view(B, pages)
+            q_lat = torch.randn(B, H, 512, device="cuda")
+            q = torch.randn(B, H * qdim, device="cuda")
+            rs = torch.arange(B, dtype=torch.int32, device="cuda")
+            rl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+            splits = max(1, min(32, -(-2 * 148 // B)))
+            return _Bytes(B * ctx * 576 * 2), (lambda: mla_attention(q_lat, q, qdim, 128, cache, bt, rs, rl, H, splits,
+                                                                      0.1)), 4.0 * B * H * ctx * 576
+        return make
+
+    def sp_reduce(T: int):
+        # owner side of a sequence-parallel site as a world of one rank (Llama-3-8B hidden 4096): wait
+        # for the pushed tiles, add them into the residual rows, RMSNorm, push the rows and their flags
+        def make():
+            from . import require_ext
+
+            C = require_ext()
+            H = 4096
+            max_tiles = (H // 128) * ((T + 31) // 32)
+            slots = torch.randn(T * H, device="cuda")
+            flags = torch.full((max_tiles,), 1 << 30, dtype=torch.int32, device="cuda")  # every tile "arrived"
+            x = torch.randn(T, H, device="cuda")
+            nw = torch.ones(H, device="cuda")
+            ag = torch.empty(T, H, dtype=torch.float16, device="cuda")
+            agf = torch.zeros(T, dtype=torch.int32, device="cuda")
+            ep = torch.zeros(1, dtype=torch.int32, device="cuda")
+            done = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+            def run():
+                C.sp_reduce_norm_ag(x, T, 0, T, slots, flags, 1, max_tiles, C.gemm_tile_rows(T), H // 128, None, nw,
+                                    1e-5, [ag.data_ptr()], [agf.data_ptr()], ep, done, 5.0, 1, 0)
+            return _Bytes(T * H * (4 + 4 + 4 + 2)), run, 0.0
+        return make
+
     return {"allreduce_w1": allreduce_w1, "attn_decode_bs32": attn_decode(32, 1024),
+            "mla_decode_bs32": mla_decode(32, 4096), "sp_reduce_t512": sp_reduce(512),
             "rope_kv_t32": rope_kv(32), "sampler_bs32": sampler(32), "prefill_attn_t2048": prefill_attn(2048),
             "moe_mixtral_t64": moe_layer(64),
             "attn_decode_bs1": attn_decode(1, 1024), "decode_step_bs1": decode_step(1, 64),
