@@ -24,7 +24,7 @@ import torch
 from .. import ops
 from ..models.config import ModelConfig
 from ..models.runner import LlamaRunner, StepInput
-from .kv_cache import BlockManager
+from .kv_cache import BlockManager, new_block_manager  # noqa: F401
 from .scheduler import ScheduledStep, Scheduler, SchedulerConfig
 from .sampling_params import SamplingParams
 from .sequence import Sequence
@@ -97,13 +97,13 @@ class Engine:
 
         self._profile = StepProfiler.from_env(self)  # BARQ_PROFILE / BARQ_NVTX
         self.last_plan = None
-        self.blocks = BlockManager(nb, ec.block_size)
+        self.blocks = new_block_manager(nb, ec.block_size)  # C++ pool when built
         self.dummy_block = self.blocks.allocate(1)[0]  # padding rows of graph batches write here
         self.prefix_cache = None
         if ec.prefix_caching:
-            from .prefix_cache import RadixPrefixCache
+            from .prefix_cache import new_prefix_cache
 
-            self.prefix_cache = RadixPrefixCache(self.blocks)
+            self.prefix_cache = new_prefix_cache(self.blocks)
         self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
                                                ec.chunked_prefill, sliding_window=cfg.sliding_window,
                                                max_waiting=ec.max_waiting),

@@ -89,3 +89,50 @@ class RadixPrefixCache:
     def stats(self) -> dict:
         return {"cached_blocks": self.n_blocks, "queries": self.queries, "hits": self.hits,
                 "hit_rate": self.hits / self.queries if self.queries else 0.0}
+
+
+class NativeRadixPrefixCache:
+    """:class:`RadixPrefixCache` backed by the C++ ``_native.RadixCache`` over a
+    :class:`~.kv_cache.NativeBlockManager` (same matches and LRU evictions; an eviction is
+    O(log n) rather than a walk over the tree)."""
+
+    def __init__(self, blocks):
+        self.bm = blocks
+        self.bs = blocks.block_size
+        from .. import _native
+
+        self.tree = _native.RadixCache(blocks.pool)
+
+    def match(self, tokens: list[int]) -> tuple[list[int], int]:
+        blocks, n = self.tree.match(list(tokens))
+        return list(blocks), n
+
+    def insert(self, tokens: list[int], block_table: list[int]) -> None:
+        self.tree.insert(list(tokens), list(block_table))
+
+    def evict(self, n: int) -> int:
+        return self.tree.evict(n)
+
+    @property
+    def n_blocks(self) -> int:
+        return self.tree.n_blocks
+
+    @property
+    def hits(self) -> int:
+        return self.tree.hits
+
+    @property
+    def queries(self) -> int:
+        return self.tree.queries
+
+    def stats(self) -> dict:
+        q = self.queries
+        return {"cached_blocks": self.n_blocks, "queries": q, "hits": self.hits,
+                "hit_rate": self.hits / q if q else 0.0}
+
+
+def new_prefix_cache(blocks):
+    """Radix prefix cache matching the block manager's backend (native pool -> native tree)."""
+    from .kv_cache import NativeBlockManager
+
+    return NativeRadixPrefixCache(blocks) if isinstance(blocks, NativeBlockManager) else RadixPrefixCache(blocks)

@@ -1,4 +1,5 @@
-"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, dequant oracle) built with
+"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool and radix
+prefix cache, dequant oracle) built with
 AddressSanitizer + UndefinedBehaviorSanitizer and driven with fuzzed and random inputs, CPU only.
 
 compute-sanitizer is not available for the device code on this pool; the host-side native code gets
@@ -26,7 +27,8 @@ DRIVER = textwrap.dedent(r'''
     flags = ["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined", "-fno-sanitize-recover=undefined",
              "-std=c++17"]
     nat = load(name="_native_asan", sources=[os.path.join(root, "csrc/native", f) for f in
-                                              ("gguf_native.cpp", "tokenizer_native.cpp", "grammar_native.cpp")],
+                                              ("gguf_native.cpp", "tokenizer_native.cpp", "grammar_native.cpp",
+                                                        "kvcache_native.cpp")],
                extra_cflags=flags, extra_ldflags=["-fsanitize=address,undefined"],
                build_directory=tempfile.mkdtemp(prefix="barq-asan-"), verbose=False)
     sys.path.insert(0, root)
@@ -86,7 +88,28 @@ DRIVER = textwrap.dedent(r'''
             m.allowed_mask(94)
             if m.done():
                 break
-    # 4) the C++ dequant / GEMV oracle on random blocks of every type it reads
+    # 4) KV block pool + radix prefix cache under random matches, inserts, evictions and frees
+    pool = nat.BlockPool(48, 4)
+    tree = nat.RadixCache(pool)
+    live = []
+    for _ in range(3000):
+        op = rng.random()
+        toks = [rng.randrange(3) for _ in range(rng.randrange(1, 40))]
+        if op < 0.35:
+            blocks, n = tree.match(toks)
+            need = pool.blocks_for(len(toks) + 1) - len(blocks)
+            if not pool.can_allocate(need):
+                tree.evict(need - pool.n_free)
+                continue
+            pool.retain(blocks)
+            live.append((toks, list(blocks) + pool.allocate(need)))
+        elif op < 0.6 and live:
+            t, table = live.pop(rng.randrange(len(live)))
+            tree.insert(t, table)
+            pool.release(table)
+        else:
+            tree.evict(rng.randrange(1, 6))
+    # 5) the C++ dequant / GEMV oracle on random blocks of every type it reads
     ref = load(name="_cpu_ref_asan", sources=[os.path.join(root, "csrc/cpu_ref/cpu_ref.cpp")], extra_cflags=flags,
                extra_ldflags=["-fsanitize=address,undefined"], build_directory=tempfile.mkdtemp(prefix="barq-asan-"))
     for ty, ts, be in ((2, 18, 32), (20, 18, 32), (8, 34, 32), (12, 144, 256), (13, 176, 256), (14, 210, 256)):
