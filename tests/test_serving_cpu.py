@@ -235,6 +235,50 @@ def test_uds_protocol(tiny_engine, tmp_path):
         ae.shutdown()
 
 
+def test_native_uds_client(tiny_engine, tmp_path):
+    """The C++ client speaks the same framing: its streamed text equals the Python client's for a
+    greedy request, --json prints every frame, and a server-side error gives exit status 1."""
+    import shutil
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSClient, UDSServer
+    from barq_inference_b200.server.uds_native import build_client
+
+    if shutil.which("g++") is None and shutil.which("c++") is None:
+        pytest.skip("no C++ compiler")
+    exe = build_client()
+    path = str(tmp_path / "barq.sock")
+    ae = AsyncEngine(tiny_engine)
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        prompt = 'say "hi"\n\u00e9 \U0001F600'
+        cl = UDSClient(path)
+        want = "".join(f["text"] for f in cl.stream(prompt, max_tokens=6, temperature=0.0, rid="py"))
+        cl.close()
+        r = subprocess.run([exe, "--socket", path, "--max-tokens", "6", "--temperature", "0", "--id", "cc", prompt],
+                           capture_output=True, timeout=120)
+        assert r.returncode == 0, r.stderr
+        assert r.stdout.decode("utf-8") == want + "\n"
+        assert b"[cc] tokens=" in r.stderr
+        r = subprocess.run([exe, "--socket", path, "--max-tokens", "3", "--temperature", "0", "--json",
+                            "--repeat", "2", "hello"], capture_output=True, timeout=120)
+        assert r.returncode == 0, r.stderr
+        frames = [json.loads(line) for line in r.stdout.decode().splitlines()]
+        assert [f["done"] for f in frames].count(True) == 2
+        assert {f["id"] for f in frames} == {"req-0", "req-1"}
+        assert b"summary: requests=2" in r.stderr
+        r = subprocess.run([exe, "--socket", path, "--max-tokens", "1000", "x " * 400], capture_output=True,
+                           timeout=120)
+        assert r.returncode == 1 and b"error=prompt exceeds max_model_len" in r.stderr
+        r = subprocess.run([exe, "--socket", path, "--max-tokens", "-1", "x"], capture_output=True, timeout=60)
+        assert r.returncode == 2  # usage error
+        r = subprocess.run([exe, "--socket", str(tmp_path / "none.sock"), "x"], capture_output=True, timeout=60)
+        assert r.returncode == 2 and b"cannot connect" in r.stderr
+    finally:
+        srv.stop()
+        ae.shutdown()
+
+
 # ------------------------------------------------------------------ CLI
 def _cli(*args, timeout=300):
     return subprocess.run([sys.executable, "-m", "barq_inference_b200.cli", *args], cwd=ROOT, capture_output=True,
