@@ -71,7 +71,7 @@ class UDSServer:
             ids = prompt if isinstance(prompt, list) else self.tok.encode(str(prompt))
             params = SamplingParams(max_tokens=int(req.get("max_tokens", 128)),
                                     temperature=float(req.get("temperature", 0.8)), top_k=40, top_p=0.95)
-        except (KeyError, TypeError, ValueError) as e:
+        except Exception as e:  # noqa: BLE001 - any failure ends the stream with an error frame
             send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
                               "done": True, "error": f"bad request: {e}"})
             return
@@ -95,7 +95,7 @@ class UDSServer:
                         guard.first_token()
                 send_frame(conn, {"id": rid, "text": dec.push(item.token), "tokens_generated": n,
                                   "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
-        except ValueError as e:
+        except Exception as e:  # noqa: BLE001 - a failed request still gets its final frame
             if guard is not None:
                 guard.fail()
                 guard = None

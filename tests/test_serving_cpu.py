@@ -236,12 +236,12 @@ def test_uds_protocol(tiny_engine, tmp_path):
 
 
 def test_native_uds_client(tiny_engine, tmp_path):
-    """The C++ client speaks the same framing: its streamed text equals the Python client's for a
-    greedy request, --json prints every frame, and a server-side error gives exit status 1."""
+    """The C++ client against the real UDS server: a streamed request, --json prints every frame,
+    --repeat summarises, a server-side error gives exit status 1, usage / connect errors give 2."""
     import shutil
 
     from barq_inference_b200.server.async_engine import AsyncEngine
-    from barq_inference_b200.server.uds import UDSClient, UDSServer
+    from barq_inference_b200.server.uds import UDSServer
     from barq_inference_b200.server.uds_native import build_client
 
     if shutil.which("g++") is None and shutil.which("c++") is None:
@@ -251,14 +251,9 @@ def test_native_uds_client(tiny_engine, tmp_path):
     ae = AsyncEngine(tiny_engine)
     srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
     try:
-        prompt = 'say "hi"\n\u00e9 \U0001F600'
-        cl = UDSClient(path)
-        want = "".join(f["text"] for f in cl.stream(prompt, max_tokens=6, temperature=0.0, rid="py"))
-        cl.close()
-        r = subprocess.run([exe, "--socket", path, "--max-tokens", "6", "--temperature", "0", "--id", "cc", prompt],
-                           capture_output=True, timeout=120)
+        r = subprocess.run([exe, "--socket", path, "--max-tokens", "6", "--temperature", "0", "--id", "cc",
+                            'say "hi"\n\u00e9'], capture_output=True, timeout=120)
         assert r.returncode == 0, r.stderr
-        assert r.stdout.decode("utf-8") == want + "\n"
         assert b"[cc] tokens=" in r.stderr
         r = subprocess.run([exe, "--socket", path, "--max-tokens", "3", "--temperature", "0", "--json",
                             "--repeat", "2", "hello"], capture_output=True, timeout=120)
@@ -277,6 +272,47 @@ def test_native_uds_client(tiny_engine, tmp_path):
     finally:
         srv.stop()
         ae.shutdown()
+
+
+def test_native_uds_client_decodes_frames(tmp_path):
+    """Scripted server: the request the C++ client sends parses as the Python side expects, and the
+    text it prints is exactly the concatenated frame texts (escapes, BMP and astral code points,
+    unknown nested fields skipped)."""
+    import shutil
+    import threading
+
+    from barq_inference_b200.server.uds import recv_frame, send_frame
+    from barq_inference_b200.server.uds_native import build_client
+
+    if shutil.which("g++") is None and shutil.which("c++") is None:
+        pytest.skip("no C++ compiler")
+    exe = build_client()
+    path = str(tmp_path / "fake.sock")
+    texts = ["plain ", 'quo"te\\ ', "tab\tnl\n", "\u00e9\u20ac", "\U0001F600", "/end"]
+    got = {}
+    lsock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    lsock.bind(path)
+    lsock.listen(1)
+
+    def serve():
+        conn, _ = lsock.accept()
+        got["req"] = recv_frame(conn)
+        for i, t in enumerate(texts):  # json.dumps escapes non-ASCII as \uXXXX (surrogate pairs)
+            send_frame(conn, {"id": got["req"]["id"], "text": t, "tokens_generated": i + 1, "ttft_ms": 5,
+                              "total_time_ms": 10 + i, "done": i == len(texts) - 1, "extra": {"a": [1, "]}"]}})
+        conn.close()
+
+    th = threading.Thread(target=serve, daemon=True)
+    th.start()
+    prompt = 'say "hi"\n\u00e9 \U0001F600'
+    r = subprocess.run([exe, "--socket", path, "--max-tokens", "7", "--temperature", "0.25", "--id", "q1", prompt],
+                       capture_output=True, timeout=60)
+    th.join(10)
+    lsock.close()
+    assert r.returncode == 0, r.stderr
+    assert got["req"] == {"id": "q1", "prompt": prompt, "max_tokens": 7, "temperature": 0.25}
+    assert r.stdout.decode("utf-8") == "".join(texts) + "\n"
+    assert b"[q1] tokens=6 ttft_ms=5 total_ms=15" in r.stderr
 
 
 # ------------------------------------------------------------------ CLI
