@@ -10,7 +10,8 @@
 //               of its edge and a reference on it.  A child is found by hashing (parent, tokens).
 //               Eviction walks an ordered set of (last use, node) over the current leaves and frees
 //               the least recently used leaf that no running sequence holds (block ref == 1), so an
-//               eviction costs O(log n) instead of a walk over the whole tree.
+//               eviction costs O(log n) plus one step per older leaf that a running sequence still
+//               holds, instead of a walk over the whole tree.
 //
 // The Python classes in engine/kv_cache.py and engine/prefix_cache.py implement the same contract
 // and serve as the oracle in tests/test_kvcache_native.py (random operation sequences, identical
