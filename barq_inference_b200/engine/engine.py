@@ -25,7 +25,7 @@ from .. import ops
 from ..models.config import ModelConfig
 from ..models.runner import LlamaRunner, StepInput
 from .kv_cache import BlockManager, new_block_manager  # noqa: F401
-from .scheduler import ScheduledStep, Scheduler, SchedulerConfig
+from .scheduler import ScheduledStep, SchedulerConfig, new_scheduler
 from .sampling_params import SamplingParams
 from .sequence import Sequence
 
@@ -104,7 +104,7 @@ class Engine:
             from .prefix_cache import new_prefix_cache
 
             self.prefix_cache = new_prefix_cache(self.blocks)
-        self.sched = Scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
+        self.sched = new_scheduler(SchedulerConfig(ec.max_num_seqs, ec.max_num_batched_tokens, ec.max_model_len,
                                                ec.chunked_prefill, sliding_window=cfg.sliding_window,
                                                max_waiting=ec.max_waiting),
                                self.blocks, self.prefix_cache)

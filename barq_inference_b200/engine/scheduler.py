@@ -130,8 +130,18 @@ class Scheduler:
         self.finish(seq, "abort")
         return True
 
-    def _preempt_youngest(self, protect: Sequence | None = None) -> bool:
-        cands = [s for s in self.running if s is not protect]
+    def clear_waiting(self, reason: str = "abort") -> None:
+        """Drop every waiting request (engine failure or shutdown); their pages return to the pool."""
+        for seq in self.waiting:
+            seq.status = SeqStatus.FINISHED
+            seq.finish_reason = seq.finish_reason or reason
+            self._free(seq)
+        self.waiting.clear()
+
+    def _preempt_youngest(self, protect=()) -> bool:
+        """Return the youngest running sequence not in ``protect`` to the front of the queue (its
+        pages are freed; it recomputes on readmission)."""
+        cands = [s for s in self.running if not any(s is p for p in protect)]
         if not cands:
             return False
         victim = max(cands, key=lambda s: s.arrival)
@@ -153,10 +163,13 @@ class Scheduler:
         budget = cfg.max_num_batched_tokens
         seqs, n_new = [], []
         for s in pre:
+            if s.status is not SeqStatus.RUNNING:
+                continue  # preempted to make room for a chunk scheduled above
             n = min(s.n_uncached, budget)
             if n <= 0:
                 break
-            if not self._reserve(s, s.n_cached + n):
+            # sequences already in this step's plan are never preempted for a later one
+            if not self._reserve(s, s.n_cached + n, protect=(*seqs, s)):
                 break
             seqs.append(s)
             n_new.append(n)
@@ -210,12 +223,173 @@ class Scheduler:
             return None
         return ScheduledStep("decode", dec, [1] * len(dec))
 
-    def _reserve(self, s: Sequence, n_tokens: int) -> bool:
+    def _reserve(self, s: Sequence, n_tokens: int, protect=None) -> bool:
         need = self.blocks.blocks_for(n_tokens) - len(s.block_table)
         while need > self.blocks.n_free:
             if self.prefix_cache is not None and self.prefix_cache.evict(need - self.blocks.n_free):
                 continue
-            if not self._preempt_youngest(protect=s):
+            if not self._preempt_youngest(protect=(s,) if protect is None else protect):
                 return False
         self.blocks.grow(s.block_table, n_tokens)
         return True
+
+
+_STATUS = (SeqStatus.WAITING, SeqStatus.RUNNING, SeqStatus.FINISHED)
+
+
+class NativeScheduler:
+    """:class:`Scheduler` whose queues, block tables, admission, window release and preemption run
+    in the C++ core ``_native.Scheduler`` (``csrc/native/scheduler_native.cpp``) over the native
+    block pool and radix tree.  Same decisions as the Python class (the tests replay random
+    workloads through both).
+
+    The :class:`Sequence` objects stay the engine's view: after ``schedule()`` the records of the
+    sequences the core changed (status, cached length, block table and its generation, window and
+    preemption counters) are copied onto them, and the cached lengths and tokens the engine wrote
+    into the sequences of a plan are committed to the core before it next reads them (the next
+    ``schedule()``, or ``finish()`` / ``abort()`` of that sequence).
+    """
+
+    def __init__(self, cfg: SchedulerConfig, blocks, prefix_cache=None):
+        from .. import _native
+
+        self.cfg = cfg
+        self.blocks = blocks
+        self.prefix_cache = prefix_cache
+        self.core = _native.Scheduler(blocks.pool, prefix_cache.tree if prefix_cache is not None else None,
+                                      cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.chunked_prefill,
+                                      cfg.sliding_window)
+        self._seqs: dict[int, Sequence] = {}
+        self._ntok: dict[int, int] = {}        # tokens of each sequence that the core holds
+        self._pending: dict[int, Sequence] = {}  # sequences of the last plan, not yet committed
+
+    # ---------------------------------------------------------------- state mirrored to Python
+    @property
+    def dummy_block(self) -> int | None:
+        b = self.core.dummy_block
+        return None if b < 0 else b
+
+    @dummy_block.setter
+    def dummy_block(self, b: int | None) -> None:
+        self.core.dummy_block = -1 if b is None else int(b)
+
+    @property
+    def waiting(self) -> list[Sequence]:
+        """Snapshot of the waiting queue (front first); change it through the methods."""
+        return [self._seqs[i] for i in self.core.waiting_ids()]
+
+    @property
+    def running(self) -> list[Sequence]:
+        return [self._seqs[i] for i in self.core.running_ids()]
+
+    @property
+    def has_work(self) -> bool:
+        return bool(self.core.n_waiting or self.core.n_running)
+
+    @property
+    def n_preemptions(self) -> int:
+        return self.core.n_preemptions
+
+    @property
+    def n_window_freed(self) -> int:
+        return self.core.n_window_freed
+
+    def _commit(self, seqs) -> None:
+        ids, cached, n_app, toks = [], [], [], []
+        for s in seqs:
+            known = self._ntok[s.seq_id]
+            new = s.output[known - len(s.prompt):] if s.n_tokens > known else []
+            ids.append(s.seq_id)
+            cached.append(s.n_cached)
+            n_app.append(len(new))
+            toks.extend(new)
+            self._ntok[s.seq_id] = known + len(new)
+        if ids:
+            self.core.commit(ids, cached, n_app, toks)
+
+    def _sync_one(self, seq: Sequence) -> None:
+        if self._pending.pop(seq.seq_id, None) is not None:
+            self._commit((seq,))
+
+    def _apply(self) -> None:
+        for sid, st, n_cached, wf, gen, npre, phit, table in self.core.take_changes():
+            s = self._seqs[sid]
+            s.status = _STATUS[st]
+            s.n_cached, s.window_freed, s.bt_gen = n_cached, wf, gen
+            s.n_preempted, s.prefix_hit, s.block_table = npre, phit, table
+            if st == 2:
+                del self._seqs[sid], self._ntok[sid]
+                self._pending.pop(sid, None)
+                self.core.forget(sid)
+
+    # ---------------------------------------------------------------- Scheduler interface
+    def add(self, seq: Sequence) -> None:
+        if len(seq.prompt) == 0:
+            raise ValueError("empty prompt")
+        if len(seq.prompt) >= self.cfg.max_model_len:
+            raise ValueError(f"prompt of {len(seq.prompt)} tokens exceeds max_model_len {self.cfg.max_model_len}")
+        usable = self.blocks.num_blocks - (1 if self.dummy_block is not None else 0)
+        need = self.blocks.blocks_for(len(seq.prompt) + 1)
+        if need > usable:
+            raise ValueError(f"prompt of {len(seq.prompt)} tokens needs {need} KV pages; the pool has {usable}")
+        if self.cfg.max_waiting and self.core.n_waiting >= self.cfg.max_waiting:
+            raise Overloaded(f"{self.core.n_waiting} requests already waiting; retry later")
+        self.core.add(seq.seq_id, float(seq.arrival), list(seq.tokens), seq.embeds is not None)
+        self._seqs[seq.seq_id] = seq
+        self._ntok[seq.seq_id] = seq.n_tokens
+        self._apply()
+
+    def finish(self, seq: Sequence, reason: str) -> None:
+        seq.finish_reason = reason
+        if seq.seq_id not in self._seqs:
+            seq.status = SeqStatus.FINISHED
+            return
+        self._sync_one(seq)
+        self.core.finish(seq.seq_id)
+        self._apply()
+
+    def abort(self, seq: Sequence) -> bool:
+        if seq.status is SeqStatus.FINISHED or seq.seq_id not in self._seqs:
+            return False
+        self._sync_one(seq)
+        if not self.core.abort(seq.seq_id):
+            return False
+        seq.finish_reason = "abort"
+        self._apply()
+        return True
+
+    def clear_waiting(self, reason: str = "abort") -> None:
+        for seq in self.waiting:
+            seq.finish_reason = seq.finish_reason or reason
+            self._sync_one(seq)
+            self.core.abort(seq.seq_id)
+        self._apply()
+
+    def schedule(self) -> ScheduledStep | None:
+        if self._pending:
+            self._commit(self._pending.values())
+            self._pending.clear()
+        kind, ids, n_new = self.core.schedule()
+        self._apply()
+        if kind == 0:
+            return None
+        seqs = [self._seqs[i] for i in ids]
+        self._pending = {s.seq_id: s for s in seqs}
+        return ScheduledStep("prefill" if kind == 1 else "decode", seqs, list(n_new))
+
+
+def new_scheduler(cfg: SchedulerConfig, blocks, prefix_cache=None):
+    """The engine's scheduler: the native core when the block pool (and prefix cache) are native
+    (``BARQ_NATIVE_SCHED=0`` forces the Python class)."""
+    import os
+
+    from .kv_cache import NativeBlockManager
+    from .prefix_cache import NativeRadixPrefixCache
+
+    native = (os.environ.get("BARQ_NATIVE_SCHED", "1") != "0" and isinstance(blocks, NativeBlockManager)
+              and (prefix_cache is None or isinstance(prefix_cache, NativeRadixPrefixCache)))
+    if native:
+        from .. import _native
+
+        native = hasattr(_native, "Scheduler")
+    return (NativeScheduler if native else Scheduler)(cfg, blocks, prefix_cache)

@@ -130,10 +130,7 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
             return
         sched = getattr(eng, "sched", None)
         if sched is not None:
-            if seq in sched.waiting:
-                sched.waiting.remove(seq)
-            elif seq in sched.running:
-                sched.finish(seq, "abort")
+            sched.abort(seq)
         else:
             for lst in (eng.waiting, eng.running):
                 if seq in lst:
@@ -168,7 +165,7 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
                     cancel(rid, err)
                 sched = getattr(eng, "sched", None)
                 if sched is not None:
-                    sched.waiting.clear()
+                    sched.clear_waiting("error")
         if events:
             outq.put((idx, "events", events))
             events = []

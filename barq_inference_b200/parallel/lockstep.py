@@ -76,7 +76,7 @@ def _reset(engine) -> None:
         return
     for s in list(sched.running):
         sched.finish(s, "error")
-    sched.waiting.clear()
+    sched.clear_waiting("error")
 
 
 def follower_loop(engine, store, wait_s: float = 7 * 24 * 3600.0, collect: list | None = None) -> int:

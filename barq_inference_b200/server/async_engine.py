@@ -132,7 +132,7 @@ class AsyncEngine:
         if hasattr(eng, "sched"):
             for s in list(eng.sched.running):
                 eng.sched.finish(s, "error")
-            eng.sched.waiting.clear()
+            eng.sched.clear_waiting("error")
         else:
             eng.running.clear()
             eng.waiting.clear()

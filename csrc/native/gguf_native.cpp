@@ -238,13 +238,15 @@ py::tuple parse_bytes(py::bytes b) {
 void register_tokenizer(py::module_& m);  // tokenizer_native.cpp
 void register_grammar(py::module_& m);    // grammar_native.cpp
 void register_kvcache(py::module_& m);    // kvcache_native.cpp
+void register_scheduler(py::module_& m);  // scheduler_native.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.doc() = "barq native runtime pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool "
-            "and radix prefix cache)";
+  m.doc() = "barq native runtime pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool, "
+            "radix prefix cache and continuous-batching scheduler core)";
   register_tokenizer(m);
   register_grammar(m);
   register_kvcache(m);
+  register_scheduler(m);
   m.def("gguf_parse", &parse, "memory-map and parse a GGUF file");
   m.def("gguf_parse_bytes", &parse_bytes, "parse a GGUF header held in memory (no tensor data view)");
 }

@@ -1,5 +1,5 @@
-"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool and radix
-prefix cache, dequant oracle) built with
+"""The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool, radix
+prefix cache and scheduler core, dequant oracle) built with
 AddressSanitizer + UndefinedBehaviorSanitizer and driven with fuzzed and random inputs, CPU only.
 
 compute-sanitizer is not available for the device code on this pool; the host-side native code gets
@@ -28,7 +28,7 @@ DRIVER = textwrap.dedent(r'''
              "-std=c++17"]
     nat = load(name="_native_asan", sources=[os.path.join(root, "csrc/native", f) for f in
                                               ("gguf_native.cpp", "tokenizer_native.cpp", "grammar_native.cpp",
-                                                        "kvcache_native.cpp")],
+                                                        "kvcache_native.cpp", "scheduler_native.cpp")],
                extra_cflags=flags, extra_ldflags=["-fsanitize=address,undefined"],
                build_directory=tempfile.mkdtemp(prefix="barq-asan-"), verbose=False)
     sys.path.insert(0, root)
@@ -109,6 +109,46 @@ DRIVER = textwrap.dedent(r'''
             pool.release(table)
         else:
             tree.evict(rng.randrange(1, 6))
+    # 4b) the scheduler core over a small pool: random adds, steps, finishes and aborts
+    pool = nat.BlockPool(14, 4)
+    tree = nat.RadixCache(pool)
+    sch = nat.Scheduler(pool, tree, 4, 24, True, 0)
+    sch.dummy_block = pool.allocate(1)[0]
+    state, nid = {}, 0  # id -> [n_tokens, n_cached, tokens left to generate]
+    for step in range(3000):
+        if rng.random() < 0.3 and len(state) < 12:
+            prompt = [rng.randrange(3) for _ in range(rng.randrange(1, 20))]
+            sch.add(nid, float(nid // 2), prompt, rng.random() < 0.1)
+            state[nid] = [len(prompt), 0, rng.randrange(1, 30)]
+            nid += 1
+        if state and rng.random() < 0.05:
+            sid = rng.choice(list(state))
+            sch.abort(sid)
+        kind, ids, n_new = sch.schedule()
+        for c in sch.take_changes():
+            if c[1] == 2:
+                sch.forget(c[0])
+                state.pop(c[0], None)
+            elif c[0] in state:
+                state[c[0]][1] = c[2]
+        n_app, flat, cached = [], [], []
+        for sid, n in zip(ids, n_new):
+            st = state[sid]
+            st[1] += n
+            app = []
+            if st[1] >= st[0]:
+                app = [rng.randrange(3)]
+                st[0] += 1
+                st[2] -= 1
+            n_app.append(len(app))
+            flat += app
+            cached.append(st[1])
+        sch.commit(ids, cached, n_app, flat)
+        for sid in ids:
+            if state[sid][2] <= 0:
+                sch.finish(sid)
+        if kind == 0 and not state and step > 100:
+            break
     # 5) the C++ dequant / GEMV oracle on random blocks of every type it reads
     ref = load(name="_cpu_ref_asan", sources=[os.path.join(root, "csrc/cpu_ref/cpu_ref.cpp")], extra_cflags=flags,
                extra_ldflags=["-fsanitize=address,undefined"], build_directory=tempfile.mkdtemp(prefix="barq-asan-"))
