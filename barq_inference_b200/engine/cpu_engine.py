@@ -15,7 +15,7 @@ import torch
 
 from ..models.config import ModelConfig
 from ..models.reference import ReferenceModel
-from ..sampling.host_samplers import HostSampler, sample_chain
+from ..sampling.host_samplers import new_host_sampler, sample_chain
 from .engine import GenerationResult
 from .sampling_params import SamplingParams
 from .sequence import Sequence, SeqStatus
@@ -62,7 +62,7 @@ class CPUEngine:
 
             seq.grammar_state = make_grammar_state(self, params)
         if params.needs_host_sampler:
-            seq.host_sampler = HostSampler(params, self.cfg.vocab)
+            seq.host_sampler = new_host_sampler(params, self.cfg.vocab)
         self.waiting.append(seq)
         return seq
 

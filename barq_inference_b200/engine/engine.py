@@ -154,9 +154,9 @@ class Engine:
 
             seq.grammar_state = make_grammar_state(self, params)
         if params.needs_host_sampler:
-            from ..sampling.host_samplers import HostSampler
+            from ..sampling.host_samplers import new_host_sampler
 
-            seq.host_sampler = HostSampler(params, self.cfg.vocab)
+            seq.host_sampler = new_host_sampler(params, self.cfg.vocab)
         self.sched.add(seq)
         return seq
 
@@ -404,8 +404,8 @@ class Engine:
                 h[i, : len(last)] = last
             pen, hist = self._to_dev(pa), self._to_dev(h)
         host = [i for i, s in enumerate(seqs) if s.host_sampler is not None]
-        if host:
-            lg = logits.float().cpu()
+        if host:  # only the rows sampled on the host cross to it
+            lg = dict(zip(host, logits[torch.tensor(host, device=logits.device)].float().cpu()))
         ids, lp = ops.sample(logits, temp, topk, topp, minp, seeds, steps, allow_mask=mask, penalties=pen,
                              history=hist, want_logprob=any(s.params.logprobs for s in seqs))
         out = ids.cpu().tolist()

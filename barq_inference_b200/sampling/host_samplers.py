@@ -13,7 +13,10 @@ thresholds raw probabilities); these follow the papers:
   probability exceeds ``xtc_threshold`` except the least likely of them.
 
 The common chain (penalties, temperature, top-k, top-p, min-p) runs on the GPU in the fused sampler
-kernel; sequences that ask for Mirostat, typical or XTC are sampled here from the logits row.
+kernel; sequences that ask for Mirostat, typical or XTC are sampled on the host from their logits
+row: by the C++ chain ``_native.HostSampler`` (``csrc/native/sampler_native.cpp``: partial sorts
+instead of whole-row sorts) when the extension is built, else by :class:`HostSampler` here, which is
+also that chain's oracle.
 """
 from __future__ import annotations
 
@@ -172,3 +175,50 @@ def sample_chain(logits: torch.Tensor, params, history: list[int], gen: torch.Ge
     lg = min_p_filter(lg, p.min_p)
     probs = torch.softmax(lg, -1)
     return int(torch.multinomial(probs, 1, generator=gen))
+
+
+class NativeHostSampler:
+    """:class:`HostSampler` on the C++ chain (same filters and Mirostat updates; its own RNG)."""
+
+    def __init__(self, params, vocab: int):
+        from .. import _native
+
+        p = self.p = params
+        self.vocab = vocab
+        self.impl = _native.HostSampler(
+            vocab=vocab, seed=int(p.seed) if p.seed else 0x5EED, temperature=p.temperature, top_k=p.top_k,
+            top_p=p.top_p, min_p=p.min_p, typical_p=p.typical_p, repetition=p.repetition_penalty,
+            frequency=p.frequency_penalty, presence=p.presence_penalty, mirostat=p.mirostat, tau=p.mirostat_tau,
+            eta=p.mirostat_eta, xtc_probability=p.xtc_probability, xtc_threshold=p.xtc_threshold)
+
+    @property
+    def mu(self) -> float:
+        return self.impl.mu
+
+    def _history(self, seq) -> list[int]:
+        p = self.p
+        if seq is None or not p.needs_penalties or p.penalty_last_n <= 0:
+            return []
+        return seq.last_tokens(p.penalty_last_n)
+
+    def sample(self, logits: torch.Tensor, seq=None) -> int:
+        return self.impl.sample(logits.detach().float().reshape(-1).cpu().numpy(), self._history(seq))
+
+    def distribution(self, logits: torch.Tensor, seq=None) -> tuple[list[int], list[float]]:
+        """The kept tokens and the probabilities the next draw uses (XTC, being random, left out)."""
+        return self.impl.distribution(logits.detach().float().reshape(-1).cpu().numpy(), self._history(seq))
+
+
+def new_host_sampler(params, vocab: int):
+    """The C++ chain when ``_native`` is built (``BARQ_NATIVE_SAMPLER=0`` forces the Python one)."""
+    import os
+
+    if os.environ.get("BARQ_NATIVE_SAMPLER", "1") != "0":
+        try:
+            from .. import _native
+
+            if hasattr(_native, "HostSampler"):
+                return NativeHostSampler(params, vocab)
+        except ImportError:
+            pass
+    return HostSampler(params, vocab)

@@ -239,14 +239,16 @@ void register_tokenizer(py::module_& m);  // tokenizer_native.cpp
 void register_grammar(py::module_& m);    // grammar_native.cpp
 void register_kvcache(py::module_& m);    // kvcache_native.cpp
 void register_scheduler(py::module_& m);  // scheduler_native.cpp
+void register_sampler(py::module_& m);    // sampler_native.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "barq native runtime pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool, "
-            "radix prefix cache and continuous-batching scheduler core)";
+            "radix prefix cache, continuous-batching scheduler core, host sampler chain)";
   register_tokenizer(m);
   register_grammar(m);
   register_kvcache(m);
   register_scheduler(m);
+  register_sampler(m);
   m.def("gguf_parse", &parse, "memory-map and parse a GGUF file");
   m.def("gguf_parse_bytes", &parse_bytes, "parse a GGUF header held in memory (no tensor data view)");
 }

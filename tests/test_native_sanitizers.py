@@ -1,5 +1,5 @@
 """The native C++ pieces (GGUF parser, tokenizer merge loops, grammar recognizer, KV block pool, radix
-prefix cache and scheduler core, dequant oracle) built with
+prefix cache, scheduler core, host sampler chain, dequant oracle) built with
 AddressSanitizer + UndefinedBehaviorSanitizer and driven with fuzzed and random inputs, CPU only.
 
 compute-sanitizer is not available for the device code on this pool; the host-side native code gets
@@ -28,7 +28,8 @@ DRIVER = textwrap.dedent(r'''
              "-std=c++17"]
     nat = load(name="_native_asan", sources=[os.path.join(root, "csrc/native", f) for f in
                                               ("gguf_native.cpp", "tokenizer_native.cpp", "grammar_native.cpp",
-                                                        "kvcache_native.cpp", "scheduler_native.cpp")],
+                                                        "kvcache_native.cpp", "scheduler_native.cpp",
+                                                        "sampler_native.cpp")],
                extra_cflags=flags, extra_ldflags=["-fsanitize=address,undefined"],
                build_directory=tempfile.mkdtemp(prefix="barq-asan-"), verbose=False)
     sys.path.insert(0, root)
@@ -149,6 +150,22 @@ DRIVER = textwrap.dedent(r'''
                 sch.finish(sid)
         if kind == 0 and not state and step > 100:
             break
+    # 4c) the host sampler chain on random parameters and rows (penalty ids out of range included)
+    for trial in range(200):
+        V = rng.choice([1, 2, 7, 300, 5000])
+        smp = nat.HostSampler(vocab=V, seed=trial, temperature=rng.choice([0.0, 0.5, 1.0, 2.0]),
+                              top_k=rng.choice([0, 1, 5, V + 3]), top_p=rng.choice([1.0, 0.9, 0.1]),
+                              min_p=rng.choice([0.0, 0.05, 1.0]), typical_p=rng.choice([1.0, 0.5, 0.01]),
+                              repetition=rng.choice([1.0, 1.5]), frequency=rng.choice([0.0, 0.3]),
+                              presence=rng.choice([0.0, 0.2]), mirostat=rng.choice([0, 1, 2]), tau=5.0, eta=0.1,
+                              xtc_probability=rng.choice([0.0, 1.0]), xtc_threshold=rng.choice([0.01, 0.5]))
+        row = (np.random.default_rng(trial).standard_normal(V + 2) * rng.choice([0.1, 3.0, 30.0])).astype(np.float32)
+        hist = [rng.randrange(-3, V + 3) for _ in range(rng.randrange(0, 20))]
+        for _ in range(3):
+            t = smp.sample(row, hist)
+            assert 0 <= t < V, (t, V)
+        ids, probs = smp.distribution(row, hist)
+        assert ids and all(0 <= i < V for i in ids) and abs(sum(probs) - 1) < 1e-6
     # 5) the C++ dequant / GEMV oracle on random blocks of every type it reads
     ref = load(name="_cpu_ref_asan", sources=[os.path.join(root, "csrc/cpu_ref/cpu_ref.cpp")], extra_cflags=flags,
                extra_ldflags=["-fsanitize=address,undefined"], build_directory=tempfile.mkdtemp(prefix="barq-asan-"))
