@@ -153,6 +153,24 @@ def test_preemption_under_a_small_pool_matches_reference():
         assert len(r.tokens) == 30 and _follows_reference(ref, p, r.tokens)
 
 
+def test_host_sampled_rows_in_a_mixed_batch_match_reference():
+    """Sequences sampled on the host (Mirostat v2 with a tiny target surprise keeps only the most
+    likely token) share decode batches with device-sampled greedy ones: each host row must get its
+    own sequence's logits, so every sequence follows the reference's greedy continuation."""
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=6)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=128, max_num_seqs=4)
+    prompts = _prompts(cfg, 4, 7)
+    params = [SamplingParams.greedy_params(max_tokens=10),
+              SamplingParams(temperature=1.0, mirostat=2, mirostat_tau=0.01, max_tokens=10, seed=1),
+              SamplingParams.greedy_params(max_tokens=10),
+              SamplingParams(temperature=1.0, mirostat=2, mirostat_tau=0.01, max_tokens=10, seed=2)]
+    res = eng.generate(prompts, params)
+    for p, r in zip(prompts, res):
+        assert len(r.tokens) == 10 and _follows_reference(ref, p, r.tokens)
+
+
 def test_prefix_cache_reuse_matches_reference():
     cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
     t = random_tensors(cfg, POLICIES["tiny"], seed=4)
