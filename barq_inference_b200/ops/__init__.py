@@ -296,13 +296,19 @@ def mla_kv_write(kv_a: torch.Tensor, norm_w: torch.Tensor, eps: float, cos: torc
 
 def mla_attention(q_lat: torch.Tensor, q: torch.Tensor, qdim: int, rope_off: int, cache: torch.Tensor,
                   block_tables: torch.Tensor, row_seq: torch.Tensor, row_len: torch.Tensor, H: int, splits: int,
-                  scale: float) -> torch.Tensor:
-    """Absorbed MLA attention (K10): returns o_lat f32 [rows, H, 512]."""
+                  scale: float, impl: int | None = None) -> torch.Tensor:
+    """Absorbed MLA attention (K10): returns o_lat f32 [rows, H, 512].
+
+    ``impl`` 0 runs the CUDA-core kernel, 1 the tensor-core kernel (``mla_attn_mma_kernel``); by
+    default ``BARQ_MLA_MMA`` picks (unset: 0)."""
     C = require_ext()
+    if impl is None:
+        impl = int(os.environ.get("BARQ_MLA_MMA", "0"))
     rows = q_lat.shape[0]
     scratch = torch.empty(C.mla_attn_scratch_floats(rows, splits), dtype=torch.float32, device=q_lat.device)
     o = torch.empty(rows, H, 512, dtype=torch.float32, device=q_lat.device)
-    C.mla_attention(q_lat, q, qdim, rope_off, cache, block_tables, row_seq, row_len, H, splits, scale, scratch, o)
+    C.mla_attention(q_lat, q, qdim, rope_off, cache, block_tables, row_seq, row_len, H, splits, scale, scratch, o,
+                    int(impl))
     _count(2)
     return o
 

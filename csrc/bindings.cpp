@@ -320,7 +320,7 @@ int64_t mla_attn_scratch_floats(int64_t rows, int64_t splits) {
 
 void mla_attention(Tensor q_lat, Tensor q, int64_t qdim, int64_t rope_off, Tensor cache, Tensor block_tables,
                    Tensor row_seq, Tensor row_len, int64_t H, int64_t splits, double scale, Tensor scratch,
-                   Tensor o_lat) {
+                   Tensor o_lat, int64_t impl) {
   c10::cuda::CUDAGuard g(q_lat.device());
   const int rows = (int)q_lat.size(0);
   TORCH_CHECK((size_t)scratch.numel() >= barq::mla_attn_scratch_floats(rows, (int)splits), "mla: scratch too small");
@@ -340,7 +340,9 @@ void mla_attention(Tensor q_lat, Tensor q, int64_t qdim, int64_t rope_off, Tenso
   a.part_acc = ptr<float>(scratch);
   a.part_ml = reinterpret_cast<float2*>(ptr<float>(scratch) + (size_t)rows * splits * H * 512);
   a.o_lat = ptr<float>(o_lat);
-  check(barq::mla_attention(a, cache.scalar_type() == torch::kBFloat16, cur_stream()), "mla_attention");
+  a.err = barq::kernel_err_word();
+  a.num_blocks = (int)cache.size(0);
+  check(barq::mla_attention(a, cache.scalar_type() == torch::kBFloat16, cur_stream(), (int)impl), "mla_attention");
 }
 
 // bufs / flags: device addresses (one per rank) of the partial buffers and flag areas.

@@ -135,9 +135,12 @@ struct MlaAttnArgs {
   float* part_acc;     // scratch [rows, splits, H, 512]
   float2* part_ml;     // scratch [rows, splits, H]
   float* o_lat;        // [rows, H, 512]
+  int* err = nullptr;  // error word of the tensor-core kernel (0xA00: block-table entry out of range)
+  int num_blocks = 0;  // cache pages, for that check (0: unchecked)
 };
 size_t mla_attn_scratch_floats(int rows, int splits);
-int mla_attention(const MlaAttnArgs& a, int cache_is_bf16, cudaStream_t st);
+// impl 0: CUDA-core kernel; 1: tensor-core kernel (mma.m16n8k16 over a copy-warp page ring)
+int mla_attention(const MlaAttnArgs& a, int cache_is_bf16, cudaStream_t st, int impl = 0);
 
 // MoE routing + dispatch (moe.cu).  logits f32 [T, E] -> ids/weights [T, k]; rows of x (fp16/bf16
 // [T, H]) are copied into xs [T*k, H] sorted by expert, off [E+1] holds each expert's row range, and
