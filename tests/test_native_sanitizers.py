@@ -201,3 +201,75 @@ def test_native_code_under_asan_ubsan(tmp_path):
     out = r.stdout + r.stderr
     assert r.returncode == 0 and "SANITIZED RUN OK" in r.stdout, out[-4000:]
     assert "runtime error" not in out and "AddressSanitizer" not in out, out[-4000:]
+
+
+@pytest.mark.skipif(os.environ.get("BARQ_SANITIZE") != "1", reason="set BARQ_SANITIZE=1 (builds with ASan/UBSan)")
+def test_uds_client_under_asan_ubsan(tmp_path):
+    """The native UDS client against a scripted server that answers with valid, truncated,
+    byte-flipped and oversized frames: every run ends with a clean exit status (0, 1 or 2) and no
+    sanitizer report."""
+    import json
+    import random
+    import socket
+    import struct
+    import threading
+
+    gxx = shutil.which("g++", path="/usr/bin") or shutil.which("g++")
+    exe = str(tmp_path / "barq-uds-asan")
+    subprocess.run([gxx, "-O1", "-g", "-std=c++17", "-fsanitize=address,undefined", "-fno-sanitize-recover=undefined",
+                    "-fno-omit-frame-pointer", "-o", exe, os.path.join(ROOT, "csrc", "client", "barq_uds.cpp")],
+                   check=True)
+    rng = random.Random(0)
+    good = [json.dumps({"id": "r", "text": t, "tokens_generated": i, "ttft_ms": 1, "total_time_ms": 2,
+                        "done": i == 2, "extra": [{"k": "v"}, None, 1e300]}).encode() for i, t in
+            enumerate(["aé", "\U0001F600", "end"])]
+
+    def mutate(b: bytes) -> bytes:
+        b = bytearray(b)
+        for _ in range(rng.randrange(1, 6)):
+            op = rng.random()
+            if op < 0.4 and b:
+                b[rng.randrange(len(b))] = rng.randrange(256)
+            elif op < 0.7 and b:
+                del b[rng.randrange(len(b)):]
+            else:
+                b[rng.randrange(len(b) + 1):0] = bytes(rng.choice([b"\\u", b"\\ud83d", b"{", b"[", b"\"", b"\\"]))
+        return bytes(b)
+
+    env = {**os.environ, "ASAN_OPTIONS": "detect_leaks=1:abort_on_error=1",
+           "UBSAN_OPTIONS": "halt_on_error=1:print_stacktrace=1"}
+    codes = set()
+    for case in range(60):
+        path = str(tmp_path / f"s{case}.sock")
+        lsock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        lsock.bind(path)
+        lsock.listen(1)
+        frames = [f if case % 3 == 0 else mutate(f) for f in good]
+        big = case % 17 == 5  # a length prefix above the 16 MiB limit
+
+        def serve():
+            conn, _ = lsock.accept()
+            try:
+                head = conn.recv(4)
+                n = struct.unpack(">I", head)[0]
+                while n > 0:
+                    n -= len(conn.recv(n))
+                for f in frames:
+                    conn.sendall(struct.pack(">I", (1 << 30) if big else len(f)) + f)
+            except OSError:
+                pass
+            finally:
+                conn.close()
+
+        th = threading.Thread(target=serve, daemon=True)
+        th.start()
+        r = subprocess.run([exe, "--socket", path, "--json", "prompt"], capture_output=True, env=env, timeout=60)
+        th.join(10)
+        lsock.close()
+        err = r.stderr.decode(errors="replace")
+        assert r.returncode in (0, 1, 2), (case, r.returncode, err[-2000:])
+        assert "runtime error" not in err and "AddressSanitizer" not in err and "LeakSanitizer" not in err, err[-2000:]
+        if case % 3 == 0 and not big:
+            assert r.returncode == 0, err
+        codes.add(r.returncode)
+    assert {0, 2} <= codes, codes  # clean streams and rejected (malformed / oversized) ones both seen
