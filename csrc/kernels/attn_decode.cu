@@ -29,29 +29,31 @@ namespace barq {
 constexpr int kBS = 16;  // tokens per KV page
 
 constexpr int kAttnRing = 6;       // shared-memory page slots per CTA (3 CTAs per SM fit)
+constexpr int kAttnRingDeep = 12;  // opt-in (BARQ_ATTN_RING=12): twice the bytes in flight per CTA, 2 CTAs per SM
 constexpr int kAttnThreads = 160;  // 4 compute warps + 1 copy warp
 
 // Ring layout: per slot one K page and one V page of 16 tokens x D operands (fp16 / bf16; an fp8
 // cache is widened to fp16 by the copy warp), rows padded to D + 8 elements so that ldmatrix reads
 // are bank-conflict free.
-template <typename TM, int D>
+template <typename TM, int D, int RING = kAttnRing>
 struct AttnRing {
   static constexpr int LD = D + 8;
   static constexpr int PAGE = kBS * LD * (int)sizeof(TM);
   static constexpr int SLOT = 2 * PAGE;
   static constexpr int QBYTES = 16 * LD * (int)sizeof(TM);  // the (padded) query heads, after the ring
-  static constexpr int BYTES = kAttnRing * SLOT + QBYTES;
+  static constexpr int BYTES = RING * SLOT + QBYTES;
 };
 
 // TC: cache element type; TM: tensor-core operand type (TC for fp16 / bf16, fp16 for fp8).
-template <typename TC, typename TM, int D, int G>
+template <typename TC, typename TM, int D, int G, int RING>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArgs a) {
   pdl_wait();
   pdl_trigger();
   constexpr int NW = 4;
   constexpr int KS = D / 16;  // k-steps of QK^T
   constexpr int ND = D / 8;   // O n-blocks
-  using R = AttnRing<TM, D>;
+  using R = AttnRing<TM, D, RING>;
+  static_assert(4 * G * D * (int)sizeof(float) <= RING * R::SLOT, "the warp merge aliases the ring");
   constexpr int LD = R::LD;
   static_assert(G <= 8, "query heads of a KV head fit the first 8 MMA rows");
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -59,14 +61,14 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
   const float sl2 = a.scale * 1.4426950408889634f;
 
   extern __shared__ __align__(128) uint8_t ring[];
-  TM* sQ = reinterpret_cast<TM*>(ring + kAttnRing * R::SLOT);
-  __shared__ __align__(8) uint64_t full[kAttnRing], empty[kAttnRing];
+  TM* sQ = reinterpret_cast<TM*>(ring + RING * R::SLOT);
+  __shared__ __align__(8) uint64_t full[RING], empty[RING];
   __shared__ float m_s[NW][G], l_s[NW][G];
   __shared__ int err_s;
 
   if (threadIdx.x == 0) {
     err_s = 0;
-    for (int i = 0; i < kAttnRing; ++i) {
+    for (int i = 0; i < RING; ++i) {
       tc::mbar_init(&full[i], 32);  // one arrival per copy-warp lane
       tc::mbar_init(&empty[i], 1);
     }
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
     constexpr int PIECES = kBS * D / 8;  // 8-element pieces per page
     int pg = 0;  // physical page of entry (i & ~31) + lane: block-table entries fetched 32 at a time
     for (int i = 0; i < npg; ++i) {
-      const int s = i % kAttnRing;
+      const int s = i % RING;
       if ((i & 31) == 0) pg = i + lane < npg ? bt[sb + i + lane] : 0;
       int phys = __shfl_sync(0xffffffffu, pg, i & 31);
       if (a.num_blocks > 0 && (phys < 0 || phys >= a.num_blocks)) {  // bad block-table entry
@@ -111,8 +113,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
         phys = 0;
       }
       bool ok = true;
-      if (i >= kAttnRing) {
-        if (lane == 0) ok = tc::mbar_wait(&empty[s], ((i / kAttnRing) - 1) & 1, err, 1);
+      if (i >= RING) {
+        if (lane == 0) ok = tc::mbar_wait(&empty[s], ((i / RING) - 1) & 1, err, 1);
         ok = __shfl_sync(0xffffffffu, ok, 0);
       }
       if (!ok) break;
@@ -160,8 +162,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(DecodeAttnArg
       ldsm_x4(qf[kk], smem_u32(sQ + r * LD + c));
     }
     for (int i = warp; i < npg; i += NW) {
-      const int s = i % kAttnRing;
-      if (*err || !tc::mbar_wait(&full[s], (uint32_t)((i / kAttnRing) & 1), err, 2)) break;
+      const int s = i % RING;
+      if (*err || !tc::mbar_wait(&full[s], (uint32_t)((i / RING) & 1), err, 2)) break;
       const TM* k_s = reinterpret_cast<const TM*>(ring + s * R::SLOT);
       const TM* v_s = reinterpret_cast<const TM*>(ring + s * R::SLOT + R::PAGE);
       // S = Q K^T: 16 (head) rows x 16 tokens
@@ -345,14 +347,29 @@ size_t decode_attention_scratch_floats(int B, int H, int Hkv, int D, int splits)
   return (size_t)B * H * splits * D + (size_t)B * H * splits * 2;
 }
 
-template <typename TC, int D, int G>
-static cudaError_t launch_attn(const DecodeAttnArgs& a, dim3 grid, cudaStream_t st) {
+template <typename TC, int D, int G, int RING>
+static cudaError_t launch_attn_ring(const DecodeAttnArgs& a, dim3 grid, cudaStream_t st) {
   using TM = typename std::conditional<std::is_same<TC, __nv_fp8_e4m3>::value, __half, TC>::type;
-  auto kern = decode_attn_kernel<TC, TM, D, G>;
-  constexpr int smem = AttnRing<TM, D>::BYTES;
+  auto kern = decode_attn_kernel<TC, TM, D, G, RING>;
+  constexpr int smem = AttnRing<TM, D, RING>::BYTES;
   static const cudaError_t attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (attr != cudaSuccess) return attr;
   return launch_pdl(kern, grid, dim3(kAttnThreads), (size_t)smem, st, a);
+}
+
+// ring depth: 6 slots (default), or 12 with BARQ_ATTN_RING=12 (not yet measured on a GPU)
+static int attn_ring_depth() {
+  static const int depth = [] {
+    const char* e = getenv("BARQ_ATTN_RING");
+    return e && atoi(e) == kAttnRingDeep ? kAttnRingDeep : kAttnRing;
+  }();
+  return depth;
+}
+
+template <typename TC, int D, int G>
+static cudaError_t launch_attn(const DecodeAttnArgs& a, dim3 grid, cudaStream_t st) {
+  return attn_ring_depth() == kAttnRingDeep ? launch_attn_ring<TC, D, G, kAttnRingDeep>(a, grid, st)
+                                            : launch_attn_ring<TC, D, G, kAttnRing>(a, grid, st);
 }
 
 template <typename TC, int D>
