@@ -196,6 +196,52 @@ def test_sliding_window_page_freeing_matches_reference():
         assert _follows_reference(ref, p, r.tokens)
 
 
+@pytest.mark.parametrize("seed,prefix,window", [(0, False, 0), (1, True, 0), (2, False, 24), (3, True, 0)])
+def test_random_arrivals_aborts_and_preemption_follow_reference(seed, prefix, window):
+    """Randomized serving on a small pool: requests arrive between steps, some clients go away,
+    prompts share prefixes, the pool forces preemption (and window release).  Every request that
+    finishes by length must be the reference's greedy continuation; aborted ones free their pages."""
+    import random
+
+    rng = random.Random(seed)
+    cfg = dataclasses.replace(preset("tiny", n_layers=1, vocab=400, max_ctx=256), sliding_window=window)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=20 + seed)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=rng.choice([14, 20]), max_num_batched_tokens=rng.choice([16, 40]),
+                  max_num_seqs=rng.choice([3, 4]), prefix_caching=prefix)
+    shared = torch.randint(0, cfg.vocab, (32,), generator=torch.Generator().manual_seed(seed)).tolist()
+    pending = []
+    for i in range(10):
+        base = shared[: rng.choice([0, 16, 32])] if prefix else []
+        prompt = base + [rng.randrange(cfg.vocab) for _ in range(rng.randint(3, 40))]
+        pending.append((prompt, SamplingParams.greedy_params(max_tokens=rng.randint(4, 24))))
+    live, done, aborted = [], [], []
+    steps = 0
+    while pending or eng.has_work():
+        if pending and (rng.random() < 0.5 or not eng.has_work()):
+            p, sp = pending.pop(0)
+            live.append(eng.add_request(p, sp))
+        if live and rng.random() < 0.06:
+            s = live.pop(rng.randrange(len(live)))
+            if eng.abort(s):
+                aborted.append(s)
+        for s in eng.step():
+            done.append(s)
+        steps += 1
+        assert steps < 5000
+    finished = [s for s in done if s.finish_reason == "length"]
+    assert finished
+    for s in finished:
+        assert len(s.output) == s.params.max_tokens and _follows_reference(ref, s.prompt, s.output)
+    assert all(not s.block_table for s in aborted + done)
+    held = eng.prefix_cache.n_blocks if eng.prefix_cache is not None else 0
+    assert eng.blocks.n_used == 1 + held  # the dummy page plus what the prefix cache keeps
+    if prefix:  # these workloads overfill the pool
+        assert eng.sched.n_preemptions > 0 and eng.prefix_cache.hits > 0
+    if window:
+        assert eng.sched.n_window_freed > 0
+
+
 def test_kv_session_export_import_through_the_engine(tmp_path):
     from barq_inference_b200.engine.session import export_session, import_session
 
