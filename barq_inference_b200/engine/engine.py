@@ -40,7 +40,7 @@ class EngineConfig:
     kv_cache_gb: float = 8.0
     kv_dtype: str = "fp16"          # fp16 | bf16 | fp8 (e4m3 with one f32 scale per stored row)
     cuda_graphs: bool = True
-    graph_buckets: tuple[int, ...] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
+    graph_buckets: tuple[int, ...] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
     prefix_caching: bool = False
     chunked_prefill: bool = True
     device: str = "cuda"

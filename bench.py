@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--bs1-steps", type=int, default=DECODE_TOKENS)
     ap.add_argument("--e2e-tokens", type=int, default=32)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
+    ap.add_argument("--batch-per-gpu", action="store_true",
+                    help="with --parallel tp: --batch requests per GPU (global batch = batch x N, weak scaling); "
+                         "default: --batch is the global batch (strong scaling)")
     ap.add_argument("--parallel", default="tp", choices=["dp", "tp"],
                     help="tp: one tensor-parallel engine over all GPUs (strong scaling, default); dp: one engine "
                          "replica per GPU (weak scaling)")
@@ -146,12 +149,13 @@ def main():
         cfg.n_layers = args.layers
     t_init = time.time()
     tensors = random_tensors(cfg, POLICIES[args.model], seed=0, device=dev)
-    B, P = args.batch, args.prompt_len
+    tp = world if args.parallel == "tp" else 1
+    weak_tp = tp > 1 and args.batch_per_gpu
+    B, P = args.batch * (world if weak_tp else 1), args.prompt_len
     max_len = P + args.warmup + args.steps + args.e2e_tokens + 64
     max_len = max(max_len, args.ttft_prompt + args.bs1_steps + 16)
     max_len = (max_len + 15) // 16 * 16
     blocks_needed = B * (max_len // 16 + 2) + 64
-    tp = world if args.parallel == "tp" else 1
     ec = EngineConfig(max_num_seqs=max(B, 1), max_num_batched_tokens=8192, max_model_len=max_len,
                       num_blocks=blocks_needed, cuda_graphs=True, tp=tp, fused_comm=args.comm == "fused",
                       ser_threshold=args.ser, fused_moe=not args.no_fmoe)
@@ -299,13 +303,14 @@ def main():
             "metric": METRIC,
             "value": round(value, 2),
             "unit": ("tokens/s (decode, batch %d per GPU, aggregate)" % B) if tp == 1 else
-                    ("tokens/s (decode, batch %d, tensor parallel over %d GPUs)" % (B, world)),
+                    ("tokens/s (decode, batch %d%s, tensor parallel over %d GPUs)"
+                     % (B, " = %d per GPU" % args.batch if weak_tp else "", world)),
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(dec_ms / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak" if tp == 1 else "strong",
+            "scaling": "weak" if tp == 1 or weak_tp else "strong",
             "vs_baseline": None,
             "dtype": "Q4_K/Q6_K weights dequantized in-kernel; decode GEMV activations two-term int8 (~15-bit: "
                      "x = d*q + dl*ql), prefill / batched GEMM activations bf16 on tcgen05; fp32 accumulation and "
