@@ -115,6 +115,8 @@ class Scheduler:
         self._free(seq)
         if seq in self.running:
             self.running.remove(seq)
+        elif seq in self.waiting:
+            self.waiting.remove(seq)
 
     def abort(self, seq: Sequence) -> bool:
         """Drop a request whose client went away: a waiting one leaves the queue, a running one

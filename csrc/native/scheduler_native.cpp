@@ -96,6 +96,8 @@ class Scheduler {
       cache_->insert(std::vector<int>(s.tokens.begin(), s.tokens.begin() + s.n_cached), s.table);
     free_seq(s);
     erase(running_, id);
+    auto w = std::find(waiting_.begin(), waiting_.end(), id);
+    if (w != waiting_.end()) waiting_.erase(w);
     dirty_.insert(id);
   }
 

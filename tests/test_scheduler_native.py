@@ -160,3 +160,17 @@ def test_prefill_phase_never_preempts_a_sequence_already_in_the_plan(native):
     assert st.kind == "prefill" and st.seqs == [young] and st.n_new == [3]
     assert young.status is SeqStatus.RUNNING and len(young.block_table) == 1
     assert old.status is SeqStatus.RUNNING and s.n_preemptions == 0
+
+
+@pytest.mark.parametrize("native", [False, True])
+def test_finishing_a_waiting_sequence_removes_it_from_the_queue(native):
+    bm = NativeBlockManager(8) if native else BlockManager(8)
+    s = (NativeScheduler if native else Scheduler)(SchedulerConfig(max_num_seqs=1, max_num_batched_tokens=64), bm)
+    a, b = Sequence([1, 2, 3], SamplingParams()), Sequence([4, 5], SamplingParams())
+    s.add(a)
+    s.add(b)
+    assert s.schedule().seqs == [a]  # b waits: one sequence at a time
+    s.finish(b, "error")
+    assert b.status is SeqStatus.FINISHED and b not in s.waiting and len(s.waiting) == 0
+    s.finish(a, "length")
+    assert not s.has_work and bm.n_used == 0
