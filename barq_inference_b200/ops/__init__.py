@@ -275,12 +275,20 @@ def _attn_counters(device, n: int):
 
 
 def prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, max_q, H, Hkv, D, scale, window=0,
-                      act_dtype=torch.bfloat16, kv_scales=None):
+                      act_dtype=torch.bfloat16, kv_scales=None, impl: int | None = None):
+    """K9 causal varlen prefill attention over the paged cache: returns [T, H * D] in ``act_dtype``.
+
+    ``impl`` 0 runs the mma.sync kernel (``attn_prefill.cu``), 1 the tcgen05 / TMEM / TMA kernel
+    (``attn_prefill_tc.cu``; fp16 / bf16 caches with D = 64 or 128, other cases fall back to 0);
+    by default ``BARQ_PREFILL_TC`` picks (unset: 0)."""
+    if impl is None:
+        impl = int(os.environ.get("BARQ_PREFILL_TC", "0"))
     T = q.shape[0]
     S = block_tables.shape[0]
     out = torch.empty(T, H * D, dtype=act_dtype, device=q.device)
     require_ext().prefill_attention(q, kcache, vcache, block_tables, q_start, ctx_lens, S, max_q, H, Hkv, D,
-                                    scale, window, out, *(kv_scales if kv_scales is not None else (None, None)))
+                                    scale, window, out, *(kv_scales if kv_scales is not None else (None, None)),
+                                    int(impl))
     _count()
     return out
 

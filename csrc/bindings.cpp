@@ -510,7 +510,7 @@ void decode_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_table
 
 void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tables, Tensor q_start, Tensor ctx_lens,
                        int64_t S, int64_t max_q, int64_t H, int64_t Hkv, int64_t D, double scale, int64_t window,
-                       Tensor out, OptT kscale, OptT vscale) {
+                       Tensor out, OptT kscale, OptT vscale, int64_t impl) {
   c10::cuda::CUDAGuard g(q.device());
   barq::PrefillAttnArgs a;
   a.q = ptr<const __nv_bfloat16>(q);
@@ -529,6 +529,11 @@ void prefill_attention(Tensor q, Tensor kcache, Tensor vcache, Tensor block_tabl
   a.out_f16 = out.scalar_type() == torch::kHalf;
   a.kscale = optptr<const float>(kscale);
   a.vscale = optptr<const float>(vscale);
+  if (impl == 1)
+    TORCH_CHECK(kcache.is_contiguous() && vcache.is_contiguous() && kcache.sizes() == vcache.sizes(),
+                "prefill_attention: the tcgen05 path reads K / V as contiguous [blocks, Hkv, 16, D] caches");
+  a.cache_rows = (long)(kcache.numel() / D);
+  a.impl = (int)impl;
   check(barq::prefill_attention(a, cur_stream()), "prefill_attention");
 }
 

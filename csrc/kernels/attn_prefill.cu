@@ -257,6 +257,10 @@ static int launch_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st) {
   if (a.block_size != 16) return -1;
   if (a.S <= 0 || a.max_q <= 0) return 0;
+  if (a.impl == 1) {
+    const int rc = prefill_attention_tc(a, st);
+    if (rc != -2) return rc;
+  }
   if (a.D == 128)
     return a.cache_type == kCacheBF16  ? launch_prefill<__nv_bfloat16, __nv_bfloat16, 128>(a, st)
            : a.cache_type == kCacheFP8 ? launch_prefill<__nv_fp8_e4m3, __half, 128>(a, st)

@@ -330,8 +330,13 @@ struct PrefillAttnArgs {
   int out_f16;
   const float* kscale = nullptr;  // fp8 cache: per-row scales (RopeKVArgs), null = unscaled
   const float* vscale = nullptr;
+  long cache_rows = 0;            // rows of the cache viewed as [blocks * Hkv * block_size, D] (tcgen05 path)
+  int impl = 0;                   // 0: mma.sync kernel; 1: tcgen05 kernel where it has an instantiation
 };
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st);
+// The tcgen05 / TMEM / TMA kernel (attn_prefill_tc.cu): -2 when the cache type or D has no
+// instantiation (fp8 caches, D other than 64 / 128).
+int prefill_attention_tc(const PrefillAttnArgs& a, cudaStream_t st);
 
 // Token embedding rows gathered from a quantized [V, H] table (planar layout) into f32 [T, H].
 int embed_gather(const QW& table, const int* ids, int T, float* out, cudaStream_t st);

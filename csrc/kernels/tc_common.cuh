@@ -172,6 +172,23 @@ BARQ_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// UMMA shared-memory descriptor, MN-major operand in the 128-byte swizzle canonical layout: along
+// MN, 64 consecutive 16-bit elements fill one 128-byte row; rows are consecutive K indices, 8-row
+// groups 1024 B apart (SBO); the next 64 MN elements start `lbo` bytes further (LBO).  This is
+// the layout a 2D TMA box {64, rows} with SWIZZLE_128B writes when its inner dimension is MN
+// (e.g. V tiles [keys][D] used as the B operand of P V).  Tile base must be 1024-byte aligned.
+BARQ_DEV uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);       // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;   // LBO: stride between 64-element MN blocks
+  d |= (uint64_t)(1024 >> 4) << 32;              // SBO: stride between 8-row K groups
+  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
+  return d;
+}
+// Instruction-descriptor bit selecting an MN-major B operand (bit 16; 0 = K-major).
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
+
 // Instruction descriptor for kind::f16 with bf16 A/B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4)            // D format f32
