@@ -397,14 +397,14 @@ def cmd_server(args) -> int:
 
     path = args.socket or f"/tmp/barq-inference-{args.port}.sock"
     if int(getattr(args, "dp", 1) or 1) > 1:
-        front, tok, _ = _dp_front(args)
-        srv = UDSServer(front, tok, path)
+        front, tok, tmpl = _dp_front(args)
+        srv = UDSServer(front, tok, path, chat_template=tmpl)
     else:
-        eng, tok, _, _ = load(args)
+        eng, tok, tmpl, _ = load(args)
         eng = _lockstep(eng, args)
         if eng is None:  # a follower rank: rank 0 has stopped serving
             return 0
-        srv = UDSServer(AsyncEngine(eng), tok, path)
+        srv = UDSServer(AsyncEngine(eng), tok, path, chat_template=tmpl)
     if getattr(args, "metrics_port", 0):
         from .server.metrics import InferenceMetrics
         from .server.metrics_server import MetricsServer, MetricsServerConfig
@@ -418,11 +418,36 @@ def cmd_server(args) -> int:
     return 0
 
 
+def _serve_native_front_end(aengine, tok, tmpl, args) -> int:
+    """HTTP served by the C++ front end ``barq-http``: the engine answers on a private UDS socket."""
+    import subprocess
+    import tempfile
+
+    from .server.uds import UDSServer
+    from .server.uds_native import build_http
+
+    exe = build_http()
+    sock = os.path.join(tempfile.mkdtemp(prefix="barq-"), "engine.sock")
+    srv = UDSServer(aengine, tok, sock, chat_template=tmpl).start()
+    cmd = [exe, "--socket", sock, "--host", args.host, "--port", str(args.port),
+           "--model-id", os.path.basename(args.model), "--rpm", str(max(0, args.rate_limit_rpm))]
+    try:
+        return subprocess.call(cmd)
+    except KeyboardInterrupt:
+        return 0
+    finally:
+        srv.stop()
+
+
 def cmd_http_server(args) -> int:
+    from .server.async_engine import AsyncEngine
     from .server.openai_api import OpenAIServer, serve
 
+    native = bool(getattr(args, "native_front_end", False))
     if int(getattr(args, "dp", 1) or 1) > 1:
         front, tok, tmpl = _dp_front(args)
+        if native:
+            return _serve_native_front_end(front, tok, tmpl, args)
         srv = OpenAIServer(front, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
                            rate_limit_rpm=args.rate_limit_rpm, arch=front.cfg.arch, aengine=front)
     else:
@@ -430,6 +455,8 @@ def cmd_http_server(args) -> int:
         eng = _lockstep(eng, args)
         if eng is None:  # a follower rank: rank 0 has stopped serving
             return 0
+        if native:
+            return _serve_native_front_end(AsyncEngine(eng), tok, tmpl, args)
         srv = OpenAIServer(eng, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
                            rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch)
     serve(srv, args.host, args.port)
@@ -574,6 +601,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--host", default="0.0.0.0")
     p.add_argument("--port", type=int, default=8000)
     p.add_argument("--rate-limit-rpm", type=int, default=60)
+    p.add_argument("--native-front-end", action="store_true",
+                   help="serve HTTP from the C++ front end barq-http (engine behind a private UDS socket); "
+                        "tools and embeddings stay on the default Python server")
     p.set_defaults(fn=cmd_http_server)
 
     sub.add_parser("metal-info").set_defaults(fn=cmd_metal_info)

@@ -429,11 +429,17 @@ class DataParallelEngine:
     def generate_blocking(self, prompt: list[int], params: SamplingParams, request_id: str = "", timeout=None):
         """Iterator of StreamItem for synchronous callers (UDS server, CLI)."""
         req = self._submit(prompt, params, request_id, sink=queue.Queue())
-        while True:
-            item = self._check(req.sink.get(timeout=timeout))
-            yield item
-            if item.token is None:
-                return
+        done = False
+        try:
+            while True:
+                item = req.sink.get(timeout=timeout)
+                done = item.token is None
+                yield self._check(item)
+                if done:
+                    return
+        finally:
+            if not done:  # the caller closed the iterator early: the replica stops generating for it
+                self.cancel(req.rid)
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | None = None) -> list[list[int]]:
         """Runs every prompt to completion across the replicas; returns the token lists in order."""

@@ -185,10 +185,17 @@ class AsyncEngine:
         """Iterator of StreamItem for synchronous callers (UDS server, CLI)."""
         sub = Submission(prompt, params, request_id, sink=queue.Queue())
         self.inbox.put(sub)
-        while True:
-            item = sub.sink.get(timeout=timeout)
-            if item.token is None and item.finish_reason == "error" and sub.error:
-                raise _refusal(sub.error[0])
-            yield item
-            if item.token is None:
-                return
+        done = False
+        try:
+            while True:
+                item = sub.sink.get(timeout=timeout)
+                if item.token is None and item.finish_reason == "error" and sub.error:
+                    done = True
+                    raise _refusal(sub.error[0])
+                yield item
+                if item.token is None:
+                    done = True
+                    return
+        finally:
+            if not done:  # the caller stopped early (closed the iterator): stop generating for it
+                self._abort(sub)

@@ -8,6 +8,12 @@ token, the last with ``done: true``.  Requests from all connections share the co
 engine (what the reference's unreachable ``cmd_server_batch`` intended, ``cli/src/main.rs:1045-1158``).
 Sampling uses top-k 40 / top-p 0.95 like the reference's handler.  Errors are reported as a final
 frame with ``done: true`` and an ``error`` field.
+
+Additive fields (a client of the reference's protocol neither sends nor needs them): a request may
+carry ``messages`` (OpenAI chat turns, rendered with the server's chat template) instead of
+``prompt``, and the OpenAI sampling fields (``top_k``, ``top_p``, ``min_p``, ``seed``, penalties,
+``response_format``, ``grammar``); the final frame adds ``prompt_tokens`` and ``finish_reason``.
+A client that disconnects mid-stream has its request aborted in the engine.
 """
 from __future__ import annotations
 
@@ -19,8 +25,8 @@ import struct
 import threading
 import time
 
-from ..engine.sampling_params import SamplingParams
-from ..tokenizer import StreamDecoder
+from ..tokenizer import ChatTemplate, StreamDecoder
+from .request_params import sampling_params_from_request
 
 MAX_FRAME = 16 << 20
 
@@ -55,22 +61,35 @@ def recv_frame(sock: socket.socket) -> dict | None:
 
 class UDSServer:
     def __init__(self, aengine, tokenizer, socket_path: str = "/tmp/barq-inference.sock", queue_size: int = 100,
-                 metrics=None):
+                 metrics=None, chat_template: ChatTemplate | None = None):
         self.ae = aengine
         self.metrics = metrics  # InferenceMetrics: per-request counters / TTFT for the metrics server
         self.tok = tokenizer
+        self.template = chat_template or ChatTemplate("generic")
         self.path = socket_path
         self.sem = threading.BoundedSemaphore(queue_size)
         self._server = None
+
+    def _prompt_ids(self, req: dict) -> list[int]:
+        msgs = req.get("messages")
+        if msgs is not None:
+            if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and "content" in m for m in msgs):
+                raise ValueError("messages must be a non-empty list of {role, content}")
+            text = self.template.render([dict(m, content=m.get("content") or "") for m in msgs],
+                                        add_generation_prompt=True)
+            bos = getattr(self.template, "bos_token", "") or "\0"
+            return self.tok.encode(text, add_special=not text.startswith(bos))
+        prompt = req["prompt"]
+        if isinstance(prompt, list):
+            return [int(t) for t in prompt]
+        return self.tok.encode(str(prompt))
 
     def handle_request(self, conn: socket.socket, req: dict) -> None:
         t0 = time.perf_counter()
         rid = str(req.get("id", ""))
         try:
-            prompt = req["prompt"]
-            ids = prompt if isinstance(prompt, list) else self.tok.encode(str(prompt))
-            params = SamplingParams(max_tokens=int(req.get("max_tokens", 128)),
-                                    temperature=float(req.get("temperature", 0.8)), top_k=40, top_p=0.95)
+            ids = self._prompt_ids(req)
+            params = sampling_params_from_request(req)
         except Exception as e:  # noqa: BLE001 - any failure ends the stream with an error frame
             send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
                               "done": True, "error": f"bad request: {e}"})
@@ -78,15 +97,17 @@ class UDSServer:
         dec = StreamDecoder(self.tok)
         n, ttft = 0, None
         guard = self.metrics.begin() if self.metrics is not None else None
+        gen = self.ae.generate_blocking(ids, params, rid)
         try:
-            for item in self.ae.generate_blocking(ids, params, rid):
+            for item in gen:
                 now = time.perf_counter()
                 if item.token is None:
                     if guard is not None:
                         guard.complete(len(ids), n)
                         guard = None
                     send_frame(conn, {"id": rid, "text": dec.flush(), "tokens_generated": n,
-                                      "ttft_ms": int(ttft or 0), "total_time_ms": int((now - t0) * 1e3), "done": True})
+                                      "ttft_ms": int(ttft or 0), "total_time_ms": int((now - t0) * 1e3), "done": True,
+                                      "prompt_tokens": len(ids), "finish_reason": item.finish_reason or "stop"})
                     return
                 n += 1
                 if ttft is None:
@@ -95,12 +116,18 @@ class UDSServer:
                         guard.first_token()
                 send_frame(conn, {"id": rid, "text": dec.push(item.token), "tokens_generated": n,
                                   "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
+        except OSError:  # the client went away mid-stream: closing the iterator aborts the request
+            gen.close()
         except Exception as e:  # noqa: BLE001 - a failed request still gets its final frame
             if guard is not None:
                 guard.fail()
                 guard = None
-            send_frame(conn, {"id": rid, "text": "", "tokens_generated": n, "ttft_ms": 0,
-                              "total_time_ms": int((time.perf_counter() - t0) * 1e3), "done": True, "error": str(e)})
+            try:
+                send_frame(conn, {"id": rid, "text": "", "tokens_generated": n, "ttft_ms": 0,
+                                  "total_time_ms": int((time.perf_counter() - t0) * 1e3), "done": True,
+                                  "error": str(e)})
+            except OSError:
+                pass
         finally:
             if guard is not None:  # client went away mid-stream
                 guard.fail()

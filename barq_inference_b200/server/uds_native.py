@@ -1,8 +1,12 @@
-"""Build and locate ``barq-uds``, the native client of the UDS server (``csrc/client/barq_uds.cpp``).
+"""Build and locate the native front-end tools of the UDS server:
 
-The binary is compiled in-tree next to this package (``barq_inference_b200/bin/barq-uds``) so that
-it travels with the checkout; ``build_client()`` is called by the package build entry point and by
-the tests when the binary is missing or older than its source.
+* ``barq-uds`` (``csrc/client/barq_uds.cpp``): command-line client;
+* ``barq-http`` (``csrc/client/barq_http.cpp``): OpenAI-compatible HTTP front end that forwards
+  every generation to the UDS server.
+
+The binaries are compiled in-tree next to this package (``barq_inference_b200/bin/``) so that they
+travel with the checkout; the package build entry point and the tests call ``build_client()`` /
+``build_http()``, which rebuild a binary when it is missing or older than its sources.
 """
 from __future__ import annotations
 
@@ -13,6 +17,8 @@ import subprocess
 PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SOURCE = os.path.join(os.path.dirname(PKG), "csrc", "client", "barq_uds.cpp")
 BINARY = os.path.join(PKG, "bin", "barq-uds")
+HTTP_SOURCES = [os.path.join(os.path.dirname(PKG), "csrc", "client", f) for f in ("barq_http.cpp", "json_lite.h")]
+HTTP_BINARY = os.path.join(PKG, "bin", "barq-http")
 
 
 def client_path() -> str:
@@ -31,3 +37,22 @@ def build_client(force: bool = False) -> str:
     os.makedirs(os.path.dirname(BINARY), exist_ok=True)
     subprocess.run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-o", BINARY, SOURCE], check=True)
     return BINARY
+
+
+def http_path() -> str:
+    return HTTP_BINARY
+
+
+def build_http(force: bool = False) -> str:
+    """Compile ``barq-http`` if it is missing or older than its sources; returns its path."""
+    fresh = os.path.exists(HTTP_BINARY) and all(
+        os.path.exists(src) and os.path.getmtime(HTTP_BINARY) >= os.path.getmtime(src) for src in HTTP_SOURCES)
+    if fresh and not force:
+        return HTTP_BINARY
+    cxx = os.environ.get("CXX") or shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("no C++ compiler found to build barq-http")
+    os.makedirs(os.path.dirname(HTTP_BINARY), exist_ok=True)
+    subprocess.run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-pthread", "-o", HTTP_BINARY,
+                    HTTP_SOURCES[0]], check=True)
+    return HTTP_BINARY

@@ -1,0 +1,968 @@
+// barq-http: native OpenAI-compatible HTTP front end for the barq engine.
+//
+// Parity: the reference's front end serves the OpenAI routes from its CLI binary
+// (cli/src/server.rs:297-370: GET /, GET /v1/models, POST /v1/completions, /v1/chat/completions,
+// /v1/responses, OPTIONS for CORS, per-IP rate limiting with 429, SSE streaming) and talks to the
+// inference side over a local socket (advanced/src/uds_server.rs).  This binary is that front end
+// in C++: it owns the HTTP side (parsing, keep-alive, CORS, rate limiting, SSE framing, stop
+// strings, request ids, Prometheus counters) and forwards every generation to the engine's UDS
+// server (`barq server --socket PATH`), one socket connection per request.  Tokenization, chat
+// templates and sampling stay in the engine process.
+//
+//   barq-http --socket PATH [--host 0.0.0.0] [--port 8080] [--model-id NAME] [--rpm N]
+//             [--max-conns N] [--engine-timeout S] [--quiet]
+//
+// Routes:
+//   GET  /                       server info
+//   GET  /v1/models              the served model id
+//   GET  /health                 200 when the engine socket accepts connections, else 503
+//   GET  /metrics                Prometheus text: this front end's request / token / latency counters
+//   POST /v1/completions         prompt (string or token ids)
+//   POST /v1/chat/completions    messages (rendered by the engine's chat template)
+//   POST /v1/responses           input (string or messages) / prompt / messages, max_output_tokens
+//   OPTIONS *                    204 with CORS headers
+// Request fields forwarded to the engine: max_tokens, temperature, top_k, top_p, min_p, seed,
+// repetition / frequency / presence penalties, response_format, grammar.  Handled here: stream,
+// stream_options.include_usage, stop (string or list; text is held back while it could still be
+// the start of a stop string, so no stop text is ever sent), n (1..16, not with stream).
+// Errors: 400 invalid request, 404 unknown route, 405 wrong method, 413 / 431 oversized, 429 rate
+// limited, 502 engine unreachable, 503 engine queue full or connection limit, 500 engine failure;
+// the body is {"error": {"message", "type"}} as in the Python server.
+#include <arpa/inet.h>
+#include <netinet/in.h>
+#include <netinet/tcp.h>
+#include <poll.h>
+#include <signal.h>
+#include <sys/socket.h>
+#include <sys/time.h>
+#include <sys/un.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cctype>
+#include <cerrno>
+#include <cmath>
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <ctime>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "json_lite.h"
+
+namespace {
+
+using barqjson::Value;
+
+constexpr size_t kMaxHeaderBytes = 32 << 10;
+constexpr size_t kMaxBodyBytes = 8 << 20;
+constexpr uint32_t kMaxFrame = 16u << 20;
+
+struct Options {
+  std::string host = "0.0.0.0";
+  int port = 8080;
+  std::string socket_path = "/tmp/barq-inference.sock";
+  std::string model_id = "barq";
+  int rpm = 0;          // requests per minute per client address (0: no limit)
+  int max_conns = 256;  // concurrent connections
+  int engine_timeout_s = 600;
+  bool quiet = false;
+};
+Options g_opt;
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// ---------------------------------------------------------------- counters (Prometheus text)
+struct Counters {
+  std::atomic<uint64_t> requests{0}, ok{0}, client_errors{0}, server_errors{0}, rate_limited{0};
+  std::atomic<uint64_t> prompt_tokens{0}, completion_tokens{0};
+  std::atomic<uint64_t> ttft_us{0}, ttft_n{0}, latency_us{0}, latency_n{0};
+  std::atomic<int64_t> active{0}, peak_active{0}, connections{0};
+
+  void begin() {
+    const int64_t a = ++active;
+    int64_t p = peak_active.load();
+    while (a > p && !peak_active.compare_exchange_weak(p, a)) {
+    }
+  }
+  std::string prometheus() const {
+    std::string s;
+    auto line = [&](const char* name, const char* type, const char* help, double v) {
+      char buf[64];
+      std::snprintf(buf, sizeof buf, "%.17g", v);
+      s += std::string("# HELP ") + name + " " + help + "\n# TYPE " + name + " " + type + "\n" + name + " " + buf + "\n";
+    };
+    line("barq_http_requests_total", "counter", "Generation requests received.", (double)requests);
+    line("barq_http_requests_ok_total", "counter", "Generation requests answered with 200.", (double)ok);
+    line("barq_http_client_errors_total", "counter", "Requests answered with a 4xx status.", (double)client_errors);
+    line("barq_http_server_errors_total", "counter", "Requests answered with a 5xx status.", (double)server_errors);
+    line("barq_http_rate_limited_total", "counter", "Requests refused by the rate limiter.", (double)rate_limited);
+    line("barq_http_prompt_tokens_total", "counter", "Prompt tokens of completed requests.", (double)prompt_tokens);
+    line("barq_http_completion_tokens_total", "counter", "Generated tokens of completed requests.",
+         (double)completion_tokens);
+    line("barq_http_ttft_seconds_sum", "counter", "Sum of time to first token.", (double)ttft_us * 1e-6);
+    line("barq_http_ttft_seconds_count", "counter", "Requests with a first token.", (double)ttft_n);
+    line("barq_http_request_seconds_sum", "counter", "Sum of generation request latency.", (double)latency_us * 1e-6);
+    line("barq_http_request_seconds_count", "counter", "Finished generation requests.", (double)latency_n);
+    line("barq_http_active_requests", "gauge", "Generation requests in flight.", (double)active);
+    line("barq_http_peak_active_requests", "gauge", "Most generation requests in flight at once.", (double)peak_active);
+    line("barq_http_open_connections", "gauge", "Open client connections.", (double)connections);
+    return s;
+  }
+};
+Counters g_ctr;
+
+// ---------------------------------------------------------------- per-client token bucket
+class RateLimiter {
+ public:
+  bool allow(const std::string& key) {
+    if (g_opt.rpm <= 0) return true;
+    const double cap = g_opt.rpm, refill = cap / 60.0, t = now_s();
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = state_.find(key);
+    if (it == state_.end()) it = state_.emplace(key, std::make_pair(cap, t)).first;
+    double& tokens = it->second.first;
+    tokens = std::min(cap, tokens + (t - it->second.second) * refill);
+    it->second.second = t;
+    if (tokens < 1.0) return false;
+    tokens -= 1.0;
+    return true;
+  }
+
+ private:
+  std::mutex mu_;
+  std::unordered_map<std::string, std::pair<double, double>> state_;
+};
+RateLimiter g_limiter;
+
+// ---------------------------------------------------------------- sockets
+bool send_all(int fd, const std::string& data) {
+  size_t off = 0;
+  while (off < data.size()) {
+    const ssize_t n = ::send(fd, data.data() + off, data.size() - off, MSG_NOSIGNAL);
+    if (n < 0 && errno == EINTR) continue;
+    if (n <= 0) return false;
+    off += (size_t)n;
+  }
+  return true;
+}
+
+bool recv_exact(int fd, void* dst, size_t n) {
+  char* p = static_cast<char*>(dst);
+  while (n) {
+    const ssize_t r = ::recv(fd, p, n, 0);
+    if (r < 0 && errno == EINTR) continue;
+    if (r <= 0) return false;
+    p += r;
+    n -= (size_t)r;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- HTTP
+struct Request {
+  std::string method, target, path, version;
+  std::vector<std::pair<std::string, std::string>> headers;  // names lower-cased
+  std::string body;
+  std::string header(const std::string& name) const {
+    for (const auto& h : headers)
+      if (h.first == name) return h.second;
+    return "";
+  }
+};
+
+std::string lower(std::string s) {
+  for (auto& c : s) c = (char)std::tolower((unsigned char)c);
+  return s;
+}
+std::string trim(const std::string& s) {
+  size_t b = 0, e = s.size();
+  while (b < e && (s[b] == ' ' || s[b] == '\t')) ++b;
+  while (e > b && (s[e - 1] == ' ' || s[e - 1] == '\t' || s[e - 1] == '\r')) --e;
+  return s.substr(b, e - b);
+}
+
+const char* reason_phrase(int status) {
+  switch (status) {
+    case 200: return "OK";
+    case 204: return "No Content";
+    case 400: return "Bad Request";
+    case 404: return "Not Found";
+    case 405: return "Method Not Allowed";
+    case 408: return "Request Timeout";
+    case 411: return "Length Required";
+    case 413: return "Payload Too Large";
+    case 429: return "Too Many Requests";
+    case 431: return "Request Header Fields Too Large";
+    case 500: return "Internal Server Error";
+    case 501: return "Not Implemented";
+    case 502: return "Bad Gateway";
+    case 503: return "Service Unavailable";
+  }
+  return "Unknown";
+}
+
+const char* kCors =
+    "Access-Control-Allow-Origin: *\r\nAccess-Control-Allow-Methods: GET, POST, OPTIONS\r\n"
+    "Access-Control-Allow-Headers: *\r\n";
+
+// Buffered reader of one client connection.  read() returns 0 for a complete request, -1 when the
+// peer closed (or went idle) between requests, or an HTTP status for a malformed request.
+class Conn {
+ public:
+  explicit Conn(int fd) : fd_(fd) {}
+
+  int read(Request& req) {
+    size_t end;
+    while ((end = buf_.find("\r\n\r\n")) == std::string::npos) {
+      if (buf_.size() > kMaxHeaderBytes) return 431;
+      if (!fill()) return buf_.empty() ? -1 : 400;
+    }
+    if (end > kMaxHeaderBytes) return 431;
+    const std::string head = buf_.substr(0, end);
+    buf_.erase(0, end + 4);
+    size_t line_end = head.find("\r\n");
+    const std::string first = head.substr(0, line_end);
+    const size_t sp1 = first.find(' '), sp2 = first.rfind(' ');
+    if (sp1 == std::string::npos || sp2 == sp1) return 400;
+    req.method = first.substr(0, sp1);
+    req.target = first.substr(sp1 + 1, sp2 - sp1 - 1);
+    req.version = first.substr(sp2 + 1);
+    if (req.version.rfind("HTTP/1.", 0) != 0 || req.target.empty()) return 400;
+    req.path = req.target.substr(0, req.target.find('?'));
+    req.headers.clear();
+    while (line_end != std::string::npos) {
+      const size_t b = line_end + 2;
+      line_end = head.find("\r\n", b);
+      const std::string line = head.substr(b, line_end == std::string::npos ? std::string::npos : line_end - b);
+      const size_t colon = line.find(':');
+      if (colon == std::string::npos || colon == 0) return 400;
+      req.headers.emplace_back(lower(line.substr(0, colon)), trim(line.substr(colon + 1)));
+    }
+    if (!req.header("transfer-encoding").empty()) return 501;  // chunked request bodies: not accepted
+    const std::string cl = req.header("content-length");
+    size_t n = 0;
+    if (!cl.empty()) {
+      char* endp = nullptr;
+      errno = 0;
+      const unsigned long long v = std::strtoull(cl.c_str(), &endp, 10);
+      if (errno || endp == cl.c_str() || *endp != '\0' || cl[0] == '-') return 400;
+      if (v > kMaxBodyBytes) return 413;
+      n = (size_t)v;
+    } else if (req.method == "POST") {
+      return 411;
+    }
+    while (buf_.size() < n)
+      if (!fill()) return 400;
+    req.body = buf_.substr(0, n);
+    buf_.erase(0, n);
+    return 0;
+  }
+
+ private:
+  bool fill() {
+    char tmp[16384];
+    for (;;) {
+      const ssize_t r = ::recv(fd_, tmp, sizeof tmp, 0);
+      if (r < 0 && errno == EINTR) continue;
+      if (r <= 0) return false;
+      buf_.append(tmp, (size_t)r);
+      return true;
+    }
+  }
+  int fd_;
+  std::string buf_;
+};
+
+bool respond(int fd, int status, const std::string& ctype, const std::string& body, bool keep_alive,
+             const std::string& rid) {
+  std::string h = "HTTP/1.1 " + std::to_string(status) + " " + reason_phrase(status) + "\r\n";
+  if (!ctype.empty()) h += "Content-Type: " + ctype + "\r\n";
+  h += "Content-Length: " + std::to_string(body.size()) + "\r\n";
+  h += kCors;
+  if (!rid.empty()) h += "x-request-id: " + rid + "\r\n";
+  h += keep_alive ? "Connection: keep-alive\r\n\r\n" : "Connection: close\r\n\r\n";
+  return send_all(fd, h + body);
+}
+
+std::string error_body(const std::string& msg, const std::string& kind) {
+  Value e = Value::object(), err = Value::object();
+  err.set("message", Value::string(msg));
+  err.set("type", Value::string(kind));
+  e.set("error", err);
+  return barqjson::dump(e);
+}
+
+const char* error_kind(int status) {
+  switch (status) {
+    case 404: return "not_found_error";
+    case 429: return "rate_limit_error";
+    case 502: return "engine_unavailable_error";
+    case 503: return "overloaded_error";
+  }
+  return status >= 500 ? "server_error" : "invalid_request_error";
+}
+
+// ---------------------------------------------------------------- engine link (UDS frames)
+class EngineLink {
+ public:
+  ~EngineLink() { close(); }
+
+  bool open(std::string& err) {
+    fd_ = ::socket(AF_UNIX, SOCK_STREAM, 0);
+    if (fd_ < 0) {
+      err = std::strerror(errno);
+      return false;
+    }
+    sockaddr_un addr{};
+    addr.sun_family = AF_UNIX;
+    if (g_opt.socket_path.size() >= sizeof(addr.sun_path)) {
+      err = "socket path too long";
+      return false;
+    }
+    std::memcpy(addr.sun_path, g_opt.socket_path.c_str(), g_opt.socket_path.size() + 1);
+    if (::connect(fd_, reinterpret_cast<sockaddr*>(&addr), sizeof(addr)) != 0) {
+      err = std::string("cannot connect to ") + g_opt.socket_path + ": " + std::strerror(errno);
+      return false;
+    }
+    timeval tv{};
+    tv.tv_sec = g_opt.engine_timeout_s;
+    setsockopt(fd_, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof tv);
+    return true;
+  }
+  bool send(const Value& frame) {
+    const std::string body = barqjson::dump(frame);
+    const uint32_t n = (uint32_t)body.size();
+    const unsigned char head[4] = {(unsigned char)(n >> 24), (unsigned char)(n >> 16), (unsigned char)(n >> 8),
+                                   (unsigned char)n};
+    return send_all(fd_, std::string(reinterpret_cast<const char*>(head), 4) + body);
+  }
+  // One frame, or false with `err` set (closed, timed out, oversized or not a JSON object).
+  bool next(Value& frame, std::string& err) {
+    unsigned char head[4];
+    if (!recv_exact(fd_, head, 4)) {
+      err = "engine closed the stream";
+      return false;
+    }
+    const uint32_t n = ((uint32_t)head[0] << 24) | ((uint32_t)head[1] << 16) | ((uint32_t)head[2] << 8) | head[3];
+    if (n > kMaxFrame) {
+      err = "engine frame too large";
+      return false;
+    }
+    std::string body(n, '\0');
+    if (n && !recv_exact(fd_, &body[0], n)) {
+      err = "engine closed the stream";
+      return false;
+    }
+    try {
+      frame = barqjson::parse(body);
+    } catch (const std::exception& e) {
+      err = std::string("bad engine frame: ") + e.what();
+      return false;
+    }
+    if (!frame.is_object()) {
+      err = "bad engine frame: not an object";
+      return false;
+    }
+    return true;
+  }
+  void close() {
+    if (fd_ >= 0) ::close(fd_);
+    fd_ = -1;
+  }
+
+ private:
+  int fd_ = -1;
+};
+
+bool engine_reachable() {
+  EngineLink l;
+  std::string err;
+  return l.open(err);
+}
+
+// ---------------------------------------------------------------- one generation
+struct Gen {
+  std::string text;
+  std::string finish = "stop";
+  long prompt_tokens = 0, completion_tokens = 0;
+  int status = 200;  // non-200: `error` says why
+  std::string error;
+};
+
+// Stop strings: returns the earliest match position in `text`, or npos.
+size_t find_stop(const std::string& text, const std::vector<std::string>& stops, size_t from) {
+  size_t best = std::string::npos;
+  for (const auto& s : stops) {
+    if (s.empty()) continue;
+    const size_t b = from > s.size() ? from - s.size() : 0;
+    const size_t p = text.find(s, b);
+    if (p != std::string::npos && p < best) best = p;
+  }
+  return best;
+}
+// Length of the longest suffix of `text` that is a proper prefix of some stop string.
+size_t held_suffix(const std::string& text, const std::vector<std::string>& stops) {
+  size_t hold = 0;
+  for (const auto& s : stops)
+    for (size_t k = std::min(s.size() - (s.empty() ? 0 : 1), text.size()); k > hold; --k)
+      if (text.compare(text.size() - k, k, s, 0, k) == 0) {
+        hold = k;
+        break;
+      }
+  return hold;
+}
+
+int engine_error_status(const std::string& msg) {
+  if (msg == "queue full" || msg.find("overloaded") != std::string::npos) return 503;
+  if (msg.rfind("bad request", 0) == 0 || msg.find("exceeds max_model_len") != std::string::npos) return 400;
+  return 500;
+}
+
+// Runs one request on the engine.  `on_first` is called once before the first delta (or not at all
+// when the engine refuses the request), `on_delta` with every piece of text that can no longer be
+// part of a stop string; either returning false (client gone) ends the generation early.
+Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const std::function<bool()>& on_first,
+             const std::function<bool(const std::string&)>& on_delta) {
+  Gen g;
+  EngineLink link;
+  std::string err;
+  const double t0 = now_s();
+  if (!link.open(err)) {
+    g.status = 502;
+    g.error = "engine unavailable: " + err;
+    return g;
+  }
+  if (!link.send(uds_req)) {
+    g.status = 502;
+    g.error = "engine unavailable: send failed";
+    return g;
+  }
+  size_t sent = 0;  // bytes of g.text already handed to on_delta
+  bool first = true;
+  for (;;) {
+    Value fr;
+    if (!link.next(fr, err)) {
+      g.status = 500;
+      g.error = err;
+      return g;
+    }
+    const Value* e = fr.get("error");
+    const Value* done = fr.get("done");
+    const bool is_done = done && done->type == Value::kBool && done->b;
+    if (e && e->is_string()) {
+      g.status = engine_error_status(e->str);
+      g.error = e->str;
+      return g;
+    }
+    const Value* t = fr.get("text");
+    const std::string piece = t && t->is_string() ? t->str : "";
+    if (const Value* n = fr.get("tokens_generated"); n && n->is_number()) g.completion_tokens = (long)n->num;
+    if (first && (!piece.empty() || is_done)) {
+      first = false;
+      if (!piece.empty() || g.completion_tokens > 0) {
+        g_ctr.ttft_us += (uint64_t)((now_s() - t0) * 1e6);
+        ++g_ctr.ttft_n;
+      }
+      if (!on_first()) return g;
+    }
+    const size_t before = g.text.size();
+    g.text += piece;
+    const size_t hit = stops.empty() ? std::string::npos : find_stop(g.text, stops, before);
+    if (hit != std::string::npos) {
+      g.text.resize(hit);
+      g.finish = "stop";
+      if (hit > sent && !on_delta(g.text.substr(sent))) return g;
+      return g;  // closing the link aborts the request in the engine
+    }
+    if (is_done) {
+      if (const Value* p = fr.get("prompt_tokens"); p && p->is_number()) g.prompt_tokens = (long)p->num;
+      if (const Value* f = fr.get("finish_reason"); f && f->is_string()) g.finish = f->str;
+      if (g.text.size() > sent && !on_delta(g.text.substr(sent))) return g;
+      return g;
+    }
+    const size_t safe = g.text.size() - (stops.empty() ? 0 : held_suffix(g.text, stops));
+    if (safe > sent) {
+      if (!on_delta(g.text.substr(sent, safe - sent))) return g;
+      sent = safe;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- request translation
+struct Call {
+  std::string kind;  // "text", "chat", "resp"
+  Value uds;         // the engine request
+  std::vector<std::string> stops;
+  bool stream = false, include_usage = false;
+  int n = 1;
+  std::string model;
+};
+
+[[noreturn]] void bad(const std::string& msg) { throw std::invalid_argument(msg); }
+
+Call translate(const std::string& kind, const Value& body, const std::string& rid) {
+  if (!body.is_object()) bad("request body must be a JSON object");
+  Call c;
+  c.kind = kind;
+  c.uds = Value::object();
+  c.uds.set("id", Value::string(rid));
+  const Value* model = body.get("model");
+  c.model = model && model->is_string() && !model->str.empty() ? model->str : g_opt.model_id;
+  auto messages = [&](const Value& m) {
+    if (!m.is_array() || m.arr.empty()) bad("messages must be a non-empty list");
+    for (const auto& x : m.arr)
+      if (!x.is_object() || !x.get("content")) bad("each message needs role and content");
+    c.uds.set("messages", m);
+  };
+  if (kind == "text") {
+    const Value* p = body.get("prompt");
+    bool ok = p && p->is_string();
+    if (p && p->is_array() && !p->arr.empty()) {
+      ok = true;
+      for (const auto& t : p->arr) ok = ok && t.is_integer();
+    }
+    if (!ok) bad("prompt must be a string or a list of token ids");
+    c.uds.set("prompt", *p);
+  } else if (kind == "chat") {
+    const Value* m = body.get("messages");
+    if (!m) bad("messages must be a non-empty list");
+    messages(*m);
+    if (const Value* t = body.get("tools"); t && t->is_array() && !t->arr.empty())
+      bad("tools are served by the Python HTTP front end (barq http-server)");
+  } else {
+    if (const Value* m = body.get("messages"); m && !m->is_null()) {
+      messages(*m);
+    } else {
+      const Value* in = body.get("input");
+      if (!in || in->is_null()) in = body.get("prompt");
+      if (in && in->is_string()) c.uds.set("prompt", *in);
+      else if (in && in->is_array()) messages(*in);
+      else bad("input (or prompt / messages) is required");
+    }
+  }
+  const Value* mt = body.get(kind == "resp" ? "max_output_tokens" : "max_tokens");
+  if (!mt || mt->is_null()) mt = body.get("max_tokens");
+  if (mt && !mt->is_null()) {
+    if (!mt->is_integer() || mt->num < 1) bad("max_tokens must be >= 1");
+    c.uds.set("max_tokens", *mt);
+  }
+  static const char* kForward[] = {"temperature", "top_k", "top_p", "min_p", "seed", "repetition_penalty",
+                                   "frequency_penalty", "presence_penalty", "response_format", "grammar"};
+  for (const char* k : kForward) {
+    const Value* v = body.get(k);
+    if (!v || v->is_null()) continue;
+    const bool numeric = std::strcmp(k, "response_format") != 0 && std::strcmp(k, "grammar") != 0;
+    if (numeric && !v->is_number()) bad(std::string(k) + " must be a number");
+    c.uds.set(k, *v);
+  }
+  if (const Value* s = body.get("stop"); s && !s->is_null()) {
+    if (s->is_string()) {
+      c.stops.push_back(s->str);
+    } else if (s->is_array()) {
+      for (const auto& x : s->arr) {
+        if (!x.is_string()) bad("stop must be a string or a list of strings");
+        c.stops.push_back(x.str);
+      }
+    } else {
+      bad("stop must be a string or a list of strings");
+    }
+  }
+  if (const Value* n = body.get("n"); n && !n->is_null()) {
+    if (!n->is_integer() || n->num < 1 || n->num > 16) bad("n must be between 1 and 16");
+    c.n = (int)n->num;
+  }
+  if (const Value* s = body.get("stream"); s && s->type == Value::kBool) c.stream = s->b;
+  if (c.stream && c.n > 1) bad("n > 1 is not supported with stream");
+  if (const Value* so = body.get("stream_options"); so && so->is_object())
+    if (const Value* iu = so->get("include_usage"); iu && iu->type == Value::kBool) c.include_usage = iu->b;
+  return c;
+}
+
+std::string make_id(const std::string& kind) {
+  static std::atomic<uint64_t> seq{0};
+  const char* prefix = kind == "text" ? "cmpl" : kind == "chat" ? "chatcmpl" : "resp";
+  return std::string(prefix) + "-" + std::to_string((long long)std::time(nullptr)) + std::to_string(++seq % 100000);
+}
+
+Value usage(long p, long c) {
+  Value u = Value::object();
+  u.set("prompt_tokens", Value::number((double)p));
+  u.set("completion_tokens", Value::number((double)c));
+  u.set("total_tokens", Value::number((double)(p + c)));
+  return u;
+}
+
+Value chunk(const Call& c, const std::string& id, long created, const std::string* delta, const std::string* finish,
+            bool role) {
+  Value o = Value::object();
+  o.set("id", Value::string(id));
+  o.set("object", Value::string(c.kind == "text" ? "text_completion.chunk"
+                                : c.kind == "chat" ? "chat.completion.chunk" : "response.chunk"));
+  o.set("created", Value::number((double)created));
+  o.set("model", Value::string(c.model));
+  if (c.kind == "resp") {
+    o.set("output", Value::string(delta ? *delta : ""));
+    return o;
+  }
+  Value ch = Value::object();
+  ch.set("index", Value::number(0));
+  if (c.kind == "text") {
+    ch.set("text", Value::string(delta ? *delta : ""));
+  } else {
+    Value d = Value::object();
+    if (role) d.set("role", Value::string("assistant"));
+    if (delta) d.set("content", Value::string(*delta));
+    ch.set("delta", d);
+  }
+  ch.set("finish_reason", finish ? Value::string(*finish) : Value());
+  Value arr = Value::array();
+  arr.push(ch);
+  o.set("choices", arr);
+  return o;
+}
+
+// ---------------------------------------------------------------- handlers
+struct Outcome {
+  int status = 200;
+  bool close = false;  // the connection cannot be reused (a streamed response was sent)
+};
+
+Outcome finish_error(int fd, int status, const std::string& msg, bool keep, const std::string& rid) {
+  respond(fd, status, "application/json", error_body(msg, error_kind(status)), keep, rid);
+  return Outcome{status, !keep};
+}
+
+Outcome generate_route(int fd, const std::string& kind, const Request& req, bool keep, const std::string& rid) {
+  Value body;
+  try {
+    body = barqjson::parse(req.body);
+  } catch (const std::exception&) {
+    return finish_error(fd, 400, "request body is not valid JSON", keep, rid);
+  }
+  Call c;
+  try {
+    c = translate(kind, body, rid);
+  } catch (const std::invalid_argument& e) {
+    return finish_error(fd, 400, e.what(), keep, rid);
+  }
+  const std::string id = make_id(kind);
+  const long created = (long)std::time(nullptr);
+  const double t0 = now_s();
+  g_ctr.begin();
+  struct ActiveGuard {
+    double t0;
+    ~ActiveGuard() {
+      --g_ctr.active;
+      g_ctr.latency_us += (uint64_t)((now_s() - t0) * 1e6);
+      ++g_ctr.latency_n;
+    }
+  } guard{t0};
+
+  if (c.stream) {
+    bool headers_sent = false, client_ok = true;
+    auto send_event = [&](const Value& v) {
+      client_ok = client_ok && send_all(fd, "data: " + barqjson::dump(v) + "\n\n");
+      return client_ok;
+    };
+    auto on_first = [&]() {
+      std::string h = "HTTP/1.1 200 OK\r\nContent-Type: text/event-stream\r\nCache-Control: no-cache\r\n";
+      h += kCors;
+      h += "x-request-id: " + rid + "\r\nConnection: close\r\n\r\n";
+      headers_sent = true;
+      client_ok = send_all(fd, h);
+      if (client_ok && kind == "chat") send_event(chunk(c, id, created, nullptr, nullptr, true));
+      return client_ok;
+    };
+    auto on_delta = [&](const std::string& d) { return send_event(chunk(c, id, created, &d, nullptr, false)); };
+    Gen g = generate(c.uds, c.stops, on_first, on_delta);
+    if (!headers_sent) {
+      if (g.status != 200) return finish_error(fd, g.status, g.error, keep, rid);
+      on_first();  // an empty generation still gets its stream
+    }
+    if (g.status != 200) {  // failed after the stream started: an error event, then the end marker
+      send_all(fd, "data: " + error_body(g.error, error_kind(g.status)) + "\n\n");
+    } else if (client_ok) {
+      if (kind != "resp") send_event(chunk(c, id, created, nullptr, &g.finish, false));
+      if (c.include_usage) {
+        Value u = Value::object();
+        u.set("id", Value::string(id));
+        u.set("object", Value::string(kind == "chat" ? "chat.completion.chunk" : "text_completion.chunk"));
+        u.set("created", Value::number((double)created));
+        u.set("model", Value::string(c.model));
+        u.set("choices", Value::array());
+        u.set("usage", usage(g.prompt_tokens, g.completion_tokens));
+        send_event(u);
+      }
+      g_ctr.prompt_tokens += (uint64_t)g.prompt_tokens;
+      g_ctr.completion_tokens += (uint64_t)g.completion_tokens;
+    }
+    if (client_ok) send_all(fd, "data: [DONE]\n\n");
+    return Outcome{g.status == 200 ? 200 : g.status, true};
+  }
+
+  std::vector<Gen> outs;
+  long p_tok = 0, c_tok = 0;
+  for (int i = 0; i < c.n; ++i) {
+    Value r = c.uds;
+    if (i > 0) {  // choice i samples with its own seed (a 0 seed already differs per request)
+      const Value* s = r.get("seed");
+      if (s && s->is_number() && s->num != 0) r.set("seed", Value::number(s->num + i));
+      r.set("id", Value::string(rid + "-" + std::to_string(i)));
+    }
+    Gen g = generate(r, c.stops, [] { return true; }, [](const std::string&) { return true; });
+    if (g.status != 200) return finish_error(fd, g.status, g.error, keep, rid);
+    p_tok = g.prompt_tokens;
+    c_tok += g.completion_tokens;
+    outs.push_back(std::move(g));
+  }
+  g_ctr.prompt_tokens += (uint64_t)p_tok;
+  g_ctr.completion_tokens += (uint64_t)c_tok;
+  Value o = Value::object();
+  o.set("id", Value::string(id));
+  o.set("object", Value::string(kind == "text" ? "text_completion" : kind == "chat" ? "chat.completion" : "response"));
+  o.set("created", Value::number((double)created));
+  o.set("model", Value::string(c.model));
+  if (kind == "resp") {
+    o.set("output", Value::string(outs[0].text));
+  } else {
+    Value arr = Value::array();
+    for (size_t i = 0; i < outs.size(); ++i) {
+      Value ch = Value::object();
+      ch.set("index", Value::number((double)i));
+      if (kind == "text") {
+        ch.set("text", Value::string(outs[i].text));
+      } else {
+        Value m = Value::object();
+        m.set("role", Value::string("assistant"));
+        m.set("content", Value::string(outs[i].text));
+        ch.set("message", m);
+      }
+      ch.set("finish_reason", Value::string(outs[i].finish));
+      arr.push(ch);
+    }
+    o.set("choices", arr);
+  }
+  o.set("usage", usage(p_tok, c_tok));
+  respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
+  return Outcome{200, !keep};
+}
+
+std::string request_id(const Request& req) {
+  std::string rid = req.header("x-request-id");
+  bool clean = !rid.empty() && rid.size() <= 128;
+  for (const char ch : rid) clean = clean && (std::isalnum((unsigned char)ch) || ch == '-' || ch == '_' || ch == '.');
+  if (clean) return rid;
+  static std::atomic<uint64_t> seq{0};
+  thread_local uint64_t salt = (uint64_t)std::chrono::steady_clock::now().time_since_epoch().count();
+  char buf[24];
+  std::snprintf(buf, sizeof buf, "%016llx", (unsigned long long)((salt * 0x9E3779B97F4A7C15ull) ^ ++seq));
+  return buf;
+}
+
+Outcome dispatch(int fd, const Request& req, const std::string& client, bool keep) {
+  const std::string rid = request_id(req);
+  if (req.method == "OPTIONS") {
+    respond(fd, 204, "", "", keep, rid);
+    return Outcome{204, !keep};
+  }
+  const std::string& p = req.path;
+  if (req.method == "GET") {
+    if (p == "/") {
+      Value o = Value::object(), eps = Value::array();
+      o.set("object", Value::string("server.info"));
+      o.set("model", Value::string(g_opt.model_id));
+      o.set("front_end", Value::string("barq-http"));
+      for (const char* e : {"/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions", "/health",
+                            "/metrics"})
+        eps.push(Value::string(e));
+      o.set("endpoints", eps);
+      respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
+      return Outcome{200, !keep};
+    }
+    if (p == "/v1/models") {
+      Value o = Value::object(), data = Value::array(), m = Value::object();
+      m.set("id", Value::string(g_opt.model_id));
+      m.set("object", Value::string("model"));
+      m.set("created", Value::number((double)std::time(nullptr)));
+      m.set("owned_by", Value::string("barq"));
+      data.push(m);
+      o.set("object", Value::string("list"));
+      o.set("data", data);
+      respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
+      return Outcome{200, !keep};
+    }
+    if (p == "/health") {
+      const bool up = engine_reachable();
+      Value o = Value::object();
+      o.set("status", Value::string(up ? "ok" : "engine_unreachable"));
+      o.set("engine_socket", Value::string(g_opt.socket_path));
+      o.set("active_requests", Value::number((double)g_ctr.active));
+      respond(fd, up ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
+      return Outcome{up ? 200 : 503, !keep};
+    }
+    if (p == "/metrics") {
+      respond(fd, 200, "text/plain; version=0.0.4", g_ctr.prometheus(), keep, rid);
+      return Outcome{200, !keep};
+    }
+  }
+  static const std::map<std::string, std::string> kRoutes = {
+      {"/v1/completions", "text"}, {"/v1/chat/completions", "chat"}, {"/v1/responses", "resp"}};
+  const auto it = kRoutes.find(p);
+  if (it != kRoutes.end()) {
+    if (req.method != "POST") return finish_error(fd, 405, "use POST for " + p, keep, rid);
+    ++g_ctr.requests;
+    if (!g_limiter.allow(client)) {
+      ++g_ctr.rate_limited;
+      return finish_error(fd, 429, "rate limit exceeded; retry later", keep, rid);
+    }
+    return generate_route(fd, it->second, req, keep, rid);
+  }
+  return finish_error(fd, 404,
+                      "route not found; try /v1/models, /v1/responses, /v1/completions or /v1/chat/completions",
+                      keep, rid);
+}
+
+void log_line(const Request& req, const std::string& client, int status, double ms) {
+  if (g_opt.quiet) return;
+  Value o = Value::object();
+  o.set("client", Value::string(client));
+  o.set("method", Value::string(req.method));
+  o.set("path", Value::string(req.path));
+  o.set("status", Value::number(status));
+  o.set("latency_ms", Value::number(std::round(ms * 1000) / 1000));
+  std::fprintf(stderr, "%s\n", barqjson::dump(o).c_str());
+}
+
+void serve_connection(int fd, std::string client) {
+  struct Close {
+    int fd;
+    ~Close() {
+      ::close(fd);
+      --g_ctr.connections;
+    }
+  } closer{fd};
+  timeval tv{};
+  tv.tv_sec = 60;  // idle keep-alive connections are dropped after a minute
+  setsockopt(fd, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof tv);
+  int one = 1;
+  setsockopt(fd, IPPROTO_TCP, TCP_NODELAY, &one, sizeof one);
+  Conn conn(fd);
+  for (;;) {
+    Request req;
+    const int rc = conn.read(req);
+    if (rc < 0) return;
+    if (rc > 0) {
+      respond(fd, rc, "application/json", error_body(reason_phrase(rc), error_kind(rc)), false, "");
+      return;
+    }
+    const double t0 = now_s();
+    const std::string connection = lower(req.header("connection"));
+    const bool keep = req.version == "HTTP/1.1" ? connection != "close" : connection == "keep-alive";
+    const Outcome out = dispatch(fd, req, client, keep);
+    if (req.path == "/v1/completions" || req.path == "/v1/chat/completions" || req.path == "/v1/responses") {
+      if (out.status == 200) ++g_ctr.ok;
+      else if (out.status >= 500) ++g_ctr.server_errors;
+      else ++g_ctr.client_errors;
+    }
+    log_line(req, client, out.status, (now_s() - t0) * 1e3);
+    if (out.close || !keep) return;
+  }
+}
+
+int usage_error(const char* msg) {
+  std::fprintf(stderr, "barq-http: %s\n", msg);
+  std::fprintf(stderr,
+               "usage: barq-http --socket PATH [--host ADDR] [--port N] [--model-id NAME] [--rpm N]\n"
+               "                 [--max-conns N] [--engine-timeout S] [--quiet]\n");
+  return 2;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  for (int i = 1; i < argc; ++i) {
+    const std::string a = argv[i];
+    auto val = [&](const char* name) -> const char* {
+      if (i + 1 >= argc) {
+        std::fprintf(stderr, "barq-http: %s needs a value\n", name);
+        std::exit(2);
+      }
+      return argv[++i];
+    };
+    auto num = [&](const char* name, int lo) {
+      const char* v = val(name);
+      char* end = nullptr;
+      const long x = std::strtol(v, &end, 10);
+      if (*v == '\0' || *end != '\0' || x < lo || x > 1000000000L) {
+        std::fprintf(stderr, "barq-http: bad value for %s: %s\n", name, v);
+        std::exit(2);
+      }
+      return (int)x;
+    };
+    if (a == "--socket") g_opt.socket_path = val("--socket");
+    else if (a == "--host") g_opt.host = val("--host");
+    else if (a == "--port") g_opt.port = num("--port", 0);
+    else if (a == "--model-id") g_opt.model_id = val("--model-id");
+    else if (a == "--rpm") g_opt.rpm = num("--rpm", 0);
+    else if (a == "--max-conns") g_opt.max_conns = num("--max-conns", 1);
+    else if (a == "--engine-timeout") g_opt.engine_timeout_s = num("--engine-timeout", 1);
+    else if (a == "--quiet") g_opt.quiet = true;
+    else if (a == "-h" || a == "--help") {
+      usage_error("OpenAI-compatible HTTP front end for a barq UDS server");
+      return 0;
+    }
+    else return usage_error(("unknown argument " + a).c_str());
+  }
+  if (g_opt.port > 65535) return usage_error("port out of range");
+  signal(SIGPIPE, SIG_IGN);
+  const int ls = ::socket(AF_INET, SOCK_STREAM, 0);
+  if (ls < 0) return usage_error(std::strerror(errno));
+  int one = 1;
+  setsockopt(ls, SOL_SOCKET, SO_REUSEADDR, &one, sizeof one);
+  sockaddr_in addr{};
+  addr.sin_family = AF_INET;
+  addr.sin_port = htons((uint16_t)g_opt.port);
+  if (inet_pton(AF_INET, g_opt.host.c_str(), &addr.sin_addr) != 1) return usage_error("--host must be an IPv4 address");
+  if (::bind(ls, reinterpret_cast<sockaddr*>(&addr), sizeof addr) != 0 || ::listen(ls, 512) != 0) {
+    std::fprintf(stderr, "barq-http: cannot listen on %s:%d: %s\n", g_opt.host.c_str(), g_opt.port,
+                 std::strerror(errno));
+    return 2;
+  }
+  socklen_t len = sizeof addr;
+  getsockname(ls, reinterpret_cast<sockaddr*>(&addr), &len);
+  // the bound port (useful with --port 0) on stdout, flushed, for whoever started the process
+  std::printf("barq-http listening on %s:%d (engine socket %s)\n", g_opt.host.c_str(), ntohs(addr.sin_port),
+              g_opt.socket_path.c_str());
+  std::fflush(stdout);
+  for (;;) {
+    sockaddr_in peer{};
+    socklen_t plen = sizeof peer;
+    const int fd = ::accept(ls, reinterpret_cast<sockaddr*>(&peer), &plen);
+    if (fd < 0) {
+      if (errno == EINTR || errno == ECONNABORTED || errno == EMFILE || errno == ENFILE) continue;
+      std::fprintf(stderr, "barq-http: accept: %s\n", std::strerror(errno));
+      return 1;
+    }
+    char host[INET_ADDRSTRLEN] = "unknown";
+    inet_ntop(AF_INET, &peer.sin_addr, host, sizeof host);
+    if (++g_ctr.connections > g_opt.max_conns) {
+      respond(fd, 503, "application/json", error_body("too many connections", "overloaded_error"), false, "");
+      ::close(fd);
+      --g_ctr.connections;
+      continue;
+    }
+    std::thread(serve_connection, fd, std::string(host)).detach();
+  }
+}

@@ -1,0 +1,394 @@
+"""The native HTTP front end (``barq-http``, ``csrc/client/barq_http.cpp``) on CPU.
+
+A scripted UDS server stands in for the engine and records the frames the front end sends, so the
+tests check both sides of the translation: OpenAI request -> UDS request, UDS frames -> OpenAI
+responses / SSE chunks.  The last test runs the front end against the real UDS server and the CPU
+engine and compares its greedy text with the UDS client's."""
+import http.client
+import json
+import os
+import shutil
+import socket
+import subprocess
+import threading
+import time
+
+import pytest
+
+from barq_inference_b200.server.uds import recv_frame, send_frame
+
+pytestmark = pytest.mark.skipif(shutil.which("g++") is None and shutil.which("c++") is None,
+                                reason="no C++ compiler")
+
+SCRIPTS = {
+    # prompt / last message content -> (frame texts, final extras) or an error string
+    "hello": (["Hel", "lo", " wor", "ld"], {"prompt_tokens": 3, "finish_reason": "length"}),
+    "stop": (["ab", "c<e", "nd>tail", "more"], {"prompt_tokens": 2, "finish_reason": "length"}),
+    "near": (["x<e", "y"], {"prompt_tokens": 1, "finish_reason": "stop"}),
+    "utf8": (["é", "\U0001F600", "\"q\"\n"], {"prompt_tokens": 4, "finish_reason": "stop"}),
+    "slow": (["s"] * 200, {"prompt_tokens": 1, "finish_reason": "length"}),
+    "queue": "queue full",
+    "badreq": "bad request: temperature must be a number",
+    "boom": "RuntimeError: engine exploded",
+}
+
+
+class FakeEngine:
+    def __init__(self, path):
+        self.path = path
+        self.requests = []
+        self.aborted = []
+        self.lock = threading.Lock()
+        self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.sock.bind(path)
+        self.sock.listen(64)
+        threading.Thread(target=self._accept, daemon=True).start()
+
+    def _accept(self):
+        while True:
+            try:
+                conn, _ = self.sock.accept()
+            except OSError:
+                return
+            threading.Thread(target=self._serve, args=(conn,), daemon=True).start()
+
+    def _serve(self, conn):
+        try:
+            req = recv_frame(conn)
+            if req is None:  # a health probe: connect and close
+                return
+            with self.lock:
+                self.requests.append(req)
+            key = req.get("prompt")
+            if key is None:
+                key = req["messages"][-1]["content"]
+            script = SCRIPTS.get(key if isinstance(key, str) else "hello", SCRIPTS["hello"])
+            rid = req.get("id", "")
+            if isinstance(script, str):
+                send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
+                                  "done": True, "error": script})
+                return
+            texts, extra = script
+            for i, t in enumerate(texts):
+                if key == "slow":
+                    time.sleep(0.01)
+                send_frame(conn, {"id": rid, "text": t, "tokens_generated": i + 1, "ttft_ms": 1,
+                                  "total_time_ms": 2, "done": False})
+            send_frame(conn, {"id": rid, "text": "", "tokens_generated": len(texts), "ttft_ms": 1,
+                              "total_time_ms": 3, "done": True, **extra})
+        except OSError:
+            with self.lock:
+                self.aborted.append(True)
+        finally:
+            conn.close()
+
+    def close(self):
+        self.sock.close()
+
+
+def _start(sock_path, *extra):
+    from barq_inference_b200.server.uds_native import build_http
+
+    exe = build_http()
+    p = subprocess.Popen([exe, "--socket", sock_path, "--host", "127.0.0.1", "--port", "0", "--model-id", "tiny-x",
+                          "--quiet", *extra], stdout=subprocess.PIPE, stderr=subprocess.PIPE)
+    line = p.stdout.readline().decode()
+    assert "listening on 127.0.0.1:" in line, (line, p.stderr.read() if p.poll() is not None else b"")
+    port = int(line.split("127.0.0.1:")[1].split()[0])
+    return p, port
+
+
+@pytest.fixture()
+def gateway(tmp_path):
+    eng = FakeEngine(str(tmp_path / "e.sock"))
+    p, port = _start(eng.path)
+    yield eng, port
+    p.kill()
+    p.wait()
+    eng.close()
+
+
+def _req(port, method, path, body=None, headers=None, raw=None):
+    c = http.client.HTTPConnection("127.0.0.1", port, timeout=30)
+    data = raw if raw is not None else (json.dumps(body).encode() if body is not None else None)
+    c.request(method, path, body=data, headers={"Content-Type": "application/json", **(headers or {})})
+    r = c.getresponse()
+    out = r.status, dict(r.getheaders()), r.read()
+    c.close()
+    return out
+
+
+def _metric(text: str, name: str) -> float:
+    return float(next(line.split()[1] for line in text.splitlines() if line.startswith(name + " ")))
+
+
+def _events(raw: bytes):
+    evs = [e[len("data: "):] for e in raw.decode().split("\n\n") if e.startswith("data: ")]
+    assert evs[-1] == "[DONE]"
+    return [json.loads(e) for e in evs[:-1]]
+
+
+def test_info_models_health_and_cors(gateway, tmp_path):
+    eng, port = gateway
+    st, h, b = _req(port, "GET", "/v1/models")
+    assert st == 200 and json.loads(b)["data"][0]["id"] == "tiny-x"
+    assert h["Access-Control-Allow-Origin"] == "*"
+    st, _, b = _req(port, "GET", "/")
+    assert st == 200 and "/v1/chat/completions" in json.loads(b)["endpoints"]
+    st, _, b = _req(port, "GET", "/health")
+    assert st == 200 and json.loads(b)["status"] == "ok"
+    st, h, b = _req(port, "OPTIONS", "/v1/chat/completions")
+    assert st == 204 and "POST" in h["Access-Control-Allow-Methods"] and b == b""
+    st, _, b = _req(port, "GET", "/nope")
+    assert st == 404 and json.loads(b)["error"]["type"] == "not_found_error"
+    assert "try /v1/models" in json.loads(b)["error"]["message"]
+    st, _, _ = _req(port, "GET", "/v1/completions")
+    assert st == 405
+    # an engine socket that does not exist: health 503, generation 502
+    p, port2 = _start(str(tmp_path / "none.sock"))
+    try:
+        assert _req(port2, "GET", "/health")[0] == 503
+        st, _, b = _req(port2, "POST", "/v1/completions", {"prompt": "hello"})
+        assert st == 502 and json.loads(b)["error"]["type"] == "engine_unavailable_error"
+    finally:
+        p.kill()
+        p.wait()
+
+
+def test_completion_translation_both_ways(gateway):
+    eng, port = gateway
+    body = {"prompt": "hello", "max_tokens": 7, "temperature": 0.25, "top_k": 5, "top_p": 0.5, "seed": 11,
+            "min_p": 0.1, "repetition_penalty": 1.1, "response_format": {"type": "json_object"}, "grammar": "root ::= \"a\"",
+            "unknown_field": [1, 2]}
+    st, h, b = _req(port, "POST", "/v1/completions", body, headers={"x-request-id": "abc-123"})
+    assert st == 200, b
+    assert h["x-request-id"] == "abc-123"
+    out = json.loads(b)
+    assert out["object"] == "text_completion" and out["id"].startswith("cmpl-") and out["model"] == "tiny-x"
+    assert out["choices"] == [{"index": 0, "text": "Hello world", "finish_reason": "length"}]
+    assert out["usage"] == {"prompt_tokens": 3, "completion_tokens": 4, "total_tokens": 7}
+    sent = eng.requests[-1]
+    assert sent == {"id": "abc-123", "prompt": "hello", "max_tokens": 7, "temperature": 0.25, "top_k": 5,
+                    "top_p": 0.5, "min_p": 0.1, "seed": 11, "repetition_penalty": 1.1,
+                    "response_format": {"type": "json_object"}, "grammar": "root ::= \"a\""}
+    # token-id prompts pass through; the model field is echoed
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": [1, 2, 3], "model": "m2"})
+    assert st == 200 and json.loads(b)["model"] == "m2" and eng.requests[-1]["prompt"] == [1, 2, 3]
+    # non-ASCII text and escapes survive both hops
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "utf8"})
+    assert json.loads(b)["choices"][0]["text"] == "é\U0001F600\"q\"\n"
+
+
+def test_chat_and_responses_routes(gateway):
+    eng, port = gateway
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"}]
+    st, _, b = _req(port, "POST", "/v1/chat/completions", {"messages": msgs, "max_tokens": 4})
+    out = json.loads(b)
+    assert st == 200 and out["object"] == "chat.completion" and out["id"].startswith("chatcmpl-")
+    assert out["choices"][0]["message"] == {"role": "assistant", "content": "Hello world"}
+    assert eng.requests[-1]["messages"] == msgs and "prompt" not in eng.requests[-1]
+    st, _, b = _req(port, "POST", "/v1/responses", {"input": "hello", "max_output_tokens": 9})
+    out = json.loads(b)
+    assert st == 200 and out["object"] == "response" and out["output"] == "Hello world"
+    assert eng.requests[-1]["prompt"] == "hello" and eng.requests[-1]["max_tokens"] == 9
+    st, _, b = _req(port, "POST", "/v1/responses", {"input": msgs})
+    assert st == 200 and eng.requests[-1]["messages"] == msgs
+    # n choices: one engine request per choice, seeds offset, usage summed
+    st, _, b = _req(port, "POST", "/v1/chat/completions", {"messages": msgs, "n": 3, "seed": 5})
+    out = json.loads(b)
+    assert [c["index"] for c in out["choices"]] == [0, 1, 2] and out["usage"]["completion_tokens"] == 12
+    assert [r.get("seed") for r in eng.requests[-3:]] == [5, 6, 7]
+
+
+def test_streams(gateway):
+    eng, port = gateway
+    st, h, b = _req(port, "POST", "/v1/chat/completions",
+                    {"messages": [{"role": "user", "content": "hello"}], "stream": True,
+                     "stream_options": {"include_usage": True}})
+    assert st == 200 and h["Content-Type"] == "text/event-stream"
+    ev = _events(b)
+    assert ev[0]["choices"][0]["delta"] == {"role": "assistant"}
+    assert "".join(e["choices"][0]["delta"].get("content", "") for e in ev[1:-1]) == "Hello world"
+    assert ev[-2]["choices"][0]["finish_reason"] == "length"
+    assert ev[-1]["choices"] == [] and ev[-1]["usage"]["total_tokens"] == 7
+    assert all(e["object"] == "chat.completion.chunk" for e in ev)
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "hello", "stream": True})
+    ev = _events(b)
+    assert "".join(e["choices"][0]["text"] for e in ev) == "Hello world" and ev[-1]["choices"][0]["finish_reason"]
+    st, _, b = _req(port, "POST", "/v1/responses", {"input": "hello", "stream": True})
+    assert "".join(e["output"] for e in _events(b)) == "Hello world"
+
+
+def test_stop_strings_are_never_sent(gateway):
+    eng, port = gateway
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "stop", "stop": ["<end>", "zz"], "stream": True})
+    ev = _events(b)
+    texts = [e["choices"][0]["text"] for e in ev]
+    assert "".join(texts) == "abc" and all("<" not in t for t in texts)
+    assert ev[-1]["choices"][0]["finish_reason"] == "stop"
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "stop", "stop": "<end>"})
+    assert json.loads(b)["choices"][0] == {"index": 0, "text": "abc", "finish_reason": "stop"}
+    # a held-back prefix that never completes the stop string is released at the end
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "near", "stop": ["<end>"], "stream": True})
+    assert "".join(e["choices"][0]["text"] for e in _events(b)) == "x<ey"
+
+
+def test_errors(gateway):
+    eng, port = gateway
+    cases = [
+        (dict(raw=b"{not json"), 400, "not valid JSON"),
+        (dict(body=[1, 2]), 400, "JSON object"),
+        (dict(body={"max_tokens": 3}), 400, "prompt must be"),
+        (dict(body={"prompt": "hello", "max_tokens": 0}), 400, "max_tokens"),
+        (dict(body={"prompt": "hello", "temperature": "hot"}), 400, "temperature must be a number"),
+        (dict(body={"prompt": "hello", "n": 17}), 400, "n must be"),
+        (dict(body={"prompt": "hello", "n": 2, "stream": True}), 400, "not supported with stream"),
+        (dict(body={"prompt": "hello", "stop": 5}), 400, "stop must be"),
+        (dict(body={"prompt": "queue"}), 503, "queue full"),
+        (dict(body={"prompt": "queue", "stream": True}), 503, "queue full"),
+        (dict(body={"prompt": "badreq"}), 400, "bad request"),
+        (dict(body={"prompt": "boom"}), 500, "engine exploded"),
+    ]
+    for kw, status, text in cases:
+        st, h, b = _req(port, "POST", "/v1/completions", **kw)
+        assert st == status, (kw, st, b)
+        assert text in json.loads(b)["error"]["message"], (kw, b)
+    st, _, b = _req(port, "POST", "/v1/chat/completions", {"messages": []})
+    assert st == 400
+    st, _, b = _req(port, "POST", "/v1/chat/completions",
+                    {"messages": [{"role": "user", "content": "x"}], "tools": [{"function": {"name": "f"}}]})
+    assert st == 400 and "tools" in json.loads(b)["error"]["message"]
+    # oversized headers and bodies are refused before any engine call
+    n_before = len(eng.requests)
+    st, _, _ = _req(port, "POST", "/v1/completions", raw=b"{}", headers={"X-Big": "a" * 40000})
+    assert st == 431
+    s = socket.create_connection(("127.0.0.1", port))
+    s.sendall(b"POST /v1/completions HTTP/1.1\r\nContent-Length: 99999999\r\n\r\n")
+    assert s.recv(100).startswith(b"HTTP/1.1 413")
+    s.close()
+    s = socket.create_connection(("127.0.0.1", port))
+    s.sendall(b"garbage\r\n\r\n")
+    assert s.recv(100).startswith(b"HTTP/1.1 400")
+    s.close()
+    assert len(eng.requests) == n_before
+    st, _, b = _req(port, "GET", "/metrics")
+    m = b.decode()
+    assert "barq_http_requests_total" in m and "barq_http_client_errors_total" in m
+    assert _metric(m, "barq_http_server_errors_total") >= 3 and _metric(m, "barq_http_client_errors_total") >= 10
+
+
+def test_keep_alive_and_client_disconnect(gateway):
+    eng, port = gateway
+    c = http.client.HTTPConnection("127.0.0.1", port, timeout=30)
+    for _ in range(3):  # three requests on one connection
+        c.request("POST", "/v1/completions", body=json.dumps({"prompt": "hello"}),
+                  headers={"Content-Type": "application/json"})
+        r = c.getresponse()
+        assert r.status == 200 and json.loads(r.read())["choices"][0]["text"] == "Hello world"
+    c.close()
+    # a streaming client that goes away: the front end closes its engine connection early
+    s = socket.create_connection(("127.0.0.1", port))
+    body = json.dumps({"prompt": "slow", "stream": True}).encode()
+    s.sendall(b"POST /v1/completions HTTP/1.1\r\nContent-Type: application/json\r\nContent-Length: "
+              + str(len(body)).encode() + b"\r\n\r\n" + body)
+    assert s.recv(64).startswith(b"HTTP/1.1 200")
+    s.close()
+    deadline = time.time() + 20
+    while time.time() < deadline and not eng.aborted:
+        time.sleep(0.05)
+    assert eng.aborted, "the engine connection stayed open after the client left"
+
+
+def test_rate_limit(tmp_path):
+    eng = FakeEngine(str(tmp_path / "e.sock"))
+    p, port = _start(eng.path, "--rpm", "2")
+    try:
+        codes = [_req(port, "POST", "/v1/completions", {"prompt": "hello"})[0] for _ in range(3)]
+        assert codes == [200, 200, 429]
+        st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "hello"})
+        assert st == 429 and json.loads(b)["error"]["type"] == "rate_limit_error"
+        m = _req(port, "GET", "/metrics")[2].decode()
+        assert _metric(m, "barq_http_rate_limited_total") == 2
+    finally:
+        p.kill()
+        p.wait()
+        eng.close()
+
+
+def test_against_real_uds_server_and_cpu_engine(tmp_path):
+    """Greedy text through barq-http equals the UDS client's for the same prompt; chat messages are
+    rendered by the engine's template; usage counts match the tokenizer."""
+    from barq_inference_b200.engine.cpu_engine import CPUEngine
+    from barq_inference_b200.models import POLICIES, preset, random_tensors
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSClient, UDSServer
+    from barq_inference_b200.tokenizer import synthetic_tokenizer
+
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
+    eng = CPUEngine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=0), max_model_len=256)
+    tok = synthetic_tokenizer(cfg.vocab)
+    path = str(tmp_path / "real.sock")
+    ae = AsyncEngine(eng)
+    srv = UDSServer(ae, tok, path).start()
+    p, port = _start(path)
+    try:
+        cl = UDSClient(path)
+        want = "".join(f["text"] for f in cl.stream("hello world", max_tokens=8, temperature=0.0, rid="u"))
+        cl.close()
+        st, _, b = _req(port, "POST", "/v1/completions",
+                        {"prompt": "hello world", "max_tokens": 8, "temperature": 0.0})
+        out = json.loads(b)
+        assert st == 200 and out["choices"][0]["text"] == want
+        assert out["usage"]["prompt_tokens"] == len(tok.encode("hello world"))
+        assert out["choices"][0]["finish_reason"] in ("length", "stop")
+        st, _, b = _req(port, "POST", "/v1/chat/completions",
+                        {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4, "temperature": 0.0,
+                         "stream": True})
+        ev = _events(b)
+        assert st == 200 and ev[0]["choices"][0]["delta"] == {"role": "assistant"}
+        st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "x " * 400, "max_tokens": 100})
+        assert st == 400 and "max_model_len" in json.loads(b)["error"]["message"]
+    finally:
+        p.kill()
+        p.wait()
+        srv.stop()
+        ae.shutdown()
+
+
+def test_cli_http_server_native_front_end(tmp_path):
+    """``barq http-server --native-front-end``: the CLI serves HTTP through barq-http with the engine
+    behind a private UDS socket."""
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    model = str(tmp_path / "tiny.gguf")
+    r = subprocess.run([sys.executable, "-m", "barq_inference_b200.cli", "make-random-gguf", "--arch", "tiny",
+                        "--layers", "1", "--output", model, "--device", "cpu"], cwd=root, capture_output=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    p = subprocess.Popen([sys.executable, "-m", "barq_inference_b200.cli", "http-server", "-m", model, "--device",
+                          "cpu", "--host", "127.0.0.1", "--port", str(port), "--native-front-end"], cwd=root,
+                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, start_new_session=True)
+    try:
+        deadline = time.time() + 240
+        while True:
+            assert p.poll() is None, p.stderr.read().decode()[-3000:]
+            try:
+                if _req(port, "GET", "/health")[0] == 200:
+                    break
+            except OSError:
+                pass
+            assert time.time() < deadline, "front end did not come up"
+            time.sleep(0.5)
+        st, _, b = _req(port, "POST", "/v1/chat/completions",
+                        {"messages": [{"role": "user", "content": "hello"}], "max_tokens": 3, "temperature": 0})
+        out = json.loads(b)
+        assert st == 200 and out["object"] == "chat.completion" and out["usage"]["completion_tokens"] >= 1
+        assert out["model"] == "tiny.gguf"
+    finally:
+        os.killpg(p.pid, 15)
+        p.wait(timeout=60)

@@ -273,3 +273,99 @@ def test_uds_client_under_asan_ubsan(tmp_path):
             assert r.returncode == 0, err
         codes.add(r.returncode)
     assert {0, 2} <= codes, codes  # clean streams and rejected (malformed / oversized) ones both seen
+
+
+@pytest.mark.skipif(os.environ.get("BARQ_SANITIZE") != "1", reason="set BARQ_SANITIZE=1 (builds with ASan/UBSan)")
+def test_http_front_end_under_asan_ubsan(tmp_path):
+    """barq-http built with ASan/UBSan: fuzzed request lines, headers and JSON bodies (byte flips,
+    truncation, deep nesting, bad escapes, bogus lengths) against a scripted engine whose frames are
+    also mutated.  The process must answer or drop every connection, keep serving, and exit with no
+    sanitizer report."""
+    import json
+    import random
+    import signal
+    import socket
+    import struct
+    import threading
+
+    gxx = shutil.which("g++", path="/usr/bin") or shutil.which("g++")
+    exe = str(tmp_path / "barq-http-asan")
+    subprocess.run([gxx, "-O1", "-g", "-std=c++17", "-pthread", "-fsanitize=address,undefined",
+                    "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer", "-o", exe,
+                    os.path.join(ROOT, "csrc", "client", "barq_http.cpp")], check=True)
+    rng = random.Random(1)
+    path = str(tmp_path / "e.sock")
+    lsock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    lsock.bind(path)
+    lsock.listen(64)
+    good = [json.dumps({"id": "r", "text": t, "tokens_generated": i + 1, "done": i == 2, "prompt_tokens": 2,
+                        "finish_reason": "stop"}).encode() for i, t in enumerate(["aé", "<e", "nd>"])]
+
+    def mutate(b: bytes) -> bytes:
+        b = bytearray(b)
+        for _ in range(rng.randrange(1, 5)):
+            op = rng.random()
+            if op < 0.4 and b:
+                b[rng.randrange(len(b))] = rng.randrange(256)
+            elif op < 0.7 and b:
+                del b[rng.randrange(len(b)):]
+            else:
+                b[rng.randrange(len(b) + 1):0] = rng.choice([b"\\u", b"\\ud800", b"{", b"[" * 80, b"\"", b"\r\n", b":"])
+        return bytes(b)
+
+    def engine():
+        while True:
+            try:
+                conn, _ = lsock.accept()
+            except OSError:
+                return
+            try:
+                head = conn.recv(4)
+                if len(head) == 4:
+                    n = struct.unpack(">I", head)[0]
+                    while n > 0:
+                        chunk = conn.recv(min(n, 65536))
+                        if not chunk:
+                            break
+                        n -= len(chunk)
+                    for f in good:
+                        f = f if rng.random() < 0.5 else mutate(f)
+                        conn.sendall(struct.pack(">I", len(f)) + f)
+            except OSError:
+                pass
+            finally:
+                conn.close()
+
+    threading.Thread(target=engine, daemon=True).start()
+    env = {**os.environ, "ASAN_OPTIONS": "detect_leaks=0:abort_on_error=1",
+           "UBSAN_OPTIONS": "halt_on_error=1:print_stacktrace=1"}
+    p = subprocess.Popen([exe, "--socket", path, "--host", "127.0.0.1", "--port", "0", "--quiet"],
+                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env)
+    port = int(p.stdout.readline().decode().split("127.0.0.1:")[1].split()[0])
+    bodies = [{"prompt": "x", "stop": ["<end>"], "stream": True}, {"messages": [{"role": "user", "content": "y"}]},
+              {"input": [{"role": "user", "content": "z"}], "n": 2}, {"prompt": [1, 2, 3], "max_tokens": 4}]
+    for case in range(300):
+        body = json.dumps(rng.choice(bodies)).encode()
+        if case % 2:
+            body = mutate(body)
+        route = rng.choice([b"/v1/completions", b"/v1/chat/completions", b"/v1/responses", b"/health", b"/x"])
+        req = b"POST " + route + b" HTTP/1.1\r\nContent-Type: application/json\r\nContent-Length: " + \
+            str(len(body)).encode() + b"\r\nConnection: close\r\n\r\n" + body
+        if case % 5 == 3:
+            req = mutate(req)
+        s = socket.create_connection(("127.0.0.1", port), timeout=20)
+        try:
+            s.sendall(req)
+            s.shutdown(socket.SHUT_WR)
+            while s.recv(65536):
+                pass
+        except OSError:
+            pass
+        finally:
+            s.close()
+        assert p.poll() is None, (case, p.stderr.read().decode(errors="replace")[-3000:])
+    p.send_signal(signal.SIGTERM)
+    _, err = p.communicate(timeout=30)
+    lsock.close()
+    err = err.decode(errors="replace")
+    assert "runtime error" not in err and "AddressSanitizer" not in err, err[-3000:]
