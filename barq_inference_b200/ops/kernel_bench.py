@@ -116,7 +116,7 @@ def cases(tokens: int):
         flags = torch.zeros(64 * 8, dtype=torch.int32, device="cuda")
         epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
         C = require_ext()
-        fn = lambda: C.allreduce_add(x, [buf.data_ptr()], [flags.data_ptr()], epoch, 0, 4, 5.0, 0)  # noqa: E731
+        fn = lambda: C.allreduce_add(x, [buf.data_ptr()], [flags.data_ptr()], epoch, 0, 4, 5.0, 0, 0)  # noqa: E731
         return _qw(128, 256, GGMLType.Q4_K, 7), fn, 0.0
 
     def decode_step(B: int, ctx: int):

@@ -85,6 +85,10 @@ class Comm:
         self._bufs = [[p + j * n * 4 for p in base] for j in (0, 1)]
         self._flags = [p + 2 * n * 4 for p in base]
         self._n = n
+        # NVLS (BARQ_AR_MULTIMEM=1): multicast addresses of the two partial buffers, when the
+        # allocation is bound to a multicast object; 0 selects the peer-load form
+        mc = int(getattr(self.hdl, "multicast_ptr", 0) or 0) if os.environ.get("BARQ_AR_MULTIMEM") == "1" else 0
+        self._mc_bufs = [mc + j * n * 4 if mc else 0 for j in (0, 1)]
         self.epoch = torch.zeros(64, dtype=torch.int32, device=self.device)
         off = 2 * n + flag_words  # a multiple of 64 floats: the words are 8-byte aligned
         self._push_bufs = [torch.tensor([p + (off + j * self.world * pe * 2) * 4 for p in base], dtype=torch.int64,
@@ -277,7 +281,7 @@ class Comm:
         n = x.numel()
         blocks = max(1, min(32, (n // 4 + 255) // 256))
         require_ext().allreduce_add(x, self._bufs[j], self._flags, self.epoch, self.rank, blocks, self.wait_s,
-                                    int(self.skip_signal))
+                                    int(self.skip_signal), self._mc_bufs[j])
 
     # ------------------------------------------------------------------ NCCL baseline
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:

@@ -21,6 +21,18 @@ HTTP_SOURCES = [os.path.join(os.path.dirname(PKG), "csrc", "client", f) for f in
 HTTP_BINARY = os.path.join(PKG, "bin", "barq-http")
 
 
+def _compile(cmd: list[str], out: str) -> None:
+    """Compile to a private file and rename it into place: concurrent builders (parallel test
+    workers) never run or overwrite a half-written binary."""
+    tmp = f"{out}.{os.getpid()}.tmp"
+    try:
+        subprocess.run([*cmd, "-o", tmp], check=True)
+        os.replace(tmp, out)
+    finally:
+        if os.path.exists(tmp):
+            os.unlink(tmp)
+
+
 def client_path() -> str:
     return BINARY
 
@@ -35,7 +47,7 @@ def build_client(force: bool = False) -> str:
     if cxx is None:
         raise RuntimeError("no C++ compiler found to build barq-uds")
     os.makedirs(os.path.dirname(BINARY), exist_ok=True)
-    subprocess.run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-o", BINARY, SOURCE], check=True)
+    _compile([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", SOURCE], BINARY)
     return BINARY
 
 
@@ -53,6 +65,5 @@ def build_http(force: bool = False) -> str:
     if cxx is None:
         raise RuntimeError("no C++ compiler found to build barq-http")
     os.makedirs(os.path.dirname(HTTP_BINARY), exist_ok=True)
-    subprocess.run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-pthread", "-o", HTTP_BINARY,
-                    HTTP_SOURCES[0]], check=True)
+    _compile([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-pthread", HTTP_SOURCES[0]], HTTP_BINARY)
     return HTTP_BINARY

@@ -347,7 +347,7 @@ void mla_attention(Tensor q_lat, Tensor q, int64_t qdim, int64_t rope_off, Tenso
 
 // bufs / flags: device addresses (one per rank) of the partial buffers and flag areas.
 void allreduce_add(Tensor x, std::vector<int64_t> bufs, std::vector<int64_t> flags, Tensor epoch, int64_t rank,
-                   int64_t blocks, double wait_s, int64_t skip_signal) {
+                   int64_t blocks, double wait_s, int64_t skip_signal, int64_t mc) {
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "allreduce_add: x must be contiguous f32");
   TORCH_CHECK(bufs.size() == flags.size() && bufs.size() <= (size_t)barq::kArMaxRanks, "allreduce_add: ranks");
@@ -365,6 +365,7 @@ void allreduce_add(Tensor x, std::vector<int64_t> bufs, std::vector<int64_t> fla
   a.blocks = (int)blocks;
   a.wait_ns = (unsigned long long)(wait_s * 1e9);
   a.skip_signal = (int)skip_signal;
+  a.mc = reinterpret_cast<float*>(mc);  // 0: peer-load form
   check(barq::allreduce_add(a, cur_stream()), "allreduce_add");
 }
 

@@ -102,6 +102,7 @@ struct ArArgs {
   int rank, world, n, blocks;
   unsigned long long wait_ns;        // barrier wait limit
   int skip_signal;                   // fault injection: do not signal the peers (their waits run out)
+  float* mc = nullptr;               // multicast address of this call's partial buffer (NVLS form), or null
 };
 int allreduce_add(const ArArgs& a, cudaStream_t st);
 

@@ -22,7 +22,7 @@ def test_fused_allreduce_peer_timeout_is_reported():
     epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
     before = x.clone()
     C.allreduce_add(x, [mine.data_ptr(), fake_peer.data_ptr()], [flags0.data_ptr(), flags1.data_ptr()], epoch, 0,
-                    4, 0.5, 0)
+                    4, 0.5, 0, 0)
     torch.cuda.synchronize()
     err = C.gemm_error()
     assert err & 0xF00 == 0x300 and err & 0xFF == 1, hex(err)
