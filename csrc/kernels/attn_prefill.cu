@@ -248,10 +248,11 @@ template <typename TC, typename TM, int D>
 static int launch_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   constexpr int LD = D + 8;
   size_t smem = (size_t)(64 * LD + 4 * 64 * LD) * sizeof(TM);
-  cudaFuncSetAttribute(prefill_attn_kernel<TC, TM, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (cudaFuncSetAttribute(prefill_attn_kernel<TC, TM, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return -12;
   dim3 grid((a.max_q + 63) / 64, a.H, a.S);
-  launch_pdl(prefill_attn_kernel<TC, TM, D>, grid, dim3(128), smem, st, a);
-  return 0;
+  return launch_pdl(prefill_attn_kernel<TC, TM, D>, grid, dim3(128), smem, st, a) == cudaSuccess ? 0 : -20;
 }
 
 int prefill_attention(const PrefillAttnArgs& a, cudaStream_t st) {

@@ -103,8 +103,7 @@ __global__ void dequant_rows_kernel(QW w, int r0, __nv_bfloat16* __restrict__ ou
 
 int dequant_rows(const QW& w, int r0, int n, __nv_bfloat16* out, cudaStream_t st) {
   if (n <= 0) return 0;
-  launch_pdl(dequant_rows_kernel, dim3(n), dim3(256), 0, st, w, r0, out);
-  return 0;
+  return launch_pdl(dequant_rows_kernel, dim3(n), dim3(256), 0, st, w, r0, out) == cudaSuccess ? 0 : -20;
 }
 
 }  // namespace barq

@@ -81,11 +81,10 @@ int quantize_q8(const void* x, int x_is_bf16, int T, int H, int ldx, ActOut out_
   if (H % 32) return -1;
   if (T <= 0) return 0;
   dim3 g((H / 32 + 7) / 8, T);
-  if (x_is_bf16)
-    launch_pdl(quant_q8_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)x, H, ldx, out_q);
-  else
-    launch_pdl(quant_q8_kernel<float>, g, dim3(256), 0, st, (const float*)x, H, ldx, out_q);
-  return 0;
+  const cudaError_t e =
+      x_is_bf16 ? launch_pdl(quant_q8_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)x, H, ldx, out_q)
+                : launch_pdl(quant_q8_kernel<float>, g, dim3(256), 0, st, (const float*)x, H, ldx, out_q);
+  return e == cudaSuccess ? 0 : -20;
 }
 
 template <typename T>
@@ -109,11 +108,12 @@ int swiglu(const void* in, int in_is_bf16, int T, int F, int ld_in, void* out_ac
   if (out_q.q && (F % 32)) return -1;
   if (T <= 0) return 0;
   dim3 g(((F + 31) / 32 + 7) / 8, T);
-  if (in_is_bf16)
-    launch_pdl(swiglu_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)in, F, ld_in, out_act, out_f16, out_q);
-  else
-    launch_pdl(swiglu_kernel<float>, g, dim3(256), 0, st, (const float*)in, F, ld_in, out_act, out_f16, out_q);
-  return 0;
+  const cudaError_t e =
+      in_is_bf16 ? launch_pdl(swiglu_kernel<__nv_bfloat16>, g, dim3(256), 0, st, (const __nv_bfloat16*)in, F, ld_in,
+                              out_act, out_f16, out_q)
+                 : launch_pdl(swiglu_kernel<float>, g, dim3(256), 0, st, (const float*)in, F, ld_in, out_act, out_f16,
+                              out_q);
+  return e == cudaSuccess ? 0 : -20;
 }
 
 // ------------------------------------------------------------------------------ RoPE + KV write
@@ -227,16 +227,17 @@ int rope_kv_write(const RopeKVArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int nh = a.H + 2 * a.Hkv;
   dim3 g(a.T, (nh + 7) / 8 > 4 ? 4 : (nh + 7) / 8);
+  cudaError_t e;
   if (a.qkv_is_bf16) {
-    if (a.cache_type == kCacheBF16) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_bfloat16>, g, dim3(256), 0, st, a);
-    else if (a.cache_type == kCacheFP8) launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
-    else launch_pdl(rope_kv_kernel<__nv_bfloat16, __half>, g, dim3(256), 0, st, a);
+    if (a.cache_type == kCacheBF16) e = launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else if (a.cache_type == kCacheFP8) e = launch_pdl(rope_kv_kernel<__nv_bfloat16, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
+    else e = launch_pdl(rope_kv_kernel<__nv_bfloat16, __half>, g, dim3(256), 0, st, a);
   } else {
-    if (a.cache_type == kCacheBF16) launch_pdl(rope_kv_kernel<float, __nv_bfloat16>, g, dim3(256), 0, st, a);
-    else if (a.cache_type == kCacheFP8) launch_pdl(rope_kv_kernel<float, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
-    else launch_pdl(rope_kv_kernel<float, __half>, g, dim3(256), 0, st, a);
+    if (a.cache_type == kCacheBF16) e = launch_pdl(rope_kv_kernel<float, __nv_bfloat16>, g, dim3(256), 0, st, a);
+    else if (a.cache_type == kCacheFP8) e = launch_pdl(rope_kv_kernel<float, __nv_fp8_e4m3>, g, dim3(256), 0, st, a);
+    else e = launch_pdl(rope_kv_kernel<float, __half>, g, dim3(256), 0, st, a);
   }
-  return 0;
+  return e == cudaSuccess ? 0 : -20;
 }
 
 }  // namespace barq
