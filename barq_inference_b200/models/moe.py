@@ -70,7 +70,7 @@ class MoEBlock:
     def forward(self, runner, hq, hb: torch.Tensor, T: int, x: torch.Tensor) -> None:
         """Adds the MoE FFN output of the normalized activations ``hb`` [T, H] into ``x`` (f32)."""
         ser = getattr(runner, "ser_threshold", 0.0)
-        logits = hb.float() @ self.router.T  # [T, E]
+        logits = ops.router_logits(hb, self.router)  # [T, E] f32
         if getattr(runner, "fused_moe", True):
             self._fused(logits, hb, T, x, ser)
         else:

@@ -341,6 +341,23 @@ class MoeRouting:
         self.xs = torch.empty(T * k, H, dtype=dtype, device=device)
 
 
+def moe_router_logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Router logits f32 [T, E] = x [T, H] (fp16 / bf16) . w [E, H]^T (f32) on the device kernel
+    (``moe_router_kernel``); replaces ``x.float() @ w.T`` when ``BARQ_MOE_ROUTER=1``."""
+    out = torch.empty(x.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
+    require_ext().moe_router_logits(x, w, out)
+    _count()
+    return out
+
+
+def router_logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """MoE router logits: the device kernel with ``BARQ_MOE_ROUTER=1`` (opt-in until it has run on a
+    GPU), else the f32 library matmul."""
+    if os.environ.get("BARQ_MOE_ROUTER") == "1" and w.shape[1] % 4 == 0:
+        return moe_router_logits(x, w)
+    return x.float() @ w.T
+
+
 def moe_route(logits: torch.Tensor, x: torch.Tensor, k: int, r: MoeRouting, sigmoid: bool = False,
               renorm: bool = True, n_group: int = 1, topk_group: int = 1, ser_threshold: float = 0.0,
               scale: float = 1.0) -> MoeRouting:

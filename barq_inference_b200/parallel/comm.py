@@ -177,7 +177,7 @@ class Comm:
 
         C = require_ext()
         rows = hb.shape[0]
-        logits = hb.float() @ moe.router.T
+        logits = ops.router_logits(hb, moe.router)
         ids, wts, d = self.ep_ids[:rows], self.ep_w[:rows], self._ep_dummy
         ra = moe._route_args(ser)
         C.moe_route(logits.contiguous(), moe.k, int(ra["sigmoid"]), int(ra["renorm"]), ra["n_group"],

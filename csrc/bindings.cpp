@@ -198,6 +198,19 @@ void qgemm_grouped(int64_t type, int64_t N, int64_t K, Tensor p0, OptT p1, OptT 
   check(barq::qgemm_tc(w, x.data_ptr(), f16, (int)T, ep, 1, cur_stream(), &grp), "qgemm_grouped");
 }
 
+void moe_router_logits(Tensor x, Tensor w, Tensor out) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.dim() == 2 && (x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16) &&
+                  x.stride(1) == 1, "moe_router_logits: x fp16/bf16 [T, H] with unit column stride");
+  TORCH_CHECK(w.dim() == 2 && w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(1) == x.size(1),
+              "moe_router_logits: w f32 [E, H] contiguous");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.size(0) == x.size(0) &&
+                  out.size(1) == w.size(0), "moe_router_logits: out f32 [T, E] contiguous");
+  check(barq::moe_router_logits(x.data_ptr(), x.scalar_type() == torch::kHalf, (int)x.stride(0), ptr<const float>(w),
+                                ptr<float>(out), (int)x.size(0), (int)w.size(0), (int)x.size(1), cur_stream()),
+        "moe_router_logits");
+}
+
 void moe_route(Tensor logits, int64_t k, int64_t sigmoid, int64_t renorm, int64_t n_group, int64_t topk_group,
                double ser_threshold, double scale, Tensor x, Tensor ids, Tensor weights, Tensor counts, Tensor cursor,
                Tensor off, Tensor row_tok, Tensor row_w, Tensor tok_row, OptT xs) {
@@ -583,6 +596,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error", &gemm_error);
   m.def("qgemm_grouped", &qgemm_grouped);
   m.def("moe_route", &moe_route);
+  m.def("moe_router_logits", &moe_router_logits);
   m.def("moe_combine", &moe_combine);
   m.def("ep_call", &ep_call);
   m.def("spec_verify", &spec_verify);

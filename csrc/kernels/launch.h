@@ -162,6 +162,9 @@ struct MoeRouteArgs {
   int* tok_row;  // [T * k] sorted row of (token, slot), -1 when SER dropped the slot
 };
 int moe_route(const MoeRouteArgs& a, const void* x, int x_is_f16, void* xs, cudaStream_t st);
+// Router logits out[T, E] (f32) = x[T, H] (fp16 / bf16, row pitch ldx) . W[E, H]^T (f32), H % 4 == 0.
+int moe_router_logits(const void* x, int x_is_f16, int ldx, const float* w, float* out, int T, int E, int H,
+                      cudaStream_t st);
 
 // ---- Expert parallelism: all-to-all dispatch / combine over NVLink peer memory (moe.cu).
 // Each rank routes its own token rows (sequence-parallel residual), sends every (token, slot) row to

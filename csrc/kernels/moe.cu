@@ -27,6 +27,72 @@ namespace barq {
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
 
+// Router logits: out[t, e] = x[t, :] . W[e, :] (x fp16 / bf16 rows, W f32 [E, H], f32 accumulate
+// in a fixed order).  A CTA stages kRtTok token rows in shared memory and its 8 warps take experts
+// blockIdx.y * kRtExp + warp, + 8, ...; every lane reads W four floats at a time, so each router row
+// is read once per CTA and applied to all staged tokens.
+constexpr int kRtTok = 8, kRtExp = 32;
+template <typename T>
+__global__ void __launch_bounds__(256) moe_router_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w,
+                                                          float* __restrict__ out, int Ttot, int E, int H) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t rt_smem[];
+  T* xs = reinterpret_cast<T*>(rt_smem);  // [kRtTok][H]
+  const int t0 = blockIdx.x * kRtTok;
+  const int nt = min(kRtTok, Ttot - t0);
+  for (int i = threadIdx.x; i < kRtTok * H; i += blockDim.x) {
+    const int r = i / H, c = i % H;
+    xs[i] = r < nt ? x[(size_t)(t0 + r) * ldx + c] : from_f<T>(0.f);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e_end = min(E, (int)(blockIdx.y + 1) * kRtExp);
+  for (int e = blockIdx.y * kRtExp + warp; e < e_end; e += 8) {
+    const float* wr = w + (size_t)e * H;
+    float acc[kRtTok];
+#pragma unroll
+    for (int r = 0; r < kRtTok; ++r) acc[r] = 0.f;
+    for (int c = lane * 4; c < H; c += 128) {
+      const float4 wv = *reinterpret_cast<const float4*>(wr + c);
+#pragma unroll
+      for (int r = 0; r < kRtTok; ++r) {
+        const T* xr = xs + r * H + c;
+        acc[r] = fmaf(wv.x, to_f(xr[0]), acc[r]);
+        acc[r] = fmaf(wv.y, to_f(xr[1]), acc[r]);
+        acc[r] = fmaf(wv.z, to_f(xr[2]), acc[r]);
+        acc[r] = fmaf(wv.w, to_f(xr[3]), acc[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRtTok; ++r) {
+      const float v = warp_sum(acc[r]);
+      if (lane == 0 && r < nt) out[(size_t)(t0 + r) * E + e] = v;
+    }
+  }
+}
+
+int moe_router_logits(const void* x, int x_is_f16, int ldx, const float* w, float* out, int T, int E, int H,
+                      cudaStream_t st) {
+  if (H % 4 || E < 1 || E > kMaxExperts || ldx < H) return -1;
+  if (reinterpret_cast<uintptr_t>(w) & 15) return -3;
+  if (T <= 0) return 0;
+  const size_t smem = (size_t)kRtTok * H * 2;
+  if (smem > 200 * 1024) return -2;
+  dim3 grid((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp);
+  cudaError_t e;
+  if (x_is_f16) {
+    auto k = moe_router_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -12;
+    e = launch_pdl(k, grid, dim3(256), smem, st, static_cast<const __half*>(x), ldx, w, out, T, E, H);
+  } else {
+    auto k = moe_router_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -12;
+    e = launch_pdl(k, grid, dim3(256), smem, st, static_cast<const __nv_bfloat16*>(x), ldx, w, out, T, E, H);
+  }
+  return e == cudaSuccess ? 0 : -20;
+}
+
 __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
   pdl_wait();
   pdl_trigger();
