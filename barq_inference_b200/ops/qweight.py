@@ -3,15 +3,17 @@
 ``QWeight.from_packed`` splits GGUF blocks into aligned planes on the device without changing a
 bit (the planar form is where rows are fused, interleaved or sharded); ``finalize`` then cuts the
 planes into 128-row x 256/64-column chunks with row-swizzled 16-byte pieces, the form every kernel
-reads.  ``to_gguf_rows`` re-emits the original blocks from either form (tests check the round trip).  Types without a
-native kernel (Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, IQ4_XS, F16, F32, ...) are dequantized once at load to
-bf16 and use the dense GEMV/GEMM; the reference instead dequantizes *everything* to f32 at load
+reads.  ``to_gguf_rows`` re-emits the original blocks from either form (tests check the round trip).  Block
+types without a kernel format are converted at load: Q3_K to Q6_K (exact), Q5_0 to Q8_0 (exact),
+Q2_K / Q4_1 / Q5_1 / IQ4_XS to Q8_0 (within one Q8_0 step); F16 / F32 and anything else become bf16
+for the dense GEMV/GEMM.  The reference instead dequantizes *everything* to f32 at load
 (``barq_core/src/gguf.rs:306-311``).
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ..gguf import TYPE_TRAITS, GGMLType, dequantize
@@ -47,6 +49,44 @@ def requant_q8_0(raw: torch.Tensor, t: GGMLType, N: int, K: int) -> torch.Tensor
 
     w = torch.from_numpy(dequantize(raw.cpu().numpy(), t, (N, K))).to(dev, torch.float32)
     return quantize(w, GGMLType.Q8_0).reshape(N, nb * 34)
+
+
+def q3_k_as_q6_k(raw: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """Q3_K rows -> Q6_K rows (uint8 [N, K/256*210]), bit-exact.
+
+    Both types are 256-value super-blocks of sixteen 16-value sub-blocks with one fp16 scale d and
+    a signed per-sub-block scale: Q3_K stores value = d * (s - 32) * c with a 6-bit s and a code
+    c in [-4, 3]; Q6_K stores value = d * sc * (q - 32) with an int8 sc and a 6-bit q.  So d is
+    copied, sc = s - 32 and q = c + 32 (28..35), and the ggml-spec dequantization of the result
+    equals the source's value for value, while the device streams 6.6 instead of 8.5 bits per weight
+    (the Q8_0 import)."""
+    from ..gguf.dequant import q3_k_scales
+
+    dev = raw.device
+    b = raw.reshape(-1, 110).cpu().numpy()
+    nb = b.shape[0]
+    hm = b[:, 0:32].astype(np.int32)
+    qs = b[:, 32:96].astype(np.int32)
+    codes = np.empty((nb, 256), np.int32)
+    y = 0
+    for n in range(2):  # element order of the Q3_K block: 2 x 4 shifts x 2 halves of 16
+        q = qs[:, 32 * n: 32 * n + 32]
+        for j in range(4):
+            m = 1 << (4 * n + j)
+            for half in range(2):
+                sl = slice(16 * half, 16 * half + 16)
+                codes[:, y:y + 16] = ((q[:, sl] >> (2 * j)) & 3) - np.where(hm[:, sl] & m, 0, 4)
+                y += 16
+    q6 = codes + 32
+    out = np.empty((nb, 210), np.uint8)
+    for n in range(2):  # Q6_K packing: low nibbles in ql, the two high bits of 4 values per qh byte
+        e1, e2, e3, e4 = (q6[:, 128 * n + 32 * i: 128 * n + 32 * i + 32] for i in range(4))
+        out[:, 64 * n: 64 * n + 32] = (e1 & 0xF) | ((e3 & 0xF) << 4)
+        out[:, 64 * n + 32: 64 * n + 64] = (e2 & 0xF) | ((e4 & 0xF) << 4)
+        out[:, 128 + 32 * n: 128 + 32 * n + 32] = (e1 >> 4) | ((e2 >> 4) << 2) | ((e3 >> 4) << 4) | ((e4 >> 4) << 6)
+    out[:, 192:208] = q3_k_scales(b[:, 96:108]).astype(np.int8).view(np.uint8)
+    out[:, 208:210] = b[:, 108:110]
+    return torch.from_numpy(out).to(dev).reshape(N, K // 256 * 210)
 
 
 def _blocks(raw: torch.Tensor, N: int, t: GGMLType) -> torch.Tensor:
@@ -110,8 +150,10 @@ class QWeight:
 
             tt, q = import_ik(raw.cpu().numpy(), t, (N, K), dev)
             return QWeight.from_packed(q, tt, N, K, dev)
+        if t == GGMLType.Q3_K and K % 256 == 0:  # exact: same super-block structure as Q6_K
+            return QWeight.from_packed(q3_k_as_q6_k(raw, N, K), GGMLType.Q6_K, N, K, dev)
         if t not in NATIVE and t in _REQUANT and K % 64 == 0:
-            # block types without a tiled kernel format (Q5_0, Q2_K, Q3_K, Q4_1, ...): import as Q8_0,
+            # block types without a tiled kernel format (Q5_0, Q2_K, Q4_1, ...): import as Q8_0,
             # which the GEMV / tcgen05 GEMM stream (exact for Q5_0, near-lossless otherwise)
             return QWeight.from_packed(requant_q8_0(raw, t, N, K), GGMLType.Q8_0, N, K, dev)
         if t not in NATIVE or K % TILE_FMT[int(t)][0]:

@@ -1,14 +1,16 @@
-"""Import of block types without a kernel format (Q5_0, Q2_K, Q3_K, Q4_1, Q5_1) as Q8_0 rows.
+"""Import of block types without a kernel format: Q3_K as Q6_K rows (exact), Q5_0, Q2_K, Q4_1, Q5_1
+as Q8_0 rows.
 
-Q5_0 maps exactly (same block size and scale); the others are requantized with an error of about
-one Q8_0 step (1/254 of each 32-value block's largest magnitude, plus the fp16 rounding of its
-scale).  Random block bytes with a fixed, finite fp16 scale are valid blocks of every type."""
+Q3_K maps exactly onto Q6_K (same super-block, signed sub-block scales, codes shifted by 32) and Q5_0
+onto Q8_0 (same block size and scale); the others are requantized with an error of about one Q8_0
+step (1/254 of each 32-value block's largest magnitude, plus the fp16 rounding of its scale).
+Random block bytes with a fixed, finite fp16 scale are valid blocks of every type."""
 import numpy as np
 import pytest
 import torch
 
 from barq_inference_b200.gguf import GGMLType, dequantize, quantize
-from barq_inference_b200.ops.qweight import W_BF16, QWeight, requant_q8_0
+from barq_inference_b200.ops.qweight import W_BF16, QWeight, q3_k_as_q6_k, requant_q8_0
 
 N, K = 8, 512
 LAYOUT = {GGMLType.Q3_K: (256, 110, [108]), GGMLType.Q2_K: (256, 84, [80, 82]),
@@ -43,6 +45,22 @@ def test_requantized_within_one_q8_step(t):
     assert (np.abs(got - ref).reshape(N, -1, 32) <= bound).all()
 
 
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_q3_k_is_exact_as_q6_k(seed):
+    raw = _random_blocks(GGMLType.Q3_K, seed)
+    raw.view(N, -1, 110)[..., 108:110] = torch.from_numpy(  # a different fp16 scale per block
+        np.random.default_rng(seed).uniform(1e-3, 0.5, (N, K // 256)).astype(np.float16).view(np.uint8).reshape(N, -1, 2))
+    q6 = q3_k_as_q6_k(raw, N, K)
+    assert q6.shape == (N, K // 256 * 210) and q6.dtype == torch.uint8
+    assert np.array_equal(dequantize(q6.numpy(), GGMLType.Q6_K, (N, K)), dequantize(raw.numpy(), GGMLType.Q3_K, (N, K)))
+    # the loader streams Q3_K as exactly these Q6_K rows
+    w = QWeight.from_packed(raw, GGMLType.Q3_K, N, K, "cpu")
+    assert w.wtype == int(GGMLType.Q6_K)
+    assert torch.equal(w.to_gguf_rows().cpu(), q6)
+
+
 def test_loader_streams_requantized_types():
-    w = QWeight.from_packed(_random_blocks(GGMLType.Q3_K), GGMLType.Q3_K, N, K, "cpu")
+    w = QWeight.from_packed(_random_blocks(GGMLType.Q2_K), GGMLType.Q2_K, N, K, "cpu")
     assert w.wtype == int(GGMLType.Q8_0) and w.wtype != W_BF16
+    w = QWeight.from_packed(_random_blocks(GGMLType.Q3_K), GGMLType.Q3_K, N, K, "cpu")
+    assert w.wtype == int(GGMLType.Q6_K)
