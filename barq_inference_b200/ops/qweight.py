@@ -5,7 +5,8 @@ bit (the planar form is where rows are fused, interleaved or sharded); ``finaliz
 planes into 128-row x 256/64-column chunks with row-swizzled 16-byte pieces, the form every kernel
 reads.  ``to_gguf_rows`` re-emits the original blocks from either form (tests check the round trip).  Block
 types without a kernel format are converted at load: Q3_K to Q6_K (exact), Q5_0 to Q8_0 (exact),
-Q2_K / Q4_1 / Q5_1 / IQ4_XS to Q8_0 (within one Q8_0 step); F16 / F32 and anything else become bf16
+IQ4_XS to IQ4_NL (fp16 rounding of the block scales only), Q2_K / Q4_1 / Q5_1 to Q8_0 (within one
+Q8_0 step); F16 / F32 and anything else become bf16
 for the dense GEMV/GEMM.  The reference instead dequantizes *everything* to f32 at load
 (``barq_core/src/gguf.rs:306-311``).
 """
@@ -89,6 +90,28 @@ def q3_k_as_q6_k(raw: torch.Tensor, N: int, K: int) -> torch.Tensor:
     return torch.from_numpy(out).to(dev).reshape(N, K // 256 * 210)
 
 
+def iq4_xs_as_iq4_nl(raw: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """IQ4_XS rows -> IQ4_NL rows (uint8 [N, K/32*18]).
+
+    An IQ4_XS super-block (fp16 d, eight 6-bit sub-block scales ls, 4-bit codebook codes) is eight
+    32-value IQ4_NL blocks with the same codes and the block scale d * (ls - 32) rounded to fp16:
+    the only change is that rounding (relative error <= 2^-11, none when ls - 32 is a power of two
+    or the product fits fp16's 11-bit significand).  4.5 bits per weight on the device, against 8.5
+    for the Q8_0 import, whose per-block error is ~2^-8 of the block maximum."""
+    dev = raw.device
+    b = raw.reshape(-1, 136).cpu().numpy()
+    nb = b.shape[0]
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)  # [nb, 1]
+    sh = b[:, 2:4].copy().view("<u2").astype(np.int32)
+    sl = b[:, 4:8].astype(np.int32)
+    out = np.empty((nb, 8, 18), np.uint8)
+    for ib in range(8):
+        ls = ((sl[:, ib // 2] >> (4 * (ib % 2))) & 0xF) | (((sh[:, 0] >> (2 * ib)) & 3) << 4)
+        out[:, ib, 0:2] = (d[:, 0] * (ls - 32)).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        out[:, ib, 2:18] = b[:, 8 + 16 * ib: 8 + 16 * ib + 16]
+    return torch.from_numpy(out).to(dev).reshape(N, K // 32 * 18)
+
+
 def _blocks(raw: torch.Tensor, N: int, t: GGMLType) -> torch.Tensor:
     ts = TYPE_TRAITS[t].type_size
     return raw.reshape(N, -1, ts)
@@ -152,6 +175,8 @@ class QWeight:
             return QWeight.from_packed(q, tt, N, K, dev)
         if t == GGMLType.Q3_K and K % 256 == 0:  # exact: same super-block structure as Q6_K
             return QWeight.from_packed(q3_k_as_q6_k(raw, N, K), GGMLType.Q6_K, N, K, dev)
+        if t == GGMLType.IQ4_XS and K % 256 == 0:  # same codes, per-block fp16 scales
+            return QWeight.from_packed(iq4_xs_as_iq4_nl(raw, N, K), GGMLType.IQ4_NL, N, K, dev)
         if t not in NATIVE and t in _REQUANT and K % 64 == 0:
             # block types without a tiled kernel format (Q5_0, Q2_K, Q4_1, ...): import as Q8_0,
             # which the GEMV / tcgen05 GEMM stream (exact for Q5_0, near-lossless otherwise)

@@ -1,5 +1,5 @@
-"""Import of block types without a kernel format: Q3_K as Q6_K rows (exact), Q5_0, Q2_K, Q4_1, Q5_1
-as Q8_0 rows.
+"""Import of block types without a kernel format: Q3_K as Q6_K rows (exact), IQ4_XS as IQ4_NL rows
+(block scales rounded to fp16), Q5_0, Q2_K, Q4_1, Q5_1 as Q8_0 rows.
 
 Q3_K maps exactly onto Q6_K (same super-block, signed sub-block scales, codes shifted by 32) and Q5_0
 onto Q8_0 (same block size and scale); the others are requantized with an error of about one Q8_0
@@ -10,10 +10,10 @@ import pytest
 import torch
 
 from barq_inference_b200.gguf import GGMLType, dequantize, quantize
-from barq_inference_b200.ops.qweight import W_BF16, QWeight, q3_k_as_q6_k, requant_q8_0
+from barq_inference_b200.ops.qweight import W_BF16, QWeight, iq4_xs_as_iq4_nl, q3_k_as_q6_k, requant_q8_0
 
 N, K = 8, 512
-LAYOUT = {GGMLType.Q3_K: (256, 110, [108]), GGMLType.Q2_K: (256, 84, [80, 82]),
+LAYOUT = {GGMLType.Q3_K: (256, 110, [108]), GGMLType.IQ4_XS: (256, 136, [0]), GGMLType.Q2_K: (256, 84, [80, 82]),
           GGMLType.Q4_1: (32, 20, [0, 2]), GGMLType.Q5_1: (32, 24, [0, 2]), GGMLType.Q5_0: (32, 22, [0])}
 
 
@@ -57,6 +57,22 @@ def test_q3_k_is_exact_as_q6_k(seed):
     w = QWeight.from_packed(raw, GGMLType.Q3_K, N, K, "cpu")
     assert w.wtype == int(GGMLType.Q6_K)
     assert torch.equal(w.to_gguf_rows().cpu(), q6)
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_iq4_xs_as_iq4_nl_rounds_only_the_block_scales(seed):
+    raw = _random_blocks(GGMLType.IQ4_XS, seed)
+    raw.view(N, -1, 136)[..., 0:2] = torch.from_numpy(
+        np.random.default_rng(seed).uniform(1e-3, 0.05, (N, K // 256)).astype(np.float16).view(np.uint8).reshape(N, -1, 2))
+    nl = iq4_xs_as_iq4_nl(raw, N, K)
+    assert nl.shape == (N, K // 32 * 18)
+    ref = dequantize(raw.numpy(), GGMLType.IQ4_XS, (N, K))
+    got = dequantize(nl.numpy(), GGMLType.IQ4_NL, (N, K))
+    assert (np.abs(got - ref) <= np.abs(ref) * 2.0 ** -11 + 1e-12).all()  # half an fp16 ulp of the scale
+    # codes are untouched: dividing out each block's scale gives the same codebook values
+    dxs = dequantize(raw.numpy(), GGMLType.IQ4_XS, (N, K)).reshape(N, -1, 32)
+    assert np.array_equal(np.sign(got.reshape(N, -1, 32)), np.sign(dxs))
+    assert QWeight.from_packed(raw, GGMLType.IQ4_XS, N, K, "cpu").wtype == int(GGMLType.IQ4_NL)
 
 
 def test_loader_streams_requantized_types():
