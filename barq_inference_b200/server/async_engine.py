@@ -147,12 +147,11 @@ class AsyncEngine:
         try:
             while True:
                 item = await sub.aqueue.get()
-                if item.token is None and item.finish_reason == "error" and sub.error:
-                    done = True
+                done = item.token is None  # before the yield: a consumer may stop right after the last item
+                if done and item.finish_reason == "error" and sub.error:
                     raise _refusal(sub.error[0])
                 yield item
-                if item.token is None:
-                    done = True
+                if done:
                     return
         finally:
             if not done:  # the consumer stopped early (client disconnected): stop generating for it
@@ -189,12 +188,11 @@ class AsyncEngine:
         try:
             while True:
                 item = sub.sink.get(timeout=timeout)
-                if item.token is None and item.finish_reason == "error" and sub.error:
-                    done = True
+                done = item.token is None  # before the yield: a caller may stop right after the last item
+                if done and item.finish_reason == "error" and sub.error:
                     raise _refusal(sub.error[0])
                 yield item
-                if item.token is None:
-                    done = True
+                if done:
                     return
         finally:
             if not done:  # the caller stopped early (closed the iterator): stop generating for it

@@ -487,3 +487,57 @@ def test_every_subcommand_has_help():
         assert r.returncode == 0 and "usage" in r.stdout.lower(), (name, r.stderr[-500:])
     assert {"run", "chat", "benchmark", "info", "convert", "server", "http-server", "metal-info",
             "wasm-info"} <= set(sub.choices)
+
+
+def test_uds_disconnect_aborts_and_messages_use_the_template(tiny_engine, tmp_path):
+    """A UDS client that leaves mid-stream has its request aborted in the engine (no tokens are
+    generated for it afterwards); a request with chat ``messages`` is rendered with the server's
+    template and its final frame carries prompt_tokens and finish_reason."""
+    import time
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSServer, recv_frame, send_frame
+
+    path = str(tmp_path / "abort.sock")
+    ae = AsyncEngine(tiny_engine)
+    tmpl = ChatTemplate("generic")
+    srv = UDSServer(ae, tiny_engine.tokenizer, path, chat_template=tmpl).start()
+    try:
+        msgs = [{"role": "user", "content": "hello there"}]
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        s.connect(path)
+        send_frame(s, {"id": "m", "messages": msgs, "max_tokens": 3, "temperature": 0.0, "top_k": 1})
+        frames = []
+        while True:
+            fr = recv_frame(s)
+            frames.append(fr)
+            if fr["done"]:
+                break
+        s.close()
+        want = tiny_engine.tokenizer.encode(tmpl.render(msgs, add_generation_prompt=True), add_special=True)
+        assert frames[-1]["prompt_tokens"] == len(want) and frames[-1]["finish_reason"] in ("length", "stop")
+        # a long request whose client leaves after two frames
+        aborted = []
+        orig_abort = tiny_engine.abort
+
+        def spy(seq, orig_abort=orig_abort):
+            ok = orig_abort(seq)
+            aborted.append((seq.request_id, ok, len(seq.output)))
+            return ok
+
+        tiny_engine.abort = spy
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        s.connect(path)
+        send_frame(s, {"id": "gone", "prompt": "tell me a long story", "max_tokens": 200, "temperature": 0.0})
+        recv_frame(s)
+        recv_frame(s)
+        s.close()
+        deadline = time.time() + 30
+        while time.time() < deadline and (tiny_engine.running or tiny_engine.waiting):
+            time.sleep(0.05)
+        assert not tiny_engine.running and not tiny_engine.waiting
+        assert aborted and aborted[0][0] == "gone" and aborted[0][1] and aborted[0][2] < 200, aborted
+    finally:
+        tiny_engine.__dict__.pop("abort", None)
+        srv.stop()
+        ae.shutdown()
