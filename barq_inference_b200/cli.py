@@ -289,6 +289,23 @@ def cmd_info(args) -> int:
     return 0
 
 
+def cmd_tokenize(args) -> int:
+    """Token ids and pieces of a text under the model's tokenizer (the reference's tokenizer debugging
+    tool, ``cli/src/debug_tokenizer.rs``): one JSON object, or ``--ids-only`` for a comma list."""
+    _, tok, tmpl, _ = load(args, need_engine=False)
+    text = args.prompt
+    if args.chat:
+        text = tmpl.render([{"role": "user", "content": text}], add_generation_prompt=True)
+    ids = tok.encode(text, add_special=not args.no_special)
+    if args.ids_only:
+        print(",".join(str(i) for i in ids))
+        return 0
+    pieces = [tok.decode([i]) for i in ids]
+    print(json.dumps({"text": text, "n_tokens": len(ids), "ids": ids, "pieces": pieces,
+                      "round_trip": tok.decode(ids)}, ensure_ascii=False))
+    return 0
+
+
 def cmd_convert(args) -> int:
     from .gguf import QUANT_NAME_TO_TYPE
     from .models.convert import convert_gguf
@@ -569,6 +586,14 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("info", help="print GGUF header, hparams and tensor types")
     p.add_argument("-m", "--model", required=True)
     p.set_defaults(fn=cmd_info)
+
+    p = sub.add_parser("tokenize", help="token ids and pieces of a text under the model's tokenizer")
+    p.add_argument("-m", "--model", required=True)
+    p.add_argument("-p", "--prompt", required=True)
+    p.add_argument("--chat", action="store_true", help="render the text as a user turn of the chat template first")
+    p.add_argument("--no-special", action="store_true", help="no BOS / special tokens")
+    p.add_argument("--ids-only", action="store_true")
+    p.set_defaults(fn=cmd_tokenize)
 
     p = sub.add_parser("convert", help="requantize a GGUF file")
     p.add_argument("--input", required=True)

@@ -541,3 +541,14 @@ def test_uds_disconnect_aborts_and_messages_use_the_template(tiny_engine, tmp_pa
         tiny_engine.__dict__.pop("abort", None)
         srv.stop()
         ae.shutdown()
+
+
+def test_cli_tokenize(tmp_path):
+    path = str(tmp_path / "tk.gguf")
+    assert _cli("make-random-gguf", "--arch", "tiny", "--layers", "1", "--output", path, "--device", "cpu").returncode == 0
+    r = _cli("tokenize", "-m", path, "-p", "Hello, my name is")
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert out["round_trip"] == "Hello, my name is" and out["n_tokens"] == len(out["ids"]) == len(out["pieces"])
+    ids = _cli("tokenize", "-m", path, "-p", "Hello, my name is", "--ids-only", "--no-special").stdout.strip()
+    assert [int(x) for x in ids.split(",")] == [i for i in out["ids"] if i != 1]
