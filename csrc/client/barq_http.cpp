@@ -712,8 +712,9 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
     return Outcome{g.status == 200 ? 200 : g.status, true};
   }
 
-  std::vector<Gen> outs;
-  long p_tok = 0, c_tok = 0;
+  // the n choices run as concurrent engine requests (continuous batching serves them together)
+  std::vector<Gen> outs(c.n);
+  std::vector<std::thread> workers;
   for (int i = 0; i < c.n; ++i) {
     Value r = c.uds;
     if (i > 0) {  // choice i samples with its own seed (a 0 seed already differs per request)
@@ -721,11 +722,18 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       if (s && s->is_number() && s->num != 0) r.set("seed", Value::number(s->num + i));
       r.set("id", Value::string(rid + "-" + std::to_string(i)));
     }
-    Gen g = generate(r, c.stops, [] { return true; }, [](const std::string&) { return true; });
+    auto run = [&outs, &c, i](Value req) {
+      outs[i] = generate(req, c.stops, [] { return true; }, [](const std::string&) { return true; });
+    };
+    if (i + 1 < c.n) workers.emplace_back(run, std::move(r));
+    else run(std::move(r));
+  }
+  for (auto& w : workers) w.join();
+  long p_tok = 0, c_tok = 0;
+  for (const Gen& g : outs) {
     if (g.status != 200) return finish_error(fd, g.status, g.error, keep, rid);
     p_tok = g.prompt_tokens;
     c_tok += g.completion_tokens;
-    outs.push_back(std::move(g));
   }
   g_ctr.prompt_tokens += (uint64_t)p_tok;
   g_ctr.completion_tokens += (uint64_t)c_tok;
