@@ -130,6 +130,10 @@ class RateLimiter {
     if (g_opt.rpm <= 0) return true;
     const double cap = g_opt.rpm, refill = cap / 60.0, t = now_s();
     std::lock_guard<std::mutex> lk(mu_);
+    if (state_.size() > 65536) {  // forget clients whose bucket has refilled completely
+      for (auto i = state_.begin(); i != state_.end();)
+        i = (t - i->second.second) * refill + i->second.first >= cap ? state_.erase(i) : std::next(i);
+    }
     auto it = state_.find(key);
     if (it == state_.end()) it = state_.emplace(key, std::make_pair(cap, t)).first;
     double& tokens = it->second.first;
