@@ -16,6 +16,7 @@ import torch
 from ..models.config import ModelConfig
 from ..models.reference import ReferenceModel
 from ..sampling.host_samplers import new_host_sampler, sample_chain
+from .logprobs import record_logprobs
 from .engine import GenerationResult
 from .sampling_params import SamplingParams
 from .sequence import Sequence, SeqStatus
@@ -117,6 +118,7 @@ class CPUEngine:
                 key = "decode"
                 n = 1
             s.n_cached = s.n_tokens
+            raw = logits
             if s.grammar_state is not None:
                 m = s.grammar_state.allowed_mask((self.cfg.vocab + 31) // 32)
                 bits = np.unpackbits(m.view(np.uint8), bitorder="little")[: self.cfg.vocab].astype(bool)
@@ -125,6 +127,8 @@ class CPUEngine:
                 tok = s.host_sampler.sample(logits, s)
             else:
                 tok = sample_chain(logits, s.params, s.tokens, self.gens[s.seq_id])
+            if s.params.logprobs:
+                record_logprobs(raw[None], [0], [tok], [s])
             self.timings[key + "_s"] += time.perf_counter() - t0
             self.timings[key + "_tokens"] += n
             if s.first_token_time is None:

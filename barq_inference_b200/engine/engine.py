@@ -25,6 +25,7 @@ from .. import ops
 from ..models.config import ModelConfig
 from ..models.runner import LlamaRunner, StepInput
 from .kv_cache import BlockManager, new_block_manager  # noqa: F401
+from .logprobs import record_logprobs
 from .scheduler import ScheduledStep, SchedulerConfig, new_scheduler
 from .sampling_params import SamplingParams
 from .sequence import Sequence
@@ -352,7 +353,7 @@ class Engine:
     def _run_decode(self, plan: ScheduledStep) -> list[int | None]:
         seqs = plan.seqs
         simple = all(s.grammar_state is None and s.host_sampler is None and not s.params.needs_penalties
-                     for s in seqs)
+                     and not s.params.logprobs for s in seqs)
         if self.ecfg.cuda_graphs and simple and self.device.type == "cuda":
             B = next((b for b in self.ecfg.graph_buckets if b >= len(seqs)), None)
             if B is not None:
@@ -406,16 +407,12 @@ class Engine:
         host = [i for i, s in enumerate(seqs) if s.host_sampler is not None]
         if host:  # only the rows sampled on the host cross to it
             lg = dict(zip(host, logits[torch.tensor(host, device=logits.device)].float().cpu()))
-        ids, lp = ops.sample(logits, temp, topk, topp, minp, seeds, steps, allow_mask=mask, penalties=pen,
-                             history=hist, want_logprob=any(s.params.logprobs for s in seqs))
+        ids, _ = ops.sample(logits, temp, topk, topp, minp, seeds, steps, allow_mask=mask, penalties=pen,
+                            history=hist)
         out = ids.cpu().tolist()
-        lps = lp.cpu().tolist() if lp is not None else None
         for i in host:
             out[i] = seqs[i].host_sampler.sample(lg[i], seqs[i])
-        if lps is not None:
-            for s, v in zip(seqs, lps):
-                if s.params.logprobs:
-                    s.logprobs.append(v)
+        record_logprobs(logits, [i for i, s in enumerate(seqs) if s.params.logprobs], out, seqs)
         return out
 
     # ------------------------------------------------------------------ CUDA graphs

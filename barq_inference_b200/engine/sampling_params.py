@@ -32,7 +32,8 @@ class SamplingParams:
     grammar: str | None = None  # GBNF text
     json_mode: bool = False
     json_schema: dict | None = None
-    logprobs: bool = False
+    logprobs: bool = False     # record log p(token) of every sampled token (log-softmax of the raw logits)
+    top_logprobs: int = 0      # ... and the most likely alternatives (0..20)
 
     @property
     def greedy(self) -> bool:

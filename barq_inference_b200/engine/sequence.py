@@ -30,6 +30,7 @@ class Sequence:
     seq_id: int = field(default_factory=lambda: next(_ids))
     output: list[int] = field(default_factory=list)
     logprobs: list[float] = field(default_factory=list)
+    top_logprobs: list[list[tuple[int, float]]] = field(default_factory=list)
     block_table: list[int] = field(default_factory=list)
     n_cached: int = 0           # tokens whose K/V are in the cache
     status: SeqStatus = SeqStatus.WAITING

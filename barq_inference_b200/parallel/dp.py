@@ -91,7 +91,7 @@ class GGUFEngineFactory:
 
 def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, outq, stats_every: float) -> None:
     """Replica loop: admit requests from ``inq``, run engine steps, send the step's token events to
-    ``outq`` as one message per step.  Messages in: ("req", rid, prompt, params) | ("cancel", rid) |
+    ``outq`` (this replica's own pipe to the front end) as one message per step.  Messages in: ("req", rid, prompt, params) | ("cancel", rid) |
     ("stop",).  Messages out (tagged with ``idx``): ("ready", info) | ("events", [(rid, tok, reason)])
     with tok None on finish | ("stats", dict) | ("fatal", msg)."""
     if device != "cpu":
@@ -105,9 +105,9 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
 
             atexit.register(eng.stop)
     except Exception as e:  # report and exit; the front end marks the replica dead
-        outq.put((idx, "fatal", f"{type(e).__name__}: {e}"))
+        outq.send((idx, "fatal", f"{type(e).__name__}: {e}"))
         return
-    outq.put((idx, "ready", {"device": device, "pid": os.getpid()}))
+    outq.send((idx, "ready", {"device": device, "pid": os.getpid()}))
     live: dict[str, Any] = {}
     events: list = []
 
@@ -145,7 +145,7 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
             while True:
                 if msg[0] == "stop":
                     if events:
-                        outq.put((idx, "events", events))
+                        outq.send((idx, "events", events))
                     if hasattr(eng, "stop"):  # release the follower ranks of a multi-rank replica
                         eng.stop()
                     return
@@ -167,7 +167,7 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
                 if sched is not None:
                     sched.clear_waiting("error")
         if events:
-            outq.put((idx, "events", events))
+            outq.send((idx, "events", events))
             events = []
         now = time.monotonic()
         if now - last_stats >= stats_every:
@@ -177,7 +177,7 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
             if blocks is not None:
                 t["kv_blocks_used"], t["kv_blocks_total"] = blocks.n_used, blocks.num_blocks
             t["in_flight"] = len(live)
-            outq.put((idx, "stats", t))
+            outq.send((idx, "stats", t))
 
 
 # ------------------------------------------------------------------ front end
@@ -204,6 +204,7 @@ class ReplicaState:
     served: int = 0
     stats: dict = field(default_factory=dict)
     error: str | None = None
+    out: Any = None  # read end of the replica's pipe (None once it has closed)
 
 
 class DataParallelEngine:
@@ -220,15 +221,20 @@ class DataParallelEngine:
         self.affinity_tokens = affinity_tokens
         self.affinity_slack = affinity_slack
         ctx = mp.get_context("spawn")
-        self._outq = ctx.Queue()
         self.replicas = [ReplicaState(i, d) for i, d in enumerate(devices)]
         for r in self.replicas:
             r.inq = ctx.Queue()
+            # one pipe per replica to the front end, written by that replica only: a replica killed
+            # in the middle of a send can only break its own pipe (a queue shared by all replicas
+            # keeps a cross-process write lock that a killed writer can leave held, which would
+            # silence every survivor)
+            r.out, out_w = ctx.Pipe(duplex=False)
             # not daemonic: a replica may start processes of its own (the other ranks of a
             # multi-GPU replica); shutdown() stops and joins every replica
-            r.proc = ctx.Process(target=_replica_main, args=(r.idx, r.device, factory, r.inq, self._outq, stats_every),
+            r.proc = ctx.Process(target=_replica_main, args=(r.idx, r.device, factory, r.inq, out_w, stats_every),
                                  name=f"barq-dp{r.idx}", daemon=False)
             r.proc.start()
+            out_w.close()  # the replica holds the only write end: its exit shows up as EOF here
         self._lock = threading.Lock()
         self._reqs: dict[str, _Request] = {}
         self._affinity: dict[tuple, int] = {}
@@ -243,6 +249,35 @@ class DataParallelEngine:
         self._router.start()
 
     # ------------------------------------------------------------------ lifecycle
+    def _recv(self, timeout: float) -> list[tuple]:
+        """Messages that arrive on any replica pipe within ``timeout`` s; a pipe that closes or
+        breaks (its replica exited, possibly mid-message) yields a ("fatal", why) message once."""
+        from multiprocessing.connection import wait
+
+        conns = {r.out: r for r in self.replicas if r.out is not None}
+        if not conns:
+            time.sleep(timeout)
+            return []
+        msgs = []
+        for c in wait(list(conns), timeout):
+            r = conns[c]
+            try:
+                while True:
+                    msgs.append(c.recv())
+                    if not c.poll():
+                        break
+            except (EOFError, OSError) as e:
+                r.out = None
+                c.close()
+                code = r.proc.exitcode if r.proc is not None else None
+                msgs.append((r.idx, "fatal", f"replica {r.idx} ({r.device}) exited with code {code}"
+                             if isinstance(e, EOFError) else f"replica {r.idx} pipe broke: {e}"))
+            except Exception as e:  # a partial message from a replica killed mid-send
+                r.out = None
+                c.close()
+                msgs.append((r.idx, "fatal", f"replica {r.idx} sent a broken message: {type(e).__name__}"))
+        return msgs
+
     def _wait_ready(self, timeout: float) -> None:
         pending = {r.idx for r in self.replicas}
         deadline = time.monotonic() + timeout
@@ -251,20 +286,13 @@ class DataParallelEngine:
             if left <= 0:
                 self.shutdown()
                 raise TimeoutError(f"data-parallel replicas {sorted(pending)} not ready after {timeout:.0f} s")
-            try:
-                idx, kind, payload = self._outq.get(timeout=min(left, 1.0))
-            except queue.Empty:
-                for i in list(pending):
-                    if not self.replicas[i].proc.is_alive():
-                        self.replicas[i].error = f"replica {i} exited with code {self.replicas[i].proc.exitcode}"
-                        pending.discard(i)
-                continue
-            r = self.replicas[idx]
-            if kind == "ready":
-                r.alive = True
-            elif kind == "fatal":
-                r.error = payload
-            pending.discard(idx)
+            for idx, kind, payload in self._recv(min(left, 1.0)):
+                r = self.replicas[idx]
+                if kind == "ready":
+                    r.alive = True
+                elif kind == "fatal":
+                    r.error = payload
+                pending.discard(idx)
         if not any(r.alive for r in self.replicas):
             errs = "; ".join(f"{r.idx}: {r.error}" for r in self.replicas)
             self.shutdown()
@@ -355,11 +383,7 @@ class DataParallelEngine:
     def _route_loop(self) -> None:
         last_check = time.monotonic()
         while not self._stop.is_set():
-            try:
-                idx, kind, payload = self._outq.get(timeout=0.05)
-            except queue.Empty:
-                idx = None
-            if idx is not None:
+            for idx, kind, payload in self._recv(0.05):
                 if kind == "events":
                     for rid, tok, reason in payload:
                         if tok is None:

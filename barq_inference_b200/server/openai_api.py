@@ -38,6 +38,17 @@ CORS = {"Access-Control-Allow-Origin": "*", "Access-Control-Allow-Methods": "GET
         "Access-Control-Allow-Headers": "*"}
 
 
+def _held_suffix(text: str, stops: list[str]) -> int:
+    """Length of the longest end of ``text`` that is a proper prefix of a stop string."""
+    hold = 0
+    for x in stops:
+        for n in range(min(len(x) - 1, len(text)), hold, -1):
+            if text.endswith(x[:n]):
+                hold = n
+                break
+    return hold
+
+
 class RateLimiter:
     """Token bucket per client key; capacity = requests per minute, refilled continuously."""
 
@@ -144,32 +155,84 @@ class OpenAIServer:
         return [s] if isinstance(s, str) else [str(x) for x in s]
 
     async def _run(self, prompt_ids: list[int], params: SamplingParams, stops: list[str]):
-        """Yields (text_delta, finish_reason | None); finish at the end."""
+        """Yields (text_delta, finish_reason | None, logprob entries, tokens) per delta: the entries
+        and the count of the generated tokens behind it; the finish comes last.  With stop strings,
+        text that could still be the start of one is held back until it cannot, so no part of a stop
+        string is ever sent."""
         dec = StreamDecoder(self.tok)
-        text = ""
+        text, sent, k, ntok = "", 0, 0, 0
+        pend: list = []  # logprob entries of tokens whose text has not been yielded yet
+        longest = max((len(x) for x in stops), default=0)
         async for item in self.aengine.stream(prompt_ids, params):
             if item.token is None:
-                tail = dec.flush()
-                if tail:
-                    yield tail, None
-                yield "", item.finish_reason or "stop"
+                text += dec.flush()
+                if len(text) > sent:
+                    yield text[sent:], None, pend, ntok
+                    pend, ntok = [], 0
+                yield "", item.finish_reason or "stop", pend, ntok
                 return
+            idx, k = k, k + 1  # position of this token among the generated ones
             if item.token in self.engine.cfg.eos_ids and not params.ignore_eos:
                 continue
-            piece = dec.push(item.token)
-            if not piece:
-                continue
+            ntok += 1
+            if params.logprobs:
+                e = self._lp_entry(item, idx)
+                if e is not None:
+                    pend.append(e)
+            before = len(text)
+            text += dec.push(item.token)
+            safe = len(text)
             if stops:
-                text += piece
-                hit = min((text.find(s) for s in stops if s and text.find(s) >= 0), default=-1)
+                hits = [text.find(x, max(0, before - longest)) for x in stops if x]
+                hit = min((h for h in hits if h >= 0), default=-1)
                 if hit >= 0:
-                    keep = text[:hit]
-                    already = len(text) - len(piece)
-                    if hit > already:
-                        yield keep[already:], None
-                    yield "", "stop"
+                    yield text[sent:hit] if hit > sent else "", None, pend, ntok
+                    yield "", "stop", [], 0
                     return
-            yield piece, None
+                safe -= _held_suffix(text, stops)
+            if safe > sent:
+                yield text[sent:safe], None, pend, ntok
+                pend, ntok = [], 0
+                sent = safe
+
+    def _lp_entry(self, item, idx: int):
+        """(token id, logprob, [(alt id, logprob), ...]) of the idx-th generated token, from the
+        engine's per-sequence record (None when the engine did not record one)."""
+        seq = item.seq
+        lps = getattr(seq, "logprobs", None)
+        if not lps or idx >= len(lps):
+            return None
+        tops = getattr(seq, "top_logprobs", None) or []
+        return item.token, float(lps[idx]), list(tops[idx]) if idx < len(tops) else []
+
+    def _lp_token(self, tid: int) -> tuple[str, list[int]]:
+        b = self.tok.token_bytes(tid) if hasattr(self.tok, "token_bytes") else self.tok.decode([tid]).encode()
+        return b.decode("utf-8", errors="replace"), list(b)
+
+    def _lp_chat(self, entries: list) -> dict:
+        """OpenAI chat form: {"content": [{token, logprob, bytes, top_logprobs: [...]}, ...]}."""
+        out = []
+        for tid, lp, top in entries:
+            t, b = self._lp_token(tid)
+            alts = []
+            for aid, alp in top:
+                at, ab = self._lp_token(aid)
+                alts.append({"token": at, "logprob": alp, "bytes": ab})
+            out.append({"token": t, "logprob": lp, "bytes": b, "top_logprobs": alts})
+        return {"content": out}
+
+    def _lp_text(self, entries: list, offset: int = 0) -> dict:
+        """OpenAI completions form: tokens, token_logprobs, top_logprobs, text_offset."""
+        toks, lps, tops, offs = [], [], [], []
+        for tid, lp, top in entries:
+            t, _ = self._lp_token(tid)
+            toks.append(t)
+            lps.append(lp)
+            tops.append({self._lp_token(a)[0]: alp for a, alp in top} if top else None)
+            offs.append(offset)
+            offset += len(t)
+        return {"tokens": toks, "token_logprobs": lps,
+                "top_logprobs": tops if any(x is not None for x in tops) else None, "text_offset": offs}
 
     def _limit(self, request: Request) -> JSONResponse | None:
         if self.limiter is None:
@@ -206,15 +269,16 @@ class OpenAIServer:
         async def one(i: int):
             # choice i samples with its own seed (a 0 seed already differs per request)
             p = dataclasses.replace(params, seed=params.seed + i) if (i and params.seed) else params
-            parts, reason, n = [], "stop", 0
-            async for delta, fin in self._run(prompt_ids, p, stops):
+            parts, reason, n, lps = [], "stop", 0, []
+            async for delta, fin, entries, ntok in self._run(prompt_ids, p, stops):
                 if delta:
                     guard.first_token()
                     parts.append(delta)
-                    n += 1
+                n += ntok
+                lps += entries
                 if fin:
                     reason = fin
-            return "".join(parts), reason, n
+            return "".join(parts), reason, n, lps
 
         try:
             outs = await asyncio.gather(*(one(i) for i in range(n_choices)))
@@ -224,14 +288,18 @@ class OpenAIServer:
         n_tok = sum(o[2] for o in outs)
         guard.complete(len(prompt_ids), n_tok)
         usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": n_tok, "total_tokens": len(prompt_ids) + n_tok}
+        lp = params.logprobs
         if kind == "text":
             return {"id": rid, "object": "text_completion", "created": created, "model": model,
-                    "choices": [{"index": i, "text": t, "finish_reason": r} for i, (t, r, _) in enumerate(outs)],
+                    "choices": [{"index": i, "text": t, "finish_reason": r,
+                                 "logprobs": self._lp_text(e) if lp else None}
+                                for i, (t, r, _, e) in enumerate(outs)],
                     "usage": usage}
         if kind == "chat":
             return {"id": rid, "object": "chat.completion", "created": created, "model": model,
-                    "choices": [{"index": i, "message": {"role": "assistant", "content": t}, "finish_reason": r}
-                                for i, (t, r, _) in enumerate(outs)], "usage": usage}
+                    "choices": [{"index": i, "message": {"role": "assistant", "content": t}, "finish_reason": r,
+                                 "logprobs": self._lp_chat(e) if lp else None}
+                                for i, (t, r, _, e) in enumerate(outs)], "usage": usage}
         return {"id": rid, "object": "response", "created": created, "model": model, "output": outs[0][0],
                 "usage": usage}
 
@@ -244,19 +312,26 @@ class OpenAIServer:
             if kind == "chat":
                 yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model,
                        "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]}
-            async for delta, fin in self._run(prompt_ids, params, stops):
+            offset = 0
+            async for delta, fin, entries, ntok in self._run(prompt_ids, params, stops):
                 if delta:
                     guard.first_token()
-                    n += 1
-                if not delta and not fin:
+                n += ntok
+                if not delta and not fin and not entries:
                     continue
                 if kind == "text":
+                    ch = {"index": 0, "text": delta, "finish_reason": fin}
+                    if params.logprobs:
+                        ch["logprobs"] = self._lp_text(entries, offset)
+                    offset += len(delta)
                     yield {"id": rid, "object": "text_completion.chunk", "created": created, "model": model,
-                           "choices": [{"index": 0, "text": delta, "finish_reason": fin}]}
+                           "choices": [ch]}
                 elif kind == "chat":
+                    ch = {"index": 0, "delta": ({"content": delta} if delta else {}), "finish_reason": fin}
+                    if params.logprobs:
+                        ch["logprobs"] = self._lp_chat(entries)
                     yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model,
-                           "choices": [{"index": 0, "delta": ({"content": delta} if delta else {}),
-                                        "finish_reason": fin}]}
+                           "choices": [ch]}
                 else:
                     yield {"id": rid, "object": "response.chunk", "created": created, "model": model, "output": delta}
             guard.complete(len(prompt_ids), n)

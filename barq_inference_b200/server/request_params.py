@@ -25,8 +25,18 @@ def sampling_params_from_request(body: dict, max_key: str = "max_tokens") -> Sam
         frequency_penalty=float(body.get("frequency_penalty", 0.0)),
         presence_penalty=float(body.get("presence_penalty", 0.0)),
         seed=int(body.get("seed", 0) or 0),
-        logprobs=bool(body.get("logprobs", False)),
     )
+    # chat: logprobs (bool) + top_logprobs (int); completions: logprobs = number of alternatives
+    lp = body.get("logprobs")
+    if isinstance(lp, bool) or lp is None:
+        p.logprobs = bool(lp)
+        p.top_logprobs = int(body.get("top_logprobs", 0) or 0) if p.logprobs else 0
+    elif isinstance(lp, int):
+        p.logprobs, p.top_logprobs = True, lp
+    else:
+        raise ValueError("logprobs must be a boolean or an integer")
+    if not 0 <= p.top_logprobs <= 20:
+        raise ValueError("top_logprobs must be between 0 and 20")
     if p.max_tokens < 1:
         raise ValueError("max_tokens must be >= 1")
     rf = body.get("response_format") or {}

@@ -129,3 +129,43 @@ def test_dp_stream_closed_early_cancels_on_the_replica(dp):
         time.sleep(0.05)
     assert all(r["load"] == 0 for r in dp.replica_info())
     assert not dp._reqs  # nothing left in flight
+
+
+def test_dp_replica_killed_mid_stream_does_not_silence_the_survivor():
+    """A replica killed while it streams tokens (possibly in the middle of a message to the front
+    end) fails only its own requests: each replica writes to its own pipe, so the survivor's
+    stream keeps arriving and finishes."""
+    import queue as q
+    import time
+
+    cfg = preset("tiny", **OVR)
+    front = DataParallelEngine(_factory(), ["cpu", "cpu"], cfg=cfg, affinity_tokens=0, start_timeout=300)
+    try:
+        p = SamplingParams.greedy_params(max_tokens=40)
+        p.ignore_eos = True
+        reqs = [front._submit([3 + i, 4, 5], p, f"r{i}", sink=q.Queue()) for i in range(4)]
+        by_rep = {}
+        for r in reqs:
+            by_rep.setdefault(r.replica, []).append(r)
+        assert set(by_rep) == {0, 1}, "both replicas took requests"
+        victim = front.replicas[0]
+        first = by_rep[0][0].sink.get(timeout=300)  # replica 0 is streaming
+        assert first.token is not None
+        victim.proc.kill()
+        for r in by_rep[1]:  # the survivor's requests run to their end
+            n, deadline = 0, time.monotonic() + 300  # generous: CPU tests may share the cores
+            while True:
+                item = r.sink.get(timeout=max(1.0, deadline - time.monotonic()))
+                if item.token is None:
+                    break
+                n += 1
+            assert item.finish_reason == "length" and n == 40
+        for r in by_rep[0]:  # the victim's requests end: with an error, unless they finished first
+            while True:
+                item = r.sink.get(timeout=300)
+                if item.token is None:
+                    break
+            assert item.finish_reason.startswith("error") or item.finish_reason == "length"
+        assert front.n_alive == 1
+    finally:
+        front.shutdown()

@@ -552,3 +552,53 @@ def test_cli_tokenize(tmp_path):
     assert out["round_trip"] == "Hello, my name is" and out["n_tokens"] == len(out["ids"]) == len(out["pieces"])
     ids = _cli("tokenize", "-m", path, "-p", "Hello, my name is", "--ids-only", "--no-special").stdout.strip()
     assert [int(x) for x in ids.split(",")] == [i for i in out["ids"] if i != 1]
+
+
+def test_http_logprobs(client, tiny_engine):
+    """logprobs / top_logprobs: one entry per generated token with the model's log-softmax; greedy
+    picks the most likely token, so it equals the first alternative; completions carry tokens,
+    token_logprobs, top_logprobs and text offsets, also in SSE chunks."""
+    import math
+
+    body = {"messages": [{"role": "user", "content": "hello"}], "max_tokens": 6, "temperature": 0,
+            "logprobs": True, "top_logprobs": 3}
+    out = client.post("/v1/chat/completions", json=body).json()
+    ch = out["choices"][0]
+    ents = ch["logprobs"]["content"]
+    assert len(ents) == out["usage"]["completion_tokens"] > 0
+    for e in ents:
+        assert e["logprob"] <= 0 and len(e["top_logprobs"]) == 3
+        alts = [a["logprob"] for a in e["top_logprobs"]]
+        assert alts == sorted(alts, reverse=True)
+        assert math.isclose(e["logprob"], alts[0], abs_tol=1e-5)  # greedy = the most likely token
+        assert e["token"] == e["top_logprobs"][0]["token"] and bytes(e["bytes"]).decode("utf-8", "replace") == e["token"]
+    # without logprobs the field is null
+    assert client.post("/v1/chat/completions", json={**body, "logprobs": False}).json()["choices"][0]["logprobs"] is None
+    r = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 5, "temperature": 0.7, "seed": 3,
+                                             "logprobs": 2}).json()
+    lp = r["choices"][0]["logprobs"]
+    n = r["usage"]["completion_tokens"]
+    assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == len(lp["text_offset"]) == n
+    assert all(len(t) <= 2 for t in lp["top_logprobs"]) and lp["text_offset"] == sorted(lp["text_offset"])
+    assert "".join(lp["tokens"]) == r["choices"][0]["text"]
+    # streamed: every chunk carries the entries of its own tokens
+    with client.stream("POST", "/v1/chat/completions", json={**body, "stream": True}) as resp:
+        evs = [json.loads(line[6:]) for line in resp.iter_lines() if line.startswith("data: ") and "[DONE]" not in line]
+    streamed = [e for ev in evs for e in (ev["choices"][0].get("logprobs") or {}).get("content", [])]
+    assert [e["token"] for e in streamed] == [e["token"] for e in ents]
+    assert client.post("/v1/completions", json={"prompt": "x", "logprobs": 21}).status_code == 400
+
+
+def test_http_stop_string_is_never_streamed(client, tiny_engine):
+    """A stop string split across streamed pieces is held back: no chunk contains any part of it."""
+    r = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 24, "temperature": 0}).json()
+    text = r["choices"][0]["text"]
+    if len(text) < 6:
+        pytest.skip("greedy continuation too short for a split stop string")
+    stop = text[3:6]
+    with client.stream("POST", "/v1/completions",
+                       json={"prompt": "hello", "max_tokens": 24, "temperature": 0, "stop": [stop], "stream": True}) as resp:
+        evs = [json.loads(line[6:]) for line in resp.iter_lines() if line.startswith("data: ") and "[DONE]" not in line]
+    pieces = [e["choices"][0]["text"] for e in evs]
+    assert "".join(pieces) == text[:text.find(stop)]
+    assert evs[-1]["choices"][0]["finish_reason"] == "stop"
