@@ -61,6 +61,8 @@ def make_grammar_state(engine, params):
     cache = engine.__dict__.setdefault(_CACHE_ATTR, {})
     if "strings" not in cache:
         tok = getattr(engine, "tokenizer", None)
+        if tok is None:  # without token strings every token would be disallowed
+            raise ValueError("grammar / JSON-mode sampling needs the engine's tokenizer (engine.tokenizer)")
         cache["strings"] = token_strings(tok, engine.cfg.vocab)
     nat = _native_mod()
     if nat is not None:

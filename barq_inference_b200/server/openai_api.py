@@ -32,6 +32,7 @@ from ..tokenizer import ChatTemplate, StreamDecoder
 from ..utils.logging import request_logger
 from .async_engine import AsyncEngine
 from .metrics import InferenceMetrics, context_health
+from .chat_tools import normalize_messages, tool_call_of, tool_names, tool_setup
 from .request_params import DEFAULTS, sampling_params_from_request as _params  # noqa: F401
 
 CORS = {"Access-Control-Allow-Origin": "*", "Access-Control-Allow-Methods": "GET, POST, OPTIONS",
@@ -72,59 +73,16 @@ def _err(status: int, msg: str, kind: str = "invalid_request_error") -> JSONResp
     return JSONResponse({"error": {"message": msg, "type": kind}}, status_code=status, headers=CORS)
 
 
-def _tool_setup(body: dict) -> dict | None:
-    """OpenAI ``tools`` / ``tool_choice``: a system prompt describing the functions, and (when a call
-    is required or a function is named) a JSON schema that constrains the reply to
-    ``{"name": ..., "arguments": {...}}`` for one of them."""
-    tools = body.get("tools")
-    if not tools:
-        return None
-    if not isinstance(tools, list):
-        raise ValueError("tools must be a list")
-    fns = []
-    for t in tools:
-        f = t.get("function", t) if isinstance(t, dict) else None
-        if not isinstance(f, dict) or not f.get("name"):
-            raise ValueError("each tool needs a function with a name")
-        fns.append(f)
-    choice = body.get("tool_choice", "auto")
-    if choice == "none":
-        return None
-    if isinstance(choice, dict):
-        name = (choice.get("function") or {}).get("name")
-        fns_c = [f for f in fns if f["name"] == name]
-        if not fns_c:
-            raise ValueError(f"tool_choice names an unknown function {name!r}")
-    else:
-        fns_c = fns
-    forced = choice == "required" or isinstance(choice, dict)
-    schema = None
-    if forced:
-        alts = [{"type": "object", "properties": {"name": {"const": f["name"]},
-                                                  "arguments": f.get("parameters") or {"type": "object"}},
-                 "required": ["name", "arguments"]} for f in fns_c]
-        schema = alts[0] if len(alts) == 1 else {"anyOf": alts}
-    desc = json.dumps([{"name": f["name"], "description": f.get("description", ""),
-                        "parameters": f.get("parameters", {})} for f in fns])
-    prompt = ("You can call these functions. To call one, reply with only a JSON object "
-              '{"name": <function name>, "arguments": <arguments object>}.\nFunctions: ' + desc)
-    return {"prompt": prompt, "schema": schema, "names": {f["name"] for f in fns}}
-
-
 def _tool_calls(out: dict, body: dict) -> None:
     """Turn chat choices whose text is a function-call object into OpenAI ``tool_calls``."""
-    names = {(t.get("function", t) or {}).get("name") for t in body.get("tools") or [] if isinstance(t, dict)}
+    names = tool_names(body)
     for i, ch in enumerate(out.get("choices", [])):
-        text = (ch.get("message") or {}).get("content") or ""
-        try:
-            obj = json.loads(text)
-        except ValueError:
-            continue
-        if isinstance(obj, dict) and obj.get("name") in names and isinstance(obj.get("arguments"), dict):
+        call = tool_call_of((ch.get("message") or {}).get("content") or "", names)
+        if call is not None:
             ch["message"] = {"role": "assistant", "content": None,
                              "tool_calls": [{"id": f"call_{out['id']}_{i}", "type": "function",
-                                             "function": {"name": obj["name"],
-                                                          "arguments": json.dumps(obj["arguments"])}}]}
+                                             "function": {"name": call["name"],
+                                                          "arguments": json.dumps(call["arguments"])}}]}
             ch["finish_reason"] = "tool_calls"
 
 
@@ -363,21 +321,7 @@ class OpenAIServer:
         return ids
 
     def _chat_prompt(self, messages: Any) -> list[int]:
-        if not isinstance(messages, list) or not messages:
-            raise ValueError("messages must be a non-empty list")
-        msgs = []
-        for m in messages:
-            if not isinstance(m, dict) or ("content" not in m and "tool_calls" not in m):
-                raise ValueError("each message needs role and content")
-            m = dict(m)
-            if m.get("content") is None and m.get("tool_calls"):  # an earlier assistant tool call
-                m["content"] = json.dumps([c.get("function", c) for c in m["tool_calls"]])
-            if m.get("role") == "tool":  # a tool's result goes back to the model as a user turn
-                m = {"role": "user", "content": f"Tool result ({m.get('name') or m.get('tool_call_id', 'tool')}): "
-                                                f"{m.get('content', '')}"}
-            m["content"] = m.get("content") or ""
-            msgs.append(m)
-        text = self.template.render(msgs, add_generation_prompt=True)
+        text = self.template.render(normalize_messages(messages), add_generation_prompt=True)
         return self.tok.encode(text, add_special=not text.startswith(getattr(self.template, "bos_token", "") or "\0"))
 
     # ------------------------------------------------------------------ app
@@ -448,7 +392,7 @@ class OpenAIServer:
                         raise ValueError("prompt must be a string or a list of token ids")
                     params = _params(body)
                 elif kind == "chat":
-                    tools = _tool_setup(body)
+                    tools = tool_setup(body)
                     msgs = body.get("messages")
                     if tools is not None and isinstance(msgs, list):
                         msgs = [{"role": "system", "content": tools["prompt"]}] + list(msgs)

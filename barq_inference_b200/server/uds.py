@@ -11,9 +11,13 @@ frame with ``done: true`` and an ``error`` field.
 
 Additive fields (a client of the reference's protocol neither sends nor needs them): a request may
 carry ``messages`` (OpenAI chat turns, rendered with the server's chat template) instead of
-``prompt``, and the OpenAI sampling fields (``top_k``, ``top_p``, ``min_p``, ``seed``, penalties,
-``response_format``, ``grammar``); the final frame adds ``prompt_tokens`` and ``finish_reason``.
-A client that disconnects mid-stream has its request aborted in the engine.
+``prompt``, the OpenAI sampling fields (``top_k``, ``top_p``, ``min_p``, ``seed``, penalties,
+``response_format``, ``grammar``) and ``tools`` / ``tool_choice``; the final frame adds
+``prompt_tokens``, ``finish_reason`` and, when the reply is a call of one of the tools,
+``tool_call`` ({"name", "arguments"}).  A request ``{"id", "embeddings": input}`` (a string, a list
+of strings, token ids or lists of token ids) is answered by one frame ``{"id", "embeddings":
+[[...]], "prompt_tokens", "done": true}``.  A client that disconnects mid-stream has its request
+aborted in the engine.
 """
 from __future__ import annotations
 
@@ -26,6 +30,7 @@ import threading
 import time
 
 from ..tokenizer import ChatTemplate, StreamDecoder
+from .chat_tools import normalize_messages, tool_call_of, tool_names, tool_setup
 from .request_params import sampling_params_from_request
 
 MAX_FRAME = 16 << 20
@@ -70,15 +75,17 @@ class UDSServer:
         self.sem = threading.BoundedSemaphore(queue_size)
         self._server = None
 
-    def _prompt_ids(self, req: dict) -> list[int]:
+    def _prompt_ids(self, req: dict, tools: dict | None = None) -> list[int]:
         msgs = req.get("messages")
         if msgs is not None:
-            if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and "content" in m for m in msgs):
-                raise ValueError("messages must be a non-empty list of {role, content}")
-            text = self.template.render([dict(m, content=m.get("content") or "") for m in msgs],
-                                        add_generation_prompt=True)
+            msgs = normalize_messages(msgs)
+            if tools is not None:
+                msgs = [{"role": "system", "content": tools["prompt"]}] + msgs
+            text = self.template.render(msgs, add_generation_prompt=True)
             bos = getattr(self.template, "bos_token", "") or "\0"
             return self.tok.encode(text, add_special=not text.startswith(bos))
+        if tools is not None:
+            raise ValueError("tools need chat messages")
         prompt = req["prompt"]
         if isinstance(prompt, list):
             return [int(t) for t in prompt]
@@ -87,15 +94,21 @@ class UDSServer:
     def handle_request(self, conn: socket.socket, req: dict) -> None:
         t0 = time.perf_counter()
         rid = str(req.get("id", ""))
+        if "embeddings" in req:
+            self._embed(conn, req, rid, t0)
+            return
         try:
-            ids = self._prompt_ids(req)
+            tools = tool_setup(req)
+            ids = self._prompt_ids(req, tools)
             params = sampling_params_from_request(req)
+            if tools is not None and tools["schema"] is not None:  # a tool call is required
+                params.json_schema, params.json_mode = tools["schema"], True
         except Exception as e:  # noqa: BLE001 - any failure ends the stream with an error frame
             send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
                               "done": True, "error": f"bad request: {e}"})
             return
         dec = StreamDecoder(self.tok)
-        n, ttft = 0, None
+        n, ttft, text = 0, None, []
         guard = self.metrics.begin() if self.metrics is not None else None
         gen = self.ae.generate_blocking(ids, params, rid)
         try:
@@ -105,16 +118,25 @@ class UDSServer:
                     if guard is not None:
                         guard.complete(len(ids), n)
                         guard = None
-                    send_frame(conn, {"id": rid, "text": dec.flush(), "tokens_generated": n,
-                                      "ttft_ms": int(ttft or 0), "total_time_ms": int((now - t0) * 1e3), "done": True,
-                                      "prompt_tokens": len(ids), "finish_reason": item.finish_reason or "stop"})
+                    tail = dec.flush()
+                    last = {"id": rid, "text": tail, "tokens_generated": n, "ttft_ms": int(ttft or 0),
+                            "total_time_ms": int((now - t0) * 1e3), "done": True, "prompt_tokens": len(ids),
+                            "finish_reason": item.finish_reason or "stop"}
+                    if tools is not None:
+                        call = tool_call_of("".join(text) + tail, tool_names(req))
+                        if call is not None:
+                            last["tool_call"], last["finish_reason"] = call, "tool_calls"
+                    send_frame(conn, last)
                     return
                 n += 1
                 if ttft is None:
                     ttft = (now - t0) * 1e3
                     if guard is not None:
                         guard.first_token()
-                send_frame(conn, {"id": rid, "text": dec.push(item.token), "tokens_generated": n,
+                piece = dec.push(item.token)
+                if tools is not None:
+                    text.append(piece)
+                send_frame(conn, {"id": rid, "text": piece, "tokens_generated": n,
                                   "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
         except OSError:  # the client went away mid-stream: closing the iterator aborts the request
             gen.close()
@@ -131,6 +153,34 @@ class UDSServer:
         finally:
             if guard is not None:  # client went away mid-stream
                 guard.fail()
+
+    def _embed(self, conn: socket.socket, req: dict, rid: str, t0: float) -> None:
+        """One frame with the mean-pooled embeddings of the request's inputs (or an error frame)."""
+        def frame(**kw):
+            return {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0,
+                    "total_time_ms": int((time.perf_counter() - t0) * 1e3), "done": True, **kw}
+
+        try:
+            inp = req["embeddings"]
+            if isinstance(inp, str):
+                batch = [self.tok.encode(inp)]
+            elif isinstance(inp, list) and inp and all(isinstance(t, int) for t in inp):
+                batch = [list(inp)]
+            elif isinstance(inp, list) and inp and all(isinstance(x, str) for x in inp):
+                batch = [self.tok.encode(x) for x in inp]
+            elif isinstance(inp, list) and inp and all(isinstance(x, list) for x in inp):
+                batch = [[int(t) for t in x] for x in inp]
+            else:
+                raise ValueError("embeddings input must be a string, a list of strings or token-id list(s)")
+            if any(not b for b in batch):
+                raise ValueError("empty embeddings input")
+            if not hasattr(self.ae, "call_sync"):
+                raise ValueError("embeddings are not served by this engine front")
+            vecs = self.ae.call_sync(lambda eng: eng.embed(batch))
+        except Exception as e:  # noqa: BLE001 - reported in the frame
+            send_frame(conn, frame(error=f"bad request: {e}" if isinstance(e, (ValueError, KeyError)) else str(e)))
+            return
+        send_frame(conn, frame(embeddings=[v.tolist() for v in vecs], prompt_tokens=sum(len(b) for b in batch)))
 
     def start(self, background: bool = True):
         if os.path.exists(self.path):

@@ -20,9 +20,12 @@
 //   POST /v1/completions         prompt (string or token ids)
 //   POST /v1/chat/completions    messages (rendered by the engine's chat template)
 //   POST /v1/responses           input (string or messages) / prompt / messages, max_output_tokens
+//   POST /v1/embeddings          input (string, strings, token ids or lists of them)
 //   OPTIONS *                    204 with CORS headers
 // Request fields forwarded to the engine: max_tokens, temperature, top_k, top_p, min_p, seed,
-// repetition / frequency / presence penalties, response_format, grammar.  Handled here: stream,
+// repetition / frequency / presence penalties, response_format, grammar, tools / tool_choice (the
+// engine renders the tool prompt and reports a recognized call, returned here as tool_calls).
+// Handled here: stream,
 // stream_options.include_usage, stop (string or list; text is held back while it could still be
 // the start of a stop string, so no stop text is ever sent), n (1..16, not with stream).
 // Errors: 400 invalid request, 404 unknown route, 405 wrong method, 413 / 431 oversized, 429 rate
@@ -400,6 +403,7 @@ bool engine_reachable() {
 struct Gen {
   std::string text;
   std::string finish = "stop";
+  Value tool_call;  // {"name", "arguments"} when the engine recognized a call of one of the tools
   long prompt_tokens = 0, completion_tokens = 0;
   int status = 200;  // non-200: `error` says why
   std::string error;
@@ -493,6 +497,7 @@ Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const 
     if (is_done) {
       if (const Value* p = fr.get("prompt_tokens"); p && p->is_number()) g.prompt_tokens = (long)p->num;
       if (const Value* f = fr.get("finish_reason"); f && f->is_string()) g.finish = f->str;
+      if (const Value* tc = fr.get("tool_call"); tc && tc->is_object()) g.tool_call = *tc;
       if (g.text.size() > sent && !on_delta(g.text.substr(sent))) return g;
       return g;
     }
@@ -509,7 +514,7 @@ struct Call {
   std::string kind;  // "text", "chat", "resp"
   Value uds;         // the engine request
   std::vector<std::string> stops;
-  bool stream = false, include_usage = false;
+  bool stream = false, include_usage = false, tools = false;
   int n = 1;
   std::string model;
 };
@@ -543,8 +548,12 @@ Call translate(const std::string& kind, const Value& body, const std::string& ri
     const Value* m = body.get("messages");
     if (!m) bad("messages must be a non-empty list");
     messages(*m);
-    if (const Value* t = body.get("tools"); t && t->is_array() && !t->arr.empty())
-      bad("tools are served by the Python HTTP front end (barq http-server)");
+    if (const Value* t = body.get("tools"); t && !t->is_null()) {
+      if (!t->is_array()) bad("tools must be a list");
+      c.uds.set("tools", *t);
+      c.tools = !t->arr.empty();
+      if (const Value* tc = body.get("tool_choice"); tc && !tc->is_null()) c.uds.set("tool_choice", *tc);
+    }
   } else {
     if (const Value* m = body.get("messages"); m && !m->is_null()) {
       messages(*m);
@@ -589,6 +598,7 @@ Call translate(const std::string& kind, const Value& body, const std::string& ri
   }
   if (const Value* s = body.get("stream"); s && s->type == Value::kBool) c.stream = s->b;
   if (c.stream && c.n > 1) bad("n > 1 is not supported with stream");
+  if (c.stream && c.tools) bad("stream with tools is not supported; send stream=false");
   if (const Value* so = body.get("stream_options"); so && so->is_object())
     if (const Value* iu = so->get("include_usage"); iu && iu->type == Value::kBool) c.include_usage = iu->b;
   return c;
@@ -755,6 +765,20 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       ch.set("index", Value::number((double)i));
       if (kind == "text") {
         ch.set("text", Value::string(outs[i].text));
+      } else if (outs[i].tool_call.is_object()) {  // the reply is a call of one of the tools
+        Value m = Value::object(), calls = Value::array(), call = Value::object(), fn = Value::object();
+        const Value* name = outs[i].tool_call.get("name");
+        const Value* args = outs[i].tool_call.get("arguments");
+        fn.set("name", name ? *name : Value::string(""));
+        fn.set("arguments", Value::string(args ? barqjson::dump(*args) : "{}"));
+        call.set("id", Value::string("call_" + id + "_" + std::to_string(i)));
+        call.set("type", Value::string("function"));
+        call.set("function", fn);
+        calls.push(call);
+        m.set("role", Value::string("assistant"));
+        m.set("content", Value());
+        m.set("tool_calls", calls);
+        ch.set("message", m);
       } else {
         Value m = Value::object();
         m.set("role", Value::string("assistant"));
@@ -767,6 +791,49 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
     o.set("choices", arr);
   }
   o.set("usage", usage(p_tok, c_tok));
+  respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
+  return Outcome{200, !keep};
+}
+
+Outcome embeddings_route(int fd, const Request& req, bool keep, const std::string& rid) {
+  Value body;
+  try {
+    body = barqjson::parse(req.body);
+  } catch (const std::exception&) {
+    return finish_error(fd, 400, "request body is not valid JSON", keep, rid);
+  }
+  const Value* in = body.is_object() ? body.get("input") : nullptr;
+  if (!in || !(in->is_string() || (in->is_array() && !in->arr.empty())))
+    return finish_error(fd, 400, "input must be a string, a list of strings or token-id list(s)", keep, rid);
+  Value r = Value::object();
+  r.set("id", Value::string(rid));
+  r.set("embeddings", *in);
+  EngineLink link;
+  std::string err;
+  if (!link.open(err)) return finish_error(fd, 502, "engine unavailable: " + err, keep, rid);
+  Value fr;
+  if (!link.send(r) || !link.next(fr, err)) return finish_error(fd, 500, err.empty() ? "send failed" : err, keep, rid);
+  if (const Value* e = fr.get("error"); e && e->is_string()) return finish_error(fd, engine_error_status(e->str), e->str, keep, rid);
+  const Value* vecs = fr.get("embeddings");
+  if (!vecs || !vecs->is_array()) return finish_error(fd, 500, "engine frame without embeddings", keep, rid);
+  Value o = Value::object(), data = Value::array();
+  for (size_t i = 0; i < vecs->arr.size(); ++i) {
+    Value d = Value::object();
+    d.set("object", Value::string("embedding"));
+    d.set("index", Value::number((double)i));
+    d.set("embedding", vecs->arr[i]);
+    data.push(d);
+  }
+  const Value* model = body.get("model");
+  const Value* pt = fr.get("prompt_tokens");
+  const double n = pt && pt->is_number() ? pt->num : 0;
+  Value u = Value::object();
+  u.set("prompt_tokens", Value::number(n));
+  u.set("total_tokens", Value::number(n));
+  o.set("object", Value::string("list"));
+  o.set("model", model && model->is_string() ? *model : Value::string(g_opt.model_id));
+  o.set("data", data);
+  o.set("usage", u);
   respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
   return Outcome{200, !keep};
 }
@@ -796,8 +863,8 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       o.set("object", Value::string("server.info"));
       o.set("model", Value::string(g_opt.model_id));
       o.set("front_end", Value::string("barq-http"));
-      for (const char* e : {"/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions", "/health",
-                            "/metrics"})
+      for (const char* e : {"/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions",
+                            "/v1/embeddings", "/health", "/metrics"})
         eps.push(Value::string(e));
       o.set("endpoints", eps);
       respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
@@ -828,6 +895,14 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       respond(fd, 200, "text/plain; version=0.0.4", g_ctr.prometheus(), keep, rid);
       return Outcome{200, !keep};
     }
+  }
+  if (p == "/v1/embeddings") {
+    if (req.method != "POST") return finish_error(fd, 405, "use POST for " + p, keep, rid);
+    if (!g_limiter.allow(client)) {
+      ++g_ctr.rate_limited;
+      return finish_error(fd, 429, "rate limit exceeded; retry later", keep, rid);
+    }
+    return embeddings_route(fd, req, keep, rid);
   }
   static const std::map<std::string, std::string> kRoutes = {
       {"/v1/completions", "text"}, {"/v1/chat/completions", "chat"}, {"/v1/responses", "resp"}};

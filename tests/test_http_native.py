@@ -59,6 +59,13 @@ class FakeEngine:
                 return
             with self.lock:
                 self.requests.append(req)
+            if "embeddings" in req:
+                inp = req["embeddings"]
+                n = len(inp) if isinstance(inp, list) and inp and not isinstance(inp[0], int) else 1
+                send_frame(conn, {"id": req["id"], "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 1,
+                                  "done": True, "embeddings": [[0.5 + i, -1.25e-3, 1e-30] for i in range(n)],
+                                  "prompt_tokens": 3 * n})
+                return
             key = req.get("prompt")
             if key is None:
                 key = req["messages"][-1]["content"]
@@ -74,8 +81,12 @@ class FakeEngine:
                     time.sleep(0.01)
                 send_frame(conn, {"id": rid, "text": t, "tokens_generated": i + 1, "ttft_ms": 1,
                                   "total_time_ms": 2, "done": False})
-            send_frame(conn, {"id": rid, "text": "", "tokens_generated": len(texts), "ttft_ms": 1,
-                              "total_time_ms": 3, "done": True, **extra})
+            last = {"id": rid, "text": "", "tokens_generated": len(texts), "ttft_ms": 1, "total_time_ms": 3,
+                    "done": True, **extra}
+            if req.get("tools"):
+                last.update(tool_call={"name": "get_weather", "arguments": {"city": "Paris", "days": 2}},
+                            finish_reason="tool_calls")
+            send_frame(conn, last)
         except OSError:
             with self.lock:
                 self.aborted.append(True)
@@ -256,8 +267,11 @@ def test_errors(gateway):
     st, _, b = _req(port, "POST", "/v1/chat/completions", {"messages": []})
     assert st == 400
     st, _, b = _req(port, "POST", "/v1/chat/completions",
-                    {"messages": [{"role": "user", "content": "x"}], "tools": [{"function": {"name": "f"}}]})
+                    {"messages": [{"role": "user", "content": "x"}], "tools": [{"function": {"name": "f"}}],
+                     "stream": True})
     assert st == 400 and "tools" in json.loads(b)["error"]["message"]
+    st, _, b = _req(port, "POST", "/v1/chat/completions", {"messages": [{"role": "user", "content": "x"}], "tools": 3})
+    assert st == 400
     # oversized headers and bodies are refused before any engine call
     n_before = len(eng.requests)
     st, _, _ = _req(port, "POST", "/v1/completions", raw=b"{}", headers={"X-Big": "a" * 40000})
@@ -275,6 +289,29 @@ def test_errors(gateway):
     m = b.decode()
     assert "barq_http_requests_total" in m and "barq_http_client_errors_total" in m
     assert _metric(m, "barq_http_server_errors_total") >= 3 and _metric(m, "barq_http_client_errors_total") >= 10
+
+
+def test_tools_and_embeddings(gateway):
+    eng, port = gateway
+    tools = [{"type": "function", "function": {"name": "get_weather", "parameters": {"type": "object"}}}]
+    body = {"messages": [{"role": "user", "content": "hello"}], "tools": tools, "tool_choice": "required"}
+    st, _, b = _req(port, "POST", "/v1/chat/completions", body)
+    out = json.loads(b)
+    assert st == 200, b
+    assert eng.requests[-1]["tools"] == tools and eng.requests[-1]["tool_choice"] == "required"
+    ch = out["choices"][0]
+    assert ch["finish_reason"] == "tool_calls" and ch["message"]["content"] is None
+    call = ch["message"]["tool_calls"][0]
+    assert call["type"] == "function" and call["function"]["name"] == "get_weather"
+    assert json.loads(call["function"]["arguments"]) == {"city": "Paris", "days": 2}
+    st, _, b = _req(port, "POST", "/v1/embeddings", {"input": ["a", "b"], "model": "e5"})
+    out = json.loads(b)
+    assert st == 200 and out["object"] == "list" and out["model"] == "e5"
+    assert [d["index"] for d in out["data"]] == [0, 1] and out["data"][1]["embedding"] == [1.5, -1.25e-3, 1e-30]
+    assert out["usage"] == {"prompt_tokens": 6, "total_tokens": 6}
+    assert eng.requests[-1]["embeddings"] == ["a", "b"]
+    assert _req(port, "POST", "/v1/embeddings", {"input": 5})[0] == 400
+    assert _req(port, "GET", "/v1/embeddings")[0] == 405
 
 
 def test_keep_alive_and_client_disconnect(gateway):
@@ -324,9 +361,10 @@ def test_against_real_uds_server_and_cpu_engine(tmp_path):
     from barq_inference_b200.server.uds import UDSClient, UDSServer
     from barq_inference_b200.tokenizer import synthetic_tokenizer
 
-    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=256)
-    eng = CPUEngine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=0), max_model_len=256)
+    cfg = preset("tiny", n_layers=1, vocab=600, max_ctx=2048)
+    eng = CPUEngine(cfg, random_tensors(cfg, POLICIES["tiny"], seed=0), max_model_len=2048)
     tok = synthetic_tokenizer(cfg.vocab)
+    eng.tokenizer = tok  # token strings for grammar-constrained (tool call) sampling
     path = str(tmp_path / "real.sock")
     ae = AsyncEngine(eng)
     srv = UDSServer(ae, tok, path).start()
@@ -346,8 +384,26 @@ def test_against_real_uds_server_and_cpu_engine(tmp_path):
                          "stream": True})
         ev = _events(b)
         assert st == 200 and ev[0]["choices"][0]["delta"] == {"role": "assistant"}
-        st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "x " * 400, "max_tokens": 100})
+        st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "x " * 2000, "max_tokens": 100})
         assert st == 400 and "max_model_len" in json.loads(b)["error"]["message"]
+        # embeddings through the engine: one vector per input, same as the engine's own
+        st, _, b = _req(port, "POST", "/v1/embeddings", {"input": ["hello", "world wide"]})
+        out = json.loads(b)
+        want = eng.embed([tok.encode("hello"), tok.encode("world wide")])
+        assert st == 200 and len(out["data"]) == 2
+        assert max(abs(a - float(b_)) for a, b_ in zip(out["data"][1]["embedding"], want[1].tolist())) < 1e-6
+        # a required tool call: the engine constrains the reply to the function's schema
+        tools = [{"type": "function", "function": {"name": "lookup", "parameters": {
+            "type": "object", "properties": {"q": {"type": "string", "maxLength": 4}}, "required": ["q"]}}}]
+        st, _, b = _req(port, "POST", "/v1/chat/completions",
+                        {"messages": [{"role": "user", "content": "find"}], "tools": tools,
+                         "tool_choice": "required", "max_tokens": 60, "temperature": 0})
+        out = json.loads(b)
+        assert st == 200, b
+        calls = out["choices"][0]["message"].get("tool_calls")
+        if out["choices"][0]["finish_reason"] != "length":  # a complete call within the token budget
+            assert calls and calls[0]["function"]["name"] == "lookup"
+            assert "q" in json.loads(calls[0]["function"]["arguments"])
     finally:
         p.kill()
         p.wait()
