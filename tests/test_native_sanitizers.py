@@ -343,12 +343,15 @@ def test_http_front_end_under_asan_ubsan(tmp_path):
                          stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env)
     port = int(p.stdout.readline().decode().split("127.0.0.1:")[1].split()[0])
     bodies = [{"prompt": "x", "stop": ["<end>"], "stream": True}, {"messages": [{"role": "user", "content": "y"}]},
-              {"input": [{"role": "user", "content": "z"}], "n": 2}, {"prompt": [1, 2, 3], "max_tokens": 4}]
+              {"input": [{"role": "user", "content": "z"}], "n": 2}, {"prompt": [1, 2, 3], "max_tokens": 4},
+              {"messages": [{"role": "user", "content": "t"}], "tools": [{"function": {"name": "f"}}]},
+              {"input": ["a", "b"]}]
     for case in range(300):
         body = json.dumps(rng.choice(bodies)).encode()
         if case % 2:
             body = mutate(body)
-        route = rng.choice([b"/v1/completions", b"/v1/chat/completions", b"/v1/responses", b"/health", b"/x"])
+        route = rng.choice([b"/v1/completions", b"/v1/chat/completions", b"/v1/responses", b"/v1/embeddings",
+                            b"/health", b"/x"])
         req = b"POST " + route + b" HTTP/1.1\r\nContent-Type: application/json\r\nContent-Length: " + \
             str(len(body)).encode() + b"\r\nConnection: close\r\n\r\n" + body
         if case % 5 == 3:
