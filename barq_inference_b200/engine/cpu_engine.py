@@ -189,4 +189,5 @@ class CPUEngine:
 
     def _result(self, s: Sequence) -> GenerationResult:
         return GenerationResult(s.prompt, s.output, s.finish_reason or "", s.ttft,
-                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs)
+                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs,
+                                s.top_logprobs)

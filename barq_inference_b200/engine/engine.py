@@ -76,6 +76,7 @@ class GenerationResult:
     ttft_s: float | None
     latency_s: float
     logprobs: list[float] = field(default_factory=list)
+    top_logprobs: list[list[tuple[int, float]]] = field(default_factory=list)
 
 
 class _GraphBucket:
@@ -186,7 +187,7 @@ class Engine:
 
     def _result(self, s: Sequence) -> GenerationResult:
         return GenerationResult(s.prompt, s.output, s.finish_reason or "", s.ttft,
-                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs)
+                                (s.finish_time or time.perf_counter()) - s.arrival, s.logprobs, s.top_logprobs)
 
     # ------------------------------------------------------------------ one engine step
     def step(self) -> list[Sequence]:

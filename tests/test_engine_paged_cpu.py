@@ -498,3 +498,27 @@ def test_data_parallel_replicas_of_two_rank_groups():
         assert all(r["served"] > 0 for r in front.replica_info())
     finally:
         front.shutdown()
+
+
+def test_logprobs_of_the_rows_that_ask_for_them():
+    """Rows with ``logprobs`` record log-softmax(raw logits)[token] (and the top alternatives) at every
+    generated token, equal to the fp32 reference's; rows without it record nothing."""
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=8)
+    ref = ReferenceModel(cfg, t)
+    eng = _engine(cfg, t, num_blocks=64, max_num_batched_tokens=128, max_num_seqs=4)
+    prompts = _prompts(cfg, 3, 9)
+    with_lp = dataclasses.replace(SamplingParams.greedy_params(max_tokens=6), logprobs=True, top_logprobs=3)
+    params = [with_lp, SamplingParams.greedy_params(max_tokens=6), with_lp]
+    res = eng.generate(prompts, params)
+    assert res[1].logprobs == [] and res[1].top_logprobs == []
+    for i in (0, 2):
+        r = res[i]
+        assert len(r.logprobs) == len(r.tokens) == 6 and all(len(x) == 3 for x in r.top_logprobs)
+        cache: dict = {}
+        logits = ref.forward(prompts[i], cache)[-1]
+        for tok, lp, top in zip(r.tokens, r.logprobs, r.top_logprobs):
+            lsm = torch.log_softmax(logits.float(), -1)
+            assert abs(lp - float(lsm[tok])) < 1e-3
+            assert [a for a, _ in top] == lsm.topk(3).indices.tolist()
+            logits = ref.forward([tok], cache)[-1]
