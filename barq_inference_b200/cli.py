@@ -627,8 +627,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--port", type=int, default=8000)
     p.add_argument("--rate-limit-rpm", type=int, default=60)
     p.add_argument("--native-front-end", action="store_true",
-                   help="serve HTTP from the C++ front end barq-http (engine behind a private UDS socket); "
-                        "logprobs need the default Python server")
+                   help="serve HTTP from the C++ front end barq-http (engine behind a private UDS socket)")
     p.set_defaults(fn=cmd_http_server)
 
     sub.add_parser("metal-info").set_defaults(fn=cmd_metal_info)

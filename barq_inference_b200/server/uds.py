@@ -14,7 +14,8 @@ carry ``messages`` (OpenAI chat turns, rendered with the server's chat template)
 ``prompt``, the OpenAI sampling fields (``top_k``, ``top_p``, ``min_p``, ``seed``, penalties,
 ``response_format``, ``grammar``) and ``tools`` / ``tool_choice``; the final frame adds
 ``prompt_tokens``, ``finish_reason`` and, when the reply is a call of one of the tools,
-``tool_call`` ({"name", "arguments"}).  A request ``{"id", "embeddings": input}`` (a string, a list
+``tool_call`` ({"name", "arguments"}); with ``logprobs`` / ``top_logprobs`` every token frame
+carries ``logprobs`` = [{token, bytes, logprob, top: [{token, bytes, logprob}, ...]}].  A request ``{"id", "embeddings": input}`` (a string, a list
 of strings, token ids or lists of token ids) is answered by one frame ``{"id", "embeddings":
 [[...]], "prompt_tokens", "done": true}``.  A client that disconnects mid-stream has its request
 aborted in the engine.
@@ -136,8 +137,13 @@ class UDSServer:
                 piece = dec.push(item.token)
                 if tools is not None:
                     text.append(piece)
-                send_frame(conn, {"id": rid, "text": piece, "tokens_generated": n,
-                                  "ttft_ms": int(ttft), "total_time_ms": int((now - t0) * 1e3), "done": False})
+                fr = {"id": rid, "text": piece, "tokens_generated": n, "ttft_ms": int(ttft),
+                      "total_time_ms": int((now - t0) * 1e3), "done": False}
+                if params.logprobs:
+                    e = self._lp_entry(item, n - 1, params)
+                    if e is not None:
+                        fr["logprobs"] = [e]
+                send_frame(conn, fr)
         except OSError:  # the client went away mid-stream: closing the iterator aborts the request
             gen.close()
         except Exception as e:  # noqa: BLE001 - a failed request still gets its final frame
@@ -153,6 +159,25 @@ class UDSServer:
         finally:
             if guard is not None:  # client went away mid-stream
                 guard.fail()
+
+    def _lp_entry(self, item, idx: int, params) -> dict | None:
+        """{token, bytes, logprob, top: [{token, bytes, logprob}]} of the idx-th generated token, from
+        the engine's per-sequence record; None for an end-of-sequence token or when nothing was
+        recorded."""
+        cfg = getattr(getattr(self.ae, "engine", None), "cfg", None) or getattr(self.ae, "cfg", None)
+        if cfg is not None and item.token in cfg.eos_ids and not params.ignore_eos:
+            return None
+        lps = getattr(item.seq, "logprobs", None)
+        if not lps or idx >= len(lps):
+            return None
+        tops = getattr(item.seq, "top_logprobs", None) or []
+
+        def tok(tid):
+            b = self.tok.token_bytes(tid) if hasattr(self.tok, "token_bytes") else self.tok.decode([tid]).encode()
+            return {"token": b.decode("utf-8", errors="replace"), "bytes": list(b)}
+
+        return {**tok(item.token), "logprob": float(lps[idx]),
+                "top": [{**tok(a), "logprob": float(v)} for a, v in (tops[idx] if idx < len(tops) else [])]}
 
     def _embed(self, conn: socket.socket, req: dict, rid: str, t0: float) -> None:
         """One frame with the mean-pooled embeddings of the request's inputs (or an error frame)."""

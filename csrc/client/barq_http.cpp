@@ -25,9 +25,10 @@
 // Request fields forwarded to the engine: max_tokens, temperature, top_k, top_p, min_p, seed,
 // repetition / frequency / presence penalties, response_format, grammar, tools / tool_choice (the
 // engine renders the tool prompt and reports a recognized call, returned here as tool_calls).
-// Handled here: stream,
-// stream_options.include_usage, stop (string or list; text is held back while it could still be
-// the start of a stop string, so no stop text is ever sent), n (1..16, not with stream).
+// logprobs / top_logprobs are forwarded too and the engine's per-token entries come back as the
+// OpenAI chat or completions logprob objects.  Handled here: stream, stream_options.include_usage,
+// stop (string or list; text is held back while it could still be the start of a stop string, so
+// no stop text is ever sent), n (1..16, not with stream).
 // Errors: 400 invalid request, 404 unknown route, 405 wrong method, 413 / 431 oversized, 429 rate
 // limited, 502 engine unreachable, 503 engine queue full or connection limit, 500 engine failure;
 // the body is {"error": {"message", "type"}} as in the Python server.
@@ -404,6 +405,7 @@ struct Gen {
   std::string text;
   std::string finish = "stop";
   Value tool_call;  // {"name", "arguments"} when the engine recognized a call of one of the tools
+  std::vector<Value> lps;  // per-token logprob entries of the text returned (non-streamed calls)
   long prompt_tokens = 0, completion_tokens = 0;
   int status = 200;  // non-200: `error` says why
   std::string error;
@@ -442,7 +444,7 @@ int engine_error_status(const std::string& msg) {
 // when the engine refuses the request), `on_delta` with every piece of text that can no longer be
 // part of a stop string; either returning false (client gone) ends the generation early.
 Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const std::function<bool()>& on_first,
-             const std::function<bool(const std::string&)>& on_delta) {
+             const std::function<bool(const std::string&, std::vector<Value>&)>& on_delta) {
   Gen g;
   EngineLink link;
   std::string err;
@@ -459,6 +461,13 @@ Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const 
   }
   size_t sent = 0;  // bytes of g.text already handed to on_delta
   bool first = true;
+  std::vector<Value> pend;  // logprob entries of tokens whose text has not been handed out yet
+  auto emit = [&](const std::string& d) {
+    for (auto& e : pend) g.lps.push_back(e);
+    const bool ok = on_delta(d, pend);
+    pend.clear();
+    return ok;
+  };
   for (;;) {
     Value fr;
     if (!link.next(fr, err)) {
@@ -476,6 +485,8 @@ Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const 
     }
     const Value* t = fr.get("text");
     const std::string piece = t && t->is_string() ? t->str : "";
+    if (const Value* lp = fr.get("logprobs"); lp && lp->is_array())
+      for (const auto& e : lp->arr) pend.push_back(e);
     if (const Value* n = fr.get("tokens_generated"); n && n->is_number()) g.completion_tokens = (long)n->num;
     if (first && (!piece.empty() || is_done)) {
       first = false;
@@ -491,19 +502,19 @@ Gen generate(const Value& uds_req, const std::vector<std::string>& stops, const 
     if (hit != std::string::npos) {
       g.text.resize(hit);
       g.finish = "stop";
-      if (hit > sent && !on_delta(g.text.substr(sent))) return g;
+      if (hit > sent) emit(g.text.substr(sent));
       return g;  // closing the link aborts the request in the engine
     }
     if (is_done) {
       if (const Value* p = fr.get("prompt_tokens"); p && p->is_number()) g.prompt_tokens = (long)p->num;
       if (const Value* f = fr.get("finish_reason"); f && f->is_string()) g.finish = f->str;
       if (const Value* tc = fr.get("tool_call"); tc && tc->is_object()) g.tool_call = *tc;
-      if (g.text.size() > sent && !on_delta(g.text.substr(sent))) return g;
+      if (g.text.size() > sent || !pend.empty()) emit(g.text.substr(sent));
       return g;
     }
     const size_t safe = g.text.size() - (stops.empty() ? 0 : held_suffix(g.text, stops));
     if (safe > sent) {
-      if (!on_delta(g.text.substr(sent, safe - sent))) return g;
+      if (!emit(g.text.substr(sent, safe - sent))) return g;
       sent = safe;
     }
   }
@@ -514,7 +525,7 @@ struct Call {
   std::string kind;  // "text", "chat", "resp"
   Value uds;         // the engine request
   std::vector<std::string> stops;
-  bool stream = false, include_usage = false, tools = false;
+  bool stream = false, include_usage = false, tools = false, logprobs = false;
   int n = 1;
   std::string model;
 };
@@ -580,6 +591,16 @@ Call translate(const std::string& kind, const Value& body, const std::string& ri
     if (numeric && !v->is_number()) bad(std::string(k) + " must be a number");
     c.uds.set(k, *v);
   }
+  if (const Value* lp = body.get("logprobs"); lp && !lp->is_null()) {
+    if (lp->type == Value::kBool) c.logprobs = lp->b;
+    else if (lp->is_integer() && lp->num >= 0 && lp->num <= 20) c.logprobs = true;
+    else bad("logprobs must be a boolean or an integer (0..20)");
+    c.uds.set("logprobs", *lp);
+    if (const Value* tl = body.get("top_logprobs"); tl && !tl->is_null()) {
+      if (!tl->is_integer() || tl->num < 0 || tl->num > 20) bad("top_logprobs must be between 0 and 20");
+      c.uds.set("top_logprobs", *tl);
+    }
+  }
   if (const Value* s = body.get("stop"); s && !s->is_null()) {
     if (s->is_string()) {
       c.stops.push_back(s->str);
@@ -616,6 +637,61 @@ Value usage(long p, long c) {
   u.set("completion_tokens", Value::number((double)c));
   u.set("total_tokens", Value::number((double)(p + c)));
   return u;
+}
+
+// OpenAI logprob objects from the engine's entries {token, bytes, logprob, top: [...]}.
+Value lp_chat(const std::vector<Value>& ents) {
+  Value content = Value::array();
+  for (const auto& e : ents) {
+    Value o = Value::object(), tops = Value::array();
+    for (const char* k : {"token", "logprob", "bytes"})
+      if (const Value* v = e.get(k)) o.set(k, *v);
+    if (const Value* t = e.get("top"); t && t->is_array())
+      for (const auto& a : t->arr) {
+        Value x = Value::object();
+        for (const char* k : {"token", "logprob", "bytes"})
+          if (const Value* v = a.get(k)) x.set(k, *v);
+        tops.push(x);
+      }
+    o.set("top_logprobs", tops);
+    content.push(o);
+  }
+  Value r = Value::object();
+  r.set("content", content);
+  return r;
+}
+
+Value lp_text(const std::vector<Value>& ents, size_t& offset) {
+  Value toks = Value::array(), lps = Value::array(), tops = Value::array(), offs = Value::array();
+  bool any_top = false;
+  for (const auto& e : ents) {
+    const Value* t = e.get("token");
+    const std::string tok = t && t->is_string() ? t->str : "";
+    toks.push(Value::string(tok));
+    const Value* lp = e.get("logprob");
+    lps.push(lp ? *lp : Value());
+    const Value* top = e.get("top");
+    if (top && top->is_array() && !top->arr.empty()) {
+      any_top = true;
+      Value m = Value::object();
+      for (const auto& a : top->arr) {
+        const Value* at = a.get("token");
+        const Value* al = a.get("logprob");
+        m.set(at && at->is_string() ? at->str : "", al ? *al : Value());
+      }
+      tops.push(m);
+    } else {
+      tops.push(Value());
+    }
+    offs.push(Value::number((double)offset));
+    offset += tok.size();
+  }
+  Value r = Value::object();
+  r.set("tokens", toks);
+  r.set("token_logprobs", lps);
+  r.set("top_logprobs", any_top ? tops : Value());
+  r.set("text_offset", offs);
+  return r;
 }
 
 Value chunk(const Call& c, const std::string& id, long created, const std::string* delta, const std::string* finish,
@@ -699,7 +775,14 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       if (client_ok && kind == "chat") send_event(chunk(c, id, created, nullptr, nullptr, true));
       return client_ok;
     };
-    auto on_delta = [&](const std::string& d) { return send_event(chunk(c, id, created, &d, nullptr, false)); };
+    size_t offset = 0;
+    auto on_delta = [&](const std::string& d, std::vector<Value>& ents) {
+      Value ev = chunk(c, id, created, &d, nullptr, false);
+      if (c.logprobs && kind != "resp")
+        for (auto& kv : ev.obj)
+          if (kv.first == "choices") kv.second.arr[0].set("logprobs", kind == "chat" ? lp_chat(ents) : lp_text(ents, offset));
+      return send_event(ev);
+    };
     Gen g = generate(c.uds, c.stops, on_first, on_delta);
     if (!headers_sent) {
       if (g.status != 200) return finish_error(fd, g.status, g.error, keep, rid);
@@ -737,7 +820,7 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       r.set("id", Value::string(rid + "-" + std::to_string(i)));
     }
     auto run = [&outs, &c, i](Value req) {
-      outs[i] = generate(req, c.stops, [] { return true; }, [](const std::string&) { return true; });
+      outs[i] = generate(req, c.stops, [] { return true; }, [](const std::string&, std::vector<Value>&) { return true; });
     };
     if (i + 1 < c.n) workers.emplace_back(run, std::move(r));
     else run(std::move(r));
@@ -786,6 +869,12 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
         ch.set("message", m);
       }
       ch.set("finish_reason", Value::string(outs[i].finish));
+      if (c.logprobs) {
+        size_t off = 0;
+        ch.set("logprobs", kind == "chat" ? lp_chat(outs[i].lps) : lp_text(outs[i].lps, off));
+      } else {
+        ch.set("logprobs", Value());
+      }
       arr.push(ch);
     }
     o.set("choices", arr);

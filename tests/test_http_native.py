@@ -176,7 +176,7 @@ def test_completion_translation_both_ways(gateway):
     assert h["x-request-id"] == "abc-123"
     out = json.loads(b)
     assert out["object"] == "text_completion" and out["id"].startswith("cmpl-") and out["model"] == "tiny-x"
-    assert out["choices"] == [{"index": 0, "text": "Hello world", "finish_reason": "length"}]
+    assert out["choices"] == [{"index": 0, "text": "Hello world", "finish_reason": "length", "logprobs": None}]
     assert out["usage"] == {"prompt_tokens": 3, "completion_tokens": 4, "total_tokens": 7}
     sent = eng.requests[-1]
     assert sent == {"id": "abc-123", "prompt": "hello", "max_tokens": 7, "temperature": 0.25, "top_k": 5,
@@ -238,7 +238,7 @@ def test_stop_strings_are_never_sent(gateway):
     assert "".join(texts) == "abc" and all("<" not in t for t in texts)
     assert ev[-1]["choices"][0]["finish_reason"] == "stop"
     st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "stop", "stop": "<end>"})
-    assert json.loads(b)["choices"][0] == {"index": 0, "text": "abc", "finish_reason": "stop"}
+    assert json.loads(b)["choices"][0] == {"index": 0, "text": "abc", "finish_reason": "stop", "logprobs": None}
     # a held-back prefix that never completes the stop string is released at the end
     st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "near", "stop": ["<end>"], "stream": True})
     assert "".join(e["choices"][0]["text"] for e in _events(b)) == "x<ey"
@@ -386,6 +386,20 @@ def test_against_real_uds_server_and_cpu_engine(tmp_path):
         assert st == 200 and ev[0]["choices"][0]["delta"] == {"role": "assistant"}
         st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "x " * 2000, "max_tokens": 100})
         assert st == 400 and "max_model_len" in json.loads(b)["error"]["message"]
+        # logprobs through the engine: one entry per generated token, greedy = the top alternative
+        st, _, b = _req(port, "POST", "/v1/chat/completions",
+                        {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 5, "temperature": 0,
+                         "logprobs": True, "top_logprobs": 2})
+        out = json.loads(b)
+        ents = out["choices"][0]["logprobs"]["content"]
+        assert st == 200 and len(ents) == out["usage"]["completion_tokens"] - (out["choices"][0]["finish_reason"] == "stop")
+        for e in ents:
+            assert len(e["top_logprobs"]) == 2 and abs(e["logprob"] - e["top_logprobs"][0]["logprob"]) < 1e-5
+        st, _, b = _req(port, "POST", "/v1/completions",
+                        {"prompt": "hello", "max_tokens": 4, "temperature": 0, "logprobs": 1, "stream": True})
+        evs = _events(b)
+        toks = [t for ev in evs for t in ((ev["choices"][0].get("logprobs") or {}).get("tokens") or [])]
+        assert "".join(toks) == "".join(ev["choices"][0]["text"] for ev in evs)
         # embeddings through the engine: one vector per input, same as the engine's own
         st, _, b = _req(port, "POST", "/v1/embeddings", {"input": ["hello", "world wide"]})
         out = json.loads(b)
