@@ -8,6 +8,8 @@
 //
 //   barq-uds [--socket PATH] [--id ID] [--max-tokens N] [--temperature T] [--repeat R] [--json]
 //            [--quiet] PROMPT
+//   barq-uds --chat [--system TEXT] ...   interactive chat: one user turn per stdin line, the history
+//            sent as OpenAI messages (rendered by the server's chat template); /exit ends it
 //
 // The generated text streams to stdout as frames arrive (or, with --json, every frame's JSON one
 // per line).  A summary line goes to stderr: tokens, TTFT and total time of each request, and for
@@ -272,7 +274,8 @@ struct Options {
   long max_tokens = 128;
   double temperature = 0.8;
   long repeat = 1;
-  bool json = false, quiet = false;
+  bool json = false, quiet = false, chat = false;
+  std::string system;
 };
 
 struct Result {
@@ -281,10 +284,12 @@ struct Result {
   std::string error;
 };
 
-Result run_request(int fd, const Options& o, const std::string& rid) {
+// `input` is the request's prompt member: "\"prompt\":..." or "\"messages\":[...]" (JSON text).
+Result run_request(int fd, const Options& o, const std::string& rid, const std::string& input,
+                   std::string* reply = nullptr) {
   char num[64];
-  std::string req = "{\"id\":" + json_quote(rid) + ",\"prompt\":" + json_quote(o.prompt) + ",\"max_tokens\":" +
-                    std::to_string(o.max_tokens) + ",\"temperature\":";
+  std::string req = "{\"id\":" + json_quote(rid) + "," + input + ",\"max_tokens\":" + std::to_string(o.max_tokens) +
+                    ",\"temperature\":";
   std::snprintf(num, sizeof num, "%.17g", o.temperature);
   req += num;
   req += "}";
@@ -304,6 +309,7 @@ Result run_request(int fd, const Options& o, const std::string& rid) {
     } else if (const JsonValue* t = get("text"); t && t->kind == JsonValue::kString && !o.quiet) {
       std::fwrite(t->str.data(), 1, t->str.size(), stdout);
     }
+    if (const JsonValue* t = get("text"); reply && t && t->kind == JsonValue::kString) *reply += t->str;
     std::fflush(stdout);
     if (const JsonValue* v = get("tokens_generated"); v && v->kind == JsonValue::kNumber) res.tokens = (long)v->num;
     if (const JsonValue* v = get("ttft_ms"); v && v->kind == JsonValue::kNumber) res.ttft_ms = v->num;
@@ -327,7 +333,9 @@ double percentile(std::vector<double> v, double p) {
   if (msg) std::fprintf(stderr, "barq-uds: %s\n", msg);
   std::fprintf(stderr,
                "usage: barq-uds [--socket PATH] [--id ID] [--max-tokens N] [--temperature T] [--repeat R]\n"
-               "                [--json] [--quiet] PROMPT\n");
+               "                [--json] [--quiet] PROMPT\n"
+               "       barq-uds --chat [--system TEXT] [--socket PATH] [--max-tokens N] [--temperature T]\n"
+               "                (one user turn per stdin line; the server renders the chat template)\n");
   std::exit(2);
 }
 
@@ -353,12 +361,15 @@ Options parse(int argc, char** argv) {
     else if (a == "--repeat") o.repeat = (long)num(arg(), true);
     else if (a == "--json") o.json = true;
     else if (a == "--quiet") o.quiet = true;
+    else if (a == "--chat") o.chat = true;
+    else if (a == "--system") o.system = arg();
     else if (a == "-h" || a == "--help") usage(nullptr);
     else if (!a.empty() && a[0] == '-' && a != "-") usage(("unknown option " + a).c_str());
     else if (have_prompt) usage("more than one prompt");
     else o.prompt = a, have_prompt = true;
   }
-  if (!have_prompt) usage("no prompt");
+  if (!have_prompt && !o.chat) usage("no prompt");
+  if (o.chat && (have_prompt || o.repeat != 1)) usage("--chat reads its turns from stdin (no PROMPT, no --repeat)");
   if (o.max_tokens < 0 || o.repeat < 1) usage("--max-tokens must be >= 0 and --repeat >= 1");
   return o;
 }
@@ -376,12 +387,52 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "barq-uds: cannot connect to %s: %s\n", o.socket_path.c_str(), std::strerror(errno));
     return 2;
   }
+  if (o.chat) {  // interactive multi-turn chat: the history travels as OpenAI messages
+    std::vector<std::pair<std::string, std::string>> turns;
+    if (!o.system.empty()) turns.emplace_back("system", o.system);
+    int status = 0;
+    char* line = nullptr;
+    size_t cap = 0;
+    ssize_t n;
+    long turn = 0;
+    try {
+      while ((n = getline(&line, &cap, stdin)) >= 0) {
+        std::string text(line, (size_t)n);
+        while (!text.empty() && (text.back() == '\n' || text.back() == '\r')) text.pop_back();
+        if (text == "/exit" || text == "/quit") break;
+        if (text.empty()) continue;
+        turns.emplace_back("user", text);
+        std::string msgs = "\"messages\":[";
+        for (size_t i = 0; i < turns.size(); ++i)
+          msgs += (i ? ",{\"role\":" : "{\"role\":") + json_quote(turns[i].first) + ",\"content\":" +
+                  json_quote(turns[i].second) + "}";
+        msgs += "]";
+        std::string reply;
+        const Result res = run_request(fd, o, o.id + "-" + std::to_string(turn++), msgs, &reply);
+        if (!o.json && !o.quiet) std::fputc('\n', stdout);
+        std::fflush(stdout);
+        if (!res.error.empty()) {
+          std::fprintf(stderr, "barq-uds: error=%s\n", res.error.c_str());
+          turns.pop_back();  // the failed turn is not part of the conversation
+          status = 1;
+          continue;
+        }
+        turns.emplace_back("assistant", reply);
+      }
+    } catch (const std::exception& e) {
+      std::fprintf(stderr, "barq-uds: %s\n", e.what());
+      status = 2;
+    }
+    std::free(line);
+    ::close(fd);
+    return status;
+  }
   std::vector<double> ttft, rate;
   int status = 0;
   try {
     for (long r = 0; r < o.repeat; ++r) {
       const std::string rid = o.repeat == 1 ? o.id : o.id + "-" + std::to_string(r);
-      const Result res = run_request(fd, o, rid);
+      const Result res = run_request(fd, o, rid, "\"prompt\":" + json_quote(o.prompt));
       if (!o.json && !o.quiet) std::fputc('\n', stdout);
       std::fprintf(stderr, "[%s] tokens=%ld ttft_ms=%.0f total_ms=%.0f%s%s\n", rid.c_str(), res.tokens, res.ttft_ms,
                    res.total_ms, res.error.empty() ? "" : " error=", res.error.c_str());

@@ -602,3 +602,54 @@ def test_http_stop_string_is_never_streamed(client, tiny_engine):
     pieces = [e["choices"][0]["text"] for e in evs]
     assert "".join(pieces) == text[:text.find(stop)]
     assert evs[-1]["choices"][0]["finish_reason"] == "stop"
+
+
+def test_native_uds_client_chat_mode(tmp_path):
+    """barq-uds --chat: one user turn per stdin line, the whole history (system, user, assistant
+    replies) sent as OpenAI messages; a failed turn is dropped from the history."""
+    import shutil
+    import threading
+
+    from barq_inference_b200.server.uds import recv_frame, send_frame
+    from barq_inference_b200.server.uds_native import build_client
+
+    if shutil.which("g++") is None and shutil.which("c++") is None:
+        pytest.skip("no C++ compiler")
+    exe = build_client()
+    path = str(tmp_path / "chat.sock")
+    seen = []
+    lsock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    lsock.bind(path)
+    lsock.listen(1)
+
+    def serve():
+        conn, _ = lsock.accept()
+        while True:
+            req = recv_frame(conn)
+            if req is None:
+                break
+            seen.append(req)
+            last = req["messages"][-1]["content"]
+            if last == "fail":
+                send_frame(conn, {"id": req["id"], "text": "", "done": True, "error": "queue full"})
+                continue
+            for i, t in enumerate(["re: ", last]):
+                send_frame(conn, {"id": req["id"], "text": t, "tokens_generated": i + 1, "done": False})
+            send_frame(conn, {"id": req["id"], "text": "", "tokens_generated": 2, "done": True})
+        conn.close()
+
+    th = threading.Thread(target=serve, daemon=True)
+    th.start()
+    r = subprocess.run([exe, "--socket", path, "--chat", "--system", "be brief", "--max-tokens", "9"],
+                       input="hello\nfail\nagain é\n/exit\nignored\n".encode(), capture_output=True, timeout=60)
+    th.join(10)
+    lsock.close()
+    assert r.returncode == 1, r.stderr  # one turn failed
+    assert r.stdout.decode() == "re: hello\n\nre: again é\n"
+    assert [q["messages"] for q in seen] == [
+        [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"}],
+        [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"},
+         {"role": "assistant", "content": "re: hello"}, {"role": "user", "content": "fail"}],
+        [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"},
+         {"role": "assistant", "content": "re: hello"}, {"role": "user", "content": "again é"}]]
+    assert all(q["max_tokens"] == 9 for q in seen)
