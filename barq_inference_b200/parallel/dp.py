@@ -116,6 +116,10 @@ def _replica_main(idx: int, device: str, factory: Callable[[str], Any], inq, out
             if tok < 0:
                 events.append((rid, None, seq.finish_reason or "stop"))
                 live.pop(rid, None)
+            elif seq.params.logprobs and len(seq.logprobs) >= len(seq.output):
+                i = len(seq.output) - 1  # this token's record (the engine records before the callback)
+                tops = seq.top_logprobs[i] if i < len(seq.top_logprobs) else []
+                events.append((rid, int(tok), None, (float(seq.logprobs[i]), [(int(a), float(v)) for a, v in tops])))
             else:
                 events.append((rid, int(tok), None))
 
@@ -191,6 +195,16 @@ class _Request:
     sink: "queue.Queue[StreamItem] | None" = None
     loop: asyncio.AbstractEventLoop | None = None
     aqueue: asyncio.Queue | None = None
+    lp: Any = None  # _LogprobRecord of a request that asked for logprobs
+
+
+class _LogprobRecord:
+    """Front-end copy of a replica sequence's per-token log-probabilities, passed as ``StreamItem.seq``
+    so that the servers read them as they read a local engine's sequence."""
+
+    def __init__(self):
+        self.logprobs: list[float] = []
+        self.top_logprobs: list[list[tuple[int, float]]] = []
 
 
 @dataclass
@@ -385,7 +399,7 @@ class DataParallelEngine:
         while not self._stop.is_set():
             for idx, kind, payload in self._recv(0.05):
                 if kind == "events":
-                    for rid, tok, reason in payload:
+                    for rid, tok, reason, *lp in payload:
                         if tok is None:
                             self._end(rid, reason)
                             continue
@@ -395,7 +409,12 @@ class DataParallelEngine:
                                 req.cost -= 1
                                 self.replicas[req.replica].load -= 1
                         if req is not None:
-                            self._deliver(req, StreamItem(tok, None))
+                            if lp:
+                                if req.lp is None:
+                                    req.lp = _LogprobRecord()
+                                req.lp.logprobs.append(lp[0][0])
+                                req.lp.top_logprobs.append(lp[0][1])
+                            self._deliver(req, StreamItem(tok, None, req.lp))
                 elif kind == "stats":
                     self.replicas[idx].stats = payload
                 elif kind == "fatal":

@@ -72,6 +72,12 @@ def test_dp_openai_server_over_replicas(dp):
     assert r.json()["usage"]["completion_tokens"] >= 1
     h = c.get("/health")
     assert h.status_code == 200 and h.json()["status"] == "ok"
+    # logprobs recorded on the replica reach the server: one entry per token, greedy = top alternative
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4,
+                                             "temperature": 0, "logprobs": True, "top_logprobs": 2}).json()
+    ents = r["choices"][0]["logprobs"]["content"]
+    assert len(ents) == r["usage"]["completion_tokens"] >= 1
+    assert all(abs(e["logprob"] - e["top_logprobs"][0]["logprob"]) < 1e-5 for e in ents)
 
 
 def test_dp_replica_death_fails_its_requests_only():
