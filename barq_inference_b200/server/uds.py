@@ -17,7 +17,8 @@ carry ``messages`` (OpenAI chat turns, rendered with the server's chat template)
 ``tool_call`` ({"name", "arguments"}); with ``logprobs`` / ``top_logprobs`` every token frame
 carries ``logprobs`` = [{token, bytes, logprob, top: [{token, bytes, logprob}, ...]}].  A request ``{"id", "embeddings": input}`` (a string, a list
 of strings, token ids or lists of token ids) is answered by one frame ``{"id", "embeddings":
-[[...]], "prompt_tokens", "done": true}``.  A client that disconnects mid-stream has its request
+[[...]], "prompt_tokens", "done": true}``; a request ``{"id", "health": true}`` by one frame with
+``healthy``, ``last_error`` and ``kv_usage``.  A client that disconnects mid-stream has its request
 aborted in the engine.
 """
 from __future__ import annotations
@@ -98,6 +99,9 @@ class UDSServer:
         if "embeddings" in req:
             self._embed(conn, req, rid, t0)
             return
+        if req.get("health"):
+            send_frame(conn, self._health(rid))
+            return
         try:
             tools = tool_setup(req)
             ids = self._prompt_ids(req, tools)
@@ -159,6 +163,15 @@ class UDSServer:
         finally:
             if guard is not None:  # client went away mid-stream
                 guard.fail()
+
+    def _health(self, rid: str) -> dict:
+        """{"healthy", "last_error", "kv_usage"} of the engine behind this server (one frame)."""
+        eng = getattr(self.ae, "engine", None)
+        blocks = getattr(eng, "blocks", None)
+        used = blocks.n_used / blocks.num_blocks if blocks is not None and blocks.num_blocks else 0.0
+        return {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0, "done": True,
+                "healthy": bool(getattr(self.ae, "healthy", True)), "last_error": getattr(self.ae, "last_error", None),
+                "kv_usage": used}
 
     def _lp_entry(self, item, idx: int, params) -> dict | None:
         """{token, bytes, logprob, top: [{token, bytes, logprob}]} of the idx-th generated token, from

@@ -10,12 +10,15 @@
 // templates and sampling stay in the engine process.
 //
 //   barq-http --socket PATH [--host 0.0.0.0] [--port 8080] [--model-id NAME] [--rpm N]
-//             [--max-conns N] [--engine-timeout S] [--quiet]
+//             [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--quiet]
+//
+// SIGTERM / SIGINT stop it gracefully: the listening socket closes and generations in flight get up
+// to --drain-timeout seconds (default 30) to finish before the process exits.
 //
 // Routes:
 //   GET  /                       server info
 //   GET  /v1/models              the served model id
-//   GET  /health                 200 when the engine socket accepts connections, else 503
+//   GET  /health                 the engine's health frame: 200 ok, 503 degraded or unreachable
 //   GET  /metrics                Prometheus text: this front end's request / token / latency counters
 //   POST /v1/completions         prompt (string or token ids)
 //   POST /v1/chat/completions    messages (rendered by the engine's chat template)
@@ -79,8 +82,11 @@ struct Options {
   int rpm = 0;          // requests per minute per client address (0: no limit)
   int max_conns = 256;  // concurrent connections
   int engine_timeout_s = 600;
+  int drain_s = 30;  // on SIGTERM / SIGINT: stop accepting, let requests in flight finish this long
   bool quiet = false;
 };
+volatile sig_atomic_t g_stop = 0;
+void on_stop_signal(int) { g_stop = 1; }
 Options g_opt;
 
 double now_s() {
@@ -394,10 +400,27 @@ class EngineLink {
   int fd_ = -1;
 };
 
-bool engine_reachable() {
+// The engine's own health frame ({"healthy", "last_error", "kv_usage"}), or a null value when the
+// engine socket does not answer.
+Value engine_health() {
   EngineLink l;
   std::string err;
-  return l.open(err);
+  if (!l.open(err)) return Value();
+  Value req = Value::object(), fr;
+  req.set("id", Value::string("health"));
+  req.set("health", Value::boolean(true));
+  if (!l.send(req) || !l.next(fr, err)) return Value();
+  return fr;
+}
+
+// True when the client has closed its side (checked between streamed pieces of a non-streamed
+// response, so that a client that gave up stops its generation).
+bool client_gone(int fd) {
+  pollfd p{fd, POLLIN | POLLRDHUP, 0};
+  if (::poll(&p, 1, 0) <= 0) return false;
+  if (p.revents & (POLLRDHUP | POLLHUP | POLLERR)) return true;
+  char c;
+  return ::recv(fd, &c, 1, MSG_PEEK | MSG_DONTWAIT) == 0;
 }
 
 // ---------------------------------------------------------------- one generation
@@ -819,8 +842,10 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       if (s && s->is_number() && s->num != 0) r.set("seed", Value::number(s->num + i));
       r.set("id", Value::string(rid + "-" + std::to_string(i)));
     }
-    auto run = [&outs, &c, i](Value req) {
-      outs[i] = generate(req, c.stops, [] { return true; }, [](const std::string&, std::vector<Value>&) { return true; });
+    auto run = [&outs, &c, i, fd](Value req) {
+      // a client that has gone away stops the generation (closing the link aborts it in the engine)
+      outs[i] = generate(req, c.stops, [] { return true; },
+                         [fd](const std::string&, std::vector<Value>&) { return !client_gone(fd); });
     };
     if (i + 1 < c.n) workers.emplace_back(run, std::move(r));
     else run(std::move(r));
@@ -972,13 +997,17 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       return Outcome{200, !keep};
     }
     if (p == "/health") {
-      const bool up = engine_reachable();
+      const Value h = engine_health();
+      const Value* healthy = h.get("healthy");
+      const bool up = h.is_object(), ok = up && (!healthy || healthy->type != Value::kBool || healthy->b);
       Value o = Value::object();
-      o.set("status", Value::string(up ? "ok" : "engine_unreachable"));
+      o.set("status", Value::string(!up ? "engine_unreachable" : ok ? "ok" : "degraded"));
       o.set("engine_socket", Value::string(g_opt.socket_path));
       o.set("active_requests", Value::number((double)g_ctr.active));
-      respond(fd, up ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
-      return Outcome{up ? 200 : 503, !keep};
+      for (const char* k : {"kv_usage", "last_error"})
+        if (const Value* v = h.get(k)) o.set(k, *v);
+      respond(fd, ok ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
+      return Outcome{ok ? 200 : 503, !keep};
     }
     if (p == "/metrics") {
       respond(fd, 200, "text/plain; version=0.0.4", g_ctr.prometheus(), keep, rid);
@@ -1061,7 +1090,7 @@ int usage_error(const char* msg) {
   std::fprintf(stderr, "barq-http: %s\n", msg);
   std::fprintf(stderr,
                "usage: barq-http --socket PATH [--host ADDR] [--port N] [--model-id NAME] [--rpm N]\n"
-               "                 [--max-conns N] [--engine-timeout S] [--quiet]\n");
+               "                 [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--quiet]\n");
   return 2;
 }
 
@@ -1094,6 +1123,7 @@ int main(int argc, char** argv) {
     else if (a == "--rpm") g_opt.rpm = num("--rpm", 0);
     else if (a == "--max-conns") g_opt.max_conns = num("--max-conns", 1);
     else if (a == "--engine-timeout") g_opt.engine_timeout_s = num("--engine-timeout", 1);
+    else if (a == "--drain-timeout") g_opt.drain_s = num("--drain-timeout", 0);
     else if (a == "--quiet") g_opt.quiet = true;
     else if (a == "-h" || a == "--help") {
       usage_error("OpenAI-compatible HTTP front end for a barq UDS server");
@@ -1103,6 +1133,10 @@ int main(int argc, char** argv) {
   }
   if (g_opt.port > 65535) return usage_error("port out of range");
   signal(SIGPIPE, SIG_IGN);
+  struct sigaction sa{};
+  sa.sa_handler = on_stop_signal;
+  sigaction(SIGTERM, &sa, nullptr);
+  sigaction(SIGINT, &sa, nullptr);
   const int ls = ::socket(AF_INET, SOCK_STREAM, 0);
   if (ls < 0) return usage_error(std::strerror(errno));
   int one = 1;
@@ -1122,12 +1156,14 @@ int main(int argc, char** argv) {
   std::printf("barq-http listening on %s:%d (engine socket %s)\n", g_opt.host.c_str(), ntohs(addr.sin_port),
               g_opt.socket_path.c_str());
   std::fflush(stdout);
-  for (;;) {
+  while (!g_stop) {
+    pollfd pl{ls, POLLIN, 0};
+    if (::poll(&pl, 1, 200) <= 0) continue;  // wakes up to notice a stop signal
     sockaddr_in peer{};
     socklen_t plen = sizeof peer;
     const int fd = ::accept(ls, reinterpret_cast<sockaddr*>(&peer), &plen);
     if (fd < 0) {
-      if (errno == EINTR || errno == ECONNABORTED || errno == EMFILE || errno == ENFILE) continue;
+      if (errno == EINTR || errno == ECONNABORTED || errno == EMFILE || errno == ENFILE || errno == EAGAIN) continue;
       std::fprintf(stderr, "barq-http: accept: %s\n", std::strerror(errno));
       return 1;
     }
@@ -1141,4 +1177,12 @@ int main(int argc, char** argv) {
     }
     std::thread(serve_connection, fd, std::string(host)).detach();
   }
+  // graceful stop: no new connections; generations in flight get up to --drain-timeout seconds
+  ::close(ls);
+  const double t0 = now_s();
+  while (g_ctr.active > 0 && now_s() - t0 < g_opt.drain_s) usleep(50 * 1000);
+  if (!g_opt.quiet)
+    std::fprintf(stderr, "barq-http: stopped (%lld request(s) still in flight)\n", (long long)g_ctr.active.load());
+  std::fflush(stdout);
+  std::_Exit(0);  // detached connection threads end with the process
 }

@@ -38,6 +38,7 @@ class FakeEngine:
         self.path = path
         self.requests = []
         self.aborted = []
+        self.healthy = True
         self.lock = threading.Lock()
         self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
         self.sock.bind(path)
@@ -55,7 +56,11 @@ class FakeEngine:
     def _serve(self, conn):
         try:
             req = recv_frame(conn)
-            if req is None:  # a health probe: connect and close
+            if req is None:  # a connect-and-close probe
+                return
+            if req.get("health"):
+                send_frame(conn, {"id": req["id"], "text": "", "done": True, "healthy": self.healthy,
+                                  "last_error": None if self.healthy else "step failed", "kv_usage": 0.25})
                 return
             with self.lock:
                 self.requests.append(req)
@@ -147,7 +152,11 @@ def test_info_models_health_and_cors(gateway, tmp_path):
     st, _, b = _req(port, "GET", "/")
     assert st == 200 and "/v1/chat/completions" in json.loads(b)["endpoints"]
     st, _, b = _req(port, "GET", "/health")
-    assert st == 200 and json.loads(b)["status"] == "ok"
+    assert st == 200 and json.loads(b)["status"] == "ok" and json.loads(b)["kv_usage"] == 0.25
+    eng.healthy = False
+    st, _, b = _req(port, "GET", "/health")
+    assert st == 503 and json.loads(b)["status"] == "degraded" and json.loads(b)["last_error"] == "step failed"
+    eng.healthy = True
     st, h, b = _req(port, "OPTIONS", "/v1/chat/completions")
     assert st == 204 and "POST" in h["Access-Control-Allow-Methods"] and b == b""
     st, _, b = _req(port, "GET", "/nope")
@@ -334,6 +343,53 @@ def test_keep_alive_and_client_disconnect(gateway):
     while time.time() < deadline and not eng.aborted:
         time.sleep(0.05)
     assert eng.aborted, "the engine connection stayed open after the client left"
+
+
+def test_non_streamed_client_leaving_stops_the_generation(gateway):
+    eng, port = gateway
+    n0 = len(eng.aborted)
+    s = socket.create_connection(("127.0.0.1", port))
+    body = json.dumps({"prompt": "slow"}).encode()
+    s.sendall(b"POST /v1/completions HTTP/1.1\r\nContent-Type: application/json\r\nContent-Length: "
+              + str(len(body)).encode() + b"\r\n\r\n" + body)
+    time.sleep(0.2)  # the engine is streaming into the front end
+    s.close()
+    deadline = time.time() + 20
+    while time.time() < deadline and len(eng.aborted) == n0:
+        time.sleep(0.05)
+    assert len(eng.aborted) > n0, "the engine connection stayed open after the client left"
+
+
+def test_graceful_stop_lets_streams_finish(tmp_path):
+    import signal
+
+    eng = FakeEngine(str(tmp_path / "e.sock"))
+    p, port = _start(eng.path, "--drain-timeout", "30")
+    try:
+        s = socket.create_connection(("127.0.0.1", port))
+        body = json.dumps({"prompt": "slow", "stream": True}).encode()
+        s.sendall(b"POST /v1/completions HTTP/1.1\r\nContent-Type: application/json\r\nContent-Length: "
+                  + str(len(body)).encode() + b"\r\n\r\n" + body)
+        first = s.recv(64)
+        assert first.startswith(b"HTTP/1.1 200")
+        p.send_signal(signal.SIGTERM)
+        data = first
+        while True:
+            chunk = s.recv(65536)
+            if not chunk:
+                break
+            data += chunk
+        s.close()
+        assert data.rstrip().endswith(b"data: [DONE]")  # the stream in flight completed
+        assert data.count(b'"text":"s"') == 200
+        assert p.wait(timeout=30) == 0
+        with pytest.raises(OSError):
+            socket.create_connection(("127.0.0.1", port), timeout=2).close()
+    finally:
+        if p.poll() is None:
+            p.kill()
+            p.wait()
+        eng.close()
 
 
 def test_rate_limit(tmp_path):
