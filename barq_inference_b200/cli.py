@@ -123,13 +123,15 @@ def cmd_run(args) -> int:
             text = tmpl.render([{"role": "user", "content": args.prompt}])
         ids = tok.encode(text)
     params = _params(args)
-    if args.speculative or args.draft_model:
+    if args.speculative or args.draft_model or args.lookup_decoding:
         from .engine.speculative import SpeculativeDecoder, SpeculativeConfig
 
-        draft_args = argparse.Namespace(**{**vars(args), "model": args.draft_model or args.model})
-        draft, _, _, _ = load(draft_args)
+        draft = None  # --lookup-decoding: drafts from n-grams of the context, no draft model
+        if not args.lookup_decoding:
+            draft_args = argparse.Namespace(**{**vars(args), "model": args.draft_model or args.model})
+            draft, _, _, _ = load(draft_args)
         sc = SpeculativeConfig.preset(args.speculation_preset, draft_max=args.draft_max)
-        out = SpeculativeDecoder(eng, draft, sc).generate(ids, params)
+        out = SpeculativeDecoder(eng, draft, sc, lookup_ngram=args.lookup_ngram).generate(ids, params)
         sys.stdout.write(tok.decode(out.tokens) + "\n")
         log.info("speculative: acceptance %.2f", out.acceptance_rate)
         return 0
@@ -563,6 +565,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--speculative", action="store_true")
     p.add_argument("--draft-model")
     p.add_argument("--draft-max", type=int, default=16)
+    p.add_argument("--lookup-decoding", action="store_true",
+                   help="speculative decoding with drafts copied from earlier n-grams of the context (no draft model)")
+    p.add_argument("--lookup-ngram", type=int, default=3, help="longest n-gram matched by --lookup-decoding")
     p.add_argument("--speculation-preset", choices=["default", "code", "creative", "max_speed"], default="default")
     p.set_defaults(fn=cmd_run)
 

@@ -173,12 +173,35 @@ def verify_drafts(ps: torch.Tensor, qs: torch.Tensor, drafts: torch.Tensor, gree
     return n_acc, acc + [int(torch.multinomial(r, 1, generator=gen))]
 
 
+def lookup_drafts(tokens: list[int], k: int, n_max: int = 3, n_min: int = 1) -> list[int]:
+    """Prompt-lookup drafting (no draft model): find the most recent earlier occurrence of the
+    context's last n tokens (longest n first, n_max down to n_min) and propose the k tokens that
+    followed it.  Pays off when the output repeats spans of its input (code edits, extraction,
+    retrieval answers, summaries); returns [] when no n-gram recurs."""
+    L = len(tokens)
+    for n in range(min(n_max, L - 1), n_min - 1, -1):
+        tail = tokens[L - n:]
+        first = tail[0]
+        for i in range(L - n - 1, -1, -1):
+            if tokens[i] == first and tokens[i:i + n] == tail:
+                cont = tokens[i + n:i + n + k]
+                if cont:
+                    return cont
+    return []
+
+
 class SpeculativeDecoder:
-    def __init__(self, target, draft, cfg: SpeculativeConfig | None = None):
+    """``draft`` is a draft engine (model drafting) or None: prompt-lookup drafting, whose drafts
+    are deterministic (q is one-hot at the proposed token), so the rejection step accepts a
+    drafted token x with probability p(x) and otherwise samples from p with x removed; the output
+    distribution stays the target's either way."""
+
+    def __init__(self, target, draft, cfg: SpeculativeConfig | None = None, lookup_ngram: int = 3):
         self.t = target
         self.d = draft
         self.cfg = cfg or SpeculativeConfig()
-        if target.cfg.vocab != draft.cfg.vocab:
+        self.lookup_ngram = lookup_ngram
+        if draft is not None and target.cfg.vocab != draft.cfg.vocab:
             raise ValueError("draft and target must share a vocabulary")
         self.stats = SpecStats()
         target.spec_stats = self.stats
@@ -189,7 +212,7 @@ class SpeculativeDecoder:
         dev = self.t.device
         gen = torch.Generator(device=dev).manual_seed(params.seed or 1234)
         greedy = params.temperature <= 0
-        ts, ds = _Seq(self.t), _Seq(self.d)
+        ts, ds = _Seq(self.t), (_Seq(self.d) if self.d is not None else None)
         try:
             # invariant: the target cache holds every token but the last; the draft may lag behind
             tokens = list(prompt)
@@ -201,29 +224,46 @@ class SpeculativeDecoder:
             while len(out) < params.max_tokens:
                 k = max(self.cfg.draft_min, min(k, params.max_tokens - len(out)))
                 last = tokens[-1]
-                # 1) draft k tokens autoregressively (first call catches the draft cache up)
+                # 1) draft up to k tokens: autoregressively with the draft model (its first call
+                # catches its cache up), or by prompt lookup
                 drafts, qs = [], []
-                feed = tokens[ds.len:]
-                for _ in range(k):
-                    q = _probs(ds.forward(feed, False)[-1:], params)  # [1, V] on the device
-                    cur = int(q.argmax()) if greedy else int(torch.multinomial(q[0], 1, generator=gen))
-                    drafts.append(cur)
-                    qs.append(q)
-                    feed = [cur]
+                if ds is not None:
+                    feed = tokens[ds.len:]
+                    for _ in range(k):
+                        q = _probs(ds.forward(feed, False)[-1:], params)  # [1, V] on the device
+                        cur = int(q.argmax()) if greedy else int(torch.multinomial(q[0], 1, generator=gen))
+                        drafts.append(cur)
+                        qs.append(q)
+                        feed = [cur]
+                else:
+                    drafts = lookup_drafts(tokens, k, self.lookup_ngram)
+                k_used = len(drafts)
                 # 2) target scores [last, d1..dk] in one forward -> k+1 distributions
                 ps = _probs(ts.forward([last] + drafts, True), params)
-                # 3) accept / reject on the device (one host synchronization)
-                n_acc, new = verify_drafts(ps, torch.cat(qs), torch.tensor(drafts, device=ps.device), greedy, gen,
-                                           seed=params.seed or 1234, step=len(out))
-                if n_acc == k:
+                if ds is None:
+                    q1 = torch.zeros(k_used, ps.shape[-1], device=ps.device)
+                    if k_used:
+                        q1[torch.arange(k_used, device=ps.device), torch.tensor(drafts, device=ps.device)] = 1.0
+                    qs = [q1]
+                # 3) accept / reject on the device (one host synchronization); with nothing drafted
+                # (no recurring n-gram) this is a plain decode step
+                if k_used:
+                    n_acc, new = verify_drafts(ps, torch.cat(qs), torch.tensor(drafts, dtype=torch.int64,
+                                                                                device=ps.device),
+                                               greedy, gen, seed=params.seed or 1234, step=len(out))
+                else:
+                    n_acc = 0
+                    new = [int(ps[0].argmax()) if greedy else int(torch.multinomial(ps[0], 1, generator=gen))]
+                if k_used and n_acc == k_used:
                     self.stats.bonus += 1
-                self.stats.drafted += k
+                self.stats.drafted += k_used
                 self.stats.accepted += n_acc
                 self.stats.steps += 1
                 # 4) roll the caches back to the accepted prefix
                 n_old = len(tokens)
                 ts.len = n_old + n_acc
-                ds.len = min(ds.len, n_old + n_acc)
+                if ds is not None:
+                    ds.len = min(ds.len, n_old + n_acc)
                 stop = False
                 for tok in new:
                     out.append(tok)
@@ -236,8 +276,8 @@ class SpeculativeDecoder:
                         break
                 if stop:
                     break
-                if self.cfg.adaptive:
-                    if n_acc == k:
+                if self.cfg.adaptive and k_used:
+                    if n_acc == k_used:
                         k += 1
                     elif n_acc == 0:
                         k -= 1
@@ -245,4 +285,5 @@ class SpeculativeDecoder:
             return SpecResult(out, self.stats.acceptance_rate, self.stats, time.perf_counter() - t0, reason)
         finally:
             ts.release()
-            ds.release()
+            if ds is not None:
+                ds.release()

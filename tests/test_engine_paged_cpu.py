@@ -522,3 +522,35 @@ def test_logprobs_of_the_rows_that_ask_for_them():
             assert abs(lp - float(lsm[tok])) < 1e-3
             assert [a for a, _ in top] == lsm.topk(3).indices.tolist()
             logits = ref.forward([tok], cache)[-1]
+
+
+def test_prompt_lookup_speculation_follows_target_reference():
+    """Drafts copied from earlier n-grams (no draft model): greedy output is the target's greedy
+    continuation; on a repetitive context the drafts are accepted and fewer target steps run."""
+    from barq_inference_b200.engine.speculative import SpeculativeConfig, SpeculativeDecoder, lookup_drafts
+
+    assert lookup_drafts([1, 2, 3, 9, 1, 2, 3], 3) == [9, 1, 2]
+    assert lookup_drafts([5, 6, 7], 2) == [] and lookup_drafts([4, 4], 2) == [4]
+    assert lookup_drafts([1, 2, 8, 2, 9, 1, 2], 2, n_max=2) == [8, 2]  # longest match first
+    cfg = preset("tiny", n_layers=1, vocab=400, max_ctx=256)
+    t = random_tensors(cfg, POLICIES["tiny"], seed=13)
+    ref = ReferenceModel(cfg, t)
+    target = _engine(cfg, t, num_blocks=64)
+    prompt = _prompts(cfg, 1, 15, lo=20, hi=21)[0]
+    # make the context repeat the model's own greedy continuation: the lookup then finds it
+    cache: dict = {}
+    logits = ref.forward(prompt, cache)[-1]
+    cont = []
+    for _ in range(12):
+        cont.append(int(logits.argmax()))
+        logits = ref.forward([cont[-1]], cache)[-1]
+    ctx = prompt + cont + prompt
+    p = SamplingParams.greedy_params(max_tokens=12)
+    res = SpeculativeDecoder(target, None, SpeculativeConfig(6)).generate(ctx, p)
+    assert len(res.tokens) == 12 and _follows_reference(ref, ctx, res.tokens)
+    assert res.stats.accepted > 0 and res.stats.steps < 12
+    assert target.blocks.n_used == 1
+    # sampled decoding stays within the target's support (drafts are one-hot proposals)
+    ps = dataclasses.replace(SamplingParams(temperature=0.8, top_k=5, seed=3), max_tokens=10)
+    res = SpeculativeDecoder(target, None, SpeculativeConfig(4)).generate(ctx, ps)
+    assert len(res.tokens) == 10

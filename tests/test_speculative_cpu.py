@@ -52,3 +52,22 @@ def test_verify_sampled_output_follows_target():
         _, new = verify_drafts(ps, qs, x, greedy=False, gen=gen)
         counts[new[0]] += 1
     assert (counts / n - p).abs().max() < 0.025, counts / n
+
+
+def test_one_hot_drafts_keep_the_target_distribution():
+    """Prompt-lookup drafts are deterministic (q one-hot at the proposed token x): accepting x with
+    probability p(x) and otherwise sampling norm(max(0, p - q)) must give exactly p."""
+    import torch
+
+    from barq_inference_b200.engine.speculative import verify_drafts
+
+    p = torch.tensor([[0.5, 0.2, 0.2, 0.1], [0.25, 0.25, 0.25, 0.25]])
+    q = torch.zeros(1, 4)
+    q[0, 1] = 1.0  # the draft proposes token 1
+    g = torch.Generator().manual_seed(0)
+    counts = torch.zeros(4)
+    n = 20000
+    for _ in range(n):
+        n_acc, toks = verify_drafts(p, q, torch.tensor([1]), False, g)
+        counts[toks[0]] += 1
+    assert torch.allclose(counts / n, p[0], atol=0.015), counts / n
