@@ -192,7 +192,7 @@ def reference_attention(q, kc, vc, bt, q_start, ctx_lens, H, Hkv, D, scale, wind
     return out
 
 
-@pytest.mark.parametrize("D,dtype,window", [(128, "bf16", 0), (64, "fp16", 0), (128, "fp16", 200)])
+@pytest.mark.parametrize("D,dtype,window", [(128, "bf16", 0), (64, "fp16", 0), (128, "fp16", 200), (64, "bf16", 37)])
 def test_prefill_tc_dataflow_matches_fp32_attention(D, dtype, window):
     rng = np.random.default_rng(3 + D + window)
     H, Hkv = 4, 2
