@@ -30,6 +30,7 @@ import socketserver
 import struct
 import threading
 import time
+from collections import OrderedDict
 
 from ..tokenizer import ChatTemplate, StreamDecoder
 from .chat_tools import normalize_messages, tool_call_of, tool_names, tool_setup
@@ -73,9 +74,30 @@ class UDSServer:
         self.metrics = metrics  # InferenceMetrics: per-request counters / TTFT for the metrics server
         self.tok = tokenizer
         self.template = chat_template or ChatTemplate("generic")
+        # recent prompt texts -> token ids (repeated system prompts and retries skip the tokenizer;
+        # the role of the reference's prompt-processing cache)
+        self._tok_cache: OrderedDict[str, tuple[int, ...]] = OrderedDict()
+        self._tok_lock = threading.Lock()
+        self.tok_cache_size = 1024
+        self.tok_cache_hits = 0
         self.path = socket_path
         self.sem = threading.BoundedSemaphore(queue_size)
         self._server = None
+
+    def _encode(self, text: str, add_special: bool = True) -> list[int]:
+        key = (text, add_special)
+        with self._tok_lock:
+            hit = self._tok_cache.get(key)
+            if hit is not None:
+                self._tok_cache.move_to_end(key)
+                self.tok_cache_hits += 1
+                return list(hit)
+        ids = self.tok.encode(text, add_special=add_special)
+        with self._tok_lock:
+            self._tok_cache[key] = tuple(ids)
+            if len(self._tok_cache) > self.tok_cache_size:
+                self._tok_cache.popitem(last=False)
+        return ids
 
     def _prompt_ids(self, req: dict, tools: dict | None = None) -> list[int]:
         msgs = req.get("messages")
@@ -85,13 +107,13 @@ class UDSServer:
                 msgs = [{"role": "system", "content": tools["prompt"]}] + msgs
             text = self.template.render(msgs, add_generation_prompt=True)
             bos = getattr(self.template, "bos_token", "") or "\0"
-            return self.tok.encode(text, add_special=not text.startswith(bos))
+            return self._encode(text, add_special=not text.startswith(bos))
         if tools is not None:
             raise ValueError("tools need chat messages")
         prompt = req["prompt"]
         if isinstance(prompt, list):
             return [int(t) for t in prompt]
-        return self.tok.encode(str(prompt))
+        return self._encode(str(prompt))
 
     def handle_request(self, conn: socket.socket, req: dict) -> None:
         t0 = time.perf_counter()

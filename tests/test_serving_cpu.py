@@ -653,3 +653,23 @@ def test_native_uds_client_chat_mode(tmp_path):
         [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"},
          {"role": "assistant", "content": "re: hello"}, {"role": "user", "content": "again é"}]]
     assert all(q["max_tokens"] == 9 for q in seen)
+
+
+def test_uds_prompt_cache(tiny_engine, tmp_path):
+    """Repeated prompt texts (and rendered chat prompts) skip the tokenizer on the UDS server."""
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSClient, UDSServer
+
+    path = str(tmp_path / "pc.sock")
+    ae = AsyncEngine(tiny_engine)
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        cl = UDSClient(path)
+        a = [f["text"] for f in cl.stream("same words again", max_tokens=3, temperature=0.0)]
+        b = [f["text"] for f in cl.stream("same words again", max_tokens=3, temperature=0.0)]
+        cl.close()
+        assert a == b and srv.tok_cache_hits == 1
+        assert srv._encode("same words again") == tiny_engine.tokenizer.encode("same words again")
+    finally:
+        srv.stop()
+        ae.shutdown()
