@@ -308,6 +308,19 @@ def cmd_tokenize(args) -> int:
     return 0
 
 
+def cmd_bench_serve(args) -> int:
+    """Concurrent streaming requests against a running OpenAI-compatible server; JSON summary."""
+    import asyncio
+
+    from .server.bench_serve import run
+
+    out = asyncio.run(run(args.url, n_requests=args.requests, concurrency=args.concurrency,
+                          prompt_words=args.prompt_words, max_tokens=args.max_tokens, rate=args.rate,
+                          chat=args.chat, model=args.model_id, seed=args.seed, temperature=args.temperature))
+    print(json.dumps(out, indent=2))
+    return 0 if out["completed"] else 1
+
+
 def cmd_convert(args) -> int:
     from .gguf import QUANT_NAME_TO_TYPE
     from .models.convert import convert_gguf
@@ -599,6 +612,19 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--no-special", action="store_true", help="no BOS / special tokens")
     p.add_argument("--ids-only", action="store_true")
     p.set_defaults(fn=cmd_tokenize)
+
+    p = sub.add_parser("bench-serve", help="load-test a running OpenAI-compatible server (TTFT, ITL, throughput)")
+    p.add_argument("--url", default="http://127.0.0.1:8000")
+    p.add_argument("--requests", type=int, default=64)
+    p.add_argument("--concurrency", type=int, default=16)
+    p.add_argument("--rate", type=float, default=0.0, help="Poisson arrivals per second (0: all at once)")
+    p.add_argument("--prompt-words", type=int, default=64)
+    p.add_argument("--max-tokens", type=int, default=128)
+    p.add_argument("--temperature", type=float, default=0.0)
+    p.add_argument("--chat", action="store_true", help="use /v1/chat/completions")
+    p.add_argument("--model-id", default="barq")
+    p.add_argument("--seed", type=int, default=0)
+    p.set_defaults(fn=cmd_bench_serve)
 
     p = sub.add_parser("convert", help="requantize a GGUF file")
     p.add_argument("--input", required=True)

@@ -518,3 +518,20 @@ def test_cli_http_server_native_front_end(tmp_path):
     finally:
         os.killpg(p.pid, 15)
         p.wait(timeout=60)
+
+
+def test_bench_serve_against_the_front_end(gateway):
+    """The serving benchmark drives barq-http with concurrent streams and reports what it saw."""
+    import asyncio
+
+    from barq_inference_b200.server.bench_serve import run
+
+    eng, port = gateway
+    out = asyncio.run(run(f"http://127.0.0.1:{port}", n_requests=12, concurrency=4, prompt_words=3, max_tokens=4,
+                          chat=True))
+    assert out["completed"] == 12 and out["failed"] == 0
+    assert out["output_tokens"] == 12 * 4  # the scripted engine streams 4 pieces per request
+    assert 0 < out["ttft_p50_ms"] <= out["latency_p50_ms"] and out["itl_p99_ms"] >= out["itl_p50_ms"] >= 0
+    assert out["request_throughput_rps"] > 0
+    bad = asyncio.run(run("http://127.0.0.1:1", n_requests=2, concurrency=2, max_tokens=2))
+    assert bad["completed"] == 0 and bad["failed"] == 2 and bad["errors"]
