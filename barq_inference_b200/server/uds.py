@@ -18,7 +18,8 @@ carry ``messages`` (OpenAI chat turns, rendered with the server's chat template)
 carries ``logprobs`` = [{token, bytes, logprob, top: [{token, bytes, logprob}, ...]}].  A request ``{"id", "embeddings": input}`` (a string, a list
 of strings, token ids or lists of token ids) is answered by one frame ``{"id", "embeddings":
 [[...]], "prompt_tokens", "done": true}``; a request ``{"id", "health": true}`` by one frame with
-``healthy``, ``last_error`` and ``kv_usage``.  A client that disconnects mid-stream has its request
+``healthy``, ``last_error`` and ``kv_usage``; ``{"id", "metrics": true}`` by one frame whose
+``prometheus`` member is the engine-side metrics text.  A client that disconnects mid-stream has its request
 aborted in the engine.
 """
 from __future__ import annotations
@@ -34,6 +35,7 @@ from collections import OrderedDict
 
 from ..tokenizer import ChatTemplate, StreamDecoder
 from .chat_tools import normalize_messages, tool_call_of, tool_names, tool_setup
+from .metrics import InferenceMetrics
 from .request_params import sampling_params_from_request
 
 MAX_FRAME = 16 << 20
@@ -71,7 +73,8 @@ class UDSServer:
     def __init__(self, aengine, tokenizer, socket_path: str = "/tmp/barq-inference.sock", queue_size: int = 100,
                  metrics=None, chat_template: ChatTemplate | None = None):
         self.ae = aengine
-        self.metrics = metrics  # InferenceMetrics: per-request counters / TTFT for the metrics server
+        # per-request counters / TTFT: served by the metrics port and by {"metrics": true} frames
+        self.metrics = metrics if metrics is not None else InferenceMetrics()
         self.tok = tokenizer
         self.template = chat_template or ChatTemplate("generic")
         # recent prompt texts -> token ids (repeated system prompts and retries skip the tokenizer;
@@ -123,6 +126,11 @@ class UDSServer:
             return
         if req.get("health"):
             send_frame(conn, self._health(rid))
+            return
+        if req.get("metrics"):
+            eng = getattr(self.ae, "engine", None)
+            send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
+                              "done": True, "prometheus": self.metrics.prometheus(eng)})
             return
         try:
             tools = tool_setup(req)

@@ -19,7 +19,7 @@
 //   GET  /                       server info
 //   GET  /v1/models              the served model id
 //   GET  /health                 the engine's health frame: 200 ok, 503 degraded or unreachable
-//   GET  /metrics                Prometheus text: this front end's request / token / latency counters
+//   GET  /metrics                Prometheus text: this front end's counters, then the engine's
 //   POST /v1/completions         prompt (string or token ids)
 //   POST /v1/chat/completions    messages (rendered by the engine's chat template)
 //   POST /v1/responses           input (string or messages) / prompt / messages, max_output_tokens
@@ -400,15 +400,15 @@ class EngineLink {
   int fd_ = -1;
 };
 
-// The engine's own health frame ({"healthy", "last_error", "kv_usage"}), or a null value when the
-// engine socket does not answer.
-Value engine_health() {
+// One-frame engine query ({"health": true} -> {"healthy", "last_error", "kv_usage"};
+// {"metrics": true} -> {"prometheus"}), or a null value when the engine socket does not answer.
+Value engine_query(const char* what) {
   EngineLink l;
   std::string err;
   if (!l.open(err)) return Value();
   Value req = Value::object(), fr;
-  req.set("id", Value::string("health"));
-  req.set("health", Value::boolean(true));
+  req.set("id", Value::string(what));
+  req.set(what, Value::boolean(true));
   if (!l.send(req) || !l.next(fr, err)) return Value();
   return fr;
 }
@@ -997,7 +997,7 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       return Outcome{200, !keep};
     }
     if (p == "/health") {
-      const Value h = engine_health();
+      const Value h = engine_query("health");
       const Value* healthy = h.get("healthy");
       const bool up = h.is_object(), ok = up && (!healthy || healthy->type != Value::kBool || healthy->b);
       Value o = Value::object();
@@ -1009,8 +1009,11 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       respond(fd, ok ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
       return Outcome{ok ? 200 : 503, !keep};
     }
-    if (p == "/metrics") {
-      respond(fd, 200, "text/plain; version=0.0.4", g_ctr.prometheus(), keep, rid);
+    if (p == "/metrics") {  // this front end's counters, then the engine's own (one scrape target)
+      std::string text = g_ctr.prometheus();
+      const Value m = engine_query("metrics");
+      if (const Value* t = m.get("prometheus"); t && t->is_string()) text += t->str;
+      respond(fd, 200, "text/plain; version=0.0.4", text, keep, rid);
       return Outcome{200, !keep};
     }
   }

@@ -58,6 +58,10 @@ class FakeEngine:
             req = recv_frame(conn)
             if req is None:  # a connect-and-close probe
                 return
+            if req.get("metrics"):
+                send_frame(conn, {"id": req["id"], "text": "", "done": True,
+                                  "prometheus": "# TYPE barq_requests_total counter\nbarq_requests_total 7\n"})
+                return
             if req.get("health"):
                 send_frame(conn, {"id": req["id"], "text": "", "done": True, "healthy": self.healthy,
                                   "last_error": None if self.healthy else "step failed", "kv_usage": 0.25})
@@ -297,6 +301,7 @@ def test_errors(gateway):
     st, _, b = _req(port, "GET", "/metrics")
     m = b.decode()
     assert "barq_http_requests_total" in m and "barq_http_client_errors_total" in m
+    assert _metric(m, "barq_requests_total") == 7  # the engine's own metrics follow the front end's
     assert _metric(m, "barq_http_server_errors_total") >= 3 and _metric(m, "barq_http_client_errors_total") >= 10
 
 
@@ -456,6 +461,8 @@ def test_against_real_uds_server_and_cpu_engine(tmp_path):
         evs = _events(b)
         toks = [t for ev in evs for t in ((ev["choices"][0].get("logprobs") or {}).get("tokens") or [])]
         assert "".join(toks) == "".join(ev["choices"][0]["text"] for ev in evs)
+        m = _req(port, "GET", "/metrics")[2].decode()
+        assert "barq_http_requests_total" in m and "barq_requests_total" in m
         # embeddings through the engine: one vector per input, same as the engine's own
         st, _, b = _req(port, "POST", "/v1/embeddings", {"input": ["hello", "world wide"]})
         out = json.loads(b)
