@@ -9,8 +9,12 @@
 // server (`barq server --socket PATH`), one socket connection per request.  Tokenization, chat
 // templates and sampling stay in the engine process.
 //
-//   barq-http --socket PATH [--host 0.0.0.0] [--port 8080] [--model-id NAME] [--rpm N]
+//   barq-http --socket PATH [--socket PATH ...] [--host 0.0.0.0] [--port 8080] [--model-id NAME] [--rpm N]
 //             [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--quiet]
+//
+// With several --socket engines (e.g. one engine process per GPU) each request goes to the engine
+// with the fewest requests in flight that accepts the connection (one that refuses is skipped for
+// 5 s, and the request fails over); /health lists every engine and /metrics labels their samples.
 //
 // SIGTERM / SIGINT stop it gracefully: the listening socket closes and generations in flight get up
 // to --drain-timeout seconds (default 30) to finish before the process exits.
@@ -77,7 +81,7 @@ constexpr uint32_t kMaxFrame = 16u << 20;
 struct Options {
   std::string host = "0.0.0.0";
   int port = 8080;
-  std::string socket_path = "/tmp/barq-inference.sock";
+  std::vector<std::string> sockets;  // engine UDS servers (one per engine process; requests are balanced)
   std::string model_id = "barq";
   int rpm = 0;          // requests per minute per client address (0: no limit)
   int max_conns = 256;  // concurrent connections
@@ -328,33 +332,55 @@ const char* error_kind(int status) {
   return status >= 500 ? "server_error" : "invalid_request_error";
 }
 
+// ---------------------------------------------------------------- engine pool
+// Several engine processes (e.g. one per GPU) can serve behind one front end: each request goes to
+// the engine with the fewest requests in flight among those that accept connections; an engine
+// whose socket refuses is skipped for a few seconds and the request fails over to the next one.
+struct EnginePool {
+  static constexpr int kMax = 64;
+  std::atomic<int> active[kMax];
+  std::atomic<double> down_until[kMax];
+  EnginePool() {
+    for (int i = 0; i < kMax; ++i) {
+      active[i] = 0;
+      down_until[i] = 0.0;
+    }
+  }
+  // Engine indices in the order to try: fewest in flight first, engines marked down last.
+  std::vector<int> order() {
+    const int n = (int)g_opt.sockets.size();
+    const double t = now_s();
+    std::vector<int> idx(n);
+    for (int i = 0; i < n; ++i) idx[i] = i;
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) {
+      const bool da = down_until[a] > t, db = down_until[b] > t;
+      if (da != db) return !da;
+      return active[a].load() < active[b].load();
+    });
+    return idx;
+  }
+};
+EnginePool g_pool;
+
 // ---------------------------------------------------------------- engine link (UDS frames)
 class EngineLink {
  public:
   ~EngineLink() { close(); }
 
-  bool open(std::string& err) {
-    fd_ = ::socket(AF_UNIX, SOCK_STREAM, 0);
-    if (fd_ < 0) {
-      err = std::strerror(errno);
-      return false;
+  // Connects to the least busy engine that answers (or to engine `only` when it is >= 0).
+  bool open(std::string& err, int only = -1) {
+    std::vector<int> order = only >= 0 ? std::vector<int>{only} : g_pool.order();
+    for (int i : order) {
+      if (connect_to(i, err)) {
+        idx_ = i;
+        ++g_pool.active[i];
+        return true;
+      }
+      g_pool.down_until[i] = now_s() + 5.0;
     }
-    sockaddr_un addr{};
-    addr.sun_family = AF_UNIX;
-    if (g_opt.socket_path.size() >= sizeof(addr.sun_path)) {
-      err = "socket path too long";
-      return false;
-    }
-    std::memcpy(addr.sun_path, g_opt.socket_path.c_str(), g_opt.socket_path.size() + 1);
-    if (::connect(fd_, reinterpret_cast<sockaddr*>(&addr), sizeof(addr)) != 0) {
-      err = std::string("cannot connect to ") + g_opt.socket_path + ": " + std::strerror(errno);
-      return false;
-    }
-    timeval tv{};
-    tv.tv_sec = g_opt.engine_timeout_s;
-    setsockopt(fd_, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof tv);
-    return true;
+    return false;
   }
+  int engine() const { return idx_; }
   bool send(const Value& frame) {
     const std::string body = barqjson::dump(frame);
     const uint32_t n = (uint32_t)body.size();
@@ -394,18 +420,47 @@ class EngineLink {
   void close() {
     if (fd_ >= 0) ::close(fd_);
     fd_ = -1;
+    if (idx_ >= 0) --g_pool.active[idx_];
+    idx_ = -1;
   }
 
  private:
-  int fd_ = -1;
+  bool connect_to(int i, std::string& err) {
+    const std::string& path = g_opt.sockets[i];
+    fd_ = ::socket(AF_UNIX, SOCK_STREAM, 0);
+    if (fd_ < 0) {
+      err = std::strerror(errno);
+      return false;
+    }
+    sockaddr_un addr{};
+    addr.sun_family = AF_UNIX;
+    if (path.size() >= sizeof(addr.sun_path)) {
+      err = "socket path too long";
+      ::close(fd_);
+      fd_ = -1;
+      return false;
+    }
+    std::memcpy(addr.sun_path, path.c_str(), path.size() + 1);
+    if (::connect(fd_, reinterpret_cast<sockaddr*>(&addr), sizeof(addr)) != 0) {
+      err = std::string("cannot connect to ") + path + ": " + std::strerror(errno);
+      ::close(fd_);
+      fd_ = -1;
+      return false;
+    }
+    timeval tv{};
+    tv.tv_sec = g_opt.engine_timeout_s;
+    setsockopt(fd_, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof tv);
+    return true;
+  }
+  int fd_ = -1, idx_ = -1;
 };
 
 // One-frame engine query ({"health": true} -> {"healthy", "last_error", "kv_usage"};
 // {"metrics": true} -> {"prometheus"}), or a null value when the engine socket does not answer.
-Value engine_query(const char* what) {
+Value engine_query(const char* what, int engine) {
   EngineLink l;
   std::string err;
-  if (!l.open(err)) return Value();
+  if (!l.open(err, engine)) return Value();
   Value req = Value::object(), fr;
   req.set("id", Value::string(what));
   req.set(what, Value::boolean(true));
@@ -996,23 +1051,64 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
       return Outcome{200, !keep};
     }
-    if (p == "/health") {
-      const Value h = engine_query("health");
-      const Value* healthy = h.get("healthy");
-      const bool up = h.is_object(), ok = up && (!healthy || healthy->type != Value::kBool || healthy->b);
-      Value o = Value::object();
-      o.set("status", Value::string(!up ? "engine_unreachable" : ok ? "ok" : "degraded"));
-      o.set("engine_socket", Value::string(g_opt.socket_path));
+    if (p == "/health") {  // ok while any engine is up and healthy
+      Value o = Value::object(), engines = Value::array();
+      int n_ok = 0, n_up = 0;
+      for (int i = 0; i < (int)g_opt.sockets.size(); ++i) {
+        const Value h = engine_query("health", i);
+        const Value* healthy = h.get("healthy");
+        const bool up = h.is_object(), ok = up && (!healthy || healthy->type != Value::kBool || healthy->b);
+        n_up += up;
+        n_ok += ok;
+        Value e = Value::object();
+        e.set("socket", Value::string(g_opt.sockets[i]));
+        e.set("status", Value::string(!up ? "unreachable" : ok ? "ok" : "degraded"));
+        e.set("active_requests", Value::number((double)g_pool.active[i].load()));
+        for (const char* k : {"kv_usage", "last_error"})
+          if (const Value* v = h.get(k)) e.set(k, *v);
+        engines.push(e);
+      }
+      o.set("status", Value::string(n_ok ? "ok" : n_up ? "degraded" : "engine_unreachable"));
       o.set("active_requests", Value::number((double)g_ctr.active));
+      const Value first = engines.arr.empty() ? Value() : engines.arr[0];
       for (const char* k : {"kv_usage", "last_error"})
-        if (const Value* v = h.get(k)) o.set(k, *v);
-      respond(fd, ok ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
-      return Outcome{ok ? 200 : 503, !keep};
+        if (const Value* v = first.get(k)) o.set(k, *v);
+      o.set("engines", engines);
+      respond(fd, n_ok ? 200 : 503, "application/json", barqjson::dump(o), keep, rid);
+      return Outcome{n_ok ? 200 : 503, !keep};
     }
-    if (p == "/metrics") {  // this front end's counters, then the engine's own (one scrape target)
+    if (p == "/metrics") {  // this front end's counters, then every engine's own (one scrape target)
       std::string text = g_ctr.prometheus();
-      const Value m = engine_query("metrics");
-      if (const Value* t = m.get("prometheus"); t && t->is_string()) text += t->str;
+      const int n = (int)g_opt.sockets.size();
+      for (int i = 0; i < n; ++i) {
+        const Value m = engine_query("metrics", i);
+        const Value* t = m.get("prometheus");
+        if (!t || !t->is_string()) continue;
+        if (n == 1) {
+          text += t->str;
+          continue;
+        }
+        // several engines: label every sample with its engine, HELP / TYPE lines once
+        size_t b = 0;
+        while (b < t->str.size()) {
+          size_t e = t->str.find('\n', b);
+          if (e == std::string::npos) e = t->str.size();
+          std::string line = t->str.substr(b, e - b);
+          b = e + 1;
+          if (line.empty()) continue;
+          if (line[0] == '#') {
+            if (i == 0) text += line + "\n";
+            continue;
+          }
+          const size_t brace = line.find('{'), sp = line.find(' ');
+          const std::string lab = "engine=\"" + std::to_string(i) + "\"";
+          if (brace != std::string::npos && brace < sp)
+            line.insert(brace + 1, lab + ",");
+          else if (sp != std::string::npos)
+            line.insert(sp, "{" + lab + "}");
+          text += line + "\n";
+        }
+      }
       respond(fd, 200, "text/plain; version=0.0.4", text, keep, rid);
       return Outcome{200, !keep};
     }
@@ -1119,7 +1215,7 @@ int main(int argc, char** argv) {
       }
       return (int)x;
     };
-    if (a == "--socket") g_opt.socket_path = val("--socket");
+    if (a == "--socket") g_opt.sockets.push_back(val("--socket"));
     else if (a == "--host") g_opt.host = val("--host");
     else if (a == "--port") g_opt.port = num("--port", 0);
     else if (a == "--model-id") g_opt.model_id = val("--model-id");
@@ -1135,6 +1231,8 @@ int main(int argc, char** argv) {
     else return usage_error(("unknown argument " + a).c_str());
   }
   if (g_opt.port > 65535) return usage_error("port out of range");
+  if (g_opt.sockets.empty()) g_opt.sockets.push_back("/tmp/barq-inference.sock");
+  if ((int)g_opt.sockets.size() > EnginePool::kMax) return usage_error("too many --socket engines");
   signal(SIGPIPE, SIG_IGN);
   struct sigaction sa{};
   sa.sa_handler = on_stop_signal;
@@ -1156,8 +1254,8 @@ int main(int argc, char** argv) {
   socklen_t len = sizeof addr;
   getsockname(ls, reinterpret_cast<sockaddr*>(&addr), &len);
   // the bound port (useful with --port 0) on stdout, flushed, for whoever started the process
-  std::printf("barq-http listening on %s:%d (engine socket %s)\n", g_opt.host.c_str(), ntohs(addr.sin_port),
-              g_opt.socket_path.c_str());
+  std::printf("barq-http listening on %s:%d (engine socket %s%s)\n", g_opt.host.c_str(), ntohs(addr.sin_port),
+              g_opt.sockets[0].c_str(), g_opt.sockets.size() > 1 ? " and more" : "");
   std::fflush(stdout);
   while (!g_stop) {
     pollfd pl{ls, POLLIN, 0};

@@ -542,3 +542,33 @@ def test_bench_serve_against_the_front_end(gateway):
     assert out["request_throughput_rps"] > 0
     bad = asyncio.run(run("http://127.0.0.1:1", n_requests=2, concurrency=2, max_tokens=2))
     assert bad["completed"] == 0 and bad["failed"] == 2 and bad["errors"]
+
+
+def test_several_engines_balanced_with_failover(tmp_path):
+    """Two engine sockets behind one front end: concurrent requests spread over both, a dead
+    engine is skipped (requests fail over), /health lists both and /metrics labels their samples."""
+    import concurrent.futures as cf
+
+    e0, e1 = FakeEngine(str(tmp_path / "a.sock")), FakeEngine(str(tmp_path / "b.sock"))
+    p, port = _start(e0.path, "--socket", e1.path)
+    try:
+        with cf.ThreadPoolExecutor(8) as ex:
+            codes = list(ex.map(lambda _: _req(port, "POST", "/v1/completions", {"prompt": "slow"})[0], range(8)))
+        assert codes == [200] * 8
+        assert len(e0.requests) > 0 and len(e1.requests) > 0 and len(e0.requests) + len(e1.requests) == 8
+        m = _req(port, "GET", "/metrics")[2].decode()
+        assert 'barq_requests_total{engine="0"} 7' in m and 'barq_requests_total{engine="1"} 7' in m
+        assert m.count("# TYPE barq_requests_total counter") == 1
+        e1.close()
+        os.unlink(e1.path)  # engine 1 is gone: connects fail, requests go to engine 0
+        n0 = len(e0.requests)
+        assert all(_req(port, "POST", "/v1/completions", {"prompt": "hello"})[0] == 200 for _ in range(4))
+        assert len(e0.requests) == n0 + 4
+        st, _, b = _req(port, "GET", "/health")
+        h = json.loads(b)
+        assert st == 200 and h["status"] == "ok"
+        assert [e["status"] for e in h["engines"]] == ["ok", "unreachable"]
+    finally:
+        p.kill()
+        p.wait()
+        e0.close()
