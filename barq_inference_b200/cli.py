@@ -471,11 +471,105 @@ def _serve_native_front_end(aengine, tok, tmpl, args) -> int:
         srv.stop()
 
 
+_DROP_WITH_VALUE = ("--dp", "--host", "--port", "--rate-limit-rpm", "--socket")
+
+
+def _engine_server_argv(argv: list[str]) -> list[str]:
+    """The command line of one engine process for ``http-server --native-front-end --dp N``: this
+    process's arguments with ``http-server`` turned into ``server`` and the front-end options
+    (--dp, --host, --port, --rate-limit-rpm, --native-front-end) removed."""
+    out, i = [], 0
+    while i < len(argv):
+        a = argv[i]
+        if a == "http-server":
+            out.append("server")
+        elif a == "--native-front-end":
+            pass
+        elif a in _DROP_WITH_VALUE:
+            i += 1  # and its value
+        elif any(a.startswith(f + "=") for f in _DROP_WITH_VALUE):
+            pass
+        else:
+            out.append(a)
+        i += 1
+    return out
+
+
+def _serve_native_replicas(args) -> int:
+    """``http-server --native-front-end --dp N``: N engine processes, each a UDS server on its own
+    GPU (``CUDA_VISIBLE_DEVICES``), behind one ``barq-http`` that balances them -- data parallelism
+    with no Python router in the request path."""
+    import socket as _socket
+    import subprocess
+    import tempfile
+
+    from .server.uds_native import build_http
+
+    n = int(args.dp)
+    exe = build_http()
+    tmp = tempfile.mkdtemp(prefix="barq-dp-")
+    socks = [os.path.join(tmp, f"engine{i}.sock") for i in range(n)]
+    base = _engine_server_argv(list(getattr(args, "_argv", sys.argv[1:])))
+    device = getattr(args, "device", None) or ("cuda" if _cuda() else "cpu")
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    devs = [d for d in visible.split(",") if d.strip()] if visible else [str(i) for i in range(n)]
+    procs = []
+    try:
+        for i, sock in enumerate(socks):
+            env = dict(os.environ)
+            if device != "cpu":
+                env["CUDA_VISIBLE_DEVICES"] = devs[i % len(devs)]
+            procs.append(subprocess.Popen([sys.executable, "-m", "barq_inference_b200.cli", *base, "--socket", sock],
+                                          env=env))
+        deadline = time.monotonic() + float(os.environ.get("BARQ_ENGINE_START_TIMEOUT", "3600"))
+        pending = set(range(n))
+        while pending:  # an engine is ready once its UDS server accepts connections
+            for i in list(pending):
+                if procs[i].poll() is not None:
+                    raise RuntimeError(f"engine {i} exited with code {procs[i].returncode} before serving")
+                try:
+                    with _socket.socket(_socket.AF_UNIX, _socket.SOCK_STREAM) as c:
+                        c.connect(socks[i])
+                    pending.discard(i)
+                except OSError:
+                    pass
+            if time.monotonic() > deadline:
+                raise TimeoutError(f"engines {sorted(pending)} not serving in time")
+            time.sleep(0.2)
+        cmd = [exe, "--host", args.host, "--port", str(args.port), "--model-id", os.path.basename(args.model),
+               "--rpm", str(max(0, args.rate_limit_rpm))]
+        for sock in socks:
+            cmd += ["--socket", sock]
+        import signal
+
+        # a SIGTERM to this process alone still stops the front end and every engine (finally below)
+        signal.signal(signal.SIGTERM, lambda *_: sys.exit(0))
+        front = subprocess.Popen(cmd)
+        procs.insert(0, front)  # stopped first: it drains, then the engines go
+        try:
+            return front.wait()
+        except KeyboardInterrupt:
+            return 0
+    finally:
+        # the front end first (it drains its requests in flight), then every engine
+        for group in (procs[:1], procs[1:]) if len(procs) > n else ((), procs):
+            for pr in group:
+                if pr.poll() is None:
+                    pr.terminate()
+            for pr in group:
+                try:
+                    pr.wait(timeout=40)
+                except subprocess.TimeoutExpired:
+                    pr.kill()
+
+
 def cmd_http_server(args) -> int:
     from .server.async_engine import AsyncEngine
     from .server.openai_api import OpenAIServer, serve
 
     native = bool(getattr(args, "native_front_end", False))
+    if native and int(getattr(args, "dp", 1) or 1) > 1 and int(getattr(args, "tp", 1) or 1) == 1:
+        return _serve_native_replicas(args)
     if int(getattr(args, "dp", 1) or 1) > 1:
         front, tok, tmpl = _dp_front(args)
         if native:
@@ -669,6 +763,7 @@ def build_parser() -> argparse.ArgumentParser:
 
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
+    args._argv = list(argv) if argv is not None else sys.argv[1:]  # for commands that start children
     logging.basicConfig(level=logging.DEBUG if args.verbose else logging.INFO, format="%(message)s")
     if args.log_format == "json" or args.log_file:
         from .utils.logging import LoggingConfig, init_logger

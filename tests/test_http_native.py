@@ -572,3 +572,48 @@ def test_several_engines_balanced_with_failover(tmp_path):
         p.kill()
         p.wait()
         e0.close()
+
+
+def test_cli_native_front_end_with_replica_processes(tmp_path):
+    """``http-server --native-front-end --dp 2``: two engine processes, each a UDS server, behind one
+    barq-http; requests are served and /health lists both engines."""
+    import sys
+
+    from barq_inference_b200.cli import _engine_server_argv
+
+    assert _engine_server_argv(["-v", "http-server", "-m", "x.gguf", "--dp", "2", "--port=9", "--host", "h",
+                                "--native-front-end", "--device", "cpu"]) == ["-v", "server", "-m", "x.gguf",
+                                                                            "--device", "cpu"]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    model = str(tmp_path / "tiny.gguf")
+    r = subprocess.run([sys.executable, "-m", "barq_inference_b200.cli", "make-random-gguf", "--arch", "tiny",
+                        "--layers", "1", "--output", model, "--device", "cpu"], cwd=root, capture_output=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    p = subprocess.Popen([sys.executable, "-m", "barq_inference_b200.cli", "http-server", "-m", model, "--device",
+                          "cpu", "--host", "127.0.0.1", "--port", str(port), "--native-front-end", "--dp", "2"],
+                         cwd=root, stdout=subprocess.PIPE, stderr=subprocess.PIPE, start_new_session=True)
+    try:
+        deadline = time.time() + 300
+        while True:
+            assert p.poll() is None, p.stderr.read().decode()[-3000:]
+            try:
+                st, _, b = _req(port, "GET", "/health")
+                if st == 200:
+                    break
+            except OSError:
+                pass
+            assert time.time() < deadline, "front end did not come up"
+            time.sleep(0.5)
+        h = json.loads(b)
+        assert [e["status"] for e in h["engines"]] == ["ok", "ok"]
+        for _ in range(4):
+            st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "hello", "max_tokens": 3, "temperature": 0})
+            assert st == 200 and json.loads(b)["usage"]["completion_tokens"] >= 1
+    finally:
+        os.killpg(p.pid, 15)
+        p.wait(timeout=60)
