@@ -463,21 +463,24 @@ def _serve_native_front_end(aengine, tok, tmpl, args) -> int:
     srv = UDSServer(aengine, tok, sock, chat_template=tmpl).start()
     cmd = [exe, "--socket", sock, "--host", args.host, "--port", str(args.port),
            "--model-id", os.path.basename(args.model), "--rpm", str(max(0, args.rate_limit_rpm))]
+    env = dict(os.environ)
+    if getattr(args, "api_key", None):
+        env["BARQ_API_KEY"] = args.api_key  # through the environment, not the command line
     try:
-        return subprocess.call(cmd)
+        return subprocess.call(cmd, env=env)
     except KeyboardInterrupt:
         return 0
     finally:
         srv.stop()
 
 
-_DROP_WITH_VALUE = ("--dp", "--host", "--port", "--rate-limit-rpm", "--socket")
+_DROP_WITH_VALUE = ("--dp", "--host", "--port", "--rate-limit-rpm", "--socket", "--api-key")
 
 
 def _engine_server_argv(argv: list[str]) -> list[str]:
     """The command line of one engine process for ``http-server --native-front-end --dp N``: this
     process's arguments with ``http-server`` turned into ``server`` and the front-end options
-    (--dp, --host, --port, --rate-limit-rpm, --native-front-end) removed."""
+    (--dp, --host, --port, --rate-limit-rpm, --api-key, --native-front-end) removed."""
     out, i = [], 0
     while i < len(argv):
         a = argv[i]
@@ -544,7 +547,10 @@ def _serve_native_replicas(args) -> int:
 
         # a SIGTERM to this process alone still stops the front end and every engine (finally below)
         signal.signal(signal.SIGTERM, lambda *_: sys.exit(0))
-        front = subprocess.Popen(cmd)
+        fenv = dict(os.environ)
+        if getattr(args, "api_key", None):
+            fenv["BARQ_API_KEY"] = args.api_key  # through the environment, not the command line
+        front = subprocess.Popen(cmd, env=fenv)
         procs.insert(0, front)  # stopped first: it drains, then the engines go
         try:
             return front.wait()
@@ -575,7 +581,8 @@ def cmd_http_server(args) -> int:
         if native:
             return _serve_native_front_end(front, tok, tmpl, args)
         srv = OpenAIServer(front, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
-                           rate_limit_rpm=args.rate_limit_rpm, arch=front.cfg.arch, aengine=front)
+                           rate_limit_rpm=args.rate_limit_rpm, arch=front.cfg.arch, aengine=front,
+                           api_key=args.api_key)
     else:
         eng, tok, tmpl, md = load(args)
         eng = _lockstep(eng, args)
@@ -584,7 +591,7 @@ def cmd_http_server(args) -> int:
         if native:
             return _serve_native_front_end(AsyncEngine(eng), tok, tmpl, args)
         srv = OpenAIServer(eng, tok, model_id=os.path.basename(args.model), chat_template=tmpl,
-                           rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch)
+                           rate_limit_rpm=args.rate_limit_rpm, arch=eng.cfg.arch, api_key=args.api_key)
     serve(srv, args.host, args.port)
     return 0
 
@@ -751,6 +758,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--host", default="0.0.0.0")
     p.add_argument("--port", type=int, default=8000)
     p.add_argument("--rate-limit-rpm", type=int, default=60)
+    p.add_argument("--api-key", default=os.environ.get("BARQ_API_KEY"),
+                   help="require 'Authorization: Bearer KEY' on the /v1 routes (default: $BARQ_API_KEY)")
     p.add_argument("--native-front-end", action="store_true",
                    help="serve HTTP from the C++ front end barq-http (engine behind a private UDS socket)")
     p.set_defaults(fn=cmd_http_server)

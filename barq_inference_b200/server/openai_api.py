@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import asyncio
 import dataclasses
+import hmac
 import json
 import threading
 import time
@@ -88,7 +89,7 @@ def _tool_calls(out: dict, body: dict) -> None:
 
 class OpenAIServer:
     def __init__(self, engine, tokenizer, model_id: str = "barq", chat_template: ChatTemplate | None = None,
-                 rate_limit_rpm: int = 0, arch: str = "llama", aengine=None):
+                 rate_limit_rpm: int = 0, arch: str = "llama", aengine=None, api_key: str | None = None):
         self.metrics = InferenceMetrics()
         # ``aengine``: a ready front with the AsyncEngine caller API (e.g. the data-parallel replica
         # router, whose ``engine`` argument is then itself)
@@ -99,6 +100,8 @@ class OpenAIServer:
         self.arch = arch
         self.template = chat_template or ChatTemplate("generic")
         self.limiter = RateLimiter(rate_limit_rpm) if rate_limit_rpm > 0 else None
+        # optional shared secret: the /v1 routes need "Authorization: Bearer <key>" (401 otherwise)
+        self.api_key = api_key or None
         self._tok_cache: OrderedDict[str, tuple[int, ...]] = OrderedDict()
         self._tok_lock = threading.Lock()
         self.tok_cache_size = 1024
@@ -333,6 +336,9 @@ class OpenAIServer:
         async def cors(request: Request, call_next):
             if request.method == "OPTIONS":
                 return Response(status_code=204, headers=CORS)
+            if srv.api_key and request.url.path.startswith("/v1/") and not hmac.compare_digest(
+                    request.headers.get("authorization", ""), f"Bearer {srv.api_key}"):
+                return _err(401, "missing or invalid API key", "authentication_error")
             resp = await call_next(request)
             for k, v in CORS.items():
                 resp.headers.setdefault(k, v)

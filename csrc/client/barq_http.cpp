@@ -10,7 +10,10 @@
 // templates and sampling stay in the engine process.
 //
 //   barq-http --socket PATH [--socket PATH ...] [--host 0.0.0.0] [--port 8080] [--model-id NAME] [--rpm N]
-//             [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--quiet]
+//             [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--api-key KEY] [--quiet]
+//
+// With --api-key (or BARQ_API_KEY in the environment) the /v1 routes answer 401 unless the request
+// carries "Authorization: Bearer KEY"; /, /health and /metrics stay open.
 //
 // With several --socket engines (e.g. one engine process per GPU) each request goes to the engine
 // with the fewest requests in flight that accepts the connection (one that refuses is skipped for
@@ -87,6 +90,7 @@ struct Options {
   int max_conns = 256;  // concurrent connections
   int engine_timeout_s = 600;
   int drain_s = 30;  // on SIGTERM / SIGINT: stop accepting, let requests in flight finish this long
+  std::string api_key;  // non-empty: /v1 routes need "Authorization: Bearer <key>"
   bool quiet = false;
 };
 volatile sig_atomic_t g_stop = 0;
@@ -216,6 +220,7 @@ const char* reason_phrase(int status) {
     case 200: return "OK";
     case 204: return "No Content";
     case 400: return "Bad Request";
+    case 401: return "Unauthorized";
     case 404: return "Not Found";
     case 405: return "Method Not Allowed";
     case 408: return "Request Timeout";
@@ -324,6 +329,7 @@ std::string error_body(const std::string& msg, const std::string& kind) {
 
 const char* error_kind(int status) {
   switch (status) {
+    case 401: return "authentication_error";
     case 404: return "not_found_error";
     case 429: return "rate_limit_error";
     case 502: return "engine_unavailable_error";
@@ -1019,6 +1025,15 @@ std::string request_id(const Request& req) {
   return buf;
 }
 
+// Constant-time comparison of the Authorization header with "Bearer <key>".
+bool authorized(const Request& req) {
+  if (g_opt.api_key.empty()) return true;
+  const std::string want = "Bearer " + g_opt.api_key, got = req.header("authorization");
+  unsigned diff = (unsigned)(want.size() ^ got.size());
+  for (size_t i = 0; i < want.size(); ++i) diff |= (unsigned char)want[i] ^ (unsigned char)(i < got.size() ? got[i] : 0);
+  return diff == 0;
+}
+
 Outcome dispatch(int fd, const Request& req, const std::string& client, bool keep) {
   const std::string rid = request_id(req);
   if (req.method == "OPTIONS") {
@@ -1026,6 +1041,8 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
     return Outcome{204, !keep};
   }
   const std::string& p = req.path;
+  if (p.rfind("/v1/", 0) == 0 && !authorized(req))
+    return finish_error(fd, 401, "missing or invalid API key", keep, rid);
   if (req.method == "GET") {
     if (p == "/") {
       Value o = Value::object(), eps = Value::array();
@@ -1189,7 +1206,7 @@ int usage_error(const char* msg) {
   std::fprintf(stderr, "barq-http: %s\n", msg);
   std::fprintf(stderr,
                "usage: barq-http --socket PATH [--host ADDR] [--port N] [--model-id NAME] [--rpm N]\n"
-               "                 [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--quiet]\n");
+               "                 [--max-conns N] [--engine-timeout S] [--drain-timeout S] [--api-key KEY] [--quiet]\n");
   return 2;
 }
 
@@ -1223,6 +1240,7 @@ int main(int argc, char** argv) {
     else if (a == "--max-conns") g_opt.max_conns = num("--max-conns", 1);
     else if (a == "--engine-timeout") g_opt.engine_timeout_s = num("--engine-timeout", 1);
     else if (a == "--drain-timeout") g_opt.drain_s = num("--drain-timeout", 0);
+    else if (a == "--api-key") g_opt.api_key = val("--api-key");
     else if (a == "--quiet") g_opt.quiet = true;
     else if (a == "-h" || a == "--help") {
       usage_error("OpenAI-compatible HTTP front end for a barq UDS server");
@@ -1232,6 +1250,8 @@ int main(int argc, char** argv) {
   }
   if (g_opt.port > 65535) return usage_error("port out of range");
   if (g_opt.sockets.empty()) g_opt.sockets.push_back("/tmp/barq-inference.sock");
+  if (g_opt.api_key.empty())
+    if (const char* k = std::getenv("BARQ_API_KEY")) g_opt.api_key = k;
   if ((int)g_opt.sockets.size() > EnginePool::kMax) return usage_error("too many --socket engines");
   signal(SIGPIPE, SIG_IGN);
   struct sigaction sa{};

@@ -617,3 +617,20 @@ def test_cli_native_front_end_with_replica_processes(tmp_path):
     finally:
         os.killpg(p.pid, 15)
         p.wait(timeout=60)
+
+
+def test_api_key(tmp_path):
+    eng = FakeEngine(str(tmp_path / "e.sock"))
+    p, port = _start(eng.path, "--api-key", "s3cret")
+    try:
+        assert _req(port, "POST", "/v1/completions", {"prompt": "hello"})[0] == 401
+        st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "hello"}, headers={"Authorization": "Bearer nope"})
+        assert st == 401 and json.loads(b)["error"]["type"] == "authentication_error"
+        assert _req(port, "GET", "/v1/models", headers={"Authorization": "Bearer s3cret"})[0] == 200
+        assert _req(port, "POST", "/v1/completions", {"prompt": "hello"},
+                    headers={"Authorization": "Bearer s3cret"})[0] == 200
+        assert _req(port, "GET", "/health")[0] == 200 and _req(port, "GET", "/metrics")[0] == 200  # stay open
+    finally:
+        p.kill()
+        p.wait()
+        eng.close()

@@ -673,3 +673,19 @@ def test_uds_prompt_cache(tiny_engine, tmp_path):
     finally:
         srv.stop()
         ae.shutdown()
+
+
+def test_http_api_key(tiny_engine):
+    from fastapi.testclient import TestClient
+
+    from barq_inference_b200.server.openai_api import OpenAIServer
+
+    srv = OpenAIServer(tiny_engine, tiny_engine.tokenizer, model_id="tiny", rate_limit_rpm=0, api_key="k1")
+    with TestClient(srv.app) as c:
+        body = {"prompt": "hello", "max_tokens": 2}
+        r = c.post("/v1/completions", json=body)
+        assert r.status_code == 401 and r.json()["error"]["type"] == "authentication_error"
+        assert c.post("/v1/completions", json=body, headers={"Authorization": "Bearer k2"}).status_code == 401
+        assert c.post("/v1/completions", json=body, headers={"Authorization": "Bearer k1"}).status_code == 200
+        assert c.get("/health").status_code == 200
+    srv.aengine.shutdown()
