@@ -845,15 +845,27 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
   } guard{t0};
 
   if (c.stream) {
+    // HTTP/1.1 clients get the event stream chunk-encoded, so the connection stays reusable;
+    // HTTP/1.0 clients get it close-delimited
+    const bool chunked = req.version == "HTTP/1.1";
     bool headers_sent = false, client_ok = true;
+    auto put = [&](const std::string& data) {
+      if (!chunked) return send_all(fd, data);
+      char len[24];
+      std::snprintf(len, sizeof len, "%zx\r\n", data.size());
+      return send_all(fd, len + data + "\r\n");
+    };
     auto send_event = [&](const Value& v) {
-      client_ok = client_ok && send_all(fd, "data: " + barqjson::dump(v) + "\n\n");
+      client_ok = client_ok && put("data: " + barqjson::dump(v) + "\n\n");
       return client_ok;
     };
     auto on_first = [&]() {
       std::string h = "HTTP/1.1 200 OK\r\nContent-Type: text/event-stream\r\nCache-Control: no-cache\r\n";
       h += kCors;
-      h += "x-request-id: " + rid + "\r\nConnection: close\r\n\r\n";
+      h += "x-request-id: " + rid + "\r\n";
+      h += chunked ? std::string("Transfer-Encoding: chunked\r\n") + (keep ? "Connection: keep-alive\r\n\r\n"
+                                                                         : "Connection: close\r\n\r\n")
+                   : "Connection: close\r\n\r\n";
       headers_sent = true;
       client_ok = send_all(fd, h);
       if (client_ok && kind == "chat") send_event(chunk(c, id, created, nullptr, nullptr, true));
@@ -873,7 +885,7 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       on_first();  // an empty generation still gets its stream
     }
     if (g.status != 200) {  // failed after the stream started: an error event, then the end marker
-      send_all(fd, "data: " + error_body(g.error, error_kind(g.status)) + "\n\n");
+      client_ok = client_ok && put("data: " + error_body(g.error, error_kind(g.status)) + "\n\n");
     } else if (client_ok) {
       if (kind != "resp") send_event(chunk(c, id, created, nullptr, &g.finish, false));
       if (c.include_usage) {
@@ -889,8 +901,9 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
       g_ctr.prompt_tokens += (uint64_t)g.prompt_tokens;
       g_ctr.completion_tokens += (uint64_t)g.completion_tokens;
     }
-    if (client_ok) send_all(fd, "data: [DONE]\n\n");
-    return Outcome{g.status == 200 ? 200 : g.status, true};
+    if (client_ok) client_ok = put("data: [DONE]\n\n");
+    if (client_ok && chunked) client_ok = send_all(fd, "0\r\n\r\n");  // last chunk
+    return Outcome{g.status == 200 ? 200 : g.status, !(chunked && keep && client_ok)};
   }
 
   // the n choices run as concurrent engine requests (continuous batching serves them together)

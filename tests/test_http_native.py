@@ -243,6 +243,34 @@ def test_streams(gateway):
     assert "".join(e["output"] for e in _events(b)) == "Hello world"
 
 
+def test_streams_are_chunk_encoded_and_keep_the_connection(gateway):
+    eng, port = gateway
+    c = http.client.HTTPConnection("127.0.0.1", port, timeout=30)
+    for _ in range(2):  # two streamed requests, then a plain one, on one connection
+        c.request("POST", "/v1/completions", body=json.dumps({"prompt": "hello", "stream": True}),
+                  headers={"Content-Type": "application/json"})
+        r = c.getresponse()
+        assert r.status == 200 and r.getheader("Transfer-Encoding") == "chunked"
+        assert "".join(e["choices"][0]["text"] for e in _events(r.read())) == "Hello world"
+    c.request("POST", "/v1/completions", body=json.dumps({"prompt": "hello"}), headers={"Content-Type": "application/json"})
+    assert json.loads(c.getresponse().read())["choices"][0]["text"] == "Hello world"
+    c.close()
+    # an HTTP/1.0 client gets a close-delimited stream
+    s = socket.create_connection(("127.0.0.1", port))
+    body = json.dumps({"prompt": "hello", "stream": True}).encode()
+    s.sendall(b"POST /v1/completions HTTP/1.0\r\nContent-Length: " + str(len(body)).encode() + b"\r\n\r\n" + body)
+    data = b""
+    while True:
+        chunk = s.recv(65536)
+        if not chunk:
+            break
+        data += chunk
+    s.close()
+    head, _, rest = data.partition(b"\r\n\r\n")
+    assert b"Transfer-Encoding" not in head and b"Connection: close" in head
+    assert "".join(e["choices"][0]["text"] for e in _events(rest)) == "Hello world"
+
+
 def test_stop_strings_are_never_sent(gateway):
     eng, port = gateway
     st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "stop", "stop": ["<end>", "zz"], "stream": True})
@@ -385,7 +413,8 @@ def test_graceful_stop_lets_streams_finish(tmp_path):
                 break
             data += chunk
         s.close()
-        assert data.rstrip().endswith(b"data: [DONE]")  # the stream in flight completed
+        assert data.rstrip().endswith(b"0")  # the chunk-encoded stream in flight completed: [DONE], last chunk
+        assert b"data: [DONE]" in data
         assert data.count(b'"text":"s"') == 200
         assert p.wait(timeout=30) == 0
         with pytest.raises(OSError):
