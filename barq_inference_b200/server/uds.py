@@ -309,5 +309,11 @@ class UDSClient:
             if fr.get("done"):
                 return
 
+    def query(self, what: str) -> dict:
+        """One-frame engine query: ``"health"`` -> {healthy, last_error, kv_usage}, ``"metrics"`` ->
+        {prometheus}."""
+        send_frame(self.sock, {"id": what, what: True})
+        return recv_frame(self.sock) or {}
+
     def close(self):
         self.sock.close()

@@ -10,6 +10,8 @@
 //            [--quiet] PROMPT
 //   barq-uds --chat [--system TEXT] ...   interactive chat: one user turn per stdin line, the history
 //            sent as OpenAI messages (rendered by the server's chat template); /exit ends it
+//   barq-uds --health | --metrics         the engine's health frame (exit status 1 when unhealthy) or
+//            its Prometheus metrics text
 //
 // The generated text streams to stdout as frames arrive (or, with --json, every frame's JSON one
 // per line).  A summary line goes to stderr: tokens, TTFT and total time of each request, and for
@@ -274,7 +276,7 @@ struct Options {
   long max_tokens = 128;
   double temperature = 0.8;
   long repeat = 1;
-  bool json = false, quiet = false, chat = false;
+  bool json = false, quiet = false, chat = false, health = false, metrics = false;
   std::string system;
 };
 
@@ -335,7 +337,8 @@ double percentile(std::vector<double> v, double p) {
                "usage: barq-uds [--socket PATH] [--id ID] [--max-tokens N] [--temperature T] [--repeat R]\n"
                "                [--json] [--quiet] PROMPT\n"
                "       barq-uds --chat [--system TEXT] [--socket PATH] [--max-tokens N] [--temperature T]\n"
-               "                (one user turn per stdin line; the server renders the chat template)\n");
+               "                (one user turn per stdin line; the server renders the chat template)\n"
+               "       barq-uds --health | --metrics [--socket PATH]   (the engine's health JSON / Prometheus text)\n");
   std::exit(2);
 }
 
@@ -362,13 +365,15 @@ Options parse(int argc, char** argv) {
     else if (a == "--json") o.json = true;
     else if (a == "--quiet") o.quiet = true;
     else if (a == "--chat") o.chat = true;
+    else if (a == "--health") o.health = true;
+    else if (a == "--metrics") o.metrics = true;
     else if (a == "--system") o.system = arg();
     else if (a == "-h" || a == "--help") usage(nullptr);
     else if (!a.empty() && a[0] == '-' && a != "-") usage(("unknown option " + a).c_str());
     else if (have_prompt) usage("more than one prompt");
     else o.prompt = a, have_prompt = true;
   }
-  if (!have_prompt && !o.chat) usage("no prompt");
+  if (!have_prompt && !o.chat && !o.health && !o.metrics) usage("no prompt");
   if (o.chat && (have_prompt || o.repeat != 1)) usage("--chat reads its turns from stdin (no PROMPT, no --repeat)");
   if (o.max_tokens < 0 || o.repeat < 1) usage("--max-tokens must be >= 0 and --repeat >= 1");
   return o;
@@ -386,6 +391,32 @@ int main(int argc, char** argv) {
   if (fd < 0 || ::connect(fd, (const sockaddr*)&addr, sizeof addr) != 0) {
     std::fprintf(stderr, "barq-uds: cannot connect to %s: %s\n", o.socket_path.c_str(), std::strerror(errno));
     return 2;
+  }
+  if (o.health || o.metrics) {  // one query frame: the engine's health (JSON) or metrics (Prometheus text)
+    const std::string what = o.health ? "health" : "metrics";
+    std::string body;
+    int status = 0;
+    try {
+      if (!send_frame(fd, "{\"id\":" + json_quote(what) + ",\"" + what + "\":true}") || !recv_frame(fd, body))
+        throw std::runtime_error("no answer from the server");
+      if (o.health) {
+        std::fwrite(body.data(), 1, body.size(), stdout);
+        std::fputc('\n', stdout);
+        const auto fr = JsonReader(body).object();
+        auto it = fr.find("healthy");
+        if (it != fr.end() && it->second.kind == JsonValue::kBool && !it->second.b) status = 1;
+      } else {
+        const auto fr = JsonReader(body).object();
+        auto it = fr.find("prometheus");
+        if (it == fr.end() || it->second.kind != JsonValue::kString) throw std::runtime_error("no metrics in the answer");
+        std::fwrite(it->second.str.data(), 1, it->second.str.size(), stdout);
+      }
+    } catch (const std::exception& e) {
+      std::fprintf(stderr, "barq-uds: %s\n", e.what());
+      status = 2;
+    }
+    ::close(fd);
+    return status;
   }
   if (o.chat) {  // interactive multi-turn chat: the history travels as OpenAI messages
     std::vector<std::pair<std::string, std::string>> turns;

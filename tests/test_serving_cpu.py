@@ -689,3 +689,32 @@ def test_http_api_key(tiny_engine):
         assert c.post("/v1/completions", json=body, headers={"Authorization": "Bearer k1"}).status_code == 200
         assert c.get("/health").status_code == 200
     srv.aengine.shutdown()
+
+
+def test_uds_health_and_metrics_queries(tiny_engine, tmp_path):
+    import shutil
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSClient, UDSServer
+    from barq_inference_b200.server.uds_native import build_client
+
+    path = str(tmp_path / "hm.sock")
+    ae = AsyncEngine(tiny_engine)
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        cl = UDSClient(path)
+        list(cl.stream("hi", max_tokens=2, temperature=0.0))
+        h = cl.query("health")
+        assert h["healthy"] is True and h["done"] is True
+        m = cl.query("metrics")["prometheus"]
+        assert "barq_requests_total 1" in m
+        cl.close()
+        if shutil.which("g++") or shutil.which("c++"):
+            exe = build_client()
+            r = subprocess.run([exe, "--socket", path, "--health"], capture_output=True, timeout=60)
+            assert r.returncode == 0 and json.loads(r.stdout)["healthy"] is True
+            r = subprocess.run([exe, "--socket", path, "--metrics"], capture_output=True, timeout=60)
+            assert r.returncode == 0 and b"barq_requests_total" in r.stdout
+    finally:
+        srv.stop()
+        ae.shutdown()
