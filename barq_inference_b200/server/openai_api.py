@@ -348,7 +348,7 @@ class OpenAIServer:
         async def root():
             return {"object": "server.info", "model": srv.model_id, "architecture": srv.arch,
                     "endpoints": ["/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions",
-                                  "/v1/embeddings",
+                                  "/v1/embeddings", "/tokenize", "/detokenize",
                                   "/health", "/metrics"]}
 
         @app.get("/v1/models")
@@ -475,6 +475,32 @@ class OpenAIServer:
                                  "data": [{"object": "embedding", "index": i, "embedding": v.tolist()}
                                           for i, v in enumerate(vecs)],
                                  "usage": {"prompt_tokens": n_tok, "total_tokens": n_tok}}, headers=CORS)
+
+        @app.post("/tokenize")
+        async def tokenize(request: Request):
+            """llama.cpp-style: {"content": str, "add_special": bool} -> {"tokens": [ids]}."""
+            try:
+                body = await srv._body(request)
+                text = body.get("content")
+                if not isinstance(text, str):
+                    raise ValueError("content must be a string")
+                ids = srv.tok.encode(text, add_special=bool(body.get("add_special", False)))
+            except ValueError as e:
+                return _err(400, str(e))
+            return JSONResponse({"tokens": ids}, headers=CORS)
+
+        @app.post("/detokenize")
+        async def detokenize(request: Request):
+            """{"tokens": [ids]} -> {"content": str}."""
+            try:
+                body = await srv._body(request)
+                ids = body.get("tokens")
+                if not isinstance(ids, list) or not all(isinstance(t, int) and 0 <= t < srv.tok.vocab_size
+                                                        for t in ids):
+                    raise ValueError("tokens must be a list of token ids")
+            except ValueError as e:
+                return _err(400, str(e))
+            return JSONResponse({"content": srv.tok.decode(ids)}, headers=CORS)
 
         @app.post("/v1/completions")
         async def completions(request: Request):

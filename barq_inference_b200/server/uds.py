@@ -19,7 +19,8 @@ carries ``logprobs`` = [{token, bytes, logprob, top: [{token, bytes, logprob}, .
 of strings, token ids or lists of token ids) is answered by one frame ``{"id", "embeddings":
 [[...]], "prompt_tokens", "done": true}``; a request ``{"id", "health": true}`` by one frame with
 ``healthy``, ``last_error`` and ``kv_usage``; ``{"id", "metrics": true}`` by one frame whose
-``prometheus`` member is the engine-side metrics text.  A client that disconnects mid-stream has its request
+``prometheus`` member is the engine-side metrics text; ``{"id", "tokenize": text}`` /
+``{"id", "detokenize": ids}`` by one frame with ``tokens`` / ``content``.  A client that disconnects mid-stream has its request
 aborted in the engine.
 """
 from __future__ import annotations
@@ -127,6 +128,9 @@ class UDSServer:
         if req.get("health"):
             send_frame(conn, self._health(rid))
             return
+        if "tokenize" in req or "detokenize" in req:
+            send_frame(conn, self._tokenize(req, rid))
+            return
         if req.get("metrics"):
             eng = getattr(self.ae, "engine", None)
             send_frame(conn, {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0,
@@ -193,6 +197,24 @@ class UDSServer:
         finally:
             if guard is not None:  # client went away mid-stream
                 guard.fail()
+
+    def _tokenize(self, req: dict, rid: str) -> dict:
+        """{"tokenize": text[, "add_special"]} -> {"tokens"}; {"detokenize": ids} -> {"content"}."""
+        out = {"id": rid, "text": "", "tokens_generated": 0, "ttft_ms": 0, "total_time_ms": 0, "done": True}
+        try:
+            if "tokenize" in req:
+                if not isinstance(req["tokenize"], str):
+                    raise ValueError("tokenize takes a string")
+                out["tokens"] = self.tok.encode(req["tokenize"], add_special=bool(req.get("add_special", False)))
+            else:
+                ids = req["detokenize"]
+                if not isinstance(ids, list) or not all(isinstance(t, int) and 0 <= t < self.tok.vocab_size
+                                                        for t in ids):
+                    raise ValueError("detokenize takes a list of token ids")
+                out["content"] = self.tok.decode(ids)
+        except ValueError as e:
+            out["error"] = f"bad request: {e}"
+        return out
 
     def _health(self, rid: str) -> dict:
         """{"healthy", "last_error", "kv_usage"} of the engine behind this server (one frame)."""

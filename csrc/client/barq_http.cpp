@@ -31,6 +31,7 @@
 //   POST /v1/chat/completions    messages (rendered by the engine's chat template)
 //   POST /v1/responses           input (string or messages) / prompt / messages, max_output_tokens
 //   POST /v1/embeddings          input (string, strings, token ids or lists of them)
+//   POST /tokenize, /detokenize  {"content"[, "add_special"]} -> {"tokens"}; {"tokens"} -> {"content"}
 //   OPTIONS *                    204 with CORS headers
 // Request fields forwarded to the engine: max_tokens, temperature, top_k, top_p, min_p, seed,
 // repetition / frequency / presence penalties, response_format, grammar, tools / tool_choice (the
@@ -1026,6 +1027,36 @@ Outcome embeddings_route(int fd, const Request& req, bool keep, const std::strin
   return Outcome{200, !keep};
 }
 
+// llama.cpp-style /tokenize ({"content", "add_special"} -> {"tokens"}) and /detokenize
+// ({"tokens"} -> {"content"}), answered by the engine's tokenizer.
+Outcome tokenize_route(int fd, const Request& req, bool keep, const std::string& rid, bool detok) {
+  Value body;
+  try {
+    body = barqjson::parse(req.body);
+  } catch (const std::exception&) {
+    return finish_error(fd, 400, "request body is not valid JSON", keep, rid);
+  }
+  Value r = Value::object();
+  r.set("id", Value::string(rid));
+  const Value* in = body.is_object() ? body.get(detok ? "tokens" : "content") : nullptr;
+  if (!in || (detok ? !in->is_array() : !in->is_string()))
+    return finish_error(fd, 400, detok ? "tokens must be a list of token ids" : "content must be a string", keep, rid);
+  r.set(detok ? "detokenize" : "tokenize", *in);
+  if (!detok)
+    if (const Value* a = body.get("add_special"); a && a->type == Value::kBool) r.set("add_special", *a);
+  EngineLink link;
+  std::string err;
+  Value fr;
+  if (!link.open(err)) return finish_error(fd, 502, "engine unavailable: " + err, keep, rid);
+  if (!link.send(r) || !link.next(fr, err)) return finish_error(fd, 500, err.empty() ? "send failed" : err, keep, rid);
+  if (const Value* e = fr.get("error"); e && e->is_string()) return finish_error(fd, engine_error_status(e->str), e->str, keep, rid);
+  Value o = Value::object();
+  const Value* v = fr.get(detok ? "content" : "tokens");
+  o.set(detok ? "content" : "tokens", v ? *v : Value());
+  respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
+  return Outcome{200, !keep};
+}
+
 std::string request_id(const Request& req) {
   std::string rid = req.header("x-request-id");
   bool clean = !rid.empty() && rid.size() <= 128;
@@ -1063,7 +1094,7 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       o.set("model", Value::string(g_opt.model_id));
       o.set("front_end", Value::string("barq-http"));
       for (const char* e : {"/v1/models", "/v1/responses", "/v1/completions", "/v1/chat/completions",
-                            "/v1/embeddings", "/health", "/metrics"})
+                            "/v1/embeddings", "/tokenize", "/detokenize", "/health", "/metrics"})
         eps.push(Value::string(e));
       o.set("endpoints", eps);
       respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
@@ -1142,6 +1173,10 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       respond(fd, 200, "text/plain; version=0.0.4", text, keep, rid);
       return Outcome{200, !keep};
     }
+  }
+  if (p == "/tokenize" || p == "/detokenize") {
+    if (req.method != "POST") return finish_error(fd, 405, "use POST for " + p, keep, rid);
+    return tokenize_route(fd, req, keep, rid, p == "/detokenize");
   }
   if (p == "/v1/embeddings") {
     if (req.method != "POST") return finish_error(fd, 405, "use POST for " + p, keep, rid);

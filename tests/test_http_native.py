@@ -492,6 +492,12 @@ def test_against_real_uds_server_and_cpu_engine(tmp_path):
         assert "".join(toks) == "".join(ev["choices"][0]["text"] for ev in evs)
         m = _req(port, "GET", "/metrics")[2].decode()
         assert "barq_http_requests_total" in m and "barq_requests_total" in m
+        st, _, b = _req(port, "POST", "/tokenize", {"content": "hello world", "add_special": True})
+        assert st == 200 and json.loads(b)["tokens"] == tok.encode("hello world", add_special=True)
+        st, _, b = _req(port, "POST", "/detokenize", {"tokens": json.loads(b)["tokens"]})
+        assert st == 200 and json.loads(b)["content"] == tok.decode(tok.encode("hello world", add_special=True))
+        assert _req(port, "POST", "/detokenize", {"tokens": [10 ** 9]})[0] == 400
+        assert _req(port, "POST", "/tokenize", {"content": 5})[0] == 400
         # embeddings through the engine: one vector per input, same as the engine's own
         st, _, b = _req(port, "POST", "/v1/embeddings", {"input": ["hello", "world wide"]})
         out = json.loads(b)

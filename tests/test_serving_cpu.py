@@ -718,3 +718,12 @@ def test_uds_health_and_metrics_queries(tiny_engine, tmp_path):
     finally:
         srv.stop()
         ae.shutdown()
+
+
+def test_http_tokenize_detokenize(client, tiny_engine):
+    tok = tiny_engine.tokenizer
+    r = client.post("/tokenize", json={"content": "hello there"}).json()
+    assert r["tokens"] == tok.encode("hello there", add_special=False)
+    assert client.post("/detokenize", json={"tokens": r["tokens"]}).json()["content"] == tok.decode(r["tokens"])
+    assert client.post("/tokenize", json={"content": 3}).status_code == 400
+    assert client.post("/detokenize", json={"tokens": [-1]}).status_code == 400
