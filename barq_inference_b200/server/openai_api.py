@@ -356,6 +356,12 @@ class OpenAIServer:
             return {"object": "list", "data": [{"id": srv.model_id, "object": "model", "created": int(time.time()),
                                                 "owned_by": "barq"}]}
 
+        @app.get("/v1/models/{model_id:path}")
+        async def model_info(model_id: str):
+            if model_id != srv.model_id:
+                return _err(404, f"model {model_id!r} not found", "not_found_error")
+            return {"id": srv.model_id, "object": "model", "created": int(time.time()), "owned_by": "barq"}
+
         @app.get("/health")
         async def health():
             blocks = getattr(srv.engine, "blocks", None)

@@ -1112,6 +1112,17 @@ Outcome dispatch(int fd, const Request& req, const std::string& client, bool kee
       respond(fd, 200, "application/json", barqjson::dump(o), keep, rid);
       return Outcome{200, !keep};
     }
+    if (p.rfind("/v1/models/", 0) == 0) {  // retrieve one model
+      const std::string name = p.substr(11);
+      if (name != g_opt.model_id) return finish_error(fd, 404, "model '" + name + "' not found", keep, rid);
+      Value m = Value::object();
+      m.set("id", Value::string(g_opt.model_id));
+      m.set("object", Value::string("model"));
+      m.set("created", Value::number((double)std::time(nullptr)));
+      m.set("owned_by", Value::string("barq"));
+      respond(fd, 200, "application/json", barqjson::dump(m), keep, rid);
+      return Outcome{200, !keep};
+    }
     if (p == "/health") {  // ok while any engine is up and healthy
       Value o = Value::object(), engines = Value::array();
       int n_ok = 0, n_up = 0;

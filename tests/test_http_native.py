@@ -152,6 +152,9 @@ def test_info_models_health_and_cors(gateway, tmp_path):
     eng, port = gateway
     st, h, b = _req(port, "GET", "/v1/models")
     assert st == 200 and json.loads(b)["data"][0]["id"] == "tiny-x"
+    st, _, b = _req(port, "GET", "/v1/models/tiny-x")
+    assert st == 200 and json.loads(b)["id"] == "tiny-x" and json.loads(b)["object"] == "model"
+    assert _req(port, "GET", "/v1/models/other")[0] == 404
     assert h["Access-Control-Allow-Origin"] == "*"
     st, _, b = _req(port, "GET", "/")
     assert st == 200 and "/v1/chat/completions" in json.loads(b)["endpoints"]

@@ -727,3 +727,8 @@ def test_http_tokenize_detokenize(client, tiny_engine):
     assert client.post("/detokenize", json={"tokens": r["tokens"]}).json()["content"] == tok.decode(r["tokens"])
     assert client.post("/tokenize", json={"content": 3}).status_code == 400
     assert client.post("/detokenize", json={"tokens": [-1]}).status_code == 400
+
+
+def test_http_retrieve_model(client):
+    assert client.get("/v1/models/tiny").json()["id"] == "tiny"
+    assert client.get("/v1/models/other").status_code == 404
