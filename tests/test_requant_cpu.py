@@ -53,6 +53,13 @@ def test_q3_k_is_exact_as_q6_k(seed):
     q6 = q3_k_as_q6_k(raw, N, K)
     assert q6.shape == (N, K // 256 * 210) and q6.dtype == torch.uint8
     assert np.array_equal(dequantize(q6.numpy(), GGMLType.Q6_K, (N, K)), dequantize(raw.numpy(), GGMLType.Q3_K, (N, K)))
+    try:  # the C++ oracle the device kernels are checked against reads the Q6_K rows the same way
+        from barq_inference_b200 import _cpu_ref
+    except ImportError:
+        _cpu_ref = None
+    if _cpu_ref is not None:
+        got = _cpu_ref.dequantize(q6.reshape(-1).contiguous(), int(GGMLType.Q6_K), N * K).numpy()
+        assert np.array_equal(got.reshape(N, K), dequantize(raw.numpy(), GGMLType.Q3_K, (N, K)))
     # the loader streams Q3_K as exactly these Q6_K rows
     w = QWeight.from_packed(raw, GGMLType.Q3_K, N, K, "cpu")
     assert w.wtype == int(GGMLType.Q6_K)
@@ -73,6 +80,13 @@ def test_iq4_xs_as_iq4_nl_rounds_only_the_block_scales(seed):
     dxs = dequantize(raw.numpy(), GGMLType.IQ4_XS, (N, K)).reshape(N, -1, 32)
     assert np.array_equal(np.sign(got.reshape(N, -1, 32)), np.sign(dxs))
     assert QWeight.from_packed(raw, GGMLType.IQ4_XS, N, K, "cpu").wtype == int(GGMLType.IQ4_NL)
+    try:  # the C++ oracle of the device kernels reads the converted rows as the Python oracle does
+        from barq_inference_b200 import _cpu_ref
+    except ImportError:
+        _cpu_ref = None
+    if _cpu_ref is not None:
+        c = _cpu_ref.dequantize(nl.reshape(-1).contiguous(), int(GGMLType.IQ4_NL), N * K).numpy().reshape(N, K)
+        assert np.array_equal(c, got)
 
 
 def test_loader_streams_requantized_types():
