@@ -5,7 +5,6 @@ missing or stale extension is an error (``require_ext``): there is no silent PyT
 """
 from __future__ import annotations
 
-import math
 import os
 
 import torch

@@ -8,7 +8,6 @@ pytestmark = pytest.mark.gpu
 
 
 def test_fused_allreduce_peer_timeout_is_reported():
-    from barq_inference_b200 import ops
     from barq_inference_b200.ops import require_ext
 
     C = require_ext()

@@ -12,7 +12,7 @@ bytes per 16-element step), whose results are verified on B200s: it must compute
 import numpy as np
 import pytest
 
-from tcgen05_emu import (IDESC_B_MAJOR_MN, Smem, Tmem, from_bits, idesc_bf16, idesc_f16, mma, swz, to_bits,
+from tcgen05_emu import (IDESC_B_MAJOR_MN, Smem, Tmem, from_bits, idesc_bf16, idesc_f16, mma, to_bits,
                          umma_desc_sw128, umma_desc_sw128_mn)
 
 
