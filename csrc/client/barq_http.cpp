@@ -287,6 +287,10 @@ class Conn {
     } else if (req.method == "POST") {
       return 411;
     }
+    // a client that asked to be told before it sends its body (curl does for bodies over 1 KB)
+    if (buf_.size() < n && lower(req.header("expect")) == "100-continue" &&
+        !send_all(fd_, "HTTP/1.1 100 Continue\r\n\r\n"))
+      return -1;
     while (buf_.size() < n)
       if (!fill()) return 400;
     req.body = buf_.substr(0, n);

@@ -274,6 +274,26 @@ def test_streams_are_chunk_encoded_and_keep_the_connection(gateway):
     assert "".join(e["choices"][0]["text"] for e in _events(rest)) == "Hello world"
 
 
+def test_expect_100_continue(gateway):
+    """A client that waits for "100 Continue" before its body (curl, for bodies over 1 KB) gets it
+    right away."""
+    eng, port = gateway
+    body = json.dumps({"prompt": "hello", "pad": "x" * 2000}).encode()
+    s = socket.create_connection(("127.0.0.1", port), timeout=5)
+    s.sendall(b"POST /v1/completions HTTP/1.1\r\nContent-Type: application/json\r\nExpect: 100-continue\r\n"
+              b"Content-Length: " + str(len(body)).encode() + b"\r\nConnection: close\r\n\r\n")
+    assert s.recv(64).startswith(b"HTTP/1.1 100 Continue")  # before any body byte was sent
+    s.sendall(body)
+    data = b""
+    while True:
+        chunk = s.recv(65536)
+        if not chunk:
+            break
+        data += chunk
+    s.close()
+    assert data.startswith(b"HTTP/1.1 200") and b"Hello world" in data
+
+
 def test_stop_strings_are_never_sent(gateway):
     eng, port = gateway
     st, _, b = _req(port, "POST", "/v1/completions", {"prompt": "stop", "stop": ["<end>", "zz"], "stream": True})
