@@ -302,6 +302,9 @@ class UDSServer:
             daemon_threads = True
 
         self._server = Server(self.path, Handler)
+        # owner-only by default: any local user who can connect can generate (BARQ_SOCKET_MODE=660
+        # shares it with the group, e.g. a front end running as another user)
+        os.chmod(self.path, int(os.environ.get("BARQ_SOCKET_MODE", "600"), 8))
         if background:
             threading.Thread(target=self._server.serve_forever, daemon=True).start()
         else:

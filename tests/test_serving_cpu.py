@@ -732,3 +732,25 @@ def test_http_tokenize_detokenize(client, tiny_engine):
 def test_http_retrieve_model(client):
     assert client.get("/v1/models/tiny").json()["id"] == "tiny"
     assert client.get("/v1/models/other").status_code == 404
+
+
+def test_uds_socket_is_owner_only(tiny_engine, tmp_path, monkeypatch):
+    import stat
+
+    from barq_inference_b200.server.async_engine import AsyncEngine
+    from barq_inference_b200.server.uds import UDSServer
+
+    ae = AsyncEngine(tiny_engine)
+    path = str(tmp_path / "perm.sock")
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        assert stat.S_IMODE(os.stat(path).st_mode) == 0o600
+    finally:
+        srv.stop()
+    monkeypatch.setenv("BARQ_SOCKET_MODE", "660")
+    srv = UDSServer(ae, tiny_engine.tokenizer, path).start()
+    try:
+        assert stat.S_IMODE(os.stat(path).st_mode) == 0o660
+    finally:
+        srv.stop()
+        ae.shutdown()
