@@ -227,11 +227,14 @@ class OpenAIServer:
         created = int(time.time())
         rid = {"text": "cmpl", "chat": "chatcmpl", "resp": "resp"}[kind] + f"-{created}{id(guard) % 100000}"
 
-        async def one(i: int):
+        # a batch of prompts (completions) gives n choices per prompt, indexed prompt-major
+        batch = prompt_ids if prompt_ids and isinstance(prompt_ids[0], list) else [prompt_ids]
+
+        async def one(b: int, i: int):
             # choice i samples with its own seed (a 0 seed already differs per request)
             p = dataclasses.replace(params, seed=params.seed + i) if (i and params.seed) else params
             parts, reason, n, lps = [], "stop", 0, []
-            async for delta, fin, entries, ntok in self._run(prompt_ids, p, stops):
+            async for delta, fin, entries, ntok in self._run(batch[b], p, stops):
                 if delta:
                     guard.first_token()
                     parts.append(delta)
@@ -242,13 +245,14 @@ class OpenAIServer:
             return "".join(parts), reason, n, lps
 
         try:
-            outs = await asyncio.gather(*(one(i) for i in range(n_choices)))
+            outs = await asyncio.gather(*(one(b, i) for b in range(len(batch)) for i in range(n_choices)))
         except Exception:
             guard.fail()
             raise
         n_tok = sum(o[2] for o in outs)
-        guard.complete(len(prompt_ids), n_tok)
-        usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": n_tok, "total_tokens": len(prompt_ids) + n_tok}
+        n_prompt = sum(len(x) for x in batch)
+        guard.complete(n_prompt, n_tok)
+        usage = {"prompt_tokens": n_prompt, "completion_tokens": n_tok, "total_tokens": n_prompt + n_tok}
         lp = params.logprobs
         if kind == "text":
             return {"id": rid, "object": "text_completion", "created": created, "model": model,
@@ -400,8 +404,15 @@ class OpenAIServer:
                         ids = list(prompt)
                     elif isinstance(prompt, str):
                         ids = srv._encode(prompt)
+                    elif isinstance(prompt, list) and prompt and all(isinstance(x, str) for x in prompt):
+                        ids = [srv._encode(x) for x in prompt]  # a batch of prompts
+                    elif isinstance(prompt, list) and prompt and all(
+                            isinstance(x, list) and x and all(isinstance(t, int) for t in x) for x in prompt):
+                        ids = [list(x) for x in prompt]
                     else:
-                        raise ValueError("prompt must be a string or a list of token ids")
+                        raise ValueError("prompt must be a string, a list of strings or token id list(s)")
+                    if ids and isinstance(ids[0], list) and body.get("stream"):
+                        raise ValueError("a batch of prompts is not supported with stream")
                     params = _params(body)
                 elif kind == "chat":
                     tools = tool_setup(body)

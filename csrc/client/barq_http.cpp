@@ -615,6 +615,7 @@ struct Call {
   Value uds;         // the engine request
   std::vector<std::string> stops;
   bool stream = false, include_usage = false, tools = false, logprobs = false;
+  std::vector<Value> prompts;  // a batch of prompts (completions), else empty
   int n = 1;
   std::string model;
 };
@@ -637,13 +638,27 @@ Call translate(const std::string& kind, const Value& body, const std::string& ri
   };
   if (kind == "text") {
     const Value* p = body.get("prompt");
-    bool ok = p && p->is_string();
+    bool ok = p && p->is_string(), ids = false, batch = false;
     if (p && p->is_array() && !p->arr.empty()) {
-      ok = true;
-      for (const auto& t : p->arr) ok = ok && t.is_integer();
+      ids = batch = true;
+      for (const auto& t : p->arr) {
+        ids = ids && t.is_integer();
+        bool one = t.is_string();
+        if (t.is_array() && !t.arr.empty()) {
+          one = true;
+          for (const auto& x : t.arr) one = one && x.is_integer();
+        }
+        batch = batch && one;
+      }
+      ok = ids || batch;
     }
-    if (!ok) bad("prompt must be a string or a list of token ids");
-    c.uds.set("prompt", *p);
+    if (!ok) bad("prompt must be a string, a list of strings or token id list(s)");
+    if (batch && !ids) {  // a batch of prompts: n choices for each, indexed prompt-major
+      c.prompts = p->arr;
+      c.uds.set("prompt", p->arr[0]);
+    } else {
+      c.uds.set("prompt", *p);
+    }
   } else if (kind == "chat") {
     const Value* m = body.get("messages");
     if (!m) bad("messages must be a non-empty list");
@@ -709,6 +724,7 @@ Call translate(const std::string& kind, const Value& body, const std::string& ri
   if (const Value* s = body.get("stream"); s && s->type == Value::kBool) c.stream = s->b;
   if (c.stream && c.n > 1) bad("n > 1 is not supported with stream");
   if (c.stream && c.tools) bad("stream with tools is not supported; send stream=false");
+  if (c.stream && !c.prompts.empty()) bad("a batch of prompts is not supported with stream");
   if (const Value* so = body.get("stream_options"); so && so->is_object())
     if (const Value* iu = so->get("include_usage"); iu && iu->type == Value::kBool) c.include_usage = iu->b;
   return c;
@@ -911,29 +927,34 @@ Outcome generate_route(int fd, const std::string& kind, const Request& req, bool
     return Outcome{g.status == 200 ? 200 : g.status, !(chunked && keep && client_ok)};
   }
 
-  // the n choices run as concurrent engine requests (continuous batching serves them together)
-  std::vector<Gen> outs(c.n);
+  // the n choices (of every prompt of a batch) run as concurrent engine requests (continuous
+  // batching serves them together); choice index = prompt * n + i
+  const int n_prompts = c.prompts.empty() ? 1 : (int)c.prompts.size();
+  std::vector<Gen> outs(n_prompts * c.n);
   std::vector<std::thread> workers;
-  for (int i = 0; i < c.n; ++i) {
+  for (int q = 0; q < n_prompts * c.n; ++q) {
+    const int i = q % c.n;
     Value r = c.uds;
+    if (!c.prompts.empty()) r.set("prompt", c.prompts[q / c.n]);
+    if (q > 0) r.set("id", Value::string(rid + "-" + std::to_string(q)));
     if (i > 0) {  // choice i samples with its own seed (a 0 seed already differs per request)
       const Value* s = r.get("seed");
       if (s && s->is_number() && s->num != 0) r.set("seed", Value::number(s->num + i));
-      r.set("id", Value::string(rid + "-" + std::to_string(i)));
     }
-    auto run = [&outs, &c, i, fd](Value req) {
+    auto run = [&outs, &c, q, fd](Value req) {
       // a client that has gone away stops the generation (closing the link aborts it in the engine)
-      outs[i] = generate(req, c.stops, [] { return true; },
+      outs[q] = generate(req, c.stops, [] { return true; },
                          [fd](const std::string&, std::vector<Value>&) { return !client_gone(fd); });
     };
-    if (i + 1 < c.n) workers.emplace_back(run, std::move(r));
+    if (q + 1 < n_prompts * c.n) workers.emplace_back(run, std::move(r));
     else run(std::move(r));
   }
   for (auto& w : workers) w.join();
   long p_tok = 0, c_tok = 0;
-  for (const Gen& g : outs) {
+  for (size_t q = 0; q < outs.size(); ++q) {
+    const Gen& g = outs[q];
     if (g.status != 200) return finish_error(fd, g.status, g.error, keep, rid);
-    p_tok = g.prompt_tokens;
+    if ((int)q % c.n == 0) p_tok += g.prompt_tokens;  // each prompt counted once
     c_tok += g.completion_tokens;
   }
   g_ctr.prompt_tokens += (uint64_t)p_tok;

@@ -227,6 +227,17 @@ def test_chat_and_responses_routes(gateway):
     assert sorted(r.get("seed") for r in eng.requests[-3:]) == [5, 6, 7]  # concurrent engine requests
 
 
+def test_batch_of_prompts(gateway):
+    eng, port = gateway
+    st, _, b = _req(port, "POST", "/v1/completions", {"prompt": ["hello", "utf8"], "n": 2})
+    out = json.loads(b)
+    assert st == 200 and [c["index"] for c in out["choices"]] == [0, 1, 2, 3]
+    assert [c["text"] for c in out["choices"]] == ["Hello world", "Hello world", "é\U0001F600\"q\"\n", "é\U0001F600\"q\"\n"]
+    assert out["usage"]["prompt_tokens"] == 3 + 4  # each prompt once (the scripted engine's counts)
+    assert _req(port, "POST", "/v1/completions", {"prompt": ["a", "b"], "stream": True})[0] == 400
+    assert _req(port, "POST", "/v1/completions", {"prompt": [[1, 2], [3]]})[0] == 200
+
+
 def test_streams(gateway):
     eng, port = gateway
     st, h, b = _req(port, "POST", "/v1/chat/completions",

@@ -754,3 +754,13 @@ def test_uds_socket_is_owner_only(tiny_engine, tmp_path, monkeypatch):
     finally:
         srv.stop()
         ae.shutdown()
+
+
+def test_http_batch_of_prompts(client):
+    r = client.post("/v1/completions", json={"prompt": ["one", "two words", "three"], "max_tokens": 2,
+                                             "temperature": 0, "n": 2}).json()
+    assert [c["index"] for c in r["choices"]] == list(range(6))
+    assert r["usage"]["completion_tokens"] > 0
+    r2 = client.post("/v1/completions", json={"prompt": [[1, 2, 3], [4, 5]], "max_tokens": 1}).json()
+    assert len(r2["choices"]) == 2 and r2["usage"]["prompt_tokens"] == 5
+    assert client.post("/v1/completions", json={"prompt": ["a", "b"], "stream": True}).status_code == 400
