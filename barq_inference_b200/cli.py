@@ -316,7 +316,8 @@ def cmd_bench_serve(args) -> int:
 
     out = asyncio.run(run(args.url, n_requests=args.requests, concurrency=args.concurrency,
                           prompt_words=args.prompt_words, max_tokens=args.max_tokens, rate=args.rate,
-                          chat=args.chat, model=args.model_id, seed=args.seed, temperature=args.temperature))
+                          chat=args.chat, model=args.model_id, seed=args.seed, temperature=args.temperature,
+                          api_key=args.api_key))
     print(json.dumps(out, indent=2))
     return 0 if out["completed"] else 1
 
@@ -725,6 +726,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--chat", action="store_true", help="use /v1/chat/completions")
     p.add_argument("--model-id", default="barq")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--api-key", default=os.environ.get("BARQ_API_KEY"), help="sent as 'Authorization: Bearer KEY'")
     p.set_defaults(fn=cmd_bench_serve)
 
     p = sub.add_parser("convert", help="requantize a GGUF file")

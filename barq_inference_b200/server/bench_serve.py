@@ -88,7 +88,7 @@ async def _one(session, url: str, body: dict) -> RequestStats:
 
 async def run(url: str, n_requests: int = 64, concurrency: int = 16, prompt_words: int = 64,
               max_tokens: int = 128, rate: float = 0.0, chat: bool = False, model: str = "barq",
-              seed: int = 0, temperature: float = 0.0) -> dict:
+              seed: int = 0, temperature: float = 0.0, api_key: str | None = None) -> dict:
     """Benchmark ``url`` (the server's base URL, e.g. ``http://127.0.0.1:8080``); returns the summary."""
     import aiohttp
 
@@ -97,7 +97,8 @@ async def run(url: str, n_requests: int = 64, concurrency: int = 16, prompt_word
     rng = random.Random(seed)
     timeout = aiohttp.ClientTimeout(total=None, sock_read=600)
 
-    async with aiohttp.ClientSession(timeout=timeout) as session:
+    headers = {"Authorization": f"Bearer {api_key}"} if api_key else None
+    async with aiohttp.ClientSession(timeout=timeout, headers=headers) as session:
         async def task(i: int, delay: float) -> RequestStats:
             if delay:
                 await asyncio.sleep(delay)

@@ -699,6 +699,12 @@ def test_api_key(tmp_path):
         assert _req(port, "POST", "/v1/completions", {"prompt": "hello"},
                     headers={"Authorization": "Bearer s3cret"})[0] == 200
         assert _req(port, "GET", "/health")[0] == 200 and _req(port, "GET", "/metrics")[0] == 200  # stay open
+        import asyncio
+
+        from barq_inference_b200.server.bench_serve import run
+        assert asyncio.run(run(f"http://127.0.0.1:{port}", n_requests=2, concurrency=2, max_tokens=2))["failed"] == 2
+        assert asyncio.run(run(f"http://127.0.0.1:{port}", n_requests=2, concurrency=2, max_tokens=2,
+                               api_key="s3cret"))["completed"] == 2
     finally:
         p.kill()
         p.wait()
