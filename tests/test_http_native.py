@@ -709,3 +709,25 @@ def test_api_key(tmp_path):
         p.kill()
         p.wait()
         eng.close()
+
+
+def test_remote_client_api(gateway):
+    """The Client API over HTTP: generate / stream / chat / generate_batch against barq-http."""
+    from barq_inference_b200.client import GenerationConfig
+    from barq_inference_b200.remote import RemoteClient
+
+    eng, port = gateway
+    rc = RemoteClient(f"http://127.0.0.1:{port}", model="tiny-x")
+    r = rc.generate("hello", GenerationConfig(max_tokens=4, temperature=0))
+    assert r.text == "Hello world" and r.finish_reason == "length" and r.completion_tokens == 4
+    assert r.prompt_tokens == 3 and r.ttft_s is not None
+    assert "".join(rc.stream("hello")) == "Hello world"
+    r = rc.generate("stop", GenerationConfig(stop=["<end>"]))
+    assert r.text == "abc" and r.finish_reason == "stop"
+    r = rc.chat([{"role": "user", "content": "hello"}], GenerationConfig(json_mode=True))
+    assert r.text == "Hello world" and eng.requests[-1]["response_format"] == {"type": "json_object"}
+    rs = rc.generate_batch(["hello", "utf8"])
+    assert [x.text for x in rs] == ["Hello world", "é\U0001F600\"q\"\n"]
+    import pytest as _pt
+    with _pt.raises(RuntimeError, match="503"):
+        rc.generate("queue")
