@@ -1,6 +1,7 @@
 """barq_inference_b200: a Blackwell (sm_100a) native GGUF LLM inference engine.
 
-Top-level names load on first use: ``Client``, ``GenerationConfig`` (text API), ``Engine``,
+Top-level names load on first use: ``Client``, ``GenerationConfig`` (text API), ``RemoteClient``
+(the same API against a running HTTP server), ``Engine``,
 ``EngineConfig``, ``SamplingParams``, ``ModelContext`` (token API), ``read_gguf``.
 """
 __version__ = "0.1.0"
@@ -8,6 +9,7 @@ __version__ = "0.1.0"
 _LAZY = {
     "Client": ("client", "Client"),
     "GenerationConfig": ("client", "GenerationConfig"),
+    "RemoteClient": ("remote", "RemoteClient"),
     "Engine": ("engine.engine", "Engine"),
     "EngineConfig": ("engine.engine", "EngineConfig"),
     "SamplingParams": ("engine.sampling_params", "SamplingParams"),
